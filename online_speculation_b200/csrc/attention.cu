@@ -1,0 +1,434 @@
+// Paged attention with per-sequence causal or bidirectional masks.
+//
+// One kernel serves every attention shape of the package:
+//   * causal prefill of prompts (queries = keys = the prompt),
+//   * single-token decode against a paged, prefix-shared KV history,
+//   * speculative verification (a block of query tokens appended causally),
+//   * block-bidirectional drafting (a block of query tokens that see the
+//     read-only history plus each other in both directions),
+//   * full bidirectional masked-diffusion steps (no history).
+// Reference call sites: online-speculation/src/blockspec/parallel/backbone.py:113-148
+// (AR / draft views), src/inference_scaling/arllm/backends/transformers_backend.py
+// decode loop (HF SDPA with DynamicCache), src/inference_scaling/dllm/backends/llada.py:417-448.
+//
+// Layouts
+//   q     [T, Hq, D]  bf16, rows of sequence b start at q_start[b]
+//   cache [pages, Hkv, P, D] bf16 for K and for V (P = kPage tokens per page)
+//   table [B, max_pages] int32 physical page ids
+//   out   [T, Hq, D]  bf16
+// Query rows of one (sequence, kv head) are flattened token-major:
+// row = token * G + head_in_group with G = Hq / Hkv.  Query token i of a block of
+// length L sits at absolute position kv_len - L + i.
+//
+// Tensor cores: bf16 mma.sync m16n8k16 with ldmatrix operand loads, online
+// softmax in fp32 with exp2.  Two warp layouts:
+//   kRowsSplit  : 4 warps x 16 rows share each 32-key page (prefill / diffusion),
+//   kKeysSplit  : 4 warps split the pages of one 16-row tile and merge their
+//                 partial softmax states in shared memory (decode / verify / draft).
+#include "attention.h"
+#include "common.cuh"
+
+namespace osb {
+namespace {
+
+constexpr int kD = 128;
+constexpr int kPage = 32;
+constexpr int kStride = kD + 8;  // padded smem row (elements) to avoid ldmatrix bank conflicts
+
+struct AttnArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  const int* table;
+  int table_stride;
+  const int* q_start;
+  const int* q_len;
+  const int* kv_len;
+  const int* mode;  // per sequence: 0 causal, 1 bidirectional
+  const int* tile_seq;
+  const int* tile_row0;
+  __nv_bfloat16* out;
+  int Hq, Hkv, G;
+  float scale_log2;  // softmax scale * log2(e)
+  int* status;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Copy one 32-key page of K and V for kv head g into padded smem rows.
+// Keys at or beyond `valid` are zero-filled so masked products stay finite.
+__device__ __forceinline__ void load_page(const AttnArgs& a, int page, int g, int valid, __nv_bfloat16* sK,
+                                          __nv_bfloat16* sV, int tid, int nthreads) {
+  const long long base = (static_cast<long long>(page) * a.Hkv + g) * (kPage * kD);
+  const __nv_bfloat16* gk = a.k_cache + base;
+  const __nv_bfloat16* gv = a.v_cache + base;
+  // 32 rows x 16 chunks of 16 bytes
+  for (int c = tid; c < kPage * (kD / 8); c += nthreads) {
+    const int row = c / (kD / 8);
+    const int col = (c % (kD / 8)) * 8;
+    if (row < valid) {
+      cp_async16(sK + row * kStride + col, gk + row * kD + col);
+      cp_async16(sV + row * kStride + col, gv + row * kD + col);
+    } else {
+      *reinterpret_cast<uint4*>(sK + row * kStride + col) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sV + row * kStride + col) = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+// Per-warp flash-attention state for 16 query rows.
+struct WarpState {
+  uint32_t qf[kD / 16][4];
+  float o[kD / 8][4];
+  float m[2], l[2];
+  int qpos[2];   // absolute query position of this thread's two rows (-1 = padding row)
+};
+
+__device__ __forceinline__ void load_q(const AttnArgs& a, WarpState& st, int q0, int rows, int row_base, int g,
+                                       int qlen, int kvlen, int lane) {
+  const int r_lo = lane / 4, c2 = (lane % 4) * 2;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = row_base + r_lo + h * 8;
+    st.qpos[h] = row < rows ? kvlen - qlen + row / a.G : -1;
+  }
+#pragma unroll
+  for (int kk = 0; kk < kD / 16; ++kk) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = row_base + r_lo + h * 8;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v = 0;
+        if (row < rows) {
+          const int tok = row / a.G, head = g * a.G + row % a.G;
+          const __nv_bfloat16* p = a.q + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD + kk * 16 + c2 + half * 8;
+          v = *reinterpret_cast<const uint32_t*>(p);
+        }
+        st.qf[kk][h + half * 2] = v;
+      }
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < kD / 8; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) st.o[n][i] = 0.0f;
+  st.m[0] = st.m[1] = -INFINITY;
+  st.l[0] = st.l[1] = 0.0f;
+}
+
+// Process one 32-key page already resident in shared memory.
+__device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, const __nv_bfloat16* sK,
+                                             const __nv_bfloat16* sV, int key0, int kvlen, int bidir, int lane) {
+  float s[4][4];
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) s[n][i] = 0.0f;
+  const uint32_t kbase = smem_u32(sK);
+  // S = Q K^T over 4 key blocks of 8
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+#pragma unroll
+    for (int kk = 0; kk < kD / 16; kk += 2) {
+      // matrices: (keys n*8.., d kk*16+0..7), (.., +8), (.., (kk+1)*16), (.., +8)
+      const int mi = lane / 8, ri = lane % 8;
+      const uint32_t addr = kbase + ((n * 8 + ri) * kStride + kk * 16 + mi * 8) * 2;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(addr, b0, b1, b2, b3);
+      mma16816(s[n], st.qf[kk], b0, b1);
+      mma16816(s[n], st.qf[kk + 1], b2, b3);
+    }
+  }
+  // mask + online softmax
+  const int c2 = (lane % 4) * 2;
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int h = i / 2;
+      const int key = key0 + n * 8 + c2 + (i & 1);
+      const int qp = st.qpos[h];
+      const bool ok = qp >= 0 && key < kvlen && (bidir || key <= qp);
+      s[n][i] = ok ? s[n][i] * a.scale_log2 : -INFINITY;
+      mx[h] = fmaxf(mx[h], s[n][i]);
+    }
+  }
+  float corr[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+    mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+    const float mnew = fmaxf(st.m[h], mx[h]);
+    corr[h] = (mnew == -INFINITY) ? 1.0f : exp2f(st.m[h] - mnew);
+    st.m[h] = mnew;
+  }
+  float rs[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int h = i / 2;
+      const float p = (st.m[h] == -INFINITY) ? 0.0f : exp2f(s[n][i] - st.m[h]);
+      s[n][i] = p;
+      rs[h] += p;
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 1);
+    rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
+    st.l[h] = st.l[h] * corr[h] + rs[h];
+  }
+#pragma unroll
+  for (int n = 0; n < kD / 8; ++n) {
+    st.o[n][0] *= corr[0];
+    st.o[n][1] *= corr[0];
+    st.o[n][2] *= corr[1];
+    st.o[n][3] *= corr[1];
+  }
+  // O += P V  (2 k-steps of 16 keys)
+  const uint32_t vbase = smem_u32(sV);
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    uint32_t pa[4];
+    pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+    pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+    pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+    for (int n = 0; n < kD / 8; n += 2) {
+      // matrices: (keys kk*16+0..7, d n*8), (keys +8, d n*8), (keys 0..7, d (n+1)*8), (keys +8, d (n+1)*8)
+      const int mi = lane / 8, ri = lane % 8;
+      const int key = kk * 16 + (mi & 1) * 8 + ri;
+      const int d = n * 8 + (mi >> 1) * 8;
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(vbase + (key * kStride + d) * 2, b0, b1, b2, b3);
+      mma16816(st.o[n], pa, b0, b1);
+      mma16816(st.o[n + 1], pa, b2, b3);
+    }
+  }
+}
+
+__device__ __forceinline__ void store_rows(const AttnArgs& a, const WarpState& st, int q0, int rows, int row_base,
+                                           int g, int lane) {
+  const int r_lo = lane / 4, c2 = (lane % 4) * 2;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = row_base + r_lo + h * 8;
+    if (row >= rows) continue;
+    const float inv = st.l[h] > 0.0f ? 1.0f / st.l[h] : 0.0f;
+    const int tok = row / a.G, head = g * a.G + row % a.G;
+    __nv_bfloat16* p = a.out + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD;
+#pragma unroll
+    for (int n = 0; n < kD / 8; ++n) {
+      *reinterpret_cast<uint32_t*>(p + n * 8 + c2) = pack_bf16(st.o[n][2 * h] * inv, st.o[n][2 * h + 1] * inv);
+    }
+  }
+}
+
+// 4 warps x 16 rows share each page.
+__global__ void __launch_bounds__(128) attn_rows_kernel(const AttnArgs a) {
+  __shared__ __align__(16) __nv_bfloat16 sK[2][kPage * kStride];
+  __shared__ __align__(16) __nv_bfloat16 sV[2][kPage * kStride];
+  const int tile = blockIdx.x, g = blockIdx.y;
+  const int b = a.tile_seq[tile];
+  const int row0 = a.tile_row0[tile];
+  const int qlen = a.q_len[b], kvlen = a.kv_len[b], q0 = a.q_start[b];
+  const int bidir = a.mode[b];
+  const int rows = qlen * a.G;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  WarpState st;
+  load_q(a, st, q0, rows, row0 + warp * 16, g, qlen, kvlen, lane);
+  // last key any row of this tile can see
+  const int last_row = min(rows - 1, row0 + 63);
+  const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
+  const int npages = (max_key + kPage - 1) / kPage;
+  const int* tbl = a.table + static_cast<long long>(b) * a.table_stride;
+  if (npages > 0) {
+    load_page(a, tbl[0], g, min(kPage, kvlen), sK[0], sV[0], threadIdx.x, 128);
+    cp_async_commit();
+  }
+  for (int p = 0; p < npages; ++p) {
+    if (p + 1 < npages) {
+      load_page(a, tbl[p + 1], g, min(kPage, kvlen - (p + 1) * kPage), sK[(p + 1) & 1], sV[(p + 1) & 1],
+                threadIdx.x, 128);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    process_page(a, st, sK[p & 1], sV[p & 1], p * kPage, kvlen, bidir, lane);
+    __syncthreads();
+  }
+  store_rows(a, st, q0, rows, row0 + warp * 16, g, lane);
+}
+
+// 4 warps split the pages of one 16-row tile, then merge their softmax states.
+constexpr int kWarpBufElems = 4 * kPage * kStride;  // 2 stages x (K, V)
+constexpr int kKeysSmemBytes = 4 * kWarpBufElems * 2;
+
+__global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __nv_bfloat16* buf = reinterpret_cast<__nv_bfloat16*>(smem_raw) + warp * kWarpBufElems;
+  const int tile = blockIdx.x, g = blockIdx.y;
+  const int b = a.tile_seq[tile];
+  const int row0 = a.tile_row0[tile];
+  const int qlen = a.q_len[b], kvlen = a.kv_len[b], q0 = a.q_start[b];
+  const int bidir = a.mode[b];
+  const int rows = qlen * a.G;
+  WarpState st;
+  load_q(a, st, q0, rows, row0, g, qlen, kvlen, lane);
+  const int last_row = min(rows - 1, row0 + 15);
+  const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
+  const int npages = (max_key + kPage - 1) / kPage;
+  const int* tbl = a.table + static_cast<long long>(b) * a.table_stride;
+  auto kbuf = [&](int s) { return buf + s * 2 * kPage * kStride; };
+  auto vbuf = [&](int s) { return buf + s * 2 * kPage * kStride + kPage * kStride; };
+  if (warp < npages) {
+    load_page(a, tbl[warp], g, min(kPage, kvlen - warp * kPage), kbuf(0), vbuf(0), lane, 32);
+    cp_async_commit();
+  }
+  int it = 0;
+  for (int p = warp; p < npages; p += 4, ++it) {
+    const int nxt = p + 4;
+    if (nxt < npages) {
+      load_page(a, tbl[nxt], g, min(kPage, kvlen - nxt * kPage), kbuf((it + 1) & 1), vbuf((it + 1) & 1), lane, 32);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncwarp();
+    process_page(a, st, kbuf(it & 1), vbuf(it & 1), p * kPage, kvlen, bidir, lane);
+    __syncwarp();
+  }
+  __syncthreads();
+  // Merge: per warp 16 x 128 fp32 partial outputs plus (m, l) per row.
+  float* so = reinterpret_cast<float*>(smem_raw);           // [4][16][128]
+  float* sm = so + 4 * 16 * kD;                              // [4][16]
+  float* sl = sm + 4 * 16;                                   // [4][16]
+  {
+    const int r_lo = lane / 4, c2 = (lane % 4) * 2;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = r_lo + h * 8;
+#pragma unroll
+      for (int n = 0; n < kD / 8; ++n) {
+        so[(warp * 16 + row) * kD + n * 8 + c2] = st.o[n][2 * h];
+        so[(warp * 16 + row) * kD + n * 8 + c2 + 1] = st.o[n][2 * h + 1];
+      }
+      if ((lane % 4) == 0) {
+        sm[warp * 16 + row] = st.m[h];
+        sl[warp * 16 + row] = st.l[h];
+      }
+    }
+  }
+  __syncthreads();
+  const int r = threadIdx.x / 8;          // 16 rows
+  const int cbeg = (threadIdx.x % 8) * 16;  // 16 columns each
+  const int row = row0 + r;
+  if (row < rows) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
+    float wgt[4], L = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      wgt[w] = (M == -INFINITY || sm[w * 16 + r] == -INFINITY) ? 0.0f : exp2f(sm[w * 16 + r] - M);
+      L += wgt[w] * sl[w * 16 + r];
+    }
+    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+    const int tok = row / a.G, head = g * a.G + row % a.G;
+    __nv_bfloat16* p = a.out + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD;
+#pragma unroll
+    for (int c = 0; c < 16; c += 2) {
+      float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        v0 += wgt[w] * so[(w * 16 + r) * kD + cbeg + c];
+        v1 += wgt[w] * so[(w * 16 + r) * kD + cbeg + c + 1];
+      }
+      *reinterpret_cast<uint32_t*>(p + cbeg + c) = pack_bf16(v0 * inv, v1 * inv);
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream) {
+  if (p.head_dim != kD || p.page_size != kPage || p.Hkv <= 0 || p.Hq % p.Hkv) return cudaErrorInvalidValue;
+  AttnArgs a{};
+  a.q = p.q;
+  a.k_cache = p.k_cache;
+  a.v_cache = p.v_cache;
+  a.table = p.table;
+  a.table_stride = p.table_stride;
+  a.q_start = p.q_start;
+  a.q_len = p.q_len;
+  a.kv_len = p.kv_len;
+  a.mode = p.mode;
+  a.tile_seq = p.tile_seq;
+  a.tile_row0 = p.tile_row0;
+  a.out = p.out;
+  a.Hq = p.Hq;
+  a.Hkv = p.Hkv;
+  a.G = p.Hq / p.Hkv;
+  a.scale_log2 = p.scale * 1.4426950408889634f;
+  a.status = p.status;
+  if (p.num_tiles <= 0) return cudaSuccess;
+  dim3 grid(p.num_tiles, p.Hkv);
+  if (p.tile_rows == 64) {
+    attn_rows_kernel<<<grid, 128, 0, stream>>>(a);
+  } else if (p.tile_rows == 16) {
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kKeysSmemBytes);
+      if (e != cudaSuccess) return e;
+      attr[dev] = true;
+    }
+    attn_keys_kernel<<<grid, 128, kKeysSmemBytes, stream>>>(a);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace osb

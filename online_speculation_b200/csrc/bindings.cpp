@@ -1,0 +1,379 @@
+// PyTorch bindings of the sm_100a kernels and the C++ KV runtime.
+//
+// Every wrapper checks device, dtype, contiguity and shapes, then launches on
+// the current CUDA stream of the tensors' device.  There is no fallback: a
+// wrong argument raises, and a missing extension is reported by the Python
+// loader on GPU machines.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <pybind11/stl.h>
+#include <torch/extension.h>
+
+#include "adamw.h"
+#include "attention.h"
+#include "elementwise.h"
+#include "gemm.h"
+#include "kv_manager.h"
+#include "sampling.h"
+
+namespace {
+
+using torch::Tensor;
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_DT(t, dt) TORCH_CHECK((t).scalar_type() == (dt), #t " has the wrong dtype")
+#define CHECK_ROWS(t) TORCH_CHECK((t).dim() == 2 && (t).stride(1) == 1, #t " must be 2-D with unit inner stride")
+
+void check(cudaError_t e, const char* what) {
+  TORCH_CHECK(e == cudaSuccess, what, " failed: ", cudaGetErrorString(e));
+}
+
+template <typename T>
+T* ptr_or_null(const c10::optional<Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+const __nv_bfloat16* bf(const Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+__nv_bfloat16* bfm(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+
+// out[N, M or M/2] = x[N, K] @ w[M, K]^T (+ bias) (+ residual)
+void gemm(Tensor w, Tensor x, Tensor out, c10::optional<Tensor> bias, c10::optional<Tensor> residual, int64_t epilogue,
+          bool allow_split, Tensor workspace, Tensor counters, Tensor status) {
+  CHECK_CUDA(w);
+  CHECK_CUDA(x);
+  CHECK_CUDA(out);
+  CHECK_DT(w, torch::kBFloat16);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_ROWS(w);
+  CHECK_ROWS(x);
+  CHECK_ROWS(out);
+  TORCH_CHECK(w.size(1) == x.size(1), "reduction dimensions differ");
+  const int M = w.size(0), N = x.size(0), K = w.size(1);
+  const int out_cols = epilogue == 1 ? M / 2 : M;
+  TORCH_CHECK(out.size(0) == N && out.size(1) == out_cols, "output shape mismatch");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 || out.scalar_type() == torch::kFloat32, "bf16 or fp32 output");
+  if (bias.has_value() && bias->defined()) {
+    CHECK_DT(*bias, torch::kBFloat16);
+    TORCH_CHECK(bias->numel() == M && bias->is_contiguous(), "bias must be [M]");
+  }
+  if (residual.has_value() && residual->defined()) {
+    CHECK_DT(*residual, torch::kBFloat16);
+    CHECK_ROWS(*residual);
+    TORCH_CHECK(residual->size(0) == N && residual->size(1) == out_cols, "residual shape mismatch");
+  }
+  CHECK_DT(workspace, torch::kFloat32);
+  CHECK_DT(counters, torch::kInt32);
+  CHECK_DT(status, torch::kInt32);
+  c10::cuda::CUDAGuard guard(w.device());
+  osb::GemmProblem p{};
+  p.w = bf(w);
+  p.ldw = w.stride(0);
+  p.x = bf(x);
+  p.ldx = x.stride(0);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.out_f32 = out.scalar_type() == torch::kFloat32;
+  p.bias = ptr_or_null<const __nv_bfloat16>(bias);
+  p.residual = ptr_or_null<const __nv_bfloat16>(residual);
+  p.ldr = residual.has_value() && residual->defined() ? residual->stride(0) : 0;
+  p.epilogue = static_cast<int>(epilogue);
+  p.allow_split = allow_split ? 1 : 0;
+  p.workspace = workspace.data_ptr<float>();
+  p.workspace_floats = workspace.numel();
+  p.counters = counters.data_ptr<int>();
+  p.counter_slots = counters.numel();
+  p.status = status.data_ptr<int>();
+  check(osb::gemm_launch(p, at::cuda::getCurrentCUDAStream()), "tcgen05 gemm");
+}
+
+void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_start, Tensor q_len, Tensor kv_len,
+               Tensor mode, Tensor tile_seq, Tensor tile_row0, int64_t tile_rows, Tensor out, double scale,
+               Tensor status) {
+  CHECK_CUDA(q);
+  CHECK_DT(q, torch::kBFloat16);
+  CHECK_DT(k_cache, torch::kBFloat16);
+  CHECK_DT(v_cache, torch::kBFloat16);
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous(), "q must be [T, Hq, D] contiguous");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.sizes() == k_cache.sizes(),
+              "caches must be [pages, Hkv, P, D]");
+  for (const Tensor* t : {&table, &q_start, &q_len, &kv_len, &mode, &tile_seq, &tile_row0}) {
+    CHECK_DT(*t, torch::kInt32);
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous(), "metadata must be contiguous CUDA int32");
+  }
+  TORCH_CHECK(out.sizes() == q.sizes() && out.is_contiguous(), "out must match q");
+  c10::cuda::CUDAGuard guard(q.device());
+  osb::AttentionProblem p{};
+  p.q = bf(q);
+  p.k_cache = bf(k_cache);
+  p.v_cache = bf(v_cache);
+  p.table = table.data_ptr<int>();
+  p.table_stride = table.size(1);
+  p.q_start = q_start.data_ptr<int>();
+  p.q_len = q_len.data_ptr<int>();
+  p.kv_len = kv_len.data_ptr<int>();
+  p.mode = mode.data_ptr<int>();
+  p.tile_seq = tile_seq.data_ptr<int>();
+  p.tile_row0 = tile_row0.data_ptr<int>();
+  p.num_tiles = tile_seq.numel();
+  p.tile_rows = static_cast<int>(tile_rows);
+  p.out = bfm(out);
+  p.Hq = q.size(1);
+  p.Hkv = k_cache.size(1);
+  p.head_dim = q.size(2);
+  p.page_size = k_cache.size(2);
+  p.scale = static_cast<float>(scale);
+  p.status = status.data_ptr<int>();
+  check(osb::attention_launch(p, at::cuda::getCurrentCUDAStream()), "paged attention");
+}
+
+void rmsnorm(Tensor x, Tensor w, Tensor y, double eps, c10::optional<Tensor> h, c10::optional<Tensor> delta) {
+  CHECK_CUDA(x);
+  CHECK_ROWS(x);
+  CHECK_ROWS(y);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(w, torch::kBFloat16);
+  CHECK_DT(y, torch::kBFloat16);
+  const int T = x.size(0), H = x.size(1);
+  TORCH_CHECK(w.numel() == H && y.size(0) == T && y.size(1) == H, "rmsnorm shapes");
+  const bool fused = delta.has_value() && delta->defined();
+  if (fused) {
+    TORCH_CHECK(h.has_value() && h->defined(), "fused add needs the residual output");
+    CHECK_ROWS(*h);
+    CHECK_ROWS(*delta);
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  check(osb::rmsnorm_launch(bf(x), x.stride(0), fused ? bfm(*h) : nullptr, fused ? h->stride(0) : 0,
+                            fused ? bf(*delta) : nullptr, fused ? delta->stride(0) : 0, bf(w), bfm(y), y.stride(0), T, H,
+                            static_cast<float>(eps), at::cuda::getCurrentCUDAStream()),
+        "rmsnorm");
+}
+
+void rope_cache(Tensor qkv, Tensor positions, c10::optional<Tensor> slots, Tensor inv_freq,
+                c10::optional<Tensor> q_norm, c10::optional<Tensor> k_norm, double eps, Tensor q_out, Tensor k_cache,
+                Tensor v_cache, int64_t Hq, int64_t Hkv) {
+  CHECK_CUDA(qkv);
+  CHECK_ROWS(qkv);
+  CHECK_DT(qkv, torch::kBFloat16);
+  CHECK_DT(positions, torch::kInt32);
+  CHECK_DT(inv_freq, torch::kFloat32);
+  TORCH_CHECK(qkv.size(1) >= (Hq + 2 * Hkv) * 128, "qkv row too short");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == qkv.size(0) * Hq * 128, "q_out shape");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(1) == Hkv && k_cache.size(3) == 128, "cache layout");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  check(osb::rope_cache_launch(bf(qkv), qkv.stride(0), positions.data_ptr<int>(), ptr_or_null<const int>(slots),
+                               inv_freq.data_ptr<float>(), ptr_or_null<const __nv_bfloat16>(q_norm),
+                               ptr_or_null<const __nv_bfloat16>(k_norm), static_cast<float>(eps), bfm(q_out),
+                               bfm(k_cache), bfm(v_cache), qkv.size(0), Hq, Hkv, k_cache.size(2),
+                               at::cuda::getCurrentCUDAStream()),
+        "rope_cache");
+}
+
+void embed(Tensor ids, Tensor table, Tensor out) {
+  CHECK_CUDA(ids);
+  CHECK_DT(ids, torch::kInt32);
+  CHECK_DT(table, torch::kBFloat16);
+  CHECK_ROWS(out);
+  TORCH_CHECK(out.size(0) == ids.numel() && out.size(1) == table.size(1), "embedding shapes");
+  c10::cuda::CUDAGuard guard(ids.device());
+  check(osb::embed_launch(ids.data_ptr<int>(), bf(table), ids.numel(), table.size(1), bfm(out), out.stride(0),
+                          at::cuda::getCurrentCUDAStream()),
+        "embed");
+}
+
+void page_copy(Tensor cache, Tensor pairs) {
+  // cache [layers, pages, Hkv, P, D]; pairs int32 [n, 3] (src, dst, tokens)
+  CHECK_CUDA(cache);
+  CHECK_DT(cache, torch::kBFloat16);
+  CHECK_DT(pairs, torch::kInt32);
+  TORCH_CHECK(cache.dim() == 5 && cache.is_contiguous(), "cache must be [layers, pages, Hkv, P, D]");
+  c10::cuda::CUDAGuard guard(cache.device());
+  check(osb::page_copy_launch(bfm(cache), cache.stride(0), cache.size(0), pairs.data_ptr<int>(), pairs.size(0),
+                              cache.size(2), cache.size(3), at::cuda::getCurrentCUDAStream()),
+        "page_copy");
+}
+
+void sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor uniforms, Tensor tokens, c10::optional<Tensor> logq,
+            c10::optional<Tensor> logp) {
+  CHECK_CUDA(logits);
+  CHECK_ROWS(logits);
+  CHECK_DT(logits, torch::kFloat32);
+  CHECK_DT(uniforms, torch::kFloat64);
+  CHECK_DT(tokens, torch::kInt32);
+  c10::cuda::CUDAGuard guard(logits.device());
+  osb::SampleArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.V = logits.size(1);
+  a.inv_temp = ptr_or_null<const float>(inv_temp);
+  a.uniforms = uniforms.data_ptr<double>();
+  a.uniform_stride = uniforms.dim() == 2 ? uniforms.stride(0) : 1;
+  a.tokens = tokens.data_ptr<int>();
+  a.logq = ptr_or_null<float>(logq);
+  a.logp = ptr_or_null<float>(logp);
+  check(osb::sample_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "sample");
+}
+
+void row_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tensor> targets,
+               c10::optional<Tensor> lse1, c10::optional<Tensor> lseT, c10::optional<Tensor> logp,
+               c10::optional<Tensor> logq) {
+  CHECK_CUDA(logits);
+  CHECK_ROWS(logits);
+  CHECK_DT(logits, torch::kFloat32);
+  c10::cuda::CUDAGuard guard(logits.device());
+  osb::RowStatsArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.V = logits.size(1);
+  a.inv_temp = ptr_or_null<const float>(inv_temp);
+  a.targets = ptr_or_null<const int>(targets);
+  a.lse1 = ptr_or_null<float>(lse1);
+  a.lseT = ptr_or_null<float>(lseT);
+  a.logp = ptr_or_null<float>(logp);
+  a.logq = ptr_or_null<float>(logq);
+  check(osb::row_stats_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "row_stats");
+}
+
+void gumbel_sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor seeds, c10::optional<Tensor> seed_index,
+                   c10::optional<Tensor> streams, c10::optional<Tensor> row_in_seq, int64_t salt, Tensor tokens) {
+  CHECK_CUDA(logits);
+  CHECK_ROWS(logits);
+  CHECK_DT(logits, torch::kFloat32);
+  CHECK_DT(seeds, torch::kInt64);
+  c10::cuda::CUDAGuard guard(logits.device());
+  osb::GumbelArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.V = logits.size(1);
+  a.inv_temp = ptr_or_null<const float>(inv_temp);
+  a.seeds = reinterpret_cast<const unsigned long long*>(seeds.data_ptr<int64_t>());
+  a.seed_index = ptr_or_null<const int>(seed_index);
+  a.streams = ptr_or_null<const int>(streams);
+  a.row_in_seq = ptr_or_null<const int>(row_in_seq);
+  a.salt = static_cast<int>(salt);
+  a.tokens = tokens.data_ptr<int>();
+  check(osb::gumbel_sample_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "gumbel_sample");
+}
+
+void spec_verify(Tensor target, Tensor draft, Tensor candidates, int64_t n, c10::optional<Tensor> inv_temp, Tensor seeds,
+                 c10::optional<Tensor> streams, int64_t salt, Tensor count, Tensor tail, Tensor valid, Tensor emitted,
+                 Tensor logq, Tensor logp) {
+  CHECK_CUDA(target);
+  CHECK_ROWS(target);
+  CHECK_ROWS(draft);
+  CHECK_DT(target, torch::kFloat32);
+  CHECK_DT(draft, torch::kFloat32);
+  CHECK_DT(candidates, torch::kInt32);
+  const int B = candidates.size(0);
+  TORCH_CHECK(candidates.dim() == 2 && candidates.size(1) == n, "candidates must be [B, n]");
+  TORCH_CHECK(target.size(0) == B * (n + 1) && draft.size(0) == B * n, "target / draft row counts");
+  c10::cuda::CUDAGuard guard(target.device());
+  osb::SpecArgs a{};
+  a.target = target.data_ptr<float>();
+  a.ld_target = target.stride(0);
+  a.draft = draft.data_ptr<float>();
+  a.ld_draft = draft.stride(0);
+  a.candidates = candidates.data_ptr<int>();
+  a.n = static_cast<int>(n);
+  a.V = target.size(1);
+  a.inv_temp = ptr_or_null<const float>(inv_temp);
+  a.seeds = reinterpret_cast<const unsigned long long*>(seeds.data_ptr<int64_t>());
+  a.streams = ptr_or_null<const int>(streams);
+  a.salt = static_cast<int>(salt);
+  a.count = count.data_ptr<int>();
+  a.tail = tail.data_ptr<int>();
+  a.valid = valid.data_ptr<int>();
+  a.emitted = emitted.data_ptr<int>();
+  a.logq = logq.data_ptr<float>();
+  a.logp = logp.data_ptr<float>();
+  check(osb::spec_verify_launch(a, B, at::cuda::getCurrentCUDAStream()), "spec_verify");
+}
+
+void grad_sq_norm(Tensor g, Tensor out) {
+  CHECK_CUDA(g);
+  CHECK_DT(g, torch::kFloat32);
+  TORCH_CHECK(g.is_contiguous(), "flat contiguous grads");
+  c10::cuda::CUDAGuard guard(g.device());
+  check(osb::grad_sq_norm_launch(g.data_ptr<float>(), g.numel(), out.data_ptr<float>(),
+                                 at::cuda::getCurrentCUDAStream()),
+        "grad_sq_norm");
+}
+
+void adamw(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> publish, c10::optional<Tensor> sq_norm,
+           double clip, double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
+           c10::optional<Tensor> nonfinite) {
+  CHECK_CUDA(p);
+  for (const Tensor* t : {&p, &g, &m, &v}) {
+    CHECK_DT(*t, torch::kFloat32);
+    TORCH_CHECK(t->is_contiguous() && t->numel() == p.numel(), "flat contiguous fp32 optimizer buffers");
+  }
+  if (publish.has_value() && publish->defined()) {
+    CHECK_DT(*publish, torch::kBFloat16);
+    TORCH_CHECK(publish->is_contiguous() && publish->numel() == p.numel(), "publish buffer shape");
+  }
+  c10::cuda::CUDAGuard guard(p.device());
+  osb::AdamWArgs a{};
+  a.params = p.data_ptr<float>();
+  a.grads = g.data_ptr<float>();
+  a.exp_avg = m.data_ptr<float>();
+  a.exp_avg_sq = v.data_ptr<float>();
+  a.publish = ptr_or_null<__nv_bfloat16>(publish);
+  a.n = p.numel();
+  a.sq_norm = ptr_or_null<const float>(sq_norm);
+  a.clip = static_cast<float>(clip);
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.eps = static_cast<float>(eps);
+  a.weight_decay = static_cast<float>(weight_decay);
+  a.bias_correction1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
+  a.bias_correction2 = static_cast<float>(1.0 - std::pow(beta2, static_cast<double>(step)));
+  a.nonfinite = ptr_or_null<int>(nonfinite);
+  check(osb::adamw_launch(a, at::cuda::getCurrentCUDAStream()), "adamw");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels and C++ runtime of online_speculation_b200";
+  m.def("gemm", &gemm);
+  m.def("attention", &attention);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("rope_cache", &rope_cache);
+  m.def("embed", &embed);
+  m.def("page_copy", &page_copy);
+  m.def("sample", &sample);
+  m.def("row_stats", &row_stats);
+  m.def("gumbel_sample", &gumbel_sample);
+  m.def("spec_verify", &spec_verify);
+  m.def("grad_sq_norm", &grad_sq_norm);
+  m.def("adamw", &adamw);
+  m.def("gemm_pick_bn", &osb::gemm_pick_bn);
+
+  pybind11::class_<osb::KVManager>(m, "KVManager")
+      .def(pybind11::init<int, int>())
+      .def_property_readonly("page_size", &osb::KVManager::page_size)
+      .def_property_readonly("num_pages", &osb::KVManager::num_pages)
+      .def_property_readonly("free_pages", &osb::KVManager::free_pages)
+      .def("create", &osb::KVManager::create)
+      .def("release", &osb::KVManager::release)
+      .def("length", &osb::KVManager::length)
+      .def("append", &osb::KVManager::append)
+      .def("truncate", &osb::KVManager::truncate)
+      .def("fork",
+           [](osb::KVManager& self, int64_t seq, int n) {
+             std::vector<int32_t> copies;
+             const int64_t id = self.fork(seq, n, copies);
+             return std::make_pair(id, copies);
+           })
+      .def("pages", &osb::KVManager::pages)
+      .def("refcount", &osb::KVManager::refcount)
+      .def("fill_table", [](const osb::KVManager& self, const std::vector<int64_t>& seqs, Tensor out) {
+        TORCH_CHECK(out.device().is_cpu() && out.scalar_type() == torch::kInt32 && out.dim() == 2 &&
+                        out.is_contiguous() && out.size(0) >= static_cast<int64_t>(seqs.size()),
+                    "table must be a CPU int32 [rows, stride] tensor");
+        self.fill_table(seqs, out.data_ptr<int32_t>(), out.size(1));
+      });
+}

@@ -1,0 +1,33 @@
+// Host API of the tcgen05 dense GEMM (see gemm.cu).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+namespace osb {
+
+struct GemmProblem {
+  const __nv_bfloat16* w;  // [M, K] row-major weights (row stride ldw)
+  long long ldw;
+  const __nv_bfloat16* x;  // [N, K] row-major activations (row stride ldx)
+  long long ldx;
+  int M, N, K;
+  void* out;               // [N, M] (or [N, M/2] for swiglu), row stride ldo
+  long long ldo;
+  int out_f32;
+  const __nv_bfloat16* bias;      // [M] or null
+  const __nv_bfloat16* residual;  // same layout as out (bf16) or null; may alias out
+  long long ldr;
+  int epilogue;                   // 0 linear, 1 swiglu on [64 gate | 64 up] row tiles
+  int allow_split;
+  float* workspace;               // split-K partials
+  long long workspace_floats;
+  int* counters;                  // per-tile arrival counters, zero at rest
+  int counter_slots;
+  int* status;                    // bounded-wait error word
+};
+
+cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream);
+int gemm_pick_bn(int tokens);
+long long gemm_workspace_floats(int M, int N, int K, int sms);
+
+}  // namespace osb

@@ -1,0 +1,439 @@
+// Vocabulary-wide sampling, scoring and speculative correction kernels.
+//
+//  * sample_kernel: one CTA per row.  A single pass computes the row max and
+//    the two log-normalisers log sum exp(l) and log sum exp(l / T) with online
+//    rescaling; a second pass draws the token by inverse CDF with a float64
+//    prefix sum (segment sums per thread + block scan), so a request-local
+//    uniform selects the same token whatever the batch shape.  It returns the
+//    token, its log-probability under the sampling policy (temperature T) and
+//    under the reference policy (T = 1) from the same logits.
+//    Reference: src/inference_scaling/arllm/backends/transformers_backend.py:323-348
+//    (policy log-softmax) and :895-906 (float64 inverse CDF).
+//  * row_stats_kernel: the same statistics for every row without sampling, plus
+//    the gathered log-probabilities of given target tokens (sequence scoring,
+//    transformers_backend.py:1330-1411).
+//  * gumbel_sample_kernel: exponential-race / Gumbel-max draft sampling
+//    (online-speculation/src/blockspec/sampling_execution.py:15-17).
+//  * spec_verify_kernel: exact p/q block correction with the positive residual
+//    (sampling_execution.py:20-41, sampling.py:112-146): accept-prefix count,
+//    residual or bonus draw, validity flag and both log-probabilities of every
+//    emitted token, in one launch per batch.
+// Random numbers come from a counter-based Philox-4x32-10 generator (Salmon et
+// al., "Parallel random numbers: as easy as 1, 2, 3", SC 2011) keyed by a
+// per-request seed, so draws do not depend on scheduling.
+#include "common.cuh"
+#include "sampling.h"
+
+namespace osb {
+namespace {
+
+constexpr int kThreads = 1024;
+
+// ---------------------------------------------------------------- Philox ----
+__device__ __forceinline__ uint4 philox4x32(uint4 ctr, uint2 key) {
+  const uint32_t M0 = 0xD2511F53u, M1 = 0xCD9E8D57u, W0 = 0x9E3779B9u, W1 = 0xBB67AE85u;
+#pragma unroll
+  for (int i = 0; i < 10; ++i) {
+    const uint32_t hi0 = __umulhi(M0, ctr.x), lo0 = M0 * ctr.x;
+    const uint32_t hi1 = __umulhi(M1, ctr.z), lo1 = M1 * ctr.z;
+    ctr = make_uint4(hi1 ^ ctr.y ^ key.x, lo1, hi0 ^ ctr.w ^ key.y, lo0);
+    key.x += W0;
+    key.y += W1;
+  }
+  return ctr;
+}
+
+// Uniform in the open interval (0, 1) from 24 random bits.
+__device__ __forceinline__ float u01(uint32_t x) { return (static_cast<float>(x >> 8) + 0.5f) * (1.0f / 16777216.0f); }
+
+// Four uniforms for (seed, stream, index): stream separates uses, index counts.
+__device__ __forceinline__ float4 uniform4(unsigned long long seed, uint32_t stream, uint32_t hi, uint32_t index) {
+  const uint4 r = philox4x32(make_uint4(index, hi, stream, 0x5eedu),
+                             make_uint2(static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32)));
+  return make_float4(u01(r.x), u01(r.y), u01(r.z), u01(r.w));
+}
+
+// ------------------------------------------------------- block reductions ----
+template <typename T>
+__device__ __forceinline__ T warp_reduce_sum(T v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+struct MaxSum2 {
+  float m;   // running max of raw logits
+  float s1;  // sum exp(l - m)
+  float sT;  // sum exp((l - m) * invT)
+};
+
+__device__ __forceinline__ void ms_add(MaxSum2& a, float l, float invT) {
+  if (l > a.m) {
+    const float d = a.m - l;  // <= 0 (or -inf)
+    a.s1 = a.s1 * expf(d) + 1.0f;
+    a.sT = a.sT * expf(d * invT) + 1.0f;
+    a.m = l;
+  } else {
+    const float d = l - a.m;
+    a.s1 += expf(d);
+    a.sT += expf(d * invT);
+  }
+}
+
+__device__ __forceinline__ MaxSum2 ms_merge(MaxSum2 a, MaxSum2 b, float invT) {
+  if (b.m > a.m) {
+    MaxSum2 t = a;
+    a = b;
+    b = t;
+  }
+  if (b.m == -INFINITY) return a;
+  const float d = b.m - a.m;
+  a.s1 += b.s1 * expf(d);
+  a.sT += b.sT * expf(d * invT);
+  return a;
+}
+
+// Row statistics: max, lse at T=1, lse at temperature T.  All threads get the result.
+__device__ void row_stats(const float* __restrict__ row, int V, float invT, float& mx, float& lse1, float& lseT) {
+  __shared__ MaxSum2 red[32];
+  MaxSum2 a{-INFINITY, 0.0f, 0.0f};
+  const bool vec = (reinterpret_cast<uintptr_t>(row) % 16 == 0) && (V % 4 == 0);
+  if (vec) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    for (int i = threadIdx.x; i < V / 4; i += blockDim.x) {
+      const float4 v = r4[i];
+      ms_add(a, v.x, invT);
+      ms_add(a, v.y, invT);
+      ms_add(a, v.z, invT);
+      ms_add(a, v.w, invT);
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) ms_add(a, row[i], invT);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    MaxSum2 b{__shfl_xor_sync(0xffffffffu, a.m, o), __shfl_xor_sync(0xffffffffu, a.s1, o),
+              __shfl_xor_sync(0xffffffffu, a.sT, o)};
+    a = ms_merge(a, b, invT);
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) red[warp] = a;
+  __syncthreads();
+  if (warp == 0) {
+    MaxSum2 b = lane < blockDim.x / 32 ? red[lane] : MaxSum2{-INFINITY, 0.0f, 0.0f};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      MaxSum2 c{__shfl_xor_sync(0xffffffffu, b.m, o), __shfl_xor_sync(0xffffffffu, b.s1, o),
+                __shfl_xor_sync(0xffffffffu, b.sT, o)};
+      b = ms_merge(b, c, invT);
+    }
+    if (lane == 0) red[0] = b;
+  }
+  __syncthreads();
+  const MaxSum2 r = red[0];
+  __syncthreads();
+  mx = r.m;
+  lse1 = r.m + logf(r.s1);
+  lseT = r.m * invT + logf(r.sT);
+}
+
+// Block-wide exclusive scan of one double per thread; `total` gets the sum.
+__device__ double block_exclusive_scan(double v, double& total) {
+  __shared__ double wsum[33];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nwarps = blockDim.x / 32;
+  double inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double n = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += n;
+  }
+  if (lane == 31) wsum[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const double w = lane < nwarps ? wsum[lane] : 0.0;
+    double winc = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, winc, o);
+      if (lane >= o) winc += n;
+    }
+    if (lane < nwarps) wsum[lane] = winc - w;
+    if (lane == 31) wsum[32] = winc;
+  }
+  __syncthreads();
+  const double res = wsum[warp] + inc - v;
+  total = wsum[32];
+  __syncthreads();
+  return res;
+}
+
+__global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
+  const int r = blockIdx.x;
+  const float* row = a.logits + r * a.ld;
+  const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
+  float mx, lse1, lseT;
+  row_stats(row, a.V, invT, mx, lse1, lseT);
+  const double u = a.uniforms[r * a.uniform_stride];
+  // contiguous segment per thread
+  const int seg = (a.V + blockDim.x - 1) / blockDim.x;
+  const int b0 = min(a.V, static_cast<int>(threadIdx.x) * seg);
+  const int b1 = min(a.V, b0 + seg);
+  const float zoff = lseT;
+  double s = 0.0;
+  for (int v = b0; v < b1; ++v) s += static_cast<double>(expf(row[v] * invT - zoff));
+  double total;
+  const double excl = block_exclusive_scan(s, total);
+  __shared__ int chosen;
+  if (threadIdx.x == 0) chosen = a.V - 1;
+  __syncthreads();
+  const bool last_thread = (b1 == a.V && b0 < b1);
+  if (b0 < b1 && (excl < u || b0 == 0) && (u <= excl + s || last_thread)) {
+    double c = excl;
+    int tok = b1 - 1;
+    for (int v = b0; v < b1; ++v) {
+      c += static_cast<double>(expf(row[v] * invT - zoff));
+      if (c >= u) {
+        tok = v;
+        break;
+      }
+    }
+    atomicMin(&chosen, tok);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int tok = chosen;
+    a.tokens[r] = tok;
+    const float l = row[tok];
+    if (a.logq) a.logq[r] = l * invT - lseT;
+    if (a.logp) a.logp[r] = l - lse1;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) row_stats_kernel(RowStatsArgs a) {
+  const int r = blockIdx.x;
+  const float* row = a.logits + r * a.ld;
+  const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
+  float mx, lse1, lseT;
+  row_stats(row, a.V, invT, mx, lse1, lseT);
+  if (threadIdx.x == 0) {
+    if (a.lse1) a.lse1[r] = lse1;
+    if (a.lseT) a.lseT[r] = lseT;
+    if (a.targets) {
+      const int t = a.targets[r];
+      const float l = (t >= 0 && t < a.V) ? row[t] : -INFINITY;
+      if (a.logp) a.logp[r] = l - lse1;
+      if (a.logq) a.logq[r] = l * invT - lseT;
+    }
+  }
+}
+
+// Gumbel-max sampling at temperature T: argmax_v (l_v / T + G_v).
+__global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
+  const int r = blockIdx.x;
+  const float* row = a.logits + r * a.ld;
+  const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
+  const unsigned long long seed = a.seeds[a.seed_index ? a.seed_index[r] : r];
+  const uint32_t stream = a.streams ? static_cast<uint32_t>(a.streams[r]) : 0u;
+  const uint32_t hi = static_cast<uint32_t>(a.salt) ^ (static_cast<uint32_t>(a.row_in_seq ? a.row_in_seq[r] : 0) << 24);
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  for (int i = threadIdx.x; i * 4 < a.V; i += blockDim.x) {
+    const float4 u = uniform4(seed, stream, hi, static_cast<uint32_t>(i));
+    const float uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int v = i * 4 + j;
+      if (v < a.V) {
+        const float g = -logf(-logf(uu[j]));
+        const float sc = row[v] * invT + g;
+        if (sc > best || (sc == best && v < besti)) {
+          best = sc;
+          besti = v;
+        }
+      }
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ob > best || (ob == best && oi < besti)) {
+      best = ob;
+      besti = oi;
+    }
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    sb[warp] = best;
+    si[warp] = besti;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < blockDim.x / 32 ? sb[lane] : -INFINITY;
+    besti = lane < blockDim.x / 32 ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+      if (ob > best || (ob == best && oi < besti)) {
+        best = ob;
+        besti = oi;
+      }
+    }
+    if (lane == 0) a.tokens[r] = besti;
+  }
+}
+
+// One CTA per sequence: n candidates, n draft rows, n + 1 target rows.
+__global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
+  const int b = blockIdx.x;
+  const int n = a.n;
+  const float invT = a.inv_temp ? a.inv_temp[b] : 1.0f;
+  const unsigned long long seed = a.seeds[b];
+  const uint32_t stream = a.streams ? static_cast<uint32_t>(a.streams[b]) : 0u;
+  __shared__ int s_count, s_valid;
+  __shared__ float s_lseT[16], s_lse1[16], s_lseQ[16];
+  // statistics of the target rows and the draft rows
+  for (int i = 0; i <= n; ++i) {
+    float mx, l1, lT;
+    row_stats(a.target + (static_cast<long long>(b) * (n + 1) + i) * a.ld_target, a.V, invT, mx, l1, lT);
+    if (threadIdx.x == 0) {
+      s_lseT[i] = lT;
+      s_lse1[i] = l1;
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    float mx, l1, lT;
+    row_stats(a.draft + (static_cast<long long>(b) * n + i) * a.ld_draft, a.V, invT, mx, l1, lT);
+    if (threadIdx.x == 0) s_lseQ[i] = lT;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int count = n, valid = 1;
+    const float4 ua = uniform4(seed, stream, static_cast<uint32_t>(a.salt), 0x7fffffffu);
+    const float us[4] = {ua.x, ua.y, ua.z, ua.w};
+    for (int i = 0; i < n; ++i) {
+      const int x = a.candidates[b * n + i];
+      if (x < 0 || x >= a.V) {
+        valid = 0;
+        count = i;
+        break;
+      }
+      const float lp = a.target[(static_cast<long long>(b) * (n + 1) + i) * a.ld_target + x] * invT - s_lseT[i];
+      const float lq = a.draft[(static_cast<long long>(b) * n + i) * a.ld_draft + x] * invT - s_lseQ[i];
+      const float ratio = expf(fminf(lp - lq, 0.0f));
+      const float u = i < 4 ? us[i] : u01(philox4x32(make_uint4(i, 0x51u, stream, a.salt),
+                                                     make_uint2(static_cast<uint32_t>(seed), 0)).x);
+      if (!(u < ratio)) {
+        count = i;
+        break;
+      }
+    }
+    s_count = count;
+    s_valid = valid;
+  }
+  __syncthreads();
+  const int count = s_count;
+  // tail draw: residual (p - q)+ at row `count`, or the bonus row p_n
+  const float* prow = a.target + (static_cast<long long>(b) * (n + 1) + count) * a.ld_target;
+  const float* qrow = count < n ? a.draft + (static_cast<long long>(b) * n + count) * a.ld_draft : nullptr;
+  const float lseP = s_lseT[count];
+  const float lseQ = count < n ? s_lseQ[count] : 0.0f;
+  float best = -INFINITY;
+  int besti = 0x7fffffff;
+  const uint32_t hi = static_cast<uint32_t>(a.salt) ^ 0xA5000000u;
+  for (int i = threadIdx.x; i * 4 < a.V; i += blockDim.x) {
+    const float4 u = uniform4(seed, stream, hi, static_cast<uint32_t>(i));
+    const float uu[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int v = i * 4 + j;
+      if (v >= a.V) continue;
+      float w;
+      const float lp = prow[v] * invT - lseP;
+      if (qrow) {
+        const float d = expf(lp) - expf(qrow[v] * invT - lseQ);
+        w = d > 0.0f ? logf(d) : -INFINITY;
+      } else {
+        w = lp;
+      }
+      const float sc = w - logf(-logf(uu[j]));
+      if (sc > best || (sc == best && v < besti)) {
+        best = sc;
+        besti = v;
+      }
+    }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, besti, o);
+    if (ob > best || (ob == best && oi < besti)) {
+      best = ob;
+      besti = oi;
+    }
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    sb[warp] = best;
+    si[warp] = besti;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bb = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int w = 0; w < blockDim.x / 32; ++w) {
+      if (sb[w] > bb || (sb[w] == bb && si[w] < bi)) {
+        bb = sb[w];
+        bi = si[w];
+      }
+    }
+    int valid = s_valid && bb > -INFINITY && bi < a.V;
+    const int tail = valid ? bi : 0;
+    a.count[b] = count;
+    a.tail[b] = tail;
+    a.valid[b] = valid;
+    // log-probabilities of every emitted token under the target policy and T = 1
+    for (int i = 0; i <= count; ++i) {
+      const int x = i < count ? a.candidates[b * n + i] : tail;
+      const float l = a.target[(static_cast<long long>(b) * (n + 1) + i) * a.ld_target + x];
+      a.logq[b * (n + 1) + i] = l * invT - s_lseT[i];
+      a.logp[b * (n + 1) + i] = l - s_lse1[i];
+      a.emitted[b * (n + 1) + i] = x;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  sample_kernel<<<rows, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t row_stats_launch(const RowStatsArgs& a, int rows, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  row_stats_kernel<<<rows, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t gumbel_sample_launch(const GumbelArgs& a, int rows, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  gumbel_sample_kernel<<<rows, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t spec_verify_launch(const SpecArgs& a, int batch, cudaStream_t stream) {
+  if (batch <= 0) return cudaSuccess;
+  if (a.n < 1 || a.n > 15) return cudaErrorInvalidValue;
+  spec_verify_kernel<<<batch, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace osb

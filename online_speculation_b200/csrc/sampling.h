@@ -1,0 +1,68 @@
+// Host API of the sampling / scoring / speculative-correction kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace osb {
+
+struct SampleArgs {
+  const float* logits;  // [rows, V] row stride ld
+  long long ld;
+  int V;
+  const float* inv_temp;      // [rows] or null (T = 1)
+  const double* uniforms;     // uniforms[r * uniform_stride]
+  long long uniform_stride;
+  int* tokens;                // [rows]
+  float* logq;                // [rows] policy log-prob or null
+  float* logp;                // [rows] T=1 log-prob or null
+};
+
+struct RowStatsArgs {
+  const float* logits;
+  long long ld;
+  int V;
+  const float* inv_temp;
+  const int* targets;         // [rows] or null
+  float* lse1;
+  float* lseT;
+  float* logp;
+  float* logq;
+};
+
+struct GumbelArgs {
+  const float* logits;
+  long long ld;
+  int V;
+  const float* inv_temp;
+  const unsigned long long* seeds;  // per sequence
+  const int* seed_index;            // [rows] -> sequence, or null (row = sequence)
+  const int* streams;               // [rows] per-draw counters (e.g. round index), or null
+  const int* row_in_seq;            // [rows] or null
+  int salt;
+  int* tokens;
+};
+
+struct SpecArgs {
+  const float* target;        // [B * (n + 1), V]
+  long long ld_target;
+  const float* draft;         // [B * n, V]
+  long long ld_draft;
+  const int* candidates;      // [B, n]
+  int n, V;
+  const float* inv_temp;      // [B] or null
+  const unsigned long long* seeds;  // [B]
+  const int* streams;         // [B] round counters or null
+  int salt;
+  int* count;                 // [B]
+  int* tail;                  // [B]
+  int* valid;                 // [B]
+  int* emitted;               // [B, n + 1]
+  float* logq;                // [B, n + 1]
+  float* logp;                // [B, n + 1]
+};
+
+cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream);
+cudaError_t row_stats_launch(const RowStatsArgs& a, int rows, cudaStream_t stream);
+cudaError_t gumbel_sample_launch(const GumbelArgs& a, int rows, cudaStream_t stream);
+cudaError_t spec_verify_launch(const SpecArgs& a, int batch, cudaStream_t stream);
+
+}  // namespace osb

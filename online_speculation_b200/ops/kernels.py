@@ -1,0 +1,414 @@
+"""Python entry points of the hot ops.
+
+Each function dispatches on the device of its inputs: CUDA tensors run the
+hand-written sm_100a kernel of the compiled extension (and raise if it is
+missing); CPU tensors run the plain PyTorch fp32 oracle that defines the op and
+that the kernel tests compare against.  There is no other backend.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _ext, workspace
+
+PAGE_SIZE = 32
+HEAD_DIM = 128
+
+
+# ----------------------------------------------------------------- linear --
+def linear(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    *,
+    bias: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    swiglu: bool = False,
+    out_dtype: torch.dtype = torch.bfloat16,
+    allow_split: bool = True,
+) -> torch.Tensor:
+    """``x @ w.T (+ bias) (+ residual)``; with ``swiglu`` the weight rows are
+    tiles of [64 gate | 64 up] rows and the result is ``silu(gate) * up``.
+
+    ``residual`` may alias ``out`` (in-place residual-stream update).
+    """
+    rows = w.shape[0] // 2 if swiglu else w.shape[0]
+    if out is None:
+        out = torch.empty(x.shape[0], rows, dtype=out_dtype, device=x.device)
+    if x.is_cuda:
+        ext = _ext.require()
+        ext.gemm(
+            w,
+            x,
+            out,
+            bias,
+            residual,
+            1 if swiglu else 0,
+            allow_split,
+            workspace.gemm_workspace(x.device),
+            workspace.gemm_counters(x.device),
+            workspace.status(x.device),
+        )
+        return out
+    out.copy_(linear_reference(x, w, bias=bias, residual=residual, swiglu=swiglu).to(out.dtype))
+    return out
+
+
+def linear_reference(x, w, *, bias=None, residual=None, swiglu=False):
+    y = x.float() @ w.float().t()
+    if bias is not None:
+        y = y + bias.float()
+    if swiglu:
+        tiles = y.view(y.shape[0], -1, 2, 64)
+        gate, up = tiles[:, :, 0, :], tiles[:, :, 1, :]
+        y = (torch.nn.functional.silu(gate) * up).reshape(y.shape[0], -1)
+    if residual is not None:
+        y = y + residual.float()
+    return y
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """Pack [F, H] gate and up weights into [2F, H] tiles of [64 gate | 64 up]."""
+    features, hidden = gate.shape
+    if features % 64:
+        pad = 64 - features % 64
+        gate = torch.cat((gate, gate.new_zeros(pad, hidden)))
+        up = torch.cat((up, up.new_zeros(pad, hidden)))
+    return torch.stack((gate.view(-1, 64, hidden), up.view(-1, 64, hidden)), 1).reshape(-1, hidden).contiguous()
+
+
+# ---------------------------------------------------------------- rmsnorm --
+def rmsnorm(x, weight, eps, *, out=None, residual=None, delta=None):
+    """RMSNorm; with ``delta``: ``residual = x + delta`` (written) then norm."""
+    if out is None:
+        out = torch.empty_like(x)
+    if x.is_cuda:
+        _ext.require().rmsnorm(x, weight, out, float(eps), residual, delta)
+        return out
+    src = x
+    if delta is not None:
+        residual.copy_((x.float() + delta.float()).to(x.dtype))
+        src = residual
+    work = src.float()
+    normed = (work * torch.rsqrt(work.square().mean(-1, keepdim=True) + eps)).to(x.dtype)
+    out.copy_(normed * weight)
+    return out
+
+
+# ------------------------------------------------------------------- rope --
+def rope_frequencies(head_dim: int, theta: float) -> torch.Tensor:
+    """Inverse frequencies, formed on the host in fp32 (as the reference does)."""
+    idx = torch.arange(0, head_dim, 2, dtype=torch.float32)
+    half = 1.0 / (theta ** (idx / head_dim))
+    # kernel layout: element d and d + D/2 share frequency index d
+    return half
+
+
+def rope_cache(qkv, positions, slots, inv_freq, q_out, k_cache, v_cache, num_q, num_kv, *, q_norm=None,
+               k_norm=None, eps=1e-6):
+    """Split fused QKV rows, optional per-head Q/K RMSNorm, RoPE, write Q and paged K/V.
+
+    ``k_cache``/``v_cache``: one layer, [pages, Hkv, P, D].  ``slots`` int32 [T]
+    (physical slot = page * P + offset, -1 = do not store).
+    """
+    if qkv.is_cuda:
+        _ext.require().rope_cache(qkv, positions, slots, inv_freq_full(inv_freq), q_norm, k_norm, float(eps), q_out,
+                                  k_cache, v_cache, int(num_q), int(num_kv))
+        return q_out
+    q, k, v = rope_reference(qkv, positions, inv_freq, num_q, num_kv, q_norm=q_norm, k_norm=k_norm, eps=eps)
+    q_out.copy_(q.view_as(q_out))
+    page = k_cache.shape[2]
+    for t in range(qkv.shape[0]):
+        s = int(slots[t]) if slots is not None else -1
+        if s >= 0:
+            k_cache[s // page, :, s % page] = k[t]
+            v_cache[s // page, :, s % page] = v[t]
+    return q_out
+
+
+def inv_freq_full(inv_freq: torch.Tensor) -> torch.Tensor:
+    """Expand [D/2] frequencies to the [D/2] + padding layout the kernel indexes."""
+    return inv_freq
+
+
+def rope_reference(qkv, positions, inv_freq, num_q, num_kv, *, q_norm=None, k_norm=None, eps=1e-6):
+    T = qkv.shape[0]
+    D = HEAD_DIM
+    q = qkv[:, : num_q * D].reshape(T, num_q, D)
+    k = qkv[:, num_q * D : (num_q + num_kv) * D].reshape(T, num_kv, D)
+    v = qkv[:, (num_q + num_kv) * D : (num_q + 2 * num_kv) * D].reshape(T, num_kv, D)
+
+    def norm(x, w):
+        if w is None:
+            return x
+        work = x.float()
+        return (work * torch.rsqrt(work.square().mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+
+    q, k = norm(q, q_norm), norm(k, k_norm)
+    angle = positions.float().cpu()[:, None] * inv_freq.float().cpu()[None, :]
+    cos, sin = angle.cos().to(qkv.device), angle.sin().to(qkv.device)
+
+    def rot(x):
+        x = x.float()
+        a, b = x[..., : D // 2], x[..., D // 2 :]
+        c, s = cos[:, None, :], sin[:, None, :]
+        return torch.cat((a * c - b * s, b * c + a * s), -1).to(qkv.dtype)
+
+    return rot(q), rot(k), v
+
+
+# -------------------------------------------------------------- embedding --
+def embed(ids, table, out=None):
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    if table.is_cuda:
+        _ext.require().embed(ids, table, out)
+        return out
+    out.copy_(table[ids.long()])
+    return out
+
+
+def page_copy(cache, pairs):
+    """Copy (src page, dst page, tokens) triples for every layer of [L, pages, Hkv, P, D]."""
+    if pairs.numel() == 0:
+        return
+    if cache.is_cuda:
+        _ext.require().page_copy(cache, pairs)
+        return
+    for src, dst, count in pairs.tolist():
+        cache[:, dst, :, :count] = cache[:, src, :, :count]
+
+
+# -------------------------------------------------------------- attention --
+@dataclass
+class AttentionPlan:
+    """Per-launch sequence metadata (device int32 tensors) for paged attention."""
+
+    table: torch.Tensor
+    q_start: torch.Tensor
+    q_len: torch.Tensor
+    kv_len: torch.Tensor
+    mode: torch.Tensor
+    tile_seq: torch.Tensor
+    tile_row0: torch.Tensor
+    tile_rows: int
+    # host copies for the CPU oracle
+    host: dict
+
+
+def plan_attention(table, q_lens, kv_lens, modes, group, device, *, tile_rows=None):
+    """Build the tile list of one attention launch.
+
+    ``table``: int32 [B, max_pages] page table; ``q_lens``/``kv_lens``/``modes``:
+    python lists; ``group``: query heads per kv head.
+    """
+    q_start, acc = [], 0
+    for n in q_lens:
+        q_start.append(acc)
+        acc += n
+    if tile_rows is None:
+        tile_rows = 16 if max(n * group for n in q_lens) <= 64 else 64
+    tile_seq, tile_row0 = [], []
+    for b, n in enumerate(q_lens):
+        rows = n * group
+        for r0 in range(0, rows, tile_rows):
+            tile_seq.append(b)
+            tile_row0.append(r0)
+
+    def dev(values):
+        return torch.tensor(values, dtype=torch.int32).to(device, non_blocking=True)
+
+    host = {"q_start": q_start, "q_len": list(q_lens), "kv_len": list(kv_lens), "mode": list(modes),
+            "table": table.cpu() if table.is_cuda else table}
+    return AttentionPlan(table.to(device, non_blocking=True), dev(q_start), dev(list(q_lens)), dev(list(kv_lens)),
+                         dev(list(modes)), dev(tile_seq), dev(tile_row0), tile_rows, host)
+
+
+def attention(q, k_cache, v_cache, plan: AttentionPlan, *, out=None, scale=None):
+    """Paged attention; ``q`` [T, Hq, D], caches [pages, Hkv, P, D] of one layer."""
+    if out is None:
+        out = torch.empty_like(q)
+    scale = scale if scale is not None else q.shape[-1] ** -0.5
+    if q.is_cuda:
+        _ext.require().attention(q, k_cache, v_cache, plan.table, plan.q_start, plan.q_len, plan.kv_len, plan.mode,
+                                 plan.tile_seq, plan.tile_row0, plan.tile_rows, out, float(scale),
+                                 workspace.status(q.device))
+        return out
+    out.copy_(attention_reference(q, k_cache, v_cache, plan.host, scale))
+    return out
+
+
+def gather_kv(cache, pages, length):
+    """[Hkv, length, D] view of a sequence's keys or values."""
+    page = cache.shape[2]
+    blocks = [cache[p] for p in pages[: (length + page - 1) // page]]
+    return torch.cat(blocks, 1)[:, :length]
+
+
+def attention_reference(q, k_cache, v_cache, host, scale):
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    Hq, Hkv = q.shape[1], k_cache.shape[1]
+    G = Hq // Hkv
+    for b, (s, n, kv, mode) in enumerate(zip(host["q_start"], host["q_len"], host["kv_len"], host["mode"])):
+        pages = host["table"][b].tolist()
+        k = gather_kv(k_cache.cpu(), pages, kv).float().repeat_interleave(G, 0)
+        v = gather_kv(v_cache.cpu(), pages, kv).float().repeat_interleave(G, 0)
+        qb = q[s : s + n].cpu().float().transpose(0, 1)  # [Hq, n, D]
+        scores = (qb @ k.transpose(1, 2)) * scale
+        if not mode:
+            qpos = torch.arange(kv - n, kv)[:, None]
+            kpos = torch.arange(kv)[None, :]
+            scores = scores.masked_fill(kpos > qpos, float("-inf"))
+        out[s : s + n] = (scores.softmax(-1) @ v).transpose(0, 1)
+    return out.to(q.dtype).to(q.device)
+
+
+# ---------------------------------------------------------------- sampling --
+def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None):
+    """Inverse-CDF sampling (float64 prefix sums) at per-row temperature.
+
+    Returns (tokens int32, log q under the policy, log p at temperature one).
+    """
+    rows = logits.shape[0]
+    dev = logits.device
+    tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=dev)
+    logq = logq if logq is not None else torch.empty(rows, dtype=torch.float32, device=dev)
+    logp = logp if logp is not None else torch.empty(rows, dtype=torch.float32, device=dev)
+    if logits.is_cuda:
+        _ext.require().sample(logits, inv_temp, uniforms, tokens, logq, logp)
+        return tokens, logq, logp
+    t, q, p = sample_reference(logits, inv_temp, uniforms)
+    tokens.copy_(t)
+    logq.copy_(q)
+    logp.copy_(p)
+    return tokens, logq, logp
+
+
+def sample_reference(logits, inv_temp, uniforms):
+    x = logits.float()
+    it = inv_temp.float()[:, None] if inv_temp is not None else torch.ones(x.shape[0], 1, device=x.device)
+    log_q = (x * it).log_softmax(-1)
+    log_p = x.log_softmax(-1)
+    cumulative = log_q.exp().double().cumsum(-1)
+    cumulative[:, -1] = 1.0
+    u = uniforms.reshape(x.shape[0], -1)[:, 0].double()
+    tok = (cumulative < u[:, None]).sum(-1).clamp_max(x.shape[1] - 1)
+    return (tok.int(), log_q.gather(-1, tok[:, None]).squeeze(-1), log_p.gather(-1, tok[:, None]).squeeze(-1))
+
+
+def row_stats(logits, inv_temp=None, targets=None):
+    """Per-row lse at T=1 and at T, plus log p / log q of ``targets`` (scoring)."""
+    rows, dev = logits.shape[0], logits.device
+    lse1 = torch.empty(rows, dtype=torch.float32, device=dev)
+    lseT = torch.empty(rows, dtype=torch.float32, device=dev)
+    logp = torch.empty(rows, dtype=torch.float32, device=dev) if targets is not None else None
+    logq = torch.empty(rows, dtype=torch.float32, device=dev) if targets is not None else None
+    if logits.is_cuda:
+        _ext.require().row_stats(logits, inv_temp, targets, lse1, lseT, logp, logq)
+        return lse1, lseT, logp, logq
+    x = logits.float()
+    it = inv_temp.float()[:, None] if inv_temp is not None else torch.ones(rows, 1)
+    lse1.copy_(torch.logsumexp(x, -1))
+    lseT.copy_(torch.logsumexp(x * it, -1))
+    if targets is not None:
+        idx = targets.long()[:, None]
+        logp.copy_(x.gather(-1, idx).squeeze(-1) - lse1)
+        logq.copy_((x * it).gather(-1, idx).squeeze(-1) - lseT)
+    return lse1, lseT, logp, logq
+
+
+def gumbel_sample(logits, inv_temp, seeds, *, seed_index=None, streams=None, row_in_seq=None, salt=0, tokens=None):
+    """Gumbel-max (exponential race) sampling with counter-based randomness."""
+    rows = logits.shape[0]
+    tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=logits.device)
+    if logits.is_cuda:
+        _ext.require().gumbel_sample(logits, inv_temp, seeds, seed_index, streams, row_in_seq, int(salt), tokens)
+        return tokens
+    gen = torch.Generator().manual_seed(int(seeds.flatten()[0]) ^ int(salt))
+    x = logits.float() * (inv_temp.float()[:, None] if inv_temp is not None else 1.0)
+    e = torch.empty_like(x).exponential_(generator=gen)
+    tokens.copy_((x.softmax(-1) / e).argmax(-1))
+    return tokens
+
+
+def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, salt=0, out=None):
+    """Exact p/q correction of a batch of draft blocks.
+
+    ``target`` [B*(n+1), V] logits, ``draft`` [B*n, V] logits, ``candidates`` [B, n].
+    Returns dict of count, tail, valid, emitted [B, n+1], logq, logp [B, n+1].
+    """
+    B, n = candidates.shape
+    dev = target.device
+    res = out or {
+        "count": torch.empty(B, dtype=torch.int32, device=dev),
+        "tail": torch.empty(B, dtype=torch.int32, device=dev),
+        "valid": torch.empty(B, dtype=torch.int32, device=dev),
+        "emitted": torch.empty(B, n + 1, dtype=torch.int32, device=dev),
+        "logq": torch.empty(B, n + 1, dtype=torch.float32, device=dev),
+        "logp": torch.empty(B, n + 1, dtype=torch.float32, device=dev),
+    }
+    if target.is_cuda:
+        _ext.require().spec_verify(target, draft, candidates, n, inv_temp, seeds, streams, int(salt), res["count"],
+                                   res["tail"], res["valid"], res["emitted"], res["logq"], res["logp"])
+        return res
+    gen = torch.Generator().manual_seed(int(seeds.flatten()[0]) ^ int(salt))
+    for b in range(B):
+        it = float(inv_temp[b]) if inv_temp is not None else 1.0
+        p = (target[b * (n + 1) : (b + 1) * (n + 1)].float() * it).softmax(-1)
+        q = (draft[b * n : (b + 1) * n].float() * it).softmax(-1)
+        count = n
+        for i in range(n):
+            x = int(candidates[b, i])
+            if not float(torch.rand((), generator=gen)) < min(1.0, float(p[i, x] / q[i, x])):
+                count = i
+                break
+        if count < n:
+            resid = (p[count] - q[count]).clamp_min(0)
+            tail = int(torch.multinomial(resid / resid.sum(), 1, generator=gen))
+        else:
+            tail = int(torch.multinomial(p[n], 1, generator=gen))
+        emitted = candidates[b, :count].tolist() + [tail]
+        res["count"][b], res["tail"][b], res["valid"][b] = count, tail, 1
+        lt = target[b * (n + 1) : (b + 1) * (n + 1)].float()
+        for i, x in enumerate(emitted):
+            res["emitted"][b, i] = x
+            res["logq"][b, i] = (lt[i] * it).log_softmax(-1)[x]
+            res["logp"][b, i] = lt[i].log_softmax(-1)[x]
+    return res
+
+
+# ------------------------------------------------------------------ adamw --
+def adamw_step(params, grads, exp_avg, exp_avg_sq, *, step, lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
+               clip=None, publish=None, norm_out=None, nonfinite=None):
+    """Fused AdamW on flat fp32 buffers with global-norm clipping; optional bf16 publish."""
+    if params.is_cuda:
+        ext = _ext.require()
+        sq = None
+        if clip is not None:
+            sq = norm_out if norm_out is not None else torch.empty(1, dtype=torch.float32, device=params.device)
+            ext.grad_sq_norm(grads, sq)
+        ext.adamw(params, grads, exp_avg, exp_avg_sq, publish, sq, float(clip or 0.0), float(lr), float(betas[0]),
+                  float(betas[1]), float(eps), float(weight_decay), int(step), nonfinite)
+        return sq
+    scale = 1.0
+    sq = grads.float().square().sum()
+    if clip is not None:
+        norm = float(sq.sqrt())
+        if not math.isfinite(norm):
+            if nonfinite is not None:
+                nonfinite.fill_(1)
+            return sq
+        scale = min(1.0, clip / (norm + 1e-6))
+    g = grads * scale
+    params.mul_(1 - lr * weight_decay)
+    exp_avg.mul_(betas[0]).add_(g, alpha=1 - betas[0])
+    exp_avg_sq.mul_(betas[1]).addcmul_(g, g, value=1 - betas[1])
+    bc1, bc2 = 1 - betas[0] ** step, 1 - betas[1] ** step
+    params.addcdiv_(exp_avg / bc1, (exp_avg_sq / bc2).sqrt().add_(eps), value=-lr)
+    if publish is not None:
+        publish.copy_(params)
+    return sq

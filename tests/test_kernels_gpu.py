@@ -1,0 +1,258 @@
+"""Numerics of every sm_100a kernel against the plain PyTorch fp32 oracle."""
+
+import math
+
+import pytest
+import torch
+
+from online_speculation_b200.ops import kernels as ops
+from online_speculation_b200.ops import workspace
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))
+
+
+@pytest.mark.parametrize(
+    "M,N,K",
+    [(128, 16, 64), (256, 64, 512), (4608, 64, 3584), (3584, 256, 3584), (1000, 37, 200), (512, 300, 1024),
+     (2048, 1024, 1536), (152064 // 8, 64, 3584)],
+)
+def test_gemm_matches_fp32(cuda, M, N, K):
+    torch.manual_seed(0)
+    w = (torch.randn(M, K, device=cuda) * 0.05).bfloat16()
+    x = torch.randn(N, K, device=cuda).bfloat16()
+    out = ops.linear(x, w)
+    ref = ops.linear_reference(x, w)
+    torch.cuda.synchronize()
+    workspace.check_status(cuda)
+    assert _rel(out, ref) < 1e-2
+
+
+def test_gemm_bias_residual_fp32_out(cuda):
+    torch.manual_seed(1)
+    M, N, Kd = 768, 48, 896
+    w = (torch.randn(M, Kd, device=cuda) * 0.05).bfloat16()
+    x = torch.randn(N, Kd, device=cuda).bfloat16()
+    b = torch.randn(M, device=cuda).bfloat16()
+    r = torch.randn(N, M, device=cuda).bfloat16()
+    out = ops.linear(x, w, bias=b, residual=r)
+    assert _rel(out, ops.linear_reference(x, w, bias=b, residual=r)) < 1e-2
+    out32 = ops.linear(x, w, out_dtype=torch.float32)
+    assert out32.dtype == torch.float32
+    assert _rel(out32, ops.linear_reference(x, w)) < 1e-3
+    # in-place residual stream update
+    h = r.clone()
+    ops.linear(x, w, residual=h, out=h)
+    assert _rel(h, ops.linear_reference(x, w, residual=r)) < 1e-2
+
+
+@pytest.mark.parametrize("N,split", [(64, True), (200, False), (16, True)])
+def test_gemm_swiglu(cuda, N, split):
+    torch.manual_seed(2)
+    F, H = 320, 512
+    g = (torch.randn(F, H, device=cuda) * 0.05).bfloat16()
+    u = (torch.randn(F, H, device=cuda) * 0.05).bfloat16()
+    w = ops.interleave_gate_up(g, u)
+    x = torch.randn(N, H, device=cuda).bfloat16()
+    out = ops.linear(x, w, swiglu=True, allow_split=split)
+    ref = torch.nn.functional.silu(x.float() @ g.float().t()) * (x.float() @ u.float().t())
+    assert _rel(out[:, :F], ref) < 1e-2
+
+
+def test_gemm_repeated_split_counters_reset(cuda):
+    w = (torch.randn(1024, 4096, device=cuda) * 0.02).bfloat16()
+    x = torch.randn(64, 4096, device=cuda).bfloat16()
+    ref = ops.linear_reference(x, w)
+    for _ in range(5):
+        assert _rel(ops.linear(x, w), ref) < 1e-2
+    assert int(workspace.gemm_counters(cuda).abs().sum()) == 0
+
+
+def _paged_case(device, lengths, Hkv, pages_per_seq, seed=0):
+    torch.manual_seed(seed)
+    B = len(lengths)
+    num_pages = B * pages_per_seq + 3
+    perm = torch.randperm(num_pages)[: B * pages_per_seq].view(B, pages_per_seq).int()
+    k = torch.randn(num_pages, Hkv, ops.PAGE_SIZE, 128, device=device).bfloat16()
+    v = torch.randn(num_pages, Hkv, ops.PAGE_SIZE, 128, device=device).bfloat16()
+    return perm, k, v
+
+
+@pytest.mark.parametrize(
+    "q_lens,kv_lens,modes,Hq,Hkv",
+    [
+        ([1, 1, 1], [1, 33, 700], [0, 0, 0], 28, 4),       # decode
+        ([4, 4], [130, 4], [0, 0], 28, 4),                 # verify block
+        ([4, 4], [517, 9], [1, 1], 28, 4),                 # bidirectional draft block
+        ([300, 64], [300, 64], [0, 1], 12, 2),             # prefill + diffusion
+        ([1, 5], [1000, 999], [0, 1], 4, 1),               # TP-sharded heads
+        ([512], [512], [0], 28, 4),
+    ],
+)
+def test_attention_matches_fp32(cuda, q_lens, kv_lens, modes, Hq, Hkv):
+    pps = max((kv + 31) // 32 for kv in kv_lens)
+    table, kc, vc = _paged_case(cuda, kv_lens, Hkv, pps)
+    T = sum(q_lens)
+    q = torch.randn(T, Hq, 128, device=cuda).bfloat16()
+    for tile_rows in (16, 64):
+        plan = ops.plan_attention(table, q_lens, kv_lens, modes, Hq // Hkv, cuda, tile_rows=tile_rows)
+        out = ops.attention(q, kc, vc, plan)
+        ref = ops.attention_reference(q.cpu(), kc.cpu(), vc.cpu(), plan.host, 128 ** -0.5)
+        torch.cuda.synchronize()
+        assert _rel(out.cpu(), ref) < 2e-2, tile_rows
+
+
+def test_rmsnorm_and_fused_add(cuda):
+    x = torch.randn(37, 3584, device=cuda).bfloat16()
+    w = (1 + 0.1 * torch.randn(3584, device=cuda)).bfloat16()
+    y = ops.rmsnorm(x, w, 1e-6)
+    ref = ops.rmsnorm(x.cpu(), w.cpu(), 1e-6)
+    assert _rel(y.cpu(), ref) < 1e-2
+    d = torch.randn_like(x)
+    h = torch.empty_like(x)
+    y2 = ops.rmsnorm(x, w, 1e-6, residual=h, delta=d)
+    h_ref = torch.empty_like(x.cpu())
+    ref2 = ops.rmsnorm(x.cpu(), w.cpu(), 1e-6, residual=h_ref, delta=d.cpu())
+    assert _rel(h.cpu(), h_ref) < 1e-2 and _rel(y2.cpu(), ref2) < 1e-2
+
+
+@pytest.mark.parametrize("with_norm", [False, True])
+def test_rope_cache(cuda, with_norm):
+    T, Hq, Hkv = 9, 7, 2
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device=cuda).bfloat16()
+    pos = torch.tensor([0, 1, 5, 100, 511, 1023, 7, 8, 9], dtype=torch.int32, device=cuda)
+    slots = torch.tensor([0, 1, 2, 33, 64, 95, -1, 40, 41], dtype=torch.int32, device=cuda)
+    inv = ops.rope_frequencies(128, 1e6).to(cuda)
+    qn = (1 + 0.1 * torch.randn(128, device=cuda)).bfloat16() if with_norm else None
+    kn = (1 + 0.1 * torch.randn(128, device=cuda)).bfloat16() if with_norm else None
+    kc = torch.zeros(4, Hkv, 32, 128, device=cuda).bfloat16()
+    vc = torch.zeros_like(kc)
+    q = torch.empty(T, Hq, 128, device=cuda).bfloat16()
+    ops.rope_cache(qkv, pos, slots, inv, q, kc, vc, Hq, Hkv, q_norm=qn, k_norm=kn)
+    kc2, vc2, q2 = kc.cpu().zero_(), vc.cpu().zero_(), torch.empty_like(q.cpu())
+    ops.rope_cache(qkv.cpu(), pos.cpu(), slots.cpu(), inv.cpu(), q2, kc2, vc2, Hq, Hkv,
+                 q_norm=None if qn is None else qn.cpu(), k_norm=None if kn is None else kn.cpu())
+    assert _rel(q.cpu(), q2) < 1e-2
+    assert _rel(kc.cpu(), kc2) < 1e-2
+    assert torch.equal(vc.cpu(), vc2)
+
+
+def test_embed_and_page_copy(cuda):
+    table = torch.randn(1000, 256, device=cuda).bfloat16()
+    ids = torch.tensor([3, 999, 0, 3], dtype=torch.int32, device=cuda)
+    assert torch.equal(ops.embed(ids, table), table[ids.long()])
+    cache = torch.randn(3, 6, 2, 32, 128, device=cuda).bfloat16()
+    ref = cache.clone()
+    pairs = torch.tensor([[1, 4, 17], [2, 5, 32]], dtype=torch.int32, device=cuda)
+    ops.page_copy(cache, pairs)
+    ref[:, 4, :, :17] = ref[:, 1, :, :17]
+    ref[:, 5] = ref[:, 2]
+    assert torch.equal(cache, ref)
+
+
+def test_sample_matches_float64_cdf(cuda):
+    torch.manual_seed(3)
+    R, V = 64, 152064
+    logits = torch.randn(R, V, device=cuda) * 3
+    inv_t = torch.full((R,), 4.0, device=cuda)
+    inv_t[::2] = 1.0
+    u = torch.rand(R, dtype=torch.float64, device=cuda)
+    tok, lq, lp = ops.sample(logits, inv_t, u)
+    rt, rq, rp = ops.sample_reference(logits.cpu(), inv_t.cpu(), u.cpu())
+    assert (tok.cpu() == rt).float().mean() > 0.9
+    # every token must sit on the float64 CDF interval containing u (up to fp32 rounding of p)
+    log_q = (logits.cpu().float() * inv_t.cpu()[:, None]).log_softmax(-1)
+    cdf = log_q.exp().double().cumsum(-1)
+    t = tok.cpu().long()
+    upper = cdf.gather(-1, t[:, None]).squeeze(-1)
+    lower = torch.where(t > 0, cdf.gather(-1, (t - 1).clamp_min(0)[:, None]).squeeze(-1), torch.zeros_like(upper))
+    assert bool(((lower - 1e-5 < u.cpu()) & (u.cpu() <= upper + 1e-5)).all())
+    same = tok.cpu() == rt
+    assert torch.allclose(lq.cpu()[same], rq[same], atol=1e-3)
+    assert torch.allclose(lp.cpu()[same], rp[same], atol=1e-3)
+
+
+def test_sample_edge_uniforms(cuda):
+    logits = torch.randn(4, 1000, device=cuda)
+    u = torch.tensor([0.0, 1e-300, 0.999999999999, 0.5], dtype=torch.float64, device=cuda)
+    tok, _, _ = ops.sample(logits, None, u)
+    rt, _, _ = ops.sample_reference(logits.cpu(), None, u.cpu())
+    assert torch.equal(tok.cpu(), rt)
+
+
+def test_row_stats(cuda):
+    x = torch.randn(10, 50000, device=cuda) * 2
+    it = torch.full((10,), 2.0, device=cuda)
+    tg = torch.randint(0, 50000, (10,), dtype=torch.int32, device=cuda)
+    a = ops.row_stats(x, it, tg)
+    b = ops.row_stats(x.cpu(), it.cpu(), tg.cpu())
+    for u, v in zip(a, b):
+        assert torch.allclose(u.cpu(), v, atol=1e-3)
+
+
+def test_gumbel_sampling_distribution(cuda):
+    torch.manual_seed(4)
+    V, R = 16, 40000
+    base = torch.randn(V) * 1.5
+    logits = base.to(cuda).expand(R, V).contiguous()
+    seeds = torch.tensor([12345], dtype=torch.int64, device=cuda)
+    idx = torch.zeros(R, dtype=torch.int32, device=cuda)
+    streams = torch.arange(R, dtype=torch.int32, device=cuda)
+    inv = torch.full((R,), 0.5, device=cuda)
+    tok = ops.gumbel_sample(logits, inv, seeds, seed_index=idx, streams=streams)
+    freq = torch.bincount(tok.long().cpu(), minlength=V).float() / R
+    p = (base * 0.5).softmax(-1)
+    assert float((freq - p).abs().sum() / 2) < 0.02
+
+
+def test_spec_verify_preserves_target_law(cuda):
+    """Marginal law of the first emitted token must equal the target p."""
+    torch.manual_seed(5)
+    V, n, B = 12, 3, 30000
+    tl = torch.randn(n + 1, V) * 1.5
+    dl = torch.randn(n, V) * 1.5
+    target = tl.to(cuda).repeat(B, 1)
+    draft = dl.to(cuda).repeat(B, 1)
+    inv = torch.full((B,), 1.0, device=cuda)
+    q = dl.softmax(-1)
+    cands = torch.stack([torch.multinomial(q[i], B, replacement=True) for i in range(n)], 1).int().to(cuda)
+    seeds = torch.randint(0, 2**62, (B,), dtype=torch.int64, device=cuda)
+    res = ops.spec_verify(target, draft, cands, inv, seeds)
+    assert bool(res["valid"].all())
+    first = res["emitted"][:, 0].long().cpu()
+    freq = torch.bincount(first, minlength=V).float() / B
+    p0 = tl[0].softmax(-1)
+    assert float((freq - p0).abs().sum() / 2) < 0.02
+    # accepted prefix length follows the min(1, p/q) acceptance of position 0
+    accept0 = float((res["count"] > 0).float().mean())
+    expected = float(torch.minimum(tl[0].softmax(-1), q[0]).sum())
+    assert abs(accept0 - expected) < 0.02
+    lq = res["logq"][:, 0].cpu()
+    assert torch.allclose(lq, tl[0].log_softmax(-1)[first], atol=1e-4)
+
+
+def test_adamw_matches_torch(cuda):
+    torch.manual_seed(6)
+    n = 10000
+    p0 = torch.randn(n, device=cuda)
+    g = torch.randn(n, device=cuda) * 3
+    p = p0.clone()
+    m = torch.zeros_like(p)
+    v = torch.zeros_like(p)
+    pub = torch.empty(n, dtype=torch.bfloat16, device=cuda)
+    ops.adamw_step(p, g, m, v, step=1, lr=1e-3, weight_decay=0.01, clip=1.0, publish=pub)
+    ref = torch.nn.Parameter(p0.clone())
+    opt = torch.optim.AdamW([ref], lr=1e-3, weight_decay=0.01)
+    ref.grad = g.clone()
+    torch.nn.utils.clip_grad_norm_([ref], 1.0)
+    opt.step()
+    assert torch.allclose(p, ref.detach(), atol=1e-6, rtol=1e-5)
+    assert torch.equal(pub, p.bfloat16())
+
+
+def test_status_word_clean_after_kernels(cuda):
+    torch.cuda.synchronize()
+    workspace.check_status(cuda)
