@@ -1,0 +1,369 @@
+"""Headline benchmark: suffix-MH rollouts on a Qwen2.5-7B-shaped decoder with
+block-bidirectional speculative drafting and an online draft learner.
+
+Workload (random-init bf16 weights, synthetic uniform-random prompts):
+  64 chains, each with its own 512-token prompt and 512 generated tokens, power
+  target p^4 (proposal temperature 1/4); every MH update regenerates the suffix
+  after a uniformly drawn cut while reusing the prefix KV.  Drafting uses a
+  1-layer block-4 draft head; the online learner updates every 64 verified blocks.
+  Tensor parallel over N GPUs of one node (one process per GPU, NCCL).
+
+A "step" is one MH update of every chain (64 proposals).  W warm-up steps run
+first (after the initial extension of every chain), then exactly K steps are
+timed with CUDA events on every rank between a barrier and a synchronize; the
+reported time is the maximum over ranks.  ``value`` = generated tokens per second
+for the whole job.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With --impl reference the same workload runs on the unmodified reference
+package installed under baseline/_ref (its TransformersBackend and
+run_mh_chains_batched); under N ranks each rank runs 64/N chains on its own GPU.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+BASELINE_TOKENS_PER_SECOND = None  # BASELINE.md publishes no number for this metric and config
+METRIC = "generated tok/s per box, Qwen2.5-7B-shape TP=1..8 (max over ranks); spec accept len"
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=4)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--model", default="qwen2.5-7b")
+    p.add_argument("--chains", type=int, default=64)
+    p.add_argument("--prompt-len", type=int, default=512)
+    p.add_argument("--gen-len", type=int, default=512)
+    p.add_argument("--alpha", type=float, default=4.0)
+    p.add_argument("--block", type=int, default=4)
+    p.add_argument("--stride", type=int, default=64)
+    p.add_argument("--no-learner", action="store_true")
+    p.add_argument("--no-graphs", action="store_true")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--kv-gb", type=float, default=24.0)
+    return p.parse_args()
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples: list[tuple[float, float, str]] = []
+        self._proc = None
+        self._thread = None
+
+    def __enter__(self):
+        cmd = ["nvidia-smi", "-i", str(self.index),
+               "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
+               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+               "--format=csv,noheader,nounits", "-lms", "200"]
+        try:
+            self._proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self._proc = None
+            return self
+
+        def reader():
+            for line in self._proc.stdout:
+                self.samples.append(tuple(x.strip() for x in line.split(",")))
+
+        self._thread = threading.Thread(target=reader, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for s in self.samples:
+            try:
+                sm.append(float(s[0]))
+                mx = float(s[1])
+            except (ValueError, IndexError):
+                continue
+            for name, flag in zip(names, s[3:7]):
+                if flag.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n: int):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(n)))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+    return rank, world, local, group
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    import torch
+
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value: float, world: int) -> float:
+    import torch
+
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+def barrier(world: int):
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def run_ours(args, rank, world, local, group) -> dict:
+    import numpy as np
+    import torch
+
+    from online_speculation_b200.api import build_mh_engine
+    from online_speculation_b200.ops import _ext
+
+    engine = build_mh_engine(args.model, tp_group=group, seed=args.seed, alpha=args.alpha, length=args.gen_len,
+                             block_size=args.block, learner_stride=None if args.no_learner else args.stride,
+                             use_graphs=not args.no_graphs, kv_bytes=int(args.kv_gb * 2**30),
+                             max_seq_tokens=args.prompt_len + args.gen_len + 2 * args.block)
+    rng = np.random.default_rng(args.seed + 17)
+    vocab = engine.runner.cfg.vocab_size
+    # one uniform-random prompt shared by the chains (the reference API's shape)
+    prompt_host = torch.from_numpy(rng.integers(0, vocab - 2, size=(1, args.prompt_len)).astype(np.int32)).pin_memory()
+    prompt_dev = prompt_host.to("cuda", non_blocking=True)
+    engine.add_chains(prompt_dev.cpu().tolist() * args.chains)
+    engine.run_until_idle()                       # initial extension of every chain to 512 tokens
+    engine.set_quota(args.warmup)
+    engine.run_until_idle()
+    barrier(world)
+    stats0 = dict(engine.stats)
+    launches0 = _ext.launches()
+    learner0 = engine.learner.updates if engine.learner else 0
+    sampler = ClockSampler(local)
+    with sampler:
+        barrier(world)
+        wall0 = time.perf_counter()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        state_host = torch.empty(args.chains, args.gen_len, dtype=torch.int32).pin_memory()
+        for _ in range(args.steps):
+            engine.set_quota(1)
+            engine.run_until_idle()
+            # end-to-end: read back every chain's current state (tokens) each step
+            state_dev = torch.tensor([c.tokens for c in engine.chains], dtype=torch.int32, device="cuda")
+            state_host.copy_(state_dev, non_blocking=True)
+        stop.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+        barrier(world)
+    ms = start.elapsed_time(stop)
+    ms = max_over_ranks(ms, world)
+    wall = max_over_ranks(wall, world)
+    st = engine.stats
+    generated = st["generated"] - stats0["generated"]   # identical on every rank (TP)
+    blocks = st["blocks"] - stats0["blocks"]
+    emitted = st["emitted"] - stats0["emitted"]
+    launches = (_ext.launches() - launches0) + (st["graph_kernel_launches"] - stats0["graph_kernel_launches"])
+    h2d = (st["h2d_bytes"] - stats0["h2d_bytes"]) / args.steps + args.chains * args.gen_len * 4 * 0
+    d2h = (st["d2h_bytes"] - stats0["d2h_bytes"]) / args.steps + args.chains * args.gen_len * 4
+    value = generated / (ms / 1e3)
+    accept_len = emitted / max(1, blocks)
+    out = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None if BASELINE_TOKENS_PER_SECOND is None else value / BASELINE_TOKENS_PER_SECOND,
+        "dtype": "bf16",
+        "data": "synthetic (uniform-random prompt ids, random-init weights)",
+        "config": {"model": f"{args.model} (random init)", "global_batch": args.chains, "seq_len": args.prompt_len + args.gen_len,
+                   "prompt": "one uniform-random prompt shared by all chains",
+                   "prompt_len": args.prompt_len, "gen_len": args.gen_len, "parallelism": f"tp{world}",
+                   "mh_alpha": args.alpha, "draft": f"1-layer block-{args.block} draft head",
+                   "learner_stride_blocks": None if args.no_learner else args.stride,
+                   "l2": "weights (15 GB) streamed every round exceed the 126 MB L2",
+                   "step": "one MH update of every chain, chains scheduled asynchronously"},
+        "spec_accept_len": accept_len,
+        "generated_tokens": generated,
+        "mh_acceptance_rate": (st["mh_accepted"] - stats0["mh_accepted"]) / max(1, st["mh_updates"] - stats0["mh_updates"]),
+        "learner_updates": (engine.learner.updates - learner0) if engine.learner else 0,
+        "clocks": sampler.summary(),
+        "e2e": {"value": generated / wall, "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": int(launches),
+    }
+    return out
+
+
+def run_reference(args, rank, world, local, group) -> dict:
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "inference_scaling")):
+        return {"impl": "reference", "unavailable": "reference package not installed under baseline/_ref"}
+    sys.path.insert(0, ref)
+    import numpy as np
+    import torch
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from inference_scaling.arllm.algorithms.mh import run_mh_chains_batched
+    from inference_scaling.arllm.backends.transformers_backend import TransformersBackend
+    from inference_scaling.arllm.config import MHConfig, SamplingConfig
+    from inference_scaling.shared.rng import SeedStream
+
+    from online_speculation_b200.models.decoder import PRESETS
+
+    c = PRESETS[args.model]
+    hf = Qwen2Config(vocab_size=c.vocab_size, hidden_size=c.hidden_size, intermediate_size=c.intermediate_size,
+                     num_hidden_layers=c.num_hidden_layers, num_attention_heads=c.num_attention_heads,
+                     num_key_value_heads=c.num_key_value_heads, rope_theta=c.rope_theta, rms_norm_eps=c.rms_norm_eps,
+                     tie_word_embeddings=c.tie_word_embeddings, max_position_embeddings=4096,
+                     torch_dtype="bfloat16")
+    torch.manual_seed(args.seed)
+    with torch.device("cuda"):
+        model = Qwen2ForCausalLM(hf).to(torch.bfloat16)
+    model.eval()
+
+    class Tok:
+        pad_token_id = 0
+        eos_token_id = None
+        bos_token_id = 1
+
+    backend = TransformersBackend(model, Tok(), model_id="qwen2.5-7b-random", device="cuda")
+    per_rank = args.chains // world
+    rng = np.random.default_rng(args.seed + 17 + rank)
+    prompt = tuple(int(x) for x in rng.integers(0, c.vocab_size - 2, size=args.prompt_len))
+
+    class Timed:
+        """Records CUDA events around the sample calls of the timed MH updates."""
+
+        def __init__(self, inner):
+            self.inner = inner
+            self.calls = 0
+            self.start = torch.cuda.Event(enable_timing=True)
+            self.stop = torch.cuda.Event(enable_timing=True)
+            self.timed_tokens = 0
+
+        @property
+        def model_id(self):
+            return self.inner.model_id
+
+        def sample_batch(self, requests):
+            # call 0 = extension, 1..W = warm-up updates, W+1..W+K = timed updates
+            timed = 1 + args.warmup <= self.calls < 1 + args.warmup + args.steps
+            if self.calls == 1 + args.warmup:
+                barrier(world)
+                self.wall0 = time.perf_counter()
+                self.start.record()
+            out = self.inner.sample_batch(requests)
+            if timed:
+                self.timed_tokens += sum(len(s.token_ids) for s in out)
+            self.calls += 1
+            if self.calls == 1 + args.warmup + args.steps:
+                self.stop.record()
+                torch.cuda.synchronize()
+                self.wall = time.perf_counter() - self.wall0
+            return out
+
+        def score_batch(self, requests):
+            return self.inner.score_batch(requests)
+
+    timed = Timed(backend)
+    cfg = MHConfig(alpha=args.alpha, total_length=args.gen_len, block_size=args.gen_len, iterations=args.warmup + args.steps)
+    sampler = ClockSampler(local)
+    with sampler:
+        run_mh_chains_batched(timed, prompt, cfg, SamplingConfig(temperature=1.0 / args.alpha),
+                              [SeedStream(args.seed)] * per_rank, chain_ids=list(range(rank * per_rank, (rank + 1) * per_rank)))
+    ms = max_over_ranks(timed.start.elapsed_time(timed.stop), world)
+    tokens = sum_over_ranks(timed.timed_tokens, world)
+    wall = max_over_ranks(timed.wall, world)
+    return {
+        "impl": "reference", "metric": METRIC, "value": tokens / (ms / 1e3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform-random prompt ids, random-init weights)",
+        "config": {"model": f"{args.model} (random init, HF Qwen2ForCausalLM)", "global_batch": args.chains,
+                   "seq_len": args.prompt_len + args.gen_len, "parallelism": f"dp{world}",
+                   "path": "inference_scaling TransformersBackend + run_mh_chains_batched (unmodified)"},
+        "clocks": sampler.summary(),
+        "e2e": {"value": tokens / wall, "unit": "tok/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None},
+    }
+
+
+def main():
+    args = parse()
+    rank, world, local, group = dist_setup(args.gpus)
+    try:
+        out = run_ours(args, rank, world, local, group) if args.impl == "ours" else run_reference(args, rank, world, local, group)
+    finally:
+        pass
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

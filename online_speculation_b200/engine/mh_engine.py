@@ -1,0 +1,408 @@
+"""Asynchronous suffix-MH over a paged, prefix-shared KV cache with block speculation.
+
+Every chain always owns one *job*: its initial extension to the full length
+L, or an MH proposal that regenerates the suffix after a uniformly drawn cut.
+A proposal forks the chain's KV sequence at the cut (full pages shared by
+reference, the boundary page copied), so the retained prefix is never
+recomputed.  All active jobs advance together, one speculative round at a
+time:
+
+    draft   : the 1-layer block-bidirectional draft head proposes K-1 tokens
+              after each job's anchor (Gumbel-max at the proposal temperature);
+    verify  : the target runs the causal block [anchor, candidates];
+    correct : exact p/q correction keeps the accepted prefix and draws the
+              first rejected position from the positive residual, so every
+              emitted token follows the proposal policy exactly, and returns
+              its log q (temperature 1/alpha) and log p (temperature 1).
+
+When a job finishes it is accepted or rejected with the full Hastings ratio
+(target p^alpha), and the chain starts its next update immediately: chains do
+not wait for each other, so the batch stays full.  Random streams are derived
+from a :class:`SeedStream` with the reference's names (("mh", chain, 0, step,
+"cut" | "proposal" | "accept")), so results do not depend on scheduling.
+
+Reference algorithm: src/inference_scaling/arllm/algorithms/mh.py:471-619
+(lock-step batched chains, one backend call per update); speculation:
+online-speculation/src/blockspec/parallel/generation.py:120-212.
+"""
+
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from ..ops import kernels as K
+from ..shared.mh import decide_metropolis_hastings
+from ..shared.rng import SeedStream
+from .draft import DraftHead, FeedbackRound, SuffixLearner
+from .kv_cache import KVCache
+from .runner import ModelRunner, StepMeta
+
+BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+
+
+@dataclass
+class Job:
+    chain: int
+    kind: str                 # "extend" or "proposal"
+    step: int
+    cut: int
+    seq: int                  # KV sequence id
+    anchor: int               # token whose KV is not yet written
+    n: int                    # position of the anchor == KV length
+    need: int                 # tokens to generate
+    seed: int
+    rounds: int = 0
+    tokens: list = field(default_factory=list)
+    logq: list = field(default_factory=list)
+    logp: list = field(default_factory=list)
+
+
+@dataclass
+class Chain:
+    prompt: list
+    tokens: list = field(default_factory=list)
+    logq: list = field(default_factory=list)
+    logp: list = field(default_factory=list)
+    seq: int = -1
+    updates_done: int = 0
+    accepted: int = 0
+    quota: int = 0
+
+
+class _RoundGraph:
+    """Static buffers (and optionally a captured CUDA graph) for one round of B blocks."""
+
+    def __init__(self, engine: "MHEngine", B: int, use_graph: bool):
+        self.e = engine
+        self.B = B
+        Kb = engine.block
+        dev = engine.device
+        mp = engine.max_pages
+        self.mp = mp
+        # int32 metadata packed for one H2D copy: positions, slots, kv_len, table, anchors, streams
+        self.n_pos = B * Kb
+        self.layout = [("positions", B * Kb), ("slots", B * Kb), ("kv_len", B), ("table", B * mp),
+                       ("anchors", B), ("streams", B)]
+        total = sum(n for _, n in self.layout)
+        self.host = torch.zeros(total, dtype=torch.int32).pin_memory()
+        self.dev = torch.zeros(total, dtype=torch.int32, device=dev)
+        self.views, off = {}, 0
+        for name, n in self.layout:
+            self.views[name] = self.dev[off:off + n]
+            off += n
+        self.host_views, off = {}, 0
+        for name, n in self.layout:
+            self.host_views[name] = self.host[off:off + n]
+            off += n
+        self.seeds_host = torch.zeros(B, dtype=torch.int64).pin_memory()
+        self.seeds = torch.zeros(B, dtype=torch.int64, device=dev)
+        table = self.views["table"].view(B, mp)
+        ql = [Kb] * B
+        mk = lambda v: torch.full((B,), v, dtype=torch.int32, device=dev)
+        starts = torch.arange(0, B * Kb, Kb, dtype=torch.int32, device=dev)
+        G = engine.runner.q_slots // engine.runner.kv_slots
+        tiles_per = -(-(Kb * G) // 16)
+        tile_seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles_per)
+        tile_row0 = (torch.arange(tiles_per, dtype=torch.int32, device=dev) * 16).repeat(B)
+        kv_len = self.views["kv_len"]
+        self.plan_draft = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(1), tile_seq, tile_row0, 16, {})
+        self.plan_verify = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(0), tile_seq, tile_row0, 16, {})
+        self.ids_draft = torch.full((B, Kb), engine.head.mask_token_id, dtype=torch.int32, device=dev)
+        self.ids_verify = torch.zeros(B, Kb, dtype=torch.int32, device=dev)
+        rows = torch.arange(B * Kb, device=dev).view(B, Kb)[:, : Kb - 1].reshape(-1)
+        self.draft_rows = rows.to(torch.int64)
+        self.inv_temp_rows = torch.full((B * (Kb - 1),), engine.inv_temp, dtype=torch.float32, device=dev)
+        self.inv_temp = torch.full((B,), engine.inv_temp, dtype=torch.float32, device=dev)
+        self.seed_index = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(Kb - 1)
+        self.row_in_seq = torch.arange(Kb - 1, dtype=torch.int32, device=dev).repeat(B)
+        self.row_streams = torch.zeros(B * (Kb - 1), dtype=torch.int32, device=dev)
+        self.cand = torch.zeros(B * (Kb - 1), dtype=torch.int32, device=dev)
+        self.out = {
+            "count": torch.zeros(B, dtype=torch.int32, device=dev),
+            "tail": torch.zeros(B, dtype=torch.int32, device=dev),
+            "valid": torch.zeros(B, dtype=torch.int32, device=dev),
+            "emitted": torch.zeros(B, Kb, dtype=torch.int32, device=dev),
+            "logq": torch.zeros(B, Kb, dtype=torch.float32, device=dev),
+            "logp": torch.zeros(B, Kb, dtype=torch.float32, device=dev),
+        }
+        # packed result for one D2H copy
+        self.result = torch.zeros(B, 2 + 3 * Kb, dtype=torch.float32, device=dev)
+        self.result_host = torch.zeros(B, 2 + 3 * Kb, dtype=torch.float32).pin_memory()
+        self.graph = None
+        self.teacher = None
+        self.launches_per_round = 0
+        if use_graph:
+            self._capture()
+
+    def _body(self):
+        e, B, Kb = self.e, self.B, self.e.block
+        v = self.views
+        self.ids_draft[:, 0].copy_(v["anchors"])
+        self.row_streams.copy_(v["streams"].repeat_interleave(Kb - 1))
+        meta_d = StepMeta(self.ids_draft.view(-1), v["positions"], v["slots"], self.plan_draft, self.draft_rows)
+        dl = e.head.forward(meta_d, self.draft_rows)
+        draft_logits = e.runner._buf("draft_logits_keep", tuple(dl.shape), torch.float32)
+        draft_logits.copy_(dl)
+        K.gumbel_sample(draft_logits, self.inv_temp_rows, self.seeds, seed_index=self.seed_index,
+                        streams=self.row_streams, row_in_seq=self.row_in_seq, salt=0x1234, tokens=self.cand)
+        self.ids_verify[:, 0].copy_(v["anchors"])
+        self.ids_verify[:, 1:].copy_(self.cand.view(B, Kb - 1))
+        meta_v = StepMeta(self.ids_verify.view(-1), v["positions"], v["slots"], self.plan_verify, None)
+        tl = e.runner.forward(meta_v)
+        self.teacher = tl
+        K.spec_verify(tl, draft_logits, self.cand.view(B, Kb - 1), self.inv_temp, self.seeds, streams=v["streams"],
+                      salt=0x777, out=self.out)
+        o = self.out
+        self.result[:, 0].copy_(o["count"])
+        self.result[:, 1].copy_(o["valid"])
+        self.result[:, 2:2 + Kb].copy_(o["emitted"])
+        self.result[:, 2 + Kb:2 + 2 * Kb].copy_(o["logq"])
+        self.result[:, 2 + 2 * Kb:].copy_(o["logp"])
+
+    def _capture(self):
+        from ..ops import _ext
+
+        s = torch.cuda.Stream(device=self.e.device)
+        s.wait_stream(torch.cuda.current_stream(self.e.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                before = _ext.launches()
+                self._body()
+                self.launches_per_round = _ext.launches() - before
+        torch.cuda.current_stream(self.e.device).wait_stream(s)
+        torch.cuda.synchronize(self.e.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self._body()
+        self.graph = g
+
+    def run(self):
+        self.e.stats["h2d_bytes"] += self.host.numel() * 4 + self.seeds_host.numel() * 8
+        self.e.stats["d2h_bytes"] += self.result_host.numel() * 4
+        self.dev.copy_(self.host, non_blocking=True)
+        self.seeds.copy_(self.seeds_host, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            self.e.stats["graph_kernel_launches"] += self.launches_per_round
+        else:
+            self._body()
+        self.result_host.copy_(self.result, non_blocking=True)
+        torch.cuda.current_stream(self.e.device).synchronize()
+        return self.result_host
+
+
+class MHEngine:
+    """Suffix-MH chains with speculative block drafting on one TP group."""
+
+    def __init__(self, runner: ModelRunner, head: DraftHead, *, alpha: float = 4.0, length: int = 512,
+                 root_seed: int = 0, learner: SuffixLearner | None = None, use_graphs: bool = True,
+                 max_pages_per_seq: int | None = None):
+        self.runner = runner
+        self.head = head
+        self.cache: KVCache = runner.cache
+        self.block = head.block_size
+        self.alpha = float(alpha)
+        self.inv_temp = self.alpha  # proposal temperature 1 / alpha
+        self.length = int(length)
+        self.seeds = SeedStream(root_seed)
+        self.learner = learner
+        self.use_graphs = use_graphs
+        self.device = runner.device
+        self.max_pages = max_pages_per_seq or 64
+        self.chains: list[Chain] = []
+        self.jobs: dict[int, Job] = {}
+        self._graphs: dict[int, _RoundGraph] = {}
+        self.stats = {"rounds": 0, "blocks": 0, "emitted": 0, "generated": 0, "mh_updates": 0, "mh_accepted": 0,
+                      "learner_updates": 0, "graph_kernel_launches": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+
+    # ---- setup ----
+    def add_chains(self, prompts: list[list[int]]) -> None:
+        P = len(prompts[0])
+        if any(len(p) != P for p in prompts):
+            raise ValueError("prompts of one engine share a length")
+        start = len(self.chains)
+        for p in prompts:
+            self.chains.append(Chain(list(p)))
+        self._prefill(list(range(start, start + len(prompts))))
+
+    def _prefill(self, chain_ids: list[int], chunk_tokens: int = 8192) -> None:
+        """Prefill prompt[:-1] once per distinct prompt and open each chain's extension job.
+
+        Chains with the same prompt fork one prefilled sequence, so they share
+        its KV pages by reference.
+        """
+        from .runner import build_meta
+
+        r = self.runner
+        P = len(self.chains[chain_ids[0]].prompt)
+        distinct: dict[tuple, int] = {}
+        for c in chain_ids:
+            distinct.setdefault(tuple(self.chains[c].prompt), c)
+        prompts = list(distinct)
+        per = max(1, chunk_tokens // max(1, P - 1))
+        roots: dict[tuple, int] = {}
+        for lo in range(0, len(prompts), per):
+            group = prompts[lo:lo + per]
+            seqs = [self.cache.create() for _ in group]
+            if P > 1:
+                slots, toks, pos = [], [], []
+                for s, pr in zip(seqs, group):
+                    slots += self.cache.append(s, P - 1)
+                    toks += list(pr[:-1])
+                    pos += list(range(P - 1))
+                table = torch.zeros(len(group), self.max_pages, dtype=torch.int32)
+                self.cache.fill_table(seqs, table)
+                meta = build_meta(self.device, table, toks, pos, slots, [P - 1] * len(group), [P - 1] * len(group),
+                                  [0] * len(group), r.q_slots // r.kv_slots, tile_rows=64)
+                r.forward(meta, compute_logits=False)
+            roots.update(zip(group, seqs))
+        for c in chain_ids:
+            ch = self.chains[c]
+            seq = self.cache.fork(roots[tuple(ch.prompt)], P - 1)
+            self.jobs[c] = Job(c, "extend", 0, 0, seq, ch.prompt[-1], P - 1, self.length,
+                               self.seeds.derive("mh", c, 0, "extend"))
+        for s in roots.values():
+            self.cache.release(s)
+
+    # ---- job bookkeeping ----
+    def _next_job(self, c: int) -> None:
+        ch = self.chains[c]
+        if ch.updates_done >= ch.quota:
+            return
+        step = ch.updates_done
+        cut = int(self.seeds.generator("mh", c, 0, step, "cut").integers(0, self.length))
+        P = len(ch.prompt)
+        full = ch.prompt + ch.tokens
+        seq = self.cache.fork(ch.seq, P + cut - 1)
+        self.jobs[c] = Job(c, "proposal", step, cut, seq, full[P + cut - 1], P + cut - 1, self.length - cut,
+                           self.seeds.derive("mh", c, 0, step, "proposal"))
+
+    def _finish(self, job: Job) -> None:
+        ch = self.chains[job.chain]
+        P = len(ch.prompt)
+        L = self.length
+        self.cache.truncate(job.seq, P + L - 1)
+        if job.kind == "extend":
+            ch.tokens, ch.logq, ch.logp = job.tokens[:L], job.logq[:L], job.logp[:L]
+            ch.seq = job.seq
+        else:
+            cut = job.cut
+            old_p, old_q = float(sum(ch.logp[cut:L])), float(sum(ch.logq[cut:L]))
+            new_p, new_q = float(sum(job.logp)), float(sum(job.logq))
+            d = decide_metropolis_hastings(
+                current_target_log_density=self.alpha * old_p, proposed_target_log_density=self.alpha * new_p,
+                forward_proposal_log_probability=new_q, reverse_proposal_log_probability=old_q,
+                uniform=float(self.seeds.generator("mh", job.chain, 0, job.step, "accept").random()))
+            ch.updates_done += 1
+            self.stats["mh_updates"] += 1
+            if d.accepted:
+                ch.accepted += 1
+                self.stats["mh_accepted"] += 1
+                ch.tokens[cut:L] = job.tokens
+                ch.logq[cut:L] = job.logq
+                ch.logp[cut:L] = job.logp
+                self.cache.release(ch.seq)
+                ch.seq = job.seq
+            else:
+                self.cache.release(job.seq)
+        del self.jobs[job.chain]
+        self._next_job(job.chain)
+
+    def set_quota(self, updates_per_chain: int) -> None:
+        """Allow every chain `updates_per_chain` more MH updates and open their jobs."""
+        for c, ch in enumerate(self.chains):
+            ch.quota = ch.updates_done + updates_per_chain
+            if c not in self.jobs and ch.seq >= 0:
+                self._next_job(c)
+
+    # ---- rounds ----
+    def _graph(self, B: int) -> _RoundGraph:
+        bucket = next(b for b in BUCKETS if b >= B) if B <= BUCKETS[-1] else B
+        g = self._graphs.get(bucket)
+        if g is None:
+            g = _RoundGraph(self, bucket, self.use_graphs)
+            self._graphs[bucket] = g
+        return g
+
+    def round(self) -> int:
+        """Advance every active job by one speculative round; returns tokens generated."""
+        jobs = sorted(self.jobs.values(), key=lambda j: j.chain)
+        if not jobs:
+            return 0
+        Kb = self.block
+        self.cache.flush_copies()
+        g = self._graph(len(jobs))
+        B = g.B
+        hv = g.host_views
+        pos = hv["positions"].view(B, Kb)
+        slots = hv["slots"].view(B, Kb)
+        table = hv["table"].view(B, g.mp)
+        seqs = []
+        for b, j in enumerate(jobs):
+            s = self.cache.append(j.seq, Kb)
+            slots[b] = torch.tensor(s, dtype=torch.int32)
+            pos[b] = torch.arange(j.n, j.n + Kb, dtype=torch.int32)
+            hv["kv_len"][b] = j.n + Kb
+            hv["anchors"][b] = j.anchor
+            hv["streams"][b] = j.rounds
+            g.seeds_host[b] = j.seed & ((1 << 63) - 1)
+            seqs.append(j.seq)
+        self.cache.fill_table(seqs, table[: len(jobs)])
+        for b in range(len(jobs), B):  # padding rows: one visible key, no cache writes
+            slots[b] = -1
+            pos[b] = torch.arange(Kb, dtype=torch.int32)
+            hv["kv_len"][b] = Kb
+            hv["anchors"][b] = 0
+            hv["streams"][b] = 0
+            table[b] = 0
+        res = g.run().numpy()
+        generated = 0
+        counts = res[:, 0].astype(np.int64)
+        if (res[: len(jobs), 1] == 0).any():
+            raise RuntimeError("speculative correction reported invalid probabilities")
+        if self.learner is not None:
+            fb = FeedbackRound(
+                block_ids=g.ids_draft[: len(jobs)].clone(), positions=g.views["positions"].view(B, Kb)[: len(jobs)].clone(),
+                hist_pages=[list(self.cache.manager.pages(j.seq)) for j in jobs], hist_len=[j.n for j in jobs],
+                teacher=g.teacher.view(B, Kb, -1)[: len(jobs), : Kb - 1].clone(),
+                valid=torch.as_tensor(np.minimum(counts[: len(jobs)] + 1, Kb - 1), device=self.device))
+            if self.learner.observe(fb) is not None:
+                self.stats["learner_updates"] += 1
+        finished = []
+        for b, j in enumerate(jobs):
+            c = int(counts[b])
+            take = min(c + 1, j.need - len(j.tokens))
+            em = res[b, 2:2 + Kb].astype(np.int64)
+            j.tokens += [int(x) for x in em[:take]]
+            j.logq += [float(x) for x in res[b, 2 + Kb:2 + Kb + take]]
+            j.logp += [float(x) for x in res[b, 2 + 2 * Kb:2 + 2 * Kb + take]]
+            generated += take
+            self.stats["emitted"] += c + 1
+            j.rounds += 1
+            self.cache.truncate(j.seq, j.n + 1 + c)
+            j.anchor = int(em[c])
+            j.n = j.n + 1 + c
+            if len(j.tokens) >= j.need:
+                finished.append(j)
+        self.stats["rounds"] += 1
+        self.stats["blocks"] += len(jobs)
+        self.stats["generated"] += generated
+        for j in finished:
+            self._finish(j)
+        return generated
+
+    def run_until_idle(self, max_rounds: int | None = None) -> int:
+        total = 0
+        rounds = 0
+        while self.jobs and (max_rounds is None or rounds < max_rounds):
+            total += self.round()
+            rounds += 1
+        return total
+
+    @property
+    def mean_accept_length(self) -> float:
+        return self.stats["emitted"] / max(1, self.stats["blocks"])

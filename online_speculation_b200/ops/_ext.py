@@ -28,11 +28,39 @@ def available() -> bool:
     return load() is not None
 
 
+class _Counted:
+    """Proxy that counts every kernel launch made through the extension."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.launches = 0
+
+    def __getattr__(self, name):
+        attr = getattr(self._mod, name)
+        if callable(attr) and not isinstance(attr, type) and name not in ("gemm_pick_bn",):
+            def call(*args, **kwargs):
+                self.launches += 1
+                return attr(*args, **kwargs)
+            return call
+        return attr
+
+
+_counted = None
+
+
+def launches() -> int:
+    """Kernel launches issued through the extension so far (graph replays not included)."""
+    return 0 if _counted is None else _counted.launches
+
+
 def require():
+    global _counted
     ext = load()
+    if ext is not None and _counted is None:
+        _counted = _Counted(ext)
     if ext is None:
         raise RuntimeError(
             "the online_speculation_b200 CUDA extension is not built; run "
             "`python setup.py build_ext --inplace` (sm_100a) before using CUDA tensors"
         ) from _error
-    return ext
+    return _counted

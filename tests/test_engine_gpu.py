@@ -1,0 +1,115 @@
+"""The batched runner and the speculative MH engine against the fp32 oracle."""
+
+import math
+
+import pytest
+import torch
+
+from online_speculation_b200.api import build_mh_engine
+from online_speculation_b200.engine.kv_cache import KVCache
+from online_speculation_b200.engine.runner import ModelRunner, build_meta
+from online_speculation_b200.models.decoder import PRESETS, DecoderConfig, build_weights, random_state_dict, reference_forward
+from online_speculation_b200.ops import workspace
+
+pytestmark = pytest.mark.gpu
+
+SMALL = DecoderConfig(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_hidden_layers=3,
+                      num_attention_heads=8, num_key_value_heads=2, name="small")
+SMALL_QK = DecoderConfig(vocab_size=1024, hidden_size=512, intermediate_size=768, num_hidden_layers=2,
+                         num_attention_heads=4, num_key_value_heads=4, attention_bias=False, qk_norm=True,
+                         tie_word_embeddings=True, name="small-qk")
+
+
+def _setup(cfg, seed=0):
+    sd = random_state_dict(cfg, seed=seed, std=0.05, device="cpu")
+    w = build_weights(cfg, sd, device="cuda")
+    cache = KVCache(cfg.num_hidden_layers, w.heads.kv_slots, 64, "cuda")
+    return sd, ModelRunner(w, cache, max_tokens=1024)
+
+
+@pytest.mark.parametrize("cfg", [SMALL, SMALL_QK])
+def test_prefill_decode_verify_match_oracle(cfg):
+    sd, r = _setup(cfg)
+    torch.manual_seed(0)
+    seq = torch.randint(0, cfg.vocab_size, (70,))
+    ref = reference_forward(cfg, sd, seq)                       # [70, V] fp32
+    G = r.q_slots // r.kv_slots
+    cache = r.cache
+    s = cache.create()
+    # prefill 60 tokens (logits for all rows)
+    slots = cache.append(s, 60)
+    table = torch.zeros(1, 8, dtype=torch.int32)
+    cache.fill_table([s], table)
+    meta = build_meta("cuda", table, seq[:60].tolist(), list(range(60)), slots, [60], [60], [0], G)
+    out = r.forward(meta)
+    rel = float((out.cpu() - ref[:60]).norm() / ref[:60].norm())
+    assert rel < 3e-2
+    # one decode step
+    slots = cache.append(s, 1)
+    cache.fill_table([s], table)
+    meta = build_meta("cuda", table, [int(seq[60])], [60], slots, [1], [61], [0], G)
+    out = r.forward(meta)
+    assert float((out.cpu()[0] - ref[60]).norm() / ref[60].norm()) < 3e-2
+    # a causal verify block of 4
+    slots = cache.append(s, 4)
+    cache.fill_table([s], table)
+    meta = build_meta("cuda", table, seq[61:65].tolist(), list(range(61, 65)), slots, [4], [65], [0], G)
+    out = r.forward(meta)
+    assert float((out.cpu() - ref[61:65]).norm() / ref[61:65].norm()) < 3e-2
+    torch.cuda.synchronize()
+    workspace.check_status()
+
+
+def test_forked_sequences_share_prefix_pages():
+    sd, r = _setup(SMALL)
+    cache = r.cache
+    G = r.q_slots // r.kv_slots
+    torch.manual_seed(1)
+    seq = torch.randint(0, SMALL.vocab_size, (80,))
+    ref = reference_forward(SMALL, sd, seq)
+    s = cache.create()
+    slots = cache.append(s, 45)
+    table = torch.zeros(1, 8, dtype=torch.int32)
+    cache.fill_table([s], table)
+    r.forward(build_meta("cuda", table, seq[:45].tolist(), list(range(45)), slots, [45], [45], [0], G),
+              compute_logits=False)
+    f = cache.fork(s, 40)          # shares page 0, copies 8 tokens of page 1
+    assert cache.manager.refcount(cache.manager.pages(s)[0]) == 2
+    cache.flush_copies()
+    slots = cache.append(f, 1)
+    cache.fill_table([f], table)
+    out = r.forward(build_meta("cuda", table, [int(seq[40])], [40], slots, [1], [41], [0], G))
+    assert float((out.cpu()[0] - ref[40]).norm() / ref[40].norm()) < 3e-2
+    cache.release(s)
+    cache.release(f)
+    assert cache.free_pages == cache.num_pages
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+def test_mh_engine_logprobs_are_exact(graphs):
+    """Every emitted token's log p / log q must equal the oracle's log-softmax of the chain prefix."""
+    cfg = SMALL
+    eng = build_mh_engine(cfg, seed=3, alpha=2.0, length=24, block_size=4, learner_stride=8, use_graphs=graphs,
+                          kv_bytes=64 << 20, max_seq_tokens=64, max_batch=8)
+    prompt = list(range(5, 21))
+    eng.add_chains([prompt] * 6)
+    eng.run_until_idle()
+    eng.set_quota(3)
+    eng.run_until_idle()
+    assert eng.stats["mh_updates"] == 18
+    assert eng.learner.updates >= 1
+    # the oracle uses the same random weights (drawn on the same device from the same seed)
+    sd = {k: v.cpu() for k, v in random_state_dict(cfg, seed=3, std=0.02, device="cuda").items()}
+    for ch in eng.chains:
+        assert len(ch.tokens) == 24
+        full = torch.tensor(ch.prompt + ch.tokens)
+        logits = reference_forward(cfg, sd, full)[len(prompt) - 1:-1]
+        lp = logits.log_softmax(-1).gather(-1, torch.tensor(ch.tokens)[:, None]).squeeze(-1)
+        lq = (logits * 2.0).log_softmax(-1).gather(-1, torch.tensor(ch.tokens)[:, None]).squeeze(-1)
+        assert torch.allclose(torch.tensor(ch.logp), lp, atol=0.05)
+        assert torch.allclose(torch.tensor(ch.logq), lq, atol=0.1)
+    # pages: each chain holds its state, nothing leaked
+    held = sum(1 for p in range(eng.cache.num_pages) if eng.cache.manager.refcount(p) > 0)
+    assert held <= 6 * 2 + 2
+    assert eng.mean_accept_length >= 1.0
+    workspace.check_status()
