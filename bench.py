@@ -253,6 +253,8 @@ def run_ours(args, rank, world, local, group) -> dict:
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
     }
+    engine.close()
+    del engine
     return out
 
 
@@ -359,8 +361,13 @@ def main():
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
+        import gc
+
+        import torch
         import torch.distributed as dist
 
+        gc.collect()
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -28,10 +28,11 @@ def resolve_config(model: str | DecoderConfig) -> DecoderConfig:
 
 
 def build_runner(model: str | DecoderConfig, *, tp_group=None, seed: int = 0, kv_bytes: int = 8 << 30,
-                 max_tokens: int = 8192, max_logit_rows: int = 512, weights=None) -> ModelRunner:
+                 max_tokens: int = 8192, max_logit_rows: int = 512, weights=None,
+                 fused_collectives: bool = True) -> ModelRunner:
     cfg = resolve_config(model)
-    comm = Collectives(tp_group)
     device = torch.device("cuda", torch.cuda.current_device())
+    comm = Collectives(tp_group, hidden=cfg.hidden_size, max_tokens=max_tokens, device=device, fused=fused_collectives)
     w = weights if weights is not None else random_weights(cfg, tp=comm.world, rank=comm.rank, seed=seed,
                                                            device=device)
     pages = KVCache.pages_for_budget(kv_bytes, cfg.num_hidden_layers, w.heads.kv_slots)
@@ -42,15 +43,16 @@ def build_runner(model: str | DecoderConfig, *, tp_group=None, seed: int = 0, kv
 def build_mh_engine(model: str | DecoderConfig = "qwen2.5-7b", *, tp_group=None, seed: int = 0, alpha: float = 4.0,
                     length: int = 512, block_size: int = 4, learner_stride: int | None = 64,
                     learner_loss: str = "tv", learning_rate: float = 1e-5, use_graphs: bool = True,
-                    kv_bytes: int = 24 << 30, max_seq_tokens: int = 1040, max_batch: int = 64) -> MHEngine:
+                    kv_bytes: int = 24 << 30, max_seq_tokens: int = 1040, max_batch: int = 64,
+                    fused_collectives: bool = True) -> MHEngine:
     runner = build_runner(model, tp_group=tp_group, seed=seed, kv_bytes=kv_bytes,
-                          max_logit_rows=max(512, max_batch * block_size))
+                          max_logit_rows=max(512, max_batch * block_size), fused_collectives=fused_collectives)
     draft = init_draft(runner.w, seed=seed + 1)
     head = DraftHead(runner, draft, block_size=block_size)
     learner = None
     if learner_stride:
         learner = SuffixLearner(head, SuffixConfig(stride=learner_stride, loss=learner_loss,
-                                                   learning_rate=learning_rate))
+                                                   learning_rate=learning_rate), use_graphs=use_graphs)
     max_pages = -(-max_seq_tokens // 32) + 1
     return MHEngine(runner, head, alpha=alpha, length=length, root_seed=seed, learner=learner,
                     use_graphs=use_graphs, max_pages_per_seq=max_pages)

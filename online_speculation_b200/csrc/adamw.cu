@@ -34,7 +34,14 @@ __global__ void sq_norm_kernel(const float* __restrict__ g, long long n, float* 
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ publish, long long n,
                              const float* __restrict__ sq_norm, float clip, float lr, float beta1, float beta2,
-                             float eps, float weight_decay, float bc1, float bc2, int* __restrict__ nonfinite) {
+                             float eps, float weight_decay, float bc1, float bc2, int* __restrict__ nonfinite,
+                             const int* __restrict__ step_ptr) {
+  if (step_ptr) {
+    // bias corrections from the device-side step counter (graph-replayable)
+    const float t = static_cast<float>(*step_ptr);
+    bc1 = 1.0f - powf(beta1, t);
+    bc2 = 1.0f - powf(beta2, t);
+  }
   float scale = 1.0f;
   if (sq_norm) {
     const float norm = sqrtf(*sq_norm);
@@ -76,7 +83,7 @@ cudaError_t adamw_launch(const AdamWArgs& a, cudaStream_t stream) {
   const int blocks = static_cast<int>(std::min<long long>(1184, (a.n + 255) / 256));
   adamw_kernel<<<blocks, 256, 0, stream>>>(a.params, a.grads, a.exp_avg, a.exp_avg_sq, a.publish, a.n, a.sq_norm,
                                            a.clip, a.lr, a.beta1, a.beta2, a.eps, a.weight_decay, a.bias_correction1,
-                                           a.bias_correction2, a.nonfinite);
+                                           a.bias_correction2, a.nonfinite, a.step_ptr);
   return cudaGetLastError();
 }
 

@@ -18,6 +18,7 @@ struct AdamWArgs {
   float lr, beta1, beta2, eps, weight_decay;
   float bias_correction1, bias_correction2;
   int* nonfinite;           // set to 1 when the norm is not finite (step skipped)
+  const int* step_ptr;      // device step counter (>= 1) for the bias corrections, or null
 };
 
 cudaError_t grad_sq_norm_launch(const float* g, long long n, float* out, cudaStream_t stream);

@@ -107,6 +107,26 @@ __device__ __forceinline__ void load_page(const AttnArgs& a, int page, int g, in
   }
 }
 
+// Copy keys [k0, k0 + CH) of one page (CH = 16) of K and V for kv head g.
+template <int CH>
+__device__ __forceinline__ void load_chunk(const AttnArgs& a, int page, int g, int k0, int valid, __nv_bfloat16* sK,
+                                           __nv_bfloat16* sV, int lane) {
+  const long long base = ((static_cast<long long>(page) * a.Hkv + g) * kPage + k0) * kD;
+  const __nv_bfloat16* gk = a.k_cache + base;
+  const __nv_bfloat16* gv = a.v_cache + base;
+  for (int c = lane; c < CH * (kD / 8); c += 32) {
+    const int row = c / (kD / 8);
+    const int col = (c % (kD / 8)) * 8;
+    if (row < valid) {
+      cp_async16(sK + row * kStride + col, gk + row * kD + col);
+      cp_async16(sV + row * kStride + col, gv + row * kD + col);
+    } else {
+      *reinterpret_cast<uint4*>(sK + row * kStride + col) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sV + row * kStride + col) = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
 // Per-warp flash-attention state for 16 query rows.
 struct WarpState {
   uint32_t qf[kD / 16][4];
@@ -148,18 +168,20 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, WarpState& st, int q0,
   st.l[0] = st.l[1] = 0.0f;
 }
 
-// Process one 32-key page already resident in shared memory.
+// Process one chunk of CH (16 or 32) keys already resident in shared memory.
+template <int CH = 32>
 __device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, const __nv_bfloat16* sK,
                                              const __nv_bfloat16* sV, int key0, int kvlen, int bidir, int lane) {
-  float s[4][4];
+  constexpr int NB = CH / 8;  // key blocks of 8
+  float s[NB][4];
 #pragma unroll
-  for (int n = 0; n < 4; ++n)
+  for (int n = 0; n < NB; ++n)
 #pragma unroll
     for (int i = 0; i < 4; ++i) s[n][i] = 0.0f;
   const uint32_t kbase = smem_u32(sK);
-  // S = Q K^T over 4 key blocks of 8
+  // S = Q K^T over NB key blocks of 8
 #pragma unroll
-  for (int n = 0; n < 4; ++n) {
+  for (int n = 0; n < NB; ++n) {
 #pragma unroll
     for (int kk = 0; kk < kD / 16; kk += 2) {
       // matrices: (keys n*8.., d kk*16+0..7), (.., +8), (.., (kk+1)*16), (.., +8)
@@ -175,7 +197,7 @@ __device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, c
   const int c2 = (lane % 4) * 2;
   float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-  for (int n = 0; n < 4; ++n) {
+  for (int n = 0; n < NB; ++n) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int h = i / 2;
@@ -197,7 +219,7 @@ __device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, c
   }
   float rs[2] = {0.0f, 0.0f};
 #pragma unroll
-  for (int n = 0; n < 4; ++n) {
+  for (int n = 0; n < NB; ++n) {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int h = i / 2;
@@ -219,10 +241,10 @@ __device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, c
     st.o[n][2] *= corr[1];
     st.o[n][3] *= corr[1];
   }
-  // O += P V  (2 k-steps of 16 keys)
+  // O += P V  (CH / 16 k-steps of 16 keys)
   const uint32_t vbase = smem_u32(sV);
 #pragma unroll
-  for (int kk = 0; kk < 2; ++kk) {
+  for (int kk = 0; kk < CH / 16; ++kk) {
     uint32_t pa[4];
     pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
     pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
@@ -291,15 +313,20 @@ __global__ void __launch_bounds__(128) attn_rows_kernel(const AttnArgs a) {
       cp_async_wait<0>();
     }
     __syncthreads();
-    process_page(a, st, sK[p & 1], sV[p & 1], p * kPage, kvlen, bidir, lane);
+    process_page<32>(a, st, sK[p & 1], sV[p & 1], p * kPage, kvlen, bidir, lane);
     __syncthreads();
   }
   store_rows(a, st, q0, rows, row0 + warp * 16, g, lane);
 }
 
-// 4 warps split the pages of one 16-row tile, then merge their softmax states.
-constexpr int kWarpBufElems = 4 * kPage * kStride;  // 2 stages x (K, V)
-constexpr int kKeysSmemBytes = 4 * kWarpBufElems * 2;
+// 4 warps split the 16-key chunks of one 16-row tile (chunk c -> warp c % 4),
+// each with a 3-stage cp.async ring, then merge their softmax states.
+constexpr int kChunk = 16;
+constexpr int kStages = 3;
+constexpr int kStageElems = 2 * kChunk * kStride;          // K and V of one chunk
+constexpr int kWarpBufElems = kStages * kStageElems;
+constexpr int kKeysSmemBytes = 4 * kWarpBufElems * 2 > (4 * 16 * kD + 128) * 4 ? 4 * kWarpBufElems * 2
+                                                                               : (4 * 16 * kD + 128) * 4;
 
 __global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -315,28 +342,33 @@ __global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
   load_q(a, st, q0, rows, row0, g, qlen, kvlen, lane);
   const int last_row = min(rows - 1, row0 + 15);
   const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
-  const int npages = (max_key + kPage - 1) / kPage;
+  const int nchunks = (max_key + kChunk - 1) / kChunk;
   const int* tbl = a.table + static_cast<long long>(b) * a.table_stride;
-  auto kbuf = [&](int s) { return buf + s * 2 * kPage * kStride; };
-  auto vbuf = [&](int s) { return buf + s * 2 * kPage * kStride + kPage * kStride; };
-  if (warp < npages) {
-    load_page(a, tbl[warp], g, min(kPage, kvlen - warp * kPage), kbuf(0), vbuf(0), lane, 32);
+  auto kbuf = [&](int s) { return buf + s * kStageElems; };
+  auto vbuf = [&](int s) { return buf + s * kStageElems + kChunk * kStride; };
+  auto issue = [&](int c, int s) {
+    const int key0 = c * kChunk;
+    load_chunk<kChunk>(a, tbl[key0 / kPage], g, key0 % kPage, min(kChunk, kvlen - key0), kbuf(s), vbuf(s), lane);
+  };
+  // prologue: up to kStages - 1 chunks of this warp in flight
+  int next = warp;
+#pragma unroll
+  for (int i = 0; i < kStages - 1; ++i) {
+    if (next < nchunks) issue(next, i);
     cp_async_commit();
+    next += 4;
   }
   int it = 0;
-  for (int p = warp; p < npages; p += 4, ++it) {
-    const int nxt = p + 4;
-    if (nxt < npages) {
-      load_page(a, tbl[nxt], g, min(kPage, kvlen - nxt * kPage), kbuf((it + 1) & 1), vbuf((it + 1) & 1), lane, 32);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+  for (int c = warp; c < nchunks; c += 4, ++it) {
+    if (next < nchunks) issue(next, (it + kStages - 1) % kStages);
+    cp_async_commit();
+    next += 4;
+    cp_async_wait<kStages - 1>();
     __syncwarp();
-    process_page(a, st, kbuf(it & 1), vbuf(it & 1), p * kPage, kvlen, bidir, lane);
+    process_page<kChunk>(a, st, kbuf(it % kStages), vbuf(it % kStages), c * kChunk, kvlen, bidir, lane);
     __syncwarp();
   }
+  cp_async_wait<0>();
   __syncthreads();
   // Merge: per warp 16 x 128 fp32 partial outputs plus (m, l) per row.
   float* so = reinterpret_cast<float*>(smem_raw);           // [4][16][128]

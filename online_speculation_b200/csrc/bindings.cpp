@@ -6,11 +6,13 @@
 // loader on GPU machines.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <pybind11/numpy.h>
 #include <pybind11/stl.h>
 #include <torch/extension.h>
 
 #include "adamw.h"
 #include "attention.h"
+#include "comm.h"
 #include "elementwise.h"
 #include "gemm.h"
 #include "kv_manager.h"
@@ -259,7 +261,8 @@ void gumbel_sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor seeds, 
 
 void spec_verify(Tensor target, Tensor draft, Tensor candidates, int64_t n, c10::optional<Tensor> inv_temp, Tensor seeds,
                  c10::optional<Tensor> streams, int64_t salt, Tensor count, Tensor tail, Tensor valid, Tensor emitted,
-                 Tensor logq, Tensor logp) {
+                 Tensor logq, Tensor logp, c10::optional<Tensor> lseT_target, c10::optional<Tensor> lse1_target,
+                 c10::optional<Tensor> lseT_draft) {
   CHECK_CUDA(target);
   CHECK_ROWS(target);
   CHECK_ROWS(draft);
@@ -288,7 +291,90 @@ void spec_verify(Tensor target, Tensor draft, Tensor candidates, int64_t n, c10:
   a.emitted = emitted.data_ptr<int>();
   a.logq = logq.data_ptr<float>();
   a.logp = logp.data_ptr<float>();
+  a.lseT_target = ptr_or_null<const float>(lseT_target);
+  a.lse1_target = ptr_or_null<const float>(lse1_target);
+  a.lseT_draft = ptr_or_null<const float>(lseT_draft);
+  TORCH_CHECK((a.lseT_target == nullptr) == (a.lse1_target == nullptr) &&
+                  (a.lseT_target == nullptr) == (a.lseT_draft == nullptr),
+              "precomputed statistics come together");
   check(osb::spec_verify_launch(a, B, at::cuda::getCurrentCUDAStream()), "spec_verify");
+}
+
+// Full-vocabulary TV / forward-KL distillation: statistics, loss pieces, gradient.
+void divergence_stats(Tensor s, Tensor t, Tensor out) {
+  CHECK_CUDA(s);
+  CHECK_ROWS(s);
+  CHECK_ROWS(t);
+  CHECK_DT(s, torch::kFloat32);
+  CHECK_DT(t, torch::kFloat32);
+  TORCH_CHECK(s.sizes() == t.sizes() && out.numel() == 4 * s.size(0), "divergence shapes");
+  c10::cuda::CUDAGuard guard(s.device());
+  check(osb::divergence_stats_launch(s.data_ptr<float>(), t.data_ptr<float>(), s.stride(0), t.stride(0), s.size(0),
+                                     s.size(1), out.data_ptr<float>(), at::cuda::getCurrentCUDAStream()),
+        "divergence_stats");
+}
+
+void divergence_loss(Tensor s, Tensor t, Tensor lse, int64_t kind, Tensor out) {
+  CHECK_CUDA(s);
+  CHECK_ROWS(s);
+  CHECK_ROWS(t);
+  TORCH_CHECK(lse.numel() == 2 * s.size(0) && out.numel() == 2 * s.size(0), "divergence loss shapes");
+  c10::cuda::CUDAGuard guard(s.device());
+  check(osb::divergence_loss_launch(s.data_ptr<float>(), t.data_ptr<float>(), s.stride(0), t.stride(0), s.size(0),
+                                    s.size(1), lse.data_ptr<float>(), static_cast<int>(kind), out.data_ptr<float>(),
+                                    at::cuda::getCurrentCUDAStream()),
+        "divergence_loss");
+}
+
+void divergence_grad(Tensor s, Tensor t, Tensor lse, Tensor pieces, Tensor w, int64_t kind, Tensor grad) {
+  CHECK_CUDA(s);
+  CHECK_ROWS(s);
+  CHECK_ROWS(t);
+  CHECK_ROWS(grad);
+  CHECK_DT(grad, torch::kBFloat16);
+  TORCH_CHECK(grad.sizes() == s.sizes() && w.numel() == s.size(0), "divergence grad shapes");
+  c10::cuda::CUDAGuard guard(s.device());
+  check(osb::divergence_grad_launch(s.data_ptr<float>(), t.data_ptr<float>(), s.stride(0), t.stride(0), s.size(0),
+                                    s.size(1), lse.data_ptr<float>(), pieces.data_ptr<float>(), w.data_ptr<float>(),
+                                    static_cast<int>(kind), bfm(grad), grad.stride(0),
+                                    at::cuda::getCurrentCUDAStream()),
+        "divergence_grad");
+}
+
+// h += sum over ranks of the partials; x = rmsnorm(h) * w  (peer pointers as int64 addresses)
+void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows, std::vector<int64_t> pads,
+                           Tensor epoch, Tensor h, Tensor w, Tensor x, int64_t T, int64_t rank, double eps,
+                           int64_t blocks, Tensor status) {
+  CHECK_CUDA(h);
+  CHECK_ROWS(h);
+  CHECK_ROWS(x);
+  CHECK_DT(h, torch::kBFloat16);
+  CHECK_DT(epoch, torch::kInt32);
+  const int world = static_cast<int>(parts.size());
+  TORCH_CHECK(world >= 1 && world <= osb::kMaxRanks && rows.size() == parts.size() && pads.size() == parts.size(),
+              "one partial, row buffer and signal pad per rank (at most 8)");
+  TORCH_CHECK(h.size(0) >= T && x.size(0) >= T && w.numel() == h.size(1), "all-reduce shapes");
+  c10::cuda::CUDAGuard guard(h.device());
+  osb::ArArgs a{};
+  for (int q = 0; q < world; ++q) {
+    a.parts[q] = reinterpret_cast<const __nv_bfloat16*>(parts[q]);
+    a.rows[q] = reinterpret_cast<__nv_bfloat16*>(rows[q]);
+    a.pads[q] = reinterpret_cast<uint32_t*>(pads[q]);
+  }
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
+  a.h = bfm(h);
+  a.ldh = h.stride(0);
+  a.w = bf(w);
+  a.x = bfm(x);
+  a.ldx = x.stride(0);
+  a.T = static_cast<int>(T);
+  a.H = h.size(1);
+  a.rank = static_cast<int>(rank);
+  a.world = world;
+  a.eps = static_cast<float>(eps);
+  a.status = status.data_ptr<int>();
+  check(osb::allreduce_add_rmsnorm_launch(a, static_cast<int>(blocks), at::cuda::getCurrentCUDAStream()),
+        "allreduce_add_rmsnorm");
 }
 
 void grad_sq_norm(Tensor g, Tensor out) {
@@ -303,7 +389,7 @@ void grad_sq_norm(Tensor g, Tensor out) {
 
 void adamw(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> publish, c10::optional<Tensor> sq_norm,
            double clip, double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
-           c10::optional<Tensor> nonfinite) {
+           c10::optional<Tensor> nonfinite, c10::optional<Tensor> step_tensor) {
   CHECK_CUDA(p);
   for (const Tensor* t : {&p, &g, &m, &v}) {
     CHECK_DT(*t, torch::kFloat32);
@@ -331,6 +417,7 @@ void adamw(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> publish
   a.bias_correction1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
   a.bias_correction2 = static_cast<float>(1.0 - std::pow(beta2, static_cast<double>(step)));
   a.nonfinite = ptr_or_null<int>(nonfinite);
+  a.step_ptr = ptr_or_null<const int>(step_tensor);
   check(osb::adamw_launch(a, at::cuda::getCurrentCUDAStream()), "adamw");
 }
 
@@ -349,6 +436,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gumbel_sample", &gumbel_sample);
   m.def("spec_verify", &spec_verify);
   m.def("grad_sq_norm", &grad_sq_norm);
+  m.def("allreduce_add_rmsnorm", &allreduce_add_rmsnorm);
+  m.def("divergence_stats", &divergence_stats);
+  m.def("divergence_loss", &divergence_loss);
+  m.def("divergence_grad", &divergence_grad);
   m.def("adamw", &adamw);
   m.def("gemm_pick_bn", &osb::gemm_pick_bn);
 
@@ -370,6 +461,30 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            })
       .def("pages", &osb::KVManager::pages)
       .def("refcount", &osb::KVManager::refcount)
+      .def("append_many",
+           [](osb::KVManager& self, const std::vector<int64_t>& seqs, int n) {
+             std::vector<int32_t> all;
+             all.reserve(seqs.size() * n);
+             for (int64_t s : seqs) {
+               const auto v = self.append(s, n);
+               all.insert(all.end(), v.begin(), v.end());
+             }
+             return all;
+           })
+      .def("truncate_many",
+           [](osb::KVManager& self, const std::vector<int64_t>& seqs, const std::vector<int64_t>& lengths) {
+             TORCH_CHECK(seqs.size() == lengths.size(), "one length per sequence");
+             for (size_t i = 0; i < seqs.size(); ++i) self.truncate(seqs[i], static_cast<int>(lengths[i]));
+           })
+      .def("fill_table_np",
+           [](const osb::KVManager& self, const std::vector<int64_t>& seqs, pybind11::array_t<int32_t> out) {
+             auto buf = out.mutable_unchecked<2>();
+             TORCH_CHECK(buf.shape(0) >= static_cast<ssize_t>(seqs.size()), "table rows");
+             std::vector<int32_t> tmp(seqs.size() * buf.shape(1));
+             self.fill_table(seqs, tmp.data(), static_cast<int>(buf.shape(1)));
+             for (size_t r = 0; r < seqs.size(); ++r)
+               for (ssize_t c = 0; c < buf.shape(1); ++c) buf(r, c) = tmp[r * buf.shape(1) + c];
+           })
       .def("fill_table", [](const osb::KVManager& self, const std::vector<int64_t>& seqs, Tensor out) {
         TORCH_CHECK(out.device().is_cpu() && out.scalar_type() == torch::kInt32 && out.dim() == 2 &&
                         out.is_contiguous() && out.size(0) >= static_cast<int64_t>(seqs.size()),

@@ -1,0 +1,185 @@
+// Tensor-parallel all-reduce of row-parallel GEMM partials over NVLink peer
+// memory, fused with the residual add and the following RMSNorm.
+//
+//   h <- h + sum_r P_r ;  x <- rmsnorm(h) * w
+//
+// Two-shot algorithm over symmetric buffers (every rank can load every other
+// rank's buffers through NVLink / NVSwitch peer mappings):
+//   kernel A  each rank owns a slice of rows; it loads those rows of every
+//             rank's partial P_r (peer loads), adds the residual, and stores
+//             the reduced rows into its own symmetric row buffer and its
+//             local residual stream;
+//   kernel B  every rank gathers the other ranks' reduced rows (peer loads)
+//             and applies RMSNorm to all rows.
+// Each kernel starts with a cross-rank barrier: block 0 publishes the call's
+// epoch into every rank's signal pad (release, system scope) and every block
+// polls its own pad (acquire) with a bounded wait.  On timeout the kernel
+// records an error and skips its work instead of hanging.  Partials are
+// double-buffered by the caller, so one barrier per kernel is enough: a rank
+// can only overwrite a partial buffer after every peer has passed the next
+// reduction's barriers.
+//
+// There is no counterpart in the reference (it has no distributed code); this
+// is the fused collective behind the tensor-parallel decoder layers.
+#include "comm.h"
+#include "common.cuh"
+
+namespace osb {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Cross-rank barrier at the start of a kernel (slot distinguishes kernels).
+__device__ __forceinline__ bool rank_barrier(const ArArgs& a, int slot, uint32_t epoch) {
+  if (blockIdx.x == 0 && threadIdx.x < a.world) {
+    __threadfence_system();
+    st_release_sys(a.pads[threadIdx.x] + slot * kMaxRanks + a.rank, epoch);
+  }
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint32_t* mine = a.pads[a.rank] + slot * kMaxRanks;
+    const unsigned long long start = global_ns();
+    for (int q = 0; q < a.world && ok; ++q) {
+      while (static_cast<int>(ld_acquire_sys(mine + q) - epoch) < 0) {
+        if (global_ns() - start > kWaitLimitNs) {
+          record_error(a.status, kErrPeerWait);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+__device__ __forceinline__ int slice_begin(int T, int world, int r) { return (T * r) / world; }
+
+__global__ void __launch_bounds__(256) reduce_rows_kernel(const ArArgs a) {
+  const uint32_t epoch = *a.epoch + 1;
+  if (!rank_barrier(a, 0, epoch)) return;
+  const int r0 = slice_begin(a.T, a.world, a.rank), r1 = slice_begin(a.T, a.world, a.rank + 1);
+  const int nvec = a.H / 8;
+  for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      float acc[8];
+      {
+        const uint4 hr = *reinterpret_cast<const uint4*>(a.h + static_cast<long long>(row) * a.ldh + v * 8);
+        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hr);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = bf2f(he[e]);
+      }
+      uint4 parts[kMaxRanks];
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q) {
+        if (q < a.world)
+          parts[q] = __ldcg(reinterpret_cast<const uint4*>(a.parts[q] + static_cast<long long>(row) * a.H + v * 8));
+      }
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q) {
+        if (q < a.world) {
+          const __nv_bfloat16* pe = reinterpret_cast<const __nv_bfloat16*>(&parts[q]);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += bf2f(pe[e]);
+        }
+      }
+      uint4 out;
+      __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ob[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+      *reinterpret_cast<uint4*>(a.h + static_cast<long long>(row) * a.ldh + v * 8) = out;
+      *reinterpret_cast<uint4*>(a.rows[a.rank] + static_cast<long long>(row) * a.H + v * 8) = out;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) gather_norm_kernel(const ArArgs a) {
+  const uint32_t epoch = *a.epoch + 1;
+  const bool ok = rank_barrier(a, 1, epoch);
+  const int nvec = a.H / 8;
+  __shared__ float red[33];
+  if (ok) {
+    for (int row = blockIdx.x; row < a.T; row += gridDim.x) {
+      int owner = 0;
+      while (owner + 1 < a.world && slice_begin(a.T, a.world, owner + 1) <= row) ++owner;
+      __nv_bfloat16* hr = a.h + static_cast<long long>(row) * a.ldh;
+      float ss = 0.0f;
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        uint4 val;
+        if (owner == a.rank) {
+          val = *reinterpret_cast<const uint4*>(hr + v * 8);
+        } else {
+          val = __ldcg(reinterpret_cast<const uint4*>(a.rows[owner] + static_cast<long long>(row) * a.H + v * 8));
+          *reinterpret_cast<uint4*>(hr + v * 8) = val;
+        }
+        const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&val);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float f = bf2f(e8[e]);
+          ss += f * f;
+        }
+      }
+      ss = warp_sum(ss);
+      const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      if (warp == 0) {
+        float t = lane < blockDim.x / 32 ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[32] = rsqrtf(t / a.H + a.eps);
+      }
+      __syncthreads();
+      const float rs = red[32];
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(hr + v * 8);
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.w + v * 8);
+        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+        uint4 out;
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = f2bf(bf2f(we[e]) * bf2f(f2bf(bf2f(he[e]) * rs)));
+        *reinterpret_cast<uint4*>(a.x + static_cast<long long>(row) * a.ldx + v * 8) = out;
+      }
+      __syncthreads();
+    }
+  }
+  // The last block to finish advances the epoch for the next reduction.
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(a.epoch + 1, 1u);
+    last = done == gridDim.x - 1;
+    if (last) {
+      a.epoch[1] = 0;
+      __threadfence();
+      a.epoch[0] = epoch;
+    }
+  }
+}
+
+}  // namespace
+
+cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
+  if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
+  const int rows_per_rank = (a.T + a.world - 1) / a.world;
+  const int grid_a = blocks < rows_per_rank ? blocks : rows_per_rank;
+  reduce_rows_kernel<<<grid_a > 0 ? grid_a : 1, 256, 0, stream>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  const int grid_b = blocks < a.T ? blocks : a.T;
+  gather_norm_kernel<<<grid_b, 256, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace osb

@@ -51,6 +51,8 @@ struct Args {
   const __nv_bfloat16* bias;
   int epilogue;         // 0 linear, 1 swiglu
   int out_f32;
+  int vec_ok;           // output / residual rows are 16-byte aligned
+  int cluster;          // >1: split-K over a thread-block cluster, reduced through DSMEM
   float* workspace;
   int* counters;
   int* status;
@@ -63,56 +65,194 @@ struct Smem {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kXchgBytes = 32 * 64 * 4;
+  static constexpr int kXchgBytes = 32 * (kBM + 4) * 4;
   static constexpr int kBarBytes = 256;
   static constexpr int kTotal = 1024 + kStages * kStageBytes + kBarBytes + kXchgBytes;
 };
 
+// Epilogue of one 32-token chunk.  Every epilogue thread owns one accumulator
+// row r (an output feature) and holds its 32 token values in v.  The chunk is
+// transposed through shared memory (stage[j][r], fp32) so that the global
+// writes -- and the residual reads -- are 16-byte vectors along the feature
+// dimension, issued in batches (the residual may alias the output, so loads
+// are grouped ahead of the stores instead of alternating with them).
 template <int BN>
 __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32], int tm, int tn, int chunk, int r,
-                                             float* xchg) {
+                                             float* stage, int ep_tid) {
   const int t0 = tn * BN + chunk * 32;
-  if (a.epilogue == 1) {
-    // rows [0,64) hold gate, rows [64,128) hold up for the same 64 features.
-    if (r >= 64) {
+  const bool swiglu = a.epilogue == 1;
+  const int f0 = swiglu ? tm * 64 : tm * kBM;       // first output feature of this tile
+  const int out_cols = swiglu ? a.M / 2 : a.M;      // output row width (valid features)
+  const int width = swiglu ? 64 : kBM;              // features produced by this tile
+  const float b = (!swiglu && a.bias && tm * kBM + r < a.M) ? bf2f(a.bias[tm * kBM + r]) : 0.0f;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) xchg[j * 64 + (r - 64)] = v[j];
+  for (int j = 0; j < 32; ++j) stage[j * (kBM + 4) + r] = v[j] + b;
+  named_barrier(1, 128);
+  const int valid_t = min(32, a.N - t0);
+  if (a.vec_ok) {
+    // vectors of 8 features; width/8 vectors per token row
+    constexpr int kMaxIter = (32 * kBM / 8 + 127) / 128;  // 4
+    const int vec_per_row = width / 8;
+    const int total = 32 * vec_per_row;
+    float res[kMaxIter][8];
+    int tv[kMaxIter], fv[kMaxIter];
+#pragma unroll
+    for (int it = 0; it < kMaxIter; ++it) {
+      const int idx = ep_tid + it * 128;
+      tv[it] = idx / vec_per_row;
+      fv[it] = (idx % vec_per_row) * 8;
+      const bool ok = idx < total && tv[it] < valid_t && f0 + fv[it] + 8 <= out_cols;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) res[it][e] = 0.0f;
+      if (ok && a.residual) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(a.residual + (t0 + tv[it]) * a.ldr + f0 + fv[it]);
+        const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) res[it][e] = bf2f(rb[e]);
+      }
     }
-    named_barrier(1, 128);
-    const int f = tm * 64 + r;
-    if (r < 64 && f < a.M / 2) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int t = t0 + j;
-        if (t < a.N) {
-          const float g = v[j];
-          const float u = xchg[j * 64 + r];
-          const float s = g / (1.0f + __expf(-g));
-          float val = s * u;
-          if (a.residual) val += bf2f(a.residual[t * a.ldr + f]);
+    for (int it = 0; it < kMaxIter; ++it) {
+      const int idx = ep_tid + it * 128;
+      const int t = tv[it], fl = fv[it];
+      if (idx >= total || t >= valid_t) continue;
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float* row = stage + t * (kBM + 4);
+        float val;
+        if (swiglu) {
+          const float g = row[fl + e], u = row[fl + e + 64];
+          val = g / (1.0f + __expf(-g)) * u;
+        } else {
+          val = row[fl + e];
+        }
+        o[e] = val + res[it][e];
+      }
+      const long long base = static_cast<long long>(t0 + t) * a.ldo + f0 + fl;
+      if (f0 + fl + 8 <= out_cols) {
+        if (a.out_f32) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + base);
+          dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+        } else {
+          uint4 pk;
+          __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) pb[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + base) = pk;
+        }
+      } else {
+        for (int e = 0; e < 8 && f0 + fl + e < out_cols; ++e) {
+          float val = o[e];
+          if (a.residual) val = o[e] - res[it][e] + bf2f(a.residual[(t0 + t) * a.ldr + f0 + fl + e]);
           if (a.out_f32)
-            static_cast<float*>(a.out)[t * a.ldo + f] = val;
+            static_cast<float*>(a.out)[base + e] = val;
           else
-            static_cast<__nv_bfloat16*>(a.out)[t * a.ldo + f] = f2bf(val);
+            static_cast<__nv_bfloat16*>(a.out)[base + e] = f2bf(val);
         }
       }
     }
-    named_barrier(1, 128);
-    return;
-  }
-  const int f = tm * kBM + r;
-  if (f >= a.M) return;
-  const float b = a.bias ? bf2f(a.bias[f]) : 0.0f;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const int t = t0 + j;
-    if (t < a.N) {
-      float val = v[j] + b;
-      if (a.residual) val += bf2f(a.residual[t * a.ldr + f]);
+  } else {
+    // scalar fallback for unaligned output / residual rows
+    for (int idx = ep_tid; idx < 32 * width; idx += 128) {
+      const int t = idx / width, fl = idx % width;
+      if (t >= valid_t || f0 + fl >= out_cols) continue;
+      const float* row = stage + t * (kBM + 4);
+      float val;
+      if (swiglu) {
+        const float g = row[fl], u = row[fl + 64];
+        val = g / (1.0f + __expf(-g)) * u;
+      } else {
+        val = row[fl];
+      }
+      const long long off = static_cast<long long>(t0 + t) * a.ldo + f0 + fl;
+      if (a.residual) val += bf2f(a.residual[(t0 + t) * a.ldr + f0 + fl]);
       if (a.out_f32)
-        static_cast<float*>(a.out)[t * a.ldo + f] = val;
+        static_cast<float*>(a.out)[off] = val;
       else
-        static_cast<__nv_bfloat16*>(a.out)[t * a.ldo + f] = f2bf(val);
+        static_cast<__nv_bfloat16*>(a.out)[off] = f2bf(val);
+    }
+  }
+  named_barrier(1, 128);
+}
+
+// Cluster split-K reduction.  Every CTA of the cluster holds one split's fp32
+// tile in its own shared memory, token-major: stage[c][r] (row stride kBM + 4).
+// CTA `rank` reduces tokens [rank * BN / S, (rank + 1) * BN / S) across all S
+// CTAs through distributed shared memory and writes them with the fused
+// epilogue (bias, SwiGLU, residual) as 16-byte vectors.
+template <int BN>
+__device__ __forceinline__ void cluster_reduce_store(const Args& a, const float* stage, int tm, int tn) {
+  const int S = a.cluster;
+  const uint32_t rank = cluster_ctarank();
+  const int cs = BN / S;
+  const bool swiglu = a.epilogue == 1;
+  const int width = swiglu ? 64 : kBM;
+  const int f0 = swiglu ? tm * 64 : tm * kBM;
+  const int out_cols = swiglu ? a.M / 2 : a.M;
+  const int vpr = width / 8;
+  const int items = cs * vpr;
+  const uint32_t base = smem_u32(stage);
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int cl = it / vpr;
+    const int fl = (it % vpr) * 8;
+    const int c = rank * cs + cl;           // token within the tile
+    const int t = tn * BN + c;
+    if (t >= a.N) continue;
+    float g[8], u[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) g[e] = u[e] = 0.0f;
+    const uint32_t row = base + static_cast<uint32_t>(c * (kBM + 4) + fl) * 4;
+    for (int q = 0; q < S; ++q) {
+      const uint32_t ra = map_shared_rank(row, q);
+      const float4 x0 = ld_dsmem_f4(ra), x1 = ld_dsmem_f4(ra + 16);
+      g[0] += x0.x; g[1] += x0.y; g[2] += x0.z; g[3] += x0.w;
+      g[4] += x1.x; g[5] += x1.y; g[6] += x1.z; g[7] += x1.w;
+      if (swiglu) {
+        const float4 y0 = ld_dsmem_f4(ra + 64 * 4), y1 = ld_dsmem_f4(ra + 64 * 4 + 16);
+        u[0] += y0.x; u[1] += y0.y; u[2] += y0.z; u[3] += y0.w;
+        u[4] += y1.x; u[5] += y1.y; u[6] += y1.z; u[7] += y1.w;
+      }
+    }
+    const int f = f0 + fl;
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (swiglu) {
+        o[e] = g[e] / (1.0f + __expf(-g[e])) * u[e];
+      } else {
+        o[e] = g[e] + ((a.bias && f + e < out_cols) ? bf2f(a.bias[f + e]) : 0.0f);
+      }
+    }
+    const long long off = static_cast<long long>(t) * a.ldo + f;
+    if (a.vec_ok && f + 8 <= out_cols) {
+      if (a.residual) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(a.residual + static_cast<long long>(t) * a.ldr + f);
+        const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] += bf2f(rb[e]);
+      }
+      if (a.out_f32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(a.out) + off);
+        dst[0] = make_float4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_float4(o[4], o[5], o[6], o[7]);
+      } else {
+        uint4 pk;
+        __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pb[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off) = pk;
+      }
+    } else {
+      for (int e = 0; e < 8 && f + e < out_cols; ++e) {
+        float val = o[e];
+        if (a.residual) val += bf2f(a.residual[static_cast<long long>(t) * a.ldr + f + e]);
+        if (a.out_f32)
+          static_cast<float*>(a.out)[off + e] = val;
+        else
+          static_cast<__nv_bfloat16*>(a.out)[off + e] = f2bf(val);
+      }
     }
   }
 }
@@ -268,11 +408,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort_flag) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + acc * BN;
-      if (a.splits == 1) {
+      if (a.cluster > 1) {
+        // Stage this split's tile token-major into the (now idle) pipeline smem.
+        float* st = reinterpret_cast<float*>(smem);
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(t_acc + c * 32, v);
-          finish_chunk<BN>(a, v, tm, tn, c, r, xchg);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) st[(c * 32 + j) * (kBM + 4) + r] = v[j];
+        }
+        tc_fence_before();
+      } else if (a.splits == 1) {
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(t_acc + c * 32, v);
+          finish_chunk<BN>(a, v, tm, tn, c, r, xchg, ep_tid);
         }
         tc_fence_before();
         __syncwarp();
@@ -312,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += __ldcg(&p[(c * 32 + j) * kBM + r]);
             }
-            finish_chunk<BN>(a, v, tm, tn, c, r, xchg);
+            finish_chunk<BN>(a, v, tm, tn, c, r, xchg, ep_tid);
           }
         }
       }
@@ -323,6 +473,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (a.cluster > 1) {
+    // Every CTA holds exactly one split of one tile (grid = tiles x cluster).
+    const int tile = blockIdx.x / a.cluster;
+    cluster_sync();                       // all splits staged
+    if (!*abort_flag) cluster_reduce_store<BN>(a, reinterpret_cast<const float*>(smem), tile % a.tiles_m,
+                                               tile / a.tiles_m);
+    cluster_sync();                       // peers finished reading this CTA's tile
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::kTmemCols);
@@ -371,6 +529,34 @@ int sm_count(int device) {
   return cached[device];
 }
 
+// Largest number of co-resident clusters of `cluster` CTAs for this kernel (cached per device).
+template <int BN>
+int max_active_clusters(int dev, int cluster) {
+  static int cache[64][4] = {};
+  const int slot = cluster == 2 ? 0 : cluster == 4 ? 1 : 2;
+  if (dev < 0 || dev >= 64) return 0;
+  if (cache[dev][slot] == 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cluster * 64);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Smem<BN>::kTotal;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_tn_kernel<BN>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = -1;
+    }
+    cache[dev][slot] = n;
+  }
+  return cache[dev][slot];
+}
+
 template <int BN>
 cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream) {
   using S = Smem<BN>;
@@ -390,7 +576,39 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
   const int sms = sm_count(dev);
   a.splits = 1;
   a.kb_per_split = a.k_blocks;
-  if (p.allow_split && tiles < sms && p.workspace != nullptr) {
+  a.cluster = 1;
+  if (p.allow_split && p.split_mode == 0 && tiles < sms) {
+    // Split-K across a thread-block cluster (2, 4 or 8 CTAs), reduced through DSMEM.
+    // Only cluster sizes whose clusters all fit on the GPU at once are used, so
+    // the launch is a single wave.
+    const int want = sms / tiles;
+    for (int c = 8; c >= 2; c /= 2) {
+      const int per = (a.k_blocks + c - 1) / c;
+      if (c <= want && a.k_blocks >= 2 * c && (c - 1) * per < a.k_blocks &&
+          tiles <= max_active_clusters<BN>(dev, c)) {
+        a.cluster = c;
+        a.splits = c;
+        a.kb_per_split = per;
+        break;
+      }
+    }
+    if (a.cluster > 1) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(tiles * a.cluster);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = S::kTotal;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = a.cluster;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      return cudaLaunchKernelEx(&cfg, gemm_tn_kernel<BN>, ma, mb, a);
+    }
+  }
+  if (p.allow_split && p.split_mode == 1 && tiles < sms && p.workspace != nullptr) {
     int want = std::max(1, sms / tiles);
     want = std::min(want, std::max(1, a.k_blocks / 2));
     int per = (a.k_blocks + want - 1) / want;
@@ -449,6 +667,13 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.workspace = p.workspace;
   a.counters = p.counters;
   a.status = p.status;
+  {
+    const int esz = p.out_f32 ? 4 : 2;
+    const bool out_ok = (reinterpret_cast<uintptr_t>(p.out) % 16 == 0) && ((p.ldo * esz) % 16 == 0);
+    const bool res_ok = p.residual == nullptr ||
+                        ((reinterpret_cast<uintptr_t>(p.residual) % 16 == 0) && ((p.ldr * 2) % 16 == 0));
+    a.vec_ok = out_ok && res_ok;
+  }
   switch (bn) {
     case 32: return launch_bn<32>(p, a, stream);
     case 64: return launch_bn<64>(p, a, stream);

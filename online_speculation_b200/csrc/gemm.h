@@ -19,6 +19,7 @@ struct GemmProblem {
   long long ldr;
   int epilogue;                   // 0 linear, 1 swiglu on [64 gate | 64 up] row tiles
   int allow_split;
+  int split_mode;                 // 0: split-K over a cluster (DSMEM reduction); 1: global workspace
   float* workspace;               // split-K partials
   long long workspace_floats;
   int* counters;                  // per-tile arrival counters, zero at rest

@@ -110,6 +110,7 @@ extern "C" __attribute__((visibility("default"))) int osb_gemm_bf16_noalloc(
   p.ldr = ldr;
   p.epilogue = swiglu ? 1 : 0;
   p.allow_split = 1;
+  p.split_mode = 1;  // split-K partials in the static scratch
   p.workspace = partials;
   p.workspace_floats = kPartialFloats;
   p.counters = counters;

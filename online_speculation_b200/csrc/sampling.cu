@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
     for (int j = 0; j < 4; ++j) {
       const int v = i * 4 + j;
       if (v < a.V) {
-        const float g = -logf(-logf(uu[j]));
+        const float g = -__logf(-__logf(uu[j]));
         const float sc = row[v] * invT + g;
         if (sc > best || (sc == best && v < besti)) {
           best = sc;
@@ -297,7 +297,13 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
   __shared__ int s_count, s_valid;
   __shared__ float s_lseT[16], s_lse1[16], s_lseQ[16];
   // statistics of the target rows and the draft rows
-  for (int i = 0; i <= n; ++i) {
+  if (a.lseT_target != nullptr) {
+    if (threadIdx.x <= n) {
+      s_lseT[threadIdx.x] = a.lseT_target[b * (n + 1) + threadIdx.x];
+      s_lse1[threadIdx.x] = a.lse1_target[b * (n + 1) + threadIdx.x];
+    }
+    if (threadIdx.x < n) s_lseQ[threadIdx.x] = a.lseT_draft[b * n + threadIdx.x];
+  } else for (int i = 0; i <= n; ++i) {
     float mx, l1, lT;
     row_stats(a.target + (static_cast<long long>(b) * (n + 1) + i) * a.ld_target, a.V, invT, mx, l1, lT);
     if (threadIdx.x == 0) {
@@ -305,7 +311,7 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
       s_lse1[i] = l1;
     }
   }
-  for (int i = 0; i < n; ++i) {
+  if (a.lseT_target == nullptr) for (int i = 0; i < n; ++i) {
     float mx, l1, lT;
     row_stats(a.draft + (static_cast<long long>(b) * n + i) * a.ld_draft, a.V, invT, mx, l1, lT);
     if (threadIdx.x == 0) s_lseQ[i] = lT;
@@ -324,7 +330,7 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
       }
       const float lp = a.target[(static_cast<long long>(b) * (n + 1) + i) * a.ld_target + x] * invT - s_lseT[i];
       const float lq = a.draft[(static_cast<long long>(b) * n + i) * a.ld_draft + x] * invT - s_lseQ[i];
-      const float ratio = expf(fminf(lp - lq, 0.0f));
+      const float ratio = __expf(fminf(lp - lq, 0.0f));
       const float u = i < 4 ? us[i] : u01(philox4x32(make_uint4(i, 0x51u, stream, a.salt),
                                                      make_uint2(static_cast<uint32_t>(seed), 0)).x);
       if (!(u < ratio)) {
@@ -355,12 +361,12 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
       float w;
       const float lp = prow[v] * invT - lseP;
       if (qrow) {
-        const float d = expf(lp) - expf(qrow[v] * invT - lseQ);
-        w = d > 0.0f ? logf(d) : -INFINITY;
+        const float d = __expf(lp) - __expf(qrow[v] * invT - lseQ);
+        w = d > 0.0f ? __logf(d) : -INFINITY;
       } else {
         w = lp;
       }
-      const float sc = w - logf(-logf(uu[j]));
+      const float sc = w - __logf(-__logf(uu[j]));
       if (sc > best || (sc == best && v < besti)) {
         best = sc;
         besti = v;
@@ -433,6 +439,131 @@ cudaError_t spec_verify_launch(const SpecArgs& a, int batch, cudaStream_t stream
   if (batch <= 0) return cudaSuccess;
   if (a.n < 1 || a.n > 15) return cudaErrorInvalidValue;
   spec_verify_kernel<<<batch, kThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace osb
+
+// ------------------------------------------------------------ divergence --
+// Full-vocabulary distillation loss between student and teacher logits, per
+// row, at temperature one (online-speculation/src/blockspec/losses.py:6-18):
+//   kind 0: total variation 0.5 * sum_v |q_v - p_v|
+//   kind 1: forward KL(p || q) = sum_v p_v (log p_v - log q_v)
+// with q = softmax(student), p = softmax(teacher).  Three kernels so a
+// vocabulary-sharded caller can all-reduce between phases:
+//   stats  : per-row max and sum exp of both rows (local shard),
+//   loss   : per-row loss pieces given the global log-normalisers
+//            (TV: sum |q - p| and A = sum sign(q - p) q; KL: sum p (log p - log q)),
+//   grad   : d loss / d student = w * 0.5 q (sign(q - p) - A)   (TV)
+//                               = w * (q - p)                    (KL)
+namespace osb {
+namespace {
+
+__global__ void __launch_bounds__(1024) div_stats_kernel(const float* __restrict__ s, const float* __restrict__ t,
+                                                        long long ld_s, long long ld_t, int V, float* __restrict__ out) {
+  // out[r] = {max_s, sum_s, max_t, sum_t}
+  const int r = blockIdx.x;
+  float ms, ss, mt, st, l1, lT;
+  row_stats(s + r * ld_s, V, 1.0f, ms, l1, lT);
+  ss = expf(l1 - ms);
+  row_stats(t + r * ld_t, V, 1.0f, mt, l1, lT);
+  st = expf(l1 - mt);
+  if (threadIdx.x == 0) {
+    out[4 * r + 0] = ms;
+    out[4 * r + 1] = ss;
+    out[4 * r + 2] = mt;
+    out[4 * r + 3] = st;
+  }
+}
+
+__global__ void __launch_bounds__(1024) div_loss_kernel(const float* __restrict__ s, const float* __restrict__ t,
+                                                       long long ld_s, long long ld_t, int V,
+                                                       const float* __restrict__ lse, int kind,
+                                                       float* __restrict__ out) {
+  // lse[2r] = global lse of student row r, lse[2r+1] of teacher row r.  out[2r] = loss piece, out[2r+1] = A.
+  const int r = blockIdx.x;
+  const float ls = lse[2 * r], lt = lse[2 * r + 1];
+  const float* sr = s + r * ld_s;
+  const float* tr = t + r * ld_t;
+  float x = 0.0f, y = 0.0f;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float lq = sr[v] - ls, lp = tr[v] - lt;
+    const float q = __expf(lq), p = __expf(lp);
+    if (kind == 0) {
+      const float d = q - p;
+      x += fabsf(d);
+      y += d > 0.0f ? q : (d < 0.0f ? -q : 0.0f);
+    } else {
+      x += p > 0.0f ? p * (lp - lq) : 0.0f;
+    }
+  }
+  __shared__ float rx[32], ry[32];
+  x = warp_sum(x);
+  y = warp_sum(y);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (lane == 0) {
+    rx[warp] = x;
+    ry[warp] = y;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    x = lane < blockDim.x / 32 ? rx[lane] : 0.0f;
+    y = lane < blockDim.x / 32 ? ry[lane] : 0.0f;
+    x = warp_sum(x);
+    y = warp_sum(y);
+    if (lane == 0) {
+      out[2 * r] = kind == 0 ? 0.5f * x : x;
+      out[2 * r + 1] = y;
+    }
+  }
+}
+
+__global__ void div_grad_kernel(const float* __restrict__ s, const float* __restrict__ t, long long ld_s,
+                                long long ld_t, int V, const float* __restrict__ lse, const float* __restrict__ pieces,
+                                const float* __restrict__ w, int kind, __nv_bfloat16* __restrict__ grad,
+                                long long ld_g) {
+  const int r = blockIdx.y;
+  const float ls = lse[2 * r], lt = lse[2 * r + 1];
+  const float A = pieces[2 * r + 1];
+  const float wr = w[r];
+  const float* sr = s + r * ld_s;
+  const float* tr = t + r * ld_t;
+  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V; v += gridDim.x * blockDim.x) {
+    const float q = __expf(sr[v] - ls), p = __expf(tr[v] - lt);
+    float g;
+    if (kind == 0) {
+      const float d = q - p;
+      const float sg = d > 0.0f ? 1.0f : (d < 0.0f ? -1.0f : 0.0f);
+      g = 0.5f * q * (sg - A);
+    } else {
+      g = q - p;
+    }
+    grad[r * ld_g + v] = f2bf(wr * g);
+  }
+}
+
+}  // namespace
+
+cudaError_t divergence_stats_launch(const float* s, const float* t, long long ld_s, long long ld_t, int rows, int V,
+                                    float* out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  div_stats_kernel<<<rows, 1024, 0, stream>>>(s, t, ld_s, ld_t, V, out);
+  return cudaGetLastError();
+}
+
+cudaError_t divergence_loss_launch(const float* s, const float* t, long long ld_s, long long ld_t, int rows, int V,
+                                   const float* lse, int kind, float* out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  div_loss_kernel<<<rows, 1024, 0, stream>>>(s, t, ld_s, ld_t, V, lse, kind, out);
+  return cudaGetLastError();
+}
+
+cudaError_t divergence_grad_launch(const float* s, const float* t, long long ld_s, long long ld_t, int rows, int V,
+                                   const float* lse, const float* pieces, const float* w, int kind,
+                                   __nv_bfloat16* grad, long long ld_g, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  dim3 grid((V + 1023) / 1024 < 32 ? (V + 1023) / 1024 : 32, rows);
+  div_grad_kernel<<<grid, 1024, 0, stream>>>(s, t, ld_s, ld_t, V, lse, pieces, w, kind, grad, ld_g);
   return cudaGetLastError();
 }
 

@@ -58,6 +58,10 @@ struct SpecArgs {
   int* emitted;               // [B, n + 1]
   float* logq;                // [B, n + 1]
   float* logp;                // [B, n + 1]
+  // optional precomputed row statistics (row_stats_kernel); null = computed in-kernel
+  const float* lseT_target;   // [B * (n + 1)]
+  const float* lse1_target;   // [B * (n + 1)]
+  const float* lseT_draft;    // [B * n]
 };
 
 cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream);
@@ -65,4 +69,15 @@ cudaError_t row_stats_launch(const RowStatsArgs& a, int rows, cudaStream_t strea
 cudaError_t gumbel_sample_launch(const GumbelArgs& a, int rows, cudaStream_t stream);
 cudaError_t spec_verify_launch(const SpecArgs& a, int batch, cudaStream_t stream);
 
+}  // namespace osb
+
+#include <cuda_bf16.h>
+namespace osb {
+cudaError_t divergence_stats_launch(const float* s, const float* t, long long ld_s, long long ld_t, int rows, int V,
+                                    float* out, cudaStream_t stream);
+cudaError_t divergence_loss_launch(const float* s, const float* t, long long ld_s, long long ld_t, int rows, int V,
+                                   const float* lse, int kind, float* out, cudaStream_t stream);
+cudaError_t divergence_grad_launch(const float* s, const float* t, long long ld_s, long long ld_t, int rows, int V,
+                                   const float* lse, const float* pieces, const float* w, int kind,
+                                   __nv_bfloat16* grad, long long ld_g, cudaStream_t stream);
 }  // namespace osb

@@ -110,16 +110,16 @@ class DraftHead:
         x = r._buf("dx", (T, r.cfg.hidden_size))
         K.rmsnorm(h, lw.in_norm, eps, out=x)
         d = self.draft
-        pend = r.attention_block(self.layer, x, meta, wq=d.w_qkv, bias=d.b_qkv, q_norm=d.q_norm, k_norm=d.k_norm,
+        part = r.attention_block(self.layer, x, meta, wq=d.w_qkv, bias=d.b_qkv, q_norm=d.q_norm, k_norm=d.k_norm,
                                  wo=d.w_o, residual=h)
         if r.comm.world == 1:
             K.rmsnorm(h, lw.post_norm, eps, out=x)
         else:
-            K.rmsnorm(h, lw.post_norm, eps, out=x, residual=h, delta=pend)
-        pend = r.mlp_block(self.layer, x, residual=h)
+            r.comm.reduce_add_norm(part, h, lw.post_norm, x, eps)
+        part = r.mlp_block(self.layer, x, residual=h)
         if r.comm.world == 1:
             return r.logits(h, logit_rows)
-        K.rmsnorm(h, r.w.final_norm, eps, out=x, residual=h, delta=pend)
+        r.comm.reduce_add_norm(part, h, r.w.final_norm, x, eps)
         sel = r._index_rows(x, logit_rows)
         return r.logits(sel, None, normed=True)
 
@@ -186,35 +186,48 @@ class SuffixConfig:
 
 @dataclass
 class FeedbackRound:
-    """One verified round of a batch of blocks (device tensors, detached)."""
+    """One verified round of a batch of blocks, as device tensors.
 
-    block_ids: torch.Tensor      # [B, K] draft inputs
-    positions: torch.Tensor      # [B, K]
-    hist_pages: list[list[int]]  # page ids of each block's history (last layer)
-    hist_len: list[int]
-    teacher: torch.Tensor        # [B, K-1, V] fp32 target logits (local vocab shard)
-    valid: torch.Tensor          # [B] reached rows (0..K-1)
+    When the round comes from a captured round graph these are that graph's
+    static buffers, read in place right after the round (before the next one
+    overwrites them), so the learner update can itself be a replayed graph.
+    """
+
+    block_ids: torch.Tensor      # [B, K] int32 draft inputs [anchor, MASK...]
+    positions: torch.Tensor      # [B, K] int32 absolute positions of the block
+    table: torch.Tensor          # [B, max_pages] int32 page table (history = keys < positions[:, 0])
+    teacher: torch.Tensor        # [B * K, V_local] fp32 target verify logits
+    count: torch.Tensor          # [B] int32 accepted draft tokens of the round
+    active: torch.Tensor         # [B] fp32, 1 for real blocks, 0 for padding rows
+    blocks: int                  # number of real blocks
 
 
 class SuffixLearner:
-    def __init__(self, head: DraftHead, config: SuffixConfig = SuffixConfig()):
+    """Online suffix learner of the draft attention (fp32 masters, fused AdamW)."""
+
+    def __init__(self, head: DraftHead, config: SuffixConfig = SuffixConfig(), *, use_graphs: bool = True):
         self.head = head
         self.config = config
         d = head.draft
-        self.names = [n for n, t in d.tensors().items()]
-        self.master = d.flat.float().clone()
-        self.grad = torch.zeros_like(self.master)
-        self.exp_avg = torch.zeros_like(self.master)
-        self.exp_avg_sq = torch.zeros_like(self.master)
-        self.norm_buf = torch.zeros(1, dtype=torch.float32, device=self.master.device)
-        self.nonfinite = torch.zeros(1, dtype=torch.int32, device=self.master.device)
-        self.replay: deque[FeedbackRound] = deque(maxlen=config.replay_blocks)
+        dev = d.flat.device
+        self.master = torch.nn.Parameter(d.flat.float().clone())
+        self.exp_avg = torch.zeros_like(self.master, requires_grad=False)
+        self.exp_avg_sq = torch.zeros_like(self.master, requires_grad=False)
+        self.norm_buf = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.nonfinite = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.step_t = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.loss_buf = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.use_graphs = use_graphs and dev.type == "cuda"
+        self._graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
         self.blocks_seen = 0
         self.updates = 0
         self.update_seconds = 0.0
-        self.last_loss: float | None = None
         self.step = 0
         self.frozen_fingerprint = self._fingerprint()
+
+    @property
+    def last_loss(self) -> float:
+        return float(self.loss_buf)
 
     def _fingerprint(self) -> str:
         w = self.head.runner.w
@@ -231,41 +244,48 @@ class SuffixLearner:
             off += t.numel()
         return out
 
-    def observe(self, fb: FeedbackRound) -> dict | None:
-        self.replay.append(fb)
+    def observe(self, fb: FeedbackRound) -> bool:
+        """Record one verified round; runs an update every ``stride`` verified blocks."""
         before = self.blocks_seen // self.config.stride
-        self.blocks_seen += fb.block_ids.shape[0]
+        self.blocks_seen += fb.blocks
         if self.blocks_seen // self.config.stride > before:
-            return self.update()
-        return None
+            self.update(fb)
+            return True
+        return False
 
-    def _forward_loss(self, fb: FeedbackRound, params: dict[str, torch.Tensor]) -> torch.Tensor:
+    # ---- replayed suffix forward + loss (static shapes, no host syncs) ----
+    def _loss(self, fb: FeedbackRound) -> torch.Tensor:
         r = self.head.runner
         cfg = r.cfg
         comm = r.comm
         lw = r.w.layers[-1]
         kc, vc = r.cache.layer(cfg.num_hidden_layers - 1)
         B, Kb = fb.block_ids.shape
-        D, H = 128, cfg.hidden_size
+        D = 128
         eps = cfg.rms_norm_eps
-        emb = r.w.embed[fb.block_ids.long()].float()                      # [B, K, H]
+        params = self._views(self.master)
+        bf = torch.bfloat16
 
         def norm(x, w):
             return x * torch.rsqrt(x.square().mean(-1, keepdim=True) + eps) * w.float()
 
+        def mm(x, w):  # bf16 tensor-core matmul with fp32 result
+            return (x.to(bf) @ w.to(bf).t()).float()
+
+        emb = r.w.embed[fb.block_ids.long()].float()                        # [B, K, H]
         x = _copy(norm(emb, lw.in_norm), comm)
-        qkv = x @ params["w_qkv"].t()
+        qkv = mm(x, params["w_qkv"])
         if "b_qkv" in params:
             qkv = qkv + params["b_qkv"]
         qs, ks = r.q_slots, r.kv_slots
+        G = qs // ks
         q = qkv[..., : qs * D].view(B, Kb, qs, D)
         k = qkv[..., qs * D:(qs + ks) * D].view(B, Kb, ks, D)
         v = qkv[..., (qs + ks) * D:(qs + 2 * ks) * D].view(B, Kb, ks, D)
         if "q_norm" in params:
             q = norm(q, params["q_norm"])
             k = norm(k, params["k_norm"])
-        inv = r.w.inv_freq
-        ang = fb.positions.float()[..., None] * inv                          # [B, K, D/2]
+        ang = fb.positions.float()[..., None] * r.w.inv_freq                # [B, K, D/2]
         cos, sin = ang.cos()[:, :, None], ang.sin()[:, :, None]
 
         def rope(t):
@@ -273,46 +293,44 @@ class SuffixLearner:
             return torch.cat((a * cos - b * sin, b * cos + a * sin), -1)
 
         q, k = rope(q), rope(k)
-        Lmax = max(fb.hist_len) if fb.hist_len else 0
-        G = qs // ks
-        pages_needed = -(-Lmax // 32) if Lmax else 0
-        if pages_needed:
-            table = torch.tensor([p[:pages_needed] + [0] * (pages_needed - len(p[:pages_needed])) for p in fb.hist_pages],
-                                 dtype=torch.long, device=emb.device)
-            hk = kc[table].permute(0, 2, 1, 3, 4).reshape(B, ks, pages_needed * 32, D)[:, :, :Lmax].float()
-            hv = vc[table].permute(0, 2, 1, 3, 4).reshape(B, ks, pages_needed * 32, D)[:, :, :Lmax].float()
-        else:
-            hk = hv = torch.zeros(B, ks, 0, D, device=emb.device)
-        kk = torch.cat((hk, k.permute(0, 2, 1, 3)), 2)                      # [B, ks, L+K, D]
-        vv = torch.cat((hv, v.permute(0, 2, 1, 3)), 2)
-        qq = q.permute(0, 2, 1, 3).reshape(B, ks, G, Kb, D).reshape(B, ks, G * Kb, D)
-        scores = qq @ kk.transpose(-1, -2) / math.sqrt(D)                   # [B, ks, G*K, L+K]
-        hl = torch.tensor(fb.hist_len, device=emb.device)
-        key = torch.arange(Lmax + Kb, device=emb.device)
-        visible = (key[None, :] < hl[:, None]) | (key[None, :] >= Lmax)      # history (ragged) + block
-        scores = scores.masked_fill(~visible[:, None, None, :], float("-inf"))
-        att = (scores.softmax(-1) @ vv).view(B, ks, G, Kb, D).permute(0, 3, 1, 2, 4).reshape(B, Kb, qs * D)
-        h = emb + _reduce(att @ params["w_o"].t(), comm)
+        P = fb.table.shape[1]
+        tbl = fb.table.long()
+        hk = kc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, P * 32, D)       # [B, ks, L, D] bf16
+        hv = vc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, P * 32, D)
+        qq = q.permute(0, 2, 1, 3).reshape(B, ks, G * Kb, D)                # [B, ks, G*K, D]
+        kb = k.permute(0, 2, 1, 3)                                          # [B, ks, K, D]
+        vb = v.permute(0, 2, 1, 3)
+        scale = D ** -0.5
+        s_hist = (qq.to(bf) @ hk.transpose(-1, -2)).float() * scale          # [B, ks, G*K, L]
+        s_blk = (qq @ kb.transpose(-1, -2)) * scale                          # [B, ks, G*K, K]
+        key = torch.arange(P * 32, device=emb.device)
+        visible = key[None, :] < fb.positions[:, :1]                          # [B, L] history keys
+        s_hist = s_hist.masked_fill(~visible[:, None, None, :], float("-inf"))
+        prob = torch.cat((s_hist, s_blk), -1).softmax(-1)
+        att = (prob[..., : P * 32].to(bf) @ hv).float() + prob[..., P * 32:] @ vb
+        att = att.view(B, ks, G, Kb, D).permute(0, 3, 1, 2, 4).reshape(B, Kb, qs * D)
+        h = emb + _reduce(mm(att, params["w_o"]), comm)
         x2 = _copy(norm(h, lw.post_norm), comm)
-        gu = (x2.to(torch.bfloat16) @ lw.w_gu.t()).float()
-        gu = gu.view(B, Kb, -1, 2, 64)
+        gu = mm(x2, lw.w_gu).view(B, Kb, -1, 2, 64)
         act = (F.silu(gu[..., 0, :]) * gu[..., 1, :]).reshape(B, Kb, -1)
-        h = h + _reduce((act.to(torch.bfloat16) @ lw.w_down.t()).float(), comm)
-        y = _copy(norm(h[:, : Kb - 1], r.w.final_norm), comm)
-        logits = (y.to(torch.bfloat16) @ r.w.head.t()).float()              # [B, K-1, V_local]
-        rows = torch.arange(Kb - 1, device=emb.device)[None, :] < fb.valid[:, None]
-        return self._divergence(logits[rows], fb.teacher[rows], comm), int(rows.sum())
+        h = h + _reduce(mm(act, lw.w_down), comm)
+        y = _copy(norm(h[:, : Kb - 1], r.w.final_norm), comm)                # [B, K-1, H]
+        teacher = fb.teacher.view(B, Kb, -1)[:, : Kb - 1].reshape(B * (Kb - 1), -1)
+        per = K.head_divergence(y.reshape(B * (Kb - 1), -1), r.w.head, teacher, self.config.loss,
+                                comm if comm.world > 1 else None).view(B, Kb - 1)
+        valid = torch.minimum(fb.count + 1, torch.full_like(fb.count, Kb - 1))
+        w = (torch.arange(Kb - 1, device=emb.device)[None, :] < valid[:, None]).float() * fb.active[:, None]
+        return (per * w).sum() / w.sum().clamp_min(1.0)
 
     def _divergence(self, student: torch.Tensor, teacher: torch.Tensor, comm) -> torch.Tensor:
-        """Sum over rows of TV or KL(teacher || student) over the (possibly sharded) vocabulary."""
+        """Per-row TV or KL(teacher || student) over the (possibly vocabulary-sharded) rows."""
         def lse(z):
             m = z.max(-1, keepdim=True).values.detach()
             if comm.world > 1:
                 import torch.distributed as dist
 
                 dist.all_reduce(m, op=dist.ReduceOp.MAX, group=comm.group)
-            s = _reduce((z - m).exp().sum(-1, keepdim=True), comm)
-            return m + s.log()
+            return m + _reduce((z - m).exp().sum(-1, keepdim=True), comm).log()
 
         log_q = student - lse(student)
         with torch.no_grad():
@@ -321,56 +339,69 @@ class SuffixLearner:
             per = 0.5 * (log_q.exp() - log_p.exp()).abs().sum(-1)
         else:
             per = (log_p.exp() * (log_p - log_q)).sum(-1)
-        return _reduce(per.sum(), comm)
+        return _reduce(per, comm)
 
-    def update(self) -> dict | None:
-        if not self.replay:
-            return None
+    def _step(self, fb: FeedbackRound) -> None:
+        loss = self._loss(fb)
+        (grad,) = torch.autograd.grad(loss, [self.master])
+        self.loss_buf.copy_(loss.detach())
+        self.step_t.add_(1)
+        K.adamw_step(self.master.data, grad, self.exp_avg, self.exp_avg_sq, step=1, lr=self.config.learning_rate,
+                     weight_decay=0.0, clip=self.config.clip_norm, publish=self.head.draft.flat,
+                     norm_out=self.norm_buf, nonfinite=self.nonfinite, step_tensor=self.step_t)
+
+    def update(self, fb: FeedbackRound) -> None:
         dev = self.master.device
-        if dev.type == "cuda":
-            torch.cuda.synchronize(dev)
         start = time.perf_counter()
-        params = {n: t.detach().clone().requires_grad_(True) for n, t in self._views(self.master).items()}
-        total = 0.0
-        rows = sum(int(fb.valid.sum()) for fb in self.replay)
-        grads = {n: torch.zeros_like(p) for n, p in params.items()}
-        for fb in self.replay:
-            loss, _ = self._forward_loss(fb, params)
-            loss = loss / max(rows, 1)
-            if not torch.isfinite(loss):
-                raise FloatingPointError("nonfinite online suffix loss")
-            g = torch.autograd.grad(loss, list(params.values()))
-            for n, gi in zip(params, g):
-                grads[n] += gi
-            total += float(loss.detach())
-        flat_g = self._views(self.grad)
-        for n in params:
-            flat_g[n].copy_(grads[n])
+        if self.use_graphs:
+            key = (fb.block_ids.data_ptr(), fb.teacher.data_ptr(), tuple(fb.block_ids.shape))
+            g = self._graphs.get(key)
+            if g is None:
+                g = self._capture(fb)
+                self._graphs[key] = g
+            g.replay()
+        else:
+            self._step(fb)
         self.step += 1
-        K.adamw_step(self.master, self.grad, self.exp_avg, self.exp_avg_sq, step=self.step,
-                     lr=self.config.learning_rate, weight_decay=0.0, clip=self.config.clip_norm,
-                     publish=self.head.draft.flat, norm_out=self.norm_buf, nonfinite=self.nonfinite)
-        if dev.type == "cuda":
-            torch.cuda.synchronize(dev)
-        elapsed = time.perf_counter() - start
         self.updates += 1
-        self.update_seconds += elapsed
-        self.last_loss = total
-        self.replay.clear()
-        return {"loss": total, "gradient_norm": float(self.norm_buf.sqrt()), "seconds": elapsed,
-                "version": self.updates}
+        self.update_seconds += time.perf_counter() - start
+
+    def _capture(self, fb: FeedbackRound) -> "torch.cuda.CUDAGraph":
+        # warm up autograd on a side stream without changing the optimizer state
+        saved = [t.clone() for t in (self.master.data, self.exp_avg, self.exp_avg_sq, self.step_t,
+                                     self.head.draft.flat)]
+        s = torch.cuda.Stream(device=self.master.device)
+        s.wait_stream(torch.cuda.current_stream(self.master.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._step(fb)
+        torch.cuda.current_stream(self.master.device).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self._step(fb)
+        for t, v in zip((self.master.data, self.exp_avg, self.exp_avg_sq, self.step_t, self.head.draft.flat), saved):
+            t.copy_(v)
+        return g
+
+    def close(self) -> None:
+        """Drop captured update graphs (call before destroying a process group)."""
+        self._graphs.clear()
+
+    def check_finite(self) -> None:
+        if int(self.nonfinite.item()):
+            self.nonfinite.zero_()
+            raise FloatingPointError("nonfinite online suffix gradient; the step was skipped")
 
     # ---- checkpoint (format "blockspec-dual-suffix-v1" fields) ----
     def state_dict(self) -> dict:
-        if self.replay:
-            raise ValueError("save online state at a request boundary after clearing replay")
+        self.check_finite()
         return {"format": "blockspec-dual-suffix-v1", "config": asdict(self.config),
                 "model_config": self.head.runner.cfg.to_dict(), "frozen_fingerprint": self.frozen_fingerprint,
-                "master": self.master.cpu().clone(),
+                "master": self.master.detach().cpu().clone(),
                 "optimizer": {"exp_avg": self.exp_avg.cpu().clone(), "exp_avg_sq": self.exp_avg_sq.cpu().clone(),
-                              "step": self.step},
+                              "step": int(self.step_t.item())},
                 "rounds": self.blocks_seen, "updates": self.updates, "version": self.updates,
-                "update_seconds": self.update_seconds, "last_loss": self.last_loss}
+                "update_seconds": self.update_seconds, "last_loss": self.last_loss if self.updates else None}
 
     def load_state_dict(self, state: dict) -> None:
         if (state.get("format") != "blockspec-dual-suffix-v1" or state.get("config") != asdict(self.config)
@@ -380,13 +411,15 @@ class SuffixLearner:
         master = state["master"]
         if master.shape != self.master.shape or master.dtype != torch.float32 or not torch.isfinite(master).all():
             raise ValueError("finite FP32 suffix masters of matching shape required")
-        self.master.copy_(master)
+        with torch.no_grad():
+            self.master.copy_(master)
         self.exp_avg.copy_(state["optimizer"]["exp_avg"])
         self.exp_avg_sq.copy_(state["optimizer"]["exp_avg_sq"])
         self.step = int(state["optimizer"]["step"])
+        self.step_t.fill_(self.step)
         self.blocks_seen = int(state["rounds"])
         self.updates = int(state["updates"])
         self.update_seconds = float(state["update_seconds"])
-        self.last_loss = state["last_loss"]
-        self.head.draft.flat.copy_(self.master)
-        self.replay.clear()
+        if state["last_loss"] is not None:
+            self.loss_buf.fill_(float(state["last_loss"]))
+        self.head.draft.flat.copy_(self.master.detach())

@@ -86,7 +86,7 @@ class _RoundGraph:
         # int32 metadata packed for one H2D copy: positions, slots, kv_len, table, anchors, streams
         self.n_pos = B * Kb
         self.layout = [("positions", B * Kb), ("slots", B * Kb), ("kv_len", B), ("table", B * mp),
-                       ("anchors", B), ("streams", B)]
+                       ("anchors", B), ("streams", B), ("active", B)]
         total = sum(n for _, n in self.layout)
         self.host = torch.zeros(total, dtype=torch.int32).pin_memory()
         self.dev = torch.zeros(total, dtype=torch.int32, device=dev)
@@ -95,11 +95,21 @@ class _RoundGraph:
             self.views[name] = self.dev[off:off + n]
             off += n
         self.host_views, off = {}, 0
+        host_np = self.host.numpy()
         for name, n in self.layout:
-            self.host_views[name] = self.host[off:off + n]
+            self.host_views[name] = host_np[off:off + n]
             off += n
+        self.seeds_np = None
         self.seeds_host = torch.zeros(B, dtype=torch.int64).pin_memory()
+        self.seeds_np = self.seeds_host.numpy()
         self.seeds = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.active = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.stats = {"inv_target": torch.full((B * Kb,), engine.inv_temp, dtype=torch.float32, device=dev),
+                      "inv_draft": torch.full((B * (Kb - 1),), engine.inv_temp, dtype=torch.float32, device=dev),
+                      "lse1_t": torch.zeros(B * Kb, dtype=torch.float32, device=dev),
+                      "lseT_t": torch.zeros(B * Kb, dtype=torch.float32, device=dev),
+                      "lse1_d": torch.zeros(B * (Kb - 1), dtype=torch.float32, device=dev),
+                      "lseT_d": torch.zeros(B * (Kb - 1), dtype=torch.float32, device=dev)}
         table = self.views["table"].view(B, mp)
         ql = [Kb] * B
         mk = lambda v: torch.full((B,), v, dtype=torch.int32, device=dev)
@@ -142,6 +152,7 @@ class _RoundGraph:
         e, B, Kb = self.e, self.B, self.e.block
         v = self.views
         self.ids_draft[:, 0].copy_(v["anchors"])
+        self.active.copy_(v["active"])
         self.row_streams.copy_(v["streams"].repeat_interleave(Kb - 1))
         meta_d = StepMeta(self.ids_draft.view(-1), v["positions"], v["slots"], self.plan_draft, self.draft_rows)
         dl = e.head.forward(meta_d, self.draft_rows)
@@ -153,9 +164,9 @@ class _RoundGraph:
         self.ids_verify[:, 1:].copy_(self.cand.view(B, Kb - 1))
         meta_v = StepMeta(self.ids_verify.view(-1), v["positions"], v["slots"], self.plan_verify, None)
         tl = e.runner.forward(meta_v)
-        self.teacher = tl
+        self.teacher = e.runner.last_local_logits
         K.spec_verify(tl, draft_logits, self.cand.view(B, Kb - 1), self.inv_temp, self.seeds, streams=v["streams"],
-                      salt=0x777, out=self.out)
+                      salt=0x777, out=self.out, stats=self.stats)
         o = self.out
         self.result[:, 0].copy_(o["count"])
         self.result[:, 1].copy_(o["valid"])
@@ -336,60 +347,61 @@ class MHEngine:
         Kb = self.block
         self.cache.flush_copies()
         g = self._graph(len(jobs))
-        B = g.B
+        B, nj = g.B, len(jobs)
         hv = g.host_views
-        pos = hv["positions"].view(B, Kb)
-        slots = hv["slots"].view(B, Kb)
-        table = hv["table"].view(B, g.mp)
-        seqs = []
-        for b, j in enumerate(jobs):
-            s = self.cache.append(j.seq, Kb)
-            slots[b] = torch.tensor(s, dtype=torch.int32)
-            pos[b] = torch.arange(j.n, j.n + Kb, dtype=torch.int32)
-            hv["kv_len"][b] = j.n + Kb
-            hv["anchors"][b] = j.anchor
-            hv["streams"][b] = j.rounds
-            g.seeds_host[b] = j.seed & ((1 << 63) - 1)
-            seqs.append(j.seq)
-        self.cache.fill_table(seqs, table[: len(jobs)])
-        for b in range(len(jobs), B):  # padding rows: one visible key, no cache writes
-            slots[b] = -1
-            pos[b] = torch.arange(Kb, dtype=torch.int32)
-            hv["kv_len"][b] = Kb
-            hv["anchors"][b] = 0
-            hv["streams"][b] = 0
-            table[b] = 0
+        seqs = [j.seq for j in jobs]
+        n = np.fromiter((j.n for j in jobs), dtype=np.int64, count=nj)
+        slots = np.asarray(self.cache.manager.append_many(seqs, Kb), dtype=np.int32).reshape(nj, Kb)
+        pos = hv["positions"].reshape(B, Kb)
+        sl = hv["slots"].reshape(B, Kb)
+        pos[:nj] = n[:, None] + np.arange(Kb)
+        sl[:nj] = slots
+        hv["kv_len"][:nj] = n + Kb
+        hv["anchors"][:nj] = [j.anchor for j in jobs]
+        hv["streams"][:nj] = [j.rounds for j in jobs]
+        hv["active"][:nj] = 1
+        g.seeds_np[:nj] = [j.seed & ((1 << 63) - 1) for j in jobs]
+        table = hv["table"].reshape(B, g.mp)
+        self.cache.manager.fill_table_np(seqs, table[:nj])
+        if nj < B:  # padding rows: one visible block, no cache writes
+            pos[nj:] = np.arange(Kb)
+            sl[nj:] = -1
+            hv["kv_len"][nj:] = Kb
+            hv["anchors"][nj:] = 0
+            hv["streams"][nj:] = 0
+            hv["active"][nj:] = 0
+            table[nj:] = 0
         res = g.run().numpy()
-        generated = 0
         counts = res[:, 0].astype(np.int64)
-        if (res[: len(jobs), 1] == 0).any():
+        if (res[:nj, 1] == 0).any():
             raise RuntimeError("speculative correction reported invalid probabilities")
         if self.learner is not None:
-            fb = FeedbackRound(
-                block_ids=g.ids_draft[: len(jobs)].clone(), positions=g.views["positions"].view(B, Kb)[: len(jobs)].clone(),
-                hist_pages=[list(self.cache.manager.pages(j.seq)) for j in jobs], hist_len=[j.n for j in jobs],
-                teacher=g.teacher.view(B, Kb, -1)[: len(jobs), : Kb - 1].clone(),
-                valid=torch.as_tensor(np.minimum(counts[: len(jobs)] + 1, Kb - 1), device=self.device))
-            if self.learner.observe(fb) is not None:
+            fb = FeedbackRound(g.ids_draft, g.views["positions"].view(B, Kb), g.views["table"].view(B, g.mp),
+                               g.teacher, g.out["count"], g.active, nj)
+            if self.learner.observe(fb):
                 self.stats["learner_updates"] += 1
+        generated = 0
         finished = []
+        emitted = res[:, 2:2 + Kb].astype(np.int64)
+        logq = res[:, 2 + Kb:2 + 2 * Kb]
+        logp = res[:, 2 + 2 * Kb:2 + 3 * Kb]
+        new_len = n + 1 + counts[:nj]
+        self.cache.manager.truncate_many(seqs, new_len.tolist())
         for b, j in enumerate(jobs):
             c = int(counts[b])
             take = min(c + 1, j.need - len(j.tokens))
-            em = res[b, 2:2 + Kb].astype(np.int64)
-            j.tokens += [int(x) for x in em[:take]]
-            j.logq += [float(x) for x in res[b, 2 + Kb:2 + Kb + take]]
-            j.logp += [float(x) for x in res[b, 2 + 2 * Kb:2 + 2 * Kb + take]]
+            j.tokens.extend(emitted[b, :take].tolist())
+            j.logq.extend(logq[b, :take].tolist())
+            j.logp.extend(logp[b, :take].tolist())
             generated += take
-            self.stats["emitted"] += c + 1
             j.rounds += 1
-            self.cache.truncate(j.seq, j.n + 1 + c)
-            j.anchor = int(em[c])
-            j.n = j.n + 1 + c
+            j.anchor = int(emitted[b, c])
+            j.n = int(new_len[b])
             if len(j.tokens) >= j.need:
                 finished.append(j)
+        self.stats["emitted"] += int((counts[:nj] + 1).sum())
         self.stats["rounds"] += 1
-        self.stats["blocks"] += len(jobs)
+        self.stats["blocks"] += nj
         self.stats["generated"] += generated
         for j in finished:
             self._finish(j)
@@ -402,6 +414,20 @@ class MHEngine:
             total += self.round()
             rounds += 1
         return total
+
+    def close(self) -> None:
+        """Release captured CUDA graphs (they may hold collective calls) and free the KV bookkeeping.
+
+        Call this before tearing down a process group: a graph that captured
+        NCCL work keeps the communicator busy at exit otherwise.
+        """
+        torch.cuda.synchronize(self.device)
+        for g in self._graphs.values():
+            g.graph = None
+        self._graphs.clear()
+        if self.learner is not None:
+            self.learner.close()
+        torch.cuda.synchronize(self.device)
 
     @property
     def mean_accept_length(self) -> float:

@@ -27,17 +27,39 @@ from .kv_cache import KVCache
 
 
 class Collectives:
-    """Tensor-parallel reductions used by the runner (identity when tp == 1)."""
+    """Tensor-parallel reductions used by the runner.
 
-    def __init__(self, group=None):
+    ``tp == 1``: identity.  Otherwise a communicator from
+    :mod:`online_speculation_b200.parallel.symm` (fused peer-memory all-reduce
+    + residual add + RMSNorm, or its NCCL baseline) provides
+    ``partial_buffer`` / ``reduce_add_norm``.
+    """
+
+    def __init__(self, group=None, *, hidden: int = 0, max_tokens: int = 0, device=None, fused: bool = True):
         self.group = group
+        self.impl = None
         if group is None:
             self.world, self.rank = 1, 0
-        else:
-            import torch.distributed as dist
+            return
+        import torch.distributed as dist
 
-            self.world = dist.get_world_size(group)
-            self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 1 and hidden:
+            from ..parallel.symm import NcclCollectives, SymmetricCollectives
+
+            cls = SymmetricCollectives if fused else NcclCollectives
+            self.impl = cls(group, hidden, max_tokens, device)
+
+    def partial_buffer(self, T: int, scratch: torch.Tensor) -> torch.Tensor:
+        return scratch if self.impl is None else self.impl.partial_buffer(T)
+
+    def reduce_add_norm(self, part, h, w, x, eps):
+        if self.impl is not None:
+            self.impl.reduce_add_norm(part, h, w, x, eps)
+        else:
+            self.all_reduce(part)
+            K.rmsnorm(h, w, eps, out=x, residual=h, delta=part)
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
@@ -133,8 +155,8 @@ class ModelRunner:
         wo = lw.w_o if wo is None else wo
         if self.comm.world == 1 and residual is not None:
             return K.linear(att.view(T, -1), wo, residual=residual, out=residual)
-        part = K.linear(att.view(T, -1), wo, out=self._buf("part", (T, self.cfg.hidden_size)))
-        return self.comm.all_reduce(part)
+        part = self.comm.partial_buffer(T, self._buf("part", (T, self.cfg.hidden_size)))
+        return K.linear(att.view(T, -1), wo, out=part)
 
     def mlp_block(self, i: int, x: torch.Tensor, residual: torch.Tensor | None) -> torch.Tensor:
         lw = self.w.layers[i]
@@ -142,33 +164,34 @@ class ModelRunner:
         act = K.linear(x, lw.w_gu, swiglu=True, out=self._buf("act", (T, lw.w_gu.shape[0] // 2)))
         if self.comm.world == 1 and residual is not None:
             return K.linear(act, lw.w_down, residual=residual, out=residual)
-        part = K.linear(act, lw.w_down, out=self._buf("part", (T, self.cfg.hidden_size)))
-        return self.comm.all_reduce(part)
+        part = self.comm.partial_buffer(T, self._buf("part", (T, self.cfg.hidden_size)))
+        return K.linear(act, lw.w_down, out=part)
 
     def layer_stack(self, h: torch.Tensor, meta: StepMeta, layers: range) -> torch.Tensor:
-        """Run decoder layers over the residual stream ``h`` (updated in place)."""
+        """Run decoder layers over the residual stream ``h`` (updated in place).
+
+        Under tensor parallelism the buffer ``x`` holds, on return, the input of
+        the layer after the range normalised by that layer's input norm (or by
+        the final norm after the last layer).
+        """
         eps = self.cfg.rms_norm_eps
         T = h.shape[0]
         x = self._buf("x", (T, self.cfg.hidden_size))
-        pending = None  # partial sum waiting to be added (tp > 1)
-        for i in layers:
+        L = self.cfg.num_hidden_layers
+        tp = self.comm.world > 1
+        for n, i in enumerate(layers):
             lw = self.w.layers[i]
-            if pending is None:
+            if n == 0 or not tp:
                 K.rmsnorm(h, lw.in_norm, eps, out=x)
+            part = self.attention_block(i, x, meta, residual=h)
+            if tp:
+                self.comm.reduce_add_norm(part, h, lw.post_norm, x, eps)
             else:
-                K.rmsnorm(h, lw.in_norm, eps, out=x, residual=h, delta=pending)
-            pending = self.attention_block(i, x, meta, residual=h)
-            if self.comm.world == 1:
-                pending = None
                 K.rmsnorm(h, lw.post_norm, eps, out=x)
-            else:
-                K.rmsnorm(h, lw.post_norm, eps, out=x, residual=h, delta=pending)
-            pending = self.mlp_block(i, x, residual=h)
-            if self.comm.world == 1:
-                pending = None
-        if pending is not None:
-            # fold the last partial sum into the residual stream
-            K.rmsnorm(h, self.w.final_norm, eps, out=x, residual=h, delta=pending)
+            part = self.mlp_block(i, x, residual=h)
+            if tp:
+                nxt = self.w.layers[i + 1].in_norm if i + 1 < L else self.w.final_norm
+                self.comm.reduce_add_norm(part, h, nxt, x, eps)
         return h
 
     def logits(self, h: torch.Tensor, rows: torch.Tensor | None, *, normed: bool = False,
@@ -180,6 +203,7 @@ class ModelRunner:
                                          out=self._buf("xl", (R, self.cfg.hidden_size)))
         local = K.linear(x, self.w.head, out=self._buf("logits_local", (R, self.vocab_local), torch.float32),
                          out_dtype=torch.float32)
+        self.last_local_logits = local  # this rank's vocabulary shard (static buffer)
         if self.comm.world == 1:
             return local
         full = out if out is not None else self._buf("logits_full", (R, self.vocab_local * self.comm.world),

@@ -335,11 +335,15 @@ def gumbel_sample(logits, inv_temp, seeds, *, seed_index=None, streams=None, row
     return tokens
 
 
-def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, salt=0, out=None):
+def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, salt=0, out=None, stats=None):
     """Exact p/q correction of a batch of draft blocks.
 
     ``target`` [B*(n+1), V] logits, ``draft`` [B*n, V] logits, ``candidates`` [B, n].
     Returns dict of count, tail, valid, emitted [B, n+1], logq, logp [B, n+1].
+    On CUDA the row log-normalisers are first computed by the row-parallel
+    statistics kernel (one CTA per row); ``stats`` may hold preallocated
+    buffers (``inv_target`` [B*(n+1)], ``inv_draft`` [B*n], ``lse1_t``,
+    ``lseT_t``, ``lse1_d``, ``lseT_d``) for graph capture.
     """
     B, n = candidates.shape
     dev = target.device
@@ -352,8 +356,19 @@ def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, sal
         "logp": torch.empty(B, n + 1, dtype=torch.float32, device=dev),
     }
     if target.is_cuda:
-        _ext.require().spec_verify(target, draft, candidates, n, inv_temp, seeds, streams, int(salt), res["count"],
-                                   res["tail"], res["valid"], res["emitted"], res["logq"], res["logp"])
+        ext = _ext.require()
+        if stats is None:
+            it = inv_temp if inv_temp is not None else torch.ones(B, dtype=torch.float32, device=dev)
+            stats = {"inv_target": it.repeat_interleave(n + 1), "inv_draft": it.repeat_interleave(n),
+                     "lse1_t": torch.empty(B * (n + 1), dtype=torch.float32, device=dev),
+                     "lseT_t": torch.empty(B * (n + 1), dtype=torch.float32, device=dev),
+                     "lse1_d": torch.empty(B * n, dtype=torch.float32, device=dev),
+                     "lseT_d": torch.empty(B * n, dtype=torch.float32, device=dev)}
+        ext.row_stats(target, stats["inv_target"], None, stats["lse1_t"], stats["lseT_t"], None, None)
+        ext.row_stats(draft, stats["inv_draft"], None, stats["lse1_d"], stats["lseT_d"], None, None)
+        ext.spec_verify(target, draft, candidates, n, inv_temp, seeds, streams, int(salt), res["count"],
+                        res["tail"], res["valid"], res["emitted"], res["logq"], res["logp"], stats["lseT_t"],
+                        stats["lse1_t"], stats["lseT_d"])
         return res
     gen = torch.Generator().manual_seed(int(seeds.flatten()[0]) ^ int(salt))
     for b in range(B):
@@ -383,8 +398,12 @@ def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, sal
 
 # ------------------------------------------------------------------ adamw --
 def adamw_step(params, grads, exp_avg, exp_avg_sq, *, step, lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
-               clip=None, publish=None, norm_out=None, nonfinite=None):
-    """Fused AdamW on flat fp32 buffers with global-norm clipping; optional bf16 publish."""
+               clip=None, publish=None, norm_out=None, nonfinite=None, step_tensor=None):
+    """Fused AdamW on flat fp32 buffers with global-norm clipping; optional bf16 publish.
+
+    ``step_tensor`` (int32 [1] on the device) supplies the step for the bias
+    corrections instead of ``step``, so the update can be replayed from a graph.
+    """
     if params.is_cuda:
         ext = _ext.require()
         sq = None
@@ -392,7 +411,7 @@ def adamw_step(params, grads, exp_avg, exp_avg_sq, *, step, lr, betas=(0.9, 0.99
             sq = norm_out if norm_out is not None else torch.empty(1, dtype=torch.float32, device=params.device)
             ext.grad_sq_norm(grads, sq)
         ext.adamw(params, grads, exp_avg, exp_avg_sq, publish, sq, float(clip or 0.0), float(lr), float(betas[0]),
-                  float(betas[1]), float(eps), float(weight_decay), int(step), nonfinite)
+                  float(betas[1]), float(eps), float(weight_decay), int(step), nonfinite, step_tensor)
         return sq
     scale = 1.0
     sq = grads.float().square().sum()
@@ -407,8 +426,70 @@ def adamw_step(params, grads, exp_avg, exp_avg_sq, *, step, lr, betas=(0.9, 0.99
     params.mul_(1 - lr * weight_decay)
     exp_avg.mul_(betas[0]).add_(g, alpha=1 - betas[0])
     exp_avg_sq.mul_(betas[1]).addcmul_(g, g, value=1 - betas[1])
+    if step_tensor is not None:
+        step = int(step_tensor.flatten()[0])
     bc1, bc2 = 1 - betas[0] ** step, 1 - betas[1] ** step
     params.addcdiv_(exp_avg / bc1, (exp_avg_sq / bc2).sqrt().add_(eps), value=-lr)
     if publish is not None:
         publish.copy_(params)
     return sq
+
+
+# ------------------------------------------------- head + distillation loss --
+class _HeadDivergence(torch.autograd.Function):
+    """Per-row TV / forward-KL between softmax(y @ W^T) and softmax(teacher).
+
+    Forward: tcgen05 GEMM to fp32 logits, then the fused statistics and loss
+    kernels (two passes over the logits).  Backward: one kernel writes
+    d loss / d logits in bf16, then d y = d logits @ W.  Under a
+    vocabulary-sharded head the row statistics and loss pieces are all-reduced
+    across ranks between the phases.
+    """
+
+    @staticmethod
+    def forward(ctx, y, weight, teacher, kind, comm):
+        ext = _ext.require()
+        R = y.shape[0]
+        logits = linear(y.to(torch.bfloat16).contiguous(), weight, out_dtype=torch.float32)
+        stats = torch.empty(R, 4, dtype=torch.float32, device=y.device)
+        ext.divergence_stats(logits, teacher, stats)
+        world = 1 if comm is None else comm.world
+        if world > 1:
+            import torch.distributed as dist
+
+            m = stats[:, 0::2].contiguous()
+            dist.all_reduce(m, op=dist.ReduceOp.MAX, group=comm.group)
+            sums = stats[:, 1::2] * torch.exp(stats[:, 0::2] - m)
+            dist.all_reduce(sums, group=comm.group)
+            lse = (m + sums.log()).contiguous()
+        else:
+            lse = (stats[:, 0::2] + stats[:, 1::2].log()).contiguous()
+        pieces = torch.empty(R, 2, dtype=torch.float32, device=y.device)
+        ext.divergence_loss(logits, teacher, lse, int(kind), pieces)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(pieces, group=comm.group)
+        ctx.save_for_backward(logits, teacher, lse, pieces, weight)
+        ctx.kind = int(kind)
+        return pieces[:, 0].clone()
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, teacher, lse, pieces, weight = ctx.saved_tensors
+        grad = torch.empty(logits.shape, dtype=torch.bfloat16, device=logits.device)
+        _ext.require().divergence_grad(logits, teacher, lse, pieces, g.float().contiguous(), ctx.kind, grad)
+        dy = (grad @ weight).float()
+        return dy, None, None, None, None
+
+
+def head_divergence(y: torch.Tensor, weight: torch.Tensor, teacher: torch.Tensor, kind: str = "tv", comm=None):
+    """Per-row divergence of the head logits of ``y`` [R, H] from ``teacher`` [R, V_local] logits."""
+    k = 0 if kind == "tv" else 1
+    if y.is_cuda:
+        return _HeadDivergence.apply(y, weight, teacher, k, comm)
+    log_q = (y.float() @ weight.float().t()).log_softmax(-1)
+    log_p = teacher.float().log_softmax(-1)
+    if k == 0:
+        return 0.5 * (log_q.exp() - log_p.exp()).abs().sum(-1)
+    return (log_p.exp() * (log_p - log_q)).sum(-1)

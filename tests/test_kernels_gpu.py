@@ -256,3 +256,21 @@ def test_adamw_matches_torch(cuda):
 def test_status_word_clean_after_kernels(cuda):
     torch.cuda.synchronize()
     workspace.check_status(cuda)
+
+
+@pytest.mark.parametrize("kind", ["tv", "forward_kl"])
+def test_head_divergence_forward_backward(cuda, kind):
+    torch.manual_seed(7)
+    R, H, V = 12, 256, 5000
+    y = torch.randn(R, H, device=cuda, requires_grad=True)
+    w = (torch.randn(V, H, device=cuda) * 0.05).bfloat16()
+    t = torch.randn(R, V, device=cuda) * 2
+    loss = ops.head_divergence(y, w, t, kind)
+    (loss * torch.arange(1, R + 1, device=cuda)).sum().backward()
+    y2 = y.detach().clone().requires_grad_(True)
+    log_q = (y2.bfloat16().float() @ w.float().t()).log_softmax(-1)
+    log_p = t.log_softmax(-1)
+    ref = 0.5 * (log_q.exp() - log_p.exp()).abs().sum(-1) if kind == "tv" else (log_p.exp() * (log_p - log_q)).sum(-1)
+    (ref * torch.arange(1, R + 1, device=cuda)).sum().backward()
+    assert torch.allclose(loss, ref.detach(), atol=2e-3, rtol=2e-3)
+    assert _rel(y.grad, y2.grad) < 3e-2
