@@ -460,6 +460,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              return std::make_pair(id, copies);
            })
       .def("pages", &osb::KVManager::pages)
+      .def("adopt", &osb::KVManager::adopt)
+      .def("retain", &osb::KVManager::retain)
+      .def("drop", &osb::KVManager::drop)
       .def("refcount", &osb::KVManager::refcount)
       .def("append_many",
            [](osb::KVManager& self, const std::vector<int64_t>& seqs, int n) {

@@ -113,6 +113,25 @@ int64_t KVManager::fork(int64_t seq, int n, std::vector<int32_t>& copies) {
 
 const std::vector<int32_t>& KVManager::pages(int64_t seq) const { return get(seq).pages; }
 
+int64_t KVManager::adopt(const std::vector<int32_t>& pages, int length) {
+  const int n = static_cast<int>(pages.size());
+  const bool ok = (n == 0 && length == 0) || (n > 0 && length > (n - 1) * page_size_ && length <= n * page_size_);
+  if (!ok) throw std::invalid_argument("adopted length must end in the last page");
+  for (int32_t p : pages) retain(p);
+  Seq s;
+  s.pages = pages;
+  s.length = length;
+  const int64_t id = next_id_++;
+  seqs_.emplace(id, std::move(s));
+  return id;
+}
+
+void KVManager::retain(int32_t page) {
+  if (page < 0 || page >= static_cast<int32_t>(ref_.size()) || ref_[page] <= 0)
+    throw std::logic_error("retain of a free page");
+  ++ref_[page];
+}
+
 void KVManager::fill_table(const std::vector<int64_t>& seqs, int32_t* out, int stride) const {
   for (size_t r = 0; r < seqs.size(); ++r) {
     const Seq& s = get(seqs[r]);

@@ -47,6 +47,11 @@ class KVManager {
   // unused entries set to 0).
   void fill_table(const std::vector<int64_t>& seqs, int32_t* out, int stride) const;
   int refcount(int page) const { return ref_.at(page); }
+  // New sequence made of existing pages (each gains a reference), `length` tokens.
+  int64_t adopt(const std::vector<int32_t>& pages, int length);
+  // Extra references held by an external owner (e.g. a prefix cache).
+  void retain(int32_t page);
+  void drop(int32_t page) { drop_page(page); }
 
  private:
   struct Seq {

@@ -1,0 +1,444 @@
+"""``AutoregressiveBackend`` on the sm_100a engine: paged KV, prefix cache, graphed decode.
+
+The B200-native counterpart of the reference's ``TransformersBackend``
+(src/inference_scaling/arllm/backends/transformers_backend.py:84-1609) with
+the same contract (:mod:`online_speculation_b200.arllm.types`):
+
+* ``sample_batch`` returns, per request, the sampled tokens, their
+  log-probabilities under the request's policy (temperature T) and under the
+  reference policy (temperature 1, full support) from the same logits.  Token
+  uniforms come from ``np.random.default_rng(seed).random(max_new_tokens)``
+  (or the request's explicit ``uniforms``) and tokens are drawn by inverse CDF
+  over a float64 prefix sum, exactly as the reference draws them, so a
+  request's tokens do not depend on what it is batched with.
+* ``score_batch`` scores continuations with the fused row-statistics kernel
+  (log-sum-exp at T = 1 and at the requested temperature plus the target
+  gather), never materialising a log-softmax.
+
+Prefix reuse: full 32-token pages are keyed by a chained hash of their tokens
+and kept (reference-counted) in a prefix cache, so requests that share a
+prompt -- and suffix-MH proposals that regenerate after a cut -- reuse the KV of
+every cached full page instead of recomputing it.  Only the uncached remainder
+is prefilled, in one packed batch.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import threading
+from collections import OrderedDict
+from collections.abc import Sequence
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..arllm.config import SamplingConfig
+from ..arllm.types import GenerationRequest, ScoreRequest, SequenceSample
+from ..ops import kernels as K
+from .kv_cache import PAGE, KVCache
+from .runner import ModelRunner, StepMeta, build_meta
+
+BASE_POLICY = SamplingConfig().policy_id
+BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 192, 256)
+
+
+class PrefixCache:
+    """Full KV pages keyed by chained token hashes, with LRU eviction.
+
+    The cache owns one reference on every cached page; evicting drops it.
+    """
+
+    def __init__(self, cache: KVCache, max_pages: int):
+        self.cache = cache
+        self.max_pages = max_pages
+        self._pages: OrderedDict[bytes, int] = OrderedDict()
+        self.hits = 0
+        self.lookups = 0
+
+    @staticmethod
+    def keys(tokens: Sequence[int], n_pages: int) -> list[bytes]:
+        out, h = [], b""
+        arr = np.asarray(tokens, dtype=np.int64)
+        for j in range(n_pages):
+            h = hashlib.blake2b(h + arr[j * PAGE:(j + 1) * PAGE].tobytes(), digest_size=16).digest()
+            out.append(h)
+        return out
+
+    def lookup(self, tokens: Sequence[int], limit: int) -> tuple[list[int], list[bytes]]:
+        """Cached leading full pages of ``tokens`` (at most ``limit`` tokens worth)."""
+        n = min(len(tokens), limit) // PAGE
+        keys = self.keys(tokens, n)
+        pages = []
+        for k in keys:
+            p = self._pages.get(k)
+            if p is None:
+                break
+            self._pages.move_to_end(k)
+            pages.append(p)
+        self.lookups += 1
+        self.hits += len(pages)
+        return pages, keys
+
+    def insert(self, keys: list[bytes], pages: list[int]) -> None:
+        mgr = self.cache.manager
+        for k, p in zip(keys, pages):
+            if k in self._pages:
+                self._pages.move_to_end(k)
+                continue
+            mgr.retain(p)
+            self._pages[k] = p
+        self.evict(0)
+
+    def evict(self, need_free: int) -> None:
+        mgr = self.cache.manager
+        while self._pages and (len(self._pages) > self.max_pages or mgr.free_pages < need_free):
+            _, p = self._pages.popitem(last=False)
+            mgr.drop(p)
+
+    def clear(self) -> None:
+        self.evict(1 << 62)
+
+
+@dataclass
+class _Active:
+    index: int
+    request: GenerationRequest
+    seq: int
+    last: int                 # token to feed next (its KV is not written yet)
+    pos: int                  # its position
+    uniforms: np.ndarray
+    tokens: list
+    logq: list
+    logp: list
+    finish: str = "length"
+
+
+class _DecodeGraph:
+    """Static buffers (+ captured graph) of one decode step for B rows."""
+
+    def __init__(self, backend: "EngineBackend", B: int, use_graph: bool):
+        r = backend.runner
+        dev = r.device
+        self.B = B
+        self.mp = backend.max_pages
+        self.host = torch.zeros(4 * B + B * self.mp, dtype=torch.int32).pin_memory()
+        self.dev = torch.zeros_like(self.host, device=dev)
+        hn = self.host.numpy()
+        self.h_ids, self.h_pos, self.h_slots, self.h_kv = (hn[i * B:(i + 1) * B] for i in range(4))
+        self.h_table = hn[4 * B:].reshape(B, self.mp)
+        d = self.dev
+        self.ids, self.pos, self.slots, self.kv = (d[i * B:(i + 1) * B] for i in range(4))
+        self.table = d[4 * B:].view(B, self.mp)
+        self.uni_host = torch.zeros(B, dtype=torch.float64).pin_memory()
+        self.uni = torch.zeros(B, dtype=torch.float64, device=dev)
+        self.it_host = torch.ones(B, dtype=torch.float32).pin_memory()
+        self.inv_temp = torch.ones(B, dtype=torch.float32, device=dev)
+        G = r.q_slots // r.kv_slots
+        tiles = -(-G // 16)
+        self.plan = K.AttentionPlan(
+            self.table, torch.arange(B, dtype=torch.int32, device=dev), torch.ones(B, dtype=torch.int32, device=dev),
+            self.kv, torch.zeros(B, dtype=torch.int32, device=dev),
+            torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles),
+            (torch.arange(tiles, dtype=torch.int32, device=dev) * 16).repeat(B), 16, {})
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.logq = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.logp = torch.zeros(B, dtype=torch.float32, device=dev)
+        self.result = torch.zeros(B, 3, dtype=torch.float32, device=dev)
+        self.result_host = torch.zeros(B, 3, dtype=torch.float32).pin_memory()
+        self.backend = backend
+        self.graph = None
+        if use_graph:
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                for _ in range(2):
+                    self._body()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            torch.cuda.synchronize(dev)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._body()
+            self.graph = g
+
+    def _body(self):
+        r = self.backend.runner
+        logits = r.forward(StepMeta(self.ids, self.pos, self.slots, self.plan, None))
+        K.sample(logits, self.inv_temp, self.uni, tokens=self.tokens, logq=self.logq, logp=self.logp)
+        self.result[:, 0].copy_(self.tokens)
+        self.result[:, 1].copy_(self.logq)
+        self.result[:, 2].copy_(self.logp)
+
+    def run(self) -> np.ndarray:
+        self.dev.copy_(self.host, non_blocking=True)
+        self.uni.copy_(self.uni_host, non_blocking=True)
+        self.inv_temp.copy_(self.it_host, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._body()
+        self.result_host.copy_(self.result, non_blocking=True)
+        torch.cuda.current_stream(self.backend.runner.device).synchronize()
+        return self.result_host.numpy()
+
+
+class EngineBackend:
+    """Batched sampling and scoring on the sm_100a runner (AutoregressiveBackend)."""
+
+    def __init__(self, runner: ModelRunner, *, model_id: str | None = None, max_batch: int = 64,
+                 bos_token_id: int | None = None, use_graphs: bool = True, prefix_cache_pages: int | None = None,
+                 max_seq_tokens: int = 4096, prefill_tokens: int = 4096):
+        self.runner = runner
+        self.cache: KVCache = runner.cache
+        self._model_id = model_id or f"b200:{runner.cfg.name}"
+        self.max_batch = max_batch
+        self.bos_token_id = bos_token_id
+        self.use_graphs = use_graphs
+        self.max_pages = -(-max_seq_tokens // PAGE) + 1
+        self.prefill_tokens = min(prefill_tokens, runner.max_tokens)
+        budget = prefix_cache_pages if prefix_cache_pages is not None else self.cache.num_pages // 2
+        self.prefix = PrefixCache(self.cache, budget)
+        self._graphs: dict[int, _DecodeGraph] = {}
+        self._lock = threading.RLock()
+        self.stats = {"sample_calls": 0, "score_calls": 0, "sampled_sequences": 0, "generated_tokens": 0,
+                      "prefill_tokens": 0, "reused_prefix_tokens": 0, "decode_steps": 0, "scored_tokens": 0}
+
+    @property
+    def model_id(self) -> str:
+        return self._model_id
+
+    @property
+    def vocab_size(self) -> int:
+        return self.runner.cfg.vocab_size
+
+    def snapshot(self) -> dict:
+        return dict(self.stats, prefix_cache_pages=len(self.prefix._pages))
+
+    def close(self) -> None:
+        with self._lock:
+            torch.cuda.synchronize(self.runner.device)
+            for g in self._graphs.values():
+                g.graph = None
+            self._graphs.clear()
+            self.prefix.clear()
+
+    # ------------------------------------------------------------- helpers --
+    def _model_prefix(self, prefix) -> tuple:
+        if prefix:
+            return tuple(prefix)
+        if self.bos_token_id is None:
+            raise ValueError("an empty prefix requires a bos_token_id")
+        return (self.bos_token_id,)
+
+    @staticmethod
+    def _check_policy(s: SamplingConfig) -> None:
+        if not s.full_support:
+            raise NotImplementedError("the fused GPU sampler implements temperature policies; top-k/top-p "
+                                      "truncation is available on the CPU tabular backend")
+
+    def _open(self, tokens: tuple, *, keep_last: bool) -> tuple[int, int]:
+        """KV sequence holding ``tokens`` (minus the last one when ``keep_last``).
+
+        Returns (seq, number of tokens whose KV still has to be computed).
+        """
+        n_kv = len(tokens) - 1 if keep_last else len(tokens)
+        pages, _ = self.prefix.lookup(tokens, n_kv)
+        reused = len(pages) * PAGE
+        seq = self.cache.manager.adopt(pages, reused) if pages else self.cache.create()
+        self.stats["reused_prefix_tokens"] += reused
+        return seq, n_kv - reused
+
+    def _prefill(self, items: list[tuple[int, tuple, int]]) -> None:
+        """Packed prefill of the uncached tails.  items: (seq, tokens, tail_len).
+
+        Long tails are split into ordered chunks of at most ``prefill_tokens``.
+        """
+        r = self.runner
+        G = r.q_slots // r.kv_slots
+        segments = []  # (seq, tokens, count), in causal order per sequence
+        for seq, tokens, tail in items:
+            while tail > 0:
+                n = min(tail, self.prefill_tokens)
+                segments.append((seq, tokens, n))
+                tail -= n
+        groups, chunk, used, seen = [], [], 0, set()
+        for seg in segments:
+            # a sequence appears at most once per packed forward
+            if chunk and (used + seg[2] > self.prefill_tokens or seg[0] in seen):
+                groups.append(chunk)
+                chunk, used, seen = [], 0, set()
+            chunk.append(seg)
+            used += seg[2]
+            seen.add(seg[0])
+        if chunk:
+            groups.append(chunk)
+        for grp in groups:
+            ids, pos, slots, qlens, kvlens, seqs = [], [], [], [], [], []
+            for seq, tokens, n in grp:
+                start = self.cache.length(seq)
+                slots += self.cache.append(seq, n)
+                ids += list(tokens[start:start + n])
+                pos += list(range(start, start + n))
+                qlens.append(n)
+                kvlens.append(start + n)
+                seqs.append(seq)
+            table = torch.zeros(len(grp), self.max_pages, dtype=torch.int32)
+            self.cache.fill_table(seqs, table)
+            meta = build_meta(r.device, table, ids, pos, slots, qlens, kvlens, [0] * len(grp), G,
+                              tile_rows=64 if max(qlens) * G > 64 else None)
+            r.forward(meta, compute_logits=False)
+            self.stats["prefill_tokens"] += len(ids)
+
+    def _cache_pages(self, seq: int, tokens: tuple) -> None:
+        n = min(self.cache.length(seq), len(tokens)) // PAGE
+        if n <= 0:
+            return
+        keys = self.prefix.keys(tokens, n)
+        self.prefix.insert(keys, list(self.cache.manager.pages(seq))[:n])
+
+    def _graph(self, B: int) -> _DecodeGraph:
+        b = next(x for x in BUCKETS if x >= B)
+        g = self._graphs.get(b)
+        if g is None:
+            g = _DecodeGraph(self, b, self.use_graphs)
+            self._graphs[b] = g
+        return g
+
+    # -------------------------------------------------------------- sample --
+    def sample_batch(self, requests: Sequence[GenerationRequest]) -> list[SequenceSample]:
+        with self._lock:
+            out: list[SequenceSample | None] = [None] * len(requests)
+            pending = list(enumerate(requests))
+            while pending:
+                group, pending = pending[: self.max_batch], pending[self.max_batch:]
+                for i, smp in self._sample_group(group):
+                    out[i] = smp
+            self.stats["sample_calls"] += 1
+            self.stats["sampled_sequences"] += len(requests)
+            return out  # type: ignore[return-value]
+
+    def _sample_group(self, group):
+        act: list[_Active] = []
+        opened = []
+        for i, req in group:
+            self._check_policy(req.sampling)
+            if req.arithmetic_uniform is not None:
+                raise NotImplementedError("arithmetic-coding sampling runs on the CPU tabular backend")
+            tokens = self._model_prefix(req.prefix)
+            seq, tail = self._open(tokens, keep_last=True)
+            opened.append((seq, tokens, tail))
+            uni = (np.asarray(req.uniforms, dtype=np.float64) if req.uniforms is not None
+                   else np.random.default_rng(req.seed).random(req.max_new_tokens))
+            act.append(_Active(i, req, seq, tokens[-1], len(tokens) - 1, uni, [], [], []))
+        self.cache.flush_copies()
+        self._prefill(opened)
+        for a, (seq, tokens, _) in zip(act, opened):
+            self._cache_pages(seq, tokens)
+        done: list[_Active] = []
+        while act:
+            g = self._graph(len(act))
+            B, n = g.B, len(act)
+            for b, a in enumerate(act):
+                g.h_slots[b] = self.cache.append(a.seq, 1)[0]
+                g.h_ids[b] = a.last
+                g.h_pos[b] = a.pos
+                g.h_kv[b] = a.pos + 1
+                g.uni_host[b] = float(a.uniforms[len(a.tokens)])
+                g.it_host[b] = 1.0 / a.request.sampling.temperature
+            self.cache.manager.fill_table_np([a.seq for a in act], g.h_table[:n])
+            if n < B:
+                g.h_slots[n:] = -1
+                g.h_ids[n:] = 0
+                g.h_pos[n:] = 0
+                g.h_kv[n:] = 1
+                g.h_table[n:] = 0
+                g.uni_host[n:] = 0.5
+            res = g.run()
+            self.stats["decode_steps"] += 1
+            still = []
+            for b, a in enumerate(act):
+                tok = int(res[b, 0])
+                a.tokens.append(tok)
+                a.logq.append(float(res[b, 1]))
+                a.logp.append(float(res[b, 2]))
+                a.last, a.pos = tok, a.pos + 1
+                eos = a.request.sampling.eos_token_id
+                if eos is not None and tok == eos:
+                    a.finish = "eos"
+                    done.append(a)
+                elif len(a.tokens) >= a.request.max_new_tokens:
+                    done.append(a)
+                else:
+                    still.append(a)
+            act = still
+        results = []
+        for a in done:
+            full = self._model_prefix(a.request.prefix) + tuple(a.tokens)
+            self._cache_pages(a.seq, full)
+            self.cache.release(a.seq)
+            req = a.request
+            results.append((a.index, SequenceSample(
+                tuple(req.prefix), tuple(a.tokens), tuple(a.logq), req.sampling.policy_id, self.model_id,
+                req.request_id, a.finish, tuple(a.logp), BASE_POLICY)))
+            self.stats["generated_tokens"] += len(a.tokens)
+        return results
+
+    # --------------------------------------------------------------- score --
+    def score_batch(self, requests: Sequence[ScoreRequest]) -> list[tuple[float, ...]]:
+        """Per-token log-probabilities of every continuation (policy ``sampling`` or T = 1)."""
+        with self._lock:
+            flat = []
+            for req in requests:
+                if req.sampling is not None:
+                    self._check_policy(req.sampling)
+                for cont in req.continuations:
+                    flat.append((self._model_prefix(req.prefix), tuple(cont), req.sampling))
+            out = [self._score_one(p, c, s) for p, c, s in flat]
+            self.stats["score_calls"] += 1
+            return out
+
+    def _score_one(self, prefix: tuple, cont: tuple, sampling: SamplingConfig | None) -> tuple[float, ...]:
+        if not cont:
+            return ()
+        r = self.runner
+        G = r.q_slots // r.kv_slots
+        full = prefix + cont
+        seq, _ = self._open(full, keep_last=True)
+        self.cache.flush_copies()
+        start = self.cache.length(seq)
+        first_row = len(prefix) - 1        # position whose logits score cont[0]
+        values: list[float] = []
+        it = torch.full((1,), 1.0 if sampling is None else 1.0 / sampling.temperature, device=r.device)
+        # positions [start, len(full) - 1) still need KV; logits are needed for [first_row, len(full) - 1)
+        if start > first_row:
+            # the cached prefix already covers scored positions: recompute from the first scored row
+            self.cache.release(seq)
+            pages, _ = self.prefix.lookup(full, first_row)
+            seq = self.cache.manager.adopt(pages, len(pages) * PAGE) if pages else self.cache.create()
+            start = self.cache.length(seq)
+        end = len(full) - 1
+        pos0 = start
+        while pos0 < end:
+            n = min(end - pos0, r.max_logit_rows, self.prefill_tokens)
+            slots = self.cache.append(seq, n)
+            table = torch.zeros(1, self.max_pages, dtype=torch.int32)
+            self.cache.fill_table([seq], table)
+            lo = max(first_row, pos0)
+            rows = list(range(lo - pos0, n))
+            meta = build_meta(r.device, table, list(full[pos0:pos0 + n]), list(range(pos0, pos0 + n)), slots, [n],
+                              [pos0 + n], [0], G, logit_rows=rows if rows else None,
+                              tile_rows=64 if n * G > 64 else None)
+            if rows:
+                logits = r.forward(meta)
+                targets = torch.tensor([full[p + 1] for p in range(lo, pos0 + n)], dtype=torch.int32,
+                                       device=r.device)
+                _, _, logp, logq = K.row_stats(logits, it.expand(len(rows)).contiguous(), targets)
+                values += (logp if sampling is None else logq).tolist()
+            else:
+                r.forward(meta, compute_logits=False)
+            self.stats["prefill_tokens"] += n
+            pos0 += n
+        self._cache_pages(seq, full)
+        self.cache.release(seq)
+        self.stats["scored_tokens"] += len(values)
+        return tuple(values)

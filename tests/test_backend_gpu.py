@@ -1,0 +1,89 @@
+"""EngineBackend (AutoregressiveBackend on the sm_100a engine) against the fp32 oracle."""
+
+import pytest
+import torch
+
+from online_speculation_b200.api import build_runner
+from online_speculation_b200.arllm.algorithms.conditional_is import run_conditional_is
+from online_speculation_b200.arllm.algorithms.mh import run_mh_chains_batched
+from online_speculation_b200.arllm.config import ConditionalISConfig, MHConfig, SamplingConfig
+from online_speculation_b200.arllm.rewards import SequenceLogProbabilityReward
+from online_speculation_b200.arllm.types import GenerationRequest, ScoreRequest
+from online_speculation_b200.engine.backend import EngineBackend
+from online_speculation_b200.models.decoder import DecoderConfig, random_state_dict, reference_forward
+from online_speculation_b200.ops import workspace
+from online_speculation_b200.shared.rng import SeedStream
+
+pytestmark = pytest.mark.gpu
+
+CFG = DecoderConfig(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                    num_attention_heads=8, num_key_value_heads=2, name="small")
+
+
+@pytest.fixture(scope="module")
+def backend():
+    runner = build_runner(CFG, seed=11, kv_bytes=128 << 20, max_tokens=2048)
+    b = EngineBackend(runner, max_batch=8, max_seq_tokens=512)
+    yield b
+    b.close()
+
+
+@pytest.fixture(scope="module")
+def oracle():
+    return {k: v.cpu() for k, v in random_state_dict(CFG, seed=11, std=0.02, device="cuda").items()}
+
+
+def _oracle_logprobs(oracle, prefix, tokens, temperature):
+    logits = reference_forward(CFG, oracle, torch.tensor(list(prefix) + list(tokens)))[len(prefix) - 1:-1]
+    idx = torch.tensor(tokens)[:, None]
+    return (logits.log_softmax(-1).gather(-1, idx).squeeze(-1),
+            (logits / temperature).log_softmax(-1).gather(-1, idx).squeeze(-1))
+
+
+def test_sample_logprobs_match_oracle(backend, oracle):
+    reqs = [GenerationRequest(tuple(range(3, 3 + n)), 12, SamplingConfig(temperature=t), seed=i, request_id=f"r{i}")
+            for i, (n, t) in enumerate([(40, 1.0), (7, 0.5), (33, 2.0)])]
+    out = backend.sample_batch(reqs)
+    for req, smp in zip(reqs, out):
+        assert len(smp.token_ids) == 12 and smp.reference_policy_id == SamplingConfig().policy_id
+        lp, lq = _oracle_logprobs(oracle, req.prefix, smp.token_ids, req.sampling.temperature)
+        # bf16 activations vs the fp32 oracle: agree to ~1% of the log-probabilities
+        got_p, got_q = torch.tensor(smp.reference_token_logprobs), torch.tensor(smp.token_logprobs)
+        assert float((got_p - lp).norm() / lp.norm()) < 0.02 and float((got_p - lp).abs().max()) < 0.2
+        assert float((got_q - lq).norm() / lq.norm()) < 0.03
+    workspace.check_status()
+
+
+def test_batch_composition_does_not_change_tokens(backend):
+    target = GenerationRequest(tuple(range(50, 90)), 10, SamplingConfig(temperature=1.5), seed=5, request_id="t")
+    others = [GenerationRequest(tuple(range(i, i + 20)), 10, SamplingConfig(), seed=100 + i, request_id=f"o{i}")
+              for i in range(3)]
+    a = backend.sample_batch([target] + others[:2])[0]      # 3 rows -> bucket 4
+    b = backend.sample_batch(others[1:] + [target])[2]      # 3 rows -> bucket 4
+    assert a.token_ids == b.token_ids
+    assert a.token_logprobs == pytest.approx(b.token_logprobs, abs=1e-6)
+
+
+def test_score_matches_sample_and_prefix_cache_reuses(backend):
+    prefix = tuple(range(200, 280))
+    smp = backend.sample_batch([GenerationRequest(prefix, 16, SamplingConfig(), 9, "s")])[0]
+    before = backend.stats["reused_prefix_tokens"]
+    scored = backend.score_batch([ScoreRequest(prefix, (smp.token_ids,), None)])[0]
+    assert torch.allclose(torch.tensor(scored), torch.tensor(smp.token_logprobs), atol=0.02)
+    assert backend.stats["reused_prefix_tokens"] > before
+    t2 = backend.score_batch([ScoreRequest(prefix, (smp.token_ids,), SamplingConfig(temperature=0.5))])[0]
+    assert all(x <= 0 for x in t2)
+
+
+def test_conditional_is_and_mh_on_engine(backend):
+    reward = SequenceLogProbabilityReward(backend, coefficient=0.5)
+    cfg = ConditionalISConfig(candidate_count=3, rollout_count=2, block_size=8, total_length=16,
+                              reward_temperature=0.5)
+    res = run_conditional_is(base_backend=backend, prompt=tuple(range(1, 40)), config=cfg, seeds=SeedStream(1),
+                             reward=reward)
+    assert len(res.token_ids) == 16 and len(res.steps) == 2
+    mh = run_mh_chains_batched(backend, tuple(range(1, 40)), MHConfig(alpha=2.0, total_length=16, block_size=16,
+                                                                      iterations=3),
+                               SamplingConfig(temperature=0.5), [SeedStream(3)] * 4, chain_ids=[0, 1, 2, 3])
+    assert all(len(c.token_ids) == 16 and c.attempts == 3 for c in mh)
+    workspace.check_status()
