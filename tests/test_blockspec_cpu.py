@@ -1,0 +1,180 @@
+"""blockspec dual-view model, decoding loop, sampling maths, formats and training (CPU)."""
+
+import itertools
+import json
+
+import pytest
+import torch
+
+from online_speculation_b200.blockspec.fitting import FitConfig, TokenDataset, Trainer
+from online_speculation_b200.blockspec.generation import MaskedAttentionBranch, ProposalSampler, generate, generate_ar
+from online_speculation_b200.blockspec.model import DualViewConfig, DualViewDecoder, trim_cache
+from online_speculation_b200.blockspec.online import OnlineFeedback, SuffixConfig, SuffixLearner
+from online_speculation_b200.blockspec.sampling import (SamplingConfig, linear_correction, probabilities, residual,
+                                                         verify_linear)
+from online_speculation_b200.blockspec.training import distillation_loss, sample_anchors
+from online_speculation_b200.blockspec.weights import (export_public, load_checkpoint, load_public,
+                                                       public_key_map, save_checkpoint)
+
+CFG = DualViewConfig(vocab_size=17, hidden_size=16, intermediate_size=32, num_hidden_layers=2,
+                     num_attention_heads=4, num_key_value_heads=2, head_dim=4, block_size=4, mask_token_id=1)
+
+
+def _model(seed=0):
+    torch.manual_seed(seed)
+    m = DualViewDecoder(CFG).eval().requires_grad_(False)
+    with torch.no_grad():  # make the draft view differ from AR
+        for layer in m.layers:
+            layer.attention.draft.q.weight.add_(torch.randn_like(layer.attention.draft.q.weight) * 0.3)
+    return m
+
+
+def test_incremental_cache_equals_full_forward():
+    m = _model()
+    x = torch.randint(0, 17, (2, 9))
+    full = m(x)
+    a = m(x[:, :5])
+    b = m(x[:, 5:], cache=a.cache)
+    torch.testing.assert_close(torch.cat((a.logits, b.logits), 1), full.logits, atol=1e-5, rtol=1e-5)
+
+
+def test_draft_view_is_read_only_and_bidirectional():
+    m = _model()
+    x = torch.randint(0, 17, (1, 6))
+    ar = m(x)
+    block = torch.tensor([[3, 1, 1, 1]])
+    d1 = m(block, view="draft", cache=ar.cache)
+    assert d1.cache is ar.cache
+    block2 = torch.tensor([[3, 1, 1, 5]])
+    d2 = m(block2, view="draft", cache=ar.cache)
+    # a later block position changes the first row's output (bidirectional)
+    assert not torch.allclose(d1.logits[0, 0], d2.logits[0, 0])
+
+
+def test_greedy_speculation_reproduces_greedy_ar():
+    m = _model(1)
+    branch = MaskedAttentionBranch(m)
+    prompt = torch.tensor([[2, 5, 7, 3]])
+    ar = generate_ar(branch, prompt, 20)
+    spec = generate(branch, prompt, 20)
+    assert spec.tokens == ar.tokens
+    assert spec.verifier_forwards <= 19
+
+
+def test_linear_verification_law_matches_target():
+    torch.manual_seed(0)
+    V = 5
+    p = torch.softmax(torch.randn(2, V), -1).double()
+    q = torch.softmax(torch.randn(1, V), -1).double()
+    g = torch.Generator().manual_seed(1)
+    counts = torch.zeros(V)
+    n = 20000
+    cands = torch.multinomial(q[0], n, replacement=True, generator=g)
+    for i in range(n):
+        counts[verify_linear(cands[i:i + 1], q, p, generator=g).tokens[0]] += 1
+    assert float((counts / n - p[0]).abs().sum() / 2) < 0.02
+    corr, mass = residual(p[0], q[0])
+    assert float(mass) == pytest.approx(float((p[0] - q[0]).clamp_min(0).sum()))
+
+
+def test_tensor_correction_matches_sequential():
+    torch.manual_seed(3)
+    V, n = 7, 3
+    p = torch.softmax(torch.randn(n + 1, V), -1)
+    q = torch.softmax(torch.randn(n, V), -1)
+    toks = torch.multinomial(q, 1).squeeze(-1)
+    u = torch.rand(n)
+    count, tail, valid = linear_correction(toks, q, p, u, torch.ones(V))
+    ref = verify_linear(toks, q, p, acceptance_uniforms=u)
+    assert int(count) == ref.accepted and bool(valid)
+
+
+def test_probability_transforms():
+    x = torch.tensor([[1.0, 3.0, 2.0, 0.0]])
+    assert torch.equal(probabilities(x, SamplingConfig(0.0)), torch.tensor([[0.0, 1, 0, 0]]))
+    p = probabilities(x, SamplingConfig(1.0, top_k=2))
+    assert p[0, 0] == 0 and p[0, 3] == 0 and abs(float(p.sum()) - 1) < 1e-6
+    p = probabilities(x, SamplingConfig(1.0, top_p=0.5))
+    assert p[0, 1] > 0.99
+
+
+def test_checkpoint_and_public_roundtrip(tmp_path):
+    m = _model()
+    save_checkpoint(tmp_path / "c.pt", m, step=3, metadata={"k": 1})
+    m2, saved = load_checkpoint(tmp_path / "c.pt")
+    assert saved["step"] == 3 and saved["metadata"] == {"k": 1}
+    for (a, x), (b, y) in zip(m.state_dict().items(), m2.state_dict().items()):
+        assert a == b and torch.equal(x, y)
+    export_public(m, tmp_path / "pub")
+    m3 = load_public(tmp_path / "pub")
+    torch.testing.assert_close(m3(torch.tensor([[1, 2, 3]])).logits, m(torch.tensor([[1, 2, 3]])).logits)
+    keys = public_key_map(CFG)
+    assert keys["layers.0.attention.draft.q.weight"] == "model.layers.0.self_attn.q_proj_diff.weight"
+
+
+def test_distillation_reduces_loss():
+    torch.manual_seed(0)
+    m = DualViewDecoder(CFG).float()
+    m.train_draft_only()
+    tokens = torch.randint(0, 17, (2, 12))
+    anchors = sample_anchors(tokens, 4, 2, generator=torch.Generator().manual_seed(0))
+    opt = torch.optim.AdamW([p for p in m.parameters() if p.requires_grad], lr=3e-2)
+    first = float(distillation_loss(m, tokens, anchors))
+    for _ in range(20):
+        opt.zero_grad()
+        distillation_loss(m, tokens, anchors).backward()
+        opt.step()
+    assert float(distillation_loss(m, tokens, anchors)) < first
+
+
+def test_fit_resume_is_bit_exact(tmp_path):
+    data = tmp_path / "d.jsonl"
+    g = torch.Generator().manual_seed(0)
+    data.write_text("".join(json.dumps({"input_ids": torch.randint(0, 17, (20,), generator=g).tolist()}) + "\n"
+                            for _ in range(6)))
+    cfg = FitConfig(steps=4, sequence_length=12, anchors_per_sequence=2, warmup_steps=1, learning_rate=1e-2)
+    ds = TokenDataset(data, 17, 12)
+    torch.manual_seed(0)
+    t1 = Trainer(DualViewDecoder(CFG).float(), ds, cfg)
+    t1.run()
+    torch.manual_seed(0)
+    t2 = Trainer(DualViewDecoder(CFG).float(), ds, cfg)
+    t2.run(until=2)
+    t2.save(tmp_path / "mid.pt")
+    t3 = Trainer.resume(tmp_path / "mid.pt", ds)
+    t3.run()
+    for (a, x), (b, y) in zip(t1.model.state_dict().items(), t3.model.state_dict().items()):
+        assert torch.equal(x, y), a
+
+
+def test_online_learner_updates_draft_only():
+    m = _model(2)
+    learner = SuffixLearner(m, SuffixConfig(stride=2, replay_blocks=1, learning_rate=1e-2, loss="tv"))
+    before = {n: p.clone() for n, p in m.named_parameters()}
+    branch = MaskedAttentionBranch(m)
+    res = generate(branch, torch.tensor([[2, 4, 6]]), 24, sampling=SamplingConfig(1.0),
+                   generator=torch.Generator().manual_seed(0), feedback=OnlineFeedback(learner=learner))
+    assert res.updates >= 1
+    changed = {n for n, p in m.named_parameters() if not torch.equal(before[n], p)}
+    assert changed and all(".attention.draft." in n and n.startswith("layers.1.") for n in changed)
+    state = learner.state_dict()
+    learner.load_state_dict(state)
+
+
+def test_cli_commands(tmp_path):
+    from online_speculation_b200.blockspec.cli import main
+
+    assert main(["fit", "demo", "--device", "cpu", "--steps", "3"]) == 0
+    assert main(["evaluate", "benchmark", "--device", "cpu", "--limit", "2", "--max-new-tokens", "12",
+                 "--report", str(tmp_path / "r.json")]) == 0
+    assert (tmp_path / "r.json").exists()
+    assert main(["online", "--device", "cpu", "--limit", "2", "--max-new-tokens", "24", "--temperature", "1.0",
+                 "--stride", "2", "--save-state", str(tmp_path / "s.pt")]) == 0
+    assert main(["evaluate", "audit", "--device", "cpu", "--limit", "2"]) == 0
+
+
+def test_measurement_ratio():
+    from online_speculation_b200.blockspec.measurement import paired_ratio
+
+    r = paired_ratio([10, 10], [1, 1], [10, 10], [2, 2], samples=200)
+    assert r["ratio"] == pytest.approx(2.0) and r["ci_low"] <= 2.0 <= r["ci_high"]

@@ -113,3 +113,34 @@ def test_mh_engine_logprobs_are_exact(graphs):
     assert held <= 6 * 2 + 2
     assert eng.mean_accept_length >= 1.0
     workspace.check_status()
+
+
+def test_kernel_branch_matches_module_branch():
+    from online_speculation_b200.blockspec.generation import MaskedAttentionBranch, ProposalSampler, generate
+    from online_speculation_b200.blockspec.kernel_branch import KernelBranch
+    from online_speculation_b200.blockspec.model import DualViewConfig, DualViewDecoder
+    from online_speculation_b200.blockspec.sampling import SamplingConfig
+
+    cfg = DualViewConfig(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                         num_attention_heads=4, num_key_value_heads=2, head_dim=128, block_size=4, mask_token_id=1)
+    torch.manual_seed(0)
+    m = DualViewDecoder(cfg).cuda().eval().requires_grad_(False)
+    with torch.no_grad():
+        for layer in m.layers:
+            layer.attention.draft.q.weight.mul_(1.3)
+    mb, kb = MaskedAttentionBranch(m), KernelBranch(m, kv_bytes=64 << 20)
+    prompt = torch.tensor([[3, 7, 11, 13, 17]], device="cuda")
+    l1, c1 = mb.ar(prompt)
+    l2, c2 = kb.ar(prompt)
+    assert float((l1 - l2).norm() / l1.norm()) < 3e-2
+    anchor = torch.tensor([[19]], device="cuda")
+    sampler = ProposalSampler(SamplingConfig(0.0))
+    d1 = mb.draft(anchor, c1, 4, sampler)
+    d2 = kb.draft(anchor, c2, 4, sampler)
+    assert kb.cache_length(c2) == 5
+    out1 = m(d1.verifier_inputs, cache=c1)
+    l3, _ = kb.ar(d1.verifier_inputs, cache=c2)
+    assert float((out1.logits - l3).norm() / out1.logits.norm()) < 3e-2
+    # full speculative generation runs on the kernel branch
+    res = generate(kb, prompt, 16, sampling=SamplingConfig(1.0), generator=torch.Generator(device="cuda").manual_seed(0))
+    assert len(res.tokens) == 16
