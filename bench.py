@@ -46,6 +46,11 @@ def parse():
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--workload", choices=("mh-spec", "grpo"), default="mh-spec",
+                   help="mh-spec: suffix-MH rollouts with speculative drafting (headline); "
+                        "grpo: GRPO training on the Qwen2.5-1.5B shape, data parallel")
+    p.add_argument("--group-size", type=int, default=8)
+    p.add_argument("--prompts-per-rank", type=int, default=1)
     p.add_argument("--model", default="qwen2.5-7b")
     p.add_argument("--chains", type=int, default=64)
     p.add_argument("--prompt-len", type=int, default=512)
@@ -264,6 +269,74 @@ def run_ours(args, rank, world, local, group) -> dict:
     return out
 
 
+GRPO_METRIC = "GRPO tokens/s (prompt + completion tokens trained per second, whole job)"
+
+
+def run_grpo(args, rank, world, local, group) -> dict:
+    """GRPO steps: rollouts with the current policy, reference log-probs, loss, backward, sharded AdamW."""
+    import torch
+
+    from online_speculation_b200.models.decoder import PRESETS
+    from online_speculation_b200.ops import _ext
+    from online_speculation_b200.training.grpo import GRPOConfig, GRPOTrainer
+
+    model = args.model if args.model != "qwen2.5-7b" else "qwen2.5-1.5b"
+    prompt_len = args.prompt_len if args.prompt_len != 512 else 256
+    conf = GRPOConfig(group_size=args.group_size, prompts_per_rank=args.prompts_per_rank, prompt_length=prompt_len,
+                      completion_length=args.gen_len, seed=args.seed)
+    tr = GRPOTrainer(PRESETS[model], conf, group=group, seed=args.seed, kv_bytes=int(min(args.kv_gb, 8) * 2**30),
+                     use_graphs=not args.no_graphs)
+    for _ in range(args.warmup):
+        tr.step()
+    barrier(world)
+    launches0 = _ext.launches()
+    graph0 = tr.backend.stats.get("graph_kernel_launches", 0)
+    sampler = ClockSampler(local)
+    tokens = completion = 0
+    parts = {"rollout_s": 0.0, "train_s": 0.0}
+    with sampler:
+        barrier(world)
+        wall0 = time.perf_counter()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            st = tr.step()
+            tokens += st["tokens"]
+            completion += st["completion_tokens"]
+            for k in parts:
+                parts[k] += st[k]
+        stop.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world)
+    wall = max_over_ranks(wall, world)
+    total = sum_over_ranks(float(tokens), world)
+    launches = _ext.launches() - launches0 + tr.backend.stats.get("graph_kernel_launches", 0) - graph0
+    B = conf.group_size * conf.prompts_per_rank
+    seq = conf.prompt_length + conf.completion_length
+    out = {
+        "metric": GRPO_METRIC, "value": total / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 (fp32 master weights and AdamW state)",
+        "data": "synthetic (uniform-random prompt ids, Bernoulli(0.5) rewards, random-init weights)",
+        "config": {"model": f"{model} (random init)", "global_batch": B * world, "seq_len": seq,
+                   "prompt_len": conf.prompt_length, "completion_len": conf.completion_length,
+                   "group_size": conf.group_size, "parallelism": f"dp{world}", "lr": conf.learning_rate,
+                   "beta": conf.beta, "epsilon": conf.epsilon,
+                   "l2": "weights, optimizer state and activations (tens of GB) exceed the 126 MB L2"},
+        "completion_tokens": sum_over_ranks(float(completion), world),
+        "rollout_fraction": parts["rollout_s"] / max(1e-9, parts["rollout_s"] + parts["train_s"]),
+        "trainable_parameters": tr.params.trainable,
+        "clocks": sampler.summary(),
+        "e2e": {"value": total / wall, "unit": "tok/s", "h2d_bytes_per_step": B * (seq * 8 + conf.completion_length + 4),
+                "d2h_bytes_per_step": B * conf.completion_length * 4 + 4},
+        "gpu_launches": int(launches),
+    }
+    tr.close()
+    return out
+
+
 def run_reference(args, rank, world, local, group) -> dict:
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "inference_scaling")):
@@ -361,7 +434,13 @@ def main():
     args = parse()
     rank, world, local, group = dist_setup(args.gpus)
     try:
-        out = run_ours(args, rank, world, local, group) if args.impl == "ours" else run_reference(args, rank, world, local, group)
+        if args.workload == "grpo":
+            out = (run_grpo(args, rank, world, local, group) if args.impl == "ours" else
+                   {"impl": "reference", "unavailable": "the reference GRPO path needs trl and peft, which are not "
+                                                        "installed in this image"})
+        else:
+            out = (run_ours(args, rank, world, local, group) if args.impl == "ours"
+                   else run_reference(args, rank, world, local, group))
     finally:
         pass
     if rank == 0:

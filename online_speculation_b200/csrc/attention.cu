@@ -285,6 +285,8 @@ __device__ __forceinline__ void store_rows(const AttnArgs& a, const WarpState& s
 __global__ void __launch_bounds__(128) attn_rows_kernel(const AttnArgs a) {
   __shared__ __align__(16) __nv_bfloat16 sK[2][kPage * kStride];
   __shared__ __align__(16) __nv_bfloat16 sV[2][kPage * kStride];
+  pdl_wait();
+  pdl_trigger();
   const int tile = blockIdx.x, g = blockIdx.y;
   const int b = a.tile_seq[tile];
   const int row0 = a.tile_row0[tile];
@@ -330,6 +332,8 @@ constexpr int kKeysSmemBytes = 4 * kWarpBufElems * 2 > (4 * 16 * kD + 128) * 4 ?
 
 __global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   __nv_bfloat16* buf = reinterpret_cast<__nv_bfloat16*>(smem_raw) + warp * kWarpBufElems;
   const int tile = blockIdx.x, g = blockIdx.y;
@@ -445,7 +449,7 @@ cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream) {
   if (p.num_tiles <= 0) return cudaSuccess;
   dim3 grid(p.num_tiles, p.Hkv);
   if (p.tile_rows == 64) {
-    attn_rows_kernel<<<grid, 128, 0, stream>>>(a);
+    return launch_pdl(attn_rows_kernel, grid, dim3(128), 0, stream, a);
   } else if (p.tile_rows == 16) {
     static bool attr[64] = {false};
     int dev = 0;
@@ -456,7 +460,7 @@ cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream) {
       if (e != cudaSuccess) return e;
       attr[dev] = true;
     }
-    attn_keys_kernel<<<grid, 128, kKeysSmemBytes, stream>>>(a);
+    return launch_pdl(attn_keys_kernel, grid, dim3(128), kKeysSmemBytes, stream, a);
   } else {
     return cudaErrorInvalidValue;
   }

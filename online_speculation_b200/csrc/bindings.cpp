@@ -40,7 +40,7 @@ __nv_bfloat16* bfm(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.
 
 // out[N, M or M/2] = x[N, K] @ w[M, K]^T (+ bias) (+ residual)
 void gemm(Tensor w, Tensor x, Tensor out, c10::optional<Tensor> bias, c10::optional<Tensor> residual, int64_t epilogue,
-          bool allow_split, Tensor workspace, Tensor counters, Tensor status) {
+          bool allow_split, Tensor workspace, Tensor counters, Tensor status, bool prefetch_weights) {
   CHECK_CUDA(w);
   CHECK_CUDA(x);
   CHECK_CUDA(out);
@@ -88,6 +88,7 @@ void gemm(Tensor w, Tensor x, Tensor out, c10::optional<Tensor> bias, c10::optio
   p.counters = counters.data_ptr<int>();
   p.counter_slots = counters.numel();
   p.status = status.data_ptr<int>();
+  p.prefetch_weights = prefetch_weights ? 1 : 0;
   check(osb::gemm_launch(p, at::cuda::getCurrentCUDAStream()), "tcgen05 gemm");
 }
 
@@ -377,6 +378,24 @@ void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows
         "allreduce_add_rmsnorm");
 }
 
+void logprob_grad(Tensor logits, Tensor lse, Tensor targets, Tensor w, Tensor grad) {
+  CHECK_CUDA(logits);
+  CHECK_ROWS(logits);
+  CHECK_ROWS(grad);
+  CHECK_DT(logits, torch::kFloat32);
+  TORCH_CHECK(grad.scalar_type() == torch::kFloat32 || grad.scalar_type() == torch::kBFloat16,
+              "fp32 or bf16 gradient");
+  CHECK_DT(targets, torch::kInt32);
+  TORCH_CHECK(grad.sizes() == logits.sizes() && lse.numel() == logits.size(0) && w.numel() == logits.size(0),
+              "logprob_grad shapes");
+  c10::cuda::CUDAGuard guard(logits.device());
+  check(osb::logprob_grad_launch(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1),
+                                 lse.data_ptr<float>(), targets.data_ptr<int>(), w.data_ptr<float>(), grad.data_ptr(),
+                                 grad.scalar_type() == torch::kBFloat16, grad.stride(0),
+                                 at::cuda::getCurrentCUDAStream()),
+        "logprob_grad");
+}
+
 void grad_sq_norm(Tensor g, Tensor out) {
   CHECK_CUDA(g);
   CHECK_DT(g, torch::kFloat32);
@@ -440,8 +459,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("divergence_stats", &divergence_stats);
   m.def("divergence_loss", &divergence_loss);
   m.def("divergence_grad", &divergence_grad);
+  m.def("logprob_grad", &logprob_grad);
   m.def("adamw", &adamw);
   m.def("gemm_pick_bn", &osb::gemm_pick_bn);
+  m.def("set_pdl", [](bool on) { osb::pdl_enabled() = on; });
+  m.def("pdl_enabled", []() -> bool { return osb::pdl_enabled(); });
 
   pybind11::class_<osb::KVManager>(m, "KVManager")
       .def(pybind11::init<int, int>())

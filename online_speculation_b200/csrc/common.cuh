@@ -13,8 +13,43 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+
+#include <utility>
 
 namespace osb {
+
+// ------------------------------------------- programmatic dependent launch --
+// Kernels of the forward path are launched with programmatic stream
+// serialisation: a kernel may become resident while its predecessor in the
+// stream is still running.  Every such kernel executes pdl_wait() before its
+// first access to global memory that another kernel may write (griddepcontrol.wait
+// returns once the predecessor grid has completed and its writes are visible),
+// and pdl_trigger() early so that its own successor can launch.  Kernels that
+// write weights never trigger early.  Without the launch attribute both
+// instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Process-wide switch (environment OSB_PDL=1 enables it); defined in gemm.cu.
+bool& pdl_enabled();
+
+// <<<grid, block, smem, stream>>> with the programmatic-serialisation attribute when enabled.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Error codes written into the status word by device-side bounded waits.
 enum KernelError : int {

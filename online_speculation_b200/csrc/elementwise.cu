@@ -21,6 +21,8 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ld
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y, long long ldy, int H,
                                float eps) {
   // If delta != null: h[row] = x[row] + delta[row] (written back), then normalise h.
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * ldx;
   extern __shared__ float red[];
@@ -76,6 +78,8 @@ __global__ void rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, long lo
                                   const __nv_bfloat16* __restrict__ kn_w, float eps, __nv_bfloat16* __restrict__ q_out,
                                   __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, int T,
                                   int Hq, int Hkv, int page) {
+  pdl_wait();
+  pdl_trigger();
   const int warps = blockDim.x / 32;
   const int gw = blockIdx.x * warps + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -131,6 +135,8 @@ __global__ void rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, long lo
 
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int H,
                              __nv_bfloat16* __restrict__ out, long long ldo) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int id = ids[t];
   const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<long long>(id) * H);
@@ -161,8 +167,8 @@ cudaError_t rmsnorm_launch(const __nv_bfloat16* x, long long ldx, __nv_bfloat16*
                            long long ldy, int T, int H, float eps, cudaStream_t stream) {
   if (H % 8 || T <= 0) return T == 0 ? cudaSuccess : cudaErrorInvalidValue;
   const int threads = H >= 2048 ? 256 : 128;
-  rmsnorm_kernel<<<T, threads, 33 * sizeof(float), stream>>>(x, ldx, h, ldh, delta, ldd, w, y, ldy, H, eps);
-  return cudaGetLastError();
+  return launch_pdl(rmsnorm_kernel, dim3(T), dim3(threads), 33 * sizeof(float), stream, x, ldx, h, ldh, delta, ldd,
+                    w, y, ldy, H, eps);
 }
 
 cudaError_t rope_cache_launch(const __nv_bfloat16* qkv, long long ldqkv, const int* positions, const int* slots,
@@ -173,17 +179,16 @@ cudaError_t rope_cache_launch(const __nv_bfloat16* qkv, long long ldqkv, const i
   const int heads = Hq + 2 * Hkv;
   const long long warps = static_cast<long long>(T) * heads;
   const int per_block = 8;
-  rope_cache_kernel<<<static_cast<int>((warps + per_block - 1) / per_block), per_block * 32, 0, stream>>>(
-      qkv, ldqkv, positions, slots, inv_freq, qn_w, kn_w, eps, q_out, k_cache, v_cache, T, Hq, Hkv, page);
-  return cudaGetLastError();
+  return launch_pdl(rope_cache_kernel, dim3(static_cast<int>((warps + per_block - 1) / per_block)),
+                    dim3(per_block * 32), 0, stream, qkv, ldqkv, positions, slots, inv_freq, qn_w, kn_w, eps, q_out,
+                    k_cache, v_cache, T, Hq, Hkv, page);
 }
 
 cudaError_t embed_launch(const int* ids, const __nv_bfloat16* table, int T, int H, __nv_bfloat16* out, long long ldo,
                          cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   if (H % 8) return cudaErrorInvalidValue;
-  embed_kernel<<<T, 256, 0, stream>>>(ids, table, H, out, ldo);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, dim3(T), dim3(256), 0, stream, ids, table, H, out, ldo);
 }
 
 cudaError_t page_copy_launch(__nv_bfloat16* cache, long long layer_stride, int layers, const int* pairs, int npairs,

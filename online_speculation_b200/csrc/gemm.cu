@@ -56,6 +56,7 @@ struct Args {
   float* workspace;
   int* counters;
   int* status;
+  int prefetch_a;       // issue the first stages' weight tiles before griddepcontrol.wait
 };
 
 template <int BN>
@@ -278,6 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -311,6 +313,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
+      // Weight tiles do not depend on the predecessor kernel: with prefetch_a
+      // the first stages of this CTA's first work item are armed and their A
+      // tiles requested before griddepcontrol.wait; their B tiles follow it.
+      int armed = 0;
+      if (a.prefetch_a && blockIdx.x < total) {
+        const int w = blockIdx.x;
+        const int tm = (w / a.splits) % a.tiles_m;
+        const int kb0 = (w % a.splits) * a.kb_per_split;
+        const int kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
+        armed = min(STAGES, kb1 - kb0);
+        for (int s = 0; s < armed; ++s) {
+          mbar_arrive_expect_tx(&full[s], S::kStageBytes);
+          tma_load_2d(sA + s * S::kABytes, &tmA, (kb0 + s) * kBK, tm * kBM, &full[s]);
+        }
+      }
+      pdl_wait();
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
         const int split = w % a.splits;
         const int tile = w / a.splits;
@@ -319,14 +337,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb0 = split * a.kb_per_split;
         const int kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, a.status, kErrTmaWait)) {
-            ok = false;
-            *abort_flag = 1;
-            break;
+          if (issued < armed) {
+            tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, tn * BN, &full[stage]);
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, a.status, kErrTmaWait)) {
+              ok = false;
+              *abort_flag = 1;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+            tma_load_2d(sA + stage * S::kABytes, &tmA, kb * kBK, tm * kBM, &full[stage]);
+            tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, tn * BN, &full[stage]);
           }
-          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-          tma_load_2d(sA + stage * S::kABytes, &tmA, kb * kBK, tm * kBM, &full[stage]);
-          tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, tn * BN, &full[stage]);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -390,6 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
+    pdl_wait();   // residual / bias / output belong to the stream's data flow
     const int quarter = warp % 4;
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
@@ -598,13 +621,15 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
       cfg.blockDim = dim3(kThreads);
       cfg.dynamicSmemBytes = S::kTotal;
       cfg.stream = stream;
-      cudaLaunchAttribute attr[1];
+      cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = a.cluster;
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
-      cfg.numAttrs = 1;
+      cfg.numAttrs = pdl_enabled() ? 2 : 1;
       return cudaLaunchKernelEx(&cfg, gemm_tn_kernel<BN>, ma, mb, a);
     }
   }
@@ -621,11 +646,21 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
   }
   const int total = tiles * a.splits;
   const int grid = std::min(total, sms);
-  gemm_tn_kernel<BN><<<grid, kThreads, S::kTotal, stream>>>(ma, mb, a);
-  return cudaGetLastError();
+  return launch_pdl(gemm_tn_kernel<BN>, dim3(grid), dim3(kThreads), S::kTotal, stream, ma, mb, a);
 }
 
 }  // namespace
+
+// Off by default: measured on B200 decode steps (28 layers, 8-64 rows) the
+// whole step ran about 6% slower with it, although chains of GEMMs alone ran
+// faster.  OSB_PDL=1 (or set_pdl) enables it.
+bool& pdl_enabled() {
+  static bool on = [] {
+    const char* v = getenv("OSB_PDL");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
 
 int gemm_pick_bn(int tokens) {
   if (tokens <= 32) return 32;
@@ -667,6 +702,7 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.workspace = p.workspace;
   a.counters = p.counters;
   a.status = p.status;
+  a.prefetch_a = p.prefetch_weights;
   {
     const int esz = p.out_f32 ? 4 : 2;
     const bool out_ok = (reinterpret_cast<uintptr_t>(p.out) % 16 == 0) && ((p.ldo * esz) % 16 == 0);

@@ -25,9 +25,12 @@ struct GemmProblem {
   int* counters;                  // per-tile arrival counters, zero at rest
   int counter_slots;
   int* status;                    // bounded-wait error word
+  int prefetch_weights;           // stream weight tiles before the predecessor kernel completes
+                                  // (only where no kernel earlier in the stream writes w)
 };
 
 cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream);
+bool& pdl_enabled();   // programmatic dependent launch for the forward-path kernels
 int gemm_pick_bn(int tokens);
 long long gemm_workspace_floats(int M, int N, int K, int sms);
 

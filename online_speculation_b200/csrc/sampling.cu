@@ -169,6 +169,8 @@ __device__ double block_exclusive_scan(double v, double& total) {
 }
 
 __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const float* row = a.logits + r * a.ld;
   const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
@@ -211,6 +213,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
 }
 
 __global__ void __launch_bounds__(kThreads) row_stats_kernel(RowStatsArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const float* row = a.logits + r * a.ld;
   const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
@@ -230,6 +234,8 @@ __global__ void __launch_bounds__(kThreads) row_stats_kernel(RowStatsArgs a) {
 
 // Gumbel-max sampling at temperature T: argmax_v (l_v / T + G_v).
 __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const float* row = a.logits + r * a.ld;
   const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
@@ -289,6 +295,8 @@ __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
 
 // One CTA per sequence: n candidates, n draft rows, n + 1 target rows.
 __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const int n = a.n;
   const float invT = a.inv_temp ? a.inv_temp[b] : 1.0f;
@@ -419,27 +427,23 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
 
 cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  sample_kernel<<<rows, kThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(sample_kernel, dim3(rows), dim3(kThreads), 0, stream, a);
 }
 
 cudaError_t row_stats_launch(const RowStatsArgs& a, int rows, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  row_stats_kernel<<<rows, kThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(row_stats_kernel, dim3(rows), dim3(kThreads), 0, stream, a);
 }
 
 cudaError_t gumbel_sample_launch(const GumbelArgs& a, int rows, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  gumbel_sample_kernel<<<rows, kThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(gumbel_sample_kernel, dim3(rows), dim3(kThreads), 0, stream, a);
 }
 
 cudaError_t spec_verify_launch(const SpecArgs& a, int batch, cudaStream_t stream) {
   if (batch <= 0) return cudaSuccess;
   if (a.n < 1 || a.n > 15) return cudaErrorInvalidValue;
-  spec_verify_kernel<<<batch, kThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(spec_verify_kernel, dim3(batch), dim3(kThreads), 0, stream, a);
 }
 
 }  // namespace osb
@@ -567,4 +571,65 @@ cudaError_t divergence_grad_launch(const float* s, const float* t, long long ld_
   return cudaGetLastError();
 }
 
+}  // namespace osb
+
+// --------------------------------------------------------- target logprob --
+// Backward of log p(target) = l_t - lse(l) per row:  d/dl_v = w_r (1[v = t] - p_v)
+// written as bf16 (or fp32) gradient rows; lse from row_stats.
+namespace osb {
+namespace {
+// d log softmax(l)[t] / d l_v = [v == t] - p_v, scaled by the row's upstream gradient.
+// Rows are processed in float4 chunks when the row stride allows it.
+template <typename T>
+__global__ void logprob_grad_kernel(const float* __restrict__ logits, long long ld, int V,
+                                    const float* __restrict__ lse, const int* __restrict__ targets,
+                                    const float* __restrict__ w, T* __restrict__ grad, long long ldg) {
+  const int r = blockIdx.y;
+  const float l = lse[r], wr = w[r];
+  const int t = targets[r];
+  const float* row = logits + r * ld;
+  T* out = grad + r * ldg;
+  const bool vec = (V % 4 == 0) && (ld % 4 == 0) && (ldg % 4 == 0);
+  if (vec) {
+    const int n4 = V / 4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+      const float4 x = reinterpret_cast<const float4*>(row)[i];
+      float g[4] = {-wr * __expf(x.x - l), -wr * __expf(x.y - l), -wr * __expf(x.z - l), -wr * __expf(x.w - l)};
+      const int v0 = 4 * i;
+      if (t >= v0 && t < v0 + 4) g[t - v0] += wr;
+      if constexpr (sizeof(T) == 4) {
+        reinterpret_cast<float4*>(out)[i] = make_float4(g[0], g[1], g[2], g[3]);
+      } else {
+        __nv_bfloat162 a = __floats2bfloat162_rn(g[0], g[1]);
+        __nv_bfloat162 b = __floats2bfloat162_rn(g[2], g[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<unsigned*>(&a);
+        u.y = *reinterpret_cast<unsigned*>(&b);
+        reinterpret_cast<uint2*>(out)[i] = u;
+      }
+    }
+    return;
+  }
+  for (int v = blockIdx.x * blockDim.x + threadIdx.x; v < V; v += gridDim.x * blockDim.x) {
+    const float g = wr * ((v == t ? 1.0f : 0.0f) - __expf(row[v] - l));
+    if constexpr (sizeof(T) == 4) out[v] = g;
+    else out[v] = __float2bfloat16(g);
+  }
+}
+}  // namespace
+
+cudaError_t logprob_grad_launch(const float* logits, long long ld, int rows, int V, const float* lse,
+                                const int* targets, const float* w, void* grad, bool grad_bf16, long long ldg,
+                                cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  const int per = (V + 4095) / 4096;
+  dim3 grid(per < 32 ? per : 32, rows);
+  if (grad_bf16)
+    logprob_grad_kernel<__nv_bfloat16><<<grid, 1024, 0, stream>>>(logits, ld, V, lse, targets, w,
+                                                                   static_cast<__nv_bfloat16*>(grad), ldg);
+  else
+    logprob_grad_kernel<float><<<grid, 1024, 0, stream>>>(logits, ld, V, lse, targets, w,
+                                                          static_cast<float*>(grad), ldg);
+  return cudaGetLastError();
+}
 }  // namespace osb

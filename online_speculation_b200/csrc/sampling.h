@@ -81,3 +81,8 @@ cudaError_t divergence_grad_launch(const float* s, const float* t, long long ld_
                                    const float* lse, const float* pieces, const float* w, int kind,
                                    __nv_bfloat16* grad, long long ld_g, cudaStream_t stream);
 }  // namespace osb
+namespace osb {
+cudaError_t logprob_grad_launch(const float* logits, long long ld, int rows, int V, const float* lse,
+                                const int* targets, const float* w, void* grad, bool grad_bf16, long long ldg,
+                                cudaStream_t stream);
+}  // namespace osb

@@ -115,39 +115,51 @@ class _Active:
 
 
 class _DecodeGraph:
-    """Static buffers (+ captured graph) of one decode step for B rows."""
+    """Static buffers (+ captured graph) of S chained decode steps for B rows.
 
-    def __init__(self, backend: "EngineBackend", B: int, use_graph: bool):
+    Step s reads its input ids from row s of ``ids`` and the sampler writes the
+    drawn token into row s + 1, so one replay decodes S tokens per row with a
+    single host round trip.  Positions, KV slots, KV lengths and the sampling
+    uniforms of all S steps are uploaded before the replay.
+    """
+
+    def __init__(self, backend: "EngineBackend", B: int, S: int, use_graph: bool):
         r = backend.runner
         dev = r.device
-        self.B = B
+        self.B, self.S = B, S
         self.mp = backend.max_pages
-        self.host = torch.zeros(4 * B + B * self.mp, dtype=torch.int32).pin_memory()
+        sizes = (B, S * B, S * B, S * B, B * self.mp)   # ids0, pos, slots, kv, table
+        self.host = torch.zeros(sum(sizes), dtype=torch.int32).pin_memory()
         self.dev = torch.zeros_like(self.host, device=dev)
-        hn = self.host.numpy()
-        self.h_ids, self.h_pos, self.h_slots, self.h_kv = (hn[i * B:(i + 1) * B] for i in range(4))
-        self.h_table = hn[4 * B:].reshape(B, self.mp)
-        d = self.dev
-        self.ids, self.pos, self.slots, self.kv = (d[i * B:(i + 1) * B] for i in range(4))
-        self.table = d[4 * B:].view(B, self.mp)
-        self.uni_host = torch.zeros(B, dtype=torch.float64).pin_memory()
-        self.uni = torch.zeros(B, dtype=torch.float64, device=dev)
+        hn, d = self.host.numpy(), self.dev
+        o = np.cumsum((0,) + sizes)
+        self.h_ids = hn[o[0]:o[1]]
+        self.h_pos, self.h_slots, self.h_kv = (hn[o[k]:o[k + 1]].reshape(S, B) for k in (1, 2, 3))
+        self.h_table = hn[o[4]:o[5]].reshape(B, self.mp)
+        self.ids = torch.zeros(S + 1, B, dtype=torch.int32, device=dev)
+        self.ids0 = d[o[0]:o[1]]
+        self.pos, self.slots, self.kv = (d[o[k]:o[k + 1]].view(S, B) for k in (1, 2, 3))
+        self.table = d[o[4]:o[5]].view(B, self.mp)
+        self.uni_host = torch.zeros(S, B, dtype=torch.float64).pin_memory()
+        self.uni = torch.zeros(S, B, dtype=torch.float64, device=dev)
         self.it_host = torch.ones(B, dtype=torch.float32).pin_memory()
         self.inv_temp = torch.ones(B, dtype=torch.float32, device=dev)
         G = r.q_slots // r.kv_slots
         tiles = -(-G // 16)
-        self.plan = K.AttentionPlan(
-            self.table, torch.arange(B, dtype=torch.int32, device=dev), torch.ones(B, dtype=torch.int32, device=dev),
-            self.kv, torch.zeros(B, dtype=torch.int32, device=dev),
-            torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles),
-            (torch.arange(tiles, dtype=torch.int32, device=dev) * 16).repeat(B), 16, {})
-        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
-        self.logq = torch.zeros(B, dtype=torch.float32, device=dev)
-        self.logp = torch.zeros(B, dtype=torch.float32, device=dev)
-        self.result = torch.zeros(B, 3, dtype=torch.float32, device=dev)
-        self.result_host = torch.zeros(B, 3, dtype=torch.float32).pin_memory()
+        q_start = torch.arange(B, dtype=torch.int32, device=dev)
+        q_len = torch.ones(B, dtype=torch.int32, device=dev)
+        mode = torch.zeros(B, dtype=torch.int32, device=dev)
+        tile_seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles)
+        tile_row = (torch.arange(tiles, dtype=torch.int32, device=dev) * 16).repeat(B)
+        self.plans = [K.AttentionPlan(self.table, q_start, q_len, self.kv[s], mode, tile_seq, tile_row, 16, {})
+                      for s in range(S)]
+        self.logq = torch.zeros(S, B, dtype=torch.float32, device=dev)
+        self.logp = torch.zeros(S, B, dtype=torch.float32, device=dev)
+        self.result = torch.zeros(S, B, 3, dtype=torch.float32, device=dev)
+        self.result_host = torch.zeros(S, B, 3, dtype=torch.float32).pin_memory()
         self.backend = backend
         self.graph = None
+        self.kernels_per_replay = 0
         if use_graph:
             s = torch.cuda.Stream(device=dev)
             s.wait_stream(torch.cuda.current_stream(dev))
@@ -157,17 +169,24 @@ class _DecodeGraph:
             torch.cuda.current_stream(dev).wait_stream(s)
             torch.cuda.synchronize(dev)
             g = torch.cuda.CUDAGraph()
+            from ..ops import _ext
+
+            before = _ext.launches()
             with torch.cuda.graph(g, stream=s):
                 self._body()
+            self.kernels_per_replay = _ext.launches() - before
             self.graph = g
 
     def _body(self):
         r = self.backend.runner
-        logits = r.forward(StepMeta(self.ids, self.pos, self.slots, self.plan, None))
-        K.sample(logits, self.inv_temp, self.uni, tokens=self.tokens, logq=self.logq, logp=self.logp)
-        self.result[:, 0].copy_(self.tokens)
-        self.result[:, 1].copy_(self.logq)
-        self.result[:, 2].copy_(self.logp)
+        self.ids[0].copy_(self.ids0)
+        for s in range(self.S):
+            logits = r.forward(StepMeta(self.ids[s], self.pos[s], self.slots[s], self.plans[s], None))
+            K.sample(logits, self.inv_temp, self.uni[s], tokens=self.ids[s + 1], logq=self.logq[s],
+                     logp=self.logp[s])
+        self.result[:, :, 0].copy_(self.ids[1:])
+        self.result[:, :, 1].copy_(self.logq)
+        self.result[:, :, 2].copy_(self.logp)
 
     def run(self) -> np.ndarray:
         self.dev.copy_(self.host, non_blocking=True)
@@ -175,6 +194,7 @@ class _DecodeGraph:
         self.inv_temp.copy_(self.it_host, non_blocking=True)
         if self.graph is not None:
             self.graph.replay()
+            self.backend.stats["graph_kernel_launches"] += self.kernels_per_replay
         else:
             self._body()
         self.result_host.copy_(self.result, non_blocking=True)
@@ -187,21 +207,23 @@ class EngineBackend:
 
     def __init__(self, runner: ModelRunner, *, model_id: str | None = None, max_batch: int = 64,
                  bos_token_id: int | None = None, use_graphs: bool = True, prefix_cache_pages: int | None = None,
-                 max_seq_tokens: int = 4096, prefill_tokens: int = 4096):
+                 max_seq_tokens: int = 4096, prefill_tokens: int = 4096, decode_chunk: int = 16):
         self.runner = runner
         self.cache: KVCache = runner.cache
         self._model_id = model_id or f"b200:{runner.cfg.name}"
         self.max_batch = max_batch
         self.bos_token_id = bos_token_id
         self.use_graphs = use_graphs
-        self.max_pages = -(-max_seq_tokens // PAGE) + 1
+        self.decode_chunk = decode_chunk
+        self.max_pages = -(-(max_seq_tokens + decode_chunk) // PAGE) + 1
         self.prefill_tokens = min(prefill_tokens, runner.max_tokens)
         budget = prefix_cache_pages if prefix_cache_pages is not None else self.cache.num_pages // 2
         self.prefix = PrefixCache(self.cache, budget)
         self._graphs: dict[int, _DecodeGraph] = {}
         self._lock = threading.RLock()
         self.stats = {"sample_calls": 0, "score_calls": 0, "sampled_sequences": 0, "generated_tokens": 0,
-                      "prefill_tokens": 0, "reused_prefix_tokens": 0, "decode_steps": 0, "scored_tokens": 0}
+                      "prefill_tokens": 0, "reused_prefix_tokens": 0, "decode_steps": 0, "scored_tokens": 0,
+                      "graph_kernel_launches": 0}
 
     @property
     def model_id(self) -> str:
@@ -296,12 +318,12 @@ class EngineBackend:
         keys = self.prefix.keys(tokens, n)
         self.prefix.insert(keys, list(self.cache.manager.pages(seq))[:n])
 
-    def _graph(self, B: int) -> _DecodeGraph:
+    def _graph(self, B: int, S: int) -> _DecodeGraph:
         b = next(x for x in BUCKETS if x >= B)
-        g = self._graphs.get(b)
+        g = self._graphs.get((b, S))
         if g is None:
-            g = _DecodeGraph(self, b, self.use_graphs)
-            self._graphs[b] = g
+            g = _DecodeGraph(self, b, S, self.use_graphs)
+            self._graphs[(b, S)] = g
         return g
 
     # -------------------------------------------------------------- sample --
@@ -336,37 +358,48 @@ class EngineBackend:
             self._cache_pages(seq, tokens)
         done: list[_Active] = []
         while act:
-            g = self._graph(len(act))
-            B, n = g.B, len(act)
+            n = len(act)
+            rem = min(a.request.max_new_tokens - len(a.tokens) for a in act)
+            S = 1 << (min(self.decode_chunk, rem).bit_length() - 1)     # power of two <= the shortest remainder
+            g = self._graph(n, S)
+            B = g.B
+            steps = np.arange(S, dtype=np.int32)
             for b, a in enumerate(act):
-                g.h_slots[b] = self.cache.append(a.seq, 1)[0]
+                g.h_slots[:, b] = self.cache.append(a.seq, S)
                 g.h_ids[b] = a.last
-                g.h_pos[b] = a.pos
-                g.h_kv[b] = a.pos + 1
-                g.uni_host[b] = float(a.uniforms[len(a.tokens)])
+                g.h_pos[:, b] = a.pos + steps
+                g.h_kv[:, b] = a.pos + 1 + steps
+                t = len(a.tokens)
+                g.uni_host[:, b] = torch.from_numpy(np.ascontiguousarray(a.uniforms[t:t + S], dtype=np.float64))
                 g.it_host[b] = 1.0 / a.request.sampling.temperature
             self.cache.manager.fill_table_np([a.seq for a in act], g.h_table[:n])
             if n < B:
-                g.h_slots[n:] = -1
+                g.h_slots[:, n:] = -1
                 g.h_ids[n:] = 0
-                g.h_pos[n:] = 0
-                g.h_kv[n:] = 1
+                g.h_pos[:, n:] = 0
+                g.h_kv[:, n:] = 1
                 g.h_table[n:] = 0
-                g.uni_host[n:] = 0.5
+                g.uni_host[:, n:] = 0.5
             res = g.run()
-            self.stats["decode_steps"] += 1
+            self.stats["decode_steps"] += S
             still = []
             for b, a in enumerate(act):
-                tok = int(res[b, 0])
-                a.tokens.append(tok)
-                a.logq.append(float(res[b, 1]))
-                a.logp.append(float(res[b, 2]))
-                a.last, a.pos = tok, a.pos + 1
                 eos = a.request.sampling.eos_token_id
-                if eos is not None and tok == eos:
-                    a.finish = "eos"
-                    done.append(a)
-                elif len(a.tokens) >= a.request.max_new_tokens:
+                start = a.pos
+                for s in range(S):
+                    tok = int(res[s, b, 0])
+                    a.tokens.append(tok)
+                    a.logq.append(float(res[s, b, 1]))
+                    a.logp.append(float(res[s, b, 2]))
+                    a.last, a.pos = tok, a.pos + 1
+                    if eos is not None and tok == eos:
+                        a.finish = "eos"
+                        break
+                    if len(a.tokens) >= a.request.max_new_tokens:
+                        break
+                if a.pos - start < S:
+                    self.cache.truncate(a.seq, a.pos)      # drop KV of steps past the sequence's end
+                if a.finish == "eos" or len(a.tokens) >= a.request.max_new_tokens:
                     done.append(a)
                 else:
                     still.append(a)

@@ -145,7 +145,7 @@ class ModelRunner:
         D = 128
         wq = lw.w_qkv if wq is None else wq
         bias = lw.b_qkv if bias is None and wq is lw.w_qkv else bias
-        qkv = K.linear(x, wq, bias=bias, out=self._buf("qkv", (T, wq.shape[0])))
+        qkv = K.linear(x, wq, bias=bias, out=self._buf("qkv", (T, wq.shape[0])), static_weights=True)
         q = self._buf("q", (T, self.q_slots, D))
         kc, vc = self.cache.layer(i)
         K.rope_cache(qkv, meta.positions, meta.slots, self.w.inv_freq, q, kc, vc, self.q_slots, self.kv_slots,
@@ -154,18 +154,19 @@ class ModelRunner:
         att = K.attention(q, kc, vc, meta.plan, out=self._buf("att", (T, self.q_slots, D)))
         wo = lw.w_o if wo is None else wo
         if self.comm.world == 1 and residual is not None:
-            return K.linear(att.view(T, -1), wo, residual=residual, out=residual)
+            return K.linear(att.view(T, -1), wo, residual=residual, out=residual, static_weights=True)
         part = self.comm.partial_buffer(T, self._buf("part", (T, self.cfg.hidden_size)))
-        return K.linear(att.view(T, -1), wo, out=part)
+        return K.linear(att.view(T, -1), wo, out=part, static_weights=True)
 
     def mlp_block(self, i: int, x: torch.Tensor, residual: torch.Tensor | None) -> torch.Tensor:
         lw = self.w.layers[i]
         T = x.shape[0]
-        act = K.linear(x, lw.w_gu, swiglu=True, out=self._buf("act", (T, lw.w_gu.shape[0] // 2)))
+        act = K.linear(x, lw.w_gu, swiglu=True, out=self._buf("act", (T, lw.w_gu.shape[0] // 2)),
+                       static_weights=True)
         if self.comm.world == 1 and residual is not None:
-            return K.linear(act, lw.w_down, residual=residual, out=residual)
+            return K.linear(act, lw.w_down, residual=residual, out=residual, static_weights=True)
         part = self.comm.partial_buffer(T, self._buf("part", (T, self.cfg.hidden_size)))
-        return K.linear(act, lw.w_down, out=part)
+        return K.linear(act, lw.w_down, out=part, static_weights=True)
 
     def layer_stack(self, h: torch.Tensor, meta: StepMeta, layers: range) -> torch.Tensor:
         """Run decoder layers over the residual stream ``h`` (updated in place).
@@ -202,7 +203,7 @@ class ModelRunner:
         x = sel if normed else K.rmsnorm(sel, self.w.final_norm, self.cfg.rms_norm_eps,
                                          out=self._buf("xl", (R, self.cfg.hidden_size)))
         local = K.linear(x, self.w.head, out=self._buf("logits_local", (R, self.vocab_local), torch.float32),
-                         out_dtype=torch.float32)
+                         out_dtype=torch.float32, static_weights=True)
         self.last_local_logits = local  # this rank's vocabulary shard (static buffer)
         if self.comm.world == 1:
             return local

@@ -30,11 +30,14 @@ def linear(
     swiglu: bool = False,
     out_dtype: torch.dtype = torch.bfloat16,
     allow_split: bool = True,
+    static_weights: bool = False,
 ) -> torch.Tensor:
     """``x @ w.T (+ bias) (+ residual)``; with ``swiglu`` the weight rows are
     tiles of [64 gate | 64 up] rows and the result is ``silu(gate) * up``.
 
     ``residual`` may alias ``out`` (in-place residual-stream update).
+    ``static_weights``: no kernel earlier in the stream writes ``w`` (inference
+    weights), so the GEMM may stream weight tiles while its predecessor runs.
     """
     rows = w.shape[0] // 2 if swiglu else w.shape[0]
     if out is None:
@@ -52,6 +55,7 @@ def linear(
             workspace.gemm_workspace(x.device),
             workspace.gemm_counters(x.device),
             workspace.status(x.device),
+            static_weights,
         )
         return out
     out.copy_(linear_reference(x, w, bias=bias, residual=residual, swiglu=swiglu).to(out.dtype))
@@ -493,3 +497,163 @@ def head_divergence(y: torch.Tensor, weight: torch.Tensor, teacher: torch.Tensor
     if k == 0:
         return 0.5 * (log_q.exp() - log_p.exp()).abs().sum(-1)
     return (log_p.exp() * (log_p - log_q)).sum(-1)
+
+
+# ------------------------------------------------ training-time autograd ops --
+def transpose_padded(a: torch.Tensor, multiple: int = 8) -> torch.Tensor:
+    """``a.t()`` as a contiguous tensor whose row length is zero-padded to ``multiple`` elements.
+
+    The tcgen05 GEMM reads K-major operands through TMA, whose row stride must
+    be a multiple of 16 bytes; weight gradients reduce over the token
+    dimension, which becomes the row length after the transpose.
+    """
+    rows, cols = a.shape
+    padded = -(-rows // multiple) * multiple
+    if padded == rows:
+        return a.t().contiguous()
+    out = torch.zeros(cols, padded, dtype=a.dtype, device=a.device)
+    out[:, :rows].copy_(a.t())
+    return out
+
+
+class _KernelLinear(torch.autograd.Function):
+    """y = x @ w^T (+ b) on the tcgen05 GEMM, with a tcgen05 backward.
+
+    dX = dY @ W runs as dY @ (W^T)^T with a transposed copy of W (cached per
+    weight version); dW = dY^T @ X runs as (dY^T) @ (X^T)^T with transposed
+    activations.  Both are ordinary K-major problems for the same kernel.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w, b, w_t, need_wgrad):
+        ctx.save_for_backward(x, w, w_t)
+        ctx.has_bias = b is not None
+        ctx.need_wgrad = need_wgrad
+        return linear(x, w, bias=b)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w, w_t = ctx.saved_tensors
+        gy = gy.to(torch.bfloat16).contiguous()
+        gx = gw = gb = None
+        if ctx.needs_input_grad[0]:
+            wt = w_t if w_t is not None else w.t().contiguous()
+            gx = linear(gy, wt)
+        if ctx.need_wgrad:
+            gw = linear(transpose_padded(gy), transpose_padded(x), out_dtype=torch.float32)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            gb = gy.float().sum(0)
+        return gx, gw, gb, None, None
+
+
+def kernel_linear(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None = None, *, w_t: torch.Tensor | None = None,
+                  weight_grad: bool = True) -> torch.Tensor:
+    """Autograd linear on the sm_100a GEMM (CUDA) or PyTorch (CPU).
+
+    ``weight_grad=True`` returns an fp32 gradient for ``w`` (for fp32 masters)."""
+    shape = x.shape
+    x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+    if x.is_cuda:
+        y = _KernelLinear.apply(x2, w, b, w_t, weight_grad and w.requires_grad)
+    else:
+        y = torch.nn.functional.linear(x2.float(), w.float(), None if b is None else b.float()).to(torch.bfloat16)
+    return y.reshape(*shape[:-1], w.shape[0])
+
+
+class _TargetLogprob(torch.autograd.Function):
+    """log softmax(logits)[target] per row with the fused statistics / gradient kernels."""
+
+    @staticmethod
+    def forward(ctx, logits, targets):
+        ext = _ext.require()
+        R = logits.shape[0]
+        lse1 = torch.empty(R, dtype=torch.float32, device=logits.device)
+        lseT = torch.empty_like(lse1)
+        logp = torch.empty_like(lse1)
+        logq = torch.empty_like(lse1)
+        ext.row_stats(logits, None, targets, lse1, lseT, logp, logq)
+        ctx.save_for_backward(logits, lse1, targets)
+        return logp
+
+    @staticmethod
+    def backward(ctx, g):
+        logits, lse, targets = ctx.saved_tensors
+        grad = torch.empty_like(logits)
+        _ext.require().logprob_grad(logits, lse, targets, g.float().contiguous(), grad)
+        return grad, None
+
+
+def target_logprob(logits: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+    """Differentiable per-row log-probability of ``targets`` under softmax(logits) (fp32 rows)."""
+    if logits.is_cuda:
+        return _TargetLogprob.apply(logits.float().contiguous(), targets.to(torch.int32).contiguous())
+    return logits.float().log_softmax(-1).gather(-1, targets.long()[:, None]).squeeze(-1)
+
+
+class _HeadLogprob(torch.autograd.Function):
+    """Per-row log softmax(h @ W^T)[target] over row chunks, without keeping [rows x V] logits.
+
+    Forward: per chunk, fp32 logits from the tcgen05 GEMM and the fused row
+    statistics (logsumexp, target log-probability).  Backward: per chunk the
+    logits are recomputed, one kernel writes ``g (onehot - softmax)`` in bf16
+    into a [rows x V] buffer, and d h = d logits @ W; finally one GEMM forms
+    d W = d logits^T @ h.  With ``sink`` the weight gradient is not returned
+    through autograd: ``sink(produce)`` is called with a function that
+    writes d W into a given fp32 [V, H] tensor (or allocates one for None).
+    """
+
+    @staticmethod
+    def forward(ctx, h, weight, targets, chunk, sink):
+        R, V = h.shape[0], weight.shape[0]
+        logp = torch.empty(R, dtype=torch.float32, device=h.device)
+        lse = torch.empty_like(logp)
+        buf = torch.empty(min(chunk, R) * V, dtype=torch.float32, device=h.device)
+        for s in range(0, R, chunk):
+            e = min(R, s + chunk)
+            logits = linear(h[s:e], weight, out=buf[: (e - s) * V].view(e - s, V), out_dtype=torch.float32)
+            if h.is_cuda:
+                _ext.require().row_stats(logits, None, targets[s:e], lse[s:e], None, logp[s:e], None)
+            else:
+                lse[s:e] = logits.logsumexp(-1)
+                logp[s:e] = logits.gather(-1, targets[s:e].long()[:, None]).squeeze(-1) - lse[s:e]
+        ctx.save_for_backward(h, weight, targets, lse)
+        ctx.chunk, ctx.sink = chunk, sink
+        return logp
+
+    @staticmethod
+    def backward(ctx, g):
+        h, weight, targets, lse = ctx.saved_tensors
+        R, V = h.shape[0], weight.shape[0]
+        g = g.float().contiguous()
+        glogits = torch.empty(R, V, dtype=torch.bfloat16, device=h.device)
+        buf = torch.empty(min(ctx.chunk, R) * V, dtype=torch.float32, device=h.device)
+        w_t = weight.t().contiguous()
+        gh = torch.empty_like(h)
+        for s in range(0, R, ctx.chunk):
+            e = min(R, s + ctx.chunk)
+            logits = linear(h[s:e], weight, out=buf[: (e - s) * V].view(e - s, V), out_dtype=torch.float32)
+            if h.is_cuda:
+                _ext.require().logprob_grad(logits, lse[s:e], targets[s:e], g[s:e], glogits[s:e])
+            else:
+                p = torch.exp(logits - lse[s:e, None])
+                onehot = torch.zeros_like(p).scatter_(1, targets[s:e].long()[:, None], 1.0)
+                glogits[s:e] = (g[s:e, None] * (onehot - p)).to(torch.bfloat16)
+            linear(glogits[s:e], w_t, out=gh[s:e])
+        del buf, w_t
+        gt, ht = transpose_padded(glogits), transpose_padded(h)
+        del glogits
+
+        def produce(out):
+            return linear(gt, ht, out=out, out_dtype=torch.float32)
+
+        if ctx.sink is not None:
+            ctx.sink(produce)
+            return gh, None, None, None, None
+        return gh, produce(None), None, None, None
+
+
+def head_logprob(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, *, chunk_rows: int = 2048,
+                 sink=None) -> torch.Tensor:
+    """log softmax(h @ weight^T)[targets] per row (fp32), differentiable in ``h`` and ``weight``."""
+    return _HeadLogprob.apply(h.to(torch.bfloat16).contiguous(), weight, targets.to(torch.int32).contiguous(),
+                              int(chunk_rows), sink)

@@ -1,0 +1,139 @@
+"""GRPO trainer on CPU: loss maths, gradients against an fp32 autograd oracle, data-parallel sharding (gloo)."""
+
+import os
+
+import pytest
+import torch
+
+from online_speculation_b200.models.decoder import DecoderConfig, build_weights, random_state_dict, reference_forward
+from online_speculation_b200.training.grpo import GRPOConfig, GRPOTrainer, group_advantages, grpo_loss
+
+TINY = DecoderConfig(vocab_size=256, hidden_size=128, intermediate_size=128, num_hidden_layers=2,
+                     num_attention_heads=2, num_key_value_heads=1, tie_word_embeddings=True, name="t")
+
+
+def test_group_advantages():
+    r = torch.tensor([1.0, 0.0, 1.0, 1.0, 0.0, 0.0, 0.0, 1.0])
+    a = group_advantages(r, 4)
+    assert torch.allclose(a, torch.tensor([0.25, -0.75, 0.25, 0.25, -0.25, -0.25, -0.25, 0.75]))
+    s = group_advantages(r, 4, "group")
+    assert torch.allclose(s.view(2, 4).std(1), torch.ones(2), atol=1e-3)
+
+
+def test_grpo_loss_ratio_one_gradient():
+    torch.manual_seed(0)
+    lp = torch.randn(2, 5, requires_grad=True)
+    ref = lp.detach() + 0.1 * torch.randn(2, 5)
+    adv = torch.tensor([0.5, -0.5])
+    mask = torch.ones(2, 5, dtype=torch.bool)
+    mask[1, 3:] = False
+    loss, info = grpo_loss(lp, lp.detach(), ref, adv, mask, beta=0.04, epsilon=0.2)
+    loss.backward()
+    # d/dlp of -(A - beta (e^{ref-lp} - (ref-lp) - 1)) / n / B
+    n = mask.float().sum(1, keepdim=True)
+    d = ref - lp.detach()
+    expect = -(adv[:, None] - 0.04 * (-torch.exp(d) + 1)) / n / 2 * mask
+    assert torch.allclose(lp.grad, expect, atol=1e-6)
+    assert info["clip_fraction"] == 0.0
+
+
+def _oracle_grads(cfg, sd, ids, prompt_len, adv, mask):
+    """fp32 autograd of the ratio-one GRPO loss (KL gradient is zero at ref = policy)."""
+    f = {k: v.float().requires_grad_(True) for k, v in sd.items()}
+    B = ids.shape[0]
+    terms = []
+    for b in range(B):
+        logits = reference_forward(cfg, f, ids[b])
+        lp = logits[prompt_len - 1:-1].log_softmax(-1).gather(-1, ids[b, prompt_len:, None]).squeeze(-1)
+        m = mask[b].float()
+        terms.append((adv[b] * lp * m).sum() / m.sum())
+    loss = -torch.stack(terms).mean()
+    loss.backward()
+    return {k: v.grad if v.grad is not None else torch.zeros_like(v) for k, v in f.items()}
+
+
+def test_gradients_match_fp32_oracle():
+    cfg = TINY
+    sd = random_state_dict(cfg, seed=3, std=0.05)
+    conf = GRPOConfig(group_size=2, prompts_per_rank=1, prompt_length=6, completion_length=10, head_chunk_rows=7)
+    tr = GRPOTrainer(cfg, conf, device="cpu", rollouts=False, state_dict=sd)
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (2, 16), generator=g)
+    mask = torch.ones(2, 10, dtype=torch.bool)
+    mask[1, 7:] = False
+    rewards = torch.tensor([1.0, 0.0])
+    grad, info = tr.compute_gradients(ids, mask, rewards)
+    oracle = _oracle_grads(cfg, sd, ids, 6, group_advantages(rewards, 2), mask)
+    mapped = build_weights(cfg, oracle, dtype=torch.float32)
+    checks = {"embed": mapped.embed, "final_norm": mapped.final_norm}
+    for i, lw in enumerate(mapped.layers):
+        for f in ("in_norm", "post_norm", "w_qkv", "b_qkv", "w_o", "w_gu", "w_down"):
+            checks[f"{i}.{f}"] = getattr(lw, f)
+    for name, ref in checks.items():
+        got = tr.params.view(name, grad)
+        err = (got - ref).norm() / ref.norm().clamp(min=1e-12)
+        assert err < 0.05, (name, float(err))
+    assert info["kl"] == pytest.approx(0.0, abs=1e-6)
+
+
+def test_optimizer_step_moves_parameters():
+    conf = GRPOConfig(group_size=2, prompts_per_rank=1, prompt_length=4, completion_length=4, learning_rate=1e-3)
+    tr = GRPOTrainer(TINY, conf, device="cpu", rollouts=False, seed=2)
+    before = tr.parameter("0.w_o").clone()
+    ids = torch.randint(0, TINY.vocab_size, (2, 8), generator=torch.Generator().manual_seed(0))
+    tr.train_on(ids, torch.ones(2, 4, dtype=torch.bool), torch.tensor([1.0, 0.0]))
+    after = tr.parameter("0.w_o")
+    assert not torch.equal(before, after)
+    assert tr.step_count == 1 and torch.isfinite(tr.master).all()
+
+
+def _dp_worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        conf = GRPOConfig(group_size=2, prompts_per_rank=1, prompt_length=4, completion_length=6)
+        tr = GRPOTrainer(TINY, conf, device="cpu", rollouts=False, seed=5, group=dist.group.WORLD)
+        ids = torch.randint(0, TINY.vocab_size, (2 * world, 10), generator=torch.Generator().manual_seed(7))
+        rewards = torch.tensor([1.0, 0.0, 0.0, 1.0, 1.0, 1.0, 0.0, 0.0][: 2 * world])
+        mask = torch.ones(2 * world, 6, dtype=torch.bool)
+        g, _ = tr.compute_gradients(ids[2 * rank:2 * rank + 2], mask[:2], rewards[2 * rank:2 * rank + 2])
+        shard = g.clone()
+        tr._optimizer_step(g)
+        q.put((rank, shard, tr.params.shard_ranges(), tr.params.flat.clone()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_data_parallel_sharded_gradients_and_allgather():
+    import torch.multiprocessing as mp
+
+    from online_speculation_b200.training.grpo import FlatParameters, _named_tensors
+
+    world, port = 2, 29611
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_dp_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=240) for _ in range(world)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+    assert torch.equal(res[0][3], res[1][3]), "all-gathered parameters differ across ranks"
+    # the data-parallel gradient, reassembled from the shards in the world-2 layout
+    layout = FlatParameters(_named_tensors(build_weights(TINY, random_state_dict(TINY, seed=5))), world, 0, "cpu")
+    dp = torch.zeros(layout.numel, dtype=torch.float32)
+    for _, shard, ranges, _ in res:
+        for lo, hi, pos in ranges:
+            dp[lo:hi] = shard[pos:pos + hi - lo]
+    # single-process oracle on the union of the ranks' batches (groups are not split across ranks)
+    conf = GRPOConfig(group_size=2, prompts_per_rank=world, prompt_length=4, completion_length=6)
+    one = GRPOTrainer(TINY, conf, device="cpu", rollouts=False, seed=5)
+    ids = torch.randint(0, TINY.vocab_size, (2 * world, 10), generator=torch.Generator().manual_seed(7))
+    full, _ = one.compute_gradients(ids, torch.ones(2 * world, 6, dtype=torch.bool),
+                                    torch.tensor([1.0, 0.0, 0.0, 1.0]))
+    for name in one.params.slots:
+        a, b = layout.view(name, dp), one.params.view(name, full)
+        err = (a - b).norm() / b.norm().clamp(min=1e-12)
+        assert err < 1e-2, (name, float(err))   # bf16 reductions over different row counts
