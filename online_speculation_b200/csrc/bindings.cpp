@@ -15,6 +15,7 @@
 #include "comm.h"
 #include "elementwise.h"
 #include "gemm.h"
+#include "moe.h"
 #include "kv_manager.h"
 #include "sampling.h"
 
@@ -442,6 +443,130 @@ void adamw(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> publish
 
 }  // namespace
 
+// ------------------------------------------------------------------- MoE ---
+void grouped_tiles(Tensor offsets, int64_t groups, int64_t tiles_m, int64_t bn, Tensor tiles, Tensor total) {
+  CHECK_CUDA(offsets);
+  CHECK_DT(offsets, torch::kInt32);
+  CHECK_DT(tiles, torch::kInt32);
+  CHECK_DT(total, torch::kInt32);
+  TORCH_CHECK(offsets.numel() >= groups + 1 && tiles.numel() % 4 == 0, "grouped_tiles shapes");
+  c10::cuda::CUDAGuard guard(offsets.device());
+  check(osb::grouped_tiles_launch(offsets.data_ptr<int>(), groups, tiles_m, bn, tiles.data_ptr<int>(),
+                                  tiles.numel() / 4, total.data_ptr<int>(), at::cuda::getCurrentCUDAStream()),
+        "grouped_tiles");
+}
+
+void grouped_gemm(Tensor w, Tensor x, Tensor out, int64_t epilogue, Tensor tiles, Tensor total, int64_t groups,
+                  int64_t bn, Tensor workspace, Tensor counters, Tensor status) {
+  CHECK_CUDA(w);
+  CHECK_CUDA(x);
+  CHECK_DT(w, torch::kBFloat16);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_ROWS(w);
+  CHECK_ROWS(x);
+  CHECK_ROWS(out);
+  TORCH_CHECK(w.size(1) == x.size(1), "reduction dimensions differ");
+  TORCH_CHECK(groups > 0 && w.size(0) % groups == 0, "w must stack `groups` equal weight blocks");
+  const int M = w.size(0) / groups;
+  const int out_cols = epilogue == 1 ? M / 2 : M;
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == out_cols, "output shape mismatch");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16 || out.scalar_type() == torch::kFloat32, "bf16 or fp32 output");
+  CHECK_DT(tiles, torch::kInt32);
+  CHECK_DT(total, torch::kInt32);
+  c10::cuda::CUDAGuard guard(w.device());
+  osb::GemmProblem p{};
+  p.w = bf(w);
+  p.ldw = w.stride(0);
+  p.x = bf(x);
+  p.ldx = x.stride(0);
+  p.M = M;
+  p.N = x.size(0);
+  p.K = w.size(1);
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.out_f32 = out.scalar_type() == torch::kFloat32;
+  p.epilogue = static_cast<int>(epilogue);
+  p.allow_split = 0;
+  p.workspace = workspace.data_ptr<float>();
+  p.workspace_floats = workspace.numel();
+  p.counters = counters.data_ptr<int>();
+  p.counter_slots = counters.numel();
+  p.status = status.data_ptr<int>();
+  p.group_tiles = tiles.data_ptr<int>();
+  p.group_total = total.data_ptr<int>();
+  p.groups = static_cast<int>(groups);
+  p.group_tile_cap = static_cast<int>(tiles.numel() / 4);
+  p.group_bn = static_cast<int>(bn);
+  if (x.size(0) == 0) return;
+  check(osb::gemm_launch(p, at::cuda::getCurrentCUDAStream()), "grouped tcgen05 gemm");
+}
+
+void moe_route(Tensor logits, int64_t k, bool renorm, Tensor topk_idx, Tensor topk_w, Tensor counts) {
+  CHECK_CUDA(logits);
+  CHECK_ROWS(logits);
+  CHECK_DT(logits, torch::kFloat32);
+  CHECK_DT(topk_idx, torch::kInt32);
+  CHECK_DT(topk_w, torch::kFloat32);
+  CHECK_DT(counts, torch::kInt32);
+  const int T = logits.size(0), E = logits.size(1);
+  TORCH_CHECK(topk_idx.numel() == static_cast<long long>(T) * k && topk_w.numel() == topk_idx.numel() &&
+                  counts.numel() >= E,
+              "moe_route shapes");
+  c10::cuda::CUDAGuard guard(logits.device());
+  check(osb::moe_route_launch(logits.data_ptr<float>(), logits.stride(0), T, E, k, renorm ? 1 : 0,
+                              topk_idx.data_ptr<int>(), topk_w.data_ptr<float>(), counts.data_ptr<int>(),
+                              at::cuda::getCurrentCUDAStream()),
+        "moe_route");
+}
+
+void moe_offsets(Tensor counts, Tensor offsets, Tensor cursor) {
+  CHECK_CUDA(counts);
+  CHECK_DT(counts, torch::kInt32);
+  CHECK_DT(offsets, torch::kInt32);
+  CHECK_DT(cursor, torch::kInt32);
+  const int E = counts.numel();
+  TORCH_CHECK(offsets.numel() == E + 1 && cursor.numel() == E, "moe_offsets shapes");
+  c10::cuda::CUDAGuard guard(counts.device());
+  check(osb::moe_offsets_launch(counts.data_ptr<int>(), E, offsets.data_ptr<int>(), cursor.data_ptr<int>(),
+                                at::cuda::getCurrentCUDAStream()),
+        "moe_offsets");
+}
+
+void moe_dispatch(Tensor x, Tensor topk_idx, Tensor cursor, Tensor xp, Tensor slot_of) {
+  CHECK_CUDA(x);
+  CHECK_ROWS(x);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(xp, torch::kBFloat16);
+  CHECK_DT(topk_idx, torch::kInt32);
+  CHECK_DT(slot_of, torch::kInt32);
+  const int T = x.size(0), H = x.size(1);
+  const int k = T > 0 ? topk_idx.numel() / T : 0;
+  TORCH_CHECK(xp.is_contiguous() && xp.size(1) == H && xp.size(0) >= static_cast<long long>(T) * k &&
+                  slot_of.numel() == topk_idx.numel(),
+              "moe_dispatch shapes");
+  c10::cuda::CUDAGuard guard(x.device());
+  check(osb::moe_dispatch_launch(bf(x), x.stride(0), T, k, H, topk_idx.data_ptr<int>(), cursor.data_ptr<int>(),
+                                 bfm(xp), slot_of.data_ptr<int>(), at::cuda::getCurrentCUDAStream()),
+        "moe_dispatch");
+}
+
+void moe_combine(Tensor y, Tensor slot_of, Tensor topk_w, Tensor h, bool accumulate) {
+  CHECK_CUDA(y);
+  CHECK_ROWS(y);
+  CHECK_ROWS(h);
+  CHECK_DT(y, torch::kBFloat16);
+  CHECK_DT(h, torch::kBFloat16);
+  CHECK_DT(slot_of, torch::kInt32);
+  CHECK_DT(topk_w, torch::kFloat32);
+  const int T = h.size(0), H = h.size(1);
+  const int k = T > 0 ? slot_of.numel() / T : 0;
+  TORCH_CHECK(y.size(1) == H && topk_w.numel() == slot_of.numel(), "moe_combine shapes");
+  c10::cuda::CUDAGuard guard(h.device());
+  check(osb::moe_combine_launch(bf(y), y.stride(0), slot_of.data_ptr<int>(), topk_w.data_ptr<float>(), T, k, H,
+                                bfm(h), h.stride(0), accumulate ? 1 : 0, at::cuda::getCurrentCUDAStream()),
+        "moe_combine");
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels and C++ runtime of online_speculation_b200";
   m.def("gemm", &gemm);
@@ -462,6 +587,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("logprob_grad", &logprob_grad);
   m.def("adamw", &adamw);
   m.def("gemm_pick_bn", &osb::gemm_pick_bn);
+  m.def("grouped_tiles", &grouped_tiles);
+  m.def("grouped_gemm", &grouped_gemm);
+  m.def("moe_route", &moe_route);
+  m.def("moe_offsets", &moe_offsets);
+  m.def("moe_dispatch", &moe_dispatch);
+  m.def("moe_combine", &moe_combine);
   m.def("set_pdl", [](bool on) { osb::pdl_enabled() = on; });
   m.def("pdl_enabled", []() -> bool { return osb::pdl_enabled(); });
 

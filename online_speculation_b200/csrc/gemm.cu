@@ -57,7 +57,37 @@ struct Args {
   int* counters;
   int* status;
   int prefetch_a;       // issue the first stages' weight tiles before griddepcontrol.wait
+  // Grouped mode (gtiles != null): tile w is gtiles[w] = {group, tm, row0, row_end}; the
+  // weight rows of group g start at g * M; the tile count is *gtotal (device memory).
+  const int4* gtiles;
+  const int* gtotal;
 };
+
+struct TileCoord {
+  int split, tile, tm, arow, row0, row_end;
+};
+
+template <int BN>
+__device__ __forceinline__ TileCoord tile_coord(const Args& a, int w) {
+  TileCoord c;
+  if (a.gtiles != nullptr) {
+    const int4 t = a.gtiles[w];
+    c.split = 0;
+    c.tile = w;
+    c.tm = t.y;
+    c.arow = t.x * a.M + t.y * kBM;
+    c.row0 = t.z;
+    c.row_end = t.w;
+  } else {
+    c.split = w % a.splits;
+    c.tile = w / a.splits;
+    c.tm = c.tile % a.tiles_m;
+    c.arow = c.tm * kBM;
+    c.row0 = (c.tile / a.tiles_m) * BN;
+    c.row_end = a.N;
+  }
+  return c;
+}
 
 template <int BN>
 struct Smem {
@@ -78,9 +108,9 @@ struct Smem {
 // dimension, issued in batches (the residual may alias the output, so loads
 // are grouped ahead of the stores instead of alternating with them).
 template <int BN>
-__device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32], int tm, int tn, int chunk, int r,
-                                             float* stage, int ep_tid) {
-  const int t0 = tn * BN + chunk * 32;
+__device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32], int tm, int row0, int row_end,
+                                             int chunk, int r, float* stage, int ep_tid) {
+  const int t0 = row0 + chunk * 32;
   const bool swiglu = a.epilogue == 1;
   const int f0 = swiglu ? tm * 64 : tm * kBM;       // first output feature of this tile
   const int out_cols = swiglu ? a.M / 2 : a.M;      // output row width (valid features)
@@ -89,7 +119,7 @@ __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32]
 #pragma unroll
   for (int j = 0; j < 32; ++j) stage[j * (kBM + 4) + r] = v[j] + b;
   named_barrier(1, 128);
-  const int valid_t = min(32, a.N - t0);
+  const int valid_t = min(32, row_end - t0);
   if (a.vec_ok) {
     // vectors of 8 features; width/8 vectors per token row
     constexpr int kMaxIter = (32 * kBM / 8 + 127) / 128;  // 4
@@ -305,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int total = a.tiles_m * a.tiles_n * a.splits;
+  const int total = a.gtiles != nullptr ? *a.gtotal : a.tiles_m * a.tiles_n * a.splits;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -317,28 +347,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the first stages of this CTA's first work item are armed and their A
       // tiles requested before griddepcontrol.wait; their B tiles follow it.
       int armed = 0;
-      if (a.prefetch_a && blockIdx.x < total) {
-        const int w = blockIdx.x;
-        const int tm = (w / a.splits) % a.tiles_m;
-        const int kb0 = (w % a.splits) * a.kb_per_split;
+      if (a.prefetch_a && a.gtiles == nullptr && blockIdx.x < total) {
+        const TileCoord c = tile_coord<BN>(a, blockIdx.x);
+        const int kb0 = c.split * a.kb_per_split;
         const int kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
         armed = min(STAGES, kb1 - kb0);
         for (int s = 0; s < armed; ++s) {
           mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-          tma_load_2d(sA + s * S::kABytes, &tmA, (kb0 + s) * kBK, tm * kBM, &full[s]);
+          tma_load_2d(sA + s * S::kABytes, &tmA, (kb0 + s) * kBK, c.arow, &full[s]);
         }
       }
       pdl_wait();
       for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-        const int split = w % a.splits;
-        const int tile = w / a.splits;
-        const int tm = tile % a.tiles_m;
-        const int tn = tile / a.tiles_m;
-        const int kb0 = split * a.kb_per_split;
+        const TileCoord c = tile_coord<BN>(a, w);
+        const int kb0 = c.split * a.kb_per_split;
         const int kb1 = min(a.k_blocks, kb0 + a.kb_per_split);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (issued < armed) {
-            tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, tn * BN, &full[stage]);
+            tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, c.row0, &full[stage]);
           } else {
             if (!mbar_wait(&empty[stage], phase ^ 1, a.status, kErrTmaWait)) {
               ok = false;
@@ -346,8 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
-            tma_load_2d(sA + stage * S::kABytes, &tmA, kb * kBK, tm * kBM, &full[stage]);
-            tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, tn * BN, &full[stage]);
+            tma_load_2d(sA + stage * S::kABytes, &tmA, kb * kBK, c.arow, &full[stage]);
+            tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, c.row0, &full[stage]);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -420,10 +446,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     const int ep_tid = threadIdx.x - 64;
     for (int w = blockIdx.x; w < total; w += gridDim.x) {
-      const int split = w % a.splits;
-      const int tile = w / a.splits;
-      const int tm = tile % a.tiles_m;
-      const int tn = tile / a.tiles_m;
+      const TileCoord tc = tile_coord<BN>(a, w);
+      const int split = tc.split;
+      const int tile = tc.tile;
+      const int tm = tc.tm;
       bool ok = mbar_wait(&tfull[acc], acc_phase, a.status, kErrEpilogueWait);
       // All epilogue threads must agree before touching shared state.
       if (!ok) *abort_flag = 1;
@@ -445,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(t_acc + c * 32, v);
-          finish_chunk<BN>(a, v, tm, tn, c, r, xchg, ep_tid);
+          finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, xchg, ep_tid);
         }
         tc_fence_before();
         __syncwarp();
@@ -485,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += __ldcg(&p[(c * 32 + j) * kBM + r]);
             }
-            finish_chunk<BN>(a, v, tm, tn, c, r, xchg, ep_tid);
+            finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, xchg, ep_tid);
           }
         }
       }
@@ -584,7 +610,8 @@ template <int BN>
 cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream) {
   using S = Smem<BN>;
   CUtensorMap ma, mb;
-  if (!make_map(&ma, p.w, p.M, p.K, p.ldw, kBM)) return cudaErrorInvalidValue;
+  const int a_rows = p.group_tiles != nullptr ? p.groups * p.M : p.M;
+  if (!make_map(&ma, p.w, a_rows, p.K, p.ldw, kBM)) return cudaErrorInvalidValue;
   if (!make_map(&mb, p.x, p.N, p.K, p.ldx, BN)) return cudaErrorInvalidValue;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -597,6 +624,15 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
   Args a = a0;
   const int tiles = a.tiles_m * a.tiles_n;
   const int sms = sm_count(dev);
+  if (p.group_tiles != nullptr) {
+    a.splits = 1;
+    a.kb_per_split = a.k_blocks;
+    a.cluster = 1;
+    a.gtiles = reinterpret_cast<const int4*>(p.group_tiles);
+    a.gtotal = p.group_total;
+    const int grid = std::max(1, std::min(p.group_tile_cap, sms));
+    return launch_pdl(gemm_tn_kernel<BN>, dim3(grid), dim3(kThreads), S::kTotal, stream, ma, mb, a);
+  }
   a.splits = 1;
   a.kb_per_split = a.k_blocks;
   a.cluster = 1;
@@ -662,6 +698,67 @@ bool& pdl_enabled() {
   return on;
 }
 
+namespace {
+// One CTA: exclusive scan of the per-group tile counts, then every thread
+// writes the tiles of its groups (tm outer, token tile inner, so that CTAs
+// running at the same time share weight tiles in L2).
+__global__ void __launch_bounds__(1024) grouped_tiles_kernel(const int* __restrict__ offsets, int groups, int tiles_m,
+                                                             int bn, int4* __restrict__ tiles, int cap,
+                                                             int* __restrict__ total) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < groups; base += blockDim.x) {
+    const int g = base + threadIdx.x;
+    int n = 0, rows = 0, lo = 0;
+    if (g < groups) {
+      lo = offsets[g];
+      rows = offsets[g + 1] - lo;
+      n = rows > 0 ? ((rows + bn - 1) / bn) * tiles_m : 0;
+    }
+    // block-wide inclusive scan of n
+    int x = n;
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int s = lane < (blockDim.x + 31) / 32 ? warp_sums[lane] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      warp_sums[lane] = s;
+    }
+    __syncthreads();
+    const int start = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + x - n;
+    if (g < groups) {
+      const int nt = rows > 0 ? (rows + bn - 1) / bn : 0;
+      int k = start;
+      for (int tm = 0; tm < tiles_m; ++tm)
+        for (int t = 0; t < nt; ++t, ++k)
+          if (k < cap) tiles[k] = make_int4(g, tm, lo + t * bn, lo + rows);
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = start + n;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = min(carry, cap);
+}
+}  // namespace
+
+cudaError_t grouped_tiles_launch(const int* offsets, int groups, int tiles_m, int bn, int* tiles, int cap, int* total,
+                                 cudaStream_t stream) {
+  if (groups <= 0 || tiles_m <= 0 || bn <= 0 || cap <= 0) return cudaErrorInvalidValue;
+  grouped_tiles_kernel<<<1, 1024, 0, stream>>>(offsets, groups, tiles_m, bn, reinterpret_cast<int4*>(tiles), cap,
+                                               total);
+  return cudaGetLastError();
+}
+
 int gemm_pick_bn(int tokens) {
   if (tokens <= 32) return 32;
   if (tokens <= 64) return 64;
@@ -689,7 +786,12 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.N = p.N;
   a.K = p.K;
   a.k_blocks = (p.K + kBK - 1) / kBK;
-  const int bn = gemm_pick_bn(p.N);
+  if (p.group_tiles != nullptr) {
+    if (p.M % kBM || p.groups <= 0 || p.group_total == nullptr || p.group_tile_cap <= 0 ||
+        (p.group_bn != 32 && p.group_bn != 64 && p.group_bn != 128 && p.group_bn != 256))
+      return cudaErrorInvalidValue;
+  }
+  const int bn = p.group_tiles != nullptr ? p.group_bn : gemm_pick_bn(p.N);
   a.tiles_m = (p.M + kBM - 1) / kBM;
   a.tiles_n = (p.N + bn - 1) / bn;
   a.out = p.out;
@@ -703,6 +805,8 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.counters = p.counters;
   a.status = p.status;
   a.prefetch_a = p.prefetch_weights;
+  a.gtiles = nullptr;
+  a.gtotal = nullptr;
   {
     const int esz = p.out_f32 ? 4 : 2;
     const bool out_ok = (reinterpret_cast<uintptr_t>(p.out) % 16 == 0) && ((p.ldo * esz) % 16 == 0);

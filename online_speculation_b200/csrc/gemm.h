@@ -27,10 +27,24 @@ struct GemmProblem {
   int* status;                    // bounded-wait error word
   int prefetch_weights;           // stream weight tiles before the predecessor kernel completes
                                   // (only where no kernel earlier in the stream writes w)
+  // Grouped GEMM (e.g. MoE experts): w holds `groups` stacked [M, K] weights; the
+  // tile list {group, tm, row0, row_end} (int4) and its length live in device memory,
+  // so the row segments of each group may be data dependent.  group_bn fixes the token
+  // tile (32/64/128/256) used to build the list.
+  const int* group_tiles;
+  const int* group_total;
+  int groups;
+  int group_tile_cap;
+  int group_bn;
 };
 
 cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream);
 bool& pdl_enabled();   // programmatic dependent launch for the forward-path kernels
+
+// Tile list of a grouped GEMM from group row offsets [groups + 1] (device): every
+// group contributes ceil(rows / bn) x tiles_m tiles; *total receives the count.
+cudaError_t grouped_tiles_launch(const int* offsets, int groups, int tiles_m, int bn, int* tiles, int cap, int* total,
+                                 cudaStream_t stream);
 int gemm_pick_bn(int tokens);
 long long gemm_workspace_floats(int M, int N, int K, int sms);
 

@@ -332,9 +332,20 @@ def gumbel_sample(logits, inv_temp, seeds, *, seed_index=None, streams=None, row
     if logits.is_cuda:
         _ext.require().gumbel_sample(logits, inv_temp, seeds, seed_index, streams, row_in_seq, int(salt), tokens)
         return tokens
-    gen = torch.Generator().manual_seed(int(seeds.flatten()[0]) ^ int(salt))
     x = logits.float() * (inv_temp.float()[:, None] if inv_temp is not None else 1.0)
-    e = torch.empty_like(x).exponential_(generator=gen)
+    if seed_index is None and streams is None and row_in_seq is None:
+        gen = torch.Generator().manual_seed(int(seeds.flatten()[0]) ^ int(salt))
+        e = torch.empty_like(x).exponential_(generator=gen)
+    else:
+        # per-row streams keyed like the device kernel's counters (row-independent draws)
+        e = torch.empty_like(x)
+        flat = seeds.flatten().tolist()
+        for r in range(rows):
+            sd = flat[int(seed_index[r])] if seed_index is not None else flat[0]
+            key = (int(sd) * 1000003 + (int(streams[r]) if streams is not None else 0)) * 1000003
+            key = (key + (int(row_in_seq[r]) if row_in_seq is not None else r)) ^ int(salt)
+            gen = torch.Generator().manual_seed(key % (2**63))
+            e[r].exponential_(generator=gen)
     tokens.copy_((x.softmax(-1) / e).argmax(-1))
     return tokens
 
@@ -657,3 +668,102 @@ def head_logprob(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, *
     """log softmax(h @ weight^T)[targets] per row (fp32), differentiable in ``h`` and ``weight``."""
     return _HeadLogprob.apply(h.to(torch.bfloat16).contiguous(), weight, targets.to(torch.int32).contiguous(),
                               int(chunk_rows), sink)
+
+
+# --------------------------------------------------------------------- MoE --
+class MoEBuffers:
+    """Static device buffers of one MoE layer invocation (reused across layers and steps)."""
+
+    def __init__(self, max_tokens: int, experts: int, top_k: int, hidden: int, ffn: int, device):
+        self.T, self.E, self.k, self.H, self.F = max_tokens, experts, top_k, hidden, ffn
+        rows = max_tokens * top_k
+        i32 = dict(dtype=torch.int32, device=device)
+        self.logits = torch.empty(max_tokens, experts, dtype=torch.float32, device=device)
+        self.idx = torch.empty(rows, **i32)
+        self.w = torch.empty(rows, dtype=torch.float32, device=device)
+        self.counts = torch.zeros(experts, **i32)
+        self.offsets = torch.zeros(experts + 1, **i32)
+        self.cursor = torch.zeros(experts, **i32)
+        self.slot_of = torch.empty(rows, **i32)
+        self.xp = torch.empty(rows, hidden, dtype=torch.bfloat16, device=device)
+        self.act = torch.empty(rows, ffn, dtype=torch.bfloat16, device=device)
+        self.y = torch.empty(rows, hidden, dtype=torch.bfloat16, device=device)
+        self.total = torch.zeros(2, **i32)
+        self.bn = 256
+        tiles_m = max(2 * ffn, hidden) // 128
+        cap = tiles_m * (-(-rows // 32) + experts)
+        self.tiles = torch.zeros(2, cap * 4, **i32)
+
+
+def moe_pick_bn(rows: int, experts: int) -> int:
+    """Token tile of the grouped expert GEMMs from the mean rows per expert."""
+    mean = rows / max(1, experts)
+    return 32 if mean <= 32 else 64 if mean <= 64 else 128 if mean <= 160 else 256
+
+
+def moe_ffn(x: torch.Tensor, h: torch.Tensor, router: torch.Tensor, w_gu: torch.Tensor, w_down: torch.Tensor, *,
+            top_k: int, renorm: bool = False, buffers: MoEBuffers | None = None) -> torch.Tensor:
+    """h += sum_j w_j * expert_{e_j}(x) for the top-k experts of every row of x (in place).
+
+    ``router`` [E, H]; ``w_gu`` [E * 2F, H] with each expert's gate/up rows
+    interleaved in 64-row tiles; ``w_down`` [E * H, F].  Routing, dispatch,
+    the per-expert tile list and the combine run on the device: no host
+    synchronisation between the router and the expert GEMMs.
+    """
+    T, H = x.shape
+    E = router.shape[0]
+    F = w_down.shape[1]
+    if T == 0:
+        return h
+    if not x.is_cuda:
+        return _moe_ffn_reference(x, h, router, w_gu, w_down, top_k, renorm)
+    b = buffers
+    if b is None or b.T < T or b.E != E or b.k != top_k or b.H != H or b.F != F:
+        b = MoEBuffers(T, E, top_k, H, F, x.device)
+    ext = _ext.require()
+    rows = T * top_k
+    logits = linear(x, router, out=b.logits[:T], out_dtype=torch.float32)
+    ext.moe_route(logits, top_k, renorm, b.idx[:rows], b.w[:rows], b.counts)
+    ext.moe_offsets(b.counts, b.offsets, b.cursor)
+    ext.moe_dispatch(x, b.idx[:rows], b.cursor, b.xp, b.slot_of[:rows])
+    bn = moe_pick_bn(rows, E)
+    ws, ctr, st = workspace.gemm_workspace(x.device), workspace.gemm_counters(x.device), workspace.status(x.device)
+    tm_gu, tm_dn = 2 * F // 128, H // 128
+    ext.grouped_tiles(b.offsets, E, tm_gu, bn, b.tiles[0], b.total[0:1])
+    ext.grouped_gemm(w_gu, b.xp[:rows], b.act[:rows], 1, b.tiles[0], b.total[0:1], E, bn, ws, ctr, st)
+    if tm_dn != tm_gu:
+        ext.grouped_tiles(b.offsets, E, tm_dn, bn, b.tiles[1], b.total[1:2])
+        tiles, total = b.tiles[1], b.total[1:2]
+    else:
+        tiles, total = b.tiles[0], b.total[0:1]
+    ext.grouped_gemm(w_down, b.act[:rows], b.y[:rows], 0, tiles, total, E, bn, ws, ctr, st)
+    ext.moe_combine(b.y[:rows], b.slot_of[:rows], b.w[:rows], h, True)
+    return h
+
+
+def moe_route_reference(x: torch.Tensor, router: torch.Tensor, top_k: int, renorm: bool):
+    probs = (x.float() @ router.float().t()).softmax(-1)
+    # stable top-k: larger probability first, ties to the lower expert id
+    order = torch.sort(-probs, dim=-1, stable=True).indices[:, :top_k]
+    w = probs.gather(-1, order)
+    if renorm:
+        w = w / w.sum(-1, keepdim=True)
+    return order, w
+
+
+def _moe_ffn_reference(x, h, router, w_gu, w_down, top_k, renorm):
+    E = router.shape[0]
+    F = w_down.shape[1]
+    H = x.shape[1]
+    idx, w = moe_route_reference(x, router, top_k, renorm)
+    xf = x.float()
+    out = torch.zeros(x.shape[0], H, dtype=torch.float32, device=x.device)
+    for e in range(E):
+        rows, slot = (idx == e).nonzero(as_tuple=True)
+        if rows.numel() == 0:
+            continue
+        gu = linear_reference(x[rows], w_gu[e * 2 * F:(e + 1) * 2 * F], swiglu=True).to(torch.bfloat16)
+        y = (gu.float() @ w_down[e * H:(e + 1) * H].float().t()).to(torch.bfloat16).float()
+        out.index_add_(0, rows, y * w[rows, slot][:, None])
+    h.copy_((h.float() + out).to(h.dtype))
+    return h
