@@ -1,4 +1,5 @@
 """MoE layer and masked-diffusion model on the sm_100a kernels, against fp32 PyTorch."""
+import math
 
 import pytest
 import torch
@@ -106,3 +107,74 @@ def test_diffusion_backend_on_moe_engine():
     greedy = DiffusionSamplingConfig(block_length=8, steps_per_block=8, temperature=0.0, cfg_scale=0.5)
     g = be.sample_batch([DiffusionGenerationRequest((3, 4, 5), 16, greedy, 0, "g")])[0]
     assert len(g.token_ids) == 16 and g.trajectory_logprob is None
+
+
+def test_lora_linear_forward_backward_matches_fp32():
+    from online_speculation_b200.training.lora import LoRAParameters, lora_linear
+
+    torch.manual_seed(4)
+    x = torch.randn(200, 256, device="cuda").bfloat16().requires_grad_(True)
+    w = (torch.randn(384, 256, device="cuda") * 0.05).bfloat16()
+    lo = LoRAParameters(256, 384, 8, groups=3, device="cuda")
+    with torch.no_grad():
+        lo.B.normal_(0, 0.1)
+    y = lora_linear(x, w, lo, 2.0)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    xf = x.detach().float().requires_grad_(True)
+    A = lo.A.detach().clone().requires_grad_(True)
+    B = lo.B.detach().clone().requires_grad_(True)
+    yf = xf @ w.float().t() + 2.0 * (xf @ A.t()) @ (B * lo.block_mask).t()
+    yf.backward(gy.float())
+    assert (y.float() - yf).norm() / yf.norm() < 0.01
+    for got, ref in ((x.grad.float(), xf.grad), (lo.A.grad, A.grad), (lo.B.grad, B.grad)):
+        assert (got - ref).norm() / ref.norm() < 0.02
+
+
+def test_moe_autograd_backward_matches_reference():
+    from online_speculation_b200.training.moe_autograd import FrozenExperts, _moe_reference_autograd, \
+        moe_ffn_autograd
+
+    torch.manual_seed(5)
+    T, H, Fd, E, k = 160, 256, 128, 8, 2
+    router = (torch.randn(E, H) * 0.5).bfloat16()
+    gu = (torch.randn(E * 2 * Fd, H) * 0.05).bfloat16()
+    down = (torch.randn(E * H, Fd) * 0.05).bfloat16()
+    x0 = torch.randn(T, H).bfloat16()
+    h0 = torch.randn(T, H).bfloat16()
+    gout = torch.randn(T, H)
+    exg = FrozenExperts(router.cuda(), gu.cuda(), down.cuda(), k, False)
+    x = x0.cuda().requires_grad_(True)
+    h = h0.cuda().requires_grad_(True)
+    out = moe_ffn_autograd(x, h, exg, torch.zeros((), device="cuda", requires_grad=True))
+    out.float().backward(gout.cuda())
+    exc = FrozenExperts(router, gu, down, k, False)
+    xc = x0.float().requires_grad_(True)
+    hc = h0.float().requires_grad_(True)
+    outc = _moe_reference_autograd(xc, hc, exc)
+    outc.float().backward(gout)
+    assert (out.float().cpu() - outc.float()).norm() / outc.float().norm() < 0.02
+    assert (x.grad.float().cpu() - xc.grad).norm() / xc.grad.norm() < 0.05
+    assert torch.allclose(h.grad.float().cpu(), hc.grad, atol=1e-2)
+
+
+def test_vrpo_step_on_gpu():
+    from online_speculation_b200.dllm.config import VRPOSamplingConfig
+    from online_speculation_b200.models.moe import PRESETS, build_weights, random_state_dict
+    from online_speculation_b200.training.lora import LoRAConfig
+    from online_speculation_b200.training.vrpo import LoRAMoEPolicy, VRPOTrainer, VRPOTrainingConfig
+
+    cfg = PRESETS["tiny-moe"]
+    sd = random_state_dict(cfg, seed=6)
+    gpu = LoRAMoEPolicy(build_weights(cfg, sd, device="cuda"), LoRAConfig(rank=8))
+    cpu = LoRAMoEPolicy(build_weights(cfg, sd, device="cpu"), LoRAConfig(rank=8))
+    g = torch.Generator().manual_seed(1)
+    pairs = [tuple(tuple(torch.randint(0, 500, (n,), generator=g).tolist()) for n in (32, 32, 32))]
+    conf = VRPOTrainingConfig(learning_rate=1e-3, gradient_accumulation_steps=1,
+                              sampling=VRPOSamplingConfig(timestep_samples=4))
+    tg, tc = VRPOTrainer(gpu, pairs, conf), VRPOTrainer(cpu, pairs, conf)
+    rg, rc = tg.train_step(), tc.train_step()
+    assert rg["loss"] == pytest.approx(math.log(2), abs=1e-4)
+    assert rg["grad_norm"] == pytest.approx(rc["grad_norm"], rel=0.1)
+    r2 = tg.train_step()
+    assert math.isfinite(r2["loss"]) and r2["preference_score"] != 0.0
