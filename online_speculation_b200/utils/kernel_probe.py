@@ -1,0 +1,197 @@
+"""Time one hot kernel in isolation (and give ``ncu`` a small, self-terminating target).
+
+    python -m online_speculation_b200.utils.kernel_probe gemm M N K [--swiglu] [--residual]
+    python -m online_speculation_b200.utils.kernel_probe grouped E M K ROWS [--swiglu]
+    python -m online_speculation_b200.utils.kernel_probe moe T [--preset llada-moe-7b-a1b]
+    python -m online_speculation_b200.utils.kernel_probe attention B CTX [--heads 28 --kv-heads 4]
+    python -m online_speculation_b200.utils.kernel_probe sample ROWS V
+
+Each subcommand builds inputs larger than L2 where the problem allows (weights
+rotate through ``--copies`` buffers so back-to-back launches read HBM), runs
+``--warmup`` launches, then times ``--iters`` launches captured in a CUDA
+graph with CUDA events, and prints one JSON line: microseconds per launch and
+the achieved bandwidth / FLOP rate against ``MEASURED_PEAKS.json`` when the
+file is present.  Under ``ncu`` use ``--iters 1 --warmup 2 --no-graph``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from ..ops import kernels as K
+
+
+def _peaks() -> dict:
+    here = os.path.dirname(os.path.abspath(__file__))
+    path = os.path.join(here, "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def _time(body, iters: int, warmup: int, graph: bool) -> float:
+    for _ in range(warmup):
+        body()
+    torch.cuda.synchronize()
+    if graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(iters):
+                body()
+        torch.cuda.synchronize()
+        run = g.replay
+    else:
+        def run():
+            for _ in range(iters):
+                body()
+    run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1e3 / iters
+
+
+class _Rotate:
+    def __init__(self, items):
+        self.items, self.i = items, 0
+
+    def next(self):
+        v = self.items[self.i % len(self.items)]
+        self.i += 1
+        return v
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(prog="python -m online_speculation_b200.utils.kernel_probe")
+    sub = p.add_subparsers(dest="kind", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("M", type=int)
+    g.add_argument("N", type=int)
+    g.add_argument("K", type=int)
+    g.add_argument("--swiglu", action="store_true")
+    g.add_argument("--residual", action="store_true")
+    gr = sub.add_parser("grouped")
+    for n in ("E", "M", "K", "rows"):
+        gr.add_argument(n, type=int)
+    gr.add_argument("--swiglu", action="store_true")
+    mo = sub.add_parser("moe")
+    mo.add_argument("T", type=int)
+    mo.add_argument("--preset", default="llada-moe-7b-a1b")
+    at = sub.add_parser("attention")
+    at.add_argument("B", type=int)
+    at.add_argument("ctx", type=int)
+    at.add_argument("--heads", type=int, default=28)
+    at.add_argument("--kv-heads", type=int, default=4)
+    sa = sub.add_parser("sample")
+    sa.add_argument("rows", type=int)
+    sa.add_argument("V", type=int)
+    for q in (g, gr, mo, at, sa):
+        q.add_argument("--iters", type=int, default=20)
+        q.add_argument("--warmup", type=int, default=3)
+        q.add_argument("--copies", type=int, default=0, help="weight buffers to rotate through (0 = auto)")
+        q.add_argument("--no-graph", action="store_true")
+    a = p.parse_args(argv)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    torch.manual_seed(0)
+    peaks = _peaks()
+    out: dict = {"kind": a.kind}
+    graph = not a.no_graph
+
+    def copies(nbytes):
+        return a.copies or max(1, min(16, int(3 * 126e6 // max(1, nbytes)) + 1))
+
+    if a.kind == "gemm":
+        wb = a.M * a.K * 2
+        ws = _Rotate([(torch.randn(a.M, a.K, device=dev) * 0.02).bfloat16() for _ in range(copies(wb))])
+        x = torch.randn(a.N, a.K, device=dev).bfloat16()
+        cols = a.M // 2 if a.swiglu else a.M
+        o = torch.randn(a.N, cols, device=dev).bfloat16()
+
+        def body():
+            K.linear(x, ws.next(), swiglu=a.swiglu, residual=o if a.residual else None, out=o)
+        us = _time(body, a.iters, a.warmup, graph)
+        flops = 2 * a.M * a.N * a.K
+        bytes_ = wb + a.N * a.K * 2 + a.N * cols * 2 * (2 if a.residual else 1)
+        out.update(M=a.M, N=a.N, K=a.K, us=us, tflops=flops / us / 1e6, gbs=bytes_ / us / 1e3)
+    elif a.kind == "grouped":
+        E, M, Kd, R = a.E, a.M, a.K, a.rows
+        w = (torch.randn(E * M, Kd, device=dev) * 0.02).bfloat16()
+        x = torch.randn(R, Kd, device=dev).bfloat16()
+        counts = torch.full((E,), R // E, dtype=torch.int32)
+        counts[: R - int(counts.sum())] += 1
+        offs = torch.cat((torch.zeros(1, dtype=torch.int32), counts.cumsum(0).int())).to(dev)
+        bn = K.moe_pick_bn(R, E)
+        tiles = torch.zeros((M // 128) * (-(-R // 32) + E) * 4, dtype=torch.int32, device=dev)
+        total = torch.zeros(1, dtype=torch.int32, device=dev)
+        ext = K._ext.require()
+        ext.grouped_tiles(offs, E, M // 128, bn, tiles, total)
+        o = torch.empty(R, M // 2 if a.swiglu else M, dtype=torch.bfloat16, device=dev)
+        wsp, ctr, st = K.workspace.gemm_workspace(dev), K.workspace.gemm_counters(dev), K.workspace.status(dev)
+
+        def body():
+            ext.grouped_gemm(w, x, o, 1 if a.swiglu else 0, tiles, total, E, bn, wsp, ctr, st)
+        us = _time(body, a.iters, a.warmup, graph)
+        flops = 2 * R * M * Kd
+        out.update(E=E, M=M, K=Kd, rows=R, bn=bn, us=us, tflops=flops / us / 1e6)
+    elif a.kind == "moe":
+        from ..models.moe import PRESETS
+
+        c = PRESETS[a.preset]
+        E, H, Fd, k = c.num_experts, c.hidden_size, c.moe_intermediate_size, c.num_experts_per_tok
+        router = (torch.randn(E, H, device=dev) * 0.02).bfloat16()
+        gu = (torch.randn(E * 2 * Fd, H, device=dev) * 0.02).bfloat16()
+        down = (torch.randn(E * H, Fd, device=dev) * 0.02).bfloat16()
+        x = torch.randn(a.T, H, device=dev).bfloat16()
+        h = torch.randn(a.T, H, device=dev).bfloat16()
+        buf = K.MoEBuffers(a.T, E, k, H, Fd, dev)
+
+        def body():
+            K.moe_ffn(x, h, router, gu, down, top_k=k, buffers=buf)
+        us = _time(body, a.iters, a.warmup, graph)
+        flops = 2 * a.T * k * 3 * H * Fd + 2 * a.T * E * H
+        out.update(T=a.T, us=us, tflops=flops / us / 1e6)
+    elif a.kind == "attention":
+        B, ctx, hq, hkv = a.B, a.ctx, a.heads, a.kv_heads
+        pps = -(-ctx // 32)
+        kc = torch.randn(B * pps, hkv, 32, 128, device=dev).bfloat16()
+        vc = torch.randn_like(kc)
+        table = (torch.arange(B, dtype=torch.int32)[:, None] * pps + torch.arange(pps, dtype=torch.int32)[None])
+        plan = K.plan_attention(table, [1] * B, [ctx] * B, [0] * B, hq // hkv, dev)
+        q = torch.randn(B, hq, 128, device=dev).bfloat16()
+        o = torch.empty_like(q)
+
+        def body():
+            K.attention(q, kc, vc, plan, out=o)
+        us = _time(body, a.iters, a.warmup, graph)
+        bytes_ = 2 * B * ctx * hkv * 128 * 2
+        out.update(B=B, ctx=ctx, us=us, gbs=bytes_ / us / 1e3)
+    else:
+        logits = torch.randn(a.rows, a.V, device=dev)
+        it = torch.ones(a.rows, device=dev)
+        uni = torch.rand(a.rows, dtype=torch.float64, device=dev)
+
+        def body():
+            K.sample(logits, it, uni)
+        us = _time(body, a.iters, a.warmup, graph)
+        out.update(rows=a.rows, V=a.V, us=us, gbs=a.rows * a.V * 4 / us / 1e3)
+    if "gbs" in out and peaks.get("hbm_gbs"):
+        out["frac_hbm_of_measured"] = out["gbs"] / peaks["hbm_gbs"]
+    if "tflops" in out and peaks.get("bf16_tflops"):
+        out["frac_bf16_of_measured"] = out["tflops"] / peaks["bf16_tflops"]
+    print(json.dumps(out))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
