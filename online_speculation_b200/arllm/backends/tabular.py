@@ -152,3 +152,36 @@ class TabularBackend:
                     ctx.append(tok)
                 out.append(tuple(vals))
         return out
+
+
+def _tabular_statistics(self, requests, *, confidence_top_k=None):
+    """Exact per-token statistics (entropy, self-certainty, top-K confidence) of the tabular model."""
+    from ...engine.backend import SequenceScoreStatistics
+
+    out = []
+    for req in requests:
+        pol = req.sampling or SamplingConfig()
+        if not pol.full_support:
+            raise ValueError("entropy and self-certainty require a full-support policy")
+        for cont in req.continuations:
+            if not cont:
+                raise ValueError("confidence rewards require nonempty continuations")
+            ctx = list(req.prefix)
+            lps, negent, cert, conf = [], [], [], []
+            for tok in cont:
+                p = self.probabilities(tuple(ctx), pol)
+                lp = np.log(np.maximum(p, 1e-300))
+                lps.append(float(lp[tok]))
+                negent.append(float((p * lp).sum()))
+                cert.append(float(-(np.log(self.vocab_size) + lp.mean())))
+                if confidence_top_k:
+                    k = min(confidence_top_k, self.vocab_size)
+                    conf.append(float(-np.sort(lp)[-k:].mean()))
+                ctx.append(tok)
+            n = len(cont)
+            out.append(SequenceScoreStatistics(tuple(lps), sum(lps) / n, sum(negent) / n, sum(cert) / n, tuple(conf),
+                                               confidence_top_k))
+    return out
+
+
+TabularBackend.score_statistics_batch = _tabular_statistics

@@ -443,6 +443,20 @@ void adamw(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> publish
 
 }  // namespace
 
+void score_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tensor> targets, int64_t topk,
+                 Tensor out) {
+  CHECK_CUDA(logits);
+  CHECK_ROWS(logits);
+  CHECK_DT(logits, torch::kFloat32);
+  CHECK_DT(out, torch::kFloat32);
+  TORCH_CHECK(out.is_contiguous() && out.numel() == logits.size(0) * 4, "out must be [rows, 4]");
+  c10::cuda::CUDAGuard guard(logits.device());
+  check(osb::score_stats_launch(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1),
+                                ptr_or_null<const float>(inv_temp), ptr_or_null<const int>(targets),
+                                static_cast<int>(topk), out.data_ptr<float>(), at::cuda::getCurrentCUDAStream()),
+        "score_stats");
+}
+
 // ------------------------------------------------------------------- MoE ---
 void grouped_tiles(Tensor offsets, int64_t groups, int64_t tiles_m, int64_t bn, Tensor tiles, Tensor total) {
   CHECK_CUDA(offsets);
@@ -587,6 +601,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("logprob_grad", &logprob_grad);
   m.def("adamw", &adamw);
   m.def("gemm_pick_bn", &osb::gemm_pick_bn);
+  m.def("score_stats", &score_stats);
   m.def("grouped_tiles", &grouped_tiles);
   m.def("grouped_gemm", &grouped_gemm);
   m.def("moe_route", &moe_route);

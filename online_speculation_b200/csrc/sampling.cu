@@ -633,3 +633,145 @@ cudaError_t logprob_grad_launch(const float* logits, long long ld, int rows, int
   return cudaGetLastError();
 }
 }  // namespace osb
+
+// --------------------------------------------------------------------------
+// Scoring statistics of one logits row at temperature T, one pass:
+//   target log-probability, sum_v p_v log p_v (negative entropy),
+//   mean_v log p_v (for self-certainty), mean of the top-K log-probabilities.
+// Every thread keeps an online (max, sum e, sum e*(x-max)) state and a sorted
+// top-K list of its strided elements; the block merges states and lists.
+namespace osb {
+namespace {
+constexpr int kStatThreads = 512;
+constexpr int kMaxTopK = 16;
+
+struct OnlineSums {
+  float m, s1, s2;  // max, sum e^(x-m), sum e^(x-m) (x-m)
+};
+
+__device__ __forceinline__ OnlineSums merge_sums(OnlineSums a, OnlineSums b) {
+  if (a.m == -INFINITY) return b;
+  if (b.m == -INFINITY) return a;
+  const float m = fmaxf(a.m, b.m);
+  const float ea = __expf(a.m - m), eb = __expf(b.m - m);
+  // rescale: s2' = e^(m_old - m) (s2 + (m_old - m) s1)
+  return {m, a.s1 * ea + b.s1 * eb, ea * (a.s2 + (a.m - m) * a.s1) + eb * (b.s2 + (b.m - m) * b.s1)};
+}
+
+__global__ void __launch_bounds__(kStatThreads) score_stats_kernel(const float* __restrict__ logits, long long ld,
+                                                                   int V, const float* __restrict__ inv_temp,
+                                                                   const int* __restrict__ targets, int topk,
+                                                                   float* __restrict__ out) {
+  const int r = blockIdx.x;
+  const float* row = logits + r * ld;
+  const float it = inv_temp ? inv_temp[r] : 1.0f;
+  OnlineSums st{-INFINITY, 0.0f, 0.0f};
+  float sum_x = 0.0f;
+  float top[kMaxTopK];
+#pragma unroll
+  for (int i = 0; i < kMaxTopK; ++i) top[i] = -INFINITY;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float x = row[v] * it;
+    sum_x += x;
+    if (x == -INFINITY) continue;                  // excluded token: no mass
+    if (x > st.m) {
+      if (st.m == -INFINITY) {
+        st = {x, 1.0f, 0.0f};
+      } else {
+        const float e = __expf(st.m - x);
+        st.s2 = e * (st.s2 + (st.m - x) * st.s1);
+        st.s1 = st.s1 * e + 1.0f;
+        st.m = x;
+      }
+    } else {
+      const float e = __expf(x - st.m);
+      st.s1 += e;
+      st.s2 += e * (x - st.m);
+    }
+    if (topk > 0 && x > top[topk - 1]) {          // insertion into the sorted list
+      int j = topk - 1;
+      while (j > 0 && top[j - 1] < x) {
+        top[j] = top[j - 1];
+        --j;
+      }
+      top[j] = x;
+    }
+  }
+  __shared__ OnlineSums s_st[kStatThreads / 32];
+  __shared__ float s_x[kStatThreads / 32];
+  __shared__ float s_top[kStatThreads / 32];
+  __shared__ int s_arg[kStatThreads / 32];
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  for (int o = 16; o > 0; o >>= 1) {
+    OnlineSums other{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s1, o),
+                     __shfl_xor_sync(0xffffffffu, st.s2, o)};
+    st = merge_sums(st, other);
+    sum_x += __shfl_xor_sync(0xffffffffu, sum_x, o);
+  }
+  if (lane == 0) {
+    s_st[warp] = st;
+    s_x[warp] = sum_x;
+  }
+  __syncthreads();
+  __shared__ float s_lse;
+  if (threadIdx.x == 0) {
+    OnlineSums a = s_st[0];
+    float sx = s_x[0];
+    for (int w = 1; w < kStatThreads / 32; ++w) {
+      a = merge_sums(a, s_st[w]);
+      sx += s_x[w];
+    }
+    const float lse = a.m + logf(a.s1);
+    s_lse = lse;
+    out[r * 4 + 0] = targets ? row[targets[r]] * it - lse : 0.0f;
+    out[r * 4 + 1] = a.s2 / a.s1 - logf(a.s1);          // sum p log p
+    out[r * 4 + 2] = sx / static_cast<float>(V) - lse;  // mean log p over the vocabulary
+  }
+  __syncthreads();
+  // top-K: K rounds of block argmax over the heads of the per-thread lists
+  float acc = 0.0f;
+  int head = 0;
+  for (int k = 0; k < topk; ++k) {
+    float best = head < topk ? top[head] : -INFINITY;
+    int who = threadIdx.x;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int ow = __shfl_xor_sync(0xffffffffu, who, o);
+      if (ob > best || (ob == best && ow < who)) {
+        best = ob;
+        who = ow;
+      }
+    }
+    if (lane == 0) {
+      s_top[warp] = best;
+      s_arg[warp] = who;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float b = s_top[0];
+      int w0 = s_arg[0];
+      for (int w = 1; w < kStatThreads / 32; ++w)
+        if (s_top[w] > b || (s_top[w] == b && s_arg[w] < w0)) {
+          b = s_top[w];
+          w0 = s_arg[w];
+        }
+      s_top[0] = b;
+      s_arg[0] = w0;
+    }
+    __syncthreads();
+    if (threadIdx.x == s_arg[0]) ++head;
+    acc += s_top[0];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[r * 4 + 3] = topk > 0 ? -(acc / topk - s_lse) : 0.0f;
+}
+}  // namespace
+
+cudaError_t score_stats_launch(const float* logits, long long ld, int rows, int V, const float* inv_temp,
+                               const int* targets, int topk, float* out, cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  if (topk < 0 || topk > kMaxTopK) return cudaErrorInvalidValue;
+  score_stats_kernel<<<rows, kStatThreads, 0, stream>>>(logits, ld, V, inv_temp, targets, topk, out);
+  return cudaGetLastError();
+}
+}  // namespace osb

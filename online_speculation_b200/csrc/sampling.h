@@ -85,4 +85,8 @@ namespace osb {
 cudaError_t logprob_grad_launch(const float* logits, long long ld, int rows, int V, const float* lse,
                                 const int* targets, const float* w, void* grad, bool grad_bf16, long long ldg,
                                 cudaStream_t stream);
+// Per row: [target log p at T, sum p log p, mean_v log p, -(mean of the top-K log p)]  (out: [rows, 4]).
+cudaError_t score_stats_launch(const float* logits, long long ld, int rows, int V, const float* inv_temp,
+                               const int* targets, int topk, float* out, cudaStream_t stream);
+
 }  // namespace osb

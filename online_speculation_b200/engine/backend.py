@@ -25,6 +25,7 @@ is prefilled, in one packed batch.
 from __future__ import annotations
 
 import hashlib
+import math
 import threading
 from collections import OrderedDict
 from collections.abc import Sequence
@@ -40,6 +41,18 @@ from .kv_cache import PAGE, KVCache
 from .runner import ModelRunner, StepMeta, build_meta
 
 BASE_POLICY = SamplingConfig().policy_id
+
+
+@dataclass(frozen=True, slots=True)
+class SequenceScoreStatistics:
+    """Statistics of one scored continuation under a full-support policy."""
+
+    token_logprobs: tuple[float, ...]
+    mean_logprob: float
+    mean_negative_entropy: float
+    mean_self_certainty: float
+    token_topk_confidences: tuple[float, ...] = ()
+    confidence_top_k: int | None = None
 BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 192, 256)
 
 
@@ -430,7 +443,40 @@ class EngineBackend:
             self.stats["score_calls"] += 1
             return out
 
-    def _score_one(self, prefix: tuple, cont: tuple, sampling: SamplingConfig | None) -> tuple[float, ...]:
+    def score_statistics_batch(self, requests: Sequence[ScoreRequest], *, confidence_top_k: int | None = None
+                               ) -> list[SequenceScoreStatistics]:
+        """Per continuation: token log-probabilities plus entropy / self-certainty / top-K confidence.
+
+        Entropy and self-certainty need finite log-probabilities over the whole
+        vocabulary, so only full-support temperature policies are accepted.
+        One fused kernel pass per logits row computes all statistics.
+        """
+        if confidence_top_k is not None and not 0 < confidence_top_k <= 16:
+            raise ValueError("confidence_top_k must lie in [1, 16]")
+        out = []
+        with self._lock:
+            for req in requests:
+                pol = req.sampling or SamplingConfig()
+                if not pol.full_support:
+                    raise ValueError("entropy and self-certainty require a full-support policy")
+                for cont in req.continuations:
+                    if not cont:
+                        raise ValueError("confidence rewards require nonempty continuations")
+                    rows = self._score_one(self._model_prefix(req.prefix), tuple(cont), pol,
+                                           stats_topk=confidence_top_k or 0)
+                    V = self.runner.cfg.vocab_size
+                    logp = tuple(r[0] for r in rows)
+                    n = len(rows)
+                    out.append(SequenceScoreStatistics(
+                        logp, sum(logp) / n, sum(r[1] for r in rows) / n,
+                        sum(-(math.log(V) + r[2]) for r in rows) / n,
+                        tuple(r[3] for r in rows) if confidence_top_k else (), confidence_top_k))
+            self.stats["score_calls"] += 1
+        return out
+
+    def _score_one(self, prefix: tuple, cont: tuple, sampling: SamplingConfig | None,
+                   stats_topk: int | None = None) -> tuple:
+        """Per-token log-probabilities of ``cont`` (or, with ``stats_topk``, per-token statistics rows)."""
         if not cont:
             return ()
         r = self.runner
@@ -465,8 +511,12 @@ class EngineBackend:
                 logits = r.forward(meta)
                 targets = torch.tensor([full[p + 1] for p in range(lo, pos0 + n)], dtype=torch.int32,
                                        device=r.device)
-                _, _, logp, logq = K.row_stats(logits, it.expand(len(rows)).contiguous(), targets)
-                values += (logp if sampling is None else logq).tolist()
+                itr = it.expand(len(rows)).contiguous()
+                if stats_topk is not None:
+                    values += [tuple(v) for v in K.score_stats(logits, itr, targets, stats_topk).tolist()]
+                else:
+                    _, _, logp, logq = K.row_stats(logits, itr, targets)
+                    values += (logp if sampling is None else logq).tolist()
             else:
                 r.forward(meta, compute_logits=False)
             self.stats["prefill_tokens"] += n

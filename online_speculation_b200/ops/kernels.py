@@ -767,3 +767,21 @@ def _moe_ffn_reference(x, h, router, w_gu, w_down, top_k, renorm):
         out.index_add_(0, rows, y * w[rows, slot][:, None])
     h.copy_((h.float() + out).to(h.dtype))
     return h
+
+
+def score_stats(logits: torch.Tensor, inv_temp: torch.Tensor | None, targets: torch.Tensor | None,
+                topk: int = 0) -> torch.Tensor:
+    """[rows, 4]: target log p at T, sum p log p, mean log p over the vocabulary, -(mean top-K log p)."""
+    rows, V = logits.shape
+    out = torch.empty(rows, 4, dtype=torch.float32, device=logits.device)
+    if logits.is_cuda:
+        _ext.require().score_stats(logits, inv_temp, None if targets is None else targets.to(torch.int32).contiguous(),
+                                   int(topk), out)
+        return out
+    x = logits.float() * (inv_temp.float()[:, None] if inv_temp is not None else 1.0)
+    lp = x.log_softmax(-1)
+    out[:, 0] = lp.gather(-1, targets.long()[:, None]).squeeze(-1) if targets is not None else 0.0
+    out[:, 1] = (lp.exp() * lp).sum(-1)
+    out[:, 2] = lp.mean(-1)
+    out[:, 3] = -lp.topk(topk, -1).values.mean(-1) if topk > 0 else 0.0
+    return out
