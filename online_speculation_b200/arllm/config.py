@@ -150,3 +150,131 @@ class ConditionalISConfig:
             if lo > hi:
                 raise ValueError("rollout_log_weight_bounds must be ordered")
         require_positive("rollout_evaluation_batch_size", self.rollout_evaluation_batch_size)
+
+
+@dataclass(frozen=True, slots=True)
+class IteratedConditionalISConfig:
+    """Finite-pool i-SIR updates per candidate block (reference config.py:174-225)."""
+
+    pool_size: int = 3
+    updates: int = 4
+    rollout_count: int = 4
+    block_size: int = 16
+    total_length: int = DEFAULT_MAX_NEW_TOKENS
+    reward_temperature: float = 1.0
+    importance_log_ratio_clip: float | None = None
+    apply_importance_correction: bool = True
+
+    def __post_init__(self) -> None:
+        for name in ("pool_size", "updates", "rollout_count", "block_size", "total_length"):
+            require_positive(name, getattr(self, name))
+        if self.pool_size < 2:
+            raise ValueError("pool_size must be at least two")
+        require_positive("reward_temperature", self.reward_temperature)
+        if self.importance_log_ratio_clip is not None:
+            require_positive("importance_log_ratio_clip", self.importance_log_ratio_clip)
+            if not self.apply_importance_correction:
+                raise ValueError("importance_log_ratio_clip requires apply_importance_correction=True")
+        if self.block_size > self.total_length:
+            raise ValueError("block_size cannot exceed total_length")
+
+    @property
+    def fresh_candidate_evaluations(self) -> int:
+        return 1 + self.updates * (self.pool_size - 1)
+
+    @property
+    def pool_candidate_uses(self) -> int:
+        return self.updates * self.pool_size
+
+
+@dataclass(frozen=True, slots=True)
+class ProgressiveISConfig:
+    """Pilot / evaluation split for cost-aware conditional weights (reference config.py:228-268)."""
+
+    candidate_count: int = 4
+    pilot_rollouts_per_candidate: int = 2
+    evaluation_cost_budget: float = 16.0
+    minimum_evaluation_per_candidate: int = 1
+    block_size: int = 16
+    total_length: int = DEFAULT_MAX_NEW_TOKENS
+    reward_temperature: float = 1.0
+    importance_log_ratio_clip: float | None = None
+    reward_workers: int = 4
+    run_ahead_rollouts_per_candidate: int = 0
+    evaluation_reference_rollouts_per_candidate: int | None = None
+
+    def __post_init__(self) -> None:
+        for name in ("candidate_count", "pilot_rollouts_per_candidate", "minimum_evaluation_per_candidate",
+                     "block_size", "total_length", "reward_workers"):
+            require_positive(name, getattr(self, name))
+        require_positive("evaluation_cost_budget", self.evaluation_cost_budget)
+        require_positive("reward_temperature", self.reward_temperature)
+        if self.importance_log_ratio_clip is not None:
+            require_positive("importance_log_ratio_clip", self.importance_log_ratio_clip)
+        if self.block_size > self.total_length:
+            raise ValueError("block_size cannot exceed total_length")
+        if self.run_ahead_rollouts_per_candidate < 0:
+            raise ValueError("run_ahead_rollouts_per_candidate must be non-negative")
+        if self.evaluation_reference_rollouts_per_candidate is not None and \
+                self.evaluation_reference_rollouts_per_candidate <= 0:
+            raise ValueError("evaluation_reference_rollouts_per_candidate must be positive")
+
+
+@dataclass(frozen=True, slots=True)
+class BaseReplayConfig:
+    """Base-candidate replay with a truncated-IS history and a fresh tail (reference config.py:271-292)."""
+
+    candidate_count: int = 4
+    block_size: int = 16
+    total_length: int = DEFAULT_MAX_NEW_TOKENS
+    reward_temperature: float = 1.0
+    max_history_per_candidate: int = 8
+    fresh_rollouts: int = 2
+    truncation: float = 8.0
+    reserve_rollouts: int = 0
+
+    def __post_init__(self) -> None:
+        for name in ("candidate_count", "block_size", "total_length"):
+            require_positive(name, getattr(self, name))
+        require_positive("reward_temperature", self.reward_temperature)
+        if self.block_size > self.total_length:
+            raise ValueError("block_size cannot exceed total_length")
+        if self.max_history_per_candidate < 0:
+            raise ValueError("max_history_per_candidate must be non-negative")
+        require_positive("fresh_rollouts", self.fresh_rollouts)
+        require_positive("truncation", self.truncation)
+        if self.reserve_rollouts < 0:
+            raise ValueError("reserve_rollouts must be non-negative")
+
+
+@dataclass(frozen=True, slots=True)
+class DynamicISConfig:
+    """Defensive-mixture candidates with a variance-cost replay budget (reference config.py:295-325)."""
+
+    candidate_count: int = 4
+    block_size: int = 16
+    total_length: int = DEFAULT_MAX_NEW_TOKENS
+    reward_temperature: float = 1.0
+    max_history_per_candidate: int = 8
+    truncation: float = 8.0
+    reserve_rollouts: int = 0
+    rollout_budget: float = 64.0
+    auxiliary_mixture: float = 0.25
+    minimum_fresh_per_candidate: int = 1
+
+    def __post_init__(self) -> None:
+        for name in ("candidate_count", "block_size", "total_length"):
+            require_positive(name, getattr(self, name))
+        require_positive("reward_temperature", self.reward_temperature)
+        if self.block_size > self.total_length:
+            raise ValueError("block_size cannot exceed total_length")
+        if self.max_history_per_candidate < 0:
+            raise ValueError("max_history_per_candidate must be non-negative")
+        require_positive("truncation", self.truncation)
+        if self.reserve_rollouts < 0:
+            raise ValueError("reserve_rollouts must be non-negative")
+        require_positive("rollout_budget", self.rollout_budget)
+        require_probability("auxiliary_mixture", self.auxiliary_mixture)
+        if self.auxiliary_mixture >= 1:
+            raise ValueError("auxiliary_mixture must lie in [0, 1)")
+        require_positive("minimum_fresh_per_candidate", self.minimum_fresh_per_candidate)
