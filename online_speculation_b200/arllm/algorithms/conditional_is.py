@@ -7,20 +7,37 @@ q add the base/proposal log-ratio log p - log q of the rollout (optionally
 clipped).  The rollout weights combine by log-mean-exp and one candidate is
 selected with an explicit uniform.
 
+Rollout designs: ``iid`` (independent seeds), ``scrambled_sobol`` (one
+scrambled Sobol net per candidate, one coordinate per rollout token, inverse
+CDF) and ``arithmetic_lattice`` (a randomly shifted lattice of arithmetic-coding
+uniforms per candidate).  Every rollout stays marginally exact, so the
+candidate weight stays unbiased; only the dependence between rollouts changes.
+
+Exact early stopping: with declared bounds [a, b] on every rollout log-weight,
+rollouts are evaluated in batches and the unseen ones bound each candidate
+weight in [(S + m e^a) / R, (S + m e^b) / R].  As soon as the categorical
+selection with the step's fixed uniform is the same for every weight vector in
+that box, the remaining rollouts are skipped; the selected index is then the
+one a full evaluation would have produced.
+
 Stream names follow src/inference_scaling/arllm/algorithms/conditional_is.py:
 ("conditional_is", step, "candidate", k) and (..., "rollout", r), with selection
-from ("conditional_is", step, "select").
+from ("conditional_is", step, "select").  Reference behaviour: same file,
+:174-872.
 """
 
 from __future__ import annotations
 
 from collections.abc import Callable, Sequence
 from dataclasses import dataclass
-from math import isfinite
+from math import exp, isfinite, log
 
 from ...shared.importance import MonteCarloRolloutWeightProvider, RolloutObservation, logmeanexp
 from ...shared.rng import SeedStream
-from ...shared.stepwise import StepwiseCandidate, run_stepwise_generation
+from ...experimental.shared.bounded_selection import invariant_categorical_index
+from ...experimental.shared.rqmc import randomized_lattice_uniforms, scrambled_sobol_uniforms
+from ...shared.stepwise import (StepwiseCandidate, categorical_index_from_uniform, normalize_log_weights,
+                                run_stepwise_generation, stepwise_generation_step)
 from ...shared.types import TokenSequence
 from ..config import ConditionalISConfig, SamplingConfig
 from ..types import AutoregressiveBackend, GenerationRequest, ScoreRequest, SequenceSample
@@ -49,6 +66,8 @@ class ConditionalCandidate:
     rollouts: tuple[RolloutEvaluation, ...]
     log_weight: float
     planned_rollout_count: int = 0
+    log_weight_lower_bound: float | None = None
+    log_weight_upper_bound: float | None = None
 
 
 @dataclass(frozen=True, slots=True)
@@ -57,6 +76,12 @@ class ConditionalISStep:
     candidates: tuple[ConditionalCandidate, ...]
     selected_index: int
     probabilities: tuple[float, ...] = ()
+    rollout_evaluations_planned: int = 0
+    rollout_evaluations_performed: int = 0
+    rollout_evaluations_skipped: int = 0
+    rollout_evaluation_batches: int = 0
+    exact_early_stop: bool = False
+    selection_invariant_verified: bool = False
 
     @property
     def selected(self) -> ConditionalCandidate:
@@ -96,7 +121,8 @@ def estimate_conditional_weights(*, base_backend: AutoregressiveBackend, rollout
                                  base_sampling: SamplingConfig, rollout_sampling: SamplingConfig,
                                  reward_temperature: float, importance_log_ratio_clip: float | None,
                                  apply_importance_correction: bool, reward: TokenReward | None, seeds: SeedStream,
-                                 step_index: int, reward_batch: TokenBatchReward | None = None
+                                 step_index: int, reward_batch: TokenBatchReward | None = None,
+                                 rollout_design: str = "iid", rollout_index_offset: int = 0
                                  ) -> tuple[ConditionalCandidate, ...]:
     """Weight every candidate with its rollouts (one batched sample call for all K * R)."""
     _full_support(rollout_sampling, "off-policy rollouts")
@@ -104,6 +130,15 @@ def estimate_conditional_weights(*, base_backend: AutoregressiveBackend, rollout
         raise ValueError("rollout_count and reward_temperature must be positive")
     if (reward is None) == (reward_batch is None):
         raise ValueError("provide exactly one of reward or reward_batch")
+    if rollout_design not in ROLLOUT_DESIGNS:
+        raise ValueError("unknown rollout_design")
+    if rollout_index_offset < 0:
+        raise ValueError("rollout_index_offset must be non-negative")
+    if rollout_index_offset and rollout_design != "iid":
+        raise ValueError("staged rollout offsets require iid rollouts")
+    if rollout_design != "iid" and reward_batch is not None:
+        raise ValueError("randomized QMC rollouts need a pointwise reward: a batch-coupled reward changes with "
+                         "the dependence between rollouts")
     eos = rollout_sampling.eos_token_id
     requests, owner, prefixes, terminal = [], [], [], set()
     for k, cand in enumerate(candidates):
@@ -111,11 +146,19 @@ def estimate_conditional_weights(*, base_backend: AutoregressiveBackend, rollout
             terminal.add(k)
             continue
         prefix = prompt + generated_prefix + cand.token_ids
-        for r in range(rollout_count):
+        tok_u = arith_u = (None,) * rollout_count
+        if rollout_design == "scrambled_sobol":
+            tok_u = scrambled_sobol_uniforms(rollout_count, rollout_length, seed=seeds.derive(
+                "conditional_is", step_index, "candidate", k, "scrambled_sobol"))
+        elif rollout_design == "arithmetic_lattice":
+            arith_u = randomized_lattice_uniforms(rollout_count, seed=seeds.derive(
+                "conditional_is", step_index, "candidate", k, "arithmetic_lattice"))
+        for j in range(rollout_count):
+            r = rollout_index_offset + j
             requests.append(GenerationRequest(
                 prefix, rollout_length, rollout_sampling,
                 seeds.derive("conditional_is", step_index, "candidate", k, "rollout", r),
-                f"conditional-is:step:{step_index}:candidate:{k}:rollout:{r}"))
+                f"conditional-is:step:{step_index}:candidate:{k}:rollout:{r}", tok_u[j], arith_u[j]))
             owner.append(k)
             prefixes.append(prefix)
     samples = rollout_backend.sample_batch(requests) if requests else []
@@ -209,24 +252,153 @@ class AutoregressiveStepwiseAdapter:
             rollout_sampling=self.rollout_sampling, reward_temperature=self.config.reward_temperature,
             importance_log_ratio_clip=self.config.importance_log_ratio_clip,
             apply_importance_correction=self.config.apply_importance_correction, reward=self.reward, seeds=seeds,
-            step_index=step_index, reward_batch=self.reward_batch)
+            step_index=step_index, reward_batch=self.reward_batch, rollout_design=self.config.rollout_design)
         return [StepwiseCandidate(c, c.log_weight) for c in cands]
 
     def advance(self, state, selected: ConditionalCandidate, step_index):
         return state + selected.token_ids
 
 
-def run_conditional_is(*, base_backend: AutoregressiveBackend, prompt: TokenSequence, config: ConditionalISConfig,
-                       seeds: SeedStream, reward: TokenReward | None = None,
-                       reward_batch: TokenBatchReward | None = None,
+def _bounded_conditional_is_step(*, base_backend, rollout_backend, prompt, generated_prefix, config, base_sampling,
+                                 rollout_sampling, reward, seeds, step_index, reward_batch) -> ConditionalISStep:
+    if reward is None or reward_batch is not None:
+        raise ValueError("exact rollout early stopping requires a fixed pointwise reward")
+    if config.rollout_log_weight_bounds is None:
+        raise ValueError("exact rollout early stopping requires log-weight bounds")
+    if config.rollout_design != "iid":
+        raise ValueError("exact rollout early stopping requires iid rollouts")
+    _full_support(base_sampling, "base candidates")
+    left = config.total_length - len(generated_prefix)
+    if left <= 0:
+        raise ValueError("generated prefix has already reached total_length")
+    props = sample_candidates(base_backend, prompt + generated_prefix, config.candidate_count,
+                              min(config.block_size, left), base_sampling, seeds, step_index)
+    roll_len = max(0, left - len(props[0].token_ids))
+    eos = rollout_sampling.eos_token_id
+    terminal = [roll_len == 0 or (eos is not None and p.token_ids[-1] == eos) for p in props]
+    planned = [1 if t else config.rollout_count for t in terminal]
+    u = float(seeds.generator("conditional_is", step_index, "select").random())
+    a, b = config.rollout_log_weight_bounds
+    try:
+        w_min, w_max = exp(a), exp(b)
+    except OverflowError as e:
+        raise ValueError("rollout log-weight bounds cannot be exponentiated") from e
+    if not (isfinite(w_min) and isfinite(w_max) and w_min > 0):
+        raise ValueError("rollout log-weight bounds must map to finite positive weights")
+    R = config.rollout_count
+    seen: list[list[RolloutEvaluation]] = [[] for _ in props]
+    lo_w, hi_w, fixed, done, batches = [], [], None, 0, 0
+    while done < R:
+        n = min(config.rollout_evaluation_batch_size, R - done)
+        got = estimate_conditional_weights(
+            base_backend=base_backend, rollout_backend=rollout_backend, prompt=prompt,
+            generated_prefix=generated_prefix, candidates=props, rollout_length=roll_len, rollout_count=n,
+            base_sampling=base_sampling, rollout_sampling=rollout_sampling,
+            reward_temperature=config.reward_temperature,
+            importance_log_ratio_clip=config.importance_log_ratio_clip,
+            apply_importance_correction=config.apply_importance_correction, reward=reward, seeds=seeds,
+            step_index=step_index, rollout_index_offset=done)
+        batches += 1
+        for k, c in enumerate(got):
+            if terminal[k]:
+                if not seen[k]:
+                    seen[k].append(c.rollouts[0])
+                continue
+            for ev in c.rollouts:
+                if not a <= ev.log_weight <= b:
+                    raise ValueError("observed rollout log-weight lies outside the declared bounds")
+            seen[k].extend(c.rollouts)
+        done += n
+        lo_w, hi_w = [], []
+        for k, evs in enumerate(seen):
+            tot = sum(exp(e.log_weight) for e in evs)
+            if terminal[k]:
+                lo_w.append(tot)
+                hi_w.append(tot)
+            else:
+                m = R - len(evs)
+                lo_w.append((tot + m * w_min) / R)
+                hi_w.append((tot + m * w_max) / R)
+        fixed = invariant_categorical_index(lo_w, hi_w, uniform=u)
+        if fixed is not None:
+            break
+    cands = tuple(ConditionalCandidate(p.token_ids, tuple(p.reference_token_logprobs or p.token_logprobs),
+                                       tuple(seen[k]), log(0.5 * (lo_w[k] + hi_w[k])), planned[k],
+                                       log(lo_w[k]), log(hi_w[k])) for k, p in enumerate(props))
+    probs = normalize_log_weights([c.log_weight for c in cands])
+    sel = categorical_index_from_uniform(probs, u)
+    if fixed is not None and sel != fixed:
+        raise RuntimeError("bounded categorical decision disagrees with the representative weights")
+    performed = sum(len(c.rollouts) for c in cands)
+    skipped = sum(planned) - performed
+    return ConditionalISStep(len(generated_prefix), cands, sel, probs, sum(planned), performed, skipped, batches,
+                             skipped > 0, skipped > 0 and fixed is not None)
+
+
+def _check_policies(base_sampling: SamplingConfig, rollout_sampling: SamplingConfig) -> None:
+    _full_support(base_sampling, "base candidates")
+    _full_support(rollout_sampling, "off-policy rollouts")
+    if base_sampling.eos_token_id != rollout_sampling.eos_token_id:
+        raise ValueError("candidate and rollout policies must agree on eos_token_id")
+
+
+def conditional_is_step(*, base_backend: AutoregressiveBackend, rollout_backend: AutoregressiveBackend,
+                        prompt: TokenSequence, generated_prefix: TokenSequence, config: ConditionalISConfig,
+                        base_sampling: SamplingConfig, rollout_sampling: SamplingConfig,
+                        reward: TokenReward | None, seeds: SeedStream, step_index: int,
+                        reward_batch: TokenBatchReward | None = None) -> ConditionalISStep:
+    """One conditional-IS block choice from an explicit generated prefix."""
+    kw = dict(base_backend=base_backend, rollout_backend=rollout_backend, prompt=tuple(prompt), config=config,
+              base_sampling=base_sampling, rollout_sampling=rollout_sampling, reward=reward,
+              reward_batch=reward_batch)
+    if config.exact_rollout_early_stop:
+        return _bounded_conditional_is_step(generated_prefix=tuple(generated_prefix), seeds=seeds,
+                                            step_index=step_index, **kw)
+    sel = stepwise_generation_step(AutoregressiveStepwiseAdapter(**kw), tuple(generated_prefix), step_index, seeds,
+                                   selection_namespace=("conditional_is",))
+    cands = tuple(c.value for c in sel.candidates)
+    n = sum(len(c.rollouts) for c in cands)
+    return ConditionalISStep(len(generated_prefix), cands, sel.selected_index, sel.probabilities, n, n, 0, 1)
+
+
+def run_conditional_is(base_backend: AutoregressiveBackend, prompt: TokenSequence, config: ConditionalISConfig,
+                       reward: TokenReward | None = None, seeds: SeedStream | None = None, *,
+                       base_sampling: SamplingConfig | None = None,
                        rollout_backend: AutoregressiveBackend | None = None,
-                       base_sampling: SamplingConfig = SamplingConfig(),
-                       rollout_sampling: SamplingConfig | None = None) -> ConditionalISResult:
+                       rollout_sampling: SamplingConfig | None = None,
+                       reward_batch: TokenBatchReward | None = None) -> ConditionalISResult:
+    """Generate a sequence by repeated conditional-IS block choices."""
+    if seeds is None:
+        raise ValueError("run_conditional_is needs a SeedStream")
+    base_sampling = base_sampling or SamplingConfig()
+    rollout_sampling = rollout_sampling or base_sampling
+    rollout_backend = rollout_backend or base_backend
+    _check_policies(base_sampling, rollout_sampling)
+    prompt = tuple(prompt)
+    if config.exact_rollout_early_stop:
+        gen: TokenSequence = ()
+        steps = []
+        eos = base_sampling.eos_token_id
+        while len(gen) < config.total_length and (eos is None or eos not in gen):
+            st = conditional_is_step(base_backend=base_backend, rollout_backend=rollout_backend, prompt=prompt,
+                                     generated_prefix=gen, config=config, base_sampling=base_sampling,
+                                     rollout_sampling=rollout_sampling, reward=reward, seeds=seeds,
+                                     step_index=len(steps), reward_batch=reward_batch)
+            gen += st.selected.token_ids
+            if eos is not None and eos in gen:
+                gen = gen[:gen.index(eos) + 1]
+            steps.append(st)
+        return ConditionalISResult(prompt, gen, tuple(steps))
     adapter = AutoregressiveStepwiseAdapter(
-        base_backend=base_backend, rollout_backend=rollout_backend or base_backend, prompt=prompt, config=config,
-        base_sampling=base_sampling, rollout_sampling=rollout_sampling or base_sampling, reward=reward,
-        reward_batch=reward_batch)
+        base_backend=base_backend, rollout_backend=rollout_backend, prompt=prompt, config=config,
+        base_sampling=base_sampling, rollout_sampling=rollout_sampling, reward=reward, reward_batch=reward_batch)
     result = run_stepwise_generation(adapter, seeds, selection_namespace=("conditional_is",))
-    steps = tuple(ConditionalISStep(len(s.state_before), tuple(c.value for c in s.candidates), s.selected_index,
-                                    s.probabilities) for s in result.steps)
-    return ConditionalISResult(tuple(prompt), result.final_state, steps)
+    steps = []
+    for s in result.steps:
+        cands = tuple(c.value for c in s.candidates)
+        n = sum(len(c.rollouts) for c in cands)
+        steps.append(ConditionalISStep(len(s.state_before), cands, s.selected_index, s.probabilities, n, n, 0, 1))
+    return ConditionalISResult(prompt, result.final_state, tuple(steps))
+
+
+ROLLOUT_DESIGNS = ("iid", "scrambled_sobol", "arithmetic_lattice")

@@ -139,8 +139,10 @@ class ConditionalISConfig:
                 raise ValueError("importance_log_ratio_clip requires apply_importance_correction=True")
         if self.block_size > self.total_length:
             raise ValueError("block_size cannot exceed total_length")
-        if self.rollout_design not in ("iid", "sobol", "lattice"):
-            raise ValueError("rollout_design must be iid, sobol or lattice")
+        if self.rollout_design not in ("iid", "scrambled_sobol", "arithmetic_lattice"):
+            raise ValueError("unknown rollout_design")
+        if self.exact_rollout_early_stop and self.rollout_design != "iid":
+            raise ValueError("exact rollout early stopping requires iid rollouts")
         if self.exact_rollout_early_stop and self.rollout_log_weight_bounds is None:
             raise ValueError("exact early stopping needs rollout_log_weight_bounds")
         if self.rollout_log_weight_bounds is not None:
