@@ -9,6 +9,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+from ..shared.config import RuntimeConfig as RuntimeConfig  # noqa: F401  (re-exported)
+from ..shared.config import SMCForestConfig as SMCForestConfig  # noqa: F401  (re-exported)
 from ..shared.config import canonical_float, require_finite, require_positive, require_probability
 
 DEFAULT_MAX_NEW_TOKENS = 32768
