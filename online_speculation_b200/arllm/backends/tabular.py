@@ -102,6 +102,12 @@ class TabularBackend:
     def probabilities(self, prefix: TokenSequence, sampling: SamplingConfig | None = None) -> np.ndarray:
         return apply_policy(self._row(tuple(prefix)), sampling)
 
+    def next_token_probabilities(self, prefix: TokenSequence, block: TokenSequence = ()) -> np.ndarray:
+        """Temperature-1 distributions after prefix + block[:i] for i = 0..len(block), [len(block) + 1, V]."""
+        ctx = tuple(prefix)
+        block = tuple(block)
+        return np.stack([self._row(ctx + block[:i]) for i in range(len(block) + 1)]).astype(np.float64)
+
     def sample_batch(self, requests: Sequence[GenerationRequest]) -> list[SequenceSample]:
         out = []
         for req in requests:

@@ -23,8 +23,9 @@
 // Tensor cores: bf16 mma.sync m16n8k16 with ldmatrix operand loads, online
 // softmax in fp32 with exp2.  Two warp layouts:
 //   kRowsSplit  : 4 warps x 16 rows share each 32-key page (prefill / diffusion),
-//   kKeysSplit  : 4 warps split the pages of one 16-row tile and merge their
-//                 partial softmax states in shared memory (decode / verify / draft).
+//   TMA key split: up to 32 rows (two m16 tiles) of one sequence; four key
+//                 groups stream 16-key chunks with TMA and merge their partial
+//                 softmax states in shared memory (decode / verify / draft).
 #include "attention.h"
 #include "common.cuh"
 
@@ -169,16 +170,17 @@ __device__ __forceinline__ void load_q(const AttnArgs& a, WarpState& st, int q0,
 }
 
 // Process one chunk of CH (16 or 32) keys already resident in shared memory.
-template <int CH = 32>
-__device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, const __nv_bfloat16* sK,
-                                             const __nv_bfloat16* sV, int key0, int kvlen, int bidir, int lane) {
+// kaddr(key, d) / vaddr(key, d): shared-memory byte address of the 8-element
+// (16-byte) row segment starting at column d of key row `key` of K / V.
+template <int CH, class KAddr, class VAddr>
+__device__ __forceinline__ void process_keys(const AttnArgs& a, WarpState& st, KAddr kaddr, VAddr vaddr, int key0,
+                                             int kvlen, int bidir, int lane) {
   constexpr int NB = CH / 8;  // key blocks of 8
   float s[NB][4];
 #pragma unroll
   for (int n = 0; n < NB; ++n)
 #pragma unroll
     for (int i = 0; i < 4; ++i) s[n][i] = 0.0f;
-  const uint32_t kbase = smem_u32(sK);
   // S = Q K^T over NB key blocks of 8
 #pragma unroll
   for (int n = 0; n < NB; ++n) {
@@ -186,7 +188,7 @@ __device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, c
     for (int kk = 0; kk < kD / 16; kk += 2) {
       // matrices: (keys n*8.., d kk*16+0..7), (.., +8), (.., (kk+1)*16), (.., +8)
       const int mi = lane / 8, ri = lane % 8;
-      const uint32_t addr = kbase + ((n * 8 + ri) * kStride + kk * 16 + mi * 8) * 2;
+      const uint32_t addr = kaddr(n * 8 + ri, kk * 16 + mi * 8);
       uint32_t b0, b1, b2, b3;
       ldsm_x4(addr, b0, b1, b2, b3);
       mma16816(s[n], st.qf[kk], b0, b1);
@@ -242,7 +244,6 @@ __device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, c
     st.o[n][3] *= corr[1];
   }
   // O += P V  (CH / 16 k-steps of 16 keys)
-  const uint32_t vbase = smem_u32(sV);
 #pragma unroll
   for (int kk = 0; kk < CH / 16; ++kk) {
     uint32_t pa[4];
@@ -257,11 +258,21 @@ __device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, c
       const int key = kk * 16 + (mi & 1) * 8 + ri;
       const int d = n * 8 + (mi >> 1) * 8;
       uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(vbase + (key * kStride + d) * 2, b0, b1, b2, b3);
+      ldsm_x4_t(vaddr(key, d), b0, b1, b2, b3);
       mma16816(st.o[n], pa, b0, b1);
       mma16816(st.o[n + 1], pa, b2, b3);
     }
   }
+}
+
+// Chunk of CH keys stored as padded rows (kStride elements per key row).
+template <int CH = 32>
+__device__ __forceinline__ void process_page(const AttnArgs& a, WarpState& st, const __nv_bfloat16* sK,
+                                             const __nv_bfloat16* sV, int key0, int kvlen, int bidir, int lane) {
+  const uint32_t kb = smem_u32(sK), vb = smem_u32(sV);
+  process_keys<CH>(
+      a, st, [kb](int key, int d) { return kb + (key * kStride + d) * 2; },
+      [vb](int key, int d) { return vb + (key * kStride + d) * 2; }, key0, kvlen, bidir, lane);
 }
 
 __device__ __forceinline__ void store_rows(const AttnArgs& a, const WarpState& st, int q0, int rows, int row_base,
@@ -321,21 +332,58 @@ __global__ void __launch_bounds__(128) attn_rows_kernel(const AttnArgs a) {
   store_rows(a, st, q0, rows, row0 + warp * 16, g, lane);
 }
 
-// 4 warps split the 16-key chunks of one 16-row tile (chunk c -> warp c % 4),
-// each with a 3-stage cp.async ring, then merge their softmax states.
-constexpr int kChunk = 16;
-constexpr int kStages = 3;
-constexpr int kStageElems = 2 * kChunk * kStride;          // K and V of one chunk
-constexpr int kWarpBufElems = kStages * kStageElems;
-constexpr int kKeysSmemBytes = 4 * kWarpBufElems * 2 > (4 * 16 * kD + 128) * 4 ? 4 * kWarpBufElems * 2
-                                                                               : (4 * 16 * kD + 128) * 4;
+// Decode / verify / draft tiles (at most 32 query rows of one sequence and kv
+// head).  MT m-tiles of 16 rows x 4 key groups = 4 * MT warps.  Key group kg
+// owns the 16-key chunks j = kg, kg + 4, ...; one lane of its first warp
+// streams them with TMA (two 64-column boxes of K and of V, 128-byte swizzle)
+// into a kTStages ring guarded by full / empty mbarriers, and the MT warps of
+// the group share every chunk, so the KV of a (sequence, kv head) crosses into
+// shared memory once per tile.  The key groups' softmax states merge in shared
+// memory at the end.
+constexpr int kCh = 16;
+constexpr int kKG = 4;
+constexpr int kTStages = 3;
+constexpr int kBoxBytes = kCh * 64 * 2;          // 16 key rows x 64 bf16 columns
+constexpr int kChunkBytes = 4 * kBoxBytes;       // K lo | K hi | V lo | V hi
+constexpr int kGroupBytes = kTStages * kChunkBytes;
 
-__global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
+template <int MT>
+struct TmaSmem {
+  static constexpr int kPipe = kKG * kGroupBytes;
+  static constexpr int kMerge = MT * kKG * (16 * kD + 32) * 4;
+  static constexpr int kBody = kPipe > kMerge ? kPipe : kMerge;
+  static constexpr int kBarOffset = kBody;
+  static constexpr int kTotal = 1024 + kBody + 2 * kKG * kTStages * 8;
+};
+
+// Address of the 16-byte segment (key, d..d+7) inside a 128B-swizzled chunk
+// whose two 64-column boxes start at box0 and box0 + kBoxBytes.
+__device__ __forceinline__ uint32_t sw128_addr(uint32_t box0, int key, int d) {
+  return box0 + (d >> 6) * kBoxBytes + key * 128 + ((((d & 63) >> 3) ^ (key & 7)) << 4);
+}
+
+template <int MT>
+__global__ void __launch_bounds__(128 * MT, 2)
+    attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                    const AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(base + TmaSmem<MT>::kBarOffset);
+  uint64_t* empty = full + kKG * kTStages;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int mt = warp / kKG, kg = warp % kKG;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kKG * kTStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], MT);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+  }
+  __syncthreads();
   pdl_wait();
   pdl_trigger();
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  __nv_bfloat16* buf = reinterpret_cast<__nv_bfloat16*>(smem_raw) + warp * kWarpBufElems;
   const int tile = blockIdx.x, g = blockIdx.y;
   const int b = a.tile_seq[tile];
   const int row0 = a.tile_row0[tile];
@@ -343,41 +391,80 @@ __global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
   const int bidir = a.mode[b];
   const int rows = qlen * a.G;
   WarpState st;
-  load_q(a, st, q0, rows, row0, g, qlen, kvlen, lane);
-  const int last_row = min(rows - 1, row0 + 15);
+  load_q(a, st, q0, rows, row0 + mt * 16, g, qlen, kvlen, lane);
+  const int last_row = min(rows - 1, row0 + 16 * MT - 1);
   const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
-  const int nchunks = (max_key + kChunk - 1) / kChunk;
+  const int nchunks = (max(max_key, 0) + kCh - 1) / kCh;
+  const int mine = nchunks > kg ? (nchunks - kg + kKG - 1) / kKG : 0;
   const int* tbl = a.table + static_cast<long long>(b) * a.table_stride;
-  auto kbuf = [&](int s) { return buf + s * kStageElems; };
-  auto vbuf = [&](int s) { return buf + s * kStageElems + kChunk * kStride; };
-  auto issue = [&](int c, int s) {
-    const int key0 = c * kChunk;
-    load_chunk<kChunk>(a, tbl[key0 / kPage], g, key0 % kPage, min(kChunk, kvlen - key0), kbuf(s), vbuf(s), lane);
+  uint8_t* gbase = base + kg * kGroupBytes;
+  uint64_t* gfull = full + kg * kTStages;
+  uint64_t* gempty = empty + kg * kTStages;
+  const bool producer = mt == 0 && lane == 0;
+  auto issue = [&](int i) {
+    const int key0 = (kg + kKG * i) * kCh;
+    const int y = (tbl[key0 / kPage] * a.Hkv + g) * kPage + key0 % kPage;
+    const int s = i % kTStages;
+    uint8_t* dst = gbase + s * kChunkBytes;
+    mbar_arrive_expect_tx(&gfull[s], kChunkBytes);
+    tma_load_2d(dst, &kmap, 0, y, &gfull[s]);
+    tma_load_2d(dst + kBoxBytes, &kmap, 64, y, &gfull[s]);
+    tma_load_2d(dst + 2 * kBoxBytes, &vmap, 0, y, &gfull[s]);
+    tma_load_2d(dst + 3 * kBoxBytes, &vmap, 64, y, &gfull[s]);
   };
-  // prologue: up to kStages - 1 chunks of this warp in flight
-  int next = warp;
-#pragma unroll
-  for (int i = 0; i < kStages - 1; ++i) {
-    if (next < nchunks) issue(next, i);
-    cp_async_commit();
-    next += 4;
-  }
-  int it = 0;
-  for (int c = warp; c < nchunks; c += 4, ++it) {
-    if (next < nchunks) issue(next, (it + kStages - 1) % kStages);
-    cp_async_commit();
-    next += 4;
-    cp_async_wait<kStages - 1>();
+  int issued = 0;
+  if (producer)
+    for (; issued < min(mine, kTStages); ++issued) issue(issued);
+  bool ok = true;
+  int consumed = 0;
+  for (int i = 0; i < mine; ++i) {
+    const int s = i % kTStages;
+    const uint32_t ph = (i / kTStages) & 1;
+    if (!mbar_wait(&gfull[s], ph, a.status, kErrMmaWait)) {
+      ok = false;
+      break;
+    }
+    consumed = i + 1;
+    const int key0 = (kg + kKG * i) * kCh;
+    const uint32_t kb = smem_u32(gbase + s * kChunkBytes);
+    const uint32_t vb = kb + 2 * kBoxBytes;
+    if (kvlen - key0 < kCh) {
+      // Rows past the sequence end hold whatever the page held before; their
+      // probabilities are exactly zero, but 0 * (non-finite V) is not, so zero them.
+      if (mt == 0) {
+        const int valid = kvlen - key0;
+        uint8_t* v = gbase + s * kChunkBytes + 2 * kBoxBytes;
+        for (int c = lane; c < 2 * kCh * 8; c += 32) {
+          const int box = c / (kCh * 8), row = (c / 8) % kCh, seg = c % 8;
+          if (row >= valid) *reinterpret_cast<uint4*>(v + box * kBoxBytes + row * 128 + seg * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      if (MT > 1) named_barrier(1 + kg, 32 * MT);
+      else __syncwarp();
+    }
+    process_keys<kCh>(
+        a, st, [kb](int key, int d) { return sw128_addr(kb, key, d); },
+        [vb](int key, int d) { return sw128_addr(vb, key, d); }, key0, kvlen, bidir, lane);
     __syncwarp();
-    process_page<kChunk>(a, st, kbuf(it % kStages), vbuf(it % kStages), c * kChunk, kvlen, bidir, lane);
-    __syncwarp();
+    if (lane == 0) mbar_arrive(&gempty[s]);
+    if (producer && issued < mine) {
+      if (!mbar_wait(&gempty[s], ph, a.status, kErrTmaWait)) {
+        ok = false;
+        break;
+      }
+      issue(issued);
+      ++issued;
+    }
   }
-  cp_async_wait<0>();
+  if (!ok && producer) {
+    // Drain this group's copies still in flight before the CTA can exit.
+    for (int i = consumed; i < issued; ++i) mbar_wait(&gfull[i % kTStages], (i / kTStages) & 1, a.status, kErrMmaWait);
+  }
   __syncthreads();
-  // Merge: per warp 16 x 128 fp32 partial outputs plus (m, l) per row.
-  float* so = reinterpret_cast<float*>(smem_raw);           // [4][16][128]
-  float* sm = so + 4 * 16 * kD;                              // [4][16]
-  float* sl = sm + 4 * 16;                                   // [4][16]
+  // Merge the key groups of each m-tile: per warp 16 x 128 fp32 partial outputs plus (m, l).
+  float* so = reinterpret_cast<float*>(base);            // [4 * MT][16][kD]
+  float* sm = so + 4 * MT * 16 * kD;                      // [4 * MT][16]
+  float* sl = sm + 4 * MT * 16;                           // [4 * MT][16]
   {
     const int r_lo = lane / 4, c2 = (lane % 4) * 2;
 #pragma unroll
@@ -395,18 +482,20 @@ __global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
     }
   }
   __syncthreads();
-  const int r = threadIdx.x / 8;          // 16 rows
-  const int cbeg = (threadIdx.x % 8) * 16;  // 16 columns each
+  const int r = threadIdx.x / 8;             // 16 * MT rows
+  const int cbeg = (threadIdx.x % 8) * 16;   // 16 columns each
+  const int tm = r / 16, rr = r % 16;
   const int row = row0 + r;
   if (row < rows) {
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm[w * 16 + r]);
-    float wgt[4], L = 0.0f;
+    for (int k = 0; k < kKG; ++k) M = fmaxf(M, sm[(tm * kKG + k) * 16 + rr]);
+    float wgt[kKG], L = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
-      wgt[w] = (M == -INFINITY || sm[w * 16 + r] == -INFINITY) ? 0.0f : exp2f(sm[w * 16 + r] - M);
-      L += wgt[w] * sl[w * 16 + r];
+    for (int k = 0; k < kKG; ++k) {
+      const float mk = sm[(tm * kKG + k) * 16 + rr];
+      wgt[k] = (M == -INFINITY || mk == -INFINITY) ? 0.0f : exp2f(mk - M);
+      L += wgt[k] * sl[(tm * kKG + k) * 16 + rr];
     }
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
     const int tok = row / a.G, head = g * a.G + row % a.G;
@@ -415,13 +504,44 @@ __global__ void __launch_bounds__(128) attn_keys_kernel(const AttnArgs a) {
     for (int c = 0; c < 16; c += 2) {
       float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        v0 += wgt[w] * so[(w * 16 + r) * kD + cbeg + c];
-        v1 += wgt[w] * so[(w * 16 + r) * kD + cbeg + c + 1];
+      for (int k = 0; k < kKG; ++k) {
+        v0 += wgt[k] * so[((tm * kKG + k) * 16 + rr) * kD + cbeg + c];
+        v1 += wgt[k] * so[((tm * kKG + k) * 16 + rr) * kD + cbeg + c + 1];
       }
       *reinterpret_cast<uint32_t*>(p + cbeg + c) = pack_bf16(v0 * inv, v1 * inv);
     }
   }
+}
+
+// 2-D view [pages * Hkv * P rows, D columns] of one cache, 16-key x 64-column boxes.
+bool make_cache_map(CUtensorMap* map, const void* ptr, long long rows) {
+  EncodeTiledFn fn = tensor_map_encoder();
+  if (!fn || rows <= 0 || (reinterpret_cast<uintptr_t>(ptr) % 16)) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kCh)};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MT>
+cudaError_t launch_tma(const AttentionProblem& p, const AttnArgs& a, dim3 grid, cudaStream_t stream) {
+  CUtensorMap km, vm;
+  const long long rows = static_cast<long long>(p.cache_pages) * p.Hkv * kPage;
+  if (!make_cache_map(&km, p.k_cache, rows) || !make_cache_map(&vm, p.v_cache, rows)) return cudaErrorInvalidValue;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tma_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         TmaSmem<MT>::kTotal);
+    if (e != cudaSuccess) return e;
+    cudaFuncSetAttribute(attn_tma_kernel<MT>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    attr[dev] = true;
+  }
+  return launch_pdl(attn_tma_kernel<MT>, grid, dim3(128 * MT), TmaSmem<MT>::kTotal, stream, km, vm, a);
 }
 
 }  // namespace
@@ -451,16 +571,9 @@ cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream) {
   if (p.tile_rows == 64) {
     return launch_pdl(attn_rows_kernel, grid, dim3(128), 0, stream, a);
   } else if (p.tile_rows == 16) {
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 64 && !attr[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(attn_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kKeysSmemBytes);
-      if (e != cudaSuccess) return e;
-      attr[dev] = true;
-    }
-    return launch_pdl(attn_keys_kernel, grid, dim3(128), kKeysSmemBytes, stream, a);
+    return launch_tma<1>(p, a, grid, stream);
+  } else if (p.tile_rows == 32) {
+    return launch_tma<2>(p, a, grid, stream);
   } else {
     return cudaErrorInvalidValue;
   }

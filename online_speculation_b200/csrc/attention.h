@@ -18,9 +18,10 @@ struct AttentionProblem {
   const int* tile_seq;           // [num_tiles]
   const int* tile_row0;          // [num_tiles]
   int num_tiles;
-  int tile_rows;                 // 64 (rows split across warps) or 16 (keys split across warps)
+  int tile_rows;                 // 64 (rows split across warps) or 16 / 32 (keys split across warps)
   __nv_bfloat16* out;            // [T, Hq, D]
   int Hq, Hkv, head_dim, page_size;
+  int cache_pages;               // pages in k_cache / v_cache
   float scale;
   int* status;
 };

@@ -128,6 +128,7 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_
   p.Hkv = k_cache.size(1);
   p.head_dim = q.size(2);
   p.page_size = k_cache.size(2);
+  p.cache_pages = k_cache.size(0);
   p.scale = static_cast<float>(scale);
   p.status = status.data_ptr<int>();
   check(osb::attention_launch(p, at::cuda::getCurrentCUDAStream()), "paged attention");

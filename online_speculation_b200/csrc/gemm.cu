@@ -537,22 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host ----
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
+EncodeTiledFn encode_fn() { return tensor_map_encoder(); }
 
 bool make_map(CUtensorMap* map, const void* ptr, int rows, int cols, long long ld, int box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -687,6 +672,19 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
 
 }  // namespace
 
+EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
 // Off by default: measured on B200 decode steps (28 layers, 8-64 rows) the
 // whole step ran about 6% slower with it, although chains of GEMMs alone ran
 // faster.  OSB_PDL=1 (or set_pdl) enables it.
@@ -791,7 +789,23 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
         (p.group_bn != 32 && p.group_bn != 64 && p.group_bn != 128 && p.group_bn != 256))
       return cudaErrorInvalidValue;
   }
-  const int bn = p.group_tiles != nullptr ? p.group_bn : gemm_pick_bn(p.N);
+  int bn = p.group_tiles != nullptr ? p.group_bn : gemm_pick_bn(p.N);
+  static const int bn_cap = [] {
+    const char* v = getenv("OSB_GEMM_BN_CAP");   // tuning experiments: largest token tile allowed
+    return v ? atoi(v) : 0;
+  }();
+  // Few weight-row tiles and a short reduction: 128-token tiles double the CTAs
+  // that stream weights and still split K over a cluster pair (measured on B200
+  // at 256 tokens: 7B qkv 22.9 -> 18.5 us, 1.5B qkv 14.7 -> 11.5 us, 1.5B down
+  // 23.1 -> 20.1 us; the 7B down projection, K = 18944, is faster with 256).
+  if (p.group_tiles == nullptr && bn == 256 && p.K <= 10240 && (p.M + kBM - 1) / kBM < 64) bn = 128;
+  if (p.group_tiles == nullptr && bn_cap >= 32 && bn > bn_cap) bn = bn_cap;
+  static const int split_mode = [] {
+    const char* v = getenv("OSB_GEMM_SPLIT_MODE");   // tuning experiments: 0 cluster, 1 workspace
+    return v ? atoi(v) : -1;
+  }();
+  GemmProblem q = p;
+  if (split_mode >= 0) q.split_mode = split_mode;
   a.tiles_m = (p.M + kBM - 1) / kBM;
   a.tiles_n = (p.N + bn - 1) / bn;
   a.out = p.out;
@@ -815,10 +829,10 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
     a.vec_ok = out_ok && res_ok;
   }
   switch (bn) {
-    case 32: return launch_bn<32>(p, a, stream);
-    case 64: return launch_bn<64>(p, a, stream);
-    case 128: return launch_bn<128>(p, a, stream);
-    default: return launch_bn<256>(p, a, stream);
+    case 32: return launch_bn<32>(q, a, stream);
+    case 64: return launch_bn<64>(q, a, stream);
+    case 128: return launch_bn<128>(q, a, stream);
+    default: return launch_bn<256>(q, a, stream);
   }
 }
 

@@ -474,10 +474,27 @@ class EngineBackend:
             self.stats["score_calls"] += 1
         return out
 
+    def next_token_probabilities(self, prefix: Sequence[int], block: Sequence[int] = ()) -> np.ndarray:
+        """Temperature-1 next-token distributions after ``prefix + block[:i]`` for i = 0..len(block).
+
+        One forward over the uncached part of ``prefix + block`` (the prefix
+        cache supplies the rest); returns float64 [len(block) + 1, V] on the host.
+        """
+        with self._lock:
+            rows: list[torch.Tensor] = []
+            self._score_one(self._model_prefix(tuple(prefix)), tuple(block), None, logits_out=rows)
+            logits = torch.cat(rows).double()
+            return torch.softmax(logits, dim=-1).numpy()
+
     def _score_one(self, prefix: tuple, cont: tuple, sampling: SamplingConfig | None,
-                   stats_topk: int | None = None) -> tuple:
-        """Per-token log-probabilities of ``cont`` (or, with ``stats_topk``, per-token statistics rows)."""
-        if not cont:
+                   stats_topk: int | None = None, logits_out: list | None = None) -> tuple:
+        """Per-token log-probabilities of ``cont`` (or, with ``stats_topk``, per-token statistics rows).
+
+        With ``logits_out`` the fp32 logits rows of every position from the last
+        prefix token to the last token of ``cont`` (len(cont) + 1 rows) are
+        appended to it (on the host) instead.
+        """
+        if not cont and logits_out is None:
             return ()
         r = self.runner
         G = r.q_slots // r.kv_slots
@@ -495,7 +512,7 @@ class EngineBackend:
             pages, _ = self.prefix.lookup(full, first_row)
             seq = self.cache.manager.adopt(pages, len(pages) * PAGE) if pages else self.cache.create()
             start = self.cache.length(seq)
-        end = len(full) - 1
+        end = len(full) - 1 + (1 if logits_out is not None else 0)
         pos0 = start
         while pos0 < end:
             n = min(end - pos0, r.max_logit_rows, self.prefill_tokens)
@@ -507,7 +524,9 @@ class EngineBackend:
             meta = build_meta(r.device, table, list(full[pos0:pos0 + n]), list(range(pos0, pos0 + n)), slots, [n],
                               [pos0 + n], [0], G, logit_rows=rows if rows else None,
                               tile_rows=64 if n * G > 64 else None)
-            if rows:
+            if rows and logits_out is not None:
+                logits_out.append(r.forward(meta).float().cpu())
+            elif rows:
                 logits = r.forward(meta)
                 targets = torch.tensor([full[p + 1] for p in range(lo, pos0 + n)], dtype=torch.int32,
                                        device=r.device)

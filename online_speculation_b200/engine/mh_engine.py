@@ -115,12 +115,13 @@ class _RoundGraph:
         mk = lambda v: torch.full((B,), v, dtype=torch.int32, device=dev)
         starts = torch.arange(0, B * Kb, Kb, dtype=torch.int32, device=dev)
         G = engine.runner.q_slots // engine.runner.kv_slots
-        tiles_per = -(-(Kb * G) // 16)
+        tr = 16 if Kb * G <= 16 else 32     # one tile holds all query rows of a block when they fit
+        tiles_per = -(-(Kb * G) // tr)
         tile_seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles_per)
-        tile_row0 = (torch.arange(tiles_per, dtype=torch.int32, device=dev) * 16).repeat(B)
+        tile_row0 = (torch.arange(tiles_per, dtype=torch.int32, device=dev) * tr).repeat(B)
         kv_len = self.views["kv_len"]
-        self.plan_draft = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(1), tile_seq, tile_row0, 16, {})
-        self.plan_verify = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(0), tile_seq, tile_row0, 16, {})
+        self.plan_draft = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(1), tile_seq, tile_row0, tr, {})
+        self.plan_verify = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(0), tile_seq, tile_row0, tr, {})
         self.ids_draft = torch.full((B, Kb), engine.head.mask_token_id, dtype=torch.int32, device=dev)
         self.ids_verify = torch.zeros(B, Kb, dtype=torch.int32, device=dev)
         rows = torch.arange(B * Kb, device=dev).view(B, Kb)[:, : Kb - 1].reshape(-1)

@@ -215,7 +215,8 @@ def plan_attention(table, q_lens, kv_lens, modes, group, device, *, tile_rows=No
         q_start.append(acc)
         acc += n
     if tile_rows is None:
-        tile_rows = 16 if max(n * group for n in q_lens) <= 64 else 64
+        most = max(n * group for n in q_lens)
+        tile_rows = 16 if most <= 16 else 32 if most <= 64 else 64
     tile_seq, tile_row0 = [], []
     for b, n in enumerate(q_lens):
         rows = n * group

@@ -3,7 +3,7 @@
     python -m online_speculation_b200.utils.kernel_probe gemm M N K [--swiglu] [--residual]
     python -m online_speculation_b200.utils.kernel_probe grouped E M K ROWS [--swiglu]
     python -m online_speculation_b200.utils.kernel_probe moe T [--preset llada-moe-7b-a1b]
-    python -m online_speculation_b200.utils.kernel_probe attention B CTX [--heads 28 --kv-heads 4]
+    python -m online_speculation_b200.utils.kernel_probe attention B CTX [--heads 28 --kv-heads 4 --qlen 4]
     python -m online_speculation_b200.utils.kernel_probe sample ROWS V
 
 Each subcommand builds inputs larger than L2 where the problem allows (weights
@@ -93,6 +93,7 @@ def main(argv=None) -> int:
     at.add_argument("ctx", type=int)
     at.add_argument("--heads", type=int, default=28)
     at.add_argument("--kv-heads", type=int, default=4)
+    at.add_argument("--qlen", type=int, default=1, help="query tokens per sequence (a causal block at the end)")
     sa = sub.add_parser("sample")
     sa.add_argument("rows", type=int)
     sa.add_argument("V", type=int)
@@ -167,15 +168,16 @@ def main(argv=None) -> int:
         kc = torch.randn(B * pps, hkv, 32, 128, device=dev).bfloat16()
         vc = torch.randn_like(kc)
         table = (torch.arange(B, dtype=torch.int32)[:, None] * pps + torch.arange(pps, dtype=torch.int32)[None])
-        plan = K.plan_attention(table, [1] * B, [ctx] * B, [0] * B, hq // hkv, dev)
-        q = torch.randn(B, hq, 128, device=dev).bfloat16()
+        plan = K.plan_attention(table, [a.qlen] * B, [ctx] * B, [0] * B, hq // hkv, dev)
+        q = torch.randn(B * a.qlen, hq, 128, device=dev).bfloat16()
         o = torch.empty_like(q)
 
         def body():
             K.attention(q, kc, vc, plan, out=o)
         us = _time(body, a.iters, a.warmup, graph)
         bytes_ = 2 * B * ctx * hkv * 128 * 2
-        out.update(B=B, ctx=ctx, us=us, gbs=bytes_ / us / 1e3)
+        flops = 4 * B * a.qlen * hq * ctx * 128
+        out.update(B=B, ctx=ctx, qlen=a.qlen, us=us, gbs=bytes_ / us / 1e3, attn_tflops=flops / us / 1e6)
     else:
         logits = torch.randn(a.rows, a.V, device=dev)
         it = torch.ones(a.rows, device=dev)

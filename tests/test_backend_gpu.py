@@ -87,3 +87,32 @@ def test_conditional_is_and_mh_on_engine(backend):
                                SamplingConfig(temperature=0.5), [SeedStream(3)] * 4, chain_ids=[0, 1, 2, 3])
     assert all(len(c.token_ids) == 16 and c.attempts == 3 for c in mh)
     workspace.check_status()
+
+
+def test_next_token_probabilities_match_oracle_and_drive_draft_speculation(backend, oracle):
+    from online_speculation_b200.arllm.acceleration import DraftModelSpeculationConfig
+    from online_speculation_b200.experimental.arllm.draft_model_speculation import DraftModelSpeculativeBackend
+
+    prefix, block = tuple(range(7, 37)), (5, 9, 11)
+    probs = backend.next_token_probabilities(prefix, block)
+    assert probs.shape == (len(block) + 1, CFG.vocab_size)
+    logits = reference_forward(CFG, oracle, torch.tensor(list(prefix) + list(block)))[len(prefix) - 1:]
+    ref = logits.double().softmax(-1).numpy()
+    assert abs(probs - ref).sum(-1).max() < 0.05           # per-row L1 (bf16 activations vs fp32)
+    # a second, smaller model drafts for the first; outputs follow the target policy
+    small = DecoderConfig(vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=1,
+                          num_attention_heads=4, num_key_value_heads=2, name="draft-small")
+    draft = EngineBackend(build_runner(small, seed=3, kv_bytes=64 << 20, max_tokens=1024), max_batch=4,
+                          max_seq_tokens=256)
+    try:
+        spec = DraftModelSpeculativeBackend(backend, draft, config=DraftModelSpeculationConfig(
+            draft_tokens=3, single_request_only=False))
+        reqs = [GenerationRequest(prefix, 8, SamplingConfig(), seed=i, request_id=f"s{i}") for i in range(2)]
+        for req, smp in zip(reqs, spec.sample_batch(reqs)):
+            assert len(smp.token_ids) == 8
+            lp, _ = _oracle_logprobs(oracle, req.prefix, smp.token_ids, 1.0)
+            assert float((torch.tensor(smp.token_logprobs) - lp).abs().max()) < 0.2
+        assert spec.snapshot().verification_rounds >= 2
+    finally:
+        draft.close()
+    workspace.check_status()

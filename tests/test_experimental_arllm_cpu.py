@@ -123,3 +123,51 @@ def test_dynamic_is_with_a_defensive_auxiliary_mixture():
     assert sum(r.reserve_records_written for r in runs) > 0
     with pytest.raises(ValueError):
         run_dynamic_is(b, BehaviorRegistry(), InMemoryReplayStore(), (4,), cfg, _zeros, "v1", SeedStream(0))
+
+
+def _context_model(seed, V=4):
+    rng = np.random.default_rng(seed)
+    table = {}
+
+    def row(prefix):
+        k = tuple(prefix[-2:])
+        if k not in table:
+            table[k] = rng.dirichlet(np.ones(V) * 0.7)
+        return table[k]
+    return TabularBackend(row, V, model_id=f"ctx{seed}")
+
+
+@pytest.mark.parametrize("temperature", [1.0, 0.7])
+def test_draft_model_speculation_is_exact(temperature):
+    import itertools
+
+    from online_speculation_b200.arllm.acceleration import DraftModelSpeculationConfig
+    from online_speculation_b200.arllm.types import GenerationRequest
+    from online_speculation_b200.experimental.arllm.draft_model_speculation import DraftModelSpeculativeBackend
+
+    target, draft = _context_model(1), _context_model(2)
+    spec = DraftModelSpeculativeBackend(target, draft, config=DraftModelSpeculationConfig(draft_tokens=2,
+                                                                                           single_request_only=False))
+    pol = SamplingConfig(temperature=temperature)
+    Lq = 3
+    reqs = [GenerationRequest((1,), Lq, pol, seed=s, request_id=f"r{s}") for s in range(6000)]
+    out = spec.sample_batch(reqs)
+    emp = {}
+    for s in out:
+        emp[s.token_ids] = emp.get(s.token_ids, 0) + 1
+        assert len(s.token_ids) == Lq
+    exact = {}
+    for seq in itertools.product(range(4), repeat=Lq):
+        p = 1.0
+        for i in range(Lq):
+            p *= target.probabilities((1,) + seq[:i], pol)[seq[i]]
+        exact[seq] = p
+    tv = 0.5 * sum(abs(emp.get(k, 0) / len(out) - v) for k, v in exact.items())
+    assert tv < 0.04
+    # returned log-probabilities are the target's
+    s = out[0]
+    want = [float(np.log(target.probabilities((1,) + s.token_ids[:i], pol)[t])) for i, t in enumerate(s.token_ids)]
+    assert s.token_logprobs == pytest.approx(want)
+    snap = spec.snapshot()
+    assert 0 < snap.draft_tokens_accepted <= snap.draft_tokens_proposed
+    assert snap.mean_tokens_per_round > 1.0

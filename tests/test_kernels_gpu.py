@@ -97,12 +97,33 @@ def test_attention_matches_fp32(cuda, q_lens, kv_lens, modes, Hq, Hkv):
     table, kc, vc = _paged_case(cuda, kv_lens, Hkv, pps)
     T = sum(q_lens)
     q = torch.randn(T, Hq, 128, device=cuda).bfloat16()
-    for tile_rows in (16, 64):
+    for tile_rows in (16, 32, 64):
         plan = ops.plan_attention(table, q_lens, kv_lens, modes, Hq // Hkv, cuda, tile_rows=tile_rows)
         out = ops.attention(q, kc, vc, plan)
         ref = ops.attention_reference(q.cpu(), kc.cpu(), vc.cpu(), plan.host, 128 ** -0.5)
         torch.cuda.synchronize()
         assert _rel(out.cpu(), ref) < 2e-2, tile_rows
+
+
+@pytest.mark.parametrize("tile_rows", [16, 32])
+def test_attention_ignores_non_finite_rows_past_the_end(cuda, tile_rows):
+    # cache rows past a sequence's end may hold anything (recycled or never-written pages)
+    kv_lens = [37, 70, 5]
+    table, kc, vc = _paged_case(cuda, kv_lens, 4, 3, seed=3)
+    for b, n in enumerate(kv_lens):
+        for key in range(n, 96):
+            page = int(table[b, key // 32])
+            kc[page, :, key % 32] = float("nan")
+            vc[page, :, key % 32] = float("inf")
+    q_lens = [4, 4, 1]
+    q = torch.randn(sum(q_lens), 28, 128, device=cuda).bfloat16()
+    plan = ops.plan_attention(table, q_lens, kv_lens, [0, 1, 0], 7, cuda, tile_rows=tile_rows)
+    out = ops.attention(q, kc, vc, plan)
+    ref = ops.attention_reference(q.cpu(), torch.nan_to_num(kc.cpu()), torch.nan_to_num(vc.cpu()), plan.host,
+                                  128 ** -0.5)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert _rel(out.cpu(), ref) < 2e-2
 
 
 def test_rmsnorm_and_fused_add(cuda):
