@@ -201,7 +201,7 @@ void page_copy(Tensor cache, Tensor pairs) {
 }
 
 void sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor uniforms, Tensor tokens, c10::optional<Tensor> logq,
-            c10::optional<Tensor> logp) {
+            c10::optional<Tensor> logp, c10::optional<Tensor> arith, c10::optional<Tensor> next_uniforms) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
   CHECK_DT(logits, torch::kFloat32);
@@ -218,6 +218,13 @@ void sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor uniforms, Tens
   a.tokens = tokens.data_ptr<int>();
   a.logq = ptr_or_null<float>(logq);
   a.logp = ptr_or_null<float>(logp);
+  a.arith = ptr_or_null<const int>(arith);
+  if (next_uniforms.has_value() && next_uniforms->defined()) {
+    CHECK_DT(*next_uniforms, torch::kFloat64);
+    TORCH_CHECK((next_uniforms->dim() == 2 ? next_uniforms->stride(0) : 1) == a.uniform_stride,
+                "next_uniforms must have the stride of uniforms");
+    a.next_uniforms = next_uniforms->data_ptr<double>();
+  }
   check(osb::sample_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "sample");
 }
 

@@ -203,12 +203,29 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     atomicMin(&chosen, tok);
   }
   __syncthreads();
+  __shared__ double code_lo, code_mass;
+  if (a.arith != nullptr && a.next_uniforms != nullptr && a.arith[r]) {
+    // the owner of the chosen token recomputes its cumulative interval
+    const int tok = chosen;
+    if (b0 <= tok && tok < b1) {
+      double c = excl;
+      for (int v = b0; v < tok; ++v) c += static_cast<double>(expf(row[v] * invT - zoff));
+      code_lo = c;
+      code_mass = static_cast<double>(expf(row[tok] * invT - zoff));
+    }
+    __syncthreads();
+  }
   if (threadIdx.x == 0) {
     const int tok = chosen;
     a.tokens[r] = tok;
     const float l = row[tok];
     if (a.logq) a.logq[r] = l * invT - lseT;
     if (a.logp) a.logp[r] = l - lse1;
+    if (a.arith != nullptr && a.next_uniforms != nullptr && a.arith[r]) {
+      double nu = code_mass > 0.0 ? (u - code_lo) / code_mass : 0.5;
+      nu = fmin(fmax(nu, 0.0), 0.99999999999999989);   // largest double below one
+      a.next_uniforms[r * a.uniform_stride] = nu;
+    }
   }
 }
 

@@ -14,6 +14,11 @@ struct SampleArgs {
   int* tokens;                // [rows]
   float* logq;                // [rows] policy log-prob or null
   float* logp;                // [rows] T=1 log-prob or null
+  // Arithmetic-coding rows (arith[r] != 0): the uniform u of the row is a code
+  // point; after drawing token t with cumulative mass [c, c + q_t) it writes
+  // the rescaled point (u - c) / q_t to next_uniforms[r * uniform_stride].
+  const int* arith;           // [rows] or null
+  double* next_uniforms;      // or null
 };
 
 struct RowStatsArgs {

@@ -10,7 +10,11 @@ the same contract (:mod:`online_speculation_b200.arllm.types`):
   uniforms come from ``np.random.default_rng(seed).random(max_new_tokens)``
   (or the request's explicit ``uniforms``) and tokens are drawn by inverse CDF
   over a float64 prefix sum, exactly as the reference draws them, so a
-  request's tokens do not depend on what it is batched with.
+  request's tokens do not depend on what it is batched with.  A request with
+  an ``arithmetic_uniform`` is decoded by arithmetic coding: the sampler
+  rescales the code point on the device after every token (cumulative mass in
+  vocabulary order), so the whole sequence is a deterministic function of one
+  uniform.
 * ``score_batch`` scores continuations with the fused row-statistics kernel
   (log-sum-exp at T = 1 and at the requested temperature plus the target
   gather), never materialising a log-softmax.
@@ -125,6 +129,7 @@ class _Active:
     logq: list
     logp: list
     finish: str = "length"
+    carry: float | None = None     # arithmetic-coding code point for the next token
 
 
 class _DecodeGraph:
@@ -154,7 +159,11 @@ class _DecodeGraph:
         self.pos, self.slots, self.kv = (d[o[k]:o[k + 1]].view(S, B) for k in (1, 2, 3))
         self.table = d[o[4]:o[5]].view(B, self.mp)
         self.uni_host = torch.zeros(S, B, dtype=torch.float64).pin_memory()
-        self.uni = torch.zeros(S, B, dtype=torch.float64, device=dev)
+        # row S receives the code point after the last step of arithmetic-coding rows
+        self.uni = torch.zeros(S + 1, B, dtype=torch.float64, device=dev)
+        self.arith_host = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.arith = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.carry_host = torch.zeros(B, dtype=torch.float64).pin_memory()
         self.it_host = torch.ones(B, dtype=torch.float32).pin_memory()
         self.inv_temp = torch.ones(B, dtype=torch.float32, device=dev)
         G = r.q_slots // r.kv_slots
@@ -196,14 +205,15 @@ class _DecodeGraph:
         for s in range(self.S):
             logits = r.forward(StepMeta(self.ids[s], self.pos[s], self.slots[s], self.plans[s], None))
             K.sample(logits, self.inv_temp, self.uni[s], tokens=self.ids[s + 1], logq=self.logq[s],
-                     logp=self.logp[s])
+                     logp=self.logp[s], arith=self.arith, next_uniforms=self.uni[s + 1])
         self.result[:, :, 0].copy_(self.ids[1:])
         self.result[:, :, 1].copy_(self.logq)
         self.result[:, :, 2].copy_(self.logp)
 
     def run(self) -> np.ndarray:
         self.dev.copy_(self.host, non_blocking=True)
-        self.uni.copy_(self.uni_host, non_blocking=True)
+        self.uni[:self.S].copy_(self.uni_host, non_blocking=True)
+        self.arith.copy_(self.arith_host, non_blocking=True)
         self.inv_temp.copy_(self.it_host, non_blocking=True)
         if self.graph is not None:
             self.graph.replay()
@@ -211,6 +221,7 @@ class _DecodeGraph:
         else:
             self._body()
         self.result_host.copy_(self.result, non_blocking=True)
+        self.carry_host.copy_(self.uni[self.S], non_blocking=True)
         torch.cuda.current_stream(self.backend.runner.device).synchronize()
         return self.result_host.numpy()
 
@@ -357,14 +368,18 @@ class EngineBackend:
         opened = []
         for i, req in group:
             self._check_policy(req.sampling)
-            if req.arithmetic_uniform is not None:
-                raise NotImplementedError("arithmetic-coding sampling runs on the CPU tabular backend")
             tokens = self._model_prefix(req.prefix)
             seq, tail = self._open(tokens, keep_last=True)
             opened.append((seq, tokens, tail))
-            uni = (np.asarray(req.uniforms, dtype=np.float64) if req.uniforms is not None
-                   else np.random.default_rng(req.seed).random(req.max_new_tokens))
-            act.append(_Active(i, req, seq, tokens[-1], len(tokens) - 1, uni, [], [], []))
+            if req.arithmetic_uniform is not None:
+                # one code point for the whole sequence, rescaled on the device after every token
+                uni = np.full(req.max_new_tokens, np.nan)
+                carry = float(req.arithmetic_uniform)
+            else:
+                uni = (np.asarray(req.uniforms, dtype=np.float64) if req.uniforms is not None
+                       else np.random.default_rng(req.seed).random(req.max_new_tokens))
+                carry = None
+            act.append(_Active(i, req, seq, tokens[-1], len(tokens) - 1, uni, [], [], [], carry=carry))
         self.cache.flush_copies()
         self._prefill(opened)
         for a, (seq, tokens, _) in zip(act, opened):
@@ -383,7 +398,12 @@ class EngineBackend:
                 g.h_pos[:, b] = a.pos + steps
                 g.h_kv[:, b] = a.pos + 1 + steps
                 t = len(a.tokens)
-                g.uni_host[:, b] = torch.from_numpy(np.ascontiguousarray(a.uniforms[t:t + S], dtype=np.float64))
+                if a.carry is not None:
+                    g.uni_host[:, b] = a.carry
+                    g.arith_host[b] = 1
+                else:
+                    g.uni_host[:, b] = torch.from_numpy(np.ascontiguousarray(a.uniforms[t:t + S], dtype=np.float64))
+                    g.arith_host[b] = 0
                 g.it_host[b] = 1.0 / a.request.sampling.temperature
             self.cache.manager.fill_table_np([a.seq for a in act], g.h_table[:n])
             if n < B:
@@ -393,12 +413,15 @@ class EngineBackend:
                 g.h_kv[:, n:] = 1
                 g.h_table[n:] = 0
                 g.uni_host[:, n:] = 0.5
+                g.arith_host[n:] = 0
             res = g.run()
             self.stats["decode_steps"] += S
             still = []
             for b, a in enumerate(act):
                 eos = a.request.sampling.eos_token_id
                 start = a.pos
+                if a.carry is not None:
+                    a.carry = float(g.carry_host[b])
                 for s in range(S):
                     tok = int(res[s, b, 0])
                     a.tokens.append(tok)

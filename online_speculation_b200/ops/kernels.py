@@ -273,10 +273,14 @@ def attention_reference(q, k_cache, v_cache, host, scale):
 
 
 # ---------------------------------------------------------------- sampling --
-def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None):
+def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None, arith=None, next_uniforms=None):
     """Inverse-CDF sampling (float64 prefix sums) at per-row temperature.
 
     Returns (tokens int32, log q under the policy, log p at temperature one).
+    With ``arith`` (int32 per row) and ``next_uniforms``, every flagged row is
+    an arithmetic-coding draw: its uniform is a code point and the rescaled
+    point for the next token, (u - cumulative mass before the token) / mass of
+    the token, is written to ``next_uniforms``.
     """
     rows = logits.shape[0]
     dev = logits.device
@@ -284,25 +288,35 @@ def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None):
     logq = logq if logq is not None else torch.empty(rows, dtype=torch.float32, device=dev)
     logp = logp if logp is not None else torch.empty(rows, dtype=torch.float32, device=dev)
     if logits.is_cuda:
-        _ext.require().sample(logits, inv_temp, uniforms, tokens, logq, logp)
+        _ext.require().sample(logits, inv_temp, uniforms, tokens, logq, logp, arith, next_uniforms)
         return tokens, logq, logp
-    t, q, p = sample_reference(logits, inv_temp, uniforms)
+    t, q, p, nxt = sample_reference(logits, inv_temp, uniforms, with_code=True)
     tokens.copy_(t)
     logq.copy_(q)
     logp.copy_(p)
+    if arith is not None and next_uniforms is not None:
+        flat = next_uniforms.reshape(rows, -1)[:, 0] if next_uniforms.dim() > 1 else next_uniforms
+        flat.copy_(torch.where(arith.bool(), nxt, flat.double()).to(flat.dtype))
     return tokens, logq, logp
 
 
-def sample_reference(logits, inv_temp, uniforms):
+def sample_reference(logits, inv_temp, uniforms, *, with_code=False):
     x = logits.float()
     it = inv_temp.float()[:, None] if inv_temp is not None else torch.ones(x.shape[0], 1, device=x.device)
     log_q = (x * it).log_softmax(-1)
     log_p = x.log_softmax(-1)
-    cumulative = log_q.exp().double().cumsum(-1)
+    mass = log_q.exp().double()
+    cumulative = mass.cumsum(-1)
     cumulative[:, -1] = 1.0
     u = uniforms.reshape(x.shape[0], -1)[:, 0].double()
     tok = (cumulative < u[:, None]).sum(-1).clamp_max(x.shape[1] - 1)
-    return (tok.int(), log_q.gather(-1, tok[:, None]).squeeze(-1), log_p.gather(-1, tok[:, None]).squeeze(-1))
+    out = (tok.int(), log_q.gather(-1, tok[:, None]).squeeze(-1), log_p.gather(-1, tok[:, None]).squeeze(-1))
+    if not with_code:
+        return out
+    m = mass.gather(-1, tok[:, None]).squeeze(-1)
+    lo = cumulative.gather(-1, tok[:, None]).squeeze(-1) - m
+    nxt = ((u - lo) / m.clamp_min(1e-300)).clamp(0.0, 0.99999999999999989)
+    return out + (nxt,)
 
 
 def row_stats(logits, inv_temp=None, targets=None):

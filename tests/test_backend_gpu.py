@@ -116,3 +116,27 @@ def test_next_token_probabilities_match_oracle_and_drive_draft_speculation(backe
     finally:
         draft.close()
     workspace.check_status()
+
+
+def test_arithmetic_coding_requests(backend, oracle):
+    prefix = tuple(range(11, 40))
+    pts = [(i + 0.37) / 64 for i in range(64)]
+    reqs = [GenerationRequest(prefix, 6, SamplingConfig(temperature=1.3), seed=0, request_id=f"a{i}",
+                              arithmetic_uniform=u) for i, u in enumerate(pts)]
+    out = backend.sample_batch(reqs)
+    # deterministic in the code point, whatever the batch
+    again = backend.sample_batch([reqs[5], GenerationRequest(prefix, 3, SamplingConfig(), seed=1, request_id="x")])
+    assert again[0].token_ids == out[5].token_ids
+    # the first token of a lattice of code points follows the policy: point i lands in the token whose
+    # cumulative interval (vocabulary order) contains it
+    logits = reference_forward(CFG, oracle, torch.tensor(list(prefix)))[-1].double() / 1.3
+    cdf = logits.softmax(-1).cumsum(0)
+    want = [int(torch.searchsorted(cdf, torch.tensor(u, dtype=torch.float64))) for u in pts]
+    got = [s.token_ids[0] for s in out]
+    assert sum(a == b for a, b in zip(got, want)) >= 60          # bf16 logits may move a boundary point
+    # code points of later tokens are rescaled, not redrawn: sequences sharing a first token differ later
+    assert len({s.token_ids for s in out}) > len({s.token_ids[0] for s in out})
+    for s in out[:4]:
+        lp, lq = _oracle_logprobs(oracle, prefix, s.token_ids, 1.3)
+        assert float((torch.tensor(s.token_logprobs) - lq).abs().max()) < 0.2
+    workspace.check_status()
