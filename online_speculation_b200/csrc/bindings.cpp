@@ -249,7 +249,8 @@ void row_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tens
 }
 
 void gumbel_sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor seeds, c10::optional<Tensor> seed_index,
-                   c10::optional<Tensor> streams, c10::optional<Tensor> row_in_seq, int64_t salt, Tensor tokens) {
+                   c10::optional<Tensor> streams, c10::optional<Tensor> row_in_seq, int64_t salt, Tensor tokens,
+                   int64_t v_lo, c10::optional<Tensor> keys) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
   CHECK_DT(logits, torch::kFloat32);
@@ -266,13 +267,21 @@ void gumbel_sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor seeds, 
   a.row_in_seq = ptr_or_null<const int>(row_in_seq);
   a.salt = static_cast<int>(salt);
   a.tokens = tokens.data_ptr<int>();
+  TORCH_CHECK(v_lo % 4 == 0, "vocabulary shards must start at a multiple of 4");
+  a.v_lo = static_cast<int>(v_lo);
+  if (keys.has_value() && keys->defined()) {
+    CHECK_DT(*keys, torch::kInt64);
+    TORCH_CHECK(keys->numel() == logits.size(0), "one key per row");
+    a.keys = reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>());
+  }
   check(osb::gumbel_sample_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "gumbel_sample");
 }
 
 void spec_verify(Tensor target, Tensor draft, Tensor candidates, int64_t n, c10::optional<Tensor> inv_temp, Tensor seeds,
                  c10::optional<Tensor> streams, int64_t salt, Tensor count, Tensor tail, Tensor valid, Tensor emitted,
                  Tensor logq, Tensor logp, c10::optional<Tensor> lseT_target, c10::optional<Tensor> lse1_target,
-                 c10::optional<Tensor> lseT_draft) {
+                 c10::optional<Tensor> lseT_draft, int64_t v_lo, int64_t V_total, c10::optional<Tensor> cand_logits,
+                 c10::optional<Tensor> keys) {
   CHECK_CUDA(target);
   CHECK_ROWS(target);
   CHECK_ROWS(draft);
@@ -307,6 +316,16 @@ void spec_verify(Tensor target, Tensor draft, Tensor candidates, int64_t n, c10:
   TORCH_CHECK((a.lseT_target == nullptr) == (a.lse1_target == nullptr) &&
                   (a.lseT_target == nullptr) == (a.lseT_draft == nullptr),
               "precomputed statistics come together");
+  TORCH_CHECK(v_lo % 4 == 0, "vocabulary shards must start at a multiple of 4");
+  a.v_lo = static_cast<int>(v_lo);
+  a.V_total = static_cast<int>(V_total);
+  a.cand_logits = ptr_or_null<const float>(cand_logits);
+  if (keys.has_value() && keys->defined()) {
+    CHECK_DT(*keys, torch::kInt64);
+    TORCH_CHECK(keys->numel() == B && a.cand_logits != nullptr, "vocabulary-parallel correction needs keys and "
+                                                                 "candidate logits");
+    a.keys = reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>());
+  }
   check(osb::spec_verify_launch(a, B, at::cuda::getCurrentCUDAStream()), "spec_verify");
 }
 

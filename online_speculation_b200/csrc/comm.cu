@@ -3,8 +3,14 @@
 //
 //   h <- h + sum_r P_r ;  x <- rmsnorm(h) * w
 //
-// Two-shot algorithm over symmetric buffers (every rank can load every other
-// rank's buffers through NVLink / NVSwitch peer mappings):
+// Up to four ranks: one-shot.  After a cross-rank barrier every rank loads the
+// rows of every rank's partial (peer loads), sums them in rank order (so the
+// residual stream stays bitwise identical on all ranks), adds the residual,
+// and applies RMSNorm in the same pass: one kernel, one barrier, and each rank
+// reads (world - 1) x T x H x 2 bytes over NVLink.
+//
+// Eight ranks: two-shot over symmetric buffers (every rank can load every
+// other rank's buffers through NVLink / NVSwitch peer mappings):
 //   kernel A  each rank owns a slice of rows; it loads those rows of every
 //             rank's partial P_r (peer loads), adds the residual, and stores
 //             the reduced rows into its own symmetric row buffer and its
@@ -168,10 +174,140 @@ __global__ void __launch_bounds__(256) gather_norm_kernel(const ArArgs a) {
   }
 }
 
+// Marks this call complete once every block has finished (the next call's epoch).
+__device__ __forceinline__ void finish_call(const ArArgs& a, uint32_t epoch) {
+  __shared__ int last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t done = atomicAdd(a.epoch + 1, 1u);
+    last = done == gridDim.x - 1;
+    if (last) {
+      a.epoch[1] = 0;
+      __threadfence();
+      a.epoch[0] = epoch;
+    }
+  }
+}
+
+constexpr int kOneShotThreads = 256;
+constexpr int kOneShotRegVecs = 4;   // rows up to 256 * 4 * 8 = 8192 wide stay in registers
+
+__global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArArgs a) {
+  const uint32_t epoch = *a.epoch + 1;
+  const bool ok = rank_barrier(a, 2, epoch);
+  const int nvec = a.H / 8;
+  __shared__ float red[33];
+  if (ok) {
+    for (int row = blockIdx.x; row < a.T; row += gridDim.x) {
+      __nv_bfloat16* hr = a.h + static_cast<long long>(row) * a.ldh;
+      uint4 keep[kOneShotRegVecs];
+      float ss = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kOneShotRegVecs; ++i) {
+        const int v = threadIdx.x + i * kOneShotThreads;
+        if (v < nvec) {
+          uint4 parts[kMaxRanks];
+#pragma unroll
+          for (int q = 0; q < kMaxRanks; ++q)
+            if (q < a.world)
+              parts[q] = __ldcg(reinterpret_cast<const uint4*>(a.parts[q] + static_cast<long long>(row) * a.H + v * 8));
+          const uint4 hv = *reinterpret_cast<const uint4*>(hr + v * 8);
+          const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
+          float acc[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] = bf2f(he[e]);
+#pragma unroll
+          for (int q = 0; q < kMaxRanks; ++q) {
+            if (q < a.world) {
+              const __nv_bfloat16* pe = reinterpret_cast<const __nv_bfloat16*>(&parts[q]);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[e] += bf2f(pe[e]);
+            }
+          }
+          uint4 out;
+          __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ob[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+          *reinterpret_cast<uint4*>(hr + v * 8) = out;
+          keep[i] = out;
+          const __nv_bfloat16* oe = reinterpret_cast<const __nv_bfloat16*>(&out);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float f = bf2f(oe[e]);
+            ss += f * f;
+          }
+        }
+      }
+      // rows wider than the register window: finish them from global memory
+      for (int v = threadIdx.x + kOneShotRegVecs * kOneShotThreads; v < nvec; v += kOneShotThreads) {
+        float acc[8];
+        const uint4 hv = *reinterpret_cast<const uint4*>(hr + v * 8);
+        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = bf2f(he[e]);
+        for (int q = 0; q < a.world; ++q) {
+          const uint4 pv = __ldcg(reinterpret_cast<const uint4*>(a.parts[q] + static_cast<long long>(row) * a.H + v * 8));
+          const __nv_bfloat16* pe = reinterpret_cast<const __nv_bfloat16*>(&pv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += bf2f(pe[e]);
+        }
+        uint4 out;
+        __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ob[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+        *reinterpret_cast<uint4*>(hr + v * 8) = out;
+        const __nv_bfloat16* oe = reinterpret_cast<const __nv_bfloat16*>(&out);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += bf2f(oe[e]) * bf2f(oe[e]);
+      }
+      ss = warp_sum(ss);
+      const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      if (warp == 0) {
+        float t = lane < kOneShotThreads / 32 ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[32] = rsqrtf(t / a.H + a.eps);
+      }
+      __syncthreads();
+      const float rs = red[32];
+      auto emit = [&](int v, const uint4& hv) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.w + v * 8);
+        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+        uint4 out;
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = f2bf(bf2f(we[e]) * bf2f(f2bf(bf2f(he[e]) * rs)));
+        *reinterpret_cast<uint4*>(a.x + static_cast<long long>(row) * a.ldx + v * 8) = out;
+      };
+#pragma unroll
+      for (int i = 0; i < kOneShotRegVecs; ++i) {
+        const int v = threadIdx.x + i * kOneShotThreads;
+        if (v < nvec) emit(v, keep[i]);
+      }
+      for (int v = threadIdx.x + kOneShotRegVecs * kOneShotThreads; v < nvec; v += kOneShotThreads)
+        emit(v, *reinterpret_cast<const uint4*>(hr + v * 8));
+      __syncthreads();
+    }
+  }
+  finish_call(a, epoch);
+}
+
 }  // namespace
 
 cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
   if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
+  static const int oneshot_max = [] {
+    const char* v = getenv("OSB_AR_ONESHOT_MAX");   // tuning experiments: largest world for one-shot
+    return v ? atoi(v) : 4;
+  }();
+  if (a.world <= oneshot_max) {
+    const int grid = blocks < a.T ? blocks : a.T;
+    oneshot_norm_kernel<<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
   const int rows_per_rank = (a.T + a.world - 1) / a.world;
   const int grid_a = blocks < rows_per_rank ? blocks : rows_per_rank;
   reduce_rows_kernel<<<grid_a > 0 ? grid_a : 1, 256, 0, stream>>>(a);

@@ -53,6 +53,18 @@ __device__ __forceinline__ float4 uniform4(unsigned long long seed, uint32_t str
   return make_float4(u01(r.x), u01(r.y), u01(r.z), u01(r.w));
 }
 
+// (score, column) -> 64-bit key whose signed order is (score, then lower column):
+// monotone bit pattern of the float in the high word, complemented column in
+// the low word, top bit flipped so that a signed 64-bit maximum (NCCL MAX on
+// int64) picks the same winner as the unsharded argmax.
+__device__ __forceinline__ unsigned long long pack_argmax_key(float score, int column) {
+  const uint32_t b = __float_as_uint(score);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  const unsigned long long k =
+      (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(column));
+  return k ^ 0x8000000000000000ull;
+}
+
 // ------------------------------------------------------- block reductions ----
 template <typename T>
 __device__ __forceinline__ T warp_reduce_sum(T v) {
@@ -261,8 +273,9 @@ __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
   const uint32_t hi = static_cast<uint32_t>(a.salt) ^ (static_cast<uint32_t>(a.row_in_seq ? a.row_in_seq[r] : 0) << 24);
   float best = -INFINITY;
   int besti = 0x7fffffff;
+  const int g0 = a.v_lo >> 2;   // v_lo is a multiple of 4: groups of four columns keep their noise
   for (int i = threadIdx.x; i * 4 < a.V; i += blockDim.x) {
-    const float4 u = uniform4(seed, stream, hi, static_cast<uint32_t>(i));
+    const float4 u = uniform4(seed, stream, hi, static_cast<uint32_t>(g0 + i));
     const float uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -306,7 +319,10 @@ __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
         besti = oi;
       }
     }
-    if (lane == 0) a.tokens[r] = besti;
+    if (lane == 0) {
+      if (a.keys != nullptr) a.keys[r] = pack_argmax_key(best, a.v_lo + besti);
+      else a.tokens[r] = a.v_lo + besti;
+    }
   }
 }
 
@@ -348,13 +364,17 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
     const float us[4] = {ua.x, ua.y, ua.z, ua.w};
     for (int i = 0; i < n; ++i) {
       const int x = a.candidates[b * n + i];
-      if (x < 0 || x >= a.V) {
+      if (x < 0 || x >= (a.V_total > 0 ? a.V_total : a.V)) {
         valid = 0;
         count = i;
         break;
       }
-      const float lp = a.target[(static_cast<long long>(b) * (n + 1) + i) * a.ld_target + x] * invT - s_lseT[i];
-      const float lq = a.draft[(static_cast<long long>(b) * n + i) * a.ld_draft + x] * invT - s_lseQ[i];
+      const float tl = a.cand_logits ? a.cand_logits[(b * n + i) * 2]
+                                     : a.target[(static_cast<long long>(b) * (n + 1) + i) * a.ld_target + x];
+      const float dl = a.cand_logits ? a.cand_logits[(b * n + i) * 2 + 1]
+                                     : a.draft[(static_cast<long long>(b) * n + i) * a.ld_draft + x];
+      const float lp = tl * invT - s_lseT[i];
+      const float lq = dl * invT - s_lseQ[i];
       const float ratio = __expf(fminf(lp - lq, 0.0f));
       const float u = i < 4 ? us[i] : u01(philox4x32(make_uint4(i, 0x51u, stream, a.salt),
                                                      make_uint2(static_cast<uint32_t>(seed), 0)).x);
@@ -376,8 +396,9 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
   float best = -INFINITY;
   int besti = 0x7fffffff;
   const uint32_t hi = static_cast<uint32_t>(a.salt) ^ 0xA5000000u;
+  const int g0 = a.v_lo >> 2;
   for (int i = threadIdx.x; i * 4 < a.V; i += blockDim.x) {
-    const float4 u = uniform4(seed, stream, hi, static_cast<uint32_t>(i));
+    const float4 u = uniform4(seed, stream, hi, static_cast<uint32_t>(g0 + i));
     const float uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -423,6 +444,13 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
         bb = sb[w];
         bi = si[w];
       }
+    }
+    if (a.keys != nullptr) {
+      // vocabulary-parallel: the caller reduces the keys over ranks and finishes
+      a.count[b] = count;
+      a.valid[b] = s_valid;
+      a.keys[b] = pack_argmax_key(bb, a.v_lo + (bi < a.V ? bi : 0));
+      return;
     }
     int valid = s_valid && bb > -INFINITY && bi < a.V;
     const int tail = valid ? bi : 0;

@@ -44,6 +44,12 @@ struct GumbelArgs {
   const int* row_in_seq;            // [rows] or null
   int salt;
   int* tokens;
+  // Vocabulary-parallel mode: the rows hold columns [v_lo, v_lo + V) of the
+  // full vocabulary.  Noise is keyed by the global column, and with `keys` set
+  // the kernel writes the packed (score, global column) key of its local best
+  // instead of a token; the maximum key over ranks is the global draw.
+  int v_lo;
+  unsigned long long* keys;
 };
 
 struct SpecArgs {
@@ -67,6 +73,14 @@ struct SpecArgs {
   const float* lseT_target;   // [B * (n + 1)]
   const float* lse1_target;   // [B * (n + 1)]
   const float* lseT_draft;    // [B * n]
+  // Vocabulary-parallel mode (see GumbelArgs): the rows hold columns
+  // [v_lo, v_lo + V) of V_total; cand_logits [B, n, 2] carries the global
+  // (target, draft) logits of every candidate; the kernel writes count / valid
+  // and the packed key of its local tail draw to `keys`; the caller reduces the
+  // keys across ranks and finishes the outputs.
+  int v_lo, V_total;
+  const float* cand_logits;
+  unsigned long long* keys;
 };
 
 cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream);

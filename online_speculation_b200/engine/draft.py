@@ -97,7 +97,7 @@ class DraftHead:
         self.mask_token_id = cfg.vocab_size - 1 if mask_token_id is None else mask_token_id
         self.layer = cfg.num_hidden_layers - 1
 
-    def forward(self, meta: StepMeta, logit_rows: torch.Tensor) -> torch.Tensor:
+    def forward(self, meta: StepMeta, logit_rows: torch.Tensor, *, gather: bool = True) -> torch.Tensor:
         """meta: ids = [anchor, MASK...] per block, bidirectional plan over history + block.
         Writes the draft K/V of the block into the last layer's cache slots (the
         verify pass overwrites them).  Returns fp32 logits of ``logit_rows``."""
@@ -121,7 +121,7 @@ class DraftHead:
             return r.logits(h, logit_rows)
         r.comm.reduce_add_norm(part, h, r.w.final_norm, x, eps)
         sel = r._index_rows(x, logit_rows)
-        return r.logits(sel, None, normed=True)
+        return r.logits(sel, None, normed=True, gather=gather)
 
 
 # ------------------------------------------------------------------ learner --
@@ -293,22 +293,7 @@ class SuffixLearner:
             return torch.cat((a * cos - b * sin, b * cos + a * sin), -1)
 
         q, k = rope(q), rope(k)
-        P = fb.table.shape[1]
-        tbl = fb.table.long()
-        hk = kc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, P * 32, D)       # [B, ks, L, D] bf16
-        hv = vc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, P * 32, D)
-        qq = q.permute(0, 2, 1, 3).reshape(B, ks, G * Kb, D)                # [B, ks, G*K, D]
-        kb = k.permute(0, 2, 1, 3)                                          # [B, ks, K, D]
-        vb = v.permute(0, 2, 1, 3)
-        scale = D ** -0.5
-        s_hist = (qq.to(bf) @ hk.transpose(-1, -2)).float() * scale          # [B, ks, G*K, L]
-        s_blk = (qq @ kb.transpose(-1, -2)) * scale                          # [B, ks, G*K, K]
-        key = torch.arange(P * 32, device=emb.device)
-        visible = key[None, :] < fb.positions[:, :1]                          # [B, L] history keys
-        s_hist = s_hist.masked_fill(~visible[:, None, None, :], float("-inf"))
-        prob = torch.cat((s_hist, s_blk), -1).softmax(-1)
-        att = (prob[..., : P * 32].to(bf) @ hv).float() + prob[..., P * 32:] @ vb
-        att = att.view(B, ks, G, Kb, D).permute(0, 3, 1, 2, 4).reshape(B, Kb, qs * D)
+        att = self._draft_attention(q, k, v, fb, kc, vc).float()            # [B, K, qs * D]
         h = emb + _reduce(mm(att, params["w_o"]), comm)
         x2 = _copy(norm(h, lw.post_norm), comm)
         gu = mm(x2, lw.w_gu).view(B, Kb, -1, 2, 64)
@@ -321,6 +306,31 @@ class SuffixLearner:
         valid = torch.minimum(fb.count + 1, torch.full_like(fb.count, Kb - 1))
         w = (torch.arange(Kb - 1, device=emb.device)[None, :] < valid[:, None]).float() * fb.active[:, None]
         return (per * w).sum() / w.sum().clamp_min(1.0)
+
+    @staticmethod
+    def _draft_attention(q, k, v, fb: FeedbackRound, kc, vc) -> torch.Tensor:
+        """Block queries over the frozen paged history (keys before the block) plus the block itself.
+
+        One fused scaled-dot-product attention (grouped-query, boolean mask) in
+        bf16: the history scores are never materialised in fp32, and its backward
+        gives the gradients of the block's q, k and v.  Returns bf16 [B, K, qs * D].
+        """
+        B, Kb, qs, D = q.shape
+        ks = k.shape[2]
+        P = fb.table.shape[1]
+        L = P * kc.shape[2]
+        tbl = fb.table.long()
+        hk = kc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, L, D)          # [B, ks, L, D] bf16 (frozen)
+        hv = vc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, L, D)
+        bf = torch.bfloat16
+        keys = torch.cat((hk, k.permute(0, 2, 1, 3).to(bf)), 2)            # [B, ks, L + K, D]
+        vals = torch.cat((hv, v.permute(0, 2, 1, 3).to(bf)), 2)
+        pos = torch.arange(L + Kb, device=q.device)
+        visible = (pos[None, :] < fb.positions[:, :1]) | (pos[None, :] >= L)   # history before the block, whole block
+        mask = visible[:, None, None, :].expand(B, 1, Kb, L + Kb)
+        out = torch.nn.functional.scaled_dot_product_attention(q.permute(0, 2, 1, 3).to(bf), keys, vals,
+                                                               attn_mask=mask, enable_gqa=True)
+        return out.permute(0, 2, 1, 3).reshape(B, Kb, qs * D)
 
     def _divergence(self, student: torch.Tensor, teacher: torch.Tensor, comm) -> torch.Tensor:
         """Per-row TV or KL(teacher || student) over the (possibly vocabulary-sharded) rows."""

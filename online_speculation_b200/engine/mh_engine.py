@@ -156,18 +156,22 @@ class _RoundGraph:
         self.active.copy_(v["active"])
         self.row_streams.copy_(v["streams"].repeat_interleave(Kb - 1))
         meta_d = StepMeta(self.ids_draft.view(-1), v["positions"], v["slots"], self.plan_draft, self.draft_rows)
-        dl = e.head.forward(meta_d, self.draft_rows)
+        # Under tensor parallelism both samplers work on this rank's vocabulary shard and
+        # exchange per-row scalars; full logits rows are never gathered.
+        shard = e.runner.vocab_shard
+        dl = e.head.forward(meta_d, self.draft_rows, gather=False)
         draft_logits = e.runner._buf("draft_logits_keep", tuple(dl.shape), torch.float32)
         draft_logits.copy_(dl)
         K.gumbel_sample(draft_logits, self.inv_temp_rows, self.seeds, seed_index=self.seed_index,
-                        streams=self.row_streams, row_in_seq=self.row_in_seq, salt=0x1234, tokens=self.cand)
+                        streams=self.row_streams, row_in_seq=self.row_in_seq, salt=0x1234, tokens=self.cand,
+                        shard=shard)
         self.ids_verify[:, 0].copy_(v["anchors"])
         self.ids_verify[:, 1:].copy_(self.cand.view(B, Kb - 1))
         meta_v = StepMeta(self.ids_verify.view(-1), v["positions"], v["slots"], self.plan_verify, None)
-        tl = e.runner.forward(meta_v)
+        tl = e.runner.forward(meta_v, gather=False)
         self.teacher = e.runner.last_local_logits
         K.spec_verify(tl, draft_logits, self.cand.view(B, Kb - 1), self.inv_temp, self.seeds, streams=v["streams"],
-                      salt=0x777, out=self.out, stats=self.stats)
+                      salt=0x777, out=self.out, stats=self.stats, shard=shard)
         o = self.out
         self.result[:, 0].copy_(o["count"])
         self.result[:, 1].copy_(o["valid"])

@@ -196,7 +196,7 @@ class ModelRunner:
         return h
 
     def logits(self, h: torch.Tensor, rows: torch.Tensor | None, *, normed: bool = False,
-               out: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor | None = None, gather: bool = True) -> torch.Tensor:
         """Final RMSNorm + vocabulary-parallel head on the selected rows -> fp32 [R, V]."""
         sel = h if rows is None else self._index_rows(h, rows)
         R = sel.shape[0]
@@ -205,7 +205,7 @@ class ModelRunner:
         local = K.linear(x, self.w.head, out=self._buf("logits_local", (R, self.vocab_local), torch.float32),
                          out_dtype=torch.float32, static_weights=True)
         self.last_local_logits = local  # this rank's vocabulary shard (static buffer)
-        if self.comm.world == 1:
+        if self.comm.world == 1 or not gather:
             return local
         full = out if out is not None else self._buf("logits_full", (R, self.vocab_local * self.comm.world),
                                                      torch.float32)
@@ -218,7 +218,12 @@ class ModelRunner:
         return out
 
     # ---- full forward ----
-    def forward(self, meta: StepMeta, *, compute_logits: bool = True) -> torch.Tensor | None:
+    def forward(self, meta: StepMeta, *, compute_logits: bool = True, gather: bool = True) -> torch.Tensor | None:
+        """Decoder forward; returns fp32 logits of ``meta.logit_rows`` (all rows when None).
+
+        Under tensor parallelism ``gather=False`` returns this rank's vocabulary
+        shard (see :attr:`vocab_shard`) instead of full rows.
+        """
         T = meta.ids.numel()
         h = self._buf("h", (T, self.cfg.hidden_size))
         self.embed(meta.ids, h)
@@ -230,8 +235,18 @@ class ModelRunner:
             x = self._buf("x", (T, self.cfg.hidden_size))
             rows = meta.logit_rows
             sel = x if rows is None else self._index_rows(x, rows)
-            return self.logits(sel, None, normed=True)
+            return self.logits(sel, None, normed=True, gather=gather)
         return self.logits(h, meta.logit_rows)
+
+    @property
+    def vocab_shard(self) -> "K.VocabShard | None":
+        """This rank's vocabulary slice for vocabulary-parallel sampling (None without TP)."""
+        if self.comm.world == 1:
+            return None
+        if getattr(self, "_vocab_shard", None) is None:
+            self._vocab_shard = K.VocabShard(self.comm.rank * self.vocab_local, self.vocab_local,
+                                             self.vocab_local * self.comm.world, self.comm.group, self.comm.world)
+        return self._vocab_shard
 
 
 def build_meta(device, table: torch.Tensor, ids, positions, slots, q_lens, kv_lens, modes, group, logit_rows=None,

@@ -340,12 +340,76 @@ def row_stats(logits, inv_temp=None, targets=None):
     return lse1, lseT, logp, logq
 
 
-def gumbel_sample(logits, inv_temp, seeds, *, seed_index=None, streams=None, row_in_seq=None, salt=0, tokens=None):
-    """Gumbel-max (exponential race) sampling with counter-based randomness."""
+@dataclass
+class VocabShard:
+    """This rank's slice [v_lo, v_lo + width) of a vocabulary of v_total columns (tensor parallel).
+
+    Samplers given a shard scan only the local logits and exchange per-row
+    scalars (packed argmax keys, log-normalisers, candidate logits) through
+    small collectives instead of gathering full logits rows.
+    """
+
+    v_lo: int
+    width: int
+    v_total: int
+    group: object
+    world: int
+
+    def __post_init__(self):
+        self._bufs: dict = {}
+
+    def buf(self, name, shape, dtype, device):
+        key = (name, tuple(shape), dtype)
+        t = self._bufs.get(key)
+        if t is None:
+            t = self._bufs[key] = torch.zeros(shape, dtype=dtype, device=device)
+        return t
+
+    def all_reduce(self, t, op="sum"):
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM, group=self.group)
+        return t
+
+    def logsumexp(self, local: torch.Tensor) -> torch.Tensor:
+        """Global log-normalisers from per-rank ones ([..] -> [..])."""
+        import torch.distributed as dist
+
+        flat = local.reshape(-1)
+        gathered = self.buf("lse_gather", (self.world, flat.numel()), flat.dtype, flat.device)
+        dist.all_gather_into_tensor(gathered, flat.contiguous(), group=self.group)
+        return torch.logsumexp(gathered, 0).view_as(local)
+
+
+_ORD_NEG_INF = 0x007FFFFF   # monotone bit pattern of -inf in the packed argmax keys
+
+
+def unpack_argmax_keys(keys: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Packed (score, column) keys -> (column int64, found bool)."""
+    k = keys ^ torch.iinfo(torch.int64).min
+    col = 0xFFFFFFFF - (k & 0xFFFFFFFF)
+    found = ((k >> 32) & 0xFFFFFFFF) != _ORD_NEG_INF
+    return col, found
+
+
+def gumbel_sample(logits, inv_temp, seeds, *, seed_index=None, streams=None, row_in_seq=None, salt=0, tokens=None,
+                  shard: VocabShard | None = None):
+    """Gumbel-max (exponential race) sampling with counter-based randomness.
+
+    With ``shard``, ``logits`` holds this rank's vocabulary columns; every rank
+    returns the same global token (noise is keyed by the global column)."""
     rows = logits.shape[0]
     tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=logits.device)
+    if logits.is_cuda and shard is not None:
+        keys = shard.buf("gumbel_keys", (rows,), torch.int64, logits.device)
+        _ext.require().gumbel_sample(logits, inv_temp, seeds, seed_index, streams, row_in_seq, int(salt), tokens,
+                                     shard.v_lo, keys)
+        shard.all_reduce(keys, "max")
+        tokens.copy_(unpack_argmax_keys(keys)[0])
+        return tokens
     if logits.is_cuda:
-        _ext.require().gumbel_sample(logits, inv_temp, seeds, seed_index, streams, row_in_seq, int(salt), tokens)
+        _ext.require().gumbel_sample(logits, inv_temp, seeds, seed_index, streams, row_in_seq, int(salt), tokens,
+                                     0, None)
         return tokens
     x = logits.float() * (inv_temp.float()[:, None] if inv_temp is not None else 1.0)
     if seed_index is None and streams is None and row_in_seq is None:
@@ -365,7 +429,8 @@ def gumbel_sample(logits, inv_temp, seeds, *, seed_index=None, streams=None, row
     return tokens
 
 
-def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, salt=0, out=None, stats=None):
+def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, salt=0, out=None, stats=None,
+                shard: VocabShard | None = None):
     """Exact p/q correction of a batch of draft blocks.
 
     ``target`` [B*(n+1), V] logits, ``draft`` [B*n, V] logits, ``candidates`` [B, n].
@@ -396,9 +461,11 @@ def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, sal
                      "lseT_d": torch.empty(B * n, dtype=torch.float32, device=dev)}
         ext.row_stats(target, stats["inv_target"], None, stats["lse1_t"], stats["lseT_t"], None, None)
         ext.row_stats(draft, stats["inv_draft"], None, stats["lse1_d"], stats["lseT_d"], None, None)
+        if shard is not None:
+            return _spec_verify_shard(target, draft, candidates, inv_temp, seeds, streams, salt, res, stats, shard)
         ext.spec_verify(target, draft, candidates, n, inv_temp, seeds, streams, int(salt), res["count"],
                         res["tail"], res["valid"], res["emitted"], res["logq"], res["logp"], stats["lseT_t"],
-                        stats["lse1_t"], stats["lseT_d"])
+                        stats["lse1_t"], stats["lseT_d"], 0, 0, None, None)
         return res
     gen = torch.Generator().manual_seed(int(seeds.flatten()[0]) ^ int(salt))
     for b in range(B):
@@ -423,6 +490,60 @@ def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, sal
             res["emitted"][b, i] = x
             res["logq"][b, i] = (lt[i] * it).log_softmax(-1)[x]
             res["logp"][b, i] = lt[i].log_softmax(-1)[x]
+    return res
+
+
+def _spec_verify_shard(target, draft, candidates, inv_temp, seeds, streams, salt, res, stats, shard: VocabShard):
+    """Vocabulary-parallel p/q correction: the same draws as the unsharded kernel.
+
+    Exchanges per rank: one all-gather of the row log-normalisers, one sum of
+    the candidates' logits (each owned by one rank), one max of the packed tail
+    keys and one sum of the tail token's logit.
+    """
+    B, n = candidates.shape
+    dev = target.device
+    lse = torch.cat((stats["lse1_t"], stats["lseT_t"], stats["lseT_d"]))
+    g = shard.logsumexp(lse)
+    R = B * (n + 1)
+    lse1_t, lseT_t, lseT_d = g[:R], g[R:2 * R], g[2 * R:]
+    cand = candidates.long()
+    local = cand - shard.v_lo
+    own = (local >= 0) & (local < shard.width)
+    lc = local.clamp(0, shard.width - 1)
+    t_rows = (torch.arange(B, device=dev)[:, None] * (n + 1) + torch.arange(n, device=dev)[None, :])
+    d_rows = (torch.arange(B, device=dev)[:, None] * n + torch.arange(n, device=dev)[None, :])
+    cl = shard.buf("spec_cand", (B, n, 2), torch.float32, dev)
+    cl[..., 0] = torch.where(own, target[t_rows, lc], 0.0)
+    cl[..., 1] = torch.where(own, draft[d_rows, lc], 0.0)
+    shard.all_reduce(cl)
+    keys = shard.buf("spec_keys", (B,), torch.int64, dev)
+    _ext.require().spec_verify(target, draft, candidates, n, inv_temp, seeds, streams, int(salt), res["count"],
+                               res["tail"], res["valid"], res["emitted"], res["logq"], res["logp"], lseT_t, lse1_t,
+                               lseT_d, shard.v_lo, shard.v_total, cl, keys)
+    shard.all_reduce(keys, "max")
+    tail, found = unpack_argmax_keys(keys)
+    count = res["count"].long()
+    row = torch.arange(B, device=dev) * (n + 1) + count
+    tl_local = tail - shard.v_lo
+    t_own = (tl_local >= 0) & (tl_local < shard.width)
+    tv = shard.buf("spec_tail", (B,), torch.float32, dev)
+    tv.copy_(torch.where(t_own, target[row, tl_local.clamp(0, shard.width - 1)], 0.0))
+    shard.all_reduce(tv)
+    valid = (res["valid"] != 0) & found
+    tail = torch.where(valid, tail, 0)
+    res["valid"].copy_(valid.int())
+    res["tail"].copy_(tail.int())
+    i = torch.arange(n + 1, device=dev)[None, :]
+    is_tail = i == count[:, None]
+    cand_pad = torch.cat((cand, torch.zeros(B, 1, dtype=torch.long, device=dev)), 1)
+    logit_pad = torch.cat((cl[..., 0], torch.zeros(B, 1, device=dev)), 1)
+    emitted = torch.where(is_tail, tail[:, None], cand_pad)
+    logit = torch.where(is_tail, tv[:, None], logit_pad)
+    it = inv_temp[:, None] if inv_temp is not None else 1.0
+    keep = i <= count[:, None]
+    res["emitted"].copy_(torch.where(keep, emitted, 0).int())
+    res["logq"].copy_(torch.where(keep, logit * it - lseT_t.view(B, n + 1), 0.0))
+    res["logp"].copy_(torch.where(keep, logit - lse1_t.view(B, n + 1), 0.0))
     return res
 
 

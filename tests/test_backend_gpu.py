@@ -134,8 +134,13 @@ def test_arithmetic_coding_requests(backend, oracle):
     want = [int(torch.searchsorted(cdf, torch.tensor(u, dtype=torch.float64))) for u in pts]
     got = [s.token_ids[0] for s in out]
     assert sum(a == b for a, b in zip(got, want)) >= 60          # bf16 logits may move a boundary point
-    # code points of later tokens are rescaled, not redrawn: sequences sharing a first token differ later
-    assert len({s.token_ids for s in out}) > len({s.token_ids[0] for s in out})
+    # later tokens use the rescaled code point, not the original one: decoding the same point
+    # as an explicit uniform at every step gives a different sequence
+    plain = backend.sample_batch([GenerationRequest(prefix, 6, SamplingConfig(temperature=1.3), seed=0,
+                                                    request_id=f"p{i}", uniforms=(u,) * 6)
+                                  for i, u in enumerate(pts)])
+    assert sum(a.token_ids != b.token_ids for a, b in zip(out, plain)) >= 48
+    assert all(a.token_ids[0] == b.token_ids[0] for a, b in zip(out, plain))
     for s in out[:4]:
         lp, lq = _oracle_logprobs(oracle, prefix, s.token_ids, 1.3)
         assert float((torch.tensor(s.token_logprobs) - lq).abs().max()) < 0.2

@@ -144,3 +144,39 @@ def test_kernel_branch_matches_module_branch():
     # full speculative generation runs on the kernel branch
     res = generate(kb, prompt, 16, sampling=SamplingConfig(1.0), generator=torch.Generator(device="cuda").manual_seed(0))
     assert len(res.tokens) == 16
+
+
+def test_learner_draft_attention_matches_fp32():
+    from online_speculation_b200.engine.draft import FeedbackRound, SuffixLearner
+
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    B, Kb, qs, ks, D, P = 5, 4, 8, 2, 128, 3
+    pages = B * P + 2
+    kc = torch.randn(pages, ks, 32, D, device=dev).bfloat16()
+    vc = torch.randn(pages, ks, 32, D, device=dev).bfloat16()
+    table = torch.randperm(pages, device=dev)[:B * P].view(B, P).int()
+    hist = torch.tensor([0, 5, 32, 70, 95], device=dev)
+    positions = (hist[:, None] + torch.arange(Kb, device=dev)[None]).int()
+    q = torch.randn(B, Kb, qs, D, device=dev, requires_grad=True)
+    k = torch.randn(B, Kb, ks, D, device=dev, requires_grad=True)
+    v = torch.randn(B, Kb, ks, D, device=dev, requires_grad=True)
+    fb = FeedbackRound(None, positions, table, None, None, None, B)
+    out = SuffixLearner._draft_attention(q, k, v, fb, kc, vc).float()
+    # fp32 oracle
+    ref = torch.zeros(B, Kb, qs, D, device=dev)
+    for b in range(B):
+        n = int(hist[b])
+        hk = kc[table[b].long()].permute(1, 0, 2, 3).reshape(ks, P * 32, D)[:, :n].float()
+        hv = vc[table[b].long()].permute(1, 0, 2, 3).reshape(ks, P * 32, D)[:, :n].float()
+        keys = torch.cat((hk, k[b].permute(1, 0, 2)), 1)
+        vals = torch.cat((hv, v[b].permute(1, 0, 2)), 1)
+        for h in range(qs):
+            g = h // (qs // ks)
+            s = (q[b, :, h] @ keys[g].T) * D ** -0.5
+            ref[b, :, h] = s.softmax(-1) @ vals[g]
+    ref = ref.reshape(B, Kb, qs * D)
+    assert float((out - ref).norm() / ref.norm()) < 2e-2
+    # gradients flow to the block's q, k and v
+    (out * torch.randn_like(out)).sum().backward()
+    assert q.grad is not None and k.grad.abs().sum() > 0 and v.grad.abs().sum() > 0

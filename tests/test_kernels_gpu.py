@@ -295,3 +295,22 @@ def test_head_divergence_forward_backward(cuda, kind):
     (ref * torch.arange(1, R + 1, device=cuda)).sum().backward()
     assert torch.allclose(loss, ref.detach(), atol=2e-3, rtol=2e-3)
     assert _rel(y.grad, y2.grad) < 3e-2
+
+
+def test_sample_arithmetic_code_point_rescaling(cuda):
+    torch.manual_seed(3)
+    rows, V = 6, 1000
+    logits = torch.randn(rows, V, device=cuda) * 2
+    inv_t = torch.full((rows,), 0.8, device=cuda)
+    u = torch.rand(rows, dtype=torch.float64, device=cuda)
+    arith = torch.tensor([1, 0, 1, 1, 0, 1], dtype=torch.int32, device=cuda)
+    nxt = torch.full((rows,), -1.0, dtype=torch.float64, device=cuda)
+    tok, _, _ = ops.sample(logits, inv_t, u, arith=arith, next_uniforms=nxt)
+    rt, _, _, rn = ops.sample_reference(logits.cpu(), inv_t.cpu(), u.cpu(), with_code=True)
+    torch.cuda.synchronize()
+    assert torch.equal(tok.cpu(), rt)
+    flagged = arith.cpu().bool()
+    assert torch.allclose(nxt.cpu()[flagged], rn[flagged], atol=1e-4)
+    assert (nxt.cpu()[~flagged] == -1.0).all()
+    assert ((nxt.cpu()[flagged] >= 0) & (nxt.cpu()[flagged] < 1)).all()
+

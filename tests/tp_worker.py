@@ -57,6 +57,37 @@ def main():
         assert rel(out.cpu(), ref[60:64]) < 3e-2, ("verify", fused)
         torch.cuda.synchronize()
         workspace.check_status(dev)
+    # vocabulary-parallel samplers draw exactly what the unsharded kernels draw on full rows
+    from online_speculation_b200.ops import kernels as K  # noqa: E402
+
+    V, width = 1024, 1024 // world
+    shard = K.VocabShard(rank * width, width, V, dist.group.WORLD, world)
+    g = torch.Generator(device=dev).manual_seed(7)
+    B, n = 5, 3
+    full_t = torch.randn(B * (n + 1), V, device=dev, generator=g) * 3
+    full_d = full_t[torch.arange(B * (n + 1), device=dev).view(B, n + 1)[:, :n].reshape(-1)] + \
+        torch.randn(B * n, V, device=dev, generator=g)
+    seeds = torch.arange(11, 11 + B, dtype=torch.int64, device=dev)
+    it = torch.full((B,), 0.7, device=dev)
+    rows_it = it.repeat_interleave(n)
+    si = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(n)
+    streams = torch.zeros(B * n, dtype=torch.int32, device=dev)
+    rin = torch.arange(n, dtype=torch.int32, device=dev).repeat(B)
+    want = K.gumbel_sample(full_d, rows_it, seeds, seed_index=si, streams=streams, row_in_seq=rin, salt=5)
+    got = K.gumbel_sample(full_d[:, rank * width:(rank + 1) * width].contiguous(), rows_it, seeds, seed_index=si,
+                          streams=streams, row_in_seq=rin, salt=5, shard=shard)
+    assert torch.equal(want, got), ("sharded gumbel", want, got)
+    cand = want.view(B, n)
+    ref = K.spec_verify(full_t, full_d, cand, it, seeds, salt=9)
+    res = K.spec_verify(full_t[:, rank * width:(rank + 1) * width].contiguous(),
+                        full_d[:, rank * width:(rank + 1) * width].contiguous(), cand, it, seeds, salt=9, shard=shard)
+    for key in ("count", "tail", "valid"):
+        assert torch.equal(ref[key], res[key]), (key, ref[key], res[key])
+    for b in range(B):
+        c = int(ref["count"][b]) + 1
+        assert torch.equal(ref["emitted"][b, :c], res["emitted"][b, :c])
+        assert torch.allclose(ref["logq"][b, :c], res["logq"][b, :c], atol=1e-4)
+        assert torch.allclose(ref["logp"][b, :c], res["logp"][b, :c], atol=1e-4)
     eng = build_mh_engine(CFG, tp_group=dist.group.WORLD, seed=3, alpha=2.0, length=24, block_size=4,
                           learner_stride=8, use_graphs=False, kv_bytes=64 << 20, max_seq_tokens=64, max_batch=8)
     prompt = list(range(5, 21))
