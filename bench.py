@@ -46,9 +46,12 @@ def parse():
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("mh-spec", "grpo"), default="mh-spec",
+    p.add_argument("--workload", choices=("mh-spec", "grpo", "dllm"), default="mh-spec",
                    help="mh-spec: suffix-MH rollouts with speculative drafting (headline); "
-                        "grpo: GRPO training on the Qwen2.5-1.5B shape, data parallel")
+                        "grpo: GRPO training on the Qwen2.5-1.5B shape, data parallel; "
+                        "dllm: LLaDA-MoE-shaped block diffusion, expert parallel")
+    p.add_argument("--requests-per-rank", type=int, default=4)
+    p.add_argument("--ep-impl", choices=("fused", "nccl"), default="fused")
     p.add_argument("--group-size", type=int, default=8)
     p.add_argument("--prompts-per-rank", type=int, default=1)
     p.add_argument("--model", default="qwen2.5-7b")
@@ -269,6 +272,91 @@ def run_ours(args, rank, world, local, group) -> dict:
     return out
 
 
+DLLM_METRIC = "block-diffusion generated tok/s (LLaDA-MoE-7B-A1B shape, expert parallel, whole job)"
+
+
+def run_dllm(args, rank, world, local, group) -> dict:
+    """256 generated tokens after a 256-token prompt, 32-token blocks, 32 reverse steps per block.
+
+    Every rank serves its own requests (data parallel outside the MoE layers);
+    the 64 experts are split over the ranks and tokens cross NVLink in every
+    MoE layer.  One step = one complete generation of every rank's requests.
+    """
+    import numpy as np
+    import torch
+
+    from online_speculation_b200.dllm.backend import DiffusionEngineBackend
+    from online_speculation_b200.dllm.config import DiffusionSamplingConfig
+    from online_speculation_b200.dllm.types import DiffusionGenerationRequest
+    from online_speculation_b200.models.moe import PRESETS, MoEDiffusionModel, build_weights, random_state_dict
+    from online_speculation_b200.ops import _ext
+
+    cfg = PRESETS["llada-moe-7b-a1b"]
+    E = cfg.num_experts
+    lo, hi = (rank * E // world, (rank + 1) * E // world)
+    sd = random_state_dict(cfg, seed=args.seed, device="cuda")
+    weights = build_weights(cfg, sd, device="cuda", expert_range=(lo, hi))
+    del sd
+    torch.cuda.empty_cache()
+    prompt_len, gen_len, B = 256, 256, args.requests_per_rank
+    ep = None
+    if world > 1:
+        from online_speculation_b200.parallel.ep import ExpertParallelMoE, NcclExpertParallelMoE
+
+        cls = ExpertParallelMoE if args.ep_impl == "fused" else NcclExpertParallelMoE
+        ep = cls(group, experts=E, top_k=cfg.num_experts_per_tok, hidden=cfg.hidden_size,
+                 ffn=cfg.moe_intermediate_size, max_tokens=B * (prompt_len + gen_len), device="cuda")
+    model = MoEDiffusionModel(weights, ep=ep)
+    backend = DiffusionEngineBackend(model, model_id="llada-moe-7b-a1b (random init)")
+    sampling = DiffusionSamplingConfig(block_length=32, steps_per_block=32, temperature=1.0)
+    rng = np.random.default_rng(args.seed + 101 * rank)
+    prompts_host = torch.from_numpy(rng.integers(0, cfg.mask_token_id - 1, size=(B, prompt_len)).astype(np.int32))
+    prompts_host = prompts_host.pin_memory()
+
+    def step(i):
+        # end to end: the prompts come from pinned host memory every step; tokens come back to the host
+        dev = prompts_host.to("cuda", non_blocking=True)
+        reqs = [DiffusionGenerationRequest(tuple(dev[b].tolist()), gen_len, sampling, seed=1000 * i + b + 7 * rank,
+                                           request_id=f"r{rank}:{i}:{b}") for b in range(B)]
+        out = backend.sample_batch(reqs)
+        return sum(len(o.token_ids) for o in out)
+
+    for i in range(args.warmup):
+        step(i)
+    barrier(world)
+    launches0 = _ext.launches()
+    sampler = ClockSampler(local)
+    with sampler:
+        barrier(world)
+        wall0 = time.perf_counter()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        generated = 0
+        for i in range(args.steps):
+            generated += step(args.warmup + i)
+        stop.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+        barrier(world)
+    ms = max_over_ranks(start.elapsed_time(stop), world)
+    wall = max_over_ranks(wall, world)
+    total = sum_over_ranks(generated, world)
+    value = total / (ms / 1e3)
+    return {
+        "metric": DLLM_METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform-random prompt ids, random-init weights)",
+        "config": {"model": "llada-moe-7b-a1b (random init)", "global_batch": B * world,
+                   "seq_len": prompt_len + gen_len, "parallelism": f"ep{world}" if world > 1 else "single",
+                   "ep_exchange": args.ep_impl if world > 1 else None, "block_length": 32, "steps_per_block": 32,
+                   "l2": "expert weights (13 GB) streamed every reverse step exceed the 126 MB L2"},
+        "clocks": sampler.summary(),
+        "e2e": {"value": total / wall, "unit": "tok/s", "h2d_bytes_per_step": int(B * prompt_len * 4),
+                "d2h_bytes_per_step": int(B * gen_len * 8)},
+        "gpu_launches": int(_ext.launches() - launches0),
+    }
+
+
 GRPO_METRIC = "GRPO tokens/s (prompt + completion tokens trained per second, whole job)"
 
 
@@ -434,7 +522,11 @@ def main():
     args = parse()
     rank, world, local, group = dist_setup(args.gpus)
     try:
-        if args.workload == "grpo":
+        if args.workload == "dllm":
+            out = (run_dllm(args, rank, world, local, group) if args.impl == "ours" else
+                   {"impl": "reference", "unavailable": "the reference LLaDA-MoE path loads remote model code from "
+                                                        "the Hugging Face hub, which this machine cannot reach"})
+        elif args.workload == "grpo":
             out = (run_grpo(args, rank, world, local, group) if args.impl == "ours" else
                    {"impl": "reference", "unavailable": "the reference GRPO path needs trl and peft, which are not "
                                                         "installed in this image"})

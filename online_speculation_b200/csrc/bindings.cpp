@@ -12,6 +12,7 @@
 
 #include "adamw.h"
 #include "attention.h"
+#include "ep.h"
 #include "comm.h"
 #include "elementwise.h"
 #include "gemm.h"
@@ -406,6 +407,63 @@ void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows
         "allreduce_add_rmsnorm");
 }
 
+// Expert-parallel MoE exchange: phase 0 dispatch (count exchange + peer stores), phase 1 combine (peer loads).
+void ep_exchange(std::vector<int64_t> tables, std::vector<int64_t> recv_x, std::vector<int64_t> recv_y,
+                 std::vector<int64_t> pads, Tensor epoch, int64_t r_max, Tensor counts, Tensor topk_idx,
+                 Tensor topk_w, Tensor x, Tensor cursor, Tensor slot_of, Tensor local_offsets, Tensor h, int64_t E,
+                 int64_t k, int64_t rank, int64_t blocks, int64_t phase, Tensor status) {
+  CHECK_CUDA(x);
+  CHECK_ROWS(x);
+  CHECK_ROWS(h);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(h, torch::kBFloat16);
+  for (const Tensor* t : {&counts, &topk_idx, &cursor, &slot_of, &local_offsets, &epoch}) {
+    CHECK_DT(*t, torch::kInt32);
+    TORCH_CHECK(t->is_cuda() && t->is_contiguous(), "EP metadata must be contiguous CUDA int32");
+  }
+  CHECK_DT(topk_w, torch::kFloat32);
+  const int world = static_cast<int>(tables.size());
+  TORCH_CHECK(world >= 1 && world <= osb::kEpMaxRanks && recv_x.size() == tables.size() &&
+                  recv_y.size() == tables.size() && pads.size() == tables.size(),
+              "one table, receive buffer, output buffer and pad per rank (at most 8)");
+  const int T = x.size(0);
+  TORCH_CHECK(topk_idx.numel() >= T * k && topk_w.numel() >= T * k && slot_of.numel() >= T * k, "top-k shapes");
+  TORCH_CHECK(counts.numel() == E && cursor.numel() == E && local_offsets.numel() == E / world + 1, "EP shapes");
+  TORCH_CHECK(h.size(0) == T && h.size(1) == x.size(1), "residual shape");
+  c10::cuda::CUDAGuard guard(x.device());
+  osb::EpArgs a{};
+  for (int q = 0; q < world; ++q) {
+    a.tables[q] = reinterpret_cast<int*>(tables[q]);
+    a.recv_x[q] = reinterpret_cast<__nv_bfloat16*>(recv_x[q]);
+    a.recv_y[q] = reinterpret_cast<__nv_bfloat16*>(recv_y[q]);
+    a.pads[q] = reinterpret_cast<uint32_t*>(pads[q]);
+  }
+  a.world = world;
+  a.rank = static_cast<int>(rank);
+  a.E = static_cast<int>(E);
+  a.E_local = static_cast<int>(E / world);
+  a.k = static_cast<int>(k);
+  a.T = T;
+  a.H = x.size(1);
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
+  a.r_max = r_max;
+  a.counts = counts.data_ptr<int>();
+  a.topk_idx = topk_idx.data_ptr<int>();
+  a.topk_w = topk_w.data_ptr<float>();
+  a.x = bf(x);
+  a.ldx = x.stride(0);
+  a.cursor = cursor.data_ptr<int>();
+  a.slot_of = slot_of.data_ptr<int>();
+  a.local_offsets = local_offsets.data_ptr<int>();
+  a.h = bfm(h);
+  a.ldh = h.stride(0);
+  a.status = status.data_ptr<int>();
+  const int b = static_cast<int>(blocks);
+  check(phase == 0 ? osb::ep_dispatch_launch(a, b, at::cuda::getCurrentCUDAStream())
+                   : osb::ep_combine_launch(a, b, at::cuda::getCurrentCUDAStream()),
+        "ep_exchange");
+}
+
 void logprob_grad(Tensor logits, Tensor lse, Tensor targets, Tensor w, Tensor grad) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
@@ -635,6 +693,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_offsets", &moe_offsets);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_combine", &moe_combine);
+  m.def("ep_exchange", &ep_exchange);
   m.def("set_pdl", [](bool on) { osb::pdl_enabled() = on; });
   m.def("pdl_enabled", []() -> bool { return osb::pdl_enabled(); });
 

