@@ -384,6 +384,7 @@ void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows
   TORCH_CHECK(world >= 1 && world <= osb::kMaxRanks && rows.size() == parts.size() && pads.size() == parts.size(),
               "one partial, row buffer and signal pad per rank (at most 8)");
   TORCH_CHECK(h.size(0) >= T && x.size(0) >= T && w.numel() == h.size(1), "all-reduce shapes");
+  TORCH_CHECK(epoch.numel() >= 4, "the all-reduce epoch buffer holds four counters");
   c10::cuda::CUDAGuard guard(h.device());
   osb::ArArgs a{};
   for (int q = 0; q < world; ++q) {

@@ -9,21 +9,21 @@
 // and applies RMSNorm in the same pass: one kernel, one barrier, and each rank
 // reads (world - 1) x T x H x 2 bytes over NVLink.
 //
-// Eight ranks: two-shot over symmetric buffers (every rank can load every
-// other rank's buffers through NVLink / NVSwitch peer mappings):
-//   kernel A  each rank owns a slice of rows; it loads those rows of every
-//             rank's partial P_r (peer loads), adds the residual, and stores
-//             the reduced rows into its own symmetric row buffer and its
-//             local residual stream;
-//   kernel B  every rank gathers the other ranks' reduced rows (peer loads)
-//             and applies RMSNorm to all rows.
-// Each kernel starts with a cross-rank barrier: block 0 publishes the call's
-// epoch into every rank's signal pad (release, system scope) and every block
-// polls its own pad (acquire) with a bounded wait.  On timeout the kernel
-// records an error and skips its work instead of hanging.  Partials are
-// double-buffered by the caller, so one barrier per kernel is enough: a rank
-// can only overwrite a partial buffer after every peer has passed the next
-// reduction's barriers.
+// More ranks: two-shot in one kernel over symmetric buffers (every rank can
+// load every other rank's buffers through NVLink / NVSwitch peer mappings):
+//   phase A  each rank owns a slice of rows; it loads those rows of every
+//            rank's partial P_r (peer loads), adds the residual, and stores the
+//            reduced rows into its own symmetric row buffer and its local
+//            residual stream;
+//   phase B  after a cross-rank barrier (the grid is co-resident, the last
+//            block of phase A signals), every rank gathers the other ranks'
+//            reduced rows (peer loads) and applies RMSNorm to all rows.
+// Barriers: block 0 (or the last block) publishes the call's epoch into every
+// rank's signal pad (release, system scope) and every block polls its own pad
+// (acquire) with a bounded wait.  On timeout the kernel records an error and
+// skips its work instead of hanging.  Partials are double-buffered by the
+// caller, so a rank can only overwrite a partial buffer after every peer has
+// passed the next reduction's first barrier.
 //
 // There is no counterpart in the reference (it has no distributed code); this
 // is the fused collective behind the tensor-parallel decoder layers.
@@ -69,110 +69,6 @@ __device__ __forceinline__ bool rank_barrier(const ArArgs& a, int slot, uint32_t
 }
 
 __device__ __forceinline__ int slice_begin(int T, int world, int r) { return (T * r) / world; }
-
-__global__ void __launch_bounds__(256) reduce_rows_kernel(const ArArgs a) {
-  const uint32_t epoch = *a.epoch + 1;
-  if (!rank_barrier(a, 0, epoch)) return;
-  const int r0 = slice_begin(a.T, a.world, a.rank), r1 = slice_begin(a.T, a.world, a.rank + 1);
-  const int nvec = a.H / 8;
-  for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
-    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-      float acc[8];
-      {
-        const uint4 hr = *reinterpret_cast<const uint4*>(a.h + static_cast<long long>(row) * a.ldh + v * 8);
-        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hr);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = bf2f(he[e]);
-      }
-      uint4 parts[kMaxRanks];
-#pragma unroll
-      for (int q = 0; q < kMaxRanks; ++q) {
-        if (q < a.world)
-          parts[q] = __ldcg(reinterpret_cast<const uint4*>(a.parts[q] + static_cast<long long>(row) * a.H + v * 8));
-      }
-#pragma unroll
-      for (int q = 0; q < kMaxRanks; ++q) {
-        if (q < a.world) {
-          const __nv_bfloat16* pe = reinterpret_cast<const __nv_bfloat16*>(&parts[q]);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] += bf2f(pe[e]);
-        }
-      }
-      uint4 out;
-      __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&out);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) ob[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
-      *reinterpret_cast<uint4*>(a.h + static_cast<long long>(row) * a.ldh + v * 8) = out;
-      *reinterpret_cast<uint4*>(a.rows[a.rank] + static_cast<long long>(row) * a.H + v * 8) = out;
-    }
-  }
-}
-
-__global__ void __launch_bounds__(256) gather_norm_kernel(const ArArgs a) {
-  const uint32_t epoch = *a.epoch + 1;
-  const bool ok = rank_barrier(a, 1, epoch);
-  const int nvec = a.H / 8;
-  __shared__ float red[33];
-  if (ok) {
-    for (int row = blockIdx.x; row < a.T; row += gridDim.x) {
-      int owner = 0;
-      while (owner + 1 < a.world && slice_begin(a.T, a.world, owner + 1) <= row) ++owner;
-      __nv_bfloat16* hr = a.h + static_cast<long long>(row) * a.ldh;
-      float ss = 0.0f;
-      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-        uint4 val;
-        if (owner == a.rank) {
-          val = *reinterpret_cast<const uint4*>(hr + v * 8);
-        } else {
-          val = __ldcg(reinterpret_cast<const uint4*>(a.rows[owner] + static_cast<long long>(row) * a.H + v * 8));
-          *reinterpret_cast<uint4*>(hr + v * 8) = val;
-        }
-        const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&val);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float f = bf2f(e8[e]);
-          ss += f * f;
-        }
-      }
-      ss = warp_sum(ss);
-      const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-      if (lane == 0) red[warp] = ss;
-      __syncthreads();
-      if (warp == 0) {
-        float t = lane < blockDim.x / 32 ? red[lane] : 0.0f;
-        t = warp_sum(t);
-        if (lane == 0) red[32] = rsqrtf(t / a.H + a.eps);
-      }
-      __syncthreads();
-      const float rs = red[32];
-      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-        const uint4 hv = *reinterpret_cast<const uint4*>(hr + v * 8);
-        const uint4 wv = *reinterpret_cast<const uint4*>(a.w + v * 8);
-        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
-        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
-        uint4 out;
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = f2bf(bf2f(we[e]) * bf2f(f2bf(bf2f(he[e]) * rs)));
-        *reinterpret_cast<uint4*>(a.x + static_cast<long long>(row) * a.ldx + v * 8) = out;
-      }
-      __syncthreads();
-    }
-  }
-  // The last block to finish advances the epoch for the next reduction.
-  __shared__ int last;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const uint32_t done = atomicAdd(a.epoch + 1, 1u);
-    last = done == gridDim.x - 1;
-    if (last) {
-      a.epoch[1] = 0;
-      __threadfence();
-      a.epoch[0] = epoch;
-    }
-  }
-}
 
 // Marks this call complete once every block has finished (the next call's epoch).
 __device__ __forceinline__ void finish_call(const ArArgs& a, uint32_t epoch) {
@@ -295,6 +191,120 @@ __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArA
   finish_call(a, epoch);
 }
 
+// Two-shot in one kernel (more than four ranks): phase A reduces this rank's row
+// slice (peer loads of every rank's partial, rank order) into h and the
+// symmetric row buffer; the last block to finish publishes slot 3 and every
+// block waits for all peers (the grid is sized to be co-resident); phase B
+// copies the other ranks' reduced rows and applies RMSNorm to every row.
+__global__ void __launch_bounds__(kOneShotThreads) twoshot_norm_kernel(const ArArgs a) {
+  const uint32_t epoch = *a.epoch + 1;
+  bool ok = rank_barrier(a, 2, epoch);
+  const int r0 = slice_begin(a.T, a.world, a.rank), r1 = slice_begin(a.T, a.world, a.rank + 1);
+  const int nvec = a.H / 8;
+  if (ok) {
+    for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
+      __nv_bfloat16* hr = a.h + static_cast<long long>(row) * a.ldh;
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        uint4 parts[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+          if (q < a.world)
+            parts[q] = __ldcg(reinterpret_cast<const uint4*>(a.parts[q] + static_cast<long long>(row) * a.H + v * 8));
+        const uint4 hv = *reinterpret_cast<const uint4*>(hr + v * 8);
+        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
+        float acc[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = bf2f(he[e]);
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q) {
+          if (q < a.world) {
+            const __nv_bfloat16* pe = reinterpret_cast<const __nv_bfloat16*>(&parts[q]);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[e] += bf2f(pe[e]);
+          }
+        }
+        uint4 out;
+        __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ob[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+        *reinterpret_cast<uint4*>(hr + v * 8) = out;
+        *reinterpret_cast<uint4*>(a.rows[a.rank] + static_cast<long long>(row) * a.H + v * 8) = out;
+      }
+    }
+  }
+  // every block's reduced rows must be visible to the peers before the slot-3 signal
+  __threadfence_system();
+  __syncthreads();
+  __shared__ int last, ok2;
+  if (threadIdx.x == 0) {
+    const uint32_t done = atomicAdd(a.epoch + 2, 1u);   // phase-A arrivals (epoch[1] counts the call's end)
+    last = done == gridDim.x - 1;
+    if (last) a.epoch[2] = 0;
+  }
+  __syncthreads();
+  if (last && threadIdx.x < a.world) st_release_sys(a.pads[threadIdx.x] + 3 * kMaxRanks + a.rank, epoch);
+  if (threadIdx.x == 0) {
+    ok2 = 1;
+    const uint32_t* mine = a.pads[a.rank] + 3 * kMaxRanks;
+    const unsigned long long start = global_ns();
+    for (int q = 0; q < a.world && ok2; ++q) {
+      while (static_cast<int>(ld_acquire_sys(mine + q) - epoch) < 0) {
+        if (global_ns() - start > kWaitLimitNs) {
+          record_error(a.status, kErrPeerWait);
+          ok2 = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  __shared__ float red[33];
+  if (ok && ok2) {
+    for (int row = blockIdx.x; row < a.T; row += gridDim.x) {
+      int owner = 0;
+      while (owner + 1 < a.world && slice_begin(a.T, a.world, owner + 1) <= row) ++owner;
+      __nv_bfloat16* hr = a.h + static_cast<long long>(row) * a.ldh;
+      float ss = 0.0f;
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        uint4 val;
+        if (owner == a.rank) {
+          val = *reinterpret_cast<const uint4*>(hr + v * 8);
+        } else {
+          val = __ldcg(reinterpret_cast<const uint4*>(a.rows[owner] + static_cast<long long>(row) * a.H + v * 8));
+          *reinterpret_cast<uint4*>(hr + v * 8) = val;
+        }
+        const __nv_bfloat16* e8 = reinterpret_cast<const __nv_bfloat16*>(&val);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += bf2f(e8[e]) * bf2f(e8[e]);
+      }
+      ss = warp_sum(ss);
+      const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      if (warp == 0) {
+        float t = lane < kOneShotThreads / 32 ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        if (lane == 0) red[32] = rsqrtf(t / a.H + a.eps);
+      }
+      __syncthreads();
+      const float rs = red[32];
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(hr + v * 8);
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.w + v * 8);
+        const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+        uint4 out;
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(&out);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = f2bf(bf2f(we[e]) * bf2f(f2bf(bf2f(he[e]) * rs)));
+        *reinterpret_cast<uint4*>(a.x + static_cast<long long>(row) * a.ldx + v * 8) = out;
+      }
+      __syncthreads();
+    }
+  }
+  finish_call(a, epoch);
+}
+
 }  // namespace
 
 cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
@@ -310,13 +320,20 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream
     oneshot_norm_kernel<<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
     return cudaGetLastError();
   }
-  const int rows_per_rank = (a.T + a.world - 1) / a.world;
-  const int grid_a = blocks < rows_per_rank ? blocks : rows_per_rank;
-  reduce_rows_kernel<<<grid_a > 0 ? grid_a : 1, 256, 0, stream>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  const int grid_b = blocks < a.T ? blocks : a.T;
-  gather_norm_kernel<<<grid_b, 256, 0, stream>>>(a);
+  // every block of the two-shot kernel waits for the others between its phases: keep the grid co-resident
+  static int resident = 0;
+  if (resident == 0) {
+    int per_sm = 0, dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, twoshot_norm_kernel, kOneShotThreads, 0) !=
+            cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    resident = per_sm * (sms > 0 ? sms : 148);
+  }
+  int grid = blocks < a.T ? blocks : a.T;
+  if (grid > resident) grid = resident;
+  twoshot_norm_kernel<<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

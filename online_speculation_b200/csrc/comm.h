@@ -12,7 +12,7 @@ struct ArArgs {
   const __nv_bfloat16* parts[kMaxRanks];  // every rank's partial sums [T, H] (symmetric, peer-mapped)
   __nv_bfloat16* rows[kMaxRanks];         // every rank's reduced-rows buffer [T, H] (symmetric)
   uint32_t* pads[kMaxRanks];              // every rank's signal pad (uint32 flags, symmetric)
-  uint32_t* epoch;                        // local [2]: completed-call counter, block arrival counter
+  uint32_t* epoch;                        // local [4]: completed-call counter, two block arrival counters
   __nv_bfloat16* h;                       // local residual stream [T, H] (row stride ldh)
   long long ldh;
   const __nv_bfloat16* w;                 // RMSNorm weight [H]

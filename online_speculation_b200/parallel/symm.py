@@ -70,7 +70,7 @@ class SymmetricCollectives(NcclCollectives):
             self._handles.append(symm.rendezvous(t, group))
         self._rows = symm.empty(max_tokens, hidden, dtype=torch.bfloat16, device=self.device)
         self._rows_h = symm.rendezvous(self._rows, group)
-        self.epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.epoch = torch.zeros(4, dtype=torch.int32, device=self.device)   # call counter, two arrival counters
         self._flip = 0
         self._parts_ptrs = [list(h.buffer_ptrs) for h in self._handles]
         self._rows_ptrs = list(self._rows_h.buffer_ptrs)
