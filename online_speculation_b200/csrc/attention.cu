@@ -134,11 +134,14 @@ struct WarpState {
   float o[kD / 8][4];
   float m[2], l[2];
   int qpos[2];   // absolute query position of this thread's two rows (-1 = padding row)
+  int frontier;  // keys below this index are visible to every row of the warp (no masking needed)
 };
 
 __device__ __forceinline__ void load_q(const AttnArgs& a, WarpState& st, int q0, int rows, int row_base, int g,
-                                       int qlen, int kvlen, int lane) {
+                                       int qlen, int kvlen, int lane, int bidir) {
   const int r_lo = lane / 4, c2 = (lane % 4) * 2;
+  // the warp's first row has the earliest causal horizon; padding rows (zero queries) need no mask
+  st.frontier = (bidir || row_base >= rows) ? kvlen : min(kvlen, kvlen - qlen + row_base / a.G + 1);
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int row = row_base + r_lo + h * 8;
@@ -195,19 +198,29 @@ __device__ __forceinline__ void process_keys(const AttnArgs& a, WarpState& st, K
       mma16816(s[n], st.qf[kk + 1], b2, b3);
     }
   }
-  // mask + online softmax
+  // mask + online softmax (chunks below the warp's causal frontier need no mask)
   const int c2 = (lane % 4) * 2;
   float mx[2] = {-INFINITY, -INFINITY};
+  if (key0 + CH <= st.frontier) {
 #pragma unroll
-  for (int n = 0; n < NB; ++n) {
+    for (int n = 0; n < NB; ++n)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int h = i / 2;
-      const int key = key0 + n * 8 + c2 + (i & 1);
-      const int qp = st.qpos[h];
-      const bool ok = qp >= 0 && key < kvlen && (bidir || key <= qp);
-      s[n][i] = ok ? s[n][i] * a.scale_log2 : -INFINITY;
-      mx[h] = fmaxf(mx[h], s[n][i]);
+      for (int i = 0; i < 4; ++i) {
+        s[n][i] *= a.scale_log2;
+        mx[i / 2] = fmaxf(mx[i / 2], s[n][i]);
+      }
+  } else {
+#pragma unroll
+    for (int n = 0; n < NB; ++n) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int h = i / 2;
+        const int key = key0 + n * 8 + c2 + (i & 1);
+        const int qp = st.qpos[h];
+        const bool ok = qp >= 0 && key < kvlen && (bidir || key <= qp);
+        s[n][i] = ok ? s[n][i] * a.scale_log2 : -INFINITY;
+        mx[h] = fmaxf(mx[h], s[n][i]);
+      }
     }
   }
   float corr[2];
@@ -236,12 +249,15 @@ __device__ __forceinline__ void process_keys(const AttnArgs& a, WarpState& st, K
     rs[h] += __shfl_xor_sync(0xffffffffu, rs[h], 2);
     st.l[h] = st.l[h] * corr[h] + rs[h];
   }
+  // the running maximum rarely moves after the first chunks: skip the rescale when no row needs it
+  if (__any_sync(0xffffffffu, corr[0] != 1.0f || corr[1] != 1.0f)) {
 #pragma unroll
-  for (int n = 0; n < kD / 8; ++n) {
-    st.o[n][0] *= corr[0];
-    st.o[n][1] *= corr[0];
-    st.o[n][2] *= corr[1];
-    st.o[n][3] *= corr[1];
+    for (int n = 0; n < kD / 8; ++n) {
+      st.o[n][0] *= corr[0];
+      st.o[n][1] *= corr[0];
+      st.o[n][2] *= corr[1];
+      st.o[n][3] *= corr[1];
+    }
   }
   // O += P V  (CH / 16 k-steps of 16 keys)
 #pragma unroll
@@ -306,7 +322,7 @@ __global__ void __launch_bounds__(128) attn_rows_kernel(const AttnArgs a) {
   const int rows = qlen * a.G;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   WarpState st;
-  load_q(a, st, q0, rows, row0 + warp * 16, g, qlen, kvlen, lane);
+  load_q(a, st, q0, rows, row0 + warp * 16, g, qlen, kvlen, lane, bidir);
   // last key any row of this tile can see
   const int last_row = min(rows - 1, row0 + 63);
   const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
@@ -391,7 +407,7 @@ __global__ void __launch_bounds__(128 * MT, 2)
   const int bidir = a.mode[b];
   const int rows = qlen * a.G;
   WarpState st;
-  load_q(a, st, q0, rows, row0 + mt * 16, g, qlen, kvlen, lane);
+  load_q(a, st, q0, rows, row0 + mt * 16, g, qlen, kvlen, lane, bidir);
   const int last_row = min(rows - 1, row0 + 16 * MT - 1);
   const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
   const int nchunks = (max(max_key, 0) + kCh - 1) / kCh;
