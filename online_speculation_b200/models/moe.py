@@ -220,8 +220,8 @@ class MoEDiffusionModel:
             self._bufs[("layout", key)] = lay
         return lay
 
-    def hidden(self, tokens: torch.Tensor) -> torch.Tensor:
-        """Final residual stream [B * L, H] (before the final norm)."""
+    def hidden(self, tokens: torch.Tensor, layer_limit: int | None = None) -> torch.Tensor:
+        """Final residual stream [B * L, H] (before the final norm) after the first ``layer_limit`` layers."""
         c = self.cfg
         B, L = tokens.shape
         T = B * L
@@ -240,7 +240,10 @@ class MoEDiffusionModel:
             self._moe_buf = K.MoEBuffers(T, c.num_experts, c.num_experts_per_tok, H, c.moe_intermediate_size,
                                          self.device) if self.device.type == "cuda" else None
         K.embed(ids, self.w.embed, out=h)
-        for lw in self.w.layers:
+        layers = self.w.layers if layer_limit is None else self.w.layers[:layer_limit]
+        if self.ep is not None and layer_limit is not None:
+            raise ValueError("an expert-parallel model runs every layer on every rank")
+        for lw in layers:
             K.rmsnorm(h, lw.in_norm, c.rms_norm_eps, out=x)
             K.linear(x, lw.w_qkv, out=qkv, static_weights=True)
             K.rope_cache(qkv, pos, slots, self.w.inv_freq, q, kc, vc, nq, nkv, q_norm=lw.q_norm, k_norm=lw.k_norm,
@@ -257,9 +260,10 @@ class MoEDiffusionModel:
         self.token_slots += T
         return h
 
-    def logits(self, tokens: torch.Tensor, rows: torch.Tensor | None = None) -> torch.Tensor:
+    def logits(self, tokens: torch.Tensor, rows: torch.Tensor | None = None,
+               layer_limit: int | None = None) -> torch.Tensor:
         B, L = tokens.shape
-        h = self.hidden(tokens)
+        h = self.hidden(tokens, layer_limit)
         if rows is not None:
             R = rows.shape[1]
             flat = (torch.arange(B, device=self.device)[:, None] * L + rows.to(self.device)).reshape(-1)

@@ -134,6 +134,25 @@ class LoRAMoEPolicy:
         finally:
             self._disabled = prev
 
+    @torch.no_grad()
+    def merged_weights(self) -> MoEWeights:
+        """Serving weights with the adapters folded in: W + scale * (B * mask) @ A (other tensors shared)."""
+        import dataclasses
+
+        self._refresh_views()
+        s = self.lora.scale
+        layers = []
+        for lw, ad in zip(self.w.layers, self.adapters):
+            upd = {}
+            for key, name in (("qkv", "w_qkv"), ("o", "w_o")):
+                a = ad.get(key)
+                if a is not None:
+                    w = getattr(lw, name)
+                    delta = s * ((a.B * a.block_mask) @ a.A)
+                    upd[name] = (w.float() + delta.to(w.device)).to(w.dtype).contiguous()
+            layers.append(dataclasses.replace(lw, **upd))
+        return dataclasses.replace(self.w, layers=layers)
+
     # ---- forward ----
     def hidden(self, tokens: torch.Tensor) -> torch.Tensor:
         c = self.cfg
