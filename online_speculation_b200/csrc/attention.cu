@@ -362,11 +362,12 @@ constexpr int kTStages = 3;
 constexpr int kBoxBytes = kCh * 64 * 2;          // 16 key rows x 64 bf16 columns
 constexpr int kChunkBytes = 4 * kBoxBytes;       // K lo | K hi | V lo | V hi
 constexpr int kGroupBytes = kTStages * kChunkBytes;
+constexpr int kMergeStride = kD + 8;            // fp32 merge row (floats)
 
 template <int MT>
 struct TmaSmem {
   static constexpr int kPipe = kKG * kGroupBytes;
-  static constexpr int kMerge = MT * kKG * (16 * kD + 32) * 4;
+  static constexpr int kMerge = MT * kKG * (16 * kMergeStride + 32) * 4;
   static constexpr int kBody = kPipe > kMerge ? kPipe : kMerge;
   static constexpr int kBarOffset = kBody;
   static constexpr int kTotal = 1024 + kBody + 2 * kKG * kTStages * 8;
@@ -478,19 +479,20 @@ __global__ void __launch_bounds__(128 * MT, 2)
   }
   __syncthreads();
   // Merge the key groups of each m-tile: per warp 16 x 128 fp32 partial outputs plus (m, l).
-  float* so = reinterpret_cast<float*>(base);            // [4 * MT][16][kD]
-  float* sm = so + 4 * MT * 16 * kD;                      // [4 * MT][16]
+  // Rows are padded to kMergeStride floats: the fragment stores (8 rows x 4 column pairs per
+  // half-warp phase) and the float4 reads (8 lanes per row) then hit 32 distinct banks.
+  float* so = reinterpret_cast<float*>(base);            // [4 * MT][16][kMergeStride]
+  float* sm = so + 4 * MT * 16 * kMergeStride;           // [4 * MT][16]
   float* sl = sm + 4 * MT * 16;                           // [4 * MT][16]
   {
     const int r_lo = lane / 4, c2 = (lane % 4) * 2;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int row = r_lo + h * 8;
+      float* dst = so + (warp * 16 + row) * kMergeStride + c2;
 #pragma unroll
-      for (int n = 0; n < kD / 8; ++n) {
-        so[(warp * 16 + row) * kD + n * 8 + c2] = st.o[n][2 * h];
-        so[(warp * 16 + row) * kD + n * 8 + c2 + 1] = st.o[n][2 * h + 1];
-      }
+      for (int n = 0; n < kD / 8; ++n)
+        *reinterpret_cast<float2*>(dst + n * 8) = make_float2(st.o[n][2 * h], st.o[n][2 * h + 1]);
       if ((lane % 4) == 0) {
         sm[warp * 16 + row] = st.m[h];
         sl[warp * 16 + row] = st.l[h];
@@ -498,8 +500,8 @@ __global__ void __launch_bounds__(128 * MT, 2)
     }
   }
   __syncthreads();
-  const int r = threadIdx.x / 8;             // 16 * MT rows
-  const int cbeg = (threadIdx.x % 8) * 16;   // 16 columns each
+  const int r = threadIdx.x / 8;             // 16 * MT rows, 8 threads per row
+  const int c4 = (threadIdx.x % 8) * 4;      // columns c4 + 32 j, j < 4
   const int tm = r / 16, rr = r % 16;
   const int row = row0 + r;
   if (row < rows) {
@@ -517,14 +519,20 @@ __global__ void __launch_bounds__(128 * MT, 2)
     const int tok = row / a.G, head = g * a.G + row % a.G;
     __nv_bfloat16* p = a.out + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD;
 #pragma unroll
-    for (int c = 0; c < 16; c += 2) {
-      float v0 = 0.0f, v1 = 0.0f;
+    for (int j = 0; j < kD / 32; ++j) {
+      float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
       for (int k = 0; k < kKG; ++k) {
-        v0 += wgt[k] * so[((tm * kKG + k) * 16 + rr) * kD + cbeg + c];
-        v1 += wgt[k] * so[((tm * kKG + k) * 16 + rr) * kD + cbeg + c + 1];
+        const float4 x = *reinterpret_cast<const float4*>(so + ((tm * kKG + k) * 16 + rr) * kMergeStride + c4 + 32 * j);
+        v.x += wgt[k] * x.x;
+        v.y += wgt[k] * x.y;
+        v.z += wgt[k] * x.z;
+        v.w += wgt[k] * x.w;
       }
-      *reinterpret_cast<uint32_t*>(p + cbeg + c) = pack_bf16(v0 * inv, v1 * inv);
+      uint2 packed;
+      packed.x = pack_bf16(v.x * inv, v.y * inv);
+      packed.y = pack_bf16(v.z * inv, v.w * inv);
+      *reinterpret_cast<uint2*>(p + c4 + 32 * j) = packed;
     }
   }
 }

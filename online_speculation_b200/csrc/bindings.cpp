@@ -696,6 +696,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("ep_exchange", &ep_exchange);
   m.def("set_pdl", [](bool on) { osb::pdl_enabled() = on; });
+  m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
+    if (buf.has_value() && buf->defined()) {
+      CHECK_CUDA(*buf);
+      TORCH_CHECK(buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 32 * 1024,
+                  "trace buffer must be a contiguous int64 tensor of at least 32 x 1024 values");
+      osb::gemm_trace_buffer() = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    } else {
+      osb::gemm_trace_buffer() = nullptr;
+    }
+  });
   m.def("pdl_enabled", []() -> bool { return osb::pdl_enabled(); });
 
   pybind11::class_<osb::KVManager>(m, "KVManager")

@@ -61,7 +61,18 @@ struct Args {
   // weight rows of group g start at g * M; the tile count is *gtotal (device memory).
   const int4* gtiles;
   const int* gtotal;
+  // Optional timeline (null in normal runs): per CTA kTraceSlots globaltimer stamps.
+  unsigned long long* trace;
 };
+
+// Timeline slots: 0 entry, 1 setup done, 2 first TMA issued, 3 first stage landed,
+// 4 last MMA committed, 5 first accumulator ready, 7 exit; 8..23 the loaded /
+// finished stamps of the 32-token chunks of the CTA's last tile; 24 cluster
+// partial staged, 25 cluster synchronised, 26 cluster reduction stored.
+constexpr int kTraceSlots = 32;
+__device__ __forceinline__ void trace_stamp(const Args& a, int slot) {
+  if (a.trace != nullptr) a.trace[blockIdx.x * kTraceSlots + slot] = global_ns();
+}
 
 struct TileCoord {
   int split, tile, tm, arow, row0, row_end;
@@ -309,6 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) trace_stamp(a, 0);
   pdl_trigger();
 
   if (threadIdx.x == 0) {
@@ -334,6 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) trace_stamp(a, 1);
 
   const int total = a.gtiles != nullptr ? *a.gtotal : a.tiles_m * a.tiles_n * a.splits;
 
@@ -375,6 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sA + stage * S::kABytes, &tmA, kb * kBK, c.arow, &full[stage]);
             tma_load_2d(sB + stage * S::kBBytes, &tmB, kb * kBK, c.row0, &full[stage]);
           }
+          if (issued == 0) trace_stamp(a, 2);
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -416,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (w == static_cast<int>(blockIdx.x) && kb == kb0) trace_stamp(a, 3);
           tc_fence_after();
 #pragma unroll
           for (int k = 0; k < kBK / kUmmaK; ++k) {
@@ -431,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         tc_commit(&tfull[acc]);
+        trace_stamp(a, 4);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1;
       }
@@ -451,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tile = tc.tile;
       const int tm = tc.tm;
       bool ok = mbar_wait(&tfull[acc], acc_phase, a.status, kErrEpilogueWait);
+      if (ep_tid == 0 && w == static_cast<int>(blockIdx.x)) trace_stamp(a, 5);
       // All epilogue threads must agree before touching shared state.
       if (!ok) *abort_flag = 1;
       named_barrier(1, 128);
@@ -466,12 +483,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) st[(c * 32 + j) * (kBM + 4) + r] = v[j];
         }
+        if (ep_tid == 0) trace_stamp(a, 24);
         tc_fence_before();
       } else if (a.splits == 1) {
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
           tmem_ld32(t_acc + c * 32, v);
+          if (ep_tid == 0 && c < 8) trace_stamp(a, 8 + 2 * c);
           finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, xchg, ep_tid);
+          if (ep_tid == 0 && c < 8) trace_stamp(a, 9 + 2 * c);
         }
         tc_fence_before();
         __syncwarp();
@@ -526,13 +546,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every CTA holds exactly one split of one tile (grid = tiles x cluster).
     const int tile = blockIdx.x / a.cluster;
     cluster_sync();                       // all splits staged
+    if (threadIdx.x == 0) trace_stamp(a, 25);
     if (!*abort_flag) cluster_reduce_store<BN>(a, reinterpret_cast<const float*>(smem), tile % a.tiles_m,
                                                tile / a.tiles_m);
+    if (threadIdx.x == 0) trace_stamp(a, 26);
     cluster_sync();                       // peers finished reading this CTA's tile
   }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::kTmemCols);
+    if (lane == 0) trace_stamp(a, 7);
   }
 }
 
@@ -757,6 +780,11 @@ cudaError_t grouped_tiles_launch(const int* offsets, int groups, int tiles_m, in
   return cudaGetLastError();
 }
 
+unsigned long long*& gemm_trace_buffer() {
+  static unsigned long long* buf = nullptr;
+  return buf;
+}
+
 int gemm_pick_bn(int tokens) {
   if (tokens <= 32) return 32;
   if (tokens <= 64) return 64;
@@ -819,6 +847,7 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.counters = p.counters;
   a.status = p.status;
   a.prefetch_a = p.prefetch_weights;
+  a.trace = gemm_trace_buffer();
   a.gtiles = nullptr;
   a.gtotal = nullptr;
   {

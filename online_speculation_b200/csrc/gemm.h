@@ -46,6 +46,11 @@ bool& pdl_enabled();   // programmatic dependent launch for the forward-path ker
 cudaError_t grouped_tiles_launch(const int* offsets, int groups, int tiles_m, int bn, int* tiles, int cap, int* total,
                                  cudaStream_t stream);
 int gemm_pick_bn(int tokens);
+// Timeline capture for tuning: when non-null, every later launch writes 32 globaltimer
+// slots per CTA (entry, setup, first TMA, first stage, last MMA, first accumulator,
+// epilogue done, exit, then per-chunk and cluster-epilogue stamps) into this device
+// buffer, which must hold grid x 32 values.
+unsigned long long*& gemm_trace_buffer();
 long long gemm_workspace_floats(int M, int N, int K, int sms);
 
 }  // namespace osb

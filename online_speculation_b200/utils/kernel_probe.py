@@ -62,6 +62,41 @@ def _time(body, iters: int, warmup: int, graph: bool) -> float:
     return e0.elapsed_time(e1) * 1e3 / iters
 
 
+_TRACE_SLOTS = (("entry", "setup", "first_tma", "first_stage", "last_mma", "first_acc", "unused", "exit")
+                + tuple(f"chunk{c}_{w}" for c in range(8) for w in ("loaded", "done"))
+                + ("cluster_staged", "cluster_synced", "cluster_reduced"))
+
+
+def _gemm_timeline(body) -> dict:
+    """Per-CTA stamps of one launch, in microseconds after the earliest CTA entry:
+    median and max over CTAs of every slot (entry, setup, first TMA, first stage
+    landed, last MMA committed, first accumulator ready, exit, then the loaded /
+    finished stamps of each 32-token epilogue chunk of the last tile and the
+    cluster split-K reduction stamps)."""
+    ext = K._ext.require()
+    buf = torch.zeros(32 * 1024, dtype=torch.int64, device="cuda")
+    body()
+    torch.cuda.synchronize()
+    ext.gemm_set_trace(buf)
+    try:
+        body()
+        torch.cuda.synchronize()
+    finally:
+        ext.gemm_set_trace(None)
+    t = buf.view(1024, 32).cpu()
+    t = t[t[:, 0] > 0]
+    t0 = int(t[:, 0].min())
+    rel = (t - t0).double() / 1e3
+    rel[t == 0] = float("nan")
+    res = {"ctas": int(t.shape[0])}
+    for i, name in enumerate(_TRACE_SLOTS):
+        col = rel[:, i]
+        col = col[~col.isnan()]
+        if col.numel():
+            res[name] = [round(float(col.median()), 2), round(float(col.max()), 2)]
+    return res
+
+
 class _Rotate:
     def __init__(self, items):
         self.items, self.i = items, 0
@@ -81,6 +116,8 @@ def main(argv=None) -> int:
     g.add_argument("K", type=int)
     g.add_argument("--swiglu", action="store_true")
     g.add_argument("--residual", action="store_true")
+    g.add_argument("--trace", action="store_true",
+                   help="also print the per-CTA timeline of one launch (globaltimer stamps, microseconds)")
     gr = sub.add_parser("grouped")
     for n in ("E", "M", "K", "rows"):
         gr.add_argument(n, type=int)
@@ -125,6 +162,8 @@ def main(argv=None) -> int:
         flops = 2 * a.M * a.N * a.K
         bytes_ = wb + a.N * a.K * 2 + a.N * cols * 2 * (2 if a.residual else 1)
         out.update(M=a.M, N=a.N, K=a.K, us=us, tflops=flops / us / 1e6, gbs=bytes_ / us / 1e3)
+        if a.trace:
+            out["timeline"] = _gemm_timeline(body)
     elif a.kind == "grouped":
         E, M, Kd, R = a.E, a.M, a.K, a.rows
         w = (torch.randn(E * M, Kd, device=dev) * 0.02).bfloat16()

@@ -18,7 +18,7 @@ def _rel(a, b):
 @pytest.mark.parametrize(
     "M,N,K",
     [(128, 16, 64), (256, 64, 512), (4608, 64, 3584), (3584, 256, 3584), (1000, 37, 200), (512, 300, 1024),
-     (2048, 1024, 1536), (152064 // 8, 64, 3584)],
+     (2048, 1024, 1536), (152064 // 8, 64, 3584), (1004, 40, 512), (4736, 256, 512)],
 )
 def test_gemm_matches_fp32(cuda, M, N, K):
     torch.manual_seed(0)
@@ -69,6 +69,45 @@ def test_gemm_repeated_split_counters_reset(cuda):
     for _ in range(5):
         assert _rel(ops.linear(x, w), ref) < 1e-2
     assert int(workspace.gemm_counters(cuda).abs().sum()) == 0
+
+
+_WORKSPACE_SPLIT_CHECK = """
+import torch
+from online_speculation_b200.ops import kernels as ops, workspace
+dev = torch.device("cuda", 0)
+torch.manual_seed(3)
+for M, N, K, swiglu, residual in [(3584, 256, 3584, False, True), (1024, 40, 4096, False, False),
+                                  (640, 96, 2048, True, False)]:
+    w = (torch.randn(M, K, device=dev) * 0.05).bfloat16()
+    x = torch.randn(N, K, device=dev).bfloat16()
+    if swiglu:
+        out = ops.linear(x, w, swiglu=True)
+        wf = w.float().view(-1, 2, 64, K)
+        g, u = x.float() @ wf[:, 0].reshape(-1, K).t(), x.float() @ wf[:, 1].reshape(-1, K).t()
+        ref = torch.nn.functional.silu(g) * u
+    else:
+        r = torch.randn(N, M, device=dev).bfloat16() if residual else None
+        out = ops.linear(x, w, residual=r)
+        ref = ops.linear_reference(x, w, residual=r).float()
+    torch.cuda.synchronize()
+    workspace.check_status(dev)
+    err = float((out.float() - ref).norm() / ref.norm())
+    assert err < 1e-2, (M, N, K, err)
+assert int(workspace.gemm_counters(dev).abs().sum()) == 0
+print("ok")
+"""
+
+
+def test_gemm_workspace_split_mode(cuda):
+    """Split-K through the global fp32 workspace (the last split to arrive reduces)."""
+    import os
+    import subprocess
+    import sys
+
+    env = dict(os.environ, OSB_GEMM_SPLIT_MODE="1")
+    r = subprocess.run([sys.executable, "-c", _WORKSPACE_SPLIT_CHECK], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
 
 
 def _paged_case(device, lengths, Hkv, pages_per_seq, seed=0):
