@@ -38,7 +38,8 @@ namespace {
 constexpr int kBM = 128;   // weight rows per tile (MMA M)
 constexpr int kBK = 64;    // reduction elements per stage: one 128-byte swizzle row
 constexpr int kUmmaK = 16; // K per tcgen05.mma for 16-bit inputs
-constexpr int kThreads = 192;
+constexpr int kEpiGroups = 2;                      // epilogue warpgroups, alternating 32-token chunks
+constexpr int kThreads = 64 + 128 * kEpiGroups;
 
 struct Args {
   int M, N, K;          // M = weight rows (features), N = tokens
@@ -102,12 +103,12 @@ __device__ __forceinline__ TileCoord tile_coord(const Args& a, int w) {
 
 template <int BN>
 struct Smem {
-  static constexpr int kStages = BN <= 32 ? 10 : BN <= 64 ? 8 : BN <= 128 ? 6 : 4;
+  static constexpr int kStages = BN <= 32 ? 9 : BN <= 64 ? 8 : BN <= 128 ? 6 : 4;
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kXchgBytes = 32 * (kBM + 4) * 4;
+  static constexpr int kXchgBytes = kEpiGroups * 32 * (kBM + 4) * 4;   // one transpose buffer per group
   static constexpr int kBarBytes = 256;
   static constexpr int kTotal = 1024 + kStages * kStageBytes + kBarBytes + kXchgBytes;
 };
@@ -120,7 +121,7 @@ struct Smem {
 // are grouped ahead of the stores instead of alternating with them).
 template <int BN>
 __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32], int tm, int row0, int row_end,
-                                             int chunk, int r, float* stage, int ep_tid) {
+                                             int chunk, int r, float* stage, int ep_tid, int bar) {
   const int t0 = row0 + chunk * 32;
   const bool swiglu = a.epilogue == 1;
   const int f0 = swiglu ? tm * 64 : tm * kBM;       // first output feature of this tile
@@ -129,7 +130,7 @@ __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32]
   const float b = (!swiglu && a.bias && tm * kBM + r < a.M) ? bf2f(a.bias[tm * kBM + r]) : 0.0f;
 #pragma unroll
   for (int j = 0; j < 32; ++j) stage[j * (kBM + 4) + r] = v[j] + b;
-  named_barrier(1, 128);
+  named_barrier(bar, 128);
   const int valid_t = min(32, row_end - t0);
   if (a.vec_ok) {
     // vectors of 8 features; width/8 vectors per token row
@@ -216,7 +217,7 @@ __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32]
         static_cast<__nv_bfloat16*>(a.out)[off] = f2bf(val);
     }
   }
-  named_barrier(1, 128);
+  named_barrier(bar, 128);
 }
 
 // Cluster split-K reduction.  Every CTA of the cluster holds one split's fp32
@@ -330,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], 4 * kEpiGroups);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -455,42 +456,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
     pdl_wait();   // residual / bias / output belong to the stream's data flow
+    // Warps 2..(1 + 4 * kEpiGroups): group g = (warp - 2) / 4 finishes the 32-token
+    // chunks c with c % kEpiGroups == g; every group covers the four TMEM lane quarters.
     const int quarter = warp % 4;
+    const int grp = (warp - 2) / 4;
+    const int gbar = 1 + grp;                         // named barrier of this group (128 threads)
+    constexpr int kAllEpi = 128 * kEpiGroups;
+    constexpr int kAllBar = 1 + kEpiGroups;           // named barrier of all epilogue threads
     const int r = quarter * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     int acc = 0;
     uint32_t acc_phase = 0;
-    const int ep_tid = threadIdx.x - 64;
+    const int ep_tid = (threadIdx.x - 64) % 128;    // thread index within the group
+    const bool ep_lead = threadIdx.x == 64;           // first epilogue thread of the CTA
+    float* gstage = xchg + grp * 32 * (kBM + 4);
     for (int w = blockIdx.x; w < total; w += gridDim.x) {
       const TileCoord tc = tile_coord<BN>(a, w);
       const int split = tc.split;
       const int tile = tc.tile;
       const int tm = tc.tm;
       bool ok = mbar_wait(&tfull[acc], acc_phase, a.status, kErrEpilogueWait);
-      if (ep_tid == 0 && w == static_cast<int>(blockIdx.x)) trace_stamp(a, 5);
+      if (ep_lead && w == static_cast<int>(blockIdx.x)) trace_stamp(a, 5);
       // All epilogue threads must agree before touching shared state.
       if (!ok) *abort_flag = 1;
-      named_barrier(1, 128);
+      named_barrier(kAllBar, kAllEpi);
       if (*abort_flag) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + acc * BN;
       if (a.cluster > 1) {
         // Stage this split's tile token-major into the (now idle) pipeline smem.
         float* st = reinterpret_cast<float*>(smem);
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = grp; c < BN / 32; c += kEpiGroups) {
           float v[32];
           tmem_ld32(t_acc + c * 32, v);
 #pragma unroll
           for (int j = 0; j < 32; ++j) st[(c * 32 + j) * (kBM + 4) + r] = v[j];
         }
-        if (ep_tid == 0) trace_stamp(a, 24);
+        if (ep_lead) trace_stamp(a, 24);
         tc_fence_before();
       } else if (a.splits == 1) {
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = grp; c < BN / 32; c += kEpiGroups) {
           float v[32];
           tmem_ld32(t_acc + c * 32, v);
           if (ep_tid == 0 && c < 8) trace_stamp(a, 8 + 2 * c);
-          finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, xchg, ep_tid);
+          finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, gstage, ep_tid, gbar);
           if (ep_tid == 0 && c < 8) trace_stamp(a, 9 + 2 * c);
         }
         tc_fence_before();
@@ -498,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&tempty[acc]);
       } else {
         float* part = a.workspace + (static_cast<long long>(split) * a.tiles_m * a.tiles_n + tile) * (kBM * BN);
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = grp; c < BN / 32; c += kEpiGroups) {
           float v[32];
           tmem_ld32(t_acc + c * 32, v);
 #pragma unroll
@@ -508,21 +517,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[acc]);
         __threadfence();
-        named_barrier(1, 128);
-        if (ep_tid == 0) {
+        named_barrier(kAllBar, kAllEpi);
+        if (ep_lead) {
           const int prev = atomicAdd(&a.counters[tile], 1);
           const int last = prev == a.splits - 1;
           if (last) a.counters[tile] = 0;
           *last_flag = last;
         }
-        named_barrier(1, 128);
+        named_barrier(kAllBar, kAllEpi);
         const int is_last = *last_flag;
-        named_barrier(1, 128);
+        named_barrier(kAllBar, kAllEpi);
         if (is_last) {
           __threadfence();
           const long long tile_stride = static_cast<long long>(a.tiles_m) * a.tiles_n * (kBM * BN);
           const float* base = a.workspace + static_cast<long long>(tile) * (kBM * BN);
-          for (int c = 0; c < BN / 32; ++c) {
+          for (int c = grp; c < BN / 32; c += kEpiGroups) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
@@ -531,7 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] += __ldcg(&p[(c * 32 + j) * kBM + r]);
             }
-            finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, xchg, ep_tid);
+            finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, gstage, ep_tid, gbar);
           }
         }
       }
