@@ -371,17 +371,19 @@ void divergence_grad(Tensor s, Tensor t, Tensor lse, Tensor pieces, Tensor w, in
         "divergence_grad");
 }
 
-// h += sum over ranks of the partials; x = rmsnorm(h) * w  (peer pointers as int64 addresses)
-void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows, std::vector<int64_t> pads,
-                           Tensor epoch, Tensor h, Tensor w, Tensor x, int64_t T, int64_t rank, double eps,
-                           int64_t blocks, Tensor status) {
+// h += sum over ranks of the partials; x = rmsnorm(h) * w  (peer pointers as int64 addresses).
+// pushed: parts are this rank's local receive slots, filled by the ranks' pushing GEMMs.
+void allreduce_norm_impl(std::vector<int64_t> parts, std::vector<int64_t> rows, std::vector<int64_t> pads,
+                         Tensor epoch, Tensor h, Tensor w, Tensor x, int64_t T, int64_t rank, double eps,
+                         int64_t blocks, Tensor status, bool pushed) {
   CHECK_CUDA(h);
   CHECK_ROWS(h);
   CHECK_ROWS(x);
   CHECK_DT(h, torch::kBFloat16);
   CHECK_DT(epoch, torch::kInt32);
   const int world = static_cast<int>(parts.size());
-  TORCH_CHECK(world >= 1 && world <= osb::kMaxRanks && rows.size() == parts.size() && pads.size() == parts.size(),
+  TORCH_CHECK(world >= 1 && world <= osb::kMaxRanks && (pushed || rows.size() == parts.size()) &&
+                  pads.size() == parts.size(),
               "one partial, row buffer and signal pad per rank (at most 8)");
   TORCH_CHECK(h.size(0) >= T && x.size(0) >= T && w.numel() == h.size(1), "all-reduce shapes");
   TORCH_CHECK(epoch.numel() >= 4, "the all-reduce epoch buffer holds four counters");
@@ -389,7 +391,7 @@ void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows
   osb::ArArgs a{};
   for (int q = 0; q < world; ++q) {
     a.parts[q] = reinterpret_cast<const __nv_bfloat16*>(parts[q]);
-    a.rows[q] = reinterpret_cast<__nv_bfloat16*>(rows[q]);
+    a.rows[q] = pushed ? nullptr : reinterpret_cast<__nv_bfloat16*>(rows[q]);
     a.pads[q] = reinterpret_cast<uint32_t*>(pads[q]);
   }
   a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int>());
@@ -404,8 +406,74 @@ void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows
   a.world = world;
   a.eps = static_cast<float>(eps);
   a.status = status.data_ptr<int>();
-  check(osb::allreduce_add_rmsnorm_launch(a, static_cast<int>(blocks), at::cuda::getCurrentCUDAStream()),
-        "allreduce_add_rmsnorm");
+  if (pushed)
+    check(osb::allreduce_pushed_add_rmsnorm_launch(a, static_cast<int>(blocks), at::cuda::getCurrentCUDAStream()),
+          "allreduce_pushed_add_rmsnorm");
+  else
+    check(osb::allreduce_add_rmsnorm_launch(a, static_cast<int>(blocks), at::cuda::getCurrentCUDAStream()),
+          "allreduce_add_rmsnorm");
+}
+
+void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows, std::vector<int64_t> pads,
+                           Tensor epoch, Tensor h, Tensor w, Tensor x, int64_t T, int64_t rank, double eps,
+                           int64_t blocks, Tensor status) {
+  allreduce_norm_impl(parts, rows, pads, epoch, h, w, x, T, rank, eps, blocks, status, false);
+}
+
+void allreduce_pushed_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> pads, Tensor epoch, Tensor h,
+                                  Tensor w, Tensor x, int64_t T, int64_t rank, double eps, int64_t blocks,
+                                  Tensor status) {
+  allreduce_norm_impl(parts, {}, pads, epoch, h, w, x, T, rank, eps, blocks, status, true);
+}
+
+// Row-parallel GEMM whose bf16 output tile is stored into every rank's receive slot for
+// this rank (dsts[q], row stride = M) and whose last CTA releases *epoch + 1 into
+// flags[q]; `out` is this rank's own slot (shape / stride checks only).
+void gemm_push(Tensor w, Tensor x, Tensor out, std::vector<int64_t> dsts, std::vector<int64_t> flags, Tensor epoch,
+               Tensor count, bool allow_split, Tensor workspace, Tensor counters, Tensor status,
+               bool prefetch_weights) {
+  CHECK_CUDA(w);
+  CHECK_CUDA(x);
+  CHECK_CUDA(out);
+  CHECK_DT(w, torch::kBFloat16);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_DT(out, torch::kBFloat16);
+  CHECK_DT(epoch, torch::kInt32);
+  CHECK_DT(count, torch::kInt32);
+  CHECK_ROWS(w);
+  CHECK_ROWS(x);
+  CHECK_ROWS(out);
+  TORCH_CHECK(w.size(1) == x.size(1), "reduction dimensions differ");
+  const int M = w.size(0), N = x.size(0), K = w.size(1);
+  TORCH_CHECK(out.size(0) == N && out.size(1) == M, "output shape mismatch");
+  const int world = static_cast<int>(dsts.size());
+  TORCH_CHECK(world >= 1 && world <= 8 && flags.size() == dsts.size(), "one destination and flag per rank (at most 8)");
+  c10::cuda::CUDAGuard guard(w.device());
+  osb::GemmProblem p{};
+  p.w = bf(w);
+  p.ldw = w.stride(0);
+  p.x = bf(x);
+  p.ldx = x.stride(0);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.out = out.data_ptr();
+  p.ldo = out.stride(0);
+  p.allow_split = allow_split ? 1 : 0;
+  p.workspace = workspace.data_ptr<float>();
+  p.workspace_floats = workspace.numel();
+  p.counters = counters.data_ptr<int>();
+  p.counter_slots = counters.numel();
+  p.status = status.data_ptr<int>();
+  p.prefetch_weights = prefetch_weights ? 1 : 0;
+  p.push_world = world;
+  for (int q = 0; q < world; ++q) {
+    p.push_dst[q] = reinterpret_cast<__nv_bfloat16*>(dsts[q]);
+    p.push_flags[q] = reinterpret_cast<uint32_t*>(flags[q]);
+  }
+  p.push_epoch = reinterpret_cast<const uint32_t*>(epoch.data_ptr<int>());
+  p.push_count = reinterpret_cast<unsigned int*>(count.data_ptr<int>());
+  check(osb::gemm_launch(p, at::cuda::getCurrentCUDAStream()), "tcgen05 gemm (push)");
 }
 
 // Expert-parallel MoE exchange: phase 0 dispatch (count exchange + peer stores), phase 1 combine (peer loads).
@@ -670,6 +738,8 @@ void moe_combine(Tensor y, Tensor slot_of, Tensor topk_w, Tensor h, bool accumul
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels and C++ runtime of online_speculation_b200";
   m.def("gemm", &gemm);
+  m.def("gemm_push", &gemm_push);
+  m.def("allreduce_pushed_add_rmsnorm", &allreduce_pushed_add_rmsnorm);
   m.def("attention", &attention);
   m.def("rmsnorm", &rmsnorm);
   m.def("rope_cache", &rope_cache);

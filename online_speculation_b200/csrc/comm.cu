@@ -68,6 +68,28 @@ __device__ __forceinline__ bool rank_barrier(const ArArgs& a, int slot, uint32_t
   return ok != 0;
 }
 
+// Waits (bounded) until every rank has released at least `epoch` into this rank's
+// flag words of `slot` (the pushing GEMMs publish there; nothing is signalled here).
+__device__ __forceinline__ bool wait_flags(const ArArgs& a, int slot, uint32_t epoch) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint32_t* mine = a.pads[a.rank] + slot * kMaxRanks;
+    const unsigned long long start = global_ns();
+    for (int q = 0; q < a.world && ok; ++q) {
+      while (static_cast<int>(ld_acquire_sys(mine + q) - epoch) < 0) {
+        if (global_ns() - start > kWaitLimitNs) {
+          record_error(a.status, kErrPeerWait);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
 __device__ __forceinline__ int slice_begin(int T, int world, int r) { return (T * r) / world; }
 
 // Marks this call complete once every block has finished (the next call's epoch).
@@ -89,9 +111,13 @@ __device__ __forceinline__ void finish_call(const ArArgs& a, uint32_t epoch) {
 constexpr int kOneShotThreads = 256;
 constexpr int kOneShotRegVecs = 4;   // rows up to 256 * 4 * 8 = 8192 wide stay in registers
 
+// kPushed: the partials were stored into this rank's memory by the ranks' GEMMs
+// (parts[q] are local slots) and each GEMM released the call's epoch into flag
+// slot kPushSlot; the kernel waits for those flags and reads only local memory.
+template <bool kPushed>
 __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArArgs a) {
   const uint32_t epoch = *a.epoch + 1;
-  const bool ok = rank_barrier(a, 2, epoch);
+  const bool ok = kPushed ? wait_flags(a, kPushSlot, epoch) : rank_barrier(a, 2, epoch);
   const int nvec = a.H / 8;
   __shared__ float red[33];
   if (ok) {
@@ -317,7 +343,7 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream
     // one row per block (the blocks of a row wait on remote loads; more rows in flight hide that latency)
     const int cap = 4 * blocks;
     const int grid = a.T < cap ? a.T : cap;
-    oneshot_norm_kernel<<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
+    oneshot_norm_kernel<false><<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
     return cudaGetLastError();
   }
   // every block of the two-shot kernel waits for the others between its phases: keep the grid co-resident
@@ -334,6 +360,14 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream
   int grid = blocks < a.T ? blocks : a.T;
   if (grid > resident) grid = resident;
   twoshot_norm_kernel<<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t allreduce_pushed_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
+  if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
+  const int cap = 4 * blocks;
+  const int grid = a.T < cap ? a.T : cap;
+  oneshot_norm_kernel<true><<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
   return cudaGetLastError();
 }
 

@@ -7,6 +7,9 @@
 namespace osb {
 
 constexpr int kMaxRanks = 8;
+// Flag slot (in units of kMaxRanks words of every signal pad) that the pushing
+// row-parallel GEMMs release into; slots 0..3 belong to the pull collectives.
+constexpr int kPushSlot = 4;
 
 struct ArArgs {
   const __nv_bfloat16* parts[kMaxRanks];  // every rank's partial sums [T, H] (symmetric, peer-mapped)
@@ -24,5 +27,11 @@ struct ArArgs {
 };
 
 cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream);
+
+// Reduction of partials that the ranks' GEMMs pushed into this rank's memory
+// (parts[q] = local receive slot of rank q): waits for every rank's completion
+// flag in slot kPushSlot of this rank's pad, then h += sum_q parts[q] (rank
+// order) and x = rmsnorm(h) * w in one pass over local memory.
+cudaError_t allreduce_pushed_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream);
 
 }  // namespace osb

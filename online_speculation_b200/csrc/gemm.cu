@@ -40,6 +40,7 @@ constexpr int kBK = 64;    // reduction elements per stage: one 128-byte swizzle
 constexpr int kUmmaK = 16; // K per tcgen05.mma for 16-bit inputs
 constexpr int kEpiGroups = 2;                      // epilogue warpgroups, alternating 32-token chunks
 constexpr int kThreads = 64 + 128 * kEpiGroups;
+constexpr int kPushMaxRanks = 8;
 
 struct Args {
   int M, N, K;          // M = weight rows (features), N = tokens
@@ -64,7 +65,32 @@ struct Args {
   const int* gtotal;
   // Optional timeline (null in normal runs): per CTA kTraceSlots globaltimer stamps.
   unsigned long long* trace;
+  // Tensor-parallel push (push_world > 0): the bf16 output tile is stored to every
+  // rank's receive slot for this rank (peer memory, row stride ldo) instead of `out`,
+  // and the last CTA to finish publishes *push_epoch + 1 to every rank's flag word.
+  int push_world;
+  __nv_bfloat16* push_dst[kPushMaxRanks];
+  uint32_t* push_flags[kPushMaxRanks];
+  const uint32_t* push_epoch;
+  unsigned int* push_count;
 };
+
+__device__ __forceinline__ void put_bf16x8(const Args& a, long long off, const uint4& pk) {
+  if (a.push_world == 0) {
+    *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off) = pk;
+    return;
+  }
+  for (int q = 0; q < a.push_world; ++q) *reinterpret_cast<uint4*>(a.push_dst[q] + off) = pk;
+}
+
+__device__ __forceinline__ void put_bf16(const Args& a, long long off, float v) {
+  const __nv_bfloat16 b = f2bf(v);
+  if (a.push_world == 0) {
+    static_cast<__nv_bfloat16*>(a.out)[off] = b;
+    return;
+  }
+  for (int q = 0; q < a.push_world; ++q) a.push_dst[q][off] = b;
+}
 
 // Timeline slots: 0 entry, 1 setup done, 2 first TMA issued, 3 first stage landed,
 // 4 last MMA committed, 5 first accumulator ready, 7 exit; 8..23 the loaded /
@@ -183,7 +209,7 @@ __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32]
           __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
           for (int e = 0; e < 4; ++e) pb[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
-          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + base) = pk;
+          put_bf16x8(a, base, pk);
         }
       } else {
         for (int e = 0; e < 8 && f0 + fl + e < out_cols; ++e) {
@@ -192,7 +218,7 @@ __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32]
           if (a.out_f32)
             static_cast<float*>(a.out)[base + e] = val;
           else
-            static_cast<__nv_bfloat16*>(a.out)[base + e] = f2bf(val);
+            put_bf16(a, base + e, val);
         }
       }
     }
@@ -214,7 +240,7 @@ __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32]
       if (a.out_f32)
         static_cast<float*>(a.out)[off] = val;
       else
-        static_cast<__nv_bfloat16*>(a.out)[off] = f2bf(val);
+        put_bf16(a, off, val);
     }
   }
   named_barrier(bar, 128);
@@ -285,7 +311,7 @@ __device__ __forceinline__ void cluster_reduce_store(const Args& a, const float*
         __nv_bfloat162* pb = reinterpret_cast<__nv_bfloat162*>(&pk);
 #pragma unroll
         for (int e = 0; e < 4; ++e) pb[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
-        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.out) + off) = pk;
+        put_bf16x8(a, off, pk);
       }
     } else {
       for (int e = 0; e < 8 && f + e < out_cols; ++e) {
@@ -294,7 +320,7 @@ __device__ __forceinline__ void cluster_reduce_store(const Args& a, const float*
         if (a.out_f32)
           static_cast<float*>(a.out)[off + e] = val;
         else
-          static_cast<__nv_bfloat16*>(a.out)[off + e] = f2bf(val);
+          put_bf16(a, off + e, val);
       }
     }
   }
@@ -565,6 +591,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, S::kTmemCols);
     if (lane == 0) trace_stamp(a, 7);
+  }
+  if (a.push_world > 0) {
+    // Every thread's peer stores are made visible system-wide before its CTA
+    // arrives; the last CTA to arrive releases the completion flag on every rank.
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned int prev = atomicAdd(a.push_count, 1u);
+      if (prev == gridDim.x - 1) {
+        atomicExch(a.push_count, 0u);
+        const uint32_t flag = *reinterpret_cast<const volatile uint32_t*>(a.push_epoch) + 1u;
+        __threadfence_system();
+        for (int q = 0; q < a.push_world; ++q)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.push_flags[q]), "r"(flag) : "memory");
+      }
+    }
   }
 }
 
@@ -857,6 +899,19 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.status = p.status;
   a.prefetch_a = p.prefetch_weights;
   a.trace = gemm_trace_buffer();
+  a.push_world = 0;
+  if (p.push_world > 0) {
+    if (p.push_world > kPushMaxRanks || p.out_f32 || p.residual != nullptr || p.epilogue != 0 ||
+        p.group_tiles != nullptr || p.push_epoch == nullptr || p.push_count == nullptr)
+      return cudaErrorInvalidValue;
+    a.push_world = p.push_world;
+    for (int q = 0; q < p.push_world; ++q) {
+      a.push_dst[q] = p.push_dst[q];
+      a.push_flags[q] = p.push_flags[q];
+    }
+    a.push_epoch = p.push_epoch;
+    a.push_count = p.push_count;
+  }
   a.gtiles = nullptr;
   a.gtotal = nullptr;
   {

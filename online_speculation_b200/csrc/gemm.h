@@ -36,6 +36,16 @@ struct GemmProblem {
   int groups;
   int group_tile_cap;
   int group_bn;
+  // Tensor-parallel push (push_world > 0; bf16 output, no residual / SwiGLU): the output
+  // tile goes to push_dst[q] (rank q's receive slot for this rank, row stride ldo) for
+  // every rank q instead of `out`; when the whole grid is done, *push_epoch + 1 is
+  // released (system scope) into push_flags[q] on every rank.  push_count is a device
+  // arrival counter, zero at rest.
+  int push_world;
+  __nv_bfloat16* push_dst[8];
+  uint32_t* push_flags[8];
+  const uint32_t* push_epoch;
+  unsigned int* push_count;
 };
 
 cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream);

@@ -35,7 +35,8 @@ class Collectives:
     ``partial_buffer`` / ``reduce_add_norm``.
     """
 
-    def __init__(self, group=None, *, hidden: int = 0, max_tokens: int = 0, device=None, fused: bool = True):
+    def __init__(self, group=None, *, hidden: int = 0, max_tokens: int = 0, device=None, fused: bool = True,
+                 push: bool | None = None):
         self.group = group
         self.impl = None
         if group is None:
@@ -48,11 +49,20 @@ class Collectives:
         if self.world > 1 and hidden:
             from ..parallel.symm import NcclCollectives, SymmetricCollectives
 
-            cls = SymmetricCollectives if fused else NcclCollectives
-            self.impl = cls(group, hidden, max_tokens, device)
+            if fused:
+                self.impl = SymmetricCollectives(group, hidden, max_tokens, device, push=push)
+            else:
+                self.impl = NcclCollectives(group, hidden, max_tokens, device)
 
     def partial_buffer(self, T: int, scratch: torch.Tensor) -> torch.Tensor:
         return scratch if self.impl is None else self.impl.partial_buffer(T)
+
+    def linear_into(self, x: torch.Tensor, w: torch.Tensor, part: torch.Tensor) -> torch.Tensor:
+        """Row-parallel GEMM into a buffer from :meth:`partial_buffer` (the push
+        communicator stores the tiles straight into every rank's receive slot)."""
+        if self.impl is None:
+            return K.linear(x, w, out=part, static_weights=True)
+        return self.impl.linear_into(x, w, part)
 
     def reduce_add_norm(self, part, h, w, x, eps):
         if self.impl is not None:
@@ -156,7 +166,7 @@ class ModelRunner:
         if self.comm.world == 1 and residual is not None:
             return K.linear(att.view(T, -1), wo, residual=residual, out=residual, static_weights=True)
         part = self.comm.partial_buffer(T, self._buf("part", (T, self.cfg.hidden_size)))
-        return K.linear(att.view(T, -1), wo, out=part, static_weights=True)
+        return self.comm.linear_into(att.view(T, -1), wo, part)
 
     def mlp_block(self, i: int, x: torch.Tensor, residual: torch.Tensor | None) -> torch.Tensor:
         lw = self.w.layers[i]
@@ -166,7 +176,7 @@ class ModelRunner:
         if self.comm.world == 1 and residual is not None:
             return K.linear(act, lw.w_down, residual=residual, out=residual, static_weights=True)
         part = self.comm.partial_buffer(T, self._buf("part", (T, self.cfg.hidden_size)))
-        return K.linear(act, lw.w_down, out=part, static_weights=True)
+        return self.comm.linear_into(act, lw.w_down, part)
 
     def layer_stack(self, h: torch.Tensor, meta: StepMeta, layers: range) -> torch.Tensor:
         """Run decoder layers over the residual stream ``h`` (updated in place).

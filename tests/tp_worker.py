@@ -39,10 +39,14 @@ def main():
     torch.manual_seed(0)
     seq = torch.randint(0, CFG.vocab_size, (70,))
     ref = reference_forward(CFG, {k: v.cpu() for k, v in sd.items()}, seq)
-    for fused in (False, True):
+    # NCCL baseline, fused pull all-reduce, and GEMM push + local reduction
+    for fused, push in ((False, None), (True, False), (True, True)):
         w = build_weights(CFG, sd, tp=world, rank=rank, device=dev)
         cache = KVCache(CFG.num_hidden_layers, w.heads.kv_slots, 64, dev)
-        comm = Collectives(dist.group.WORLD, hidden=CFG.hidden_size, max_tokens=1024, device=dev, fused=fused)
+        comm = Collectives(dist.group.WORLD, hidden=CFG.hidden_size, max_tokens=1024, device=dev, fused=fused,
+                           push=push)
+        if fused:
+            assert comm.impl.push == (push and world <= 4)
         r = ModelRunner(w, cache, collectives=comm, max_tokens=1024)
         G = r.q_slots // r.kv_slots
         s = cache.create()
@@ -50,11 +54,11 @@ def main():
         slots = cache.append(s, 60)
         cache.fill_table([s], table)
         out = r.forward(build_meta(dev, table, seq[:60].tolist(), list(range(60)), slots, [60], [60], [0], G))
-        assert rel(out.cpu(), ref[:60]) < 3e-2, ("prefill", fused, rel(out.cpu(), ref[:60]))
+        assert rel(out.cpu(), ref[:60]) < 3e-2, ("prefill", fused, push, rel(out.cpu(), ref[:60]))
         slots = cache.append(s, 4)
         cache.fill_table([s], table)
         out = r.forward(build_meta(dev, table, seq[60:64].tolist(), list(range(60, 64)), slots, [4], [64], [0], G))
-        assert rel(out.cpu(), ref[60:64]) < 3e-2, ("verify", fused)
+        assert rel(out.cpu(), ref[60:64]) < 3e-2, ("verify", fused, push)
         torch.cuda.synchronize()
         workspace.check_status(dev)
     # vocabulary-parallel samplers draw exactly what the unsharded kernels draw on full rows
