@@ -102,7 +102,11 @@ def estimate_masked_elbo(model: Any, *, prompt: TokenSequence, answer: TokenSequ
     corrupted[rows, cols] = mask_token_id
     targets = batch[rows, cols]
     if hasattr(model, "masked_logprobs"):
-        logp = model.masked_logprobs(corrupted, rows * L + cols, targets, cfg_scale=cfg_scale)
+        unc = None
+        if cfg_scale > 0:
+            unc = corrupted.clone()
+            unc[:, :P] = mask_token_id
+        logp = model.masked_logprobs(corrupted, rows * L + cols, targets, cfg_scale=cfg_scale, unconditional=unc)
     else:
         if cfg_scale > 0:
             unc = corrupted.clone()

@@ -60,51 +60,55 @@ class LoRAParameters:
 
 
 class _LoRALinear(torch.autograd.Function):
+    """y = x W^T (+ bias) + s (xa A^T) (B * mask)^T.  ``xa`` is the adapter's input
+    (x itself, or x after dropout); gradients flow to both."""
+
     @staticmethod
-    def forward(ctx, x, A, B, w, bias, scale, mask):
+    def forward(ctx, x, xa, A, B, w, bias, scale, mask):
         xb = x.to(torch.bfloat16).contiguous()
+        xab = xb if xa is x else xa.to(torch.bfloat16).contiguous()
         Ab = A.to(torch.bfloat16).contiguous()
         Bb = (B * mask).to(torch.bfloat16).contiguous()
-        u = K.linear(xb, Ab)                                          # [T, g r]
+        u = K.linear(xab, Ab)                                         # [T, g r]
         y = K.linear(xb, w, bias=bias)
         us = (u.float() * scale).to(torch.bfloat16)
         K.linear(us, Bb, residual=y, out=y)                           # y += s u B^T
-        ctx.save_for_backward(xb, Ab, Bb, u, w, mask)
+        ctx.save_for_backward(xab, Ab, Bb, u, w, mask)
         ctx.scale = scale
+        ctx.same = xa is x
         return y
 
     @staticmethod
     def backward(ctx, gy):
-        xb, Ab, Bb, u, w, mask = ctx.saved_tensors
+        xab, Ab, Bb, u, w, mask = ctx.saved_tensors
         s = ctx.scale
         gy = gy.to(torch.bfloat16).contiguous()
         gu = K.linear(gy, Bb.t().contiguous(), out_dtype=torch.float32) * s        # [T, g r]
         gB = K.linear(K.transpose_padded(gy), K.transpose_padded((u.float() * s).to(torch.bfloat16)),
                       out_dtype=torch.float32) * mask                               # [out, g r]
         gub = gu.to(torch.bfloat16).contiguous()
-        gA = K.linear(K.transpose_padded(gub), K.transpose_padded(xb), out_dtype=torch.float32)  # [g r, in]
+        gA = K.linear(K.transpose_padded(gub), K.transpose_padded(xab), out_dtype=torch.float32)  # [g r, in]
         gx = K.linear(gy, w.t().contiguous())
-        K.linear(gub, Ab.t().contiguous(), residual=gx, out=gx)                     # gx += gu A
-        return gx, gA, gB, None, None, None, None
+        if ctx.same:
+            K.linear(gub, Ab.t().contiguous(), residual=gx, out=gx)                 # gx += gu A
+            return gx, None, gA, gB, None, None, None, None
+        gxa = K.linear(gub, Ab.t().contiguous())
+        return gx, gxa, gA, gB, None, None, None, None
 
 
 def lora_linear(x: torch.Tensor, w: torch.Tensor, lora: LoRAParameters | None, scale: float,
                 bias: torch.Tensor | None = None, *, dropout: float = 0.0, training: bool = False) -> torch.Tensor:
-    """Frozen ``w`` (+ bias) plus the adapter; plain kernel linear when ``lora`` is None."""
+    """Frozen ``w`` (+ bias) plus the adapter; plain kernel linear when ``lora`` is None.
+
+    Dropout (training only) acts on the adapter's input, as in PEFT; the frozen
+    product always sees the undropped input and passes its gradient on.
+    """
     if lora is None:
         return K.linear(x, w, bias=bias) if x.is_cuda else K.linear_reference(x, w, bias=bias).to(torch.bfloat16)
-    if dropout > 0 and training:
-        # dropout acts on the adapter input only, as in PEFT
-        xa = torch.nn.functional.dropout(x.float(), dropout, True).to(x.dtype)
-        base = K.linear(x, w, bias=bias) if x.is_cuda else K.linear_reference(x, w, bias=bias).to(torch.bfloat16)
-        return base + _adapter_only(xa, lora, scale)
+    xa = torch.nn.functional.dropout(x.float(), dropout, True).to(x.dtype) if dropout > 0 and training else x
     if x.is_cuda:
-        return _LoRALinear.apply(x, lora.A, lora.B, w, bias, float(scale), lora.block_mask)
+        return _LoRALinear.apply(x, xa, lora.A, lora.B, w, bias, float(scale), lora.block_mask)
     y = x.float() @ w.float().t()
     if bias is not None:
         y = y + bias.float()
-    return (y + scale * (x.float() @ lora.A.t()) @ (lora.B * lora.block_mask).t()).to(torch.bfloat16)
-
-
-def _adapter_only(x, lora: LoRAParameters, scale: float):
-    return (scale * (x.float() @ lora.A.t()) @ (lora.B * lora.block_mask).t()).to(torch.bfloat16)
+    return (y + scale * (xa.float() @ lora.A.t()) @ (lora.B * lora.block_mask).t()).to(torch.bfloat16)

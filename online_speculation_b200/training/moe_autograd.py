@@ -132,6 +132,50 @@ def moe_ffn_autograd(x: torch.Tensor, h: torch.Tensor, experts: FrozenExperts, a
     return _MoEFFN.apply(x, h, anchor, experts)
 
 
+def moe_ffn_lora(x: torch.Tensor, h: torch.Tensor, ex: FrozenExperts, gu_adapters, down_adapters, scale: float, *,
+                 dropout: float = 0.0, training: bool = False) -> torch.Tensor:
+    """h + MoE(x) with LoRA adapters on every expert's gate / up / down projection.
+
+    ``gu_adapters[e]`` adapts expert e's interleaved gate / up rows (its B is
+    block-masked so gate rows use the gate block of A and up rows the up block),
+    ``down_adapters[e]`` its down projection; either list may hold None.  Routing
+    is the top-k of the router softmax (renormalised when the model says so) with
+    gradients through the routing weights; the experts run one after another on
+    their routed rows through the differentiable LoRA linear (tcgen05 GEMMs on
+    the GPU), as PEFT-adapted expert modules run in the reference's LLaDA-MoE
+    (configs/gsm8k_llada_moe_3090.toml ``[vrpo_lora]`` targets gate/up/down_proj).
+    """
+    from .lora import lora_linear
+
+    T, E, Fd, H, k = x.shape[0], ex.E, ex.F, ex.H, ex.k
+    logits = x.float() @ ex.router.float().t()
+    p = torch.softmax(logits, -1)
+    order = torch.sort(-p.detach(), dim=-1, stable=True).indices[:, :k]
+    w = p.gather(1, order)
+    if ex.renorm:
+        w = w / w.sum(1, keepdim=True)
+    flat = order.reshape(-1)
+    perm = torch.sort(flat, stable=True).indices
+    counts = torch.bincount(flat, minlength=E).tolist()      # one host read per layer
+    tok, slot = perm // k, perm % k
+    out = h.float()
+    xb = x.to(torch.bfloat16)
+    start = 0
+    for e, c in enumerate(counts):
+        if c == 0:
+            continue
+        rows, slots = tok[start:start + c], slot[start:start + c]
+        start += c
+        gu = lora_linear(xb[rows], ex.w_gu[e * 2 * Fd:(e + 1) * 2 * Fd], gu_adapters[e], scale, dropout=dropout,
+                         training=training)
+        g, u = _swiglu_split(gu)
+        act = (F.silu(g.float()) * u.float()).reshape(c, Fd).to(torch.bfloat16)
+        ye = lora_linear(act, ex.w_down[e * H:(e + 1) * H], down_adapters[e], scale, dropout=dropout,
+                         training=training)
+        out = out.index_add(0, rows, ye.float() * w[rows, slots][:, None])
+    return out.to(torch.bfloat16)
+
+
 def _moe_reference_autograd(x, h, ex: FrozenExperts):
     """Plain PyTorch (CPU) version with autograd through routing weights."""
     p = torch.softmax(x.float() @ ex.router.float().t(), -1)

@@ -41,9 +41,14 @@ from ..dllm.vrpo import AdapterDisabledReference, estimate_vrpo_preference_loss
 from ..models.moe import MoEConfig, MoEWeights
 from ..ops import kernels as K
 from .lora import LoRAConfig, LoRAParameters, lora_linear
-from .moe_autograd import FrozenExperts, moe_ffn_autograd
+from .moe_autograd import FrozenExperts, moe_ffn_autograd, moe_ffn_lora
 
 FORMAT = "vrpo-lora-v1"
+
+# The reference's [vrpo_lora] target modules (configs/gsm8k_llada_moe_3090.toml): the
+# attention projections and every expert's gate / up / down projection.
+VRPO_TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+SUPPORTED_TARGETS = frozenset(VRPO_TARGETS)
 
 
 def _rms(x, w, eps):
@@ -58,11 +63,18 @@ def _rope(t, cos, sin):
 
 
 class LoRAMoEPolicy:
-    """Masked-diffusion policy = frozen MoE weights + LoRA adapters on the attention projections."""
+    """Masked-diffusion policy = frozen MoE weights + LoRA adapters.
 
-    def __init__(self, weights: MoEWeights, lora: LoRAConfig = LoRAConfig(), *, seed: int = 0,
-                 head_chunk_rows: int = 2048):
-        unknown = set(lora.targets) - {"q_proj", "k_proj", "v_proj", "o_proj"}
+    Targets: the attention projections (q / k / v on the fused QKV weight with
+    per-projection blocks, o) and every expert's gate / up (one block-masked
+    adapter per expert on the interleaved gate / up rows) and down projection.
+    The default is the reference's full target list (``VRPO_TARGETS``, r 16,
+    alpha 32, dropout 0.05).
+    """
+
+    def __init__(self, weights: MoEWeights, lora: LoRAConfig = LoRAConfig(dropout=0.05, targets=VRPO_TARGETS), *,
+                 seed: int = 0, head_chunk_rows: int = 2048):
+        unknown = set(lora.targets) - SUPPORTED_TARGETS
         if unknown:
             raise ValueError(f"LoRA targets not supported on this model: {sorted(unknown)}")
         self.w = weights
@@ -84,6 +96,14 @@ class LoRAMoEPolicy:
                 layer["qkv"] = _qkv_adapter(H, nq, nkv, D, lora.rank, qkv_targets, self.device, gen)
             if "o_proj" in lora.targets:
                 layer["o"] = LoRAParameters(nq * D, H, lora.rank, device=self.device, generator=gen)
+            gu_targets = [t for t in ("gate_proj", "up_proj") if t in lora.targets]
+            for e in range(c.num_experts):
+                if gu_targets:
+                    layer[f"gu{e}"] = _gate_up_adapter(H, c.moe_intermediate_size, lora.rank, gu_targets, self.device,
+                                                       gen)
+                if "down_proj" in lora.targets:
+                    layer[f"down{e}"] = LoRAParameters(c.moe_intermediate_size, H, lora.rank, device=self.device,
+                                                       generator=gen)
             self.adapters.append(layer)
         self._flatten()
         self.experts = [FrozenExperts(lw.router, lw.w_gu, lw.w_down, c.num_experts_per_tok, c.norm_topk_prob)
@@ -142,6 +162,7 @@ class LoRAMoEPolicy:
         self._refresh_views()
         s = self.lora.scale
         layers = []
+        E, Fd, H = self.cfg.num_experts, self.cfg.moe_intermediate_size, self.cfg.hidden_size
         for lw, ad in zip(self.w.layers, self.adapters):
             upd = {}
             for key, name in (("qkv", "w_qkv"), ("o", "w_o")):
@@ -150,6 +171,14 @@ class LoRAMoEPolicy:
                     w = getattr(lw, name)
                     delta = s * ((a.B * a.block_mask) @ a.A)
                     upd[name] = (w.float() + delta.to(w.device)).to(w.dtype).contiguous()
+            for prefix, name, rows in (("gu", "w_gu", 2 * Fd), ("down", "w_down", H)):
+                if f"{prefix}0" not in ad:
+                    continue
+                w = getattr(lw, name).float().clone()
+                for e in range(E):
+                    a = ad[f"{prefix}{e}"]
+                    w[e * rows:(e + 1) * rows] += s * ((a.B * a.block_mask) @ a.A).to(w.device)
+                upd[name] = w.to(getattr(lw, name).dtype).contiguous()
             layers.append(dataclasses.replace(lw, **upd))
         return dataclasses.replace(self.w, layers=layers)
 
@@ -181,17 +210,77 @@ class LoRAMoEPolicy:
             h = h + lora_linear(att, lw.w_o, ad.get("o") if use else None, s, dropout=drop,
                                 training=self.training).view(B, L, -1)
             x = _rms(h, lw.post_norm, eps).reshape(B * L, -1)
-            h = moe_ffn_autograd(x, h.reshape(B * L, -1), ex, self.anchor).view(B, L, -1)
+            if "gu0" in ad or "down0" in ad:
+                # with the adapters off (the reference policy) the same expert path runs without
+                # the LoRA terms, so policy and reference agree bit for bit while B is zero
+                E = self.cfg.num_experts
+                h = moe_ffn_lora(x, h.reshape(B * L, -1), ex,
+                                 [ad.get(f"gu{e}") if use else None for e in range(E)],
+                                 [ad.get(f"down{e}") if use else None for e in range(E)], s, dropout=drop,
+                                 training=self.training).view(B, L, -1)
+            else:
+                h = moe_ffn_autograd(x, h.reshape(B * L, -1), ex, self.anchor).view(B, L, -1)
         return h.reshape(B * L, -1)
 
     def masked_logprobs(self, tokens: torch.Tensor, flat_index: torch.Tensor, targets: torch.Tensor, *,
-                        cfg_scale: float = 0.0) -> torch.Tensor:
-        """log p(target) at the given flattened (row * L + position) indices."""
+                        cfg_scale: float = 0.0, unconditional: torch.Tensor | None = None) -> torch.Tensor:
+        """log p(target) at the given flattened (row * L + position) indices.
+
+        With ``cfg_scale`` > 0 the logits are classifier-free guided,
+        u + (s + 1)(c - u), where u comes from ``unconditional`` (the same rows
+        with the prompt masked), as in the reference's ELBO.
+        """
+        idx = flat_index.to(self.device)
         h = self.hidden(tokens)
-        sel = _rms(h[flat_index.to(self.device)], self.w.final_norm, self.cfg.rms_norm_eps)
-        if cfg_scale > 0:
-            raise NotImplementedError("classifier-free guidance inside the VRPO ELBO is not supported")
-        return K.head_logprob(sel, self.w.head, targets.to(self.device), chunk_rows=self.head_chunk_rows)
+        sel = _rms(h[idx], self.w.final_norm, self.cfg.rms_norm_eps)
+        if cfg_scale <= 0:
+            return K.head_logprob(sel, self.w.head, targets.to(self.device), chunk_rows=self.head_chunk_rows)
+        if unconditional is None:
+            raise ValueError("classifier-free guidance needs the unconditional (prompt-masked) rows")
+        hu = self.hidden(unconditional)
+        sel_u = _rms(hu[idx], self.w.final_norm, self.cfg.rms_norm_eps)
+        return _guided_logprob(sel, sel_u, self.w.head, targets.to(self.device), float(cfg_scale),
+                               self.head_chunk_rows)
+
+
+def _guided_chunk(c: torch.Tensor, u: torch.Tensor, head: torch.Tensor, t: torch.Tensor, s: float) -> torch.Tensor:
+    lc = (c.to(torch.bfloat16) @ head.t()).float()
+    lu = (u.to(torch.bfloat16) @ head.t()).float()
+    return (lu + (s + 1.0) * (lc - lu)).log_softmax(-1).gather(1, t[:, None].long()).squeeze(1)
+
+
+def _guided_logprob(c: torch.Tensor, u: torch.Tensor, head: torch.Tensor, targets: torch.Tensor, s: float,
+                    chunk: int) -> torch.Tensor:
+    """log softmax(u + (s + 1)(c - u))[target] per row, logits from hidden rows c / u and
+    the head; row chunks are recomputed in the backward instead of keeping [rows, V]."""
+    from torch.utils.checkpoint import checkpoint
+
+    outs = []
+    for i in range(0, c.shape[0], chunk):
+        outs.append(checkpoint(_guided_chunk, c[i:i + chunk], u[i:i + chunk], head, targets[i:i + chunk], s,
+                               use_reentrant=False))
+    return torch.cat(outs)
+
+
+def _gate_up_adapter(H, Fd, r, targets, device, gen) -> LoRAParameters:
+    """One expert's gate / up adapter on the interleaved [64 gate | 64 up] rows of its
+    fused weight: A stacks a gate and an up block [2r, H]; B [2F, 2r] is masked so
+    gate rows read the gate block and up rows the up block (a projection that is not
+    a target keeps all-zero rows)."""
+    a = LoRAParameters(H, 2 * Fd, r, groups=1, device=device, generator=gen)
+    a.A = torch.cat([((torch.rand(r, H, generator=gen) * 2 - 1) / math.sqrt(H)) for _ in range(2)]).to(
+        device).requires_grad_(True)
+    a.B = torch.zeros(2 * Fd, 2 * r, device=device, requires_grad=True)
+    row = torch.arange(2 * Fd, device=device)
+    is_up = (row % 128) >= 64
+    mask = torch.zeros(2 * Fd, 2 * r, device=device)
+    if "gate_proj" in targets:
+        mask[~is_up, :r] = 1
+    if "up_proj" in targets:
+        mask[is_up, r:] = 1
+    a.block_mask = mask
+    a.groups = 2
+    return a
 
 
 def _qkv_adapter(H, nq, nkv, D, r, targets, device, gen) -> LoRAParameters:
@@ -309,4 +398,4 @@ def _jsonable(x):
     return x
 
 
-__all__ = ["FORMAT", "LoRAMoEPolicy", "VRPOTrainer", "VRPOTrainingConfig"]
+__all__ = ["FORMAT", "LoRAMoEPolicy", "VRPO_TARGETS", "VRPOTrainer", "VRPOTrainingConfig"]

@@ -131,6 +131,56 @@ def test_lora_linear_forward_backward_matches_fp32():
         assert (got - ref).norm() / ref.norm() < 0.02
 
 
+def test_lora_linear_dropout_keeps_the_base_gradient():
+    """With adapter dropout the frozen product still passes its input gradient on."""
+    from online_speculation_b200.training.lora import LoRAParameters, lora_linear
+
+    torch.manual_seed(5)
+    x = torch.randn(96, 256, device="cuda").bfloat16().requires_grad_(True)
+    w = (torch.randn(128, 256, device="cuda") * 0.05).bfloat16()
+    lo = LoRAParameters(256, 128, 8, device="cuda")
+    with torch.no_grad():
+        lo.B.normal_(0, 0.1)
+    torch.manual_seed(11)
+    y = lora_linear(x, w, lo, 2.0, dropout=0.3, training=True)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    xf = x.detach().float().requires_grad_(True)
+    A = lo.A.detach().clone().requires_grad_(True)
+    B = lo.B.detach().clone().requires_grad_(True)
+    torch.manual_seed(11)
+    xa = torch.nn.functional.dropout(xf, 0.3, True)      # the same mask (same generator state, same call)
+    yf = xf @ w.float().t() + 2.0 * (xa @ A.t()) @ (B * lo.block_mask).t()
+    yf.backward(gy.float())
+    assert (y.float() - yf).norm() / yf.norm() < 0.01
+    for got, ref in ((x.grad.float(), xf.grad), (lo.A.grad, A.grad), (lo.B.grad, B.grad)):
+        assert (got - ref).norm() / ref.norm() < 0.02
+
+
+def test_vrpo_expert_adapters_on_gpu():
+    """Expert gate / up / down adapters: GPU and CPU training steps agree."""
+    from online_speculation_b200.dllm.config import VRPOSamplingConfig
+    from online_speculation_b200.models.moe import PRESETS, build_weights, random_state_dict
+    from online_speculation_b200.training.lora import LoRAConfig
+    from online_speculation_b200.training.vrpo import VRPO_TARGETS, LoRAMoEPolicy, VRPOTrainer, VRPOTrainingConfig
+
+    cfg = PRESETS["tiny-moe"]
+    sd = random_state_dict(cfg, seed=7)
+    lora = LoRAConfig(rank=8, targets=VRPO_TARGETS)
+    gpu = LoRAMoEPolicy(build_weights(cfg, sd, device="cuda"), lora)
+    cpu = LoRAMoEPolicy(build_weights(cfg, sd, device="cpu"), lora)
+    g = torch.Generator().manual_seed(2)
+    pairs = [tuple(tuple(torch.randint(0, 500, (n,), generator=g).tolist()) for n in (32, 32, 32))]
+    conf = VRPOTrainingConfig(learning_rate=1e-3, gradient_accumulation_steps=1,
+                              sampling=VRPOSamplingConfig(timestep_samples=4))
+    tg, tc = VRPOTrainer(gpu, pairs, conf), VRPOTrainer(cpu, pairs, conf)
+    rg, rc = tg.train_step(), tc.train_step()
+    assert rg["loss"] == pytest.approx(math.log(2), abs=1e-4)
+    assert rg["grad_norm"] == pytest.approx(rc["grad_norm"], rel=0.1)
+    r2 = tg.train_step()
+    assert math.isfinite(r2["loss"]) and r2["preference_score"] != 0.0
+
+
 def test_moe_autograd_backward_matches_reference():
     from online_speculation_b200.training.moe_autograd import FrozenExperts, _moe_reference_autograd, \
         moe_ffn_autograd

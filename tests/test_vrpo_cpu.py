@@ -13,7 +13,7 @@ from online_speculation_b200.dllm.vrpo import (estimate_masked_elbo, estimate_vr
                                                sample_vrpo_mask_plan, vrpo_forward_token_slots)
 from online_speculation_b200.models.moe import PRESETS, build_weights, random_state_dict
 from online_speculation_b200.training.lora import LoRAConfig
-from online_speculation_b200.training.vrpo import LoRAMoEPolicy, VRPOTrainer, VRPOTrainingConfig
+from online_speculation_b200.training.vrpo import VRPO_TARGETS, LoRAMoEPolicy, VRPOTrainer, VRPOTrainingConfig
 
 
 def test_mask_plan_layout():
@@ -103,3 +103,115 @@ def test_preference_pair_selection():
     assert q.chosen == "gold" and q.chosen_source == "dataset_reference_completion"
     with pytest.raises(ValueError):
         select_scored_preference_pair(candidate_texts=["a"], candidate_rewards=[float("nan")])
+
+
+def _expert_policy(seed=0, targets=VRPO_TARGETS):
+    cfg = PRESETS["tiny-moe"]
+    return LoRAMoEPolicy(build_weights(cfg, random_state_dict(cfg, seed=seed), device="cpu"),
+                         LoRAConfig(rank=4, targets=targets))
+
+
+def test_expert_adapters_default_targets_and_gradients():
+    cfg = PRESETS["tiny-moe"]
+    pol = LoRAMoEPolicy(build_weights(cfg, random_state_dict(cfg, seed=0), device="cpu"))
+    assert pol.lora.targets == VRPO_TARGETS and pol.lora.dropout == 0.05 and pol.lora.rank == 16
+    assert {f"gu{e}" for e in range(cfg.num_experts)} <= set(pol.adapters[0])
+    pol = _expert_policy()
+    from online_speculation_b200.dllm.vrpo import AdapterDisabledReference
+
+    est = estimate_vrpo_preference_loss(pol, AdapterDisabledReference(pol), prompt=(1, 2, 3), chosen=(4, 5, 6, 7),
+                                        rejected=(8, 9, 10, 11), mask_token_id=511,
+                                        config=VRPOSamplingConfig(timestep_samples=2), beta=0.1)
+    assert float(est.loss) == pytest.approx(math.log(2), abs=1e-6)
+    est.loss.backward()
+    # B starts at zero, so only the B blocks of routed experts receive gradient at initialisation
+    got = 0.0
+    for layer in pol.adapters:
+        for e in range(cfg.num_experts):
+            for key in (f"gu{e}", f"down{e}"):
+                a = layer[key]
+                off = next(o for (ad, name, o, shape) in pol._views if ad is a and name == "B")
+                got += float(pol.flat.grad[off:off + a.B.numel()].abs().sum())
+    assert got > 0
+
+
+def test_expert_adapters_fold_into_merged_weights():
+    torch.manual_seed(0)
+    pol = _expert_policy(seed=2)
+    with torch.no_grad():
+        pol.flat.add_(torch.randn_like(pol.flat) * 0.05)      # non-zero B everywhere
+    pol.eval()
+    tokens = torch.randint(0, 500, (2, 12))
+    with torch.no_grad():
+        got = pol.hidden(tokens).float()
+    merged = LoRAMoEPolicy(pol.merged_weights(), LoRAConfig(rank=4, targets=("o_proj",)))
+    merged.eval()
+    with torch.no_grad(), merged.disable_adapter():
+        want = merged.hidden(tokens).float()
+    assert float((got - want).norm() / want.norm()) < 5e-2    # bf16 rounding accumulated over the layers
+
+
+def test_expert_adapters_layer_matches_folded_weights():
+    """One MoE layer: adapted experts == the same experts with W + s (B * mask) A folded in."""
+    from online_speculation_b200.training.moe_autograd import FrozenExperts, moe_ffn_lora
+
+    torch.manual_seed(1)
+    cfg = PRESETS["tiny-moe"]
+    pol = _expert_policy(seed=3)
+    with torch.no_grad():
+        pol.flat.copy_(torch.randn_like(pol.flat) * 0.05)
+    pol.eval()
+    pol._refresh_views()
+    lw, mlw, ad = pol.w.layers[0], pol.merged_weights().layers[0], pol.adapters[0]
+    E = cfg.num_experts
+    ex = FrozenExperts(lw.router, lw.w_gu, lw.w_down, cfg.num_experts_per_tok, cfg.norm_topk_prob)
+    exm = FrozenExperts(mlw.router, mlw.w_gu, mlw.w_down, cfg.num_experts_per_tok, cfg.norm_topk_prob)
+    x = torch.randn(16, cfg.hidden_size).bfloat16()
+    h = torch.zeros(16, cfg.hidden_size).bfloat16()
+    with torch.no_grad():
+        a = moe_ffn_lora(x, h, ex, [ad[f"gu{e}"] for e in range(E)], [ad[f"down{e}"] for e in range(E)],
+                         pol.lora.scale).float()
+        b = moe_ffn_lora(x, h, exm, [None] * E, [None] * E, pol.lora.scale).float()
+    assert float((a - b).norm() / b.norm()) < 1.5e-2
+
+
+def test_expert_gate_only_target_masks_up_rows():
+    pol = _expert_policy(targets=("gate_proj",))
+    a = pol.adapters[0]["gu0"]
+    rows = torch.arange(a.block_mask.shape[0])
+    up = (rows % 128) >= 64
+    assert float(a.block_mask[up].abs().sum()) == 0 and float(a.block_mask[~up][:, :4].min()) == 1
+    assert "down0" not in pol.adapters[0] and "qkv" not in pol.adapters[0]
+
+
+def test_policy_elbo_with_classifier_free_guidance_matches_full_logits():
+    from online_speculation_b200.training.vrpo import _rms
+
+    pol = _policy(seed=4)
+    with torch.no_grad():
+        pol.flat.add_(torch.randn_like(pol.flat) * 0.05)
+    pol.eval()
+
+    class Full:
+        """The same policy exposed as full-vocabulary logits (the generic ELBO path)."""
+
+        def parameters(self):
+            return iter([pol.flat])
+
+        def __call__(self, t):
+            class O:
+                pass
+            o = O()
+            B, L = t.shape
+            h = _rms(pol.hidden(t), pol.w.final_norm, pol.cfg.rms_norm_eps)
+            o.logits = (h.float() @ pol.w.head.float().t()).view(B, L, -1)
+            return o
+
+    plan = sample_vrpo_mask_plan(5, VRPOSamplingConfig(timestep_samples=3), np.random.default_rng(2))
+    kw = dict(prompt=(1, 2, 3), answer=(4, 5, 6, 7, 8), mask_token_id=511, plan=plan, cfg_scale=1.5)
+    got = estimate_masked_elbo(pol, **kw)
+    want = estimate_masked_elbo(Full(), **kw)
+    assert float(got) == pytest.approx(float(want), rel=2e-2)
+    assert float(got) != pytest.approx(float(estimate_masked_elbo(pol, **dict(kw, cfg_scale=0.0))), rel=1e-4)
+    got.backward()
+    assert torch.isfinite(pol.flat.grad).all() and pol.flat.grad.abs().sum() > 0
