@@ -23,12 +23,25 @@ been trained:
   publishes when every paired throughput ratio clears ``publish_margin``
   (falling back to AR when the published version stops beating AR).
 
+Live validation policies (one at a time) replace the gate-prompt probe while
+the service still answers autoregressively:
+
+* ``reuse_ar_prefix``: the delivered AR answer's first ``probe_tokens`` outputs
+  are timed as the reference; the candidate answers the same prompt and seed for
+  that many tokens; ``live_probe_requests`` such trials of one learning version
+  are pooled into one decision;
+* ``full_answer_screen``: the candidate is screened on delivered answers with
+  the exact conditional work law (``virtual_work.estimate_trace``) against the
+  measured answer time (``FullAnswerGate``); a screen that clears its margin
+  earns one fresh paired full-request confirmation, which decides publication.
+  With ``reuse_speculative_answers`` the screen continues after publication
+  against the serving speculative version.
+
 ``state_dict`` / ``load_state_dict`` (format ``cold-start-research-v1``) keep the
 request-boundary state: masters, optimizer, serving weights, replay with its
-random states, counters and the budget.
+random states, counters, pending live evidence and the budget.
 
-Reference behaviour: online-speculation/ablation/src/blockspec_ablation/cold_start.py:42-663
-(the AR-prefix live trials and the full-answer screening gate are not built).
+Reference behaviour: online-speculation/ablation/src/blockspec_ablation/cold_start.py:42-663.
 """
 
 from __future__ import annotations
@@ -45,6 +58,7 @@ from .fitting import FitConfig, frozen_fingerprint
 from .generation import MaskedAttentionBranch, ProposalSampler, generate, generate_ar
 from .sampling import SamplingConfig
 from .training import distillation_update, sample_anchors
+from .virtual_work import FullAnswerGate, TraceSupportError, estimate_trace
 
 
 def _sync(model):
@@ -191,9 +205,25 @@ class ServiceConfig:
     initial_step_estimate: float = 0.5
     seed: int = 731
     initial_probe_factor: float = 2.0
+    reuse_ar_prefix: bool = False
+    live_probe_requests: int = 1
+    full_answer_screen: bool = False
+    reuse_speculative_answers: bool = False
+    screen_requests: int = 2
+    screen_margin: float = 1.02
+    initial_screen_estimate: float = 0.4
 
     def __post_init__(self):
         TimeBudget(self.fraction)
+        flags = (self.reuse_ar_prefix, self.full_answer_screen, self.reuse_speculative_answers)
+        if any(type(f) is not bool for f in flags) or (self.reuse_ar_prefix and self.full_answer_screen):
+            raise ValueError("select at most one explicit live validation policy")
+        if self.reuse_speculative_answers and not self.full_answer_screen:
+            raise ValueError("reusing speculative answers requires full-answer screening")
+        FullAnswerGate(self.screen_requests, self.screen_margin, self.initial_screen_estimate)
+        if (type(self.live_probe_requests) is not int or self.live_probe_requests < 1
+                or (self.live_probe_requests > 1 and not self.reuse_ar_prefix)):
+            raise ValueError("several pooled live trials require AR-prefix validation")
         if (min(self.replay_records, self.probe_every, self.probe_tokens) < 1
                 or not math.isfinite(self.publish_margin) or self.publish_margin <= 1
                 or not math.isfinite(self.initial_step_estimate) or self.initial_step_estimate <= 0
@@ -216,6 +246,8 @@ class ColdStartService:
 
     def __init__(self, model, fit: FitConfig, config: ServiceConfig = ServiceConfig(), *, gate_prompts=(),
                  sampling: SamplingConfig = SamplingConfig(1.0)):
+        if (config.reuse_ar_prefix or config.full_answer_screen) and not gate_prompts:
+            raise ValueError("gate prompts are required for the trials after publication")
         _sync(model)
         t0 = time.perf_counter()
         self.learner = FullBlockLearner(model, fit)
@@ -232,6 +264,10 @@ class ColdStartService:
         self.probe_estimate = 0.0
         self.tokens = self.requests = 0
         self.last_probe = None
+        self.pending_live: list[dict] = []
+        self.full_gate = (FullAnswerGate(config.screen_requests, config.screen_margin, config.initial_screen_estimate,
+                                         reuse_speculative=config.reuse_speculative_answers)
+                          if config.full_answer_screen else None)
         _sync(model)
         self.budget.charge("setup", time.perf_counter() - t0)
 
@@ -244,11 +280,120 @@ class ColdStartService:
             _sync(self.model)
             self.budget.charge(kind, time.perf_counter() - t0)
 
-    def _generate(self, prompt, tokens, *, speculative, seed):
+    def _generate(self, prompt, tokens, *, speculative, seed, prefix_tokens=None):
         g = torch.Generator(device=prompt.device).manual_seed(seed)
+        kw = {} if prefix_tokens is None else {"prefix_tokens": prefix_tokens}
         fn = generate if speculative else generate_ar
         return fn(self.branch, prompt, tokens, sampling=self.sampling, eos_id=self.model.config.eos_token_id,
-                  generator=g, sampler=self.sampler)
+                  generator=g, sampler=self.sampler, **kw)
+
+    # ---- live validation on delivered requests ----
+    def _live_prefix(self, prompt, reference, seed) -> dict:
+        """Candidate vs the delivered AR answer's timed prefix (same prompt and seed, so the
+        candidate's exact sampler reproduces that prefix)."""
+        with self.learner.candidate():
+            cand = self._generate(prompt, reference.prefix_tokens, speculative=True, seed=seed)
+        row = {"step": self.learner.steps, "reference_tokens": reference.prefix_tokens,
+               "reference_seconds": reference.prefix_seconds, "candidate_tokens": len(cand.tokens),
+               "candidate_seconds": cand.seconds}
+        if any(r["step"] != row["step"] for r in self.pending_live):
+            raise RuntimeError("pooled prefix trials require one learning version")
+        self.pending_live.append(row)
+        keys = ("reference_tokens", "reference_seconds", "candidate_tokens", "candidate_seconds")
+        tot = {k: sum(r[k] for r in self.pending_live) for k in keys}
+        ratio = (tot["candidate_tokens"] / tot["candidate_seconds"]) / (tot["reference_tokens"] /
+                                                                          tot["reference_seconds"])
+        ratios = [(r["candidate_tokens"] / r["candidate_seconds"]) / (r["reference_tokens"] / r["reference_seconds"])
+                  for r in self.pending_live]
+        complete = len(self.pending_live) == self.config.live_probe_requests
+        out = {**row, **tot, "reference_kind": "delivered_ar_prefix", "paired_ratios": ratios, "ratio": ratio,
+               "candidate_over_ar": ratio, "probe_requests": len(self.pending_live), "complete": complete,
+               "passed": complete and ratio >= self.config.publish_margin, "fallback": False}
+        if complete:
+            self.pending_live = []
+        return out
+
+    def _screen(self, prompt, reference, tokens, seed) -> dict:
+        with self.learner.candidate():
+            t = estimate_trace(self.branch, prompt, prompt.new_tensor(reference.tokens), output_budget=tokens,
+                               prefill_seconds=reference.prefix_seconds, sampler=self.sampler,
+                               sampling=self.sampling, eos_id=self.model.config.eos_token_id,
+                               generator=torch.Generator(device=prompt.device).manual_seed(seed + 300000))
+        return {"step": self.learner.steps, "stage": "screen",
+                "reference_kind": "delivered_speculative_full" if self.speculating else "delivered_ar_full",
+                "reference_step": self.learner.serving_step if self.speculating else 0,
+                "reference_tokens": len(reference.tokens),
+                "reference_seconds": reference.seconds - reference.prefix_capture_seconds,
+                "predicted_seconds": t.predicted_seconds, "virtual_forwards": float(t.work.decode_forwards),
+                "evaluation_seconds": t.measured_seconds, "score_seconds": t.score_seconds,
+                "calibration_seconds": t.calibration_seconds}
+
+    def _confirm(self, prompt, reference, tokens, seed) -> dict:
+        pair = {}
+        names = ["candidate", "ar"] if self.speculating else ["candidate"]
+        if self.requests % 2:
+            names.reverse()
+        for name in names:
+            if name == "candidate":
+                with self.learner.candidate():
+                    pair[name] = self._generate(prompt, tokens, speculative=True, seed=seed)
+            else:
+                pair[name] = self._generate(prompt, tokens, speculative=False, seed=seed)
+        cand, ar = pair["candidate"], pair.get("ar", reference)
+        ratio, vs_ar = cand.tps / reference.tps, cand.tps / ar.tps
+        return {"step": self.learner.steps, "stage": "confirmation",
+                "reference_kind": "delivered_speculative_full" if self.speculating else "delivered_ar_full",
+                "ratio": ratio, "candidate_over_ar": vs_ar, "paired_ratios": [ratio], "complete": True,
+                "passed": min(ratio, vs_ar) >= self.config.publish_margin,
+                "fallback": self.speculating and reference.tps < ar.tps, "ar_tps": ar.tps,
+                "reference_tokens": len(reference.tokens), "reference_seconds": reference.seconds,
+                "candidate_tokens": len(cand.tokens), "candidate_seconds": cand.seconds}
+
+    def _decide(self, probe: dict) -> None:
+        self.last_probe = probe
+        if not probe.get("complete", True):
+            return
+        if probe["passed"]:
+            self._timed("publication", self.learner.publish)
+            self.speculating = True
+        elif probe.get("fallback", False):
+            self.speculating = False
+        self.next_probe = self.learner.steps + self.config.probe_every
+
+    def _live(self, prompt, result, max_new_tokens, seed):
+        """One live validation step on the delivered request, if its policy applies and the
+        budget admits it; returns the trial record or None."""
+        cfg = self.config
+        if cfg.reuse_ar_prefix and not self.speculating and result.prefix_tokens:
+            est = (self.probe_estimate or
+                   cfg.initial_probe_factor * result.prefix_seconds)
+            if not self.budget.admits(est):
+                return None
+            before = self.budget.spent
+            probe = self._timed("validation", lambda: self._live_prefix(prompt, result, seed))
+            self.probe_estimate = 1.2 * (self.budget.spent - before)
+            self._decide(probe)
+            return probe
+        gate = self.full_gate
+        if gate is not None and (not self.speculating or cfg.reuse_speculative_answers) and result.tokens:
+            if not self.budget.admits(gate.estimate):
+                return None
+            before = self.budget.spent
+            if gate.ready:
+                probe = self._timed("validation", lambda: self._confirm(prompt, result, max_new_tokens, seed))
+                gate.confirmed(ar_tps=probe["ar_tps"] if cfg.reuse_speculative_answers else None)
+                self._decide(probe)
+                return probe
+            try:
+                row = self._timed("validation", lambda: self._screen(prompt, result, max_new_tokens, seed))
+            except TraceSupportError:
+                return None      # the recomputed target law cannot explain this answer: no evidence
+            out = gate.observe(row, self.budget.spent - before)
+            self.last_probe = out
+            if out["complete"]:
+                self.next_probe = self.learner.steps + cfg.probe_every
+            return out
+        return None
 
     def _probe(self) -> dict:
         base, cand, ar = [], [], []
@@ -288,9 +433,10 @@ class ColdStartService:
 
     def serve(self, prompt: torch.Tensor, max_new_tokens: int, *, seed: int):
         speculative = self.speculating
+        prefix = self.config.probe_tokens if (self.config.reuse_ar_prefix and not speculative) else None
         _sync(self.model)
         t0 = time.perf_counter()
-        result = self._generate(prompt, max_new_tokens, speculative=speculative, seed=seed)
+        result = self._generate(prompt, max_new_tokens, speculative=speculative, seed=seed, prefix_tokens=prefix)
         _sync(self.model)
         self.budget.delivered(time.perf_counter() - t0)
         self.tokens += len(result.tokens)
@@ -312,17 +458,14 @@ class ColdStartService:
             elapsed = self.budget.spent - before
             self.step_estimate = max(1.2 * elapsed, 0.8 * self.step_estimate)
             update["seconds"] = elapsed
-        if due and self.budget.admits(self._probe_cost()):
+        live = self.config.reuse_ar_prefix or self.config.full_answer_screen
+        if due and live and (not self.speculating or self.config.reuse_speculative_answers):
+            probe = self._live(prompt, result, max_new_tokens, seed)
+        elif due and self.budget.admits(self._probe_cost()):
             before = self.budget.spent
             probe = self._timed("validation", self._probe)
             self.probe_estimate = 1.2 * (self.budget.spent - before)
-            self.last_probe = probe
-            if probe["passed"]:
-                self._timed("publication", self.learner.publish)
-                self.speculating = True
-            elif probe["fallback"]:
-                self.speculating = False
-            self.next_probe = self.learner.steps + self.config.probe_every
+            self._decide(probe)
         return result, {"request": self.requests, "mode": "speculative" if speculative else "ar", "update": update,
                         "probe": probe, **self.summary()}
 
@@ -344,7 +487,8 @@ class ColdStartService:
                 "replay_rng": self.replay.rng.get_state(), "anchors_rng": self.replay.anchors_rng.get_state(),
                 "budget": self.budget.summary(), "tokens": self.tokens, "requests": self.requests,
                 "next_probe": self.next_probe, "step_estimate": self.step_estimate,
-                "probe_estimate": self.probe_estimate}
+                "probe_estimate": self.probe_estimate, "pending_live": [dict(r) for r in self.pending_live],
+                "full_gate": None if self.full_gate is None else self.full_gate.state_dict()}
 
     def load_state_dict(self, state: dict) -> None:
         """Restore into a fresh service over the same frozen model and policies (restoring time is charged)."""
@@ -383,6 +527,16 @@ class ColdStartService:
         self.learner.steps, self.learner.serving_step = state["step"], state["serving_step"]
         self.speculating, self.next_probe = state["speculating"], state["next_probe"]
         self.step_estimate, self.probe_estimate = state["step_estimate"], state["probe_estimate"]
+        pending = state.get("pending_live", [])
+        if len(pending) >= self.config.live_probe_requests or any(r["step"] != state["step"] for r in pending):
+            raise ValueError("pending live trials must be fewer than a decision and from the saved version")
+        self.pending_live = [dict(r) for r in pending]
+        if (self.full_gate is None) != (state.get("full_gate") is None):
+            raise ValueError("the saved stream and this service use different validation policies")
+        if self.full_gate is not None:
+            self.full_gate.load_state_dict(state["full_gate"], step=state["step"], next_probe=state["next_probe"],
+                                           speculating=state["speculating"], requests=state["requests"],
+                                           serving_step=state["serving_step"])
         self.replay.records.clear()
         self.replay.records.extend(r.clone() for r in records)
         self.replay.rng.set_state(state["replay_rng"])

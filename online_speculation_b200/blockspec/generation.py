@@ -46,6 +46,11 @@ class Generation:
     updates: int = 0
     update_seconds: float = 0.0
     feedback_blocks: int = 0
+    # generate_ar(prefix_tokens=k): time at which the first min(k, delivered) tokens were
+    # out, and the synchronisation time spent taking that measurement
+    prefix_tokens: int = 0
+    prefix_seconds: float = 0.0
+    prefix_capture_seconds: float = 0.0
 
     @property
     def tps(self) -> float:
@@ -148,8 +153,16 @@ def _sync(device):
 
 @torch.no_grad()
 def generate_ar(branch, prompt: Tensor, max_new_tokens: int, *, sampling=SamplingConfig(), eos_id=None,
-                generator=None, sampler=None) -> Generation:
-    """Plain autoregressive decoding with the AR view (the speed-up denominator)."""
+                generator=None, sampler=None, prefix_tokens: int | None = None) -> Generation:
+    """Plain autoregressive decoding with the AR view (the speed-up denominator).
+
+    ``prefix_tokens``: also record when the first ``prefix_tokens`` outputs were
+    delivered (``prefix_seconds``; the answer's end when it is shorter) -- the
+    reference time of a live AR-prefix trial.  The device synchronisation that
+    measurement needs is reported as ``prefix_capture_seconds``.
+    """
+    if prefix_tokens is not None and (type(prefix_tokens) is not int or prefix_tokens < 1):
+        raise ValueError("a positive prefix length is required")
     if prompt.ndim != 2 or prompt.shape[0] != 1 or prompt.shape[1] < 1:
         raise ValueError("nonempty batch-one prompt required")
     result = Generation()
@@ -162,11 +175,24 @@ def generate_ar(branch, prompt: Tensor, max_new_tokens: int, *, sampling=Samplin
     token = sampler.sample_ar(logits[0, -1], generator)
     result.prefill_forwards = result.prefill_output_tokens = 1
     stopped = _append(result, [token], max_new_tokens, eos_id)
+
+    def capture():
+        if prefix_tokens is not None and not result.prefix_tokens and (
+                len(result.tokens) >= prefix_tokens or stopped):
+            c0 = time.perf_counter()
+            _sync(prompt.device)
+            c1 = time.perf_counter()
+            result.prefix_tokens = len(result.tokens)
+            result.prefix_seconds = c1 - start
+            result.prefix_capture_seconds = c1 - c0
+
+    capture()
     while not stopped:
         logits, cache = branch.ar(prompt.new_tensor([[token]]), cache=cache, logits_to_keep=1)
         token = sampler.sample_ar(logits[0, -1], generator)
         result.tail_ar_forwards += 1
         stopped = _append(result, [token], max_new_tokens, eos_id)
+        capture()
     _sync(prompt.device)
     result.seconds = time.perf_counter() - start
     result.rounds = len(result.tokens)
