@@ -322,9 +322,12 @@ class SuffixLearner:
         P = fb.table.shape[1]
         L = P * kc.shape[2]
         bf = torch.bfloat16
-        tbl = fb.table.long()
-        hk = kc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, L, D)          # [B, ks, L, D] bf16 (frozen)
-        hv = vc[tbl].permute(0, 2, 1, 3, 4).reshape(B, ks, L, D)
+        # one gather of the history pages straight into [B, ks, L, D]: cache row (page * ks + head) holds
+        # that head's 32 keys of the page
+        page = kc.shape[2]
+        idx = (fb.table.long()[:, None, :] * ks + torch.arange(ks, device=q.device)[None, :, None]).reshape(-1)
+        hk = kc.view(-1, page * D).index_select(0, idx).view(B, ks, L, D)   # bf16 (frozen)
+        hv = vc.view(-1, page * D).index_select(0, idx).view(B, ks, L, D)
         qq = q.permute(0, 2, 1, 3).reshape(B, ks, G * Kb, D)               # [B, ks, G*K, D]
         kb = k.permute(0, 2, 1, 3)                                         # [B, ks, K, D]
         vb = v.permute(0, 2, 1, 3)
