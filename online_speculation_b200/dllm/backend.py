@@ -169,9 +169,14 @@ class DiffusionEngineBackend:
         if sampling.cfg_scale > 0:
             uncond = tokens.clone()
             uncond[:, :prompt_len] = mask
-            both = self.model.logits(torch.cat((tokens, uncond)), torch.cat((rows, rows)), **kw)
-            c, u = both.chunk(2)
-            logits = u + (sampling.cfg_scale + 1.0) * (c - u)
+            if getattr(self.model, "hidden_guidance", False):
+                # guidance combined on the normalised hidden rows: one vocabulary GEMM
+                logits = self.model.logits(torch.cat((tokens, uncond)), torch.cat((rows, rows)),
+                                           guidance=float(sampling.cfg_scale), **kw)
+            else:
+                both = self.model.logits(torch.cat((tokens, uncond)), torch.cat((rows, rows)), **kw)
+                c, u = both.chunk(2)
+                logits = u + (sampling.cfg_scale + 1.0) * (c - u)
             seqs = 2 * tokens.shape[0]
         else:
             logits = self.model.logits(tokens, rows, **kw)

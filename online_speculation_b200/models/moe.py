@@ -260,9 +260,22 @@ class MoEDiffusionModel:
         self.token_slots += T
         return h
 
+    # logits(guidance=s) applies classifier-free guidance before the head (see below)
+    hidden_guidance = True
+
     def logits(self, tokens: torch.Tensor, rows: torch.Tensor | None = None,
-               layer_limit: int | None = None) -> torch.Tensor:
+               layer_limit: int | None = None, *, guidance: float = 0.0) -> torch.Tensor:
+        """fp32 logits of ``rows`` (all positions when None).
+
+        ``guidance`` = s > 0: ``tokens`` / ``rows`` stack B conditional and then
+        B unconditional sequences, and the result is the B guided rows
+        u + (s + 1)(c - u).  The head is linear after the final RMSNorm, so the
+        combination is taken on the normalised hidden rows, (s + 1) n_c - s n_u,
+        and the vocabulary GEMM runs once over B rows instead of twice.
+        """
         B, L = tokens.shape
+        if guidance > 0 and B % 2:
+            raise ValueError("guided logits need conditional and unconditional halves")
         h = self.hidden(tokens, layer_limit)
         if rows is not None:
             R = rows.shape[1]
@@ -274,7 +287,11 @@ class MoEDiffusionModel:
             sel = h
         xn = self._buf("xn", sel.shape)
         K.rmsnorm(sel, self.w.final_norm, self.cfg.rms_norm_eps, out=xn)
-        out = torch.empty(sel.shape[0], self.cfg.vocab_size, dtype=torch.float32, device=self.device)
+        if guidance > 0:
+            half = xn.shape[0] // 2
+            xn = ((guidance + 1.0) * xn[:half].float() - guidance * xn[half:].float()).to(torch.bfloat16)
+            B //= 2
+        out = torch.empty(xn.shape[0], self.cfg.vocab_size, dtype=torch.float32, device=self.device)
         K.linear(xn, self.w.head, out=out, out_dtype=torch.float32, static_weights=True)
         return out.view(B, R, -1)
 

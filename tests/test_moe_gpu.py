@@ -86,6 +86,25 @@ def test_moe_diffusion_model_matches_fp32_reference():
         assert err < 0.03, float(err)
 
 
+def test_guided_logits_combine_hidden_rows():
+    """CFG on the normalised hidden rows equals the logit-space combination u + (s+1)(c-u)."""
+    from online_speculation_b200.models.moe import PRESETS, MoEDiffusionModel, build_weights, random_state_dict
+
+    cfg = PRESETS["tiny-moe"]
+    model = MoEDiffusionModel(build_weights(cfg, random_state_dict(cfg, seed=4), device="cuda"))
+    torch.manual_seed(0)
+    tok = torch.randint(0, cfg.vocab_size - 1, (3, 20), device="cuda")
+    unc = tok.clone()
+    unc[:, :6] = cfg.vocab_size - 1
+    rows = torch.arange(8, 16, device="cuda").expand(3, 8)
+    both = torch.cat((tok, unc))
+    c, u = model.logits(both, torch.cat((rows, rows))).chunk(2)
+    want = u + 2.5 * (c - u)
+    got = model.logits(both, torch.cat((rows, rows)), guidance=1.5)
+    assert got.shape == want.shape
+    assert float((got - want).norm() / want.norm()) < 1e-2
+
+
 def test_diffusion_backend_on_moe_engine():
     from online_speculation_b200.dllm import (DiffusionEngineBackend, DiffusionGenerationRequest,
                                               DiffusionSamplingConfig, DiffusionTrajectoryScoreRequest)
