@@ -759,13 +759,16 @@ EncodeTiledFn tensor_map_encoder() {
   return fn;
 }
 
-// Off by default: measured on B200 decode steps (28 layers, 8-64 rows) the
-// whole step ran about 6% slower with it, although chains of GEMMs alone ran
-// faster.  OSB_PDL=1 (or set_pdl) enables it.
+// On by default: the 7B suffix-MH round (bench.py, one B200) ran 6904 tok/s with
+// programmatic dependent launch against 6788 without it, once the GEMM epilogue
+// used two warpgroups (an earlier build, with a single-warpgroup epilogue, ran
+// decode steps about 6% slower with it).  Every kernel launched this way waits
+// (griddepcontrol.wait) before it reads its predecessor's output; only static
+// weights are prefetched ahead of that wait.  OSB_PDL=0 (or set_pdl) disables it.
 bool& pdl_enabled() {
   static bool on = [] {
     const char* v = getenv("OSB_PDL");
-    return v != nullptr && v[0] == '1';
+    return v == nullptr || v[0] != '0';
   }();
   return on;
 }
