@@ -213,6 +213,11 @@ class SuffixLearner:
         self.master = torch.nn.Parameter(d.flat.float().clone())
         self.exp_avg = torch.zeros_like(self.master, requires_grad=False)
         self.exp_avg_sq = torch.zeros_like(self.master, requires_grad=False)
+        # one autograd leaf per draft tensor, aliasing the flat master's storage: the backward then
+        # yields one gradient per tensor (no zero-filled master-sized accumulator and scatter-add),
+        # gathered once into the flat gradient buffer the fused AdamW reads
+        self.leaves = {n: t.detach().requires_grad_(True) for n, t in self._views(self.master.data).items()}
+        self.grad_buf = torch.zeros_like(self.master, requires_grad=False)
         self.norm_buf = torch.zeros(1, dtype=torch.float32, device=dev)
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=dev)
         self.step_t = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -263,7 +268,7 @@ class SuffixLearner:
         B, Kb = fb.block_ids.shape
         D = 128
         eps = cfg.rms_norm_eps
-        params = self._views(self.master)
+        params = self.leaves
         bf = torch.bfloat16
 
         def norm(x, w):
@@ -362,7 +367,11 @@ class SuffixLearner:
 
     def _step(self, fb: FeedbackRound) -> None:
         loss = self._loss(fb)
-        (grad,) = torch.autograd.grad(loss, [self.master])
+        leaves = list(self.leaves.values())
+        grads = torch.autograd.grad(loss, leaves, allow_unused=True)
+        torch.cat([(g if g is not None else torch.zeros_like(t)).reshape(-1) for g, t in zip(grads, leaves)],
+                  out=self.grad_buf)
+        grad = self.grad_buf
         self.loss_buf.copy_(loss.detach())
         self.step_t.add_(1)
         K.adamw_step(self.master.data, grad, self.exp_avg, self.exp_avg_sq, step=1, lr=self.config.learning_rate,
