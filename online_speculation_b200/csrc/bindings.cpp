@@ -251,7 +251,8 @@ void row_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tens
 
 void gumbel_sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor seeds, c10::optional<Tensor> seed_index,
                    c10::optional<Tensor> streams, c10::optional<Tensor> row_in_seq, int64_t salt, Tensor tokens,
-                   int64_t v_lo, c10::optional<Tensor> keys) {
+                   int64_t v_lo, c10::optional<Tensor> keys, c10::optional<Tensor> split_best,
+                   c10::optional<Tensor> split_count) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
   CHECK_DT(logits, torch::kFloat32);
@@ -274,6 +275,14 @@ void gumbel_sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor seeds, 
     CHECK_DT(*keys, torch::kInt64);
     TORCH_CHECK(keys->numel() == logits.size(0), "one key per row");
     a.keys = reinterpret_cast<unsigned long long*>(keys->data_ptr<int64_t>());
+  }
+  if (split_best.has_value() && split_best->defined() && split_count.has_value() && split_count->defined()) {
+    CHECK_DT(*split_best, torch::kInt64);
+    CHECK_DT(*split_count, torch::kInt32);
+    TORCH_CHECK(split_best->numel() >= osb::kGumbelSplitRows && split_count->numel() >= osb::kGumbelSplitRows,
+                "split scratch holds one word per row");
+    a.row_best = reinterpret_cast<unsigned long long*>(split_best->data_ptr<int64_t>());
+    a.row_count = split_count->data_ptr<int>();
   }
   check(osb::gumbel_sample_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "gumbel_sample");
 }

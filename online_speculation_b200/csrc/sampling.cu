@@ -266,6 +266,8 @@ __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
   pdl_wait();
   pdl_trigger();
   const int r = blockIdx.x;
+  const int c_begin = blockIdx.y * a.chunk;                  // this CTA's columns of the row
+  const int c_end = min(a.V, c_begin + a.chunk);
   const float* row = a.logits + r * a.ld;
   const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
   const unsigned long long seed = a.seeds[a.seed_index ? a.seed_index[r] : r];
@@ -274,13 +276,13 @@ __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
   float best = -INFINITY;
   int besti = 0x7fffffff;
   const int g0 = a.v_lo >> 2;   // v_lo is a multiple of 4: groups of four columns keep their noise
-  for (int i = threadIdx.x; i * 4 < a.V; i += blockDim.x) {
+  for (int i = c_begin / 4 + threadIdx.x; i * 4 < c_end; i += blockDim.x) {
     const float4 u = uniform4(seed, stream, hi, static_cast<uint32_t>(g0 + i));
     const float uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int v = i * 4 + j;
-      if (v < a.V) {
+      if (v < c_end) {
         const float g = -__logf(-__logf(uu[j]));
         const float sc = row[v] * invT + g;
         if (sc > best || (sc == best && v < besti)) {
@@ -320,8 +322,22 @@ __global__ void __launch_bounds__(kThreads) gumbel_sample_kernel(GumbelArgs a) {
       }
     }
     if (lane == 0) {
-      if (a.keys != nullptr) a.keys[r] = pack_argmax_key(best, a.v_lo + besti);
-      else a.tokens[r] = a.v_lo + besti;
+      if (a.split <= 1) {
+        if (a.keys != nullptr) a.keys[r] = pack_argmax_key(best, a.v_lo + besti);
+        else a.tokens[r] = a.v_lo + besti;
+      } else {
+        // unsigned order of the unflipped key = (score, then lower column)
+        const unsigned long long k = pack_argmax_key(best, a.v_lo + besti) ^ 0x8000000000000000ull;
+        atomicMax(a.row_best + r, k);
+        __threadfence();
+        if (atomicAdd(a.row_count + r, 1) == a.split - 1) {
+          __threadfence();
+          const unsigned long long win = atomicExch(a.row_best + r, 0ull);   // read the winner, reset
+          a.row_count[r] = 0;
+          if (a.keys != nullptr) a.keys[r] = win ^ 0x8000000000000000ull;
+          else a.tokens[r] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(win & 0xFFFFFFFFull));
+        }
+      }
     }
   }
 }
@@ -480,9 +496,28 @@ cudaError_t row_stats_launch(const RowStatsArgs& a, int rows, cudaStream_t strea
   return launch_pdl(row_stats_kernel, dim3(rows), dim3(kThreads), 0, stream, a);
 }
 
-cudaError_t gumbel_sample_launch(const GumbelArgs& a, int rows, cudaStream_t stream) {
+cudaError_t gumbel_sample_launch(const GumbelArgs& a0, int rows, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  return launch_pdl(gumbel_sample_kernel, dim3(rows), dim3(kThreads), 0, stream, a);
+  GumbelArgs a = a0;
+  a.split = 1;
+  a.chunk = (a.V + 3) / 4 * 4;
+  if (a.row_best != nullptr && a.row_count != nullptr && rows <= kGumbelSplitRows) {
+    // Few rows: about two CTAs per SM in total, at least 8192 columns per CTA.
+    static int sms = 0;
+    if (sms == 0) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (sms <= 0) sms = 148;
+    }
+    int split = (2 * sms + rows - 1) / rows;
+    split = split < a.V / 8192 ? split : a.V / 8192;
+    if (split > 1) {
+      a.chunk = ((a.V + split - 1) / split + 3) / 4 * 4;
+      a.split = (a.V + a.chunk - 1) / a.chunk;     // every chunk non-empty
+    }
+  }
+  return launch_pdl(gumbel_sample_kernel, dim3(rows, a.split), dim3(kThreads), 0, stream, a);
 }
 
 cudaError_t spec_verify_launch(const SpecArgs& a, int batch, cudaStream_t stream) {

@@ -33,6 +33,9 @@ struct RowStatsArgs {
   float* logq;
 };
 
+// Rows up to this count may be split across CTAs (the scratch holds one word per row).
+constexpr int kGumbelSplitRows = 4096;
+
 struct GumbelArgs {
   const float* logits;
   long long ld;
@@ -50,6 +53,14 @@ struct GumbelArgs {
   // instead of a token; the maximum key over ranks is the global draw.
   int v_lo;
   unsigned long long* keys;
+  // Split rows (set by the launcher): `split` CTAs per row, `chunk` columns each (a
+  // multiple of 4).  With split > 1 every CTA folds its key into row_best[r]
+  // (unsigned maximum) and the last to arrive (row_count[r]) writes the result and
+  // resets both words; the buffers are zero at rest.
+  int split;
+  int chunk;
+  unsigned long long* row_best;
+  int* row_count;
 };
 
 struct SpecArgs {

@@ -400,16 +400,18 @@ def gumbel_sample(logits, inv_temp, seeds, *, seed_index=None, streams=None, row
     returns the same global token (noise is keyed by the global column)."""
     rows = logits.shape[0]
     tokens = tokens if tokens is not None else torch.empty(rows, dtype=torch.int32, device=logits.device)
+    if logits.is_cuda:
+        best, count = workspace.sampler_split(logits.device)
     if logits.is_cuda and shard is not None:
         keys = shard.buf("gumbel_keys", (rows,), torch.int64, logits.device)
         _ext.require().gumbel_sample(logits, inv_temp, seeds, seed_index, streams, row_in_seq, int(salt), tokens,
-                                     shard.v_lo, keys)
+                                     shard.v_lo, keys, best, count)
         shard.all_reduce(keys, "max")
         tokens.copy_(unpack_argmax_keys(keys)[0])
         return tokens
     if logits.is_cuda:
         _ext.require().gumbel_sample(logits, inv_temp, seeds, seed_index, streams, row_in_seq, int(salt), tokens,
-                                     0, None)
+                                     0, None, best, count)
         return tokens
     x = logits.float() * (inv_temp.float()[:, None] if inv_temp is not None else 1.0)
     if seed_index is None and streams is None and row_in_seq is None:

@@ -51,6 +51,16 @@ def gemm_counters(device: torch.device) -> torch.Tensor:
     return _get(device, "gemm_cnt", lambda d: torch.zeros(GEMM_COUNTER_SLOTS, dtype=torch.int32, device=d))
 
 
+SAMPLER_SPLIT_ROWS = 4096   # csrc/sampling.h kGumbelSplitRows
+
+
+def sampler_split(device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row scratch of the split-row Gumbel sampler (best key, arrival count), zero at rest."""
+    best = _get(device, "gumbel_best", lambda d: torch.zeros(SAMPLER_SPLIT_ROWS, dtype=torch.int64, device=d))
+    count = _get(device, "gumbel_count", lambda d: torch.zeros(SAMPLER_SPLIT_ROWS, dtype=torch.int32, device=d))
+    return best, count
+
+
 def status(device: torch.device) -> torch.Tensor:
     return _get(device, "status", lambda d: torch.zeros(1, dtype=torch.int32, device=d))
 

@@ -17,6 +17,15 @@ if ROOT not in sys.path:
 torch.set_num_threads(max(1, min(4, os.cpu_count() or 1)))
 
 
+def free_port() -> int:
+    """A TCP port on 127.0.0.1 that is free right now (for multi-process rendezvous)."""
+    import socket
+
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as sock:
+        sock.bind(("127.0.0.1", 0))
+        return sock.getsockname()[1]
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 and the compiled sm_100a extension")
     config.addinivalue_line("markers", "slow: long-running test")

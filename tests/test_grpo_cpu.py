@@ -111,7 +111,9 @@ def test_data_parallel_sharded_gradients_and_allgather():
 
     from online_speculation_b200.training.grpo import FlatParameters, _named_tensors
 
-    world, port = 2, 29611
+    from conftest import free_port
+
+    world, port = 2, free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     procs = [ctx.Process(target=_dp_worker, args=(r, world, port, q)) for r in range(world)]

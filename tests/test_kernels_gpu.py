@@ -268,6 +268,29 @@ def test_gumbel_sampling_distribution(cuda):
     assert float((freq - p).abs().sum() / 2) < 0.02
 
 
+def test_gumbel_split_rows_match_one_cta_per_row(cuda):
+    """Few rows: the vocabulary is split over CTAs; the draw equals the one-CTA-per-row draw."""
+    from online_speculation_b200.ops import _ext
+
+    torch.manual_seed(6)
+    R, V = 8, 152064
+    logits = torch.randn(R, V, device=cuda) * 3
+    seeds = torch.tensor([11, 12], dtype=torch.int64, device=cuda)
+    si = torch.tensor([0, 1] * 4, dtype=torch.int32, device=cuda)
+    streams = torch.arange(R, dtype=torch.int32, device=cuda)
+    rin = torch.arange(R, dtype=torch.int32, device=cuda) % 4
+    inv = torch.full((R,), 0.8, device=cuda)
+    for _ in range(3):
+        got = ops.gumbel_sample(logits, inv, seeds, seed_index=si, streams=streams, row_in_seq=rin, salt=5)
+        want = torch.empty(R, dtype=torch.int32, device=cuda)
+        _ext.require().gumbel_sample(logits, inv, seeds, si, streams, rin, 5, want, 0, None, None, None)
+        assert torch.equal(got, want)
+        streams += R
+    best, count = workspace.sampler_split(cuda)
+    torch.cuda.synchronize()
+    assert int(best.abs().sum()) == 0 and int(count.abs().sum()) == 0      # the scratch is back at rest
+
+
 def test_spec_verify_preserves_target_law(cuda):
     """Marginal law of the first emitted token must equal the target p."""
     torch.manual_seed(5)

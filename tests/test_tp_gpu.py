@@ -10,12 +10,14 @@ import torch
 pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+from conftest import free_port  # noqa: E402
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_tensor_parallel_matches_oracle():
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29533", os.path.join(HERE, "tp_worker.py")]
+           "--master-addr=127.0.0.1", f"--master-port={free_port()}", os.path.join(HERE, "tp_worker.py")]
     out = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
     assert out.returncode == 0 and "TP_OK" in out.stdout, out.stdout[-3000:] + out.stderr[-3000:]
