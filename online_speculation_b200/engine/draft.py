@@ -202,6 +202,30 @@ class FeedbackRound:
     blocks: int                  # number of real blocks
 
 
+class _PublishedMM(torch.autograd.Function):
+    """x @ W^T in bf16 with an fp32 result, W an fp32 master leaf whose bf16 copy is
+    already published (the fused AdamW writes bf16(master) after every step).
+
+    Same numerics as ``(x.bf16() @ W.bf16().T).float()`` under autograd, without
+    converting the master to bf16 in the forward or the bf16 weight gradient
+    through a separate cast kernel in the backward.
+    """
+
+    @staticmethod
+    def forward(ctx, x, w_master, w_pub):
+        xb = x.to(torch.bfloat16)
+        ctx.save_for_backward(xb, w_pub)
+        return (xb @ w_pub.t()).float()
+
+    @staticmethod
+    def backward(ctx, g):
+        xb, w_pub = ctx.saved_tensors
+        gb = g.to(torch.bfloat16)
+        gx = (gb @ w_pub).float()
+        gw = (gb.reshape(-1, gb.shape[-1]).t() @ xb.reshape(-1, xb.shape[-1])).float()
+        return gx, gw, None
+
+
 class SuffixLearner:
     """Online suffix learner of the draft attention (fp32 masters, fused AdamW)."""
 
@@ -277,9 +301,11 @@ class SuffixLearner:
         def mm(x, w):  # bf16 tensor-core matmul with fp32 result
             return (x.to(bf) @ w.to(bf).t()).float()
 
+        published = self.head.draft.tensors()    # bf16(master), written by every AdamW step
+
         emb = r.w.embed[fb.block_ids.long()].float()                        # [B, K, H]
         x = _copy(norm(emb, lw.in_norm), comm)
-        qkv = mm(x, params["w_qkv"])
+        qkv = _PublishedMM.apply(x, params["w_qkv"], published["w_qkv"])
         if "b_qkv" in params:
             qkv = qkv + params["b_qkv"]
         qs, ks = r.q_slots, r.kv_slots
@@ -299,7 +325,7 @@ class SuffixLearner:
 
         q, k = rope(q), rope(k)
         att = self._draft_attention(q, k, v, fb, kc, vc)                    # [B, K, qs * D]
-        h = emb + _reduce(mm(att, params["w_o"]), comm)
+        h = emb + _reduce(_PublishedMM.apply(att, params["w_o"], published["w_o"]), comm)
         x2 = _copy(norm(h, lw.post_norm), comm)
         gu = mm(x2, lw.w_gu).view(B, Kb, -1, 2, 64)
         act = (F.silu(gu[..., 0, :]) * gu[..., 1, :]).reshape(B, Kb, -1)
