@@ -134,6 +134,9 @@ def main(argv=None) -> int:
     sa = sub.add_parser("sample")
     sa.add_argument("rows", type=int)
     sa.add_argument("V", type=int)
+    sa.add_argument("--gumbel", choices=("split", "one-cta"), default=None,
+                    help="time the Gumbel-max draft sampler (split rows, or one CTA per row) instead of the "
+                         "inverse-CDF sampler")
     for q in (g, gr, mo, at, sa):
         q.add_argument("--iters", type=int, default=20)
         q.add_argument("--warmup", type=int, default=3)
@@ -221,9 +224,17 @@ def main(argv=None) -> int:
         logits = torch.randn(a.rows, a.V, device=dev)
         it = torch.ones(a.rows, device=dev)
         uni = torch.rand(a.rows, dtype=torch.float64, device=dev)
+        seeds = torch.arange(1, a.rows + 1, dtype=torch.int64, device=dev)
+        tok = torch.empty(a.rows, dtype=torch.int32, device=dev)
 
         def body():
-            K.sample(logits, it, uni)
+            if a.gumbel == "split":
+                K.gumbel_sample(logits, it, seeds, tokens=tok)
+            elif a.gumbel == "one-cta":
+                K._ext.require().gumbel_sample(logits, it, seeds, None, None, None, 0, tok, 0, None, None, None)
+            else:
+                K.sample(logits, it, uni)
+        out["sampler"] = a.gumbel or "inverse-cdf"
         us = _time(body, a.iters, a.warmup, graph)
         out.update(rows=a.rows, V=a.V, us=us, gbs=a.rows * a.V * 4 / us / 1e3)
     if "gbs" in out and peaks.get("hbm_gbs"):
