@@ -231,7 +231,7 @@ void sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor uniforms, Tens
 
 void row_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tensor> targets,
                c10::optional<Tensor> lse1, c10::optional<Tensor> lseT, c10::optional<Tensor> logp,
-               c10::optional<Tensor> logq) {
+               c10::optional<Tensor> logq, c10::optional<Tensor> split_part, c10::optional<Tensor> split_count) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
   CHECK_DT(logits, torch::kFloat32);
@@ -246,6 +246,15 @@ void row_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tens
   a.lseT = ptr_or_null<float>(lseT);
   a.logp = ptr_or_null<float>(logp);
   a.logq = ptr_or_null<float>(logq);
+  if (split_part.has_value() && split_part->defined() && split_count.has_value() && split_count->defined()) {
+    CHECK_DT(*split_part, torch::kFloat32);
+    CHECK_DT(*split_count, torch::kInt32);
+    TORCH_CHECK(split_part->numel() >= static_cast<long long>(osb::kRowStatsSplitRows) * osb::kRowStatsMaxSplit * 3 &&
+                    split_count->numel() >= osb::kRowStatsSplitRows,
+                "row-statistics split scratch too small");
+    a.part = split_part->data_ptr<float>();
+    a.count = split_count->data_ptr<int>();
+  }
   check(osb::row_stats_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "row_stats");
 }
 

@@ -105,14 +105,15 @@ __device__ __forceinline__ MaxSum2 ms_merge(MaxSum2 a, MaxSum2 b, float invT) {
   return a;
 }
 
-// Row statistics: max, lse at T=1, lse at temperature T.  All threads get the result.
-__device__ void row_stats(const float* __restrict__ row, int V, float invT, float& mx, float& lse1, float& lseT) {
+// Block-reduced (max, sum exp, sum exp at 1/T) of columns [c0, c1) of a row.
+// c0 must be a multiple of 4.  All threads get the result.
+__device__ MaxSum2 row_partial(const float* __restrict__ row, int c0, int c1, float invT) {
   __shared__ MaxSum2 red[32];
   MaxSum2 a{-INFINITY, 0.0f, 0.0f};
-  const bool vec = (reinterpret_cast<uintptr_t>(row) % 16 == 0) && (V % 4 == 0);
+  const bool vec = (reinterpret_cast<uintptr_t>(row) % 16 == 0) && (c1 % 4 == 0);
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
-    for (int i = threadIdx.x; i < V / 4; i += blockDim.x) {
+    for (int i = c0 / 4 + threadIdx.x; i < c1 / 4; i += blockDim.x) {
       const float4 v = r4[i];
       ms_add(a, v.x, invT);
       ms_add(a, v.y, invT);
@@ -120,7 +121,7 @@ __device__ void row_stats(const float* __restrict__ row, int V, float invT, floa
       ms_add(a, v.w, invT);
     }
   } else {
-    for (int i = threadIdx.x; i < V; i += blockDim.x) ms_add(a, row[i], invT);
+    for (int i = c0 + threadIdx.x; i < c1; i += blockDim.x) ms_add(a, row[i], invT);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
@@ -144,6 +145,12 @@ __device__ void row_stats(const float* __restrict__ row, int V, float invT, floa
   __syncthreads();
   const MaxSum2 r = red[0];
   __syncthreads();
+  return r;
+}
+
+// Row statistics: max, lse at T=1, lse at temperature T.  All threads get the result.
+__device__ void row_stats(const float* __restrict__ row, int V, float invT, float& mx, float& lse1, float& lseT) {
+  const MaxSum2 r = row_partial(row, 0, V, invT);
   mx = r.m;
   lse1 = r.m + logf(r.s1);
   lseT = r.m * invT + logf(r.sT);
@@ -247,8 +254,36 @@ __global__ void __launch_bounds__(kThreads) row_stats_kernel(RowStatsArgs a) {
   const int r = blockIdx.x;
   const float* row = a.logits + r * a.ld;
   const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
-  float mx, lse1, lseT;
-  row_stats(row, a.V, invT, mx, lse1, lseT);
+  float lse1, lseT;
+  if (a.split > 1) {
+    // This CTA's column chunk; the last CTA of the row to arrive merges the chunks
+    // in chunk order (independent of arrival order) and finishes the row.
+    const int c0 = blockIdx.y * a.chunk;
+    const MaxSum2 part = row_partial(row, c0, min(a.V, c0 + a.chunk), invT);
+    __shared__ int last;
+    if (threadIdx.x == 0) {
+      float* slot = a.part + (static_cast<long long>(r) * kRowStatsMaxSplit + blockIdx.y) * 3;
+      slot[0] = part.m;
+      slot[1] = part.s1;
+      slot[2] = part.sT;
+      __threadfence();
+      last = atomicAdd(a.count + r, 1) == a.split - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    if (threadIdx.x != 0) return;
+    __threadfence();
+    const float* slots = a.part + static_cast<long long>(r) * kRowStatsMaxSplit * 3;
+    MaxSum2 tot{-INFINITY, 0.0f, 0.0f};
+    for (int k = 0; k < a.split; ++k)
+      tot = ms_merge(tot, MaxSum2{__ldcg(slots + 3 * k), __ldcg(slots + 3 * k + 1), __ldcg(slots + 3 * k + 2)}, invT);
+    a.count[r] = 0;
+    lse1 = tot.m + logf(tot.s1);
+    lseT = tot.m * invT + logf(tot.sT);
+  } else {
+    float mx;
+    row_stats(row, a.V, invT, mx, lse1, lseT);
+  }
   if (threadIdx.x == 0) {
     if (a.lse1) a.lse1[r] = lse1;
     if (a.lseT) a.lseT[r] = lseT;
@@ -491,9 +526,29 @@ cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream) {
   return launch_pdl(sample_kernel, dim3(rows), dim3(kThreads), 0, stream, a);
 }
 
-cudaError_t row_stats_launch(const RowStatsArgs& a, int rows, cudaStream_t stream) {
+cudaError_t row_stats_launch(const RowStatsArgs& a0, int rows, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  return launch_pdl(row_stats_kernel, dim3(rows), dim3(kThreads), 0, stream, a);
+  RowStatsArgs a = a0;
+  a.split = 1;
+  a.chunk = a.V;
+  if (a.part != nullptr && a.count != nullptr && rows <= kRowStatsSplitRows) {
+    // Few rows: about two CTAs per SM in total, at least 8192 columns per CTA.
+    static int sms = 0;
+    if (sms == 0) {
+      int dev = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      if (sms <= 0) sms = 148;
+    }
+    int split = (2 * sms + rows - 1) / rows;
+    split = split < a.V / 8192 ? split : a.V / 8192;
+    split = split < kRowStatsMaxSplit ? split : kRowStatsMaxSplit;
+    if (split > 1) {
+      a.chunk = ((a.V + split - 1) / split + 3) / 4 * 4;
+      a.split = (a.V + a.chunk - 1) / a.chunk;     // every chunk non-empty
+    }
+  }
+  return launch_pdl(row_stats_kernel, dim3(rows, a.split), dim3(kThreads), 0, stream, a);
 }
 
 cudaError_t gumbel_sample_launch(const GumbelArgs& a0, int rows, cudaStream_t stream) {

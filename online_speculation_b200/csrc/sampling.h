@@ -31,7 +31,18 @@ struct RowStatsArgs {
   float* lseT;
   float* logp;
   float* logq;
+  // Split rows (set by the launcher): `split` CTAs per row over `chunk` columns each;
+  // partial (max, sum exp, sum exp at 1/T) go to part[row][chunk][3] and the last CTA
+  // of a row to arrive (count[row]) merges them and resets its counter (zero at rest).
+  int split;
+  int chunk;
+  float* part;
+  int* count;
 };
+
+// Rows up to this count may be split across at most kRowStatsMaxSplit CTAs each.
+constexpr int kRowStatsSplitRows = 4096;
+constexpr int kRowStatsMaxSplit = 16;
 
 // Rows up to this count may be split across CTAs (the scratch holds one word per row).
 constexpr int kGumbelSplitRows = 4096;

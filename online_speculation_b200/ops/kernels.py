@@ -327,7 +327,8 @@ def row_stats(logits, inv_temp=None, targets=None):
     logp = torch.empty(rows, dtype=torch.float32, device=dev) if targets is not None else None
     logq = torch.empty(rows, dtype=torch.float32, device=dev) if targets is not None else None
     if logits.is_cuda:
-        _ext.require().row_stats(logits, inv_temp, targets, lse1, lseT, logp, logq)
+        _ext.require().row_stats(logits, inv_temp, targets, lse1, lseT, logp, logq,
+                                 *workspace.row_stats_split(dev))
         return lse1, lseT, logp, logq
     x = logits.float()
     it = inv_temp.float()[:, None] if inv_temp is not None else torch.ones(rows, 1)
@@ -461,8 +462,9 @@ def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, sal
                      "lseT_t": torch.empty(B * (n + 1), dtype=torch.float32, device=dev),
                      "lse1_d": torch.empty(B * n, dtype=torch.float32, device=dev),
                      "lseT_d": torch.empty(B * n, dtype=torch.float32, device=dev)}
-        ext.row_stats(target, stats["inv_target"], None, stats["lse1_t"], stats["lseT_t"], None, None)
-        ext.row_stats(draft, stats["inv_draft"], None, stats["lse1_d"], stats["lseT_d"], None, None)
+        split = workspace.row_stats_split(target.device)
+        ext.row_stats(target, stats["inv_target"], None, stats["lse1_t"], stats["lseT_t"], None, None, *split)
+        ext.row_stats(draft, stats["inv_draft"], None, stats["lse1_d"], stats["lseT_d"], None, None, *split)
         if shard is not None:
             return _spec_verify_shard(target, draft, candidates, inv_temp, seeds, streams, salt, res, stats, shard)
         ext.spec_verify(target, draft, candidates, n, inv_temp, seeds, streams, int(salt), res["count"],
@@ -720,7 +722,7 @@ class _TargetLogprob(torch.autograd.Function):
         lseT = torch.empty_like(lse1)
         logp = torch.empty_like(lse1)
         logq = torch.empty_like(lse1)
-        ext.row_stats(logits, None, targets, lse1, lseT, logp, logq)
+        ext.row_stats(logits, None, targets, lse1, lseT, logp, logq, *workspace.row_stats_split(logits.device))
         ctx.save_for_backward(logits, lse1, targets)
         return logp
 
@@ -761,7 +763,8 @@ class _HeadLogprob(torch.autograd.Function):
             e = min(R, s + chunk)
             logits = linear(h[s:e], weight, out=buf[: (e - s) * V].view(e - s, V), out_dtype=torch.float32)
             if h.is_cuda:
-                _ext.require().row_stats(logits, None, targets[s:e], lse[s:e], None, logp[s:e], None)
+                _ext.require().row_stats(logits, None, targets[s:e], lse[s:e], None, logp[s:e], None,
+                                         *workspace.row_stats_split(logits.device))
             else:
                 lse[s:e] = logits.logsumexp(-1)
                 logp[s:e] = logits.gather(-1, targets[s:e].long()[:, None]).squeeze(-1) - lse[s:e]

@@ -61,6 +61,18 @@ def sampler_split(device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
     return best, count
 
 
+ROW_STATS_SPLIT_ROWS, ROW_STATS_MAX_SPLIT = 4096, 16   # csrc/sampling.h
+
+
+def row_stats_split(device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Scratch of the split-row statistics kernel: per-chunk partials and per-row arrival counts
+    (the counts are zero at rest)."""
+    part = _get(device, "rowstats_part",
+                lambda d: torch.zeros(ROW_STATS_SPLIT_ROWS * ROW_STATS_MAX_SPLIT * 3, dtype=torch.float32, device=d))
+    count = _get(device, "rowstats_count", lambda d: torch.zeros(ROW_STATS_SPLIT_ROWS, dtype=torch.int32, device=d))
+    return part, count
+
+
 def status(device: torch.device) -> torch.Tensor:
     return _get(device, "status", lambda d: torch.zeros(1, dtype=torch.int32, device=d))
 

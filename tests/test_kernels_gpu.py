@@ -291,6 +291,27 @@ def test_gumbel_split_rows_match_one_cta_per_row(cuda):
     assert int(best.abs().sum()) == 0 and int(count.abs().sum()) == 0      # the scratch is back at rest
 
 
+def test_row_stats_split_rows_match_one_cta_per_row(cuda):
+    """Few rows: statistics are reduced over column chunks and merged by the last CTA."""
+    from online_speculation_b200.ops import _ext
+
+    torch.manual_seed(7)
+    for R, V in ((8, 152064), (100, 65536), (3, 20000)):
+        logits = torch.randn(R, V, device=cuda) * 4
+        inv = torch.rand(R, device=cuda) + 0.5
+        tg = torch.randint(0, V, (R,), dtype=torch.int32, device=cuda)
+        for _ in range(2):
+            got = ops.row_stats(logits, inv, tg)
+            want = [torch.empty(R, device=cuda) for _ in range(4)]
+            _ext.require().row_stats(logits, inv, tg, *want, None, None)
+            for g, w in zip(got, want):
+                assert torch.allclose(g, w, atol=1e-4, rtol=1e-5)
+        ref = torch.logsumexp(logits.double(), -1)
+        assert torch.allclose(got[0].double(), ref, atol=1e-4)
+    torch.cuda.synchronize()
+    assert int(workspace.row_stats_split(cuda)[1].abs().sum()) == 0       # counters back at rest
+
+
 def test_spec_verify_preserves_target_law(cuda):
     """Marginal law of the first emitted token must equal the target p."""
     torch.manual_seed(5)
