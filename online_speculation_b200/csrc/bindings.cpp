@@ -159,7 +159,7 @@ void rmsnorm(Tensor x, Tensor w, Tensor y, double eps, c10::optional<Tensor> h, 
 
 void rope_cache(Tensor qkv, Tensor positions, c10::optional<Tensor> slots, Tensor inv_freq,
                 c10::optional<Tensor> q_norm, c10::optional<Tensor> k_norm, double eps, Tensor q_out, Tensor k_cache,
-                Tensor v_cache, int64_t Hq, int64_t Hkv) {
+                Tensor v_cache, int64_t Hq, int64_t Hkv, c10::optional<Tensor> status) {
   CHECK_CUDA(qkv);
   CHECK_ROWS(qkv);
   CHECK_DT(qkv, torch::kBFloat16);
@@ -173,19 +173,20 @@ void rope_cache(Tensor qkv, Tensor positions, c10::optional<Tensor> slots, Tenso
                                inv_freq.data_ptr<float>(), ptr_or_null<const __nv_bfloat16>(q_norm),
                                ptr_or_null<const __nv_bfloat16>(k_norm), static_cast<float>(eps), bfm(q_out),
                                bfm(k_cache), bfm(v_cache), qkv.size(0), Hq, Hkv, k_cache.size(2),
+                               static_cast<long long>(k_cache.size(0)) * k_cache.size(2), ptr_or_null<int>(status),
                                at::cuda::getCurrentCUDAStream()),
         "rope_cache");
 }
 
-void embed(Tensor ids, Tensor table, Tensor out) {
+void embed(Tensor ids, Tensor table, Tensor out, c10::optional<Tensor> status) {
   CHECK_CUDA(ids);
   CHECK_DT(ids, torch::kInt32);
   CHECK_DT(table, torch::kBFloat16);
   CHECK_ROWS(out);
   TORCH_CHECK(out.size(0) == ids.numel() && out.size(1) == table.size(1), "embedding shapes");
   c10::cuda::CUDAGuard guard(ids.device());
-  check(osb::embed_launch(ids.data_ptr<int>(), bf(table), ids.numel(), table.size(1), bfm(out), out.stride(0),
-                          at::cuda::getCurrentCUDAStream()),
+  check(osb::embed_launch(ids.data_ptr<int>(), bf(table), table.size(0), ids.numel(), table.size(1), bfm(out),
+                          out.stride(0), ptr_or_null<int>(status), at::cuda::getCurrentCUDAStream()),
         "embed");
 }
 

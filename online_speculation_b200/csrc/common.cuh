@@ -60,7 +60,17 @@ enum KernelError : int {
   kErrAccumWait = 4,      // MMA issuer waited too long for a free accumulator
   kErrPeerWait = 5,       // a fused collective waited too long for a peer flag
   kErrBadArgument = 6,    // a kernel rejected its launch arguments
+  kErrBadIndex = 7,       // an index input (token id, KV slot) was out of range; the access was skipped
 };
+
+// Device-side index checks: kernels that address memory through host-supplied
+// indices (token ids into the embedding table, KV slots into the paged cache)
+// test them against the buffer's extent, record kErrBadIndex and skip the access
+// instead of reading or writing out of bounds.  On by default (one compare per
+// index); build with -DOSB_DEVICE_CHECKS=0 to compile them out.
+#ifndef OSB_DEVICE_CHECKS
+#define OSB_DEVICE_CHECKS 1
+#endif
 
 // Two seconds: legitimate waits in this package last microseconds.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;

@@ -77,7 +77,7 @@ __global__ void rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, long lo
                                   const float* __restrict__ inv_freq, const __nv_bfloat16* __restrict__ qn_w,
                                   const __nv_bfloat16* __restrict__ kn_w, float eps, __nv_bfloat16* __restrict__ q_out,
                                   __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, int T,
-                                  int Hq, int Hkv, int page) {
+                                  int Hq, int Hkv, int page, long long slot_capacity, int* status) {
   pdl_wait();
   pdl_trigger();
   const int warps = blockDim.x / 32;
@@ -90,7 +90,13 @@ __global__ void rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, long lo
   const int d0 = 2 * lane;
   float a0 = bf2f(src[d0]), a1 = bf2f(src[d0 + 1]);
   float b0 = bf2f(src[d0 + 64]), b1 = bf2f(src[d0 + 65]);
-  const int slot = slots ? slots[t] : -1;
+  int slot = slots ? slots[t] : -1;
+#if OSB_DEVICE_CHECKS
+  if (slot >= slot_capacity) {      // beyond the cache: store nothing, report once per token
+    if (lane == 0 && hh == Hq) record_error(status, kErrBadIndex);
+    slot = -1;
+  }
+#endif
   if (hh >= Hq + Hkv) {
     if (slot >= 0) {
       const int g = hh - Hq - Hkv;
@@ -133,14 +139,21 @@ __global__ void rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv, long lo
   *reinterpret_cast<__nv_bfloat162*>(dst + d0 + 64) = __floats2bfloat162_rn(rb0, rb1);
 }
 
-__global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int H,
-                             __nv_bfloat16* __restrict__ out, long long ldo) {
+__global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int V, int H,
+                             __nv_bfloat16* __restrict__ out, long long ldo, int* status) {
   pdl_wait();
   pdl_trigger();
   const int t = blockIdx.x;
   const int id = ids[t];
-  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<long long>(id) * H);
   uint4* dst = reinterpret_cast<uint4*>(out + t * ldo);
+#if OSB_DEVICE_CHECKS
+  if (id < 0 || id >= V) {          // outside the table: zero row, report
+    if (threadIdx.x == 0) record_error(status, kErrBadIndex);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+#endif
+  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<long long>(id) * H);
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
 }
 
@@ -174,21 +187,21 @@ cudaError_t rmsnorm_launch(const __nv_bfloat16* x, long long ldx, __nv_bfloat16*
 cudaError_t rope_cache_launch(const __nv_bfloat16* qkv, long long ldqkv, const int* positions, const int* slots,
                               const float* inv_freq, const __nv_bfloat16* qn_w, const __nv_bfloat16* kn_w, float eps,
                               __nv_bfloat16* q_out, __nv_bfloat16* k_cache, __nv_bfloat16* v_cache, int T, int Hq,
-                              int Hkv, int page, cudaStream_t stream) {
+                              int Hkv, int page, long long slot_capacity, int* status, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   const int heads = Hq + 2 * Hkv;
   const long long warps = static_cast<long long>(T) * heads;
   const int per_block = 8;
   return launch_pdl(rope_cache_kernel, dim3(static_cast<int>((warps + per_block - 1) / per_block)),
                     dim3(per_block * 32), 0, stream, qkv, ldqkv, positions, slots, inv_freq, qn_w, kn_w, eps, q_out,
-                    k_cache, v_cache, T, Hq, Hkv, page);
+                    k_cache, v_cache, T, Hq, Hkv, page, slot_capacity, status);
 }
 
-cudaError_t embed_launch(const int* ids, const __nv_bfloat16* table, int T, int H, __nv_bfloat16* out, long long ldo,
-                         cudaStream_t stream) {
+cudaError_t embed_launch(const int* ids, const __nv_bfloat16* table, int V, int T, int H, __nv_bfloat16* out,
+                         long long ldo, int* status, cudaStream_t stream) {
   if (T <= 0) return cudaSuccess;
   if (H % 8) return cudaErrorInvalidValue;
-  return launch_pdl(embed_kernel, dim3(T), dim3(256), 0, stream, ids, table, H, out, ldo);
+  return launch_pdl(embed_kernel, dim3(T), dim3(256), 0, stream, ids, table, V, H, out, ldo, status);
 }
 
 cudaError_t page_copy_launch(__nv_bfloat16* cache, long long layer_stride, int layers, const int* pairs, int npairs,

@@ -121,7 +121,7 @@ def rope_cache(qkv, positions, slots, inv_freq, q_out, k_cache, v_cache, num_q, 
     """
     if qkv.is_cuda:
         _ext.require().rope_cache(qkv, positions, slots, inv_freq_full(inv_freq), q_norm, k_norm, float(eps), q_out,
-                                  k_cache, v_cache, int(num_q), int(num_kv))
+                                  k_cache, v_cache, int(num_q), int(num_kv), workspace.status(qkv.device))
         return q_out
     q, k, v = rope_reference(qkv, positions, inv_freq, num_q, num_kv, q_norm=q_norm, k_norm=k_norm, eps=eps)
     q_out.copy_(q.view_as(q_out))
@@ -170,7 +170,7 @@ def embed(ids, table, out=None):
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
     if table.is_cuda:
-        _ext.require().embed(ids, table, out)
+        _ext.require().embed(ids, table, out, workspace.status(ids.device))
         return out
     out.copy_(table[ids.long()])
     return out

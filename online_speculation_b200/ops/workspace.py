@@ -27,6 +27,7 @@ ERROR_NAMES = {
     4: "MMA issuer timed out waiting for a free accumulator",
     5: "fused collective timed out waiting for a peer",
     6: "kernel rejected its arguments",
+    7: "an index input (token id or KV slot) was out of range; the access was skipped",
 }
 
 

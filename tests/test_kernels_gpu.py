@@ -312,6 +312,42 @@ def test_row_stats_split_rows_match_one_cta_per_row(cuda):
     assert int(workspace.row_stats_split(cuda)[1].abs().sum()) == 0       # counters back at rest
 
 
+def test_device_index_checks_skip_out_of_range_accesses(cuda):
+    """Token ids outside the table and KV slots beyond the cache are reported, not followed.
+
+    Each buffer is a view of a larger allocation whose extra row is a sentinel, so an
+    unchecked access would stay inside this test's own memory (and show up)."""
+    st = workspace.status(cuda)
+    torch.cuda.synchronize()
+    st.zero_()
+    table_full = torch.randn(1001, 256, device=cuda).bfloat16()
+    table_full[1000] = 7.0
+    table = table_full[:1000]
+    ids = torch.tensor([3, 1000, 5, -1], dtype=torch.int32, device=cuda)
+    out = ops.embed(ids, table, torch.empty(4, 256, dtype=torch.bfloat16, device=cuda))
+    torch.cuda.synchronize()
+    assert torch.equal(out[0], table[3]) and torch.equal(out[2], table[5])
+    assert int(out[1].abs().sum()) == 0 and int(out[3].abs().sum()) == 0
+    assert int(st.item()) == 7
+    st.zero_()
+    Hq, Hkv, P = 4, 2, 32
+    k_full = torch.zeros(5, Hkv, P, 128, dtype=torch.bfloat16, device=cuda)
+    v_full = torch.zeros_like(k_full)
+    kc, vc = k_full[:4], v_full[:4]                     # capacity 4 * 32 = 128 slots
+    T = 3
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * 128, device=cuda).bfloat16()
+    pos = torch.tensor([0, 1, 2], dtype=torch.int32, device=cuda)
+    slots = torch.tensor([5, 128, 127], dtype=torch.int32, device=cuda)
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, 128, 2, device=cuda).float() / 128))
+    q_out = torch.empty(T, Hq, 128, dtype=torch.bfloat16, device=cuda)
+    ops.rope_cache(qkv, pos, slots, inv_freq, q_out, kc, vc, Hq, Hkv)
+    torch.cuda.synchronize()
+    assert int(k_full[4].abs().sum()) == 0 and int(v_full[4].abs().sum()) == 0   # sentinel page untouched
+    assert int(kc[0, :, 5].abs().sum()) > 0 and int(vc[3, :, 31].abs().sum()) > 0  # valid slots stored
+    assert int(st.item()) == 7
+    st.zero_()
+
+
 def test_spec_verify_preserves_target_law(cuda):
     """Marginal law of the first emitted token must equal the target p."""
     torch.manual_seed(5)
