@@ -136,20 +136,31 @@ class SuffixLearner:
             return self.update()
         return None
 
+    def _replay_items(self) -> list:
+        """Replayed blocks that enter the next update."""
+        return list(self.replay)
+
+    def _replay_loss(self, fb: Feedback, logits: torch.Tensor, rows: int, blocks: int) -> torch.Tensor:
+        """Loss of one replayed block; the update sums it over ``_replay_items``."""
+        return divergence(logits, fb.teacher_logits, self.config.loss).sum() / rows
+
     def update(self):
         if not self.replay:
             return None
         self._check()
         start = time.perf_counter()
-        rows = sum(f.valid for f in self.replay)
+        items = self._replay_items()
+        if not items:
+            return None
+        rows = sum(f.valid for f in items)
         total = 0.0
         grad = torch.zeros_like(self.master)
         with torch.enable_grad():
-            for fb in self.replay:
+            for fb in items:
                 weights = {n: v.to(self.execution[n].dtype) for n, v in self._views(self.master).items()}
                 out = self.model.forward_suffix(fb.boundary, cache=fb.cache, logit_range=(0, fb.valid),
                                                 draft_weights=weights)
-                loss = divergence(out.logits[0], fb.teacher_logits, self.config.loss).sum() / rows
+                loss = self._replay_loss(fb, out.logits[0], rows, len(items))
                 if not torch.isfinite(loss):
                     raise FloatingPointError("nonfinite online suffix loss")
                 (g,) = torch.autograd.grad(loss, [self.master])
