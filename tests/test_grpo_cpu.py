@@ -101,7 +101,9 @@ def _dp_worker(rank, world, port, q):
         g, _ = tr.compute_gradients(ids[2 * rank:2 * rank + 2], mask[:2], rewards[2 * rank:2 * rank + 2])
         shard = g.clone()
         tr._optimizer_step(g)
-        q.put((rank, shard, tr.params.shard_ranges(), tr.params.flat.clone()))
+        # numpy copies travel by value: a tensor would be passed through shared memory owned by
+        # this process, which may have exited before the parent unpickles it
+        q.put((rank, shard.float().numpy().copy(), tr.params.shard_ranges(), tr.params.flat.float().numpy()))
     finally:
         dist.destroy_process_group()
 
@@ -120,6 +122,7 @@ def test_data_parallel_sharded_gradients_and_allgather():
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=240) for _ in range(world)], key=lambda x: x[0])
+    res = [(r, torch.from_numpy(shard), ranges, torch.from_numpy(flat)) for r, shard, ranges, flat in res]
     for p in procs:
         p.join(timeout=60)
     assert torch.equal(res[0][3], res[1][3]), "all-gathered parameters differ across ranks"
