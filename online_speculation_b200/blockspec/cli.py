@@ -1,6 +1,6 @@
 """Command line for the dual-view speculation stack.
 
-    python -m online_speculation_b200.blockspec evaluate {benchmark,audit} ...
+    python -m online_speculation_b200.blockspec evaluate {benchmark,audit,trace,profile} ...
     python -m online_speculation_b200.blockspec online --model M --prompts P.jsonl ...
     python -m online_speculation_b200.blockspec fit {train,resume,demo} ...
 
@@ -23,9 +23,9 @@ import torch
 
 from .data import read_records
 from .fitting import FitConfig, TokenDataset, Trainer
-from .generation import MaskedAttentionBranch, generate, generate_ar
+from .generation import MaskedAttentionBranch, ProposalSampler, generate, generate_ar
 from .measurement import paired_ratio
-from .model import DualViewConfig, DualViewDecoder
+from .model import DualViewConfig, DualViewDecoder, cache_length
 from .online import OnlineFeedback, SuffixConfig, SuffixLearner
 from .reporting import write_report
 from .sampling import SamplingConfig
@@ -105,6 +105,147 @@ def cmd_audit(a) -> dict:
     return audit(original, learned, seqs, anchors)
 
 
+def _compare(a: torch.Tensor, b: torch.Tensor) -> dict:
+    """Max logit error, total variation of the two softmaxes and argmax agreement of [N, V] rows."""
+    a, b = a.float(), b.float()
+    tv = 0.5 * (a.softmax(-1) - b.softmax(-1)).abs().sum(-1)
+    return {"max_logit_error": float((a - b).abs().max()), "max_tv": float(tv.max()),
+            "argmax_equal": bool(torch.equal(a.argmax(-1), b.argmax(-1)))}
+
+
+@torch.inference_mode()
+def cmd_trace(a) -> dict:
+    """Explain one greedy decision: the AR and speculative logits for output token ``token_index``
+    of request ``request_index``, and a same-cache replay of that row alone against the row inside
+    a full masked block (online-speculation/src/blockspec/commands/evaluate.py trace_decision)."""
+    model = load_model(a.model, a.device)
+    prompts = _prompts(a.prompts, a.request_index + 1, a.device, model.config.vocab_size)
+    if a.request_index >= len(prompts) or not 0 <= a.token_index < a.max_new_tokens:
+        raise ValueError("trace needs a valid request index and a token index below --max-new-tokens")
+    prompt = prompts[a.request_index]
+    block = a.block_size or model.config.block_size
+    branch, captures, outputs = MaskedAttentionBranch(model), {}, {}
+    for mode in ("ar", "speculative"):
+        got = {}
+
+        def hook(module, args, kwargs, out, got=got):
+            if kwargs.get("view", "ar") == "draft":
+                return
+            tokens = args[0] if args else kwargs["tokens"]
+            first = cache_length(kwargs.get("cache")) + tokens.shape[1] - out.logits.shape[1] + 1
+            row = prompt.shape[1] + a.token_index - first
+            if 0 <= row < out.logits.shape[1]:
+                got.update(logits=out.logits[0, row].float().clone(), cache=kwargs.get("cache"),
+                           inputs=tokens.clone())
+
+        h = model.register_forward_hook(hook, with_kwargs=True)
+        try:
+            res = (generate_ar(branch, prompt, a.max_new_tokens) if mode == "ar" else
+                   generate(branch, prompt, a.max_new_tokens, block_size=block))
+        finally:
+            h.remove()
+        outputs[mode], captures[mode] = res.tokens, got
+    if not all(captures.values()):
+        raise ValueError("the traced token lies outside the generated range")
+    ar, sp = captures["ar"]["logits"], captures["speculative"]["logits"]
+    ar_id, sp_id = int(ar.argmax()), int(sp.argmax())
+    saved = captures["ar"]
+    future = prompt.new_full((1, block), model.config.mask_token_id)
+    future[:, :1] = saved["inputs"][:, -1:]
+    single = model(future[:, :1], cache=saved["cache"]).logits[0, 0]
+    whole = model(future, cache=saved["cache"]).logits[0, 0]
+    diff = next((i for i, (x, y) in enumerate(zip(outputs["ar"], outputs["speculative"])) if x != y), None)
+    return {"request_index": a.request_index, "token_index": a.token_index, "first_difference": diff,
+            "prefix_identical": outputs["ar"][:a.token_index] == outputs["speculative"][:a.token_index],
+            "actual_path": _compare(ar[None], sp[None]), "ar_choice": ar_id, "speculative_choice": sp_id,
+            "ar_gap_between_choices": float(ar[ar_id] - ar[sp_id]),
+            "block_gap_between_choices": float(sp[ar_id] - sp[sp_id]),
+            "same_cache_single_vs_block": _compare(single[None], whole[None]),
+            "same_cache_single_choice": int(single.argmax()), "same_cache_block_choice": int(whole.argmax())}
+
+
+class _ScopedSampler(ProposalSampler):
+    """A sampler whose three decisions run inside named profiler regions."""
+
+    def sample_ar(self, logits, generator):
+        with torch.profiler.record_function("blockspec.sample_ar"):
+            return super().sample_ar(logits, generator)
+
+    def propose(self, logits, generator):
+        with torch.profiler.record_function("blockspec.propose"):
+            return super().propose(logits, generator)
+
+    def verify(self, proposal, target_logits, generator):
+        with torch.profiler.record_function("blockspec.correct"):
+            return super().verify(proposal, target_logits, generator)
+
+
+def cmd_profile(a) -> dict:
+    """Operator attribution for AR and speculative decoding of one request, kept apart from the
+    throughput numbers: an uninstrumented run fixes the expected tokens and round counters, the
+    profiled run must reproduce them, and no parameter may change
+    (online-speculation/src/blockspec/commands/evaluate.py profile_generation)."""
+    if a.max_new_tokens > 256:
+        raise ValueError("profile takes at most 256 new tokens")
+    model = load_model(a.model, a.device)          # outside inference mode: parameters keep versions
+    with torch.inference_mode():
+        return _profile(a, model)
+
+
+def _profile(a, model) -> dict:
+    prompt = _prompts(a.prompts, 1, a.device, model.config.vocab_size)[0]
+    block = a.block_size or model.config.block_size
+    sampling = SamplingConfig(temperature=a.temperature)
+    activities = [torch.profiler.ProfilerActivity.CPU]
+    if prompt.is_cuda:
+        activities.append(torch.profiler.ProfilerActivity.CUDA)
+    versions = {n: p._version for n, p in model.named_parameters()}
+    branch, records = MaskedAttentionBranch(model), []
+
+    def run(method, sampler):
+        g = torch.Generator(device=prompt.device).manual_seed(0)
+        kw = {"sampler": sampler, "sampling": sampling, "generator": g}
+        return (generate_ar(branch, prompt, a.max_new_tokens, **kw) if method == "ar" else
+                generate(branch, prompt, a.max_new_tokens, block_size=block, **kw))
+
+    for method in ("ar", "speculative"):
+        expected = run(method, ProposalSampler(sampling))
+        open_scopes = []
+
+        def enter(module, args, kwargs, stack=open_scopes):
+            stage = ("draft" if kwargs.get("view") == "draft" else
+                     "prefill" if kwargs.get("cache") is None else "ar_forward")
+            scope = torch.profiler.record_function(f"blockspec.{stage}")
+            scope.__enter__()
+            stack.append(scope)
+
+        def leave(module, args, out, stack=open_scopes):
+            stack.pop().__exit__(None, None, None)
+
+        pre = model.register_forward_pre_hook(enter, with_kwargs=True)
+        post = model.register_forward_hook(leave, always_call=True)
+        try:
+            with torch.profiler.profile(activities=activities, acc_events=True) as prof:
+                actual = run(method, _ScopedSampler(sampling))
+        finally:
+            pre.remove()
+            post.remove()
+        events = [{"name": e.key, "count": e.count, "self_cpu_us": e.self_cpu_time_total,
+                   "self_device_us": e.self_device_time_total, "inclusive_device_us": e.device_time_total}
+                  for e in prof.key_averages() if e.device_type == torch.autograd.DeviceType.CPU]
+        records.append({
+            "method": method, "tokens": len(actual.tokens), "decode_forwards": actual.decode_forwards,
+            "tokens_unchanged": actual.tokens == expected.tokens,
+            "counters_unchanged": (actual.accepted_per_round == expected.accepted_per_round
+                                   and actual.decode_forwards == expected.decode_forwards),
+            "regions": [e for e in events if e["name"].startswith("blockspec.")],
+            "operators": sorted((e for e in events if not e["name"].startswith("blockspec.")),
+                                key=lambda e: (e["self_device_us"], e["self_cpu_us"]), reverse=True)[:20]})
+    unchanged = versions == {n: p._version for n, p in model.named_parameters()}
+    return {"profiles": records, "parameters_unchanged": unchanged,
+            "pass": unchanged and all(r["tokens_unchanged"] and r["counters_unchanged"] for r in records)}
+
+
 def cmd_online(a) -> dict:
     model = load_model(a.model, a.device)
     learner = SuffixLearner(model, SuffixConfig(last_layers=a.last_layers, stride=a.stride,
@@ -161,7 +302,7 @@ def main(argv=None) -> int:
     p = argparse.ArgumentParser(prog="python -m online_speculation_b200.blockspec")
     sub = p.add_subparsers(dest="group", required=True)
     ev = sub.add_parser("evaluate")
-    ev.add_argument("mode", choices=("benchmark", "audit"))
+    ev.add_argument("mode", choices=("benchmark", "audit", "trace", "profile"))
     on = sub.add_parser("online")
     fi = sub.add_parser("fit")
     fi.add_argument("action", choices=("train", "resume", "demo"))
@@ -176,6 +317,9 @@ def main(argv=None) -> int:
     ev.add_argument("--engine", choices=("module", "kernel"), default="module")
     ev.add_argument("--learned", default=None)
     ev.add_argument("--online-state", default=None)
+    ev.add_argument("--request-index", type=int, default=0)
+    ev.add_argument("--token-index", type=int, default=0)
+    ev.add_argument("--block-size", type=int, default=None)
     on.add_argument("--last-layers", type=int, default=1)
     on.add_argument("--stride", type=int, default=16)
     on.add_argument("--replay-blocks", type=int, default=1)
@@ -193,7 +337,8 @@ def main(argv=None) -> int:
     fi.add_argument("--warmup", type=int, default=10)
     a = p.parse_args(argv)
     if a.group == "evaluate":
-        out = cmd_benchmark(a) if a.mode == "benchmark" else cmd_audit(a)
+        out = {"benchmark": cmd_benchmark, "audit": cmd_audit, "trace": cmd_trace,
+               "profile": cmd_profile}[a.mode](a)
     elif a.group == "online":
         out = cmd_online(a)
     else:
@@ -201,7 +346,7 @@ def main(argv=None) -> int:
     if a.report:
         write_report(a.report, out)
     print(json.dumps(out))
-    return 0
+    return 1 if a.group == "evaluate" and a.mode == "profile" and not out["pass"] else 0
 
 
 if __name__ == "__main__":

@@ -20,11 +20,18 @@ def parameter_digest(model) -> str:
     return h.hexdigest()
 
 
+def _identity(key: str, value) -> bool:
+    """A string or path stored under a location-like key names a local resource; measurements
+    under such keys (``actual_path``, ``profiles``) are kept."""
+    names = isinstance(value, (str, os.PathLike)) or (
+        isinstance(value, (list, tuple)) and bool(value) and all(isinstance(v, (str, os.PathLike)) for v in value))
+    return names and any(s in key.lower() for s in _SENSITIVE)
+
+
 def scrub(value, *, key: str = ""):
     """Drop local resource identities (paths, host names) and non-finite numbers."""
     if isinstance(value, dict):
-        return {k: scrub(v, key=k) for k, v in value.items()
-                if not any(s in k.lower() for s in _SENSITIVE)}
+        return {k: scrub(v, key=k) for k, v in value.items() if not _identity(str(k), v)}
     if isinstance(value, (list, tuple)):
         return [scrub(v, key=key) for v in value]
     if isinstance(value, float) and not math.isfinite(value):

@@ -173,6 +173,27 @@ def test_cli_commands(tmp_path):
     assert main(["evaluate", "audit", "--device", "cpu", "--limit", "2"]) == 0
 
 
+def test_cli_trace_and_profile(tmp_path):
+    import json
+
+    from online_speculation_b200.blockspec.cli import main
+
+    assert main(["evaluate", "trace", "--device", "cpu", "--max-new-tokens", "12", "--request-index", "1",
+                 "--token-index", "5", "--report", str(tmp_path / "t.json")]) == 0
+    t = json.loads((tmp_path / "t.json").read_text())
+    # a greedy speculative decode reproduces AR decoding, so the traced decision agrees
+    assert t["prefix_identical"] and t["first_difference"] is None and t["ar_choice"] == t["speculative_choice"]
+    assert t["actual_path"]["max_tv"] < 1e-4
+    assert main(["evaluate", "profile", "--device", "cpu", "--max-new-tokens", "16", "--temperature", "1.0",
+                 "--report", str(tmp_path / "p.json")]) == 0
+    p = json.loads((tmp_path / "p.json").read_text())
+    assert p["pass"] and [r["method"] for r in p["profiles"]] == ["ar", "speculative"]
+    names = {e["name"] for e in p["profiles"][1]["regions"]}
+    assert {"blockspec.prefill", "blockspec.draft", "blockspec.propose", "blockspec.correct"} <= names
+    with pytest.raises(ValueError):
+        main(["evaluate", "profile", "--device", "cpu", "--max-new-tokens", "300"])
+
+
 def test_measurement_ratio():
     from online_speculation_b200.blockspec.measurement import paired_ratio
 
