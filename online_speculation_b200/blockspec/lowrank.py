@@ -230,7 +230,9 @@ class Attention(nn.Module):
             q, k = self.q_norm(q), self.k_norm(k)
         cos, sin = rotary
         q, k = _rotate(q.transpose(1, 2), cos, sin), _rotate(k.transpose(1, 2), cos, sin)
-        if past is not None:
+        if isinstance(past, WorkspaceLayer):
+            k, v = past.write(k, v)
+        elif past is not None:
             k, v = torch.cat((past[0], k), 2), torch.cat((past[1], v), 2)
         if self.backend == "grouped":
             o = grouped_attention(q, k, v, allowed)
@@ -275,6 +277,21 @@ class Body(nn.Module):
         nn.init.normal_(self.embed_tokens.weight, std=0.02)
         self.layers = nn.ModuleList(Layer(c) for _ in range(c.num_hidden_layers))
         self.norm = GroupedRMSNorm(c.hidden_size, c.rms_norm_eps, c.norm_groups)
+
+
+@dataclass
+class WorkspaceLayer:
+    """One layer of a fixed-capacity KV workspace: this forward's rows are written in place at
+    ``index`` (their positions) and attention reads the whole capacity under the caller's mask."""
+
+    k: Tensor          # [1, Hkv, capacity, D]
+    v: Tensor
+    index: Tensor      # [T] write positions
+
+    def write(self, k: Tensor, v: Tensor):
+        self.k.index_copy_(2, self.index, k.to(self.k.dtype))
+        self.v.index_copy_(2, self.index, v.to(self.v.dtype))
+        return self.k, self.v
 
 
 @dataclass
@@ -388,6 +405,16 @@ class LowRankDecoder(nn.Module):
         if capture_layer == self.config.num_hidden_layers:
             boundary = Boundary(h, positions, allowed, adapter_mask, capture_layer)
         return LowRankOutput(self._head(h, logit_range), tuple(new), boundary)
+
+    def forward_workspace(self, tokens: Tensor, positions: Tensor, allowed: Tensor, adapter_mask, layers,
+                          logit_range=None) -> Tensor:
+        """Forward over a KV workspace (one :class:`WorkspaceLayer` per layer); fixed shapes, no
+        host synchronisation, so it can be captured in a CUDA graph."""
+        h = self.model.embed_tokens(tokens)
+        rotary = self._rotary(positions, h.dtype)
+        for layer, past in zip(self.model.layers, layers):
+            h, _ = layer(h, adapter_mask, past, rotary, allowed)
+        return self._head(h, logit_range)
 
     def forward_suffix(self, boundary: Boundary, *, cache=None, logit_range=None) -> Tensor:
         """Recompute layers ``boundary.start..`` from a captured boundary; ``cache`` holds those
@@ -650,7 +677,7 @@ class LowRankFeedback:
         result.feedback_blocks = self.learner.feedback_blocks - f
 
 
-__all__ = ["LowRankConfig", "GatedLinear", "GroupedRMSNorm", "LowRankDecoder", "LowRankOutput", "Boundary",
+__all__ = ["LowRankConfig", "GatedLinear", "WorkspaceLayer", "GroupedRMSNorm", "LowRankDecoder", "LowRankOutput", "Boundary",
            "grouped_attention", "rotary_frequencies", "is_adapter", "save", "load", "from_hf", "PairedBatch",
            "paired_batch", "divergence", "paired_loss", "offline_step", "NoiseBranch", "NoiseDraft",
            "LowRankLearner", "LowRankFeedback", "ATTENTION_BACKENDS", "LOSS_KINDS", "PROJECTIONS"]

@@ -8,12 +8,11 @@ import pytest
 import torch
 
 from online_speculation_b200.blockspec.diffusion import UniformNoise
-from online_speculation_b200.blockspec.generation import generate, generate_ar
+from online_speculation_b200.blockspec.generation import ProposalSampler, generate, generate_ar
 from online_speculation_b200.blockspec.lowrank import (LowRankConfig, LowRankDecoder, LowRankFeedback,
                                                        LowRankLearner, NoiseBranch, from_hf, grouped_attention,
                                                        load, offline_step, paired_batch, paired_loss,
                                                        rotary_frequencies, save)
-from online_speculation_b200.blockspec.model import trim_cache
 from online_speculation_b200.blockspec.sampling import SamplingConfig
 
 
@@ -165,9 +164,8 @@ def test_online_learner_loss_gradient_is_exact():
     br = NoiseBranch(m, block_size=4)
     gen = torch.Generator().manual_seed(2)
     hist = m(torch.tensor([[4, 8, 15]])).cache
-    d = br.draft(torch.tensor([[16]]), hist, 4, __import__("online_speculation_b200.blockspec.generation",
-                                                          fromlist=["ProposalSampler"]).ProposalSampler(
-        SamplingConfig(1.0)), gen, feedback=LowRankFeedback(learner))
+    d = br.draft(torch.tensor([[16]]), hist, 4, ProposalSampler(SamplingConfig(1.0)), gen,
+                 feedback=LowRankFeedback(learner))
     teacher = m(d.verifier_inputs, cache=d.cache).logits[0]
     learner.observe(d.boundary, teacher, 3, may_update=False)
     assert learner.feedback_blocks == 1 and learner.updates == 0
@@ -203,3 +201,38 @@ def test_hf_qwen3_backbone_imports_exactly():
         want = hf(x).logits
     assert torch.allclose(m(x).logits, want, atol=1e-5)
     assert len(m.adapter_parameters()) == 2 * 7 * 2
+
+
+def test_workspace_executor_matches_the_eager_branch():
+    from online_speculation_b200.blockspec.lowrank_exec import GraphNoiseBranch
+
+    m = _model(13)
+    prompt = torch.tensor([[5, 9, 13, 2, 7, 1, 11, 4, 3, 8]])            # longer than a block: eager prefill
+    eager = NoiseBranch(m, block_size=4)
+    ws = GraphNoiseBranch(m, block_size=4, capacity=128)
+    ws.prepare()
+    for t in (0.0, 1.0):
+        s = SamplingConfig(t)
+        a = generate(eager, prompt, 25, sampling=s, generator=torch.Generator().manual_seed(3))
+        b = generate(ws, prompt, 25, sampling=s, generator=torch.Generator().manual_seed(3))
+        assert a.tokens == b.tokens and a.accepted_per_round == b.accepted_per_round
+    assert ws.eager_forwards >= 1 and ws.graph_replays == 0
+    assert generate_ar(ws, prompt, 12, sampling=SamplingConfig(0.0)).tokens == \
+        generate_ar(eager, prompt, 12, sampling=SamplingConfig(0.0)).tokens
+    with pytest.raises(ValueError):
+        generate(ws, prompt, 200, sampling=SamplingConfig(0.0))              # past the capacity
+
+
+def test_workspace_executor_learns_online_and_detects_storage_changes():
+    from online_speculation_b200.blockspec.lowrank_exec import GraphNoiseBranch
+
+    m = _model(14, scale=0.0).float()
+    learner = LowRankLearner(m, learning_rate=1e-2, interval=2)
+    ws = GraphNoiseBranch(m, block_size=4, capacity=128)
+    out = generate(ws, torch.tensor([[5, 9, 13]]), 40, sampling=SamplingConfig(1.0),
+                   generator=torch.Generator().manual_seed(1), feedback=LowRankFeedback(learner))
+    assert out.updates >= 1 and any(float(p.abs().sum()) > 0 for n, p in m.named_parameters()
+                                    if n.endswith("lora_B"))
+    m.lm_head.weight.data = m.lm_head.weight.data.clone()
+    with pytest.raises(RuntimeError):
+        generate(ws, torch.tensor([[5, 9, 13]]), 4)
