@@ -471,6 +471,52 @@ def from_hf(source, *, device="cpu", dtype=torch.bfloat16, **adapter) -> LowRank
     return m.to(device).set_base_dtype(dtype).eval().requires_grad_(False)
 
 
+_PEFT_PREFIX = "base_model.model."
+
+
+def save_peft(model: LowRankDecoder, directory) -> None:
+    """Write the adapters as a PEFT LoRA artifact (``adapter_config.json`` and
+    ``adapter_model.safetensors`` with ``base_model.model.<module>.lora_A.weight`` keys)."""
+    from safetensors.torch import save_file
+
+    c, d = model.config, Path(directory)
+    d.mkdir(parents=True, exist_ok=True)
+    (d / "adapter_config.json").write_text(json.dumps({
+        "peft_type": "LORA", "task_type": "CAUSAL_LM", "r": c.adapter_rank, "lora_alpha": c.adapter_alpha,
+        "target_modules": list(c.adapter_targets), "bias": "none", "lora_dropout": 0.0,
+        "fan_in_fan_out": False, "use_rslora": False, "use_dora": False}, indent=1))
+    save_file({f"{_PEFT_PREFIX}{n}.weight": p.detach().float().contiguous().cpu()
+               for n, p in model.named_parameters() if is_adapter(n)}, str(d / "adapter_model.safetensors"))
+
+
+def load_peft(model: LowRankDecoder, directory) -> dict:
+    """Load a PEFT LoRA artifact into the adapters after checking all of it: plain LoRA (no DoRA,
+    rsLoRA, bias, per-module rank or alpha), the model's rank, alpha and targets, and exactly
+    the model's adapter tensors with their shapes. Nothing changes when a check fails."""
+    from safetensors.torch import load_file
+
+    d, c = Path(directory), model.config
+    cfg = json.loads((d / "adapter_config.json").read_text())
+    if (cfg.get("peft_type") != "LORA" or cfg.get("bias", "none") != "none" or cfg.get("use_dora")
+            or cfg.get("use_rslora") or cfg.get("fan_in_fan_out") or cfg.get("rank_pattern")
+            or cfg.get("alpha_pattern") or cfg.get("modules_to_save")):
+        raise ValueError("only uniform, alpha / r scaled, bias-free LoRA adapters are supported")
+    if (cfg.get("r") != c.adapter_rank or cfg.get("lora_alpha") != c.adapter_alpha
+            or set(cfg.get("target_modules") or ()) != set(c.adapter_targets)):
+        raise ValueError("the adapter's rank, alpha or targets differ from the model's")
+    own = {n: p for n, p in model.named_parameters() if is_adapter(n)}
+    state = {}
+    for key, value in load_file(str(d / "adapter_model.safetensors")).items():
+        if not key.startswith(_PEFT_PREFIX) or not key.endswith((".lora_A.weight", ".lora_B.weight")):
+            raise ValueError(f"unexpected tensor {key}")
+        state[key[len(_PEFT_PREFIX):-len(".weight")]] = value
+    if set(state) != set(own) or any(state[n].shape != own[n].shape for n in own):
+        raise ValueError("the adapter tensors do not match the model")
+    with torch.no_grad():
+        for n, p in own.items():
+            p.copy_(state[n])
+    return {"tensors": len(state), "rank": c.adapter_rank, "alpha": c.adapter_alpha}
+
 # --- offline distillation ----------------------------------------------------------------------
 
 @dataclass
@@ -678,6 +724,6 @@ class LowRankFeedback:
 
 
 __all__ = ["LowRankConfig", "GatedLinear", "WorkspaceLayer", "GroupedRMSNorm", "LowRankDecoder", "LowRankOutput", "Boundary",
-           "grouped_attention", "rotary_frequencies", "is_adapter", "save", "load", "from_hf", "PairedBatch",
+           "grouped_attention", "rotary_frequencies", "is_adapter", "save", "load", "from_hf", "save_peft", "load_peft", "PairedBatch",
            "paired_batch", "divergence", "paired_loss", "offline_step", "NoiseBranch", "NoiseDraft",
            "LowRankLearner", "LowRankFeedback", "ATTENTION_BACKENDS", "LOSS_KINDS", "PROJECTIONS"]

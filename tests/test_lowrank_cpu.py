@@ -236,3 +236,29 @@ def test_workspace_executor_learns_online_and_detects_storage_changes():
     m.lm_head.weight.data = m.lm_head.weight.data.clone()
     with pytest.raises(RuntimeError):
         generate(ws, torch.tensor([[5, 9, 13]]), 4)
+
+
+def test_peft_adapter_roundtrip(tmp_path):
+    pytest.importorskip("safetensors")
+    import json
+
+    from online_speculation_b200.blockspec.lowrank import load_peft, save_peft
+
+    m = _model(15).float()
+    save_peft(m, tmp_path / "a")
+    fresh = LowRankDecoder(m.config)
+    fresh.load_state_dict({k: v for k, v in m.state_dict().items() if "lora" not in k}, strict=False)
+    info = load_peft(fresh, tmp_path / "a")
+    assert info["tensors"] == len(m.adapter_parameters())
+    x = torch.tensor([[1, 2, 3, 4]])
+    assert torch.equal(fresh(x, adapter_mask=x > 1).logits, m(x, adapter_mask=x > 1).logits)
+    cfg = json.loads((tmp_path / "a" / "adapter_config.json").read_text())
+    cfg["use_dora"] = True
+    (tmp_path / "a" / "adapter_config.json").write_text(json.dumps(cfg))
+    with pytest.raises(ValueError):
+        load_peft(fresh, tmp_path / "a")
+    other = LowRankDecoder(LowRankConfig(vocab_size=32, adapter_rank=4))
+    cfg["use_dora"] = False
+    (tmp_path / "a" / "adapter_config.json").write_text(json.dumps(cfg))
+    with pytest.raises(ValueError):
+        load_peft(other, tmp_path / "a")
