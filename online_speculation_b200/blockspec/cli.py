@@ -3,9 +3,11 @@
     python -m online_speculation_b200.blockspec evaluate {benchmark,audit,trace,profile} ...
     python -m online_speculation_b200.blockspec online --model M --prompts P.jsonl ...
     python -m online_speculation_b200.blockspec fit {train,resume,demo} ...
+    python -m online_speculation_b200.blockspec lowrank {demo,train,benchmark} ...
 
 Mirrors the reference command groups (online-speculation/src/blockspec/cli.py,
-commands/{evaluate,continue_training,fit}.py).  ``--model`` is a
+commands/{evaluate,continue_training,fit}.py; the ``lowrank`` group follows
+online-speculation/ablation/src/blockspec_ablation/cli.py demo/train/benchmark).  ``--model`` is a
 ``blockspec-dual-view-v1`` checkpoint, a published dual-view directory, or
 ``random:<preset>`` for random weights (``tiny``, ``qwen3-1.7b``).  With
 ``--engine kernel`` (CUDA, head_dim 128) decoding runs on the sm_100a kernels.
@@ -298,6 +300,88 @@ def cmd_fit(a) -> dict:
             "seconds": time.perf_counter() - t0}
 
 
+def _lowrank_model(spec: str, device: str, dtype):
+    from . import lowrank as lr
+
+    if spec.startswith("random:"):
+        torch.manual_seed(0)
+        presets = {"tiny": lr.LowRankConfig(vocab_size=64),
+                   "small": lr.LowRankConfig(vocab_size=2048, hidden_size=256, intermediate_size=512,
+                                             num_hidden_layers=4, head_dim=64, adapter_rank=16, adapter_alpha=16.0)}
+        return lr.LowRankDecoder(presets[spec.split(":", 1)[1]]).to(device).set_base_dtype(dtype).eval()
+    if Path(spec).is_dir():
+        return lr.from_hf(spec, device=device, dtype=dtype)
+    return lr.load(spec, device=device).set_base_dtype(dtype).eval()
+
+
+def _sequences(path, vocab: int, length: int, device):
+    if path is None:
+        g = torch.Generator().manual_seed(0)
+        base = torch.randint(2, vocab, (4, 8), generator=g)
+        return base.repeat(4, length // 8 + 1)[:, :length].to(device)     # repetitive text a draft can learn
+    rows = [r["input_ids"][:length] for r in read_records(path) if len(r["input_ids"]) >= length]
+    if not rows:
+        raise ValueError("no sequence in the data is long enough")
+    return torch.tensor(rows, device=device)
+
+
+def cmd_lowrank(a) -> dict:
+    from . import lowrank as lr
+    from .lowrank_exec import GraphNoiseBranch
+
+    dtype = {"float32": torch.float32, "bfloat16": torch.bfloat16}[a.dtype]
+    out = {"action": a.action}
+    model = _lowrank_model(a.model, a.device, dtype)
+    if a.action in ("train", "demo"):
+        data = _sequences(a.data, model.config.vocab_size, a.sequence_length, a.device)
+        model.train_adapters_only()
+        opt = torch.optim.AdamW(model.adapter_parameters(), lr=a.lr)
+        g = torch.Generator(device=a.device).manual_seed(0)
+        t0, losses = time.perf_counter(), []
+        for step in range(a.steps):
+            kind = a.warmup_loss if step < a.warmup else a.loss
+            rows = torch.randint(0, data.shape[0], (min(a.batch, data.shape[0]),), generator=g, device=a.device)
+            losses.append(lr.offline_step(model, opt, data[rows], a.block_size, kind=kind, generator=g)["loss"])
+        out.update(steps=a.steps, first_loss=losses[0] if losses else None, final_loss=losses[-1] if losses else None,
+                   train_seconds=time.perf_counter() - t0)
+        if a.save:
+            lr.save(model, a.save)
+        if a.save_peft:
+            lr.save_peft(model, a.save_peft)
+        if a.action == "train":
+            return out
+        model = model.eval().requires_grad_(False)
+    sampling = SamplingConfig(temperature=a.temperature)
+    graph = a.execution == "cuda_graph"
+    branch = (GraphNoiseBranch(model, block_size=a.block_size, capacity=a.capacity) if graph
+              else lr.NoiseBranch(model, block_size=a.block_size))
+    if graph:
+        branch.prepare()
+    prompts = _prompts(a.prompts, a.limit, a.device, model.config.vocab_size)
+    runs = {"ar": [], "static": [], "online": []}
+    learner = lr.LowRankLearner(model, learning_rate=a.online_lr, interval=a.interval) if a.online else None
+    for i, prompt in enumerate(prompts):
+        def gen():
+            return torch.Generator(device=a.device).manual_seed(i)
+
+        runs["ar"].append(generate_ar(branch, prompt, a.max_new_tokens, sampling=sampling, generator=gen()))
+        runs["static"].append(generate(branch, prompt, a.max_new_tokens, sampling=sampling, generator=gen()))
+        if learner is not None:
+            runs["online"].append(generate(branch, prompt, a.max_new_tokens, sampling=sampling, generator=gen(),
+                                           feedback=lr.LowRankFeedback(learner)))
+    for name, rs in runs.items():
+        if rs:
+            secs = sum(r.seconds for r in rs)
+            rounds = sum(len(r.accepted_per_round) for r in rs)
+            out[name] = {"tps": sum(len(r.tokens) for r in rs) / secs if secs else 0.0,
+                         "decode_forwards": sum(r.decode_forwards for r in rs),
+                         "mean_accepted": sum(sum(r.accepted_per_round) for r in rs) / rounds if rounds else None,
+                         "updates": sum(r.updates for r in rs)}
+    out.update(execution=a.execution, block_size=a.block_size, requests=len(prompts),
+               setup_seconds=getattr(branch, "setup_seconds", 0.0))
+    return out
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(prog="python -m online_speculation_b200.blockspec")
     sub = p.add_subparsers(dest="group", required=True)
@@ -306,7 +390,9 @@ def main(argv=None) -> int:
     on = sub.add_parser("online")
     fi = sub.add_parser("fit")
     fi.add_argument("action", choices=("train", "resume", "demo"))
-    for q in (ev, on, fi):
+    lo = sub.add_parser("lowrank")
+    lo.add_argument("action", choices=("demo", "train", "benchmark"))
+    for q in (ev, on, fi, lo):
         q.add_argument("--model", default="random:tiny")
         q.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
         q.add_argument("--prompts", default=None)
@@ -335,12 +421,31 @@ def main(argv=None) -> int:
     fi.add_argument("--anchors", type=int, default=4)
     fi.add_argument("--lr", type=float, default=1e-4)
     fi.add_argument("--warmup", type=int, default=10)
+    lo.add_argument("--dtype", choices=("float32", "bfloat16"), default="float32")
+    lo.add_argument("--data", default=None)
+    lo.add_argument("--steps", type=int, default=30)
+    lo.add_argument("--warmup", type=int, default=0)
+    lo.add_argument("--batch", type=int, default=8)
+    lo.add_argument("--sequence-length", type=int, default=32)
+    lo.add_argument("--block-size", type=int, default=4)
+    lo.add_argument("--lr", type=float, default=1e-2)
+    lo.add_argument("--loss", choices=("l1", "tv", "forward_kl", "reverse_kl", "reverse_kl_l1"), default="l1")
+    lo.add_argument("--warmup-loss", choices=("forward_kl", "reverse_kl", "reverse_kl_l1"), default="reverse_kl_l1")
+    lo.add_argument("--save", default=None)
+    lo.add_argument("--save-peft", default=None)
+    lo.add_argument("--execution", choices=("eager", "cuda_graph"), default="eager")
+    lo.add_argument("--capacity", type=int, default=4096)
+    lo.add_argument("--online", action="store_true")
+    lo.add_argument("--online-lr", type=float, default=1e-3)
+    lo.add_argument("--interval", type=int, default=2)
     a = p.parse_args(argv)
     if a.group == "evaluate":
         out = {"benchmark": cmd_benchmark, "audit": cmd_audit, "trace": cmd_trace,
                "profile": cmd_profile}[a.mode](a)
     elif a.group == "online":
         out = cmd_online(a)
+    elif a.group == "lowrank":
+        out = cmd_lowrank(a)
     else:
         out = cmd_fit(a)
     if a.report:

@@ -199,3 +199,18 @@ def test_measurement_ratio():
 
     r = paired_ratio([10, 10], [1, 1], [10, 10], [2, 2], samples=200)
     assert r["ratio"] == pytest.approx(2.0) and r["ci_low"] <= 2.0 <= r["ci_high"]
+
+
+def test_cli_lowrank(tmp_path):
+    import json
+
+    from online_speculation_b200.blockspec.cli import main
+
+    assert main(["lowrank", "demo", "--device", "cpu", "--steps", "20", "--limit", "2", "--max-new-tokens", "24",
+                 "--temperature", "1.0", "--online", "--save", str(tmp_path / "m.pt"),
+                 "--report", str(tmp_path / "d.json")]) == 0
+    d = json.loads((tmp_path / "d.json").read_text())
+    assert d["final_loss"] < d["first_loss"] and d["static"]["mean_accepted"] is not None
+    assert d["online"]["updates"] >= 1
+    assert main(["lowrank", "benchmark", "--device", "cpu", "--model", str(tmp_path / "m.pt"), "--limit", "1",
+                 "--max-new-tokens", "16"]) == 0
