@@ -1,10 +1,12 @@
 """Headline benchmark: suffix-MH rollouts on a Qwen2.5-7B-shaped decoder with
 block-bidirectional speculative drafting and an online draft learner.
 
-Workload (random-init bf16 weights, synthetic uniform-random prompts):
-  64 chains, each with its own 512-token prompt and 512 generated tokens, power
-  target p^4 (proposal temperature 1/4); every MH update regenerates the suffix
-  after a uniformly drawn cut while reusing the prefix KV.  Drafting uses a
+Workload (random-init bf16 weights, synthetic uniform-random prompt ids):
+  64 chains over one shared 512-token uniform-random prompt (the shape of the
+  reference's batched MH API, which takes one prompt for all chains; both arms
+  run it) and 512 generated tokens each, power target p^4 (proposal temperature
+  1/4); every MH update regenerates the suffix after a uniformly drawn cut while
+  reusing the prefix KV.  Drafting uses a
   1-layer block-4 draft head; the online learner updates every 64 verified blocks.
   Tensor parallel over N GPUs of one node (one process per GPU, NCCL).
 

@@ -394,7 +394,7 @@ void divergence_grad(Tensor s, Tensor t, Tensor lse, Tensor pieces, Tensor w, in
 // pushed: parts are this rank's local receive slots, filled by the ranks' pushing GEMMs.
 void allreduce_norm_impl(std::vector<int64_t> parts, std::vector<int64_t> rows, std::vector<int64_t> pads,
                          Tensor epoch, Tensor h, Tensor w, Tensor x, int64_t T, int64_t rank, double eps,
-                         int64_t blocks, Tensor status, bool pushed) {
+                         int64_t blocks, Tensor status, bool pushed, int64_t algorithm, int64_t wait_ns) {
   CHECK_CUDA(h);
   CHECK_ROWS(h);
   CHECK_ROWS(x);
@@ -425,6 +425,10 @@ void allreduce_norm_impl(std::vector<int64_t> parts, std::vector<int64_t> rows, 
   a.world = world;
   a.eps = static_cast<float>(eps);
   a.status = status.data_ptr<int>();
+  TORCH_CHECK(algorithm >= 0 && algorithm <= 2, "all-reduce algorithm: 0 automatic, 1 one-shot, 2 two-shot");
+  TORCH_CHECK(wait_ns >= 0, "wait limit must be non-negative (0 selects the default)");
+  a.algorithm = static_cast<int>(algorithm);
+  a.wait_ns = static_cast<unsigned long long>(wait_ns);
   if (pushed)
     check(osb::allreduce_pushed_add_rmsnorm_launch(a, static_cast<int>(blocks), at::cuda::getCurrentCUDAStream()),
           "allreduce_pushed_add_rmsnorm");
@@ -435,14 +439,14 @@ void allreduce_norm_impl(std::vector<int64_t> parts, std::vector<int64_t> rows, 
 
 void allreduce_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> rows, std::vector<int64_t> pads,
                            Tensor epoch, Tensor h, Tensor w, Tensor x, int64_t T, int64_t rank, double eps,
-                           int64_t blocks, Tensor status) {
-  allreduce_norm_impl(parts, rows, pads, epoch, h, w, x, T, rank, eps, blocks, status, false);
+                           int64_t blocks, Tensor status, int64_t algorithm, int64_t wait_ns) {
+  allreduce_norm_impl(parts, rows, pads, epoch, h, w, x, T, rank, eps, blocks, status, false, algorithm, wait_ns);
 }
 
 void allreduce_pushed_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_t> pads, Tensor epoch, Tensor h,
                                   Tensor w, Tensor x, int64_t T, int64_t rank, double eps, int64_t blocks,
-                                  Tensor status) {
-  allreduce_norm_impl(parts, {}, pads, epoch, h, w, x, T, rank, eps, blocks, status, true);
+                                  Tensor status, int64_t wait_ns) {
+  allreduce_norm_impl(parts, {}, pads, epoch, h, w, x, T, rank, eps, blocks, status, true, 0, wait_ns);
 }
 
 // Row-parallel GEMM whose bf16 output tile is stored into every rank's receive slot for
@@ -499,7 +503,7 @@ void gemm_push(Tensor w, Tensor x, Tensor out, std::vector<int64_t> dsts, std::v
 void ep_exchange(std::vector<int64_t> tables, std::vector<int64_t> recv_x, std::vector<int64_t> recv_y,
                  std::vector<int64_t> pads, Tensor epoch, int64_t r_max, Tensor counts, Tensor topk_idx,
                  Tensor topk_w, Tensor x, Tensor cursor, Tensor slot_of, Tensor local_offsets, Tensor h, int64_t E,
-                 int64_t k, int64_t rank, int64_t blocks, int64_t phase, Tensor status) {
+                 int64_t k, int64_t rank, int64_t blocks, int64_t phase, Tensor status, int64_t wait_ns) {
   CHECK_CUDA(x);
   CHECK_ROWS(x);
   CHECK_ROWS(h);
@@ -546,6 +550,8 @@ void ep_exchange(std::vector<int64_t> tables, std::vector<int64_t> recv_x, std::
   a.h = bfm(h);
   a.ldh = h.stride(0);
   a.status = status.data_ptr<int>();
+  TORCH_CHECK(wait_ns >= 0, "wait limit must be non-negative (0 selects the default)");
+  a.wait_ns = static_cast<unsigned long long>(wait_ns);
   const int b = static_cast<int>(blocks);
   check(phase == 0 ? osb::ep_dispatch_launch(a, b, at::cuda::getCurrentCUDAStream())
                    : osb::ep_combine_launch(a, b, at::cuda::getCurrentCUDAStream()),

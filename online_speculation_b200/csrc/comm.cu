@@ -56,7 +56,7 @@ __device__ __forceinline__ bool rank_barrier(const ArArgs& a, int slot, uint32_t
     const unsigned long long start = global_ns();
     for (int q = 0; q < a.world && ok; ++q) {
       while (static_cast<int>(ld_acquire_sys(mine + q) - epoch) < 0) {
-        if (global_ns() - start > kWaitLimitNs) {
+        if (global_ns() - start > wait_limit(a.wait_ns)) {
           record_error(a.status, kErrPeerWait);
           ok = 0;
           break;
@@ -78,7 +78,7 @@ __device__ __forceinline__ bool wait_flags(const ArArgs& a, int slot, uint32_t e
     const unsigned long long start = global_ns();
     for (int q = 0; q < a.world && ok; ++q) {
       while (static_cast<int>(ld_acquire_sys(mine + q) - epoch) < 0) {
-        if (global_ns() - start > kWaitLimitNs) {
+        if (global_ns() - start > wait_limit(a.wait_ns)) {
           record_error(a.status, kErrPeerWait);
           ok = 0;
           break;
@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kOneShotThreads) twoshot_norm_kernel(const ArA
     const unsigned long long start = global_ns();
     for (int q = 0; q < a.world && ok2; ++q) {
       while (static_cast<int>(ld_acquire_sys(mine + q) - epoch) < 0) {
-        if (global_ns() - start > kWaitLimitNs) {
+        if (global_ns() - start > wait_limit(a.wait_ns)) {
           record_error(a.status, kErrPeerWait);
           ok2 = 0;
           break;
@@ -335,11 +335,9 @@ __global__ void __launch_bounds__(kOneShotThreads) twoshot_norm_kernel(const ArA
 
 cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
   if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
-  static const int oneshot_max = [] {
-    const char* v = getenv("OSB_AR_ONESHOT_MAX");   // tuning experiments: largest world for one-shot
-    return v ? atoi(v) : 4;
-  }();
-  if (a.world <= oneshot_max) {
+  if (a.algorithm < 0 || a.algorithm > 2) return cudaErrorInvalidValue;
+  const bool oneshot = a.algorithm == 1 || (a.algorithm == 0 && a.world <= 4);
+  if (oneshot) {
     // one row per block (the blocks of a row wait on remote loads; more rows in flight hide that latency)
     const int cap = 4 * blocks;
     const int grid = a.T < cap ? a.T : cap;

@@ -24,6 +24,8 @@ struct ArArgs {
   int T, H, rank, world;
   float eps;
   int* status;
+  int algorithm;                          // 0: one-shot up to four ranks, two-shot above; 1: one-shot; 2: two-shot
+  unsigned long long wait_ns;             // limit of every cross-rank wait (0: two seconds)
 };
 
 cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream);

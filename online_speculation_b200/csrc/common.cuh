@@ -72,8 +72,14 @@ enum KernelError : int {
 #define OSB_DEVICE_CHECKS 1
 #endif
 
-// Two seconds: legitimate waits in this package last microseconds.
+// Default limit of a bounded wait: two seconds (legitimate waits in this package
+// last microseconds).  Kernels that wait on other ranks take a per-call limit
+// (0 selects this default), so a test can make a wait run out in a millisecond.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+__host__ __device__ __forceinline__ unsigned long long wait_limit(unsigned long long requested_ns) {
+  return requested_ns ? requested_ns : kWaitLimitNs;
+}
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;

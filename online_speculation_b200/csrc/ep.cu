@@ -61,7 +61,7 @@ __device__ __forceinline__ bool await_all(const EpArgs& a, int slot, uint32_t ep
   const unsigned long long start = global_ns();
   for (int q = 0; q < a.world && ok; ++q) {
     while (static_cast<int>(ld_acquire_sys(mine + q) - epoch) < 0) {
-      if (global_ns() - start > kWaitLimitNs) {
+      if (global_ns() - start > wait_limit(a.wait_ns)) {
         record_error(a.status, kErrPeerWait);
         ok = false;
         break;

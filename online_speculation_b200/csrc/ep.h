@@ -28,6 +28,7 @@ struct EpArgs {
   __nv_bfloat16* h;                       // local residual [T, H] (row stride ldh), combine adds into it
   long long ldh;
   int* status;
+  unsigned long long wait_ns;             // limit of every cross-rank wait (0: two seconds)
 };
 
 // Exchange routing counts, then copy every (token, choice) row into the receive

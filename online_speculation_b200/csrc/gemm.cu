@@ -729,14 +729,11 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
     }
   }
   if (p.allow_split && p.split_mode == 1 && tiles < sms && p.workspace != nullptr) {
-    int want = std::max(1, sms / tiles);
-    want = std::min(want, std::max(1, a.k_blocks / 2));
-    int per = (a.k_blocks + want - 1) / want;
-    int splits = (a.k_blocks + per - 1) / per;
-    const long long need = static_cast<long long>(splits) * tiles * kBM * BN;
-    if (splits > 1 && need <= p.workspace_floats && tiles <= p.counter_slots) {
-      a.splits = splits;
-      a.kb_per_split = per;
+    const GemmPlan plan = gemm_workspace_plan(p.M, p.N, p.K, sms);
+    if (plan.bn == BN && plan.splits > 1 && plan.workspace_floats <= p.workspace_floats &&
+        tiles <= p.counter_slots) {
+      a.splits = plan.splits;
+      a.kb_per_split = plan.kb_per_split;
     }
   }
   const int total = tiles * a.splits;
@@ -846,13 +843,35 @@ int gemm_pick_bn(int tokens) {
   return 256;
 }
 
-long long gemm_workspace_floats(int M, int N, int K, int sms) {
-  const int bn = gemm_pick_bn(N);
-  const long long tiles = static_cast<long long>((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+int gemm_token_tile(int M, int N, int K) {
+  int bn = gemm_pick_bn(N);
+  // Few weight-row tiles and a short reduction: 128-token tiles double the CTAs
+  // that stream weights and still split K over a cluster pair (measured on B200
+  // at 256 tokens: 7B qkv 22.9 -> 18.5 us, 1.5B qkv 14.7 -> 11.5 us, 1.5B down
+  // 23.1 -> 20.1 us; the 7B down projection, K = 18944, is faster with 256).
+  if (bn == 256 && K <= 10240 && (M + kBM - 1) / kBM < 64) bn = 128;
+  return bn;
+}
+
+GemmPlan gemm_workspace_plan(int M, int N, int K, int sms) {
+  GemmPlan plan{};
+  plan.bn = gemm_token_tile(M, N, K);
+  plan.tiles = ((M + kBM - 1) / kBM) * ((N + plan.bn - 1) / plan.bn);
   const int kb = (K + kBK - 1) / kBK;
-  long long splits = std::min<long long>(std::max<long long>(1, sms / std::max<long long>(1, tiles)),
-                                         std::max(1, kb / 2));
-  return splits * tiles * kBM * bn;
+  plan.splits = 1;
+  plan.kb_per_split = kb;
+  plan.workspace_floats = 0;
+  if (plan.tiles < sms) {
+    const int want = std::min(std::max(1, sms / plan.tiles), std::max(1, kb / 2));
+    const int per = (kb + want - 1) / want;
+    const int splits = (kb + per - 1) / per;
+    if (splits > 1) {
+      plan.splits = splits;
+      plan.kb_per_split = per;
+      plan.workspace_floats = static_cast<long long>(splits) * plan.tiles * kBM * plan.bn;
+    }
+  }
+  return plan;
 }
 
 cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
@@ -871,23 +890,8 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
         (p.group_bn != 32 && p.group_bn != 64 && p.group_bn != 128 && p.group_bn != 256))
       return cudaErrorInvalidValue;
   }
-  int bn = p.group_tiles != nullptr ? p.group_bn : gemm_pick_bn(p.N);
-  static const int bn_cap = [] {
-    const char* v = getenv("OSB_GEMM_BN_CAP");   // tuning experiments: largest token tile allowed
-    return v ? atoi(v) : 0;
-  }();
-  // Few weight-row tiles and a short reduction: 128-token tiles double the CTAs
-  // that stream weights and still split K over a cluster pair (measured on B200
-  // at 256 tokens: 7B qkv 22.9 -> 18.5 us, 1.5B qkv 14.7 -> 11.5 us, 1.5B down
-  // 23.1 -> 20.1 us; the 7B down projection, K = 18944, is faster with 256).
-  if (p.group_tiles == nullptr && bn == 256 && p.K <= 10240 && (p.M + kBM - 1) / kBM < 64) bn = 128;
-  if (p.group_tiles == nullptr && bn_cap >= 32 && bn > bn_cap) bn = bn_cap;
-  static const int split_mode = [] {
-    const char* v = getenv("OSB_GEMM_SPLIT_MODE");   // tuning experiments: 0 cluster, 1 workspace
-    return v ? atoi(v) : -1;
-  }();
-  GemmProblem q = p;
-  if (split_mode >= 0) q.split_mode = split_mode;
+  const int bn = p.group_tiles != nullptr ? p.group_bn : gemm_token_tile(p.M, p.N, p.K);
+  const GemmProblem& q = p;
   a.tiles_m = (p.M + kBM - 1) / kBM;
   a.tiles_n = (p.N + bn - 1) / bn;
   a.out = p.out;

@@ -56,11 +56,24 @@ bool& pdl_enabled();   // programmatic dependent launch for the forward-path ker
 cudaError_t grouped_tiles_launch(const int* offsets, int groups, int tiles_m, int bn, int* tiles, int cap, int* total,
                                  cudaStream_t stream);
 int gemm_pick_bn(int tokens);
+
+// The launcher's plan for a plain (non-grouped) problem: the token tile it uses and,
+// when split-K partials go to a global workspace (split_mode 1), the split factor and
+// the scratch that needs.  gemm_launch and every caller that sizes a workspace for it
+// use this one function, so the sizes agree.
+struct GemmPlan {
+  int bn;                      // token tile (32 / 64 / 128 / 256)
+  int tiles;                   // output tiles (128 weight rows x bn tokens)
+  int splits;                  // split-K factor over the workspace (1: no split)
+  int kb_per_split;            // 64-wide K blocks per split
+  long long workspace_floats;  // fp32 partial tiles the split needs (0 without split)
+};
+int gemm_token_tile(int M, int N, int K);
+GemmPlan gemm_workspace_plan(int M, int N, int K, int sms);
 // Timeline capture for tuning: when non-null, every later launch writes 32 globaltimer
 // slots per CTA (entry, setup, first TMA, first stage, last MMA, first accumulator,
 // epilogue done, exit, then per-chunk and cluster-epilogue stamps) into this device
 // buffer, which must hold grid x 32 values.
 unsigned long long*& gemm_trace_buffer();
-long long gemm_workspace_floats(int M, int N, int K, int sms);
 
 }  // namespace osb

@@ -36,7 +36,7 @@ class Collectives:
     """
 
     def __init__(self, group=None, *, hidden: int = 0, max_tokens: int = 0, device=None, fused: bool = True,
-                 push: bool | None = None):
+                 push: bool | None = None, algorithm: str = "auto"):
         self.group = group
         self.impl = None
         if group is None:
@@ -50,7 +50,7 @@ class Collectives:
             from ..parallel.symm import NcclCollectives, SymmetricCollectives
 
             if fused:
-                self.impl = SymmetricCollectives(group, hidden, max_tokens, device, push=push)
+                self.impl = SymmetricCollectives(group, hidden, max_tokens, device, push=push, algorithm=algorithm)
             else:
                 self.impl = NcclCollectives(group, hidden, max_tokens, device)
 

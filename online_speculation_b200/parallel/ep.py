@@ -41,7 +41,8 @@ class ExpertParallelMoE:
     """Fused expert-parallel MoE exchange over symmetric memory."""
 
     def __init__(self, group, *, experts: int, top_k: int, hidden: int, ffn: int, max_tokens: int, device,
-                 blocks: int = 132):
+                 blocks: int = 132, wait_limit_ns: int = 0):
+        """``wait_limit_ns`` bounds every cross-rank wait of the exchange kernels (0: two seconds)."""
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm
 
@@ -57,6 +58,7 @@ class ExpertParallelMoE:
         self.max_tokens = max_tokens
         self.device = torch.device(device)
         self.blocks = blocks
+        self.wait_limit_ns = int(wait_limit_ns)
         # worst case: every rank routes every choice of every token to this rank
         self.r_max = max_tokens * top_k * self.world
         self._table = symm.empty(self.world * experts, dtype=torch.int32, device=self.device)
@@ -99,7 +101,7 @@ class ExpertParallelMoE:
         st = workspace.status(self.device)
         args = (self._tables, self._xs, self._ys, self._pads, self.epoch, self.r_max, rt.counts, rt.idx, rt.w, x,
                 self.cursor, self.slot_of, self.local_offsets, h, self.E, self.k, self.rank, self.blocks)
-        ext.ep_exchange(*args, 0, st)
+        ext.ep_exchange(*args, 0, st, self.wait_limit_ns)
         # local experts over the received rows (tile list built on the device from the exchanged counts)
         bn = K.moe_pick_bn(rows, self.E_local)
         ws, ctr = workspace.gemm_workspace(self.device), workspace.gemm_counters(self.device)
@@ -110,7 +112,7 @@ class ExpertParallelMoE:
         ext.grouped_tiles(self.local_offsets, self.E_local, tm_dn, bn, self.tiles[1], self.total[1:2])
         ext.grouped_gemm(w_down, self.act, self._recv_y, 0, self.tiles[1], self.total[1:2], self.E_local, bn, ws,
                          ctr, st)
-        ext.ep_exchange(*args, 1, st)
+        ext.ep_exchange(*args, 1, st, self.wait_limit_ns)
         return h
 
 

@@ -63,7 +63,13 @@ class SymmetricCollectives(NcclCollectives):
     PUSH_SLOT = 4          # flag slot of the pushing GEMMs (csrc/comm.h kPushSlot)
     MAX_RANKS = 8
 
-    def __init__(self, group, hidden: int, max_tokens: int, device, *, blocks: int = 132, push: bool | None = None):
+    ALGORITHMS = {"auto": 0, "oneshot": 1, "twoshot": 2}
+
+    def __init__(self, group, hidden: int, max_tokens: int, device, *, blocks: int = 132, push: bool | None = None,
+                 algorithm: str = "auto", wait_limit_ns: int = 0):
+        """``algorithm``: "auto" (one-shot up to four ranks, two-shot above), "oneshot" or "twoshot".
+        ``wait_limit_ns``: limit of every cross-rank wait inside the kernels (0: two seconds); a wait
+        that runs out records an error in the status word instead of hanging."""
         import os
 
         import torch.distributed as dist
@@ -75,6 +81,10 @@ class SymmetricCollectives(NcclCollectives):
         if self.world > 8:
             raise ValueError("the fused all-reduce supports at most 8 ranks")
         self.device = torch.device(device)
+        if algorithm not in self.ALGORITHMS:
+            raise ValueError(f"algorithm must be one of {sorted(self.ALGORITHMS)}")
+        self.algorithm = self.ALGORITHMS[algorithm]
+        self.wait_limit_ns = int(wait_limit_ns)
         self.blocks = blocks
         self.hidden = hidden
         self.max_tokens = max_tokens
@@ -145,7 +155,7 @@ class SymmetricCollectives(NcclCollectives):
             T = part.shape[0]
             _ext.require().allreduce_pushed_add_rmsnorm(self._push_local[pf], self._pads, self.epoch, h, w, x, T,
                                                         self.rank, float(eps), self.blocks,
-                                                        workspace.status(self.device))
+                                                        workspace.status(self.device), self.wait_limit_ns)
             return
         flip = 0 if part.data_ptr() == self._bufs[0].data_ptr() else 1
         if part.data_ptr() != self._bufs[flip].data_ptr():
@@ -153,4 +163,4 @@ class SymmetricCollectives(NcclCollectives):
         T = part.shape[0]
         _ext.require().allreduce_add_rmsnorm(self._parts_ptrs[flip], self._rows_ptrs, self._pads, self.epoch, h, w,
                                              x, T, self.rank, float(eps), self.blocks,
-                                             workspace.status(self.device))
+                                             workspace.status(self.device), self.algorithm, self.wait_limit_ns)

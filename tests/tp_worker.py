@@ -21,8 +21,10 @@ from online_speculation_b200.engine.runner import Collectives, ModelRunner, buil
 from online_speculation_b200.models.decoder import DecoderConfig, build_weights, random_state_dict, reference_forward  # noqa: E402
 from online_speculation_b200.ops import workspace  # noqa: E402
 
-CFG = DecoderConfig(vocab_size=1024, hidden_size=512, intermediate_size=1024, num_hidden_layers=3,
-                    num_attention_heads=8, num_key_value_heads=2, name="small")
+# 14 query heads over 2 KV heads: at 4 and 8 ranks the query heads are padded to 16
+# (zero heads) and every KV head is replicated on the ranks that share it.
+CFG = DecoderConfig(vocab_size=1024, hidden_size=1792, intermediate_size=1024, num_hidden_layers=3,
+                    num_attention_heads=14, num_key_value_heads=2, name="small")
 
 
 def rel(a, b):
@@ -39,14 +41,20 @@ def main():
     torch.manual_seed(0)
     seq = torch.randint(0, CFG.vocab_size, (70,))
     ref = reference_forward(CFG, {k: v.cpu() for k, v in sd.items()}, seq)
-    # NCCL baseline, fused pull all-reduce, and GEMM push + local reduction
-    for fused, push in ((False, None), (True, False), (True, True)):
+    # NCCL baseline, fused pull all-reduce (both algorithms at every world size), and
+    # GEMM push + local reduction (up to four ranks)
+    variants = [(False, None, "auto"), (True, False, "oneshot"), (True, False, "twoshot")]
+    if world <= 4:
+        variants.append((True, True, "auto"))
+    for fused, push, algorithm in variants:
         w = build_weights(CFG, sd, tp=world, rank=rank, device=dev)
+        if world > 2:
+            assert w.heads.q_slots * world > CFG.num_attention_heads   # padded query heads
         cache = KVCache(CFG.num_hidden_layers, w.heads.kv_slots, 64, dev)
         comm = Collectives(dist.group.WORLD, hidden=CFG.hidden_size, max_tokens=1024, device=dev, fused=fused,
-                           push=push)
+                           push=push, algorithm=algorithm)
         if fused:
-            assert comm.impl.push == (push and world <= 4)
+            assert comm.impl.push == bool(push and world <= 4)
         r = ModelRunner(w, cache, collectives=comm, max_tokens=1024)
         G = r.q_slots // r.kv_slots
         s = cache.create()
@@ -54,11 +62,11 @@ def main():
         slots = cache.append(s, 60)
         cache.fill_table([s], table)
         out = r.forward(build_meta(dev, table, seq[:60].tolist(), list(range(60)), slots, [60], [60], [0], G))
-        assert rel(out.cpu(), ref[:60]) < 3e-2, ("prefill", fused, push, rel(out.cpu(), ref[:60]))
+        assert rel(out.cpu(), ref[:60]) < 3e-2, ("prefill", fused, push, algorithm, rel(out.cpu(), ref[:60]))
         slots = cache.append(s, 4)
         cache.fill_table([s], table)
         out = r.forward(build_meta(dev, table, seq[60:64].tolist(), list(range(60, 64)), slots, [4], [64], [0], G))
-        assert rel(out.cpu(), ref[60:64]) < 3e-2, ("verify", fused, push)
+        assert rel(out.cpu(), ref[60:64]) < 3e-2, ("verify", fused, push, algorithm)
         torch.cuda.synchronize()
         workspace.check_status(dev)
     # vocabulary-parallel samplers draw exactly what the unsharded kernels draw on full rows
