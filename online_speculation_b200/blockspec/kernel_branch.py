@@ -104,7 +104,7 @@ class KernelBranch:
         r.cache.fill_table([cache.seq], table)
         G = r.q_slots // r.kv_slots
         return build_meta(self.device, table, tokens, list(range(cache.length, cache.length + n)), slots, [n],
-                          [cache.length + n], [mode], G, logit_rows=rows, tile_rows=64 if n * G > 64 else None)
+                          [cache.length + n], [mode], G, logit_rows=rows, kv_heads=r.kv_slots)
 
     def ar(self, tokens: torch.Tensor, cache: PagedHistory | None = None, logits_to_keep: int = 0):
         if cache is None:

@@ -52,6 +52,7 @@ struct AttnArgs {
   int Hq, Hkv, G;
   float scale_log2;  // softmax scale * log2(e)
   int* status;
+  unsigned long long* trace;  // tcgen05 kernel timeline (tuning): kTraceSlots globaltimer stamps per CTA, or null
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -537,13 +538,503 @@ __global__ void __launch_bounds__(128 * MT, 2)
   }
 }
 
-// 2-D view [pages * Hkv * P rows, D columns] of one cache, 16-key x 64-column boxes.
-bool make_cache_map(CUtensorMap* map, const void* ptr, long long rows) {
+
+// ------------------------------------------------------------------------------
+// tcgen05 attention (every shape: prefill, decode, verify / draft blocks, diffusion).
+//
+// One CTA computes a 128-row query tile of one (sequence, kv head) over a range of
+// key chunks; with key splitting, the S CTAs of a thread-block cluster take
+// consecutive chunk ranges of the same tile and merge their partial softmax states
+// through distributed shared memory.
+//
+//   warp 0      TMA producer: per 64-key chunk (two pages) the K and V rows of this
+//               kv head, two 64-column boxes each with 128-byte swizzle, into a
+//               3-stage ring (full / empty mbarriers).
+//   warp 1      TMEM owner and MMA issuer (one thread):
+//                 S_j = Q K_j^T     M=128, N=64, K=128  (Q, K both K-major)
+//                 O  += P_j V_j     M=128, N=128, K=64  (P K-major, V MN-major)
+//               S is double-buffered in TMEM (columns 0-63 / 64-127), O lives in
+//               columns 128-255.  S_{j+1} is issued before O += P_j V_j, so the
+//               softmax of chunk j+1 overlaps the P V product of chunk j.
+//   warps 2-5   one thread per query row (TMEM lane): load the row of S, mask,
+//               online softmax in the log2 domain, write P (bf16, K-major SW128)
+//               to shared memory, arrive.  The running maximum is only raised when
+//               a chunk's maximum exceeds it by more than 8 (a factor of 256), so
+//               the O rescale (TMEM load, scale, store) is rare; it waits for the
+//               previous P V product first.  Rows past the sequence end in the last
+//               chunk are zeroed in the V stage before P V (their probabilities are
+//               exactly zero, but 0 x a non-finite stale value is not).
+// Query rows of one (sequence, kv head) are flattened token-major (row = token * G
+// + head_in_group), as in the kernels above.  Every wait is bounded.
+namespace tca {
+constexpr int kRows = 128;
+constexpr int kNC = 64;                         // keys per chunk (two 32-key pages)
+constexpr int kStages = 4;
+constexpr int kBox = kRows * 128;               // 128 rows x 64 bf16 columns, SW128: 16 KB
+constexpr int kQBytes = 2 * kBox;               // Q tile: two column boxes
+constexpr int kKVBox = kNC * 128;               // 64 keys x 64 columns: 8 KB
+constexpr int kPageBox = kPage * 128;           // 32 keys x 64 columns: 4 KB (one TMA box)
+constexpr int kStageBytes = 4 * kKVBox;         // K lo | K hi | V lo | V hi
+constexpr int kPBytes = kRows * 128;            // P tile: 128 rows x 64 keys bf16
+constexpr int kOffKV = kQBytes;
+constexpr int kOffP = kOffKV + kStages * kStageBytes;
+constexpr int kOffBar = kOffP + 2 * kPBytes;
+constexpr int kNumBars = 14;
+constexpr int kOffMisc = kOffBar + 16 * 8;
+constexpr int kOffML = kOffMisc + 16;
+constexpr int kSmem = 1024 + kOffML + 2 * kRows * 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kColO = 128;
+constexpr int kMergeRow = 132;                  // fp32 row of the cluster merge buffer
+constexpr float kRescaleLog2 = 8.0f;
+constexpr int kMaxSplits = 8;
+constexpr uint32_t kIdescS = idesc_bf16_f32(kRows, kNC);
+constexpr uint32_t kIdescPV = idesc_bf16_f32(kRows, kD) | (1u << 16);   // B (V) MN-major
+static_assert(kRows * kMergeRow * 4 <= kStages * kStageBytes, "merge buffer reuses the KV ring");
+
+// Timeline slots per traced CTA (the first kTraceCtas CTAs of the grid): 0 entry,
+// 1 after set-up, then per chunk j < 24: 2+j producer issued, 26+j S issued,
+// 50+j P arrived at the MMA issuer, 74+j S seen by softmax warp 2, 98+j P written
+// by softmax warp 2; 122 softmax done, 123 exit.
+constexpr int kTraceSlots = 128;
+constexpr int kTraceCtas = 8;
+constexpr int kTraceChunks = 24;
+
+__device__ __forceinline__ uint32_t sw128_row_chunk(int row, int chunk) {
+  return (row >> 3) * 1024 + (row & 7) * 128 + (((chunk ^ row) & 7) << 4);
+}
+
+// Non-blocking test of one mbarrier phase (the MMA issuer polls two barriers).
+__device__ __forceinline__ bool mbar_ready(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// 2^x with the hardware approximation (flush-to-zero); probabilities are rounded to
+// bf16 right after, so its error (a few ulp of fp32) is far below what is kept.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 32 lanes x 64 consecutive fp32 TMEM columns in one load, one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
+      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
+}  // namespace tca
+
+template <bool kSplit>
+__global__ void __launch_bounds__(tca::kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   const AttnArgs a, int splits) {
+  using namespace tca;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = base;
+  uint8_t* sKV = base + kOffKV;
+  uint8_t* sP = base + kOffP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + kOffBar);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 1 + kStages;
+  uint64_t* s_full = bars + 1 + 2 * kStages;
+  uint64_t* p_full = s_full + 2;
+  // o_done[j & 1] completes when O += P_j V_j is done.  Two barriers alternate by
+  // chunk so that every wait targets a phase at most one completion away: when the
+  // softmax waits for product j, product j - 2 is known complete and product j + 2
+  // cannot have been issued.
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + kOffMisc);
+  float* sm_m = reinterpret_cast<float*>(base + kOffML);
+  float* sm_l = sm_m + kRows;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0 && a.trace != nullptr && blockIdx.y * gridDim.x + blockIdx.x < tca::kTraceCtas)
+    a.trace[(blockIdx.y * gridDim.x + blockIdx.x) * tca::kTraceSlots] = global_ns();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 4);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
+  const int cta = blockIdx.y * gridDim.x + blockIdx.x;
+  unsigned long long* trace = (a.trace != nullptr && cta < kTraceCtas) ? a.trace + cta * kTraceSlots : nullptr;
+  auto stamp = [&](int slot) {
+    if (trace != nullptr) trace[slot] = global_ns();
+  };
+  if (threadIdx.x == 0) stamp(1);
+
+  const int S = kSplit ? splits : 1;
+  const int split = kSplit ? static_cast<int>(cluster_ctarank()) : 0;
+  const int tile = blockIdx.x / S, g = blockIdx.y;
+  const int b = a.tile_seq[tile];
+  const int row0 = a.tile_row0[tile];
+  const int qlen = a.q_len[b], kvlen = a.kv_len[b], q0 = a.q_start[b];
+  const int bidir = a.mode[b];
+  const int rows = qlen * a.G;
+  const int last_row = min(rows - 1, row0 + kRows - 1);
+  const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
+  const int nch_all = (max(max_key, 0) + kNC - 1) / kNC;
+  const int per = (nch_all + S - 1) / S;
+  const int c0 = min(nch_all, split * per);
+  const int n = min(nch_all, c0 + per) - c0;
+  const int* tbl = a.table + static_cast<long long>(b) * a.table_stride;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kStages;
+        if (!mbar_wait(&kv_empty[s], ((j / kStages) & 1) ^ 1, a.status, kErrTmaWait)) break;
+        const int key0 = (c0 + j) * kNC;
+        const int pages = min(2, (kvlen - key0 + kPage - 1) / kPage);
+        uint8_t* dst = sKV + s * kStageBytes;
+        mbar_arrive_expect_tx(&kv_full[s], pages * 4 * kPageBox);
+        for (int pi = 0; pi < pages; ++pi) {
+          const int y = (tbl[key0 / kPage + pi] * a.Hkv + g) * kPage;
+          tma_load_2d(dst + pi * kPageBox, &kmap, 0, y, &kv_full[s]);
+          tma_load_2d(dst + kKVBox + pi * kPageBox, &kmap, 64, y, &kv_full[s]);
+          tma_load_2d(dst + 2 * kKVBox + pi * kPageBox, &vmap, 0, y, &kv_full[s]);
+          tma_load_2d(dst + 3 * kKVBox + pi * kPageBox, &vmap, 64, y, &kv_full[s]);
+        }
+        issued = j + 1;
+        if (j < kTraceChunks) stamp(2 + j);
+      }
+      // Copies still in flight must land before the CTA exits: wait for the last
+      // stages' phases (their stage was not reused, so the parity is unambiguous).
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, a.status, kErrTmaWait);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0 && n > 0) {
+      const uint32_t qa = smem_u32(sQ);
+      auto issue_s = [&](int j) {
+        const uint32_t kb = smem_u32(sKV + (j % kStages) * kStageBytes);
+        const uint32_t d = tmem + (j & 1) * kNC;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint64_t ad = sdesc_k_sw128(qa + (kk >> 2) * kBox + (kk & 3) * 32);
+          const uint64_t bd = sdesc_k_sw128(kb + (kk >> 2) * kKVBox + (kk & 3) * 32);
+          tc_mma_bf16(d, ad, bd, kIdescS, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[j & 1]);
+        if (j < kTraceChunks) stamp(26 + j);
+      };
+      auto issue_pv = [&](int j) {
+        const int s = j % kStages;
+        const uint32_t vb = smem_u32(sKV + s * kStageBytes + 2 * kKVBox);
+        const uint32_t pb = smem_u32(sP + (j & 1) * kPBytes);
+#pragma unroll
+        for (int kk = 0; kk < kNC / 16; ++kk) {
+          const uint64_t ad = sdesc_k_sw128(pb + kk * 32);
+          const uint64_t bd = sdesc_mn_sw128(vb + kk * 16 * 128, kKVBox, 1024);
+          tc_mma_bf16(tmem + kColO, ad, bd, kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&kv_empty[s]);
+        tc_commit(&o_done[j & 1]);
+      };
+      // Issue whichever product is ready, never holding a P V product (which frees a
+      // KV stage) behind a K tile that is still in flight.  S_ns may be issued once the
+      // softmax has read S_{ns-2} (same TMEM buffer), i.e. once P_{ns-2} arrived, which
+      // holds when ns - np < 2; P_np needs S_np, so np < ns.
+      bool ok = mbar_wait(q_full, 0, a.status, kErrMmaWait);
+      tc_fence_after();
+      int ns = 0, np = 0;
+      unsigned long long idle_since = 0;
+      while (ok && np < n) {
+        if (ns < n && ns - np < 2 && mbar_ready(&kv_full[ns % kStages], (ns / kStages) & 1)) {
+          tc_fence_after();
+          issue_s(ns);
+          ++ns;
+          idle_since = 0;
+        } else if (np < ns && mbar_ready(&p_full[np & 1], (np >> 1) & 1)) {
+          tc_fence_after();
+          if (np < kTraceChunks) stamp(50 + np);
+          issue_pv(np);
+          ++np;
+          idle_since = 0;
+        } else if (idle_since == 0) {
+          idle_since = global_ns();
+        } else if (global_ns() - idle_since > kWaitLimitNs) {
+          record_error(a.status, kErrMmaWait);
+          ok = false;
+        }
+      }
+      // every issued MMA completes before TMEM can be released
+      tc_commit(drain);
+      mbar_wait(drain, 0, a.status, kErrMmaWait);
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int quarter = warp & 3;
+    const int t = quarter * 32 + lane;
+    const int row = row0 + t;
+    const bool valid_row = row < rows;
+    const int qpos = valid_row ? kvlen - qlen + row / a.G : -1;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    {
+      const uint4* src = nullptr;
+      if (valid_row) {
+        const int tok = row / a.G, head = g * a.G + row % a.G;
+        src = reinterpret_cast<const uint4*>(a.q + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD);
+      }
+#pragma unroll
+      for (int c = 0; c < kD / 8; ++c) {
+        const uint4 v = valid_row ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sQ + (c >> 3) * kBox + sw128_row_chunk(t, c & 7)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full);
+    }
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.status, kErrEpilogueWait));
+      if (!ok) break;
+      tc_fence_after();
+      if (warp == 2 && lane == 0 && j < kTraceChunks) stamp(74 + j);
+      float sc[kNC];
+      tmem_ld64(tmem + lane_base + (j & 1) * kNC, sc);
+      const int key0 = (c0 + j) * kNC;
+      // eight independent max chains, then a short tree
+      float mp[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mp[k] = -INFINITY;
+      if (valid_row && key0 + kNC <= kvlen && (bidir || key0 + kNC - 1 <= qpos)) {
+#pragma unroll
+        for (int i = 0; i < kNC; ++i) {
+          sc[i] *= a.scale_log2;
+          mp[i & 7] = fmaxf(mp[i & 7], sc[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kNC; ++i) {
+          const int key = key0 + i;
+          const bool vis = valid_row && key < kvlen && (bidir || key <= qpos);
+          sc[i] = vis ? sc[i] * a.scale_log2 : -INFINITY;
+          mp[i & 7] = fmaxf(mp[i & 7], sc[i]);
+        }
+      }
+      const float mx = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+      if (j == 0) {
+        m = mx;
+      } else {
+        const bool need = mx > m + kRescaleLog2;
+        if (__any_sync(0xffffffffu, need)) {
+          const float mnew = need ? mx : m;
+          const float corr = (m == -INFINITY) ? 0.0f : exp2f(m - mnew);
+          // O holds the products of chunks < j once the previous P V product is done
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status, kErrEpilogueWait));
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < kD / 32; ++c) {
+            float o[32];
+            tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tmem_st32(tmem + lane_base + kColO + c * 32, o);
+          }
+          l *= corr;
+          m = mnew;
+        }
+      }
+      if (key0 + kNC > kvlen) {
+        // last chunk: zero the V rows past the sequence end (acquire the stage first;
+        // its phase is complete and not yet reused, so this returns at once)
+        const int s = j % kStages;
+        mbar_wait(&kv_full[s], (j / kStages) & 1, a.status, kErrEpilogueWait);
+        const int valid = max(0, kvlen - key0);
+        uint8_t* v = sKV + s * kStageBytes + 2 * kKVBox;
+        for (int c = t; c < 2 * kNC * 8; c += kRows) {
+          const int box = c / (kNC * 8), r = (c / 8) % kNC, seg = c % 8;
+          if (r >= valid) *reinterpret_cast<uint4*>(v + box * kKVBox + r * 128 + seg * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      uint8_t* prow = sP + (j & 1) * kPBytes;
+      // rows that see no key yet keep m = -inf: shift by 0 instead (every score is -inf, 2^-inf = 0)
+      const float shift = (m == -INFINITY) ? 0.0f : m;
+      float sp[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sp[k] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < kNC / 8; ++c) {
+        uint32_t w4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = fast_exp2(sc[c * 8 + 2 * e] - shift);
+          const float p1 = fast_exp2(sc[c * 8 + 2 * e + 1] - shift);
+          sp[2 * e] += p0;
+          sp[2 * e + 1] += p1;
+          w4[e] = pack_bf16(p0, p1);
+        }
+        *reinterpret_cast<uint4*>(prow + sw128_row_chunk(t, c)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+      }
+      l += ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+      if (warp == 2 && lane == 0 && j < kTraceChunks) stamp(98 + j);
+    }
+    if (warp == 2 && lane == 0) stamp(122);
+    const bool have = n > 0 && ok &&
+                      __all_sync(0xffffffffu, mbar_wait(&o_done[(n - 1) & 1], ((n - 1) >> 1) & 1, a.status,
+                                                        kErrEpilogueWait));
+    if (have) tc_fence_after();
+    if (!kSplit) {
+      if (have) {
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        __nv_bfloat16* dst = nullptr;
+        if (valid_row) {
+          const int tok = row / a.G, head = g * a.G + row % a.G;
+          dst = a.out + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD;
+        }
+#pragma unroll
+        for (int c = 0; c < kD / 32; ++c) {
+          float o[32];
+          tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+          if (valid_row) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint4 w;
+              w.x = pack_bf16(o[8 * e] * inv, o[8 * e + 1] * inv);
+              w.y = pack_bf16(o[8 * e + 2] * inv, o[8 * e + 3] * inv);
+              w.z = pack_bf16(o[8 * e + 4] * inv, o[8 * e + 5] * inv);
+              w.w = pack_bf16(o[8 * e + 6] * inv, o[8 * e + 7] * inv);
+              *reinterpret_cast<uint4*>(dst + c * 32 + 8 * e) = w;
+            }
+          }
+        }
+      } else if (valid_row && n == 0) {
+        // no visible key (empty sequence): the output row is zero
+        const int tok = row / a.G, head = g * a.G + row % a.G;
+        uint4* dst = reinterpret_cast<uint4*>(a.out + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD);
+        for (int c = 0; c < kD / 8; ++c) dst[c] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      // this CTA's partial state for the cluster merge (the KV ring is idle now)
+      float* mo = reinterpret_cast<float*>(sKV) + t * kMergeRow;
+      if (have) {
+#pragma unroll
+        for (int c = 0; c < kD / 32; ++c) {
+          float o[32];
+          tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            *reinterpret_cast<float4*>(mo + c * 32 + 4 * e) = make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+        }
+      }
+      sm_m[t] = have ? m : -INFINITY;
+      sm_l[t] = have ? l : 0.0f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (kSplit) {
+    cluster_sync();
+    if (warp >= 2) {
+      const float* mo0 = reinterpret_cast<const float*>(sKV);
+      for (int r = split + S * (warp - 2); r < kRows; r += 4 * S) {
+        const int row = row0 + r;
+        if (row >= rows) break;
+        float mk[kMaxSplits], wk[kMaxSplits];
+        float M = -INFINITY, L = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kMaxSplits; ++k) {
+          mk[k] = k < S ? ld_dsmem_f32(map_shared_rank(smem_u32(sm_m + r), k)) : -INFINITY;
+          M = fmaxf(M, mk[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < kMaxSplits; ++k) {
+          wk[k] = (k >= S || mk[k] == -INFINITY) ? 0.0f : exp2f(mk[k] - M);
+          if (wk[k] != 0.0f) L += wk[k] * ld_dsmem_f32(map_shared_rank(smem_u32(sm_l + r), k));
+        }
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < kMaxSplits; ++k) {
+          if (wk[k] == 0.0f) continue;
+          const float4 x = ld_dsmem_f4(map_shared_rank(smem_u32(mo0 + r * kMergeRow + lane * 4), k));
+          acc.x += wk[k] * x.x;
+          acc.y += wk[k] * x.y;
+          acc.z += wk[k] * x.z;
+          acc.w += wk[k] * x.w;
+        }
+        const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+        const int tok = row / a.G, head = g * a.G + row % a.G;
+        __nv_bfloat16* dst = a.out + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD + lane * 4;
+        uint2 w;
+        w.x = pack_bf16(acc.x * inv, acc.y * inv);
+        w.y = pack_bf16(acc.z * inv, acc.w * inv);
+        *reinterpret_cast<uint2*>(dst) = w;
+      }
+    }
+    cluster_sync();   // peers read this CTA's shared memory until here
+  }
+  if (threadIdx.x == 0) stamp(123);
+}
+
+// 2-D view [pages * Hkv * P rows, D columns] of one cache, box_rows-key x 64-column boxes.
+bool make_cache_map(CUtensorMap* map, const void* ptr, long long rows, int box_rows = kCh) {
   EncodeTiledFn fn = tensor_map_encoder();
   if (!fn || rows <= 0 || (reinterpret_cast<uintptr_t>(ptr) % 16)) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD) * 2};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kCh)};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -568,7 +1059,54 @@ cudaError_t launch_tma(const AttentionProblem& p, const AttnArgs& a, dim3 grid, 
   return launch_pdl(attn_tma_kernel<MT>, grid, dim3(128 * MT), TmaSmem<MT>::kTotal, stream, km, vm, a);
 }
 
+
+cudaError_t launch_tc(const AttentionProblem& p, const AttnArgs& a, cudaStream_t stream) {
+  const int S = p.kv_splits;
+  if (S != 1 && S != 2 && S != 4 && S != 8) return cudaErrorInvalidValue;
+  CUtensorMap km, vm;
+  const long long rows = static_cast<long long>(p.cache_pages) * p.Hkv * kPage;
+  if (!make_cache_map(&km, p.k_cache, rows, kPage) || !make_cache_map(&vm, p.v_cache, rows, kPage))
+    return cudaErrorInvalidValue;
+  static bool attr[2][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int which = S > 1 ? 1 : 0;
+  if (dev < 64 && !attr[which][dev]) {
+    cudaError_t e = cudaFuncSetAttribute(S > 1 ? attn_tc_kernel<true> : attn_tc_kernel<false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, tca::kSmem);
+    if (e != cudaSuccess) return e;
+    attr[which][dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.num_tiles * S, p.Hkv);
+  cfg.blockDim = dim3(tca::kThreads);
+  cfg.dynamicSmemBytes = tca::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (S > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = S;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  return S > 1 ? cudaLaunchKernelEx(&cfg, attn_tc_kernel<true>, km, vm, a, S)
+               : cudaLaunchKernelEx(&cfg, attn_tc_kernel<false>, km, vm, a, 1);
+}
 }  // namespace
+
+unsigned long long*& attention_trace_buffer() {
+  static unsigned long long* buf = nullptr;
+  return buf;
+}
 
 cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream) {
   if (p.head_dim != kD || p.page_size != kPage || p.Hkv <= 0 || p.Hq % p.Hkv) return cudaErrorInvalidValue;
@@ -590,9 +1128,12 @@ cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream) {
   a.G = p.Hq / p.Hkv;
   a.scale_log2 = p.scale * 1.4426950408889634f;
   a.status = p.status;
+  a.trace = attention_trace_buffer();
   if (p.num_tiles <= 0) return cudaSuccess;
   dim3 grid(p.num_tiles, p.Hkv);
-  if (p.tile_rows == 64) {
+  if (p.tile_rows == 128) {
+    return launch_tc(p, a, stream);
+  } else if (p.tile_rows == 64) {
     return launch_pdl(attn_rows_kernel, grid, dim3(128), 0, stream, a);
   } else if (p.tile_rows == 16) {
     return launch_tma<1>(p, a, grid, stream);

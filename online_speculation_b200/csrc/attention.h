@@ -18,7 +18,8 @@ struct AttentionProblem {
   const int* tile_seq;           // [num_tiles]
   const int* tile_row0;          // [num_tiles]
   int num_tiles;
-  int tile_rows;                 // 64 (rows split across warps) or 16 / 32 (keys split across warps)
+  int tile_rows;                 // 128: tcgen05 kernel; 64 / 16 / 32: mma.sync kernels (rows / keys split across warps)
+  int kv_splits;                 // tcgen05 kernel: key ranges per tile, merged within a cluster (1, 2, 4, 8)
   __nv_bfloat16* out;            // [T, Hq, D]
   int Hq, Hkv, head_dim, page_size;
   int cache_pages;               // pages in k_cache / v_cache
@@ -27,5 +28,11 @@ struct AttentionProblem {
 };
 
 cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream);
+
+// Timeline capture for tuning the tcgen05 kernel: when non-null, its first 8 CTAs
+// write 128 globaltimer stamps each (entry, set-up, and per key chunk the producer's
+// issue, the S product's issue, P's arrival at the MMA issuer, S and P as seen by the
+// first softmax warp) into this device buffer of at least 1024 values.
+unsigned long long*& attention_trace_buffer();
 
 }  // namespace osb

@@ -42,7 +42,8 @@ __nv_bfloat16* bfm(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.
 
 // out[N, M or M/2] = x[N, K] @ w[M, K]^T (+ bias) (+ residual)
 void gemm(Tensor w, Tensor x, Tensor out, c10::optional<Tensor> bias, c10::optional<Tensor> residual, int64_t epilogue,
-          bool allow_split, Tensor workspace, Tensor counters, Tensor status, bool prefetch_weights) {
+          bool allow_split, Tensor workspace, Tensor counters, Tensor status, bool prefetch_weights,
+          int64_t split_mode) {
   CHECK_CUDA(w);
   CHECK_CUDA(x);
   CHECK_CUDA(out);
@@ -85,6 +86,8 @@ void gemm(Tensor w, Tensor x, Tensor out, c10::optional<Tensor> bias, c10::optio
   p.ldr = residual.has_value() && residual->defined() ? residual->stride(0) : 0;
   p.epilogue = static_cast<int>(epilogue);
   p.allow_split = allow_split ? 1 : 0;
+  TORCH_CHECK(split_mode == 0 || split_mode == 1, "split_mode: 0 cluster (DSMEM), 1 global workspace");
+  p.split_mode = static_cast<int>(split_mode);
   p.workspace = workspace.data_ptr<float>();
   p.workspace_floats = workspace.numel();
   p.counters = counters.data_ptr<int>();
@@ -95,8 +98,8 @@ void gemm(Tensor w, Tensor x, Tensor out, c10::optional<Tensor> bias, c10::optio
 }
 
 void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_start, Tensor q_len, Tensor kv_len,
-               Tensor mode, Tensor tile_seq, Tensor tile_row0, int64_t tile_rows, Tensor out, double scale,
-               Tensor status) {
+               Tensor mode, Tensor tile_seq, Tensor tile_row0, int64_t tile_rows, int64_t kv_splits, Tensor out,
+               double scale, Tensor status) {
   CHECK_CUDA(q);
   CHECK_DT(q, torch::kBFloat16);
   CHECK_DT(k_cache, torch::kBFloat16);
@@ -124,6 +127,7 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_
   p.tile_row0 = tile_row0.data_ptr<int>();
   p.num_tiles = tile_seq.numel();
   p.tile_rows = static_cast<int>(tile_rows);
+  p.kv_splits = static_cast<int>(kv_splits);
   p.out = bfm(out);
   p.Hq = q.size(1);
   p.Hkv = k_cache.size(1);
@@ -791,6 +795,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine", &moe_combine);
   m.def("ep_exchange", &ep_exchange);
   m.def("set_pdl", [](bool on) { osb::pdl_enabled() = on; });
+  m.def("attention_set_trace", [](c10::optional<Tensor> buf) {
+    if (buf.has_value() && buf->defined()) {
+      CHECK_CUDA(*buf);
+      TORCH_CHECK(buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 1024,
+                  "trace buffer must be a contiguous int64 tensor of at least 1024 values");
+      osb::attention_trace_buffer() = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    } else {
+      osb::attention_trace_buffer() = nullptr;
+    }
+  });
   m.def("gemm_set_trace", [](c10::optional<Tensor> buf) {
     if (buf.has_value() && buf->defined()) {
       CHECK_CUDA(*buf);

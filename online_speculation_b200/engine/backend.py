@@ -167,14 +167,16 @@ class _DecodeGraph:
         self.it_host = torch.ones(B, dtype=torch.float32).pin_memory()
         self.inv_temp = torch.ones(B, dtype=torch.float32, device=dev)
         G = r.q_slots // r.kv_slots
-        tiles = -(-G // 16)
+        tr = K.attention_tile_rows(G, B * r.kv_slots, self.mp * K.PAGE_SIZE)
+        tiles = -(-G // tr)
         q_start = torch.arange(B, dtype=torch.int32, device=dev)
         q_len = torch.ones(B, dtype=torch.int32, device=dev)
         mode = torch.zeros(B, dtype=torch.int32, device=dev)
         tile_seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles)
-        tile_row = (torch.arange(tiles, dtype=torch.int32, device=dev) * 16).repeat(B)
-        self.plans = [K.AttentionPlan(self.table, q_start, q_len, self.kv[s], mode, tile_seq, tile_row, 16, {})
-                      for s in range(S)]
+        tile_row = (torch.arange(tiles, dtype=torch.int32, device=dev) * tr).repeat(B)
+        splits = K.attention_kv_splits(B * tiles * r.kv_slots, self.mp * K.PAGE_SIZE) if tr == K.TC_TILE_ROWS else 1
+        self.plans = [K.AttentionPlan(self.table, q_start, q_len, self.kv[s], mode, tile_seq, tile_row, tr, {},
+                                      splits) for s in range(S)]
         self.logq = torch.zeros(S, B, dtype=torch.float32, device=dev)
         self.logp = torch.zeros(S, B, dtype=torch.float32, device=dev)
         self.result = torch.zeros(S, B, 3, dtype=torch.float32, device=dev)
@@ -331,7 +333,7 @@ class EngineBackend:
             table = torch.zeros(len(grp), self.max_pages, dtype=torch.int32)
             self.cache.fill_table(seqs, table)
             meta = build_meta(r.device, table, ids, pos, slots, qlens, kvlens, [0] * len(grp), G,
-                              tile_rows=64 if max(qlens) * G > 64 else None)
+                              kv_heads=r.kv_slots)
             r.forward(meta, compute_logits=False)
             self.stats["prefill_tokens"] += len(ids)
 
@@ -545,8 +547,7 @@ class EngineBackend:
             lo = max(first_row, pos0)
             rows = list(range(lo - pos0, n))
             meta = build_meta(r.device, table, list(full[pos0:pos0 + n]), list(range(pos0, pos0 + n)), slots, [n],
-                              [pos0 + n], [0], G, logit_rows=rows if rows else None,
-                              tile_rows=64 if n * G > 64 else None)
+                              [pos0 + n], [0], G, logit_rows=rows if rows else None, kv_heads=r.kv_slots)
             if rows and logits_out is not None:
                 logits_out.append(r.forward(meta).float().cpu())
             elif rows:

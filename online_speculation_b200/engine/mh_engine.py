@@ -115,13 +115,16 @@ class _RoundGraph:
         mk = lambda v: torch.full((B,), v, dtype=torch.int32, device=dev)
         starts = torch.arange(0, B * Kb, Kb, dtype=torch.int32, device=dev)
         G = engine.runner.q_slots // engine.runner.kv_slots
-        tr = 16 if Kb * G <= 16 else 32     # one tile holds all query rows of a block when they fit
+        # the graph is captured once, so kernel and key split are chosen for the longest sequence
+        ctas = B * engine.runner.kv_slots
+        tr = K.attention_tile_rows(Kb * G, ctas, mp * K.PAGE_SIZE)
         tiles_per = -(-(Kb * G) // tr)
         tile_seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles_per)
         tile_row0 = (torch.arange(tiles_per, dtype=torch.int32, device=dev) * tr).repeat(B)
         kv_len = self.views["kv_len"]
-        self.plan_draft = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(1), tile_seq, tile_row0, tr, {})
-        self.plan_verify = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(0), tile_seq, tile_row0, tr, {})
+        splits = K.attention_kv_splits(ctas * tiles_per, mp * K.PAGE_SIZE) if tr == K.TC_TILE_ROWS else 1
+        self.plan_draft = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(1), tile_seq, tile_row0, tr, {}, splits)
+        self.plan_verify = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(0), tile_seq, tile_row0, tr, {}, splits)
         self.ids_draft = torch.full((B, Kb), engine.head.mask_token_id, dtype=torch.int32, device=dev)
         self.ids_verify = torch.zeros(B, Kb, dtype=torch.int32, device=dev)
         rows = torch.arange(B * Kb, device=dev).view(B, Kb)[:, : Kb - 1].reshape(-1)
@@ -273,7 +276,7 @@ class MHEngine:
                 table = torch.zeros(len(group), self.max_pages, dtype=torch.int32)
                 self.cache.fill_table(seqs, table)
                 meta = build_meta(self.device, table, toks, pos, slots, [P - 1] * len(group), [P - 1] * len(group),
-                                  [0] * len(group), r.q_slots // r.kv_slots, tile_rows=64)
+                                  [0] * len(group), r.q_slots // r.kv_slots, kv_heads=r.kv_slots)
                 r.forward(meta, compute_logits=False)
             roots.update(zip(group, seqs))
         for c in chain_ids:

@@ -260,11 +260,11 @@ class ModelRunner:
 
 
 def build_meta(device, table: torch.Tensor, ids, positions, slots, q_lens, kv_lens, modes, group, logit_rows=None,
-               tile_rows=None) -> StepMeta:
+               tile_rows=None, kv_heads: int = 1) -> StepMeta:
     """Host-side helper: pack python lists into device metadata (eager paths and tests)."""
     def dev(v):
         return torch.as_tensor(v, dtype=torch.int32).to(device, non_blocking=True)
 
-    plan = K.plan_attention(table, q_lens, kv_lens, modes, group, device, tile_rows=tile_rows)
+    plan = K.plan_attention(table, q_lens, kv_lens, modes, group, device, tile_rows=tile_rows, kv_heads=kv_heads)
     rows = None if logit_rows is None else torch.as_tensor(logit_rows, dtype=torch.int64).to(device)
     return StepMeta(dev(ids), dev(positions), dev(slots), plan, rows)

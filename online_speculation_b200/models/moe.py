@@ -215,7 +215,7 @@ class MoEDiffusionModel:
             slots = (torch.arange(B, dtype=torch.int32)[:, None] * (pps * PAGE)
                      + torch.arange(L, dtype=torch.int32)[None]).reshape(-1)
             G = self.cfg.num_attention_heads // self.cfg.num_key_value_heads
-            plan = K.plan_attention(table, [L] * B, [L] * B, [1] * B, G, dev, tile_rows=64 if L * G > 64 else None)
+            plan = K.plan_attention(table, [L] * B, [L] * B, [1] * B, G, dev, kv_heads=self.cfg.num_key_value_heads)
             lay = (pos.to(dev), slots.to(dev), plan, B * pps)
             self._bufs[("layout", key)] = lay
         return lay

@@ -31,9 +31,14 @@ def linear(
     out_dtype: torch.dtype = torch.bfloat16,
     allow_split: bool = True,
     static_weights: bool = False,
+    split_mode: int = 0,
 ) -> torch.Tensor:
     """``x @ w.T (+ bias) (+ residual)``; with ``swiglu`` the weight rows are
     tiles of [64 gate | 64 up] rows and the result is ``silu(gate) * up``.
+
+    ``split_mode``: with fewer output tiles than SMs, K is split across a
+    thread-block cluster reduced through distributed shared memory (0) or across
+    CTAs reduced through the global fp32 workspace by the last arrival (1).
 
     ``residual`` may alias ``out`` (in-place residual-stream update).
     ``static_weights``: no kernel earlier in the stream writes ``w`` (inference
@@ -56,6 +61,7 @@ def linear(
             workspace.gemm_counters(x.device),
             workspace.status(x.device),
             static_weights,
+            split_mode,
         )
         return out
     out.copy_(linear_reference(x, w, bias=bias, residual=residual, swiglu=swiglu).to(out.dtype))
@@ -202,27 +208,66 @@ class AttentionPlan:
     tile_rows: int
     # host copies for the CPU oracle
     host: dict
+    kv_splits: int = 1
 
 
-def plan_attention(table, q_lens, kv_lens, modes, group, device, *, tile_rows=None):
+TC_TILE_ROWS = 128          # query rows per CTA of the tcgen05 attention kernel
+TC_CHUNK_KEYS = 64          # keys per pipeline chunk of that kernel
+SM_COUNT = 148
+
+
+def attention_kv_splits(tiles: int, max_kv: int, sms: int = SM_COUNT) -> int:
+    """Key splits per tile for the tcgen05 kernel: the (tile, kv head) CTAs of one launch
+    are few when sequences are few (e.g. a handful of decode rows per rank under tensor
+    parallelism), so long key ranges are cut into 2, 4 or 8 pieces whose partial softmax
+    states merge inside a thread-block cluster.  Every piece keeps at least two chunks."""
+    splits = 1
+    while splits < 8 and tiles * splits * 2 <= sms and max_kv >= 2 * splits * 2 * TC_CHUNK_KEYS:
+        splits *= 2
+    return splits
+
+
+def attention_tile_rows(rows_per_seq: int, ctas: int, max_kv: int, sms: int = SM_COUNT) -> int:
+    """Kernel choice by shape (measured on B200).  The tcgen05 kernel runs one softmax
+    thread per query row of a 128-row tile, so it wins wherever tiles are full or the
+    key range can be split over a cluster: prefill and diffusion (1.8-1.9x the mma.sync
+    kernel), and decode / verify with few (sequence, kv head) pairs (64 x 1024 keys on
+    one kv head: 17.8 vs 25.3 us; 8 x 4096: 27.5 vs 57.9 us).  Many short decode tiles
+    (64 sequences x 4 kv heads x 1024 keys, 28 rows each) still run faster on the
+    mma.sync kernel with TMA-fed key groups (35.8 vs 55 us), which streams four key
+    groups per tile and co-schedules two tiles per SM."""
+    if rows_per_seq >= 64 or attention_kv_splits(ctas, max_kv, sms) > 1:
+        return TC_TILE_ROWS
+    return 16 if rows_per_seq <= 16 else 32
+
+
+def plan_attention(table, q_lens, kv_lens, modes, group, device, *, tile_rows=None, kv_splits=None, kv_heads=1):
     """Build the tile list of one attention launch.
 
     ``table``: int32 [B, max_pages] page table; ``q_lens``/``kv_lens``/``modes``:
-    python lists; ``group``: query heads per kv head.
+    python lists; ``group``: query heads per kv head.  ``tile_rows`` None (default)
+    chooses by shape (:func:`attention_tile_rows`): 128 is the tcgen05 kernel (128-row
+    tiles, optional key splits over a cluster), 16 / 32 / 64 the mma.sync kernels.
+    ``kv_heads``: KV heads of the launch (the grid's second dimension), used only to
+    choose the key split.
     """
     q_start, acc = [], 0
     for n in q_lens:
         q_start.append(acc)
         acc += n
     if tile_rows is None:
-        most = max(n * group for n in q_lens)
-        tile_rows = 16 if most <= 16 else 32 if most <= 64 else 64
+        most = max(n * group for n in q_lens) if q_lens else 0
+        tile_rows = attention_tile_rows(most, len(q_lens) * max(1, kv_heads), max(kv_lens) if kv_lens else 0)
     tile_seq, tile_row0 = [], []
     for b, n in enumerate(q_lens):
         rows = n * group
         for r0 in range(0, rows, tile_rows):
             tile_seq.append(b)
             tile_row0.append(r0)
+    if tile_rows != TC_TILE_ROWS:
+        kv_splits = 1
+    elif kv_splits is None:
+        kv_splits = attention_kv_splits(len(tile_seq) * max(1, kv_heads), max(kv_lens) if kv_lens else 0)
 
     def dev(values):
         return torch.tensor(values, dtype=torch.int32).to(device, non_blocking=True)
@@ -230,7 +275,7 @@ def plan_attention(table, q_lens, kv_lens, modes, group, device, *, tile_rows=No
     host = {"q_start": q_start, "q_len": list(q_lens), "kv_len": list(kv_lens), "mode": list(modes),
             "table": table.cpu() if table.is_cuda else table}
     return AttentionPlan(table.to(device, non_blocking=True), dev(q_start), dev(list(q_lens)), dev(list(kv_lens)),
-                         dev(list(modes)), dev(tile_seq), dev(tile_row0), tile_rows, host)
+                         dev(list(modes)), dev(tile_seq), dev(tile_row0), tile_rows, host, kv_splits)
 
 
 def attention(q, k_cache, v_cache, plan: AttentionPlan, *, out=None, scale=None):
@@ -240,7 +285,7 @@ def attention(q, k_cache, v_cache, plan: AttentionPlan, *, out=None, scale=None)
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
         _ext.require().attention(q, k_cache, v_cache, plan.table, plan.q_start, plan.q_len, plan.kv_len, plan.mode,
-                                 plan.tile_seq, plan.tile_row0, plan.tile_rows, out, float(scale),
+                                 plan.tile_seq, plan.tile_row0, plan.tile_rows, plan.kv_splits, out, float(scale),
                                  workspace.status(q.device))
         return out
     out.copy_(attention_reference(q, k_cache, v_cache, plan.host, scale))

@@ -35,6 +35,26 @@ def _peaks() -> dict:
         return {}
 
 
+def _attention_timeline(t) -> list:
+    """Per traced CTA: ns from entry to set-up, and per chunk the producer issue, S issue,
+    P arrival at the MMA issuer, S seen and P written by the first softmax warp."""
+    rows = []
+    for c in range(t.shape[0]):
+        if int(t[c, 0]) == 0:
+            continue
+        t0 = int(t[c, 0])
+        rel = lambda v: None if int(v) == 0 else int(v) - t0
+        chunks = []
+        for j in range(24):
+            vals = [rel(t[c, base + j]) for base in (2, 26, 50, 74, 98)]
+            if all(v is None for v in vals):
+                break
+            chunks.append(dict(zip(("tma", "s_issue", "p_at_mma", "s_seen", "p_done"), vals)))
+        rows.append({"cta": c, "setup": rel(t[c, 1]), "softmax_done": rel(t[c, 122]), "exit": rel(t[c, 123]),
+                     "chunks": chunks})
+    return rows
+
+
 def _time(body, iters: int, warmup: int, graph: bool) -> float:
     for _ in range(warmup):
         body()
@@ -131,6 +151,12 @@ def main(argv=None) -> int:
     at.add_argument("--heads", type=int, default=28)
     at.add_argument("--kv-heads", type=int, default=4)
     at.add_argument("--qlen", type=int, default=1, help="query tokens per sequence (a causal block at the end)")
+    at.add_argument("--bidirectional", action="store_true", help="every query sees every key (diffusion / draft)")
+    at.add_argument("--tile-rows", type=int, default=None,
+                    help="16 / 32 / 64: the mma.sync kernels; default: the tcgen05 kernel (128-row tiles)")
+    at.add_argument("--kv-splits", type=int, default=None, help="tcgen05 kernel: key splits per tile (default: auto)")
+    at.add_argument("--trace", action="store_true",
+                    help="tcgen05 kernel: print the per-chunk timeline of the first CTAs (one extra launch)")
     sa = sub.add_parser("sample")
     sa.add_argument("rows", type=int)
     sa.add_argument("V", type=int)
@@ -210,16 +236,28 @@ def main(argv=None) -> int:
         kc = torch.randn(B * pps, hkv, 32, 128, device=dev).bfloat16()
         vc = torch.randn_like(kc)
         table = (torch.arange(B, dtype=torch.int32)[:, None] * pps + torch.arange(pps, dtype=torch.int32)[None])
-        plan = K.plan_attention(table, [a.qlen] * B, [ctx] * B, [0] * B, hq // hkv, dev)
+        plan = K.plan_attention(table, [a.qlen] * B, [ctx] * B, [int(a.bidirectional)] * B, hq // hkv, dev,
+                                tile_rows=a.tile_rows, kv_splits=a.kv_splits, kv_heads=hkv)
         q = torch.randn(B * a.qlen, hq, 128, device=dev).bfloat16()
         o = torch.empty_like(q)
 
         def body():
             K.attention(q, kc, vc, plan, out=o)
         us = _time(body, a.iters, a.warmup, graph)
+        if a.trace and plan.tile_rows == K.TC_TILE_ROWS:
+            buf = torch.zeros(1024, dtype=torch.int64, device=dev)
+            ext = K._ext.require()
+            ext.attention_set_trace(buf)
+            body()
+            torch.cuda.synchronize()
+            ext.attention_set_trace(None)
+            out["trace"] = _attention_timeline(buf.cpu().view(8, 128))
         bytes_ = 2 * B * ctx * hkv * 128 * 2
-        flops = 4 * B * a.qlen * hq * ctx * 128
-        out.update(B=B, ctx=ctx, qlen=a.qlen, us=us, gbs=bytes_ / us / 1e3, attn_tflops=flops / us / 1e6)
+        # causal blocks see on average about half of a prompt-sized query range
+        seen = ctx if a.bidirectional or a.qlen == 1 else ctx - (a.qlen - 1) / 2
+        flops = 4 * B * a.qlen * hq * seen * 128
+        out.update(B=B, ctx=ctx, qlen=a.qlen, tile_rows=plan.tile_rows, kv_splits=plan.kv_splits, us=us,
+                   gbs=bytes_ / us / 1e3, tflops=flops / us / 1e6)
     else:
         logits = torch.randn(a.rows, a.V, device=dev)
         it = torch.ones(a.rows, device=dev)

@@ -71,43 +71,20 @@ def test_gemm_repeated_split_counters_reset(cuda):
     assert int(workspace.gemm_counters(cuda).abs().sum()) == 0
 
 
-_WORKSPACE_SPLIT_CHECK = """
-import torch
-from online_speculation_b200.ops import kernels as ops, workspace
-dev = torch.device("cuda", 0)
-torch.manual_seed(3)
-for M, N, K, swiglu, residual in [(3584, 256, 3584, False, True), (1024, 40, 4096, False, False),
-                                  (640, 96, 2048, True, False)]:
-    w = (torch.randn(M, K, device=dev) * 0.05).bfloat16()
-    x = torch.randn(N, K, device=dev).bfloat16()
-    if swiglu:
-        out = ops.linear(x, w, swiglu=True)
-        wf = w.float().view(-1, 2, 64, K)
-        g, u = x.float() @ wf[:, 0].reshape(-1, K).t(), x.float() @ wf[:, 1].reshape(-1, K).t()
-        ref = torch.nn.functional.silu(g) * u
-    else:
-        r = torch.randn(N, M, device=dev).bfloat16() if residual else None
-        out = ops.linear(x, w, residual=r)
-        ref = ops.linear_reference(x, w, residual=r).float()
-    torch.cuda.synchronize()
-    workspace.check_status(dev)
-    err = float((out.float() - ref).norm() / ref.norm())
-    assert err < 1e-2, (M, N, K, err)
-assert int(workspace.gemm_counters(dev).abs().sum()) == 0
-print("ok")
-"""
-
-
-def test_gemm_workspace_split_mode(cuda):
+@pytest.mark.parametrize("M,N,K,swiglu,residual", [(3584, 256, 3584, False, True), (1024, 40, 4096, False, False),
+                                                (640, 96, 2048, True, False)])
+def test_gemm_workspace_split_mode(cuda, M, N, K, swiglu, residual):
     """Split-K through the global fp32 workspace (the last split to arrive reduces)."""
-    import os
-    import subprocess
-    import sys
-
-    env = dict(os.environ, OSB_GEMM_SPLIT_MODE="1")
-    r = subprocess.run([sys.executable, "-c", _WORKSPACE_SPLIT_CHECK], env=env, capture_output=True, text=True,
-                       timeout=300)
-    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+    torch.manual_seed(3)
+    w = (torch.randn(M, K, device=cuda) * 0.05).bfloat16()
+    x = torch.randn(N, K, device=cuda).bfloat16()
+    r = torch.randn(N, M, device=cuda).bfloat16() if residual else None
+    out = ops.linear(x, w, swiglu=swiglu, residual=r, split_mode=1)
+    ref = ops.linear_reference(x, w, swiglu=swiglu, residual=r)
+    torch.cuda.synchronize()
+    workspace.check_status(cuda)
+    assert _rel(out, ref) < 1e-2, (M, N, K)
+    assert int(workspace.gemm_counters(cuda).abs().sum()) == 0
 
 
 def _paged_case(device, lengths, Hkv, pages_per_seq, seed=0):
@@ -120,32 +97,51 @@ def _paged_case(device, lengths, Hkv, pages_per_seq, seed=0):
     return perm, k, v
 
 
-@pytest.mark.parametrize(
-    "q_lens,kv_lens,modes,Hq,Hkv",
-    [
-        ([1, 1, 1], [1, 33, 700], [0, 0, 0], 28, 4),       # decode
-        ([4, 4], [130, 4], [0, 0], 28, 4),                 # verify block
-        ([4, 4], [517, 9], [1, 1], 28, 4),                 # bidirectional draft block
-        ([300, 64], [300, 64], [0, 1], 12, 2),             # prefill + diffusion
-        ([1, 5], [1000, 999], [0, 1], 4, 1),               # TP-sharded heads
-        ([512], [512], [0], 28, 4),
-    ],
-)
-def test_attention_matches_fp32(cuda, q_lens, kv_lens, modes, Hq, Hkv):
+ATTENTION_CASES = [
+    ([1, 1, 1], [1, 33, 700], [0, 0, 0], 28, 4),       # decode
+    ([4, 4], [130, 4], [0, 0], 28, 4),                 # verify block
+    ([4, 4], [517, 9], [1, 1], 28, 4),                 # bidirectional draft block
+    ([300, 64], [300, 64], [0, 1], 12, 2),             # prefill + diffusion
+    ([1, 5], [1000, 999], [0, 1], 4, 1),               # TP-sharded heads
+    ([512], [512], [0], 28, 4),                        # causal prefill over 28 row tiles of 128
+    ([37, 4], [1061, 70], [0, 0], 16, 2),              # prompt chunk after history; ragged last chunk
+]
+
+# (tile_rows, kv_splits): None = the tcgen05 kernel (128-row tiles, key ranges merged in a
+# cluster of kv_splits CTAs); 16 / 32 / 64 = the mma.sync kernels kept for comparison
+ATTENTION_KERNELS = [(None, 1), (None, 2), (None, 4), (None, 8), (16, 1), (32, 1), (64, 1)]
+
+
+@pytest.mark.parametrize("q_lens,kv_lens,modes,Hq,Hkv", ATTENTION_CASES)
+@pytest.mark.parametrize("tile_rows,kv_splits", ATTENTION_KERNELS)
+def test_attention_matches_fp32(cuda, q_lens, kv_lens, modes, Hq, Hkv, tile_rows, kv_splits):
     pps = max((kv + 31) // 32 for kv in kv_lens)
     table, kc, vc = _paged_case(cuda, kv_lens, Hkv, pps)
     T = sum(q_lens)
     q = torch.randn(T, Hq, 128, device=cuda).bfloat16()
-    for tile_rows in (16, 32, 64):
-        plan = ops.plan_attention(table, q_lens, kv_lens, modes, Hq // Hkv, cuda, tile_rows=tile_rows)
-        out = ops.attention(q, kc, vc, plan)
-        ref = ops.attention_reference(q.cpu(), kc.cpu(), vc.cpu(), plan.host, 128 ** -0.5)
-        torch.cuda.synchronize()
-        assert _rel(out.cpu(), ref) < 2e-2, tile_rows
+    plan = ops.plan_attention(table, q_lens, kv_lens, modes, Hq // Hkv, cuda, tile_rows=tile_rows,
+                              kv_splits=kv_splits)
+    out = torch.full_like(q, float("nan"))
+    ops.attention(q, kc, vc, plan, out=out)
+    ref = ops.attention_reference(q.cpu(), kc.cpu(), vc.cpu(), plan.host, 128 ** -0.5)
+    torch.cuda.synchronize()
+    workspace.check_status(cuda)
+    assert torch.isfinite(out).all()
+    assert _rel(out.cpu(), ref) < 2e-2, (tile_rows, kv_splits)
 
 
-@pytest.mark.parametrize("tile_rows", [16, 32])
-def test_attention_ignores_non_finite_rows_past_the_end(cuda, tile_rows):
+def test_attention_default_plan_choice(cuda):
+    table, kc, vc = _paged_case(cuda, [1024] * 2, 1, 32)
+    plan = ops.plan_attention(table, [4, 4], [1024, 1024], [0, 0], 7, cuda, kv_heads=1)
+    assert plan.tile_rows == 128 and plan.kv_splits == 8     # 2 tiles x 1 head: long key ranges are split
+    plan = ops.plan_attention(table, [4] * 2, [1024] * 2, [0] * 2, 7, cuda, kv_heads=148)
+    assert plan.tile_rows == 32 and plan.kv_splits == 1      # many short tiles: mma.sync key groups
+    plan = ops.plan_attention(table, [300, 64], [300, 64], [0, 1], 6, cuda, kv_heads=2)
+    assert plan.tile_rows == 128                             # prefill / diffusion: full tiles
+
+
+@pytest.mark.parametrize("tile_rows,kv_splits", [(None, 1), (None, 4), (16, 1), (32, 1)])
+def test_attention_ignores_non_finite_rows_past_the_end(cuda, tile_rows, kv_splits):
     # cache rows past a sequence's end may hold anything (recycled or never-written pages)
     kv_lens = [37, 70, 5]
     table, kc, vc = _paged_case(cuda, kv_lens, 4, 3, seed=3)
@@ -156,7 +152,7 @@ def test_attention_ignores_non_finite_rows_past_the_end(cuda, tile_rows):
             vc[page, :, key % 32] = float("inf")
     q_lens = [4, 4, 1]
     q = torch.randn(sum(q_lens), 28, 128, device=cuda).bfloat16()
-    plan = ops.plan_attention(table, q_lens, kv_lens, [0, 1, 0], 7, cuda, tile_rows=tile_rows)
+    plan = ops.plan_attention(table, q_lens, kv_lens, [0, 1, 0], 7, cuda, tile_rows=tile_rows, kv_splits=kv_splits)
     out = ops.attention(q, kc, vc, plan)
     ref = ops.attention_reference(q.cpu(), torch.nan_to_num(kc.cpu()), torch.nan_to_num(vc.cpu()), plan.host,
                                   128 ** -0.5)

@@ -62,11 +62,11 @@ def main():
         slots = cache.append(s, 60)
         cache.fill_table([s], table)
         out = r.forward(build_meta(dev, table, seq[:60].tolist(), list(range(60)), slots, [60], [60], [0], G))
-        assert rel(out.cpu(), ref[:60]) < 3e-2, ("prefill", fused, push, algorithm, rel(out.cpu(), ref[:60]))
+        assert rel(out.cpu(), ref[:60]) < 5e-2, ("prefill", fused, push, algorithm, rel(out.cpu(), ref[:60]))
         slots = cache.append(s, 4)
         cache.fill_table([s], table)
         out = r.forward(build_meta(dev, table, seq[60:64].tolist(), list(range(60, 64)), slots, [4], [64], [0], G))
-        assert rel(out.cpu(), ref[60:64]) < 3e-2, ("verify", fused, push, algorithm)
+        assert rel(out.cpu(), ref[60:64]) < 5e-2, ("verify", fused, push, algorithm)
         torch.cuda.synchronize()
         workspace.check_status(dev)
     # vocabulary-parallel samplers draw exactly what the unsharded kernels draw on full rows
