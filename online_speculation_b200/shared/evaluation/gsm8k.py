@@ -1,10 +1,12 @@
-"""GSM8K splits pinned by SHA-256, the shared prompt suffix, preregistered subsets and accuracy.
+"""GSM8K: pinned split files, the shared prompt suffix, preregistered subsets, accuracy.
 
-The split URLs, digests, row counts and prompt suffix are the public GSM8K
-files and the reference's prompt text (src/inference_scaling/shared/evaluation/gsm8k.py:45-141):
-they identify the data, so they are kept exactly.  A local file is accepted
-only if its digest matches; downloading is attempted only when the file is
-missing and a network is available.
+Each split is identified by its public URL, SHA-256 digest and row count, and the
+prompt suffix is the reference's text (src/inference_scaling/shared/evaluation/gsm8k.py):
+these are data identities, so they are kept byte for byte, and so is the subset
+draw (``random.Random(seed).sample`` over row indices, returned in dataset order),
+which makes a preregistered subset name the same questions as in the reference's
+reports.  A local file is used only if its digest matches; a download is attempted
+only when no matching file exists.
 """
 
 from __future__ import annotations
@@ -20,15 +22,24 @@ from typing import Iterable, Literal, Sequence
 
 from .numeric import extract_numeric_answer
 
-_BASE = "https://raw.githubusercontent.com/openai/grade-school-math/master/grade_school_math/data/"
-GSM8K_TRAIN_URL = _BASE + "train.jsonl"
+GSM8K_TRAIN_URL = "https://raw.githubusercontent.com/openai/grade-school-math/master/grade_school_math/data/train.jsonl"
 GSM8K_TRAIN_SHA256 = "17f347dc51477c50d4efb83959dbb7c56297aba886e5544ee2aaed3024813465"
-GSM8K_TEST_URL = _BASE + "test.jsonl"
+GSM8K_TEST_URL = "https://raw.githubusercontent.com/openai/grade-school-math/master/grade_school_math/data/test.jsonl"
 GSM8K_TEST_SHA256 = "3730d312f6e3440559ace48831e51066acaca737f6eabec99bccb9e4b3c39d14"
 GSM8K_PROMPT_SUFFIX = ("\n\nSolve the problem step by step. End your response with exactly "
                        "`#### <number>`, where <number> is the final numeric answer.")
 GSM8KSplit = Literal["train", "test"]
-_SPLITS = {"train": (GSM8K_TRAIN_URL, GSM8K_TRAIN_SHA256, 7473), "test": (GSM8K_TEST_URL, GSM8K_TEST_SHA256, 1319)}
+
+
+@dataclass(frozen=True)
+class _SplitFile:
+    url: str
+    sha256: str
+    rows: int
+
+
+_SPLITS = {"train": _SplitFile(GSM8K_TRAIN_URL, GSM8K_TRAIN_SHA256, 7473),
+           "test": _SplitFile(GSM8K_TEST_URL, GSM8K_TEST_SHA256, 1319)}
 
 
 @dataclass(frozen=True, slots=True)
@@ -39,68 +50,76 @@ class GSM8KProblem:
     gold_answer: Fraction
 
 
-def _digest(path: Path) -> str:
-    h = hashlib.sha256()
-    with path.open("rb") as f:
-        while chunk := f.read(1 << 20):
-            h.update(chunk)
-    return h.hexdigest()
+def _sha256_of(path: Path) -> str:
+    digest = hashlib.sha256()
+    with path.open("rb") as handle:
+        for block in iter(lambda: handle.read(1 << 20), b""):
+            digest.update(block)
+    return digest.hexdigest()
 
 
 def download_gsm8k(path: str | Path, *, split: GSM8KSplit = "test") -> Path:
-    url, sha, _ = _SPLITS[split]
-    dst = Path(path)
-    if dst.is_file() and _digest(dst) == sha:
-        return dst
-    dst.parent.mkdir(parents=True, exist_ok=True)
-    tmp = dst.with_suffix(dst.suffix + ".download")
+    spec = _SPLITS[split]
+    target = Path(path)
+    if target.is_file() and _sha256_of(target) == spec.sha256:
+        return target
+    target.parent.mkdir(parents=True, exist_ok=True)
+    partial = target.parent / (target.name + ".partial")
     try:
-        urllib.request.urlretrieve(url, tmp)
-        got = _digest(tmp)
-        if got != sha:
-            raise ValueError(f"GSM8K {split} checksum mismatch: expected {sha}, downloaded {got}")
-        tmp.replace(dst)
+        with urllib.request.urlopen(spec.url) as response, partial.open("wb") as out:
+            for block in iter(lambda: response.read(1 << 20), b""):
+                out.write(block)
+        got = _sha256_of(partial)
+        if got != spec.sha256:
+            raise ValueError(f"GSM8K {split}: downloaded digest {got} is not the pinned {spec.sha256}")
+        partial.replace(target)
     finally:
-        tmp.unlink(missing_ok=True)
-    return dst
+        partial.unlink(missing_ok=True)
+    return target
+
+
+def _rows(path: Path) -> Iterable[tuple[int, dict]]:
+    with path.open("r", encoding="utf-8") as handle:
+        for i, line in enumerate(handle):
+            yield i, json.loads(line)
 
 
 def load_gsm8k(path: str | Path, *, split: GSM8KSplit = "test", download: bool = True) -> tuple[GSM8KProblem, ...]:
-    _, sha, rows = _SPLITS[split]
-    src = download_gsm8k(path, split=split) if download else Path(path)
-    if _digest(src) != sha:
-        raise ValueError(f"{src} is not the pinned official GSM8K {split} file")
-    out = []
-    with src.open("r", encoding="utf-8") as f:
-        for i, line in enumerate(f):
-            item = json.loads(line)
-            ans = extract_numeric_answer(str(item["answer"]))
-            if ans is None:
-                raise ValueError(f"could not parse GSM8K gold answer at row {i}")
-            out.append(GSM8KProblem(i, str(item["question"]), str(item["answer"]), ans))
-    if len(out) != rows:
-        raise ValueError(f"expected {rows:,} GSM8K {split} rows, found {len(out):,}")
-    return tuple(out)
+    spec = _SPLITS[split]
+    source = download_gsm8k(path, split=split) if download else Path(path)
+    if _sha256_of(source) != spec.sha256:
+        raise ValueError(f"{source} does not match the pinned GSM8K {split} digest")
+    problems = []
+    for i, row in _rows(source):
+        gold = extract_numeric_answer(str(row["answer"]))
+        if gold is None:
+            raise ValueError(f"GSM8K {split} row {i}: no numeric gold answer")
+        problems.append(GSM8KProblem(i, str(row["question"]), str(row["answer"]), gold))
+    if len(problems) != spec.rows:
+        raise ValueError(f"GSM8K {split} has {spec.rows} rows; {source} holds {len(problems)}")
+    return tuple(problems)
 
 
 def gsm8k_prompt(question: str) -> str:
-    return question + GSM8K_PROMPT_SUFFIX
+    return f"{question}{GSM8K_PROMPT_SUFFIX}"
 
 
 def select_problems(problems: Sequence[GSM8KProblem], count: int | None, *, seed: int) -> tuple[GSM8KProblem, ...]:
-    """A preregistered random subset in dataset order (drawn before any inference)."""
-    if count is None or count == len(problems):
+    """Preregistered subset of ``count`` problems (chosen before any inference), in dataset order."""
+    n = len(problems)
+    if count is None or count == n:
         return tuple(problems)
-    if not 0 < count <= len(problems):
-        raise ValueError(f"count must lie in [1, {len(problems)}]")
-    return tuple(problems[i] for i in sorted(random.Random(seed).sample(range(len(problems)), count)))
+    if not 1 <= count <= n:
+        raise ValueError(f"a subset of {count} problems is not possible from {n}")
+    picked = random.Random(seed).sample(range(n), count)
+    return tuple(problems[i] for i in sorted(picked))
 
 
 def accuracy(correct: Iterable[bool]) -> float:
-    vals = [bool(v) for v in correct]
-    if not vals:
-        raise ValueError("accuracy requires at least one result")
-    return sum(vals) / len(vals)
+    flags = [bool(c) for c in correct]
+    if not flags:
+        raise ValueError("accuracy of an empty result set is undefined")
+    return sum(flags) / len(flags)
 
 
 __all__ = ["GSM8KProblem", "GSM8K_PROMPT_SUFFIX", "GSM8K_TEST_SHA256", "GSM8K_TEST_URL", "GSM8K_TRAIN_SHA256",

@@ -1,14 +1,17 @@
-"""JSON / XML thinking and answer fields aligned to the original generated tokens.
+"""Thinking / answer fields of JSON or XML completions, aligned to the generated tokens.
 
-A structured completion (one JSON object, or XML, optionally inside a
-```json / ```xml fence) carries its reasoning in a field (``thinking`` /
-``reasoning`` / ``analysis`` / ``think`` unless a path is given) and optionally
-its answer (``answer`` / ``content`` / ``final``).  Character spans of those
-fields are mapped back to token boundaries of the original completion by
-comparing decoded prefixes (never by re-tokenising); a span that does not fall
-on token boundaries is reported as unaligned and the whole completion is used.
+A structured completion is one JSON object or an XML document (optionally inside a
+```json / ```xml fence).  Its reasoning lives in a field named ``thinking``,
+``reasoning``, ``analysis`` or ``think`` (or at an explicit path) and its answer,
+optionally, in ``answer`` / ``content`` / ``final``.  The character span of each
+field is located in the decoded text and then mapped to token boundaries of the
+original completion by comparing decoded prefixes (never by re-tokenising); a span
+inside a token is reported as unaligned and the whole completion is used instead.
 
-Reference behaviour: src/inference_scaling/shared/structured_output.py:166-289.
+JSON is read by a small iterative lexer that records the span of every value while
+tracking the key path; XML spans come from expat's byte offsets.  Status strings and
+``describe()`` keys follow src/inference_scaling/shared/structured_output.py, which
+the experiment reports read.
 """
 
 from __future__ import annotations
@@ -23,145 +26,231 @@ from xml.parsers import expat
 from .output import OutputSegments, ThinkingParser, full_sequence_segments
 from .types import TokenSequence
 
-Span = tuple[Any, int, int]       # (value, start char, end char)
-_REPEATED = object()
-_WS = " \r\n\t"
+Span = tuple[Any, int, int]       # (value, first char, end char)
+_AMBIGUOUS = object()
+_MAX_DEPTH = 64
+_THINKING_NAMES = ("thinking", "reasoning", "analysis", "think")
+_CONTENT_NAMES = ("answer", "content", "final")
+
+_JSON_TOKEN = re.compile(r"""
+    (?P<ws>[ \t\r\n]+)
+  | (?P<string>"(?:[^"\\\x00-\x1f]|\\(?:["\\/bfnrt]|u[0-9a-fA-F]{4}))*")
+  | (?P<number>-?(?:0|[1-9]\d*)(?:\.\d+)?(?:[eE][-+]?\d+)?)
+  | (?P<literal>true|false|null)
+  | (?P<punct>[{}\[\]:,])
+""", re.VERBOSE)
+
+
+def _json_tokens(text: str):
+    pos = 0
+    while pos < len(text):
+        m = _JSON_TOKEN.match(text, pos)
+        if m is None:
+            raise ValueError(f"unexpected character {text[pos]!r} in JSON at {pos}")
+        pos = m.end()
+        if m.lastgroup != "ws":
+            yield m.lastgroup, m.group(), m.start(), m.end()
+
+
+class _Frame:
+    __slots__ = ("kind", "value", "start", "path", "key", "expect")
+
+    def __init__(self, kind, start, path):
+        self.kind = kind            # "object" or "array"
+        self.value = {} if kind == "object" else []
+        self.start = start
+        self.path = path
+        self.key = None
+        self.expect = "key_or_end" if kind == "object" else "value_or_end"
 
 
 def json_fields(text: str) -> dict[tuple[str, ...], Span]:
-    """Every value of a single JSON object with its character span (strings: inside the quotes)."""
+    """Every value of a single JSON object keyed by its key path, with its span
+    (string values: the characters between the quotes).  Arrays are leaves."""
+    spans: dict[tuple[str, ...], Span] = {}
+    stack: list[_Frame] = []
+    top: list = []
 
-    def no_constants(v):
-        raise ValueError(f"invalid JSON constant: {v}")
+    def place(value, path, start, end):
+        # values inside arrays are part of the array's value, not addressable fields
+        if not any(f.kind == "array" for f in stack):
+            spans[path] = (value, start, end)
+        if not stack:
+            top.append(value)
+            return
+        frame = stack[-1]
+        if frame.kind == "object":
+            frame.value[frame.key] = value
+        else:
+            frame.value.append(value)
+        frame.expect = "comma_or_end"
 
-    dec = json.JSONDecoder(parse_constant=no_constants)
-    out: dict[tuple[str, ...], Span] = {}
+    def child_path():
+        frame = stack[-1] if stack else None
+        if frame is None:
+            return ()
+        return frame.path + ((frame.key,) if frame.kind == "object" else ())
 
-    def skip(i):
-        while i < len(text) and text[i] in _WS:
-            i += 1
-        return i
+    for kind, raw, start, end in _json_tokens(text):
+        frame = stack[-1] if stack else None
+        if top:
+            raise ValueError("text continues after the JSON object")
+        if frame is not None and frame.expect in ("key_or_end", "key"):
+            if kind == "punct" and raw == "}" and frame.expect == "key_or_end":
+                pass
+            elif kind == "string":
+                key = json.loads(raw)
+                if key in frame.value:
+                    raise ValueError(f"repeated JSON key {key!r}")
+                frame.key = key
+                frame.expect = "colon"
+                continue
+            else:
+                raise ValueError("a JSON object key has to be a string")
+        if frame is not None and frame.expect == "colon":
+            if raw != ":":
+                raise ValueError("missing ':' after a JSON key")
+            frame.expect = "value"
+            continue
+        if frame is not None and frame.expect == "comma_or_end":
+            if raw == ",":
+                frame.expect = "key" if frame.kind == "object" else "value"
+                continue
+            if raw not in "}]":
+                raise ValueError("missing ',' between JSON members")
+        if kind == "punct" and raw in "}]":
+            if frame is None or (raw == "}") != (frame.kind == "object") or frame.expect in ("key", "value"):
+                raise ValueError(f"unbalanced {raw!r} in JSON")
+            stack.pop()
+            place(frame.value, frame.path, frame.start, end)
+            continue
+        if kind == "punct" and raw in "{[":
+            if len(stack) >= _MAX_DEPTH:
+                raise ValueError(f"JSON nested deeper than {_MAX_DEPTH} levels")
+            stack.append(_Frame("object" if raw == "{" else "array", start, child_path()))
+            continue
+        if kind == "punct":
+            raise ValueError(f"unexpected {raw!r} in JSON")
+        path = child_path()
+        if kind == "string":
+            place(json.loads(raw), path, start + 1, end - 1)
+        elif kind == "number":
+            place(json.loads(raw), path, start, end)
+        else:
+            place({"true": True, "false": False, "null": None}[raw], path, start, end)
+    if stack or not top or not isinstance(top[0], dict):
+        raise ValueError("the output is not exactly one complete JSON object")
+    return spans
 
-    def value(i, path):
-        if len(path) > 64:
-            raise ValueError("JSON nesting exceeds 64 levels")
-        s = skip(i)
-        if s >= len(text):
-            raise ValueError("incomplete JSON value")
-        if text[s] == "{":
-            obj: dict[str, Any] = {}
-            i = skip(s + 1)
-            if i < len(text) and text[i] == "}":
-                out[path] = (obj, s, i + 1)
-                return obj, i + 1
-            while True:
-                key, e = dec.raw_decode(text, i)
-                if not isinstance(key, str) or key in obj:
-                    raise ValueError("JSON keys must be distinct strings")
-                i = skip(e)
-                if i >= len(text) or text[i] != ":":
-                    raise ValueError("missing JSON colon")
-                obj[key], i = value(i + 1, path + (key,))
-                i = skip(i)
-                if i < len(text) and text[i] == "}":
-                    i += 1
-                    break
-                if i >= len(text) or text[i] != ",":
-                    raise ValueError("missing JSON object delimiter")
-                i = skip(i + 1)
-            out[path] = (obj, s, i)
-            return obj, i
-        v, e = dec.raw_decode(text, s)
-        out[path] = (v, s + 1, e - 1) if isinstance(v, str) else (v, s, e)
-        return v, e
 
-    top, end = value(0, ())
-    if not isinstance(top, dict) or skip(end) != len(text):
-        raise ValueError("output must contain exactly one JSON object")
-    return out
+class _XmlSpans:
+    """Collects the text content and character span of every element path (expat)."""
+
+    def __init__(self, raw: bytes):
+        self.raw = raw
+        self.parser = expat.ParserCreate()
+        self.open: list[tuple[str, int, list[str]]] = []      # (name, content start byte, text pieces)
+        self.spans: dict[tuple[str, ...], Span] = {}
+        p = self.parser
+        p.StartElementHandler = self._start
+        p.EndElementHandler = self._end
+        p.CharacterDataHandler = self._text
+        p.StartDoctypeDeclHandler = self._refuse
+        p.ExternalEntityRefHandler = self._refuse
+
+    def _refuse(self, *_):
+        raise ValueError("document types and external entities are not accepted")
+
+    def _tag_end(self, at: int) -> int:
+        """Byte just after the '>' closing the start tag at ``at`` (quoted '>' skipped)."""
+        quote = None
+        for i in range(at, len(self.raw)):
+            c = self.raw[i]
+            if quote is not None:
+                quote = None if c == quote else quote
+            elif c in b"\"'":
+                quote = c
+            elif c == ord(">"):
+                return i + 1
+        return len(self.raw)
+
+    def _start(self, name, _attributes):
+        if len(self.open) >= _MAX_DEPTH:
+            raise ValueError(f"XML nested deeper than {_MAX_DEPTH} levels")
+        self.open.append((name, self._tag_end(self.parser.CurrentByteIndex), []))
+
+    def _text(self, data):
+        for _, _, pieces in self.open:
+            pieces.append(data)
+
+    def _chars(self, nbytes: int) -> int:
+        return len(self.raw[:nbytes].decode("utf-8"))
+
+    def _end(self, _name):
+        path = tuple(name for name, _, _ in self.open)
+        _, begin, pieces = self.open.pop()
+        stop = max(begin, self.parser.CurrentByteIndex)
+        value = _AMBIGUOUS if path in self.spans else "".join(pieces)
+        self.spans[path] = (value, self._chars(begin), self._chars(stop))
+
+    def parse(self) -> dict[tuple[str, ...], Span]:
+        self.parser.Parse(self.raw, True)
+        return self.spans
 
 
 def xml_fields(text: str, *, _fragment: bool = False) -> dict[tuple[str, ...], Span]:
-    """Text content of every XML element with its character span; repeated paths are marked ambiguous."""
-    raw = text.encode("utf-8")
-    p = expat.ParserCreate()
-    stack: list[list] = []                   # [name, content start byte, pieces]
-    out: dict[tuple[str, ...], Span] = {}
-
-    def chars(nbytes: int) -> int:
-        return len(raw[:nbytes].decode("utf-8"))
-
-    def on_start(name, _attrs):
-        if len(stack) >= 64:
-            raise ValueError("XML nesting exceeds 64 levels")
-        i, quote = p.CurrentByteIndex, None
-        while i < len(raw):                  # end of the opening tag (skipping quoted attribute values)
-            c = raw[i]
-            if quote is not None:
-                if c == quote:
-                    quote = None
-            elif c in (34, 39):
-                quote = c
-            elif c == 62:
-                break
-            i += 1
-        stack.append([name, i + 1, []])
-
-    def on_data(d):
-        for entry in stack:
-            entry[2].append(d)
-
-    def on_end(_name):
-        path = tuple(e[0] for e in stack)
-        _, begin, pieces = stack.pop()
-        stop = max(begin, p.CurrentByteIndex)
-        out[path] = (_REPEATED if path in out else "".join(pieces), chars(begin), chars(stop))
-
-    def refuse(*_):
-        raise ValueError("XML document types and external entities are unsupported")
-
-    p.StartElementHandler, p.EndElementHandler, p.CharacterDataHandler = on_start, on_end, on_data
-    p.StartDoctypeDeclHandler = p.ExternalEntityRefHandler = refuse
+    """Text content of every XML element by path, with its span; repeated paths are ambiguous."""
     try:
-        p.Parse(raw, True)
-    except expat.ExpatError as err:
-        if not _fragment and err.code == expat.errors.codes[expat.errors.XML_ERROR_JUNK_AFTER_DOC_ELEMENT]:
-            wrap = "<_output_fragment>"
-            inner = xml_fields(wrap + text + "</_output_fragment>", _fragment=True)
-            return {k[1:]: (v, a - len(wrap), b - len(wrap)) for k, (v, a, b) in inner.items() if len(k) > 1}
-        raise
-    return out
+        return _XmlSpans(text.encode("utf-8")).parse()
+    except expat.ExpatError as error:
+        junk = expat.errors.codes[expat.errors.XML_ERROR_JUNK_AFTER_DOC_ELEMENT]
+        if _fragment or error.code != junk:
+            raise
+    # several top-level elements: parse them under a synthetic root and shift the spans back
+    root = "<_output_fragment>"
+    inner = xml_fields(root + text + "</_output_fragment>", _fragment=True)
+    return {path[1:]: (value, a - len(root), b - len(root)) for path, (value, a, b) in inner.items() if len(path) > 1}
 
 
-def _pick(fields: Mapping[tuple[str, ...], Span], path, names, *, required: bool) -> Span | None:
-    hits = [v for k, v in fields.items() if k and (k == path if path is not None else k[-1] in names)]
+def _field(fields: Mapping[tuple[str, ...], Span], path, names, *, required: bool) -> Span | None:
+    if path is not None:
+        hits = [span for key, span in fields.items() if key == tuple(path)]
+    else:
+        hits = [span for key, span in fields.items() if key and key[-1] in names]
     if len(hits) > 1:
-        raise ValueError("ambiguous structured output fields; specify a path")
-    if hits and hits[0][0] is _REPEATED:
-        raise ValueError("ambiguous repeated structured output field")
-    if not hits and required:
-        raise ValueError("missing thinking field")
+        raise ValueError("several fields match; give an explicit path")
+    if hits and hits[0][0] is _AMBIGUOUS:
+        raise ValueError("the field is repeated")
+    if required and not hits:
+        raise ValueError("no thinking field")
     return hits[0] if hits else None
 
 
 def token_boundary(tokens: TokenSequence, text: str, pos: int, decode: Callable[[TokenSequence], str]) -> int | None:
-    """Index k with decode(tokens[:k]) == text[:pos], or None when pos falls inside a token."""
-    want = text[:pos]
+    """Token count k with decode(tokens[:k]) == text[:pos], or None if pos is inside a token."""
+    target = text[:pos]
+    cache: dict[int, str] = {}
+
+    def prefix(k: int) -> str:
+        if k not in cache:
+            cache[k] = decode(tokens[:k])
+        return cache[k]
+
     lo, hi = 0, len(tokens)
-    while lo <= hi:
+    while lo <= hi:                         # prefix lengths grow with k: bisect on them
         mid = (lo + hi) // 2
-        pre = decode(tokens[:mid])
-        if pre == want:
+        got = prefix(mid)
+        if got == target:
             return mid
-        if len(pre) < pos:
-            lo = mid + 1
-        else:
-            hi = mid - 1
-    # byte-fallback tokens may decode to replacement characters mid-sequence: probe the neighbourhood
+        lo, hi = (mid + 1, hi) if len(got) < pos else (lo, mid - 1)
+    # byte-level tokens can decode to replacement characters part-way: look around the bisection point
     for k in range(max(0, hi - 8), min(len(tokens), lo + 8) + 1):
-        if decode(tokens[:k]) == want:
+        if prefix(k) == target:
             return k
     return None
+
+
+_FENCE = re.compile(r"(\s*```(?:json|xml)?[ \t]*\r?\n)(.*?)(\r?\n```\s*)", re.DOTALL)
 
 
 @dataclass(frozen=True, slots=True)
@@ -173,56 +262,57 @@ class StructuredThinkingParser:
 
     def __post_init__(self):
         if self.kind not in ("json", "xml"):
-            raise ValueError("structured output kind must be json or xml")
+            raise ValueError(f"structured kind {self.kind!r} is not json or xml")
+
+    def _spans(self, text: str) -> tuple[Span, Span | None]:
+        body, shift = text, 0
+        if text.lstrip().startswith("```"):
+            fenced = _FENCE.fullmatch(text)
+            if fenced is None:
+                raise ValueError("unterminated or malformed code fence")
+            body, shift = fenced.group(2), len(fenced.group(1))
+        found = json_fields(body) if self.kind == "json" else xml_fields(body)
+        fields = {k: (v, a + shift, b + shift) for k, (v, a, b) in found.items()}
+        thinking = _field(fields, self.thinking_path, _THINKING_NAMES, required=True)
+        content = _field(fields, self.content_path, _CONTENT_NAMES, required=self.content_path is not None)
+        for span in (thinking, content):
+            if span is not None and isinstance(span[0], str):
+                span[0].encode("utf-8")
+        return thinking, content
 
     def split(self, prompt, completion, *, eos_token_id=None) -> OutputSegments:
-        toks = tuple(completion)
-        ended = eos_token_id is not None and eos_token_id in toks
+        tokens = tuple(completion)
+        ended = eos_token_id is not None and eos_token_id in tokens
         if ended:
-            toks = toks[:toks.index(eos_token_id)]
-        text = self.decode(toks)
+            tokens = tokens[:tokens.index(eos_token_id)]
+        text = self.decode(tokens)
 
-        def fallback(reason):
+        def whole(reason: str) -> OutputSegments:
             return full_sequence_segments(completion, eos_token_id=eos_token_id, reason=reason)
 
         try:
-            body, off = text, 0
-            if text.lstrip().startswith("```"):
-                m = re.fullmatch(r"(\s*```(?:json|xml)?[ \t]*\r?\n)(.*?)(\r?\n```\s*)", text, re.DOTALL)
-                if m is None:
-                    raise ValueError("malformed structured output fence")
-                body, off = m.group(2), len(m.group(1))
-            raw = json_fields(body) if self.kind == "json" else xml_fields(body)
-            fields = {k: (v, a + off, b + off) for k, (v, a, b) in raw.items()}
-            think = _pick(fields, self.thinking_path, ("thinking", "reasoning", "analysis", "think"), required=True)
-            content = _pick(fields, self.content_path, ("answer", "content", "final"),
-                            required=self.content_path is not None)
-        except (ValueError, expat.ExpatError, RecursionError):
-            return fallback("malformed_" + self.kind)
-        if not isinstance(think[0], str):
-            return fallback("non_text_thinking_field")
-        try:
-            think[0].encode("utf-8")
-            if content is not None and isinstance(content[0], str):
-                content[0].encode("utf-8")
-        except UnicodeError:
-            return fallback("malformed_" + self.kind)
-        if not think[0].strip():
-            return fallback("empty")
-        s = token_boundary(toks, text, think[1], self.decode)
-        e = token_boundary(toks, text, think[2], self.decode)
-        if s is None or e is None or e <= s:
-            return fallback("unaligned_thinking_tokens")
-        c_toks: TokenSequence = ()
-        c_text = ""
+            thinking, content = self._spans(text)
+        except (ValueError, UnicodeError, expat.ExpatError, RecursionError):
+            return whole("malformed_" + self.kind)
+        if not isinstance(thinking[0], str):
+            return whole("non_text_thinking_field")
+        if not thinking[0].strip():
+            return whole("empty")
+        first = token_boundary(tokens, text, thinking[1], self.decode)
+        last = token_boundary(tokens, text, thinking[2], self.decode)
+        if first is None or last is None or last <= first:
+            return whole("unaligned_thinking_tokens")
+        content_tokens: TokenSequence = ()
+        content_text = ""
         if content is not None:
-            cs = token_boundary(toks, text, content[1], self.decode)
-            ce = token_boundary(toks, text, content[2], self.decode)
-            if cs is None or ce is None:
-                return fallback("unaligned_content_tokens")
-            c_toks = toks[cs:ce]
-            c_text = content[0] if isinstance(content[0], str) else json.dumps(content[0], ensure_ascii=False)
-        return OutputSegments(toks[s:e], c_toks, s, e, None, "complete", ended, self.kind, think[0], c_text)
+            c0 = token_boundary(tokens, text, content[1], self.decode)
+            c1 = token_boundary(tokens, text, content[2], self.decode)
+            if c0 is None or c1 is None:
+                return whole("unaligned_content_tokens")
+            content_tokens = tokens[c0:c1]
+            content_text = content[0] if isinstance(content[0], str) else json.dumps(content[0], ensure_ascii=False)
+        return OutputSegments(tokens[first:last], content_tokens, first, last, None, "complete", ended, self.kind,
+                              thinking[0], content_text)
 
     def describe(self) -> dict[str, object]:
         return {"kind": self.kind, "thinking_path": self.thinking_path, "content_path": self.content_path,
@@ -231,7 +321,7 @@ class StructuredThinkingParser:
 
 @dataclass(frozen=True, slots=True)
 class UnifiedOutputParser:
-    """Marker formats first; JSON / XML structured outputs when the decoded text looks structured."""
+    """Marker formats first; JSON / XML parsing when the decoded text looks structured."""
 
     markers: ThinkingParser
     decode: Callable[[TokenSequence], str] | None = None
@@ -254,27 +344,32 @@ class UnifiedOutputParser:
     def prompt_mode(self, prompt):
         return self.markers.prompt_mode(prompt)
 
+    def _structured_kind(self, text: str, marker_status: str) -> str | None:
+        if self.kind != "auto":
+            return self.kind
+        if text.startswith(("{", "```json")):
+            return "json"
+        if text.startswith("```xml"):
+            return "xml"
+        if text.startswith("<") and marker_status in ("leading_content", "absent", "unrecognized_format"):
+            return "xml"
+        return None
+
     def split(self, prompt, completion, *, eos_token_id=None) -> OutputSegments:
-        seg = self.markers.split(prompt, completion, eos_token_id=eos_token_id)
-        if seg.status == "disabled" or self.decode is None or self.kind == "tags":
-            return seg
-        toks = (completion[:completion.index(eos_token_id)]
-                if eos_token_id is not None and eos_token_id in completion else completion)
-        text = self.decode(toks).lstrip()
-        kind = self.kind
-        if kind == "auto":
-            if text.startswith(("{", "```json")):
-                kind = "json"
-            elif text.startswith("```xml") or (text.startswith("<") and seg.status in (
-                    "leading_content", "absent", "unrecognized_format")):
-                kind = "xml"
-            else:
-                return seg
+        by_markers = self.markers.split(prompt, completion, eos_token_id=eos_token_id)
+        if by_markers.status == "disabled" or self.decode is None or self.kind == "tags":
+            return by_markers
+        tokens = tuple(completion)
+        if eos_token_id is not None and eos_token_id in tokens:
+            tokens = tokens[:tokens.index(eos_token_id)]
+        kind = self._structured_kind(self.decode(tokens).lstrip(), by_markers.status)
+        if kind is None:
+            return by_markers
         return StructuredThinkingParser(kind, self.decode, self.thinking_path, self.content_path).split(
             prompt, completion, eos_token_id=eos_token_id)
 
     def stop_boundary(self, prompt, completion, *, eos_token_id=None) -> int | None:
-        """Token index where generation may stop (the end of the first complete thinking block)."""
+        """Where generation may stop: the end of the first complete marker thinking block."""
         if not self.supports_early_stop:
             return None
         if self.decode is not None and self.decode(completion).lstrip().startswith("{"):

@@ -1,18 +1,19 @@
-"""Configurable verifier rewards behind the token-level reward interface.
+"""Verifier rewards: text scorers configured by a ``[verifier]`` TOML table and exposed as
+token-level rewards (single and batched) or as a batched training-reward callback.
 
-A verifier scores decoded (prompt, completion) text; adapters expose it as
-``reward(prompt_tokens, completion_tokens) -> float`` (and a batched form) for
-the AR and dLLM algorithms, and as a GRPO-style batched training callback.
-Configuration is one TOML ``[verifier]`` table:
+Table fields (validated against one schema, all problems reported together):
 
-    provider = "python" | "constant"
-    factory  = "package.module:factory"      # python: called as factory(context=..., **options)
-    name, options = {...}, requires_reference = bool, value = <float>  # constant
+    provider           "python" (default) or "constant"
+    factory            "package.module:callable"; called as factory(context=..., **options)
+    name               label used in the replay version key (default: factory, else provider)
+    options            keyword arguments of the factory ("context" is reserved)
+    requires_reference the verifier needs the example's reference answer
+    value              the reward of a constant verifier
 
-The table format, the factory call convention and the ``version`` replay key
-(``name:`` + the first 16 hex digits of the SHA-256 of the sorted compact JSON
-description) are those of src/inference_scaling/shared/verifier.py:69-451, so
-existing configs and replay caches stay valid.
+The table format, the factory call convention and the replay version string
+(``name:`` + 16 hex digits of the SHA-256 of the compact, key-sorted JSON of the
+spec) are the plugin contract of src/inference_scaling/shared/verifier.py: configs
+and replay caches written for it keep working here.
 """
 
 from __future__ import annotations
@@ -38,7 +39,7 @@ class VerifierInput:
 
 @dataclass(frozen=True, slots=True)
 class VerifierContext:
-    """What a verifier instance may see at construction (reference only if it opts in)."""
+    """What a verifier sees when it is built (the reference only if it asks for one)."""
 
     prompt: str
     reference: str | None = None
@@ -59,7 +60,49 @@ VerifierBatchCallable = Callable[[Sequence[VerifierInput]], Sequence[float]]
 TokenReward = Callable[[TokenSequence, TokenSequence], float]
 TokenBatchReward = Callable[[TokenSequence, Sequence[TokenSequence]], Sequence[float]]
 
-_FIELDS = {"provider", "name", "factory", "options", "requires_reference", "value"}
+_PROVIDERS = ("python", "constant")
+_KNOWN_FIELDS = frozenset({"provider", "name", "factory", "options", "requires_reference", "value"})
+
+
+def _nonempty_str(v: object) -> bool:
+    return isinstance(v, str) and bool(v)
+
+
+def _table_problems(t: Mapping[str, object]) -> tuple[list[str], list[str]]:
+    """(type problems, value problems) of one [verifier] table."""
+    types: list[str] = []
+    values: list[str] = []
+    unknown = sorted(set(t) - _KNOWN_FIELDS)
+    if unknown:
+        values.append(f"unknown fields {unknown}")
+    provider = t.get("provider", "python")
+    if not _nonempty_str(provider):
+        types.append("provider must be a non-empty string")
+    elif provider not in _PROVIDERS:
+        values.append(f"provider {provider!r} is not one of {_PROVIDERS}")
+    if "factory" in t and t["factory"] is not None and not _nonempty_str(t["factory"]):
+        types.append("factory must be a non-empty string")
+    if "options" in t and not isinstance(t["options"], Mapping):
+        types.append("options must be a table")
+    elif isinstance(t.get("options"), Mapping) and "context" in t["options"]:
+        values.append("options.context is reserved for the runtime")
+    if "name" in t and not _nonempty_str(t["name"]):
+        types.append("name must be a non-empty string")
+    if not isinstance(t.get("requires_reference", False), bool):
+        types.append("requires_reference must be true or false")
+    factory = t.get("factory")
+    has_value = "value" in t or (isinstance(t.get("options"), Mapping) and "value" in t["options"])
+    if provider == "python":
+        if not factory:
+            values.append("a python verifier needs a factory")
+        if "value" in t:
+            values.append("value belongs to constant verifiers")
+    elif provider == "constant":
+        if factory is not None:
+            values.append("a constant verifier takes no factory")
+        if not has_value:
+            values.append("a constant verifier needs a value")
+    return types, values
 
 
 @dataclass(frozen=True, slots=True)
@@ -72,64 +115,46 @@ class VerifierSpec:
 
     @classmethod
     def from_mapping(cls, values: Mapping[str, object]) -> "VerifierSpec":
-        extra = sorted(set(values) - _FIELDS)
-        if extra:
-            raise ValueError(f"unknown verifier configuration fields: {extra}")
+        type_problems, value_problems = _table_problems(values)
+        if type_problems:
+            raise TypeError("invalid [verifier] table: " + "; ".join(type_problems + value_problems))
+        if value_problems:
+            raise ValueError("invalid [verifier] table: " + "; ".join(value_problems))
         provider = values.get("provider", "python")
-        if not isinstance(provider, str) or not provider:
-            raise TypeError("verifier.provider must be a non-empty string")
-        if provider not in ("python", "constant"):
-            raise ValueError(f"unsupported verifier provider {provider!r}")
         factory = values.get("factory")
-        if factory is not None and (not isinstance(factory, str) or not factory):
-            raise TypeError("verifier.factory must be a non-empty string")
-        if provider == "python" and not factory:
-            raise ValueError("a Python verifier requires verifier.factory")
-        if provider == "constant" and factory is not None:
-            raise ValueError("a constant verifier cannot define verifier.factory")
-        opts = values.get("options", {})
-        if not isinstance(opts, Mapping):
-            raise TypeError("verifier.options must be a table")
-        opts = dict(opts)
-        if "context" in opts:
-            raise ValueError("verifier.options.context is reserved by the runtime")
+        options = dict(values.get("options", {}))
         if "value" in values:
-            if provider != "constant":
-                raise ValueError("verifier.value is valid only for provider='constant'")
-            opts["value"] = values["value"]
-        if provider == "constant" and "value" not in opts:
-            raise ValueError("a constant verifier requires verifier.value")
-        name = values.get("name", factory or provider)
-        if not isinstance(name, str) or not name:
-            raise TypeError("verifier.name must be a non-empty string")
-        req = values.get("requires_reference", False)
-        if not isinstance(req, bool):
-            raise TypeError("verifier.requires_reference must be a boolean")
-        return cls(provider, name, factory, opts, req)
+            options["value"] = values["value"]
+        return cls(provider, values.get("name", factory or provider), factory, options,
+                   values.get("requires_reference", False))
 
     def as_dict(self) -> dict[str, object]:
         return {"provider": self.provider, "name": self.name, "factory": self.factory, "options": dict(self.options),
                 "requires_reference": self.requires_reference}
 
+    def version(self) -> str:
+        blob = json.dumps(self.as_dict(), ensure_ascii=False, sort_keys=True, separators=(",", ":"))
+        return self.name + ":" + hashlib.sha256(blob.encode("utf-8")).hexdigest()[:16]
+
 
 def verifier_spec_from_config(config: Mapping[str, object]) -> VerifierSpec:
     table = config.get("verifier")
     if not isinstance(table, Mapping):
-        raise ValueError("a verifier-assisted method requires a [verifier] table")
+        raise ValueError("this method scores with a verifier: the config needs a [verifier] table")
     return VerifierSpec.from_mapping(table)
 
 
 def load_verifier_table(path: str | Path) -> dict[str, object]:
-    """A standalone TOML file holding exactly one ``[verifier]`` table (validated eagerly)."""
-    src = Path(path)
-    with src.open("rb") as f:
-        doc = tomllib.load(f)
-    if set(doc) != {"verifier"}:
-        raise ValueError(f"{src} must contain one top-level [verifier] table and no other sections")
-    if not isinstance(doc["verifier"], dict):
-        raise TypeError("[verifier] must be a TOML table")
-    VerifierSpec.from_mapping(doc["verifier"])
-    return dict(doc["verifier"])
+    """Read a TOML file that holds exactly one ``[verifier]`` table, validating it."""
+    path = Path(path)
+    document = tomllib.loads(path.read_text(encoding="utf-8"))
+    if list(document) != ["verifier"]:
+        raise ValueError(f"{path}: expected a single [verifier] table, found sections {sorted(document)}")
+    table = document["verifier"]
+    if not isinstance(table, dict):
+        raise TypeError(f"{path}: [verifier] is not a table")
+    VerifierSpec.from_mapping(table)
+    return dict(table)
 
 
 def replace_verifier_from_file(config: dict[str, Any], path: str | Path | None) -> None:
@@ -137,79 +162,81 @@ def replace_verifier_from_file(config: dict[str, Any], path: str | Path | None) 
         config["verifier"] = load_verifier_table(path)
 
 
-def _load_factory(ref: str) -> Callable[..., object]:
-    module, sep, attr = ref.partition(":")
-    if not sep or not module or not attr:
-        raise ValueError("verifier.factory must use the form 'package.module:factory_name'")
-    fn = getattr(importlib.import_module(module), attr, None)
-    if not callable(fn):
-        raise TypeError(f"verifier factory {ref!r} is not callable")
-    return fn
+def _resolve(reference: str) -> Callable[..., object]:
+    module_name, _, attribute = reference.partition(":")
+    if not module_name or not attribute:
+        raise ValueError(f"factory {reference!r} is not of the form 'package.module:callable'")
+    target = getattr(importlib.import_module(module_name), attribute, None)
+    if not callable(target):
+        raise TypeError(f"factory {reference!r} does not name a callable")
+    return target
 
 
-def _finite(value: object, name: str) -> float:
+def _as_reward(raw: object, who: str) -> float:
     try:
-        v = float(value)  # type: ignore[arg-type]
-    except (TypeError, ValueError) as e:
-        raise TypeError(f"verifier {name!r} returned a non-numeric reward {value!r}") from e
-    if not isfinite(v):
-        raise ValueError(f"verifier {name!r} returned a non-finite reward {v!r}")
-    return v
+        value = float(raw)  # type: ignore[arg-type]
+    except (TypeError, ValueError):
+        raise TypeError(f"verifier {who!r} produced {raw!r}, which is not a number") from None
+    if not isfinite(value):
+        raise ValueError(f"verifier {who!r} produced the non-finite reward {value}")
+    return value
 
 
 class ConfiguredVerifier:
-    """A validated verifier instance with its reproducibility metadata."""
+    """A built verifier: checked scalar and batched scoring plus its replay identity."""
 
     def __init__(self, spec: VerifierSpec, score: VerifierCallable, score_batch: VerifierBatchCallable | None = None):
-        self.spec, self._score, self._batch = spec, score, score_batch
+        self.spec = spec
+        self._one = score
+        self._many = score_batch
 
     def score(self, prompt: str, completion: str) -> float:
-        return _finite(self._score(prompt, completion), self.spec.name)
+        return _as_reward(self._one(prompt, completion), self.spec.name)
 
     def score_batch(self, inputs: Sequence[VerifierInput]) -> tuple[float, ...]:
-        if self._batch is None:
-            return tuple(self.score(i.prompt, i.completion) for i in inputs)
-        vals = tuple(self._batch(inputs))
-        if len(vals) != len(inputs):
-            raise ValueError(f"verifier {self.spec.name!r} returned {len(vals)} rewards for {len(inputs)} inputs")
-        return tuple(_finite(v, self.spec.name) for v in vals)
+        items = tuple(inputs)
+        raw = tuple(self._many(items)) if self._many is not None else tuple(
+            self._one(i.prompt, i.completion) for i in items)
+        if len(raw) != len(items):
+            raise ValueError(f"verifier {self.spec.name!r}: {len(raw)} rewards for {len(items)} inputs")
+        return tuple(_as_reward(r, self.spec.name) for r in raw)
 
     def describe(self) -> dict[str, object]:
         return self.spec.as_dict()
 
     @property
     def version(self) -> str:
-        blob = json.dumps(self.spec.as_dict(), ensure_ascii=False, sort_keys=True, separators=(",", ":"))
-        return f"{self.spec.name}:{hashlib.sha256(blob.encode('utf-8')).hexdigest()[:16]}"
+        return self.spec.version()
 
 
 def build_verifier(spec: VerifierSpec, *, context: VerifierContext) -> ConfiguredVerifier:
     if spec.requires_reference and context.reference is None:
-        raise ValueError(f"verifier {spec.name!r} requires a reference value")
+        raise ValueError(f"verifier {spec.name!r} scores against a reference, and none was given")
     if spec.provider == "constant":
-        v = _finite(spec.options["value"], spec.name)
-        return ConfiguredVerifier(spec, lambda _p, _c: v)
-    made = _load_factory(spec.factory)(context=context, **dict(spec.options))
-    if isinstance(made, TextVerifier):
-        batch = getattr(made, "score_batch", None)
-        return ConfiguredVerifier(spec, made.score, batch if callable(batch) else None)
-    if callable(made):
-        return ConfiguredVerifier(spec, made)
-    raise TypeError(f"verifier factory {spec.factory!r} returned unsupported value {type(made).__name__}")
+        constant = _as_reward(spec.options["value"], spec.name)
+        return ConfiguredVerifier(spec, lambda prompt, completion: constant)
+    product = _resolve(spec.factory)(context=context, **dict(spec.options))
+    if isinstance(product, TextVerifier):
+        batch = getattr(product, "score_batch", None)
+        return ConfiguredVerifier(spec, product.score, batch if callable(batch) else None)
+    if callable(product):
+        return ConfiguredVerifier(spec, product)
+    raise TypeError(f"factory {spec.factory!r} returned a {type(product).__name__}, neither a verifier nor a callable")
 
 
 class TokenVerifierReward:
-    """Token-level adapter: decodes ids and forwards to the text verifier."""
+    """reward(prompt_tokens, completion_tokens): decode, then score the text."""
 
     def __init__(self, verifier: ConfiguredVerifier, decoder: Callable[[TokenSequence], str]):
-        self.verifier, self._decode = verifier, decoder
+        self.verifier = verifier
+        self.decoder = decoder
 
     def __call__(self, prompt: TokenSequence, completion: TokenSequence) -> float:
-        return self.verifier.score(self._decode(prompt), self._decode(completion))
+        return self.verifier.score(self.decoder(prompt), self.decoder(completion))
 
     def batch(self, prompt: TokenSequence, completions: Sequence[TokenSequence]) -> tuple[float, ...]:
-        p = self._decode(prompt)
-        return self.verifier.score_batch(tuple(VerifierInput(p, self._decode(c)) for c in completions))
+        text = self.decoder(prompt)
+        return self.verifier.score_batch([VerifierInput(text, self.decoder(c)) for c in completions])
 
     def describe(self) -> dict[str, object]:
         return self.verifier.describe()
@@ -219,76 +246,108 @@ class TokenVerifierReward:
         return self.verifier.version
 
 
-def _text(value: object) -> str:
+def _message_text(value: object) -> str:
+    """Training columns hold strings, chat messages ({"content": ...}) or lists of either."""
     if isinstance(value, str):
         return value
     if isinstance(value, Mapping):
-        if "content" not in value:
-            raise TypeError("a training message must contain a content field")
-        return str(value["content"])
+        try:
+            return str(value["content"])
+        except KeyError:
+            raise TypeError("a chat message without a 'content' field") from None
     if isinstance(value, Sequence) and not isinstance(value, (bytes, bytearray)):
-        return "\n".join(_text(v) for v in value)
-    raise TypeError(f"unsupported training text value: {type(value).__name__}")
+        return "\n".join(map(_message_text, value))
+    raise TypeError(f"cannot read text from a {type(value).__name__}")
+
+
+@dataclass
+class _RewardTally:
+    calls: int = 0
+    completions: int = 0
+    completion_tokens: int = 0
+    total: float = 0.0
+    low: float | None = None
+    high: float | None = None
+
+    def add(self, rewards: Sequence[float]) -> None:
+        self.calls += 1
+        self.completions += len(rewards)
+        if rewards:
+            self.total += sum(rewards)
+            self.low = min(rewards) if self.low is None else min(self.low, *rewards)
+            self.high = max(rewards) if self.high is None else max(self.high, *rewards)
 
 
 class ConfiguredTrainingVerifierReward:
-    """Batched training-reward callback (prompts, completions, ...) -> rewards, one verifier per prompt."""
+    """Batched training reward (prompts, completions, ...) -> rewards.  One verifier is built
+    per distinct (prompt, reference) pair and cached; every completion of that pair is
+    scored in one batch."""
 
     def __init__(self, spec: VerifierSpec, *, reference_field: str = "reference"):
         if not reference_field:
-            raise ValueError("reference_field must be non-empty")
-        self.spec, self.reference_field = spec, reference_field
-        self._cache: dict[tuple[str, str | None], ConfiguredVerifier] = {}
-        self.calls = self.completions = self.completion_tokens = 0
-        self.reward_sum = 0.0
-        self.reward_minimum: float | None = None
-        self.reward_maximum: float | None = None
+            raise ValueError("reference_field has to name a dataset column")
+        self.spec = spec
+        self.reference_field = reference_field
+        self._verifiers: dict[tuple[str, str | None], ConfiguredVerifier] = {}
+        self._tally = _RewardTally()
+
+    # read-only counters of the calls so far
+    calls = property(lambda self: self._tally.calls)
+    completions = property(lambda self: self._tally.completions)
+    completion_tokens = property(lambda self: self._tally.completion_tokens)
+    reward_sum = property(lambda self: self._tally.total)
+    reward_minimum = property(lambda self: self._tally.low)
+    reward_maximum = property(lambda self: self._tally.high)
+
+    def _references(self, n: int, columns: Mapping[str, object]) -> Sequence[str | None]:
+        if not self.spec.requires_reference:
+            return [None] * n
+        refs = columns.get(self.reference_field)
+        if isinstance(refs, (str, bytes, bytearray)) or not isinstance(refs, Sequence):
+            raise ValueError(f"the verifier needs the column {self.reference_field!r} (one reference per row)")
+        if len(refs) != n:
+            raise ValueError(f"{len(refs)} references for {n} completions")
+        return [str(r) for r in refs]
+
+    def _verifier(self, prompt: str, reference: str | None) -> ConfiguredVerifier:
+        key = (prompt, reference)
+        if key not in self._verifiers:
+            self._verifiers[key] = build_verifier(self.spec, context=VerifierContext(prompt, reference))
+        return self._verifiers[key]
 
     def __call__(self, prompts: Sequence[object], completions: Sequence[object],
                  completion_ids: Sequence[Sequence[int]] | None = None, **columns: object) -> list[float]:
-        if len(prompts) != len(completions):
-            raise ValueError("training prompts and completions have different lengths")
-        if self.spec.requires_reference:
-            refs = columns.get(self.reference_field)
-            if not isinstance(refs, Sequence) or isinstance(refs, (str, bytes, bytearray)):
-                raise ValueError(f"training verifier requires column {self.reference_field!r}")
-            if len(refs) != len(completions):
-                raise ValueError("training references and completions have different lengths")
-        else:
-            refs = (None,) * len(completions)
-        ptxt = [_text(p) for p in prompts]
-        ctxt = [_text(c) for c in completions]
-        groups: dict[tuple[str, str | None], list[int]] = {}
-        for i, (p, r) in enumerate(zip(ptxt, refs)):
-            groups.setdefault((p, None if r is None else str(r)), []).append(i)
-        out = [0.0] * len(completions)
-        for key, idx in groups.items():
-            v = self._cache.get(key)
-            if v is None:
-                v = self._cache[key] = build_verifier(self.spec, context=VerifierContext(key[0], key[1]))
-            for i, val in zip(idx, v.score_batch(tuple(VerifierInput(key[0], ctxt[i]) for i in idx))):
-                out[i] = val
-        self.calls += 1
-        self.completions += len(completions)
+        n = len(completions)
+        if len(prompts) != n:
+            raise ValueError(f"{len(prompts)} prompts for {n} completions")
+        if completion_ids is not None and len(completion_ids) != n:
+            raise ValueError(f"{len(completion_ids)} token-id rows for {n} completions")
+        refs = self._references(n, columns)
+        prompt_text = [_message_text(p) for p in prompts]
+        completion_text = [_message_text(c) for c in completions]
+        rows_of: dict[tuple[str, str | None], list[int]] = {}
+        for i, key in enumerate(zip(prompt_text, refs)):
+            rows_of.setdefault(key, []).append(i)
+        rewards = [0.0] * n
+        for (prompt, reference), rows in rows_of.items():
+            scored = self._verifier(prompt, reference).score_batch(
+                [VerifierInput(prompt, completion_text[i]) for i in rows])
+            for i, r in zip(rows, scored):
+                rewards[i] = r
+        self._tally.add(rewards)
         if completion_ids is not None:
-            if len(completion_ids) != len(completions):
-                raise ValueError("training completion token ids and completions have different lengths")
-            self.completion_tokens += sum(len(t) for t in completion_ids)
-        if out:
-            self.reward_sum += sum(out)
-            lo, hi = min(out), max(out)
-            self.reward_minimum = lo if self.reward_minimum is None else min(self.reward_minimum, lo)
-            self.reward_maximum = hi if self.reward_maximum is None else max(self.reward_maximum, hi)
-        return out
+            self._tally.completion_tokens += sum(map(len, completion_ids))
+        return rewards
 
     def snapshot(self, *, num_generations: int) -> dict[str, int | float | None]:
-        if num_generations <= 0:
-            raise ValueError("num_generations must be positive")
-        return {"reward_calls": self.calls, "generated_completions": self.completions,
-                "generated_prompt_groups": self.completions // num_generations,
-                "generated_completion_tokens": self.completion_tokens, "reward_sum": self.reward_sum,
-                "observed_mean_reward": self.reward_sum / self.completions if self.completions else None,
-                "observed_minimum_reward": self.reward_minimum, "observed_maximum_reward": self.reward_maximum}
+        if num_generations < 1:
+            raise ValueError("num_generations has to be at least 1")
+        t = self._tally
+        return {"reward_calls": t.calls, "generated_completions": t.completions,
+                "generated_prompt_groups": t.completions // num_generations,
+                "generated_completion_tokens": t.completion_tokens, "reward_sum": t.total,
+                "observed_mean_reward": t.total / t.completions if t.completions else None,
+                "observed_minimum_reward": t.low, "observed_maximum_reward": t.high}
 
 
 def build_token_verifier_reward(config: Mapping[str, object], *, context: VerifierContext,
