@@ -1,6 +1,8 @@
-"""EOS-absorbing fixed-length view (the stopped-sequence backend with EOS as the only stop).
-
-Reference behaviour: src/inference_scaling/arllm/backends/absorbing.py:11-30.
+"""Fixed-length generation with EOS absorbing: once EOS is emitted every later token is
+EOS with probability one, so an outer fixed-length policy sees sequences of the length
+it asked for.  Implemented as a stop-sequence backend whose only stop is EOS; tokens
+before ``absorbing_after`` may not stop.  The model-id suffix is part of the cache and
+replay identity (src/inference_scaling/arllm/backends/absorbing.py).
 """
 
 from __future__ import annotations
@@ -19,9 +21,10 @@ class AbsorbingEOSBackend(StoppedSequenceBackend):
         self.model_id = f"{backend.model_id}|absorbing-eos={eos_token_id};after={absorbing_after}"
 
     def sample_batch(self, requests: Sequence[GenerationRequest]) -> list[SequenceSample]:
-        if any(r.sampling.eos_token_id is not None for r in requests):
-            raise ValueError("the outer fixed-length policy must leave eos_token_id unset; "
-                             "the adapter supplies absorbing EOS semantics")
+        owners = [r.request_id for r in requests if r.sampling.eos_token_id is not None]
+        if owners:
+            raise ValueError(f"requests {owners[:3]} set eos_token_id; with an absorbing-EOS backend the "
+                             "outer policy is fixed-length and EOS handling belongs to this adapter")
         return super().sample_batch(requests)
 
 

@@ -1,9 +1,10 @@
-"""Exact LRU cache of continuation scores keyed by (policy, prefix, continuation).
+"""Least-recently-used cache of exact continuation scores.
 
-Generations are never cached (they are random); scores are deterministic, so a
-repeated (policy, prefix, continuation) is served from the cache and only the
-misses go to the wrapped backend, grouped by (policy, prefix).
-Reference behaviour: src/inference_scaling/arllm/backends/cache.py:35-123.
+Scores are deterministic functions of (sampling policy, prefix, continuation), so a
+repeated triple is answered from memory and only the misses reach the wrapped backend,
+one request per distinct (policy, prefix).  Generations are random and never cached.
+Interface of src/inference_scaling/arllm/backends/cache.py (ScoreCachingBackend and
+its snapshot fields).
 """
 
 from __future__ import annotations
@@ -25,18 +26,43 @@ class ScoreCacheSnapshot:
 
     @property
     def hit_rate(self) -> float:
-        t = self.hits + self.misses
-        return self.hits / t if t else 0.0
+        looked_up = self.hits + self.misses
+        return self.hits / looked_up if looked_up else 0.0
+
+
+class _LRU:
+    def __init__(self, capacity: int):
+        self.capacity = capacity
+        self.items: OrderedDict = OrderedDict()
+        self.evictions = 0
+
+    def get(self, key):
+        value = self.items.get(key)
+        if value is not None:
+            self.items.move_to_end(key)
+        return value
+
+    def put_if_absent(self, key, value):
+        """Store ``value`` unless another thread stored one first; returns the stored value."""
+        held = self.get(key)
+        if held is not None:
+            return held
+        self.items[key] = value
+        while len(self.items) > self.capacity:
+            self.items.popitem(last=False)
+            self.evictions += 1
+        return value
 
 
 class ScoreCachingBackend:
     def __init__(self, backend: AutoregressiveBackend, *, maximum_entries: int = 100_000):
-        if maximum_entries <= 0:
-            raise ValueError("maximum_entries must be positive")
-        self._backend, self._cap = backend, int(maximum_entries)
-        self._cache: OrderedDict = OrderedDict()
+        if maximum_entries < 1:
+            raise ValueError("the score cache needs room for at least one entry")
+        self._backend = backend
+        self._lru = _LRU(int(maximum_entries))
         self._lock = threading.RLock()
-        self._hits = self._misses = self._evictions = 0
+        self._hits = 0
+        self._misses = 0
 
     @property
     def model_id(self) -> str:
@@ -49,53 +75,47 @@ class ScoreCachingBackend:
     def sample_batch(self, requests: Sequence[GenerationRequest]) -> list[SequenceSample]:
         return self._backend.sample_batch(requests)
 
-    def score_batch(self, requests: Sequence[ScoreRequest]) -> list[tuple[float, ...]]:
-        order, found, missing = [], {}, OrderedDict()
+    def _score_misses(self, misses: dict) -> dict:
+        by_context: dict[tuple, list] = {}
+        for policy, prefix, continuation in misses:
+            by_context.setdefault((policy, prefix), []).append(continuation)
+        batch = [ScoreRequest(prefix, tuple(conts), policy) for (policy, prefix), conts in by_context.items()]
+        keys = [(policy, prefix, c) for (policy, prefix), conts in by_context.items() for c in conts]
+        scores = self._backend.score_batch(batch)
+        if len(scores) != len(keys):
+            raise RuntimeError(f"the wrapped backend returned {len(scores)} scores for {len(keys)} continuations")
+        fresh = {}
         with self._lock:
-            for r in requests:
-                for c in r.continuations:
-                    key = (r.sampling, r.prefix, c)
-                    order.append(key)
-                    hit = self._cache.get(key)
-                    if hit is None:
-                        self._misses += 1
-                        missing.setdefault(key, None)
-                    else:
-                        self._hits += 1
-                        self._cache.move_to_end(key)
-                        found[key] = hit
-        if missing:
-            groups: OrderedDict = OrderedDict()
-            for s, p, c in missing:
-                groups.setdefault((s, p), []).append(c)
-            reqs = [ScoreRequest(p, tuple(cs), s) for (s, p), cs in groups.items()]
-            keys = [(s, p, c) for (s, p), cs in groups.items() for c in cs]
-            scored = self._backend.score_batch(reqs)
-            if len(scored) != len(keys):
-                raise RuntimeError("underlying backend returned an invalid score batch")
-            with self._lock:
-                for key, val in zip(keys, scored):
-                    if len(val) != len(key[2]):
-                        raise RuntimeError("underlying backend returned an invalid score shape")
-                    old = self._cache.get(key)
-                    if old is None:
-                        self._cache[key] = val
-                        while len(self._cache) > self._cap:
-                            self._cache.popitem(last=False)
-                            self._evictions += 1
-                        found[key] = val
-                    else:
-                        self._cache.move_to_end(key)
-                        found[key] = old
-        return [found[k] for k in order]
+            for key, value in zip(keys, scores):
+                if len(value) != len(key[2]):
+                    raise RuntimeError("a score does not have one entry per continuation token")
+                fresh[key] = self._lru.put_if_absent(key, value)
+        return fresh
+
+    def score_batch(self, requests: Sequence[ScoreRequest]) -> list[tuple[float, ...]]:
+        wanted = [(r.sampling, r.prefix, c) for r in requests for c in r.continuations]
+        known: dict = {}
+        misses: dict = {}
+        with self._lock:
+            for key in wanted:
+                value = self._lru.get(key)
+                if value is None:
+                    self._misses += 1
+                    misses[key] = None
+                else:
+                    self._hits += 1
+                    known[key] = value
+        if misses:
+            known.update(self._score_misses(misses))
+        return [known[key] for key in wanted]
 
     def clear(self) -> None:
         with self._lock:
-            self._cache.clear()
+            self._lru.items.clear()
 
     def snapshot(self) -> ScoreCacheSnapshot:
         with self._lock:
-            return ScoreCacheSnapshot(len(self._cache), self._hits, self._misses, self._evictions)
+            return ScoreCacheSnapshot(len(self._lru.items), self._hits, self._misses, self._lru.evictions)
 
 
 __all__ = ["ScoreCacheSnapshot", "ScoreCachingBackend"]

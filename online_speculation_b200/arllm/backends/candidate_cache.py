@@ -1,8 +1,8 @@
-"""Replay of frozen candidate samples by request id, with scoring delegated to a live backend.
+"""Serve frozen candidate samples again by request id; scores still come from a live backend.
 
-A request can only retrieve the sample frozen under the same request id,
-prefix, policy and model (and no longer than its budget).
-Reference behaviour: src/inference_scaling/arllm/backends/candidate_cache.py:15-59.
+A request gets the sample frozen under its own id only when prefix, policy, model and
+length budget all agree with it, so a replayed run is the run that was frozen.
+Behaviour of src/inference_scaling/arllm/backends/candidate_cache.py.
 """
 
 from __future__ import annotations
@@ -12,28 +12,39 @@ from collections.abc import Sequence
 from ..types import AutoregressiveBackend, GenerationRequest, ScoreRequest, SequenceSample
 
 
+def _mismatch(sample: SequenceSample, request: GenerationRequest, model_id: str) -> str | None:
+    checks = (("prefix", sample.prefix == request.prefix),
+              ("policy", sample.policy_id == request.sampling.policy_id),
+              ("model", sample.model_id == model_id),
+              ("length", len(sample.token_ids) <= request.max_new_tokens))
+    failed = [name for name, ok in checks if not ok]
+    return ", ".join(failed) if failed else None
+
+
 class CachedCandidateBackend:
     def __init__(self, scoring_backend: AutoregressiveBackend, samples: Sequence[SequenceSample]):
         self.scoring_backend = scoring_backend
-        self.samples = {s.request_id: s for s in samples}
-        if len(self.samples) != len(samples):
-            raise ValueError("cached candidate request ids must be unique")
+        ids = [s.request_id for s in samples]
+        if len(set(ids)) != len(ids):
+            raise ValueError("frozen candidates must have distinct request ids")
+        self.samples = dict(zip(ids, samples))
 
     @property
     def model_id(self) -> str:
         return self.scoring_backend.model_id
 
+    def _lookup(self, request: GenerationRequest) -> SequenceSample:
+        try:
+            sample = self.samples[request.request_id]
+        except KeyError:
+            raise KeyError(f"no frozen candidate for request {request.request_id!r}") from None
+        problem = _mismatch(sample, request, self.model_id)
+        if problem is not None:
+            raise RuntimeError(f"frozen candidate {request.request_id!r} differs from its request in: {problem}")
+        return sample
+
     def sample_batch(self, requests: Sequence[GenerationRequest]) -> list[SequenceSample]:
-        out = []
-        for r in requests:
-            s = self.samples.get(r.request_id)
-            if s is None:
-                raise KeyError(f"candidate request {r.request_id!r} is absent from the frozen cache")
-            if (s.prefix != r.prefix or s.policy_id != r.sampling.policy_id or s.model_id != self.model_id
-                    or len(s.token_ids) > r.max_new_tokens):
-                raise RuntimeError("cached candidate does not match its frozen request")
-            out.append(s)
-        return out
+        return [self._lookup(r) for r in requests]
 
     def score_batch(self, requests: Sequence[ScoreRequest]) -> list[tuple[float, ...]]:
         return self.scoring_backend.score_batch(requests)

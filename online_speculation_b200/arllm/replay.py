@@ -1,22 +1,26 @@
-"""Replay records, behaviour policies and a single-use data-pool lifecycle.
+"""Replay records, behaviour policies, and a store whose evaluation records are used once.
 
-A record stores a completion generated from ``key.rollout_prefix`` by a named
-behaviour policy, its reward and its behaviour log-probability.  Evaluation
-records are used at most once: ``freeze_claims`` reserves them before any
-completion or reward is revealed (only behaviour-id counts are visible), and
-``reveal_and_consume`` moves them to the design pool.  Mixture behaviour
-log-probabilities (several behaviour policies) and re-validation of stored
-probabilities are computed by re-scoring with the registered backends.
+A record is a completion generated from ``key.rollout_prefix`` by a named behaviour
+policy, with its reward and behaviour log-probability.  The store tracks every record
+in one table with a lifecycle state:
 
-Reference behaviour: src/inference_scaling/arllm/replay.py:28-478.
+    evaluation  ->  reserved (by a frozen claim)  ->  design
+
+``freeze_claims`` reserves up to n evaluation records per key before anything about
+them except their behaviour ids is revealed; ``reveal_and_consume`` hands a claim's
+records over and moves them to the design pool, so an evaluation record can inform
+at most one estimate.  Mixture behaviour log-probabilities (records drawn by several
+policies) and checks of stored probabilities re-score completions with the registered
+backends.  Request ids ``replay:<record_id>`` and claim ids ``claim-<n>`` follow
+src/inference_scaling/arllm/replay.py (they key caches and saved runs).
 """
 
 from __future__ import annotations
 
-from collections import Counter, defaultdict
+from collections import Counter
 from collections.abc import Callable, Iterable, Mapping, Sequence
 from dataclasses import dataclass
-from math import isclose, isfinite, log
+from math import isfinite
 
 import numpy as np
 
@@ -37,7 +41,7 @@ class ReplayKey:
 
     @property
     def rollout_prefix(self) -> TokenSequence:
-        return self.prompt + self.generated_prefix + self.candidate
+        return tuple(self.prompt) + tuple(self.generated_prefix) + tuple(self.candidate)
 
 
 @dataclass(frozen=True, slots=True)
@@ -50,12 +54,10 @@ class ReplayRecord:
     behavior_logprob: float
 
     def __post_init__(self) -> None:
-        if not self.record_id or not self.behavior_id:
-            raise ValueError("record_id and behavior_id cannot be empty")
-        if not isfinite(self.reward):
-            raise ValueError("stored reward must be finite")
-        if not isfinite(self.behavior_logprob):
-            raise ValueError("a generated completion must have finite behavior log-probability")
+        if not (self.record_id and self.behavior_id):
+            raise ValueError("a replay record needs a record id and a behaviour id")
+        if not (isfinite(self.reward) and isfinite(self.behavior_logprob)):
+            raise ValueError("a replay record's reward and behaviour log-probability have to be finite")
 
 
 @dataclass(frozen=True, slots=True)
@@ -66,10 +68,14 @@ class ReplaySampleRequest:
     record_id: str
 
     def __post_init__(self) -> None:
-        if self.max_new_tokens < 0 or self.seed < 0:
-            raise ValueError("max_new_tokens and seed must be non-negative")
+        if min(self.max_new_tokens, self.seed) < 0:
+            raise ValueError("max_new_tokens and seed cannot be negative")
         if not self.record_id:
-            raise ValueError("record_id cannot be empty")
+            raise ValueError("a replay request needs a record id")
+
+
+def _request_id(record_id: str) -> str:
+    return f"replay:{record_id}"
 
 
 @dataclass(frozen=True, slots=True)
@@ -80,33 +86,32 @@ class BehaviorPolicy:
 
     @classmethod
     def for_backend(cls, backend: AutoregressiveBackend, sampling: SamplingConfig, *, label: str | None = None):
-        return cls(label or f"{backend.model_id}|{sampling.policy_id}", backend, sampling)
+        return cls(label if label else f"{backend.model_id}|{sampling.policy_id}", backend, sampling)
 
 
 @dataclass(frozen=True, slots=True)
 class BrokeredReplayState:
-    """Replay metadata paired with a resumable, unfinished rollout."""
+    """Replay metadata paired with its resumable, unfinished rollout."""
 
     request: ReplaySampleRequest
     rollout: PartialRollout
 
     def __post_init__(self) -> None:
         g = self.rollout.request
-        if self.request.max_new_tokens <= 0:
-            raise ValueError("brokered replay requires a positive rollout length")
-        if g.request_id != f"replay:{self.request.record_id}":
-            raise ValueError("brokered replay request id does not match its record")
-        if (g.prefix, g.max_new_tokens, g.seed) != (self.request.key.rollout_prefix, self.request.max_new_tokens,
-                                                    self.request.seed):
-            raise ValueError("brokered replay rollout does not match its request")
+        expected = (_request_id(self.request.record_id), self.request.key.rollout_prefix,
+                    self.request.max_new_tokens, self.request.seed)
+        if self.request.max_new_tokens < 1:
+            raise ValueError("a brokered replay rollout generates at least one token")
+        if (g.request_id, g.prefix, g.max_new_tokens, g.seed) != expected:
+            raise ValueError("the rollout does not belong to this replay request")
 
     @classmethod
     def start(cls, policy: BehaviorPolicy, request: ReplaySampleRequest, *, priority: float = 0.0):
-        if request.max_new_tokens <= 0:
-            raise ValueError("brokered replay requires a positive rollout length")
-        g = GenerationRequest(request.key.rollout_prefix, request.max_new_tokens, policy.sampling, request.seed,
-                              f"replay:{request.record_id}")
-        return cls(request, PartialRollout.from_request(g, priority=float(priority)))
+        if request.max_new_tokens < 1:
+            raise ValueError("a brokered replay rollout generates at least one token")
+        generation = GenerationRequest(request.key.rollout_prefix, request.max_new_tokens, policy.sampling,
+                                       request.seed, _request_id(request.record_id))
+        return cls(request, PartialRollout.from_request(generation, priority=float(priority)))
 
 
 @dataclass(frozen=True, slots=True)
@@ -117,32 +122,31 @@ class BrokeredReplayResult:
 
 
 class BehaviorRegistry:
+    """Behaviour policies by id; registering the same id twice must describe the same policy."""
+
     def __init__(self, policies: Iterable[BehaviorPolicy] = ()):
-        self._p: dict[str, BehaviorPolicy] = {}
-        for p in policies:
-            self.register(p)
+        self._policies: dict[str, BehaviorPolicy] = {}
+        for policy in policies:
+            self.register(policy)
 
     def register(self, policy: BehaviorPolicy) -> None:
-        old = self._p.get(policy.behavior_id)
-        if old is not None:
-            if old.backend.model_id != policy.backend.model_id or old.sampling != policy.sampling:
-                raise ValueError(f"behavior id {policy.behavior_id!r} has conflicting definitions")
-            return
-        self._p[policy.behavior_id] = policy
+        known = self._policies.setdefault(policy.behavior_id, policy)
+        if known is not policy and (known.backend.model_id, known.sampling) != (policy.backend.model_id,
+                                                                                 policy.sampling):
+            raise ValueError(f"behaviour id {policy.behavior_id!r} is already registered with another policy")
 
     def get(self, behavior_id: str) -> BehaviorPolicy:
-        try:
-            return self._p[behavior_id]
-        except KeyError as e:
-            raise KeyError(f"unknown behavior policy {behavior_id!r}") from e
+        if behavior_id not in self._policies:
+            raise KeyError(f"no behaviour policy is registered as {behavior_id!r}")
+        return self._policies[behavior_id]
 
     def __contains__(self, behavior_id: str) -> bool:
-        return behavior_id in self._p
+        return behavior_id in self._policies
 
 
 @dataclass(frozen=True, slots=True)
 class FrozenReplayClaim:
-    """Metadata-only claim (behaviour counts) made before any completion is revealed."""
+    """Claim made before any completion is revealed: only behaviour counts are visible."""
 
     claim_id: str
     key: ReplayKey
@@ -150,149 +154,158 @@ class FrozenReplayClaim:
 
     @property
     def count(self) -> int:
-        return sum(c for _, c in self.behavior_counts)
+        return sum(n for _, n in self.behavior_counts)
+
+
+def _behaviour_counts(records: Iterable[ReplayRecord]) -> tuple[tuple[str, int], ...]:
+    return tuple(sorted(Counter(r.behavior_id for r in records).items()))
 
 
 class InMemoryReplayStore:
-    """Evaluation records are single use by construction; consumed records join the design pool."""
+    """One table of records, each in state "evaluation", "design" or a claim id (reserved)."""
+
+    _EVAL, _DESIGN = "evaluation", "design"
 
     def __init__(self):
-        self._eval: dict[ReplayKey, list[ReplayRecord]] = defaultdict(list)
-        self._design: list[ReplayRecord] = []
-        self._reserved: dict[str, tuple[ReplayRecord, ...]] = {}
+        self._records: list[ReplayRecord] = []
+        self._state: list[str] = []
         self._ids: set[str] = set()
         self._claims = 0
+        self._open_claims: set[str] = set()
 
-    def _new(self, r: ReplayRecord) -> None:
-        if r.record_id in self._ids:
-            raise ValueError(f"duplicate replay record id {r.record_id!r}")
-        self._ids.add(r.record_id)
+    def _add(self, record: ReplayRecord, state: str) -> None:
+        if record.record_id in self._ids:
+            raise ValueError(f"replay record id {record.record_id!r} is already stored")
+        self._ids.add(record.record_id)
+        self._records.append(record)
+        self._state.append(state)
 
     def add_evaluation(self, record: ReplayRecord) -> None:
-        self._new(record)
-        self._eval[record.key].append(record)
+        self._add(record, self._EVAL)
 
     def add_design(self, record: ReplayRecord) -> None:
-        self._new(record)
-        self._design.append(record)
+        self._add(record, self._DESIGN)
+
+    def _rows(self, state: str, key: ReplayKey | None = None) -> list[int]:
+        return [i for i, (r, s) in enumerate(zip(self._records, self._state))
+                if s == state and (key is None or r.key == key)]
 
     def inventory(self, key: ReplayKey) -> dict[str, int]:
-        return dict(Counter(r.behavior_id for r in self._eval.get(key, ())))
+        return dict(Counter(self._records[i].behavior_id for i in self._rows(self._EVAL, key)))
 
     def freeze_claims(self, keys: Sequence[ReplayKey], max_records_per_candidate: int
                       ) -> tuple[FrozenReplayClaim, ...]:
         if max_records_per_candidate < 0:
-            raise ValueError("max_records_per_candidate must be non-negative")
-        out = []
-        for k in keys:
-            avail = self._eval.get(k, [])
-            take = tuple(avail[:max_records_per_candidate])
-            del avail[:len(take)]
+            raise ValueError("max_records_per_candidate cannot be negative")
+        claims = []
+        for key in keys:
             self._claims += 1
-            cid = f"claim-{self._claims}"
-            self._reserved[cid] = take
-            out.append(FrozenReplayClaim(cid, k, tuple(sorted(Counter(r.behavior_id for r in take).items()))))
-        return tuple(out)
+            claim_id = f"claim-{self._claims}"
+            taken = self._rows(self._EVAL, key)[:max_records_per_candidate]
+            for i in taken:
+                self._state[i] = claim_id
+            self._open_claims.add(claim_id)
+            claims.append(FrozenReplayClaim(claim_id, key, _behaviour_counts(self._records[i] for i in taken)))
+        return tuple(claims)
 
     def reveal_and_consume(self, claim: FrozenReplayClaim) -> tuple[ReplayRecord, ...]:
-        try:
-            recs = self._reserved.pop(claim.claim_id)
-        except KeyError as e:
-            raise ValueError(f"claim {claim.claim_id!r} is unknown or already consumed") from e
-        if any(r.key != claim.key for r in recs):
-            raise RuntimeError("replay claim key mismatch")
-        if tuple(sorted(Counter(r.behavior_id for r in recs).items())) != claim.behavior_counts:
-            raise RuntimeError("replay claim metadata changed after freezing")
-        self._design.extend(recs)
-        return recs
+        if claim.claim_id not in self._open_claims:
+            raise ValueError(f"claim {claim.claim_id!r} is unknown or was already consumed")
+        rows = self._rows(claim.claim_id)
+        records = tuple(self._records[i] for i in rows)
+        if any(r.key != claim.key for r in records) or _behaviour_counts(records) != claim.behavior_counts:
+            raise RuntimeError(f"the records reserved by {claim.claim_id!r} no longer match the claim")
+        self._open_claims.discard(claim.claim_id)
+        for i in rows:
+            self._state[i] = self._DESIGN
+        return records
 
     def design_records(self, key: ReplayKey | None = None) -> tuple[ReplayRecord, ...]:
-        return tuple(self._design) if key is None else tuple(r for r in self._design if r.key == key)
+        return tuple(self._records[i] for i in self._rows(self._DESIGN, key))
 
     @property
     def evaluation_count(self) -> int:
-        return sum(len(v) for v in self._eval.values())
+        return self._state.count(self._EVAL)
 
     @property
     def design_count(self) -> int:
-        return len(self._design)
+        return self._state.count(self._DESIGN)
 
     @property
     def reserved_count(self) -> int:
-        return sum(len(v) for v in self._reserved.values())
+        return sum(s not in (self._EVAL, self._DESIGN) for s in self._state)
 
 
 def score_continuations(policy: BehaviorPolicy, key: ReplayKey, completions: Sequence[TokenSequence]
                         ) -> tuple[float, ...]:
-    if not completions:
+    """Sequence log-probabilities of ``completions`` after the key's rollout prefix."""
+    if not len(completions):
         return ()
-    got = policy.backend.score_batch([ScoreRequest(key.rollout_prefix, tuple(completions), policy.sampling)])
-    if len(got) != len(completions):
-        raise RuntimeError("behavior backend returned an invalid number of scores")
-    out = []
-    for c, s in zip(completions, got):
-        if len(s) != len(c):
-            raise RuntimeError("behavior backend returned an invalid token score shape")
-        out.append(float(sum(s)))
-    return tuple(out)
+    scores = policy.backend.score_batch([ScoreRequest(key.rollout_prefix, tuple(completions), policy.sampling)])
+    if len(scores) != len(completions) or any(len(s) != len(c) for s, c in zip(scores, completions)):
+        raise RuntimeError("the behaviour backend's scores do not match the completions")
+    return tuple(float(np.sum(s)) for s in scores)
 
 
 def mixture_logprobabilities(registry: BehaviorRegistry, key: ReplayKey, behavior_counts: Mapping[str, int],
                              completions: Sequence[TokenSequence]) -> tuple[float, ...]:
-    """log sum_b (n_b / n) q_b(completion) over the behaviour policies that produced the records."""
-    total = sum(behavior_counts.values())
-    if total <= 0:
-        raise ValueError("a behavior mixture requires at least one selected record")
-    comps = []
-    for bid, n in sorted(behavior_counts.items()):
-        if n <= 0:
-            raise ValueError("behavior mixture counts must be positive")
-        comps.append(np.asarray(score_continuations(registry.get(bid), key, completions)) + log(n / total))
-    return tuple(float(v) for v in np.logaddexp.reduce(np.stack(comps), axis=0))
+    """log sum_b (n_b / n) q_b(completion): the behaviour law of records pooled from several policies."""
+    ids = sorted(behavior_counts)
+    counts = np.asarray([behavior_counts[b] for b in ids], dtype=np.float64)
+    if counts.size == 0 or counts.sum() <= 0:
+        raise ValueError("a behaviour mixture needs at least one record")
+    if (counts <= 0).any():
+        raise ValueError("every behaviour in a mixture needs a positive count")
+    table = np.asarray([score_continuations(registry.get(b), key, completions) for b in ids], dtype=np.float64)
+    weights = np.log(counts / counts.sum())[:, None]
+    return tuple(np.logaddexp.reduce(table + weights, axis=0).tolist())
 
 
 def validate_record_probabilities(records: Sequence[ReplayRecord], registry: BehaviorRegistry, *,
                                   absolute_tolerance: float = 1e-5, per_token_tolerance: float = 2e-4) -> None:
-    """Re-score stored completions; reject a record whose stored behaviour probability is not reproduced."""
-    if absolute_tolerance < 0 or per_token_tolerance < 0:
-        raise ValueError("probability validation tolerances must be non-negative")
-    groups: dict[tuple, list[ReplayRecord]] = defaultdict(list)
-    for r in records:
-        groups[(r.key, r.behavior_id)].append(r)
-    for (k, bid), g in groups.items():
-        for r, s in zip(g, score_continuations(registry.get(bid), k, [x.completion for x in g])):
-            tol = absolute_tolerance + per_token_tolerance * len(r.completion)
-            if not isclose(r.behavior_logprob, s, rel_tol=0.0, abs_tol=tol):
-                raise ValueError(f"stored behavior probability for {r.record_id!r} cannot be reproduced within "
-                                 f"tolerance {tol:g}")
+    """Re-score stored completions; a stored behaviour probability that is not reproduced is an error."""
+    if min(absolute_tolerance, per_token_tolerance) < 0:
+        raise ValueError("tolerances cannot be negative")
+    groups: dict[tuple, list[ReplayRecord]] = {}
+    for record in records:
+        groups.setdefault((record.key, record.behavior_id), []).append(record)
+    for (key, behavior), group in groups.items():
+        fresh = np.asarray(score_continuations(registry.get(behavior), key, [r.completion for r in group]))
+        stored = np.asarray([r.behavior_logprob for r in group])
+        allowed = absolute_tolerance + per_token_tolerance * np.asarray([len(r.completion) for r in group])
+        bad = np.flatnonzero(np.abs(stored - fresh) > allowed)
+        if bad.size:
+            r = group[int(bad[0])]
+            raise ValueError(f"record {r.record_id!r}: stored behaviour log-probability {r.behavior_logprob:.6g} "
+                             f"is not reproduced (re-scored {fresh[bad[0]]:.6g}, tolerance {allowed[bad[0]]:g})")
+
+
+def _record(policy: BehaviorPolicy, request: ReplaySampleRequest, completion, logprob, reward: TokenReward):
+    k = request.key
+    value = float(reward(k.prompt, tuple(k.generated_prefix) + tuple(k.candidate) + tuple(completion)))
+    return ReplayRecord(request.record_id, k, tuple(completion), value, policy.behavior_id, logprob)
+
+
+def _check_policy(policy: BehaviorPolicy, sample) -> None:
+    if sample.model_id != policy.backend.model_id or sample.policy_id != policy.sampling.policy_id:
+        raise RuntimeError("a replay sample was not drawn by its declared behaviour policy")
 
 
 def sample_replay_records(policy: BehaviorPolicy, requests: Sequence[ReplaySampleRequest], reward: TokenReward
                           ) -> tuple[ReplayRecord, ...]:
-    """Generate replay completions for heterogeneous keys in one backend batch."""
-    gen, where = [], []
-    for i, r in enumerate(requests):
-        if r.max_new_tokens:
-            gen.append(GenerationRequest(r.key.rollout_prefix, r.max_new_tokens, policy.sampling, r.seed,
-                                         f"replay:{r.record_id}"))
-            where.append(i)
-    got = policy.backend.sample_batch(gen) if gen else []
-    if len(got) != len(gen):
-        raise RuntimeError("replay backend returned an invalid number of samples")
-    by = dict(zip(where, got))
-    out = []
-    for i, r in enumerate(requests):
-        s = by.get(i)
-        if s is None:
-            comp, lp = (), 0.0
-        else:
-            if s.model_id != policy.backend.model_id or s.policy_id != policy.sampling.policy_id:
-                raise RuntimeError("replay sample does not match its declared behavior policy")
-            comp, lp = s.token_ids, s.logprob
-        out.append(ReplayRecord(r.record_id, r.key, comp,
-                                float(reward(r.key.prompt, r.key.generated_prefix + r.key.candidate + comp)),
-                                policy.behavior_id, lp))
-    return tuple(out)
+    """Generate completions for requests of different keys in one backend batch
+    (zero-length requests record an empty completion of log-probability 0)."""
+    active = [r for r in requests if r.max_new_tokens]
+    batch = [GenerationRequest(r.key.rollout_prefix, r.max_new_tokens, policy.sampling, r.seed,
+                               _request_id(r.record_id)) for r in active]
+    samples = policy.backend.sample_batch(batch) if batch else []
+    if len(samples) != len(batch):
+        raise RuntimeError(f"{len(samples)} replay samples came back for {len(batch)} requests")
+    drawn = {}
+    for request, sample in zip(active, samples):
+        _check_policy(policy, sample)
+        drawn[request.record_id] = (sample.token_ids, sample.logprob)
+    return tuple(_record(policy, r, *drawn.get(r.record_id, ((), 0.0)), reward) for r in requests)
 
 
 def sample_replay_record(policy: BehaviorPolicy, key: ReplayKey, max_new_tokens: int, reward: TokenReward, *,
@@ -304,39 +317,35 @@ def sample_replay_records_brokered(policy: BehaviorPolicy, work: Sequence[Replay
                                    reward: TokenReward, broker: AsyncRolloutBroker, *,
                                    completion_target: int | None = None,
                                    on_record: Callable[[ReplayRecord], None] | None = None) -> BrokeredReplayResult:
-    """Replay generation through the rollout broker; only finished trajectories become records."""
+    """Replay generation through a rollout broker; only finished trajectories become records."""
     if broker.backend is not policy.backend:
-        raise ValueError("rollout broker must use the behavior policy backend")
-    states = tuple(w if isinstance(w, BrokeredReplayState) else BrokeredReplayState.start(policy, w) for w in work)
+        raise ValueError("the broker has to sample from the behaviour policy's backend")
+    states = [w if isinstance(w, BrokeredReplayState) else BrokeredReplayState.start(policy, w) for w in work]
     if not states:
-        raise ValueError("brokered replay requires at least one rollout")
-    by_id: dict[str, BrokeredReplayState] = {}
-    for st in states:
-        g = st.rollout.request
+        raise ValueError("brokered replay needs at least one rollout")
+    by_request: dict[str, BrokeredReplayState] = {}
+    for state in states:
+        g = state.rollout.request
         if g.sampling != policy.sampling:
-            raise ValueError("brokered replay state uses the wrong behavior policy")
-        if st.rollout.complete:
-            raise ValueError("completed replay state must not be resubmitted")
-        if g.request_id in by_id:
-            raise ValueError("brokered replay record ids must be unique")
-        by_id[g.request_id] = st
-    res = broker.run_until(tuple(s.rollout for s in states), completion_target=completion_target)
-    recs = []
-    for smp in res.completed:
-        st = by_id.get(smp.request_id)
-        if st is None:
-            raise RuntimeError("broker completed an unknown replay request")
-        if smp.model_id != policy.backend.model_id or smp.policy_id != policy.sampling.policy_id:
-            raise RuntimeError("brokered replay sample used the wrong behavior policy")
-        k = st.request.key
-        rec = ReplayRecord(st.request.record_id, k, smp.token_ids,
-                           float(reward(k.prompt, k.generated_prefix + k.candidate + smp.token_ids)),
-                           policy.behavior_id, smp.logprob)
-        recs.append(rec)
+            raise ValueError(f"{g.request_id} samples from another behaviour policy")
+        if state.rollout.complete:
+            raise ValueError(f"{g.request_id} is already finished")
+        if g.request_id in by_request:
+            raise ValueError(f"{g.request_id} was submitted twice")
+        by_request[g.request_id] = state
+    result = broker.run_until([s.rollout for s in states], completion_target=completion_target)
+    records = []
+    for sample in result.completed:
+        state = by_request.get(sample.request_id)
+        if state is None:
+            raise RuntimeError(f"the broker finished {sample.request_id!r}, which was not submitted")
+        _check_policy(policy, sample)
+        record = _record(policy, state.request, sample.token_ids, sample.logprob, reward)
+        records.append(record)
         if on_record is not None:
-            on_record(rec)
-    partial = tuple(BrokeredReplayState(by_id[p.request.request_id].request, p) for p in res.partial)
-    return BrokeredReplayResult(tuple(recs), partial, res.snapshot)
+            on_record(record)
+    partial = tuple(BrokeredReplayState(by_request[p.request.request_id].request, p) for p in result.partial)
+    return BrokeredReplayResult(tuple(records), partial, result.snapshot)
 
 
 __all__ = ["BehaviorPolicy", "BehaviorRegistry", "BrokeredReplayResult", "BrokeredReplayState", "FrozenReplayClaim",

@@ -1,18 +1,21 @@
-"""Resumable partial rollouts and an over-provisioning rollout broker.
+"""Resumable rollouts and a broker that stops once enough of them have finished.
 
-State is token sequences, not engine KV objects, so an interrupted rollout can
-resume on any backend (and survives cache eviction).  Each resumed segment is
-sampled from the requested policy given the tokens so far; the log-probabilities
-returned are those actually used.  ``AsyncRolloutBroker.run_until`` advances
-requests in ``chunk_tokens`` segments (partial trajectories first, then by
-priority) until ``completion_target`` of them finished, bounding the work left
-unfinished in an over-provisioned batch.
-
-Reference behaviour: src/inference_scaling/arllm/rollout_broker.py:32-333.
+A :class:`PartialRollout` stores tokens, not engine KV state, so an interrupted
+rollout can continue on any backend.  Each resumed segment is sampled from the
+request's own policy given the tokens so far, and the log-probabilities kept are
+the ones that segment actually used.  :class:`AsyncRolloutBroker` advances rollouts
+``chunk_tokens`` at a time, most urgent first (priority, then those already
+started, then the longest), until ``completion_target`` of them have finished; what
+is left is returned as partial rollouts, which bounds the work an
+over-provisioned batch wastes.  Segment seeds come from the stream
+``(seed, "partial-rollout", request_id, segment)`` and segment request ids end in
+``:segment:<n>``, the random-stream and id conventions of
+src/inference_scaling/arllm/rollout_broker.py.
 """
 
 from __future__ import annotations
 
+import heapq
 import threading
 from collections.abc import Callable, Sequence
 from dataclasses import dataclass
@@ -37,16 +40,20 @@ class PartialRollout:
     priority: float = 0.0
 
     def __post_init__(self) -> None:
-        if len(self.token_ids) != len(self.token_logprobs):
-            raise ValueError("partial rollout tokens and log-probabilities must align")
+        n = len(self.token_ids)
+        problems = []
+        if len(self.token_logprobs) != n:
+            problems.append("one log-probability per token")
         if (self.reference_token_logprobs is None) != (self.reference_policy_id is None):
-            raise ValueError("partial reference probabilities require a policy id")
-        if self.reference_token_logprobs is not None and len(self.reference_token_logprobs) != len(self.token_ids):
-            raise ValueError("partial reference probabilities must align with tokens")
-        if len(self.token_ids) > self.request.max_new_tokens:
-            raise ValueError("partial rollout exceeds its original token budget")
+            problems.append("reference log-probabilities and their policy id go together")
+        if self.reference_token_logprobs is not None and len(self.reference_token_logprobs) != n:
+            problems.append("one reference log-probability per token")
+        if n > self.request.max_new_tokens:
+            problems.append("no more tokens than the request's budget")
         if self.segments < 0:
-            raise ValueError("partial rollout segment count must be non-negative")
+            problems.append("a non-negative segment count")
+        if problems:
+            raise ValueError("inconsistent partial rollout, expected " + "; ".join(problems))
 
     @classmethod
     def from_request(cls, request: GenerationRequest, *, priority: float = 0.0) -> "PartialRollout":
@@ -62,50 +69,56 @@ class PartialRollout:
 
     def next_request(self, chunk_tokens: int) -> GenerationRequest:
         if self.complete or self.remaining_tokens <= 0:
-            raise ValueError("completed rollout cannot be resumed")
-        if chunk_tokens <= 0:
-            raise ValueError("chunk_tokens must be positive")
-        n = min(int(chunk_tokens), self.remaining_tokens)
+            raise ValueError("this rollout is finished; there is nothing to resume")
+        if chunk_tokens < 1:
+            raise ValueError("chunk_tokens has to be positive")
         r = self.request
+        size = min(int(chunk_tokens), self.remaining_tokens)
+        offset = len(self.token_ids)
         seed = r.seed if self.segments == 0 else SeedStream(r.seed).derive("partial-rollout", r.request_id,
                                                                              self.segments)
-        done = len(self.token_ids)
-        return GenerationRequest(r.prefix + self.token_ids, n, r.sampling, seed, f"{r.request_id}:segment:{self.segments}",
-                                 r.uniforms[done:done + n] if r.uniforms is not None else None)
+        uniforms = None if r.uniforms is None else r.uniforms[offset:offset + size]
+        return GenerationRequest(r.prefix + tuple(self.token_ids), size, r.sampling, seed,
+                                 f"{r.request_id}:segment:{self.segments}", uniforms)
+
+    def _segment_problem(self, segment: GenerationRequest, sample: SequenceSample) -> str | None:
+        expected = self.request.prefix + tuple(self.token_ids)
+        rules = (
+            (segment.prefix == expected and sample.prefix == expected, "the segment continues a different prefix"),
+            (sample.request_id == segment.request_id, "the sample answers another request"),
+            (sample.policy_id == self.request.sampling.policy_id, "the segment used another policy"),
+            (len(sample.token_ids) <= segment.max_new_tokens, "the segment exceeded its chunk"),
+            (bool(sample.token_ids) or not self.remaining_tokens, "the segment made no progress"),
+            (self.model_id is None or sample.model_id == self.model_id, "the model changed between segments"),
+            (self.reference_policy_id is None or (sample.reference_policy_id == self.reference_policy_id
+                                                  and sample.reference_token_logprobs is not None),
+             "the reference policy changed or disappeared between segments"),
+            (self.reference_policy_id is not None or not self.segments or sample.reference_policy_id is None,
+             "reference scores appeared after the first segment"),
+        )
+        return next((message for ok, message in rules if not ok), None)
 
     def append(self, segment: GenerationRequest, sample: SequenceSample) -> "PartialRollout":
-        want = self.request.prefix + self.token_ids
-        if segment.prefix != want or sample.prefix != want:
-            raise RuntimeError("partial rollout segment has the wrong prefix")
-        if sample.request_id != segment.request_id:
-            raise RuntimeError("partial rollout segment has the wrong request id")
-        if sample.policy_id != self.request.sampling.policy_id:
-            raise RuntimeError("partial rollout segment used the wrong policy")
-        if len(sample.token_ids) > segment.max_new_tokens:
-            raise RuntimeError("partial rollout segment exceeded its chunk budget")
-        if not sample.token_ids and self.remaining_tokens:
-            raise RuntimeError("partial rollout segment made no progress")
-        if self.model_id is not None and sample.model_id != self.model_id:
-            raise RuntimeError("partial rollout changed model between segments")
-        if self.reference_policy_id is not None:
-            if sample.reference_policy_id != self.reference_policy_id or sample.reference_token_logprobs is None:
-                raise RuntimeError("partial rollout changed or dropped its reference policy between segments")
-        elif self.segments and sample.reference_policy_id is not None:
-            raise RuntimeError("partial rollout added reference scores after the first segment")
-        toks = self.token_ids + sample.token_ids
+        problem = self._segment_problem(segment, sample)
+        if problem is not None:
+            raise RuntimeError(f"rollout {self.request.request_id!r}: {problem}")
+        tokens = tuple(self.token_ids) + tuple(sample.token_ids)
         if sample.reference_token_logprobs is None:
-            refs, ref_id = None, None
+            reference, reference_id = None, None
         else:
-            refs, ref_id = (self.reference_token_logprobs or ()) + sample.reference_token_logprobs, \
-                sample.reference_policy_id
-        finished = sample.finish_reason == "eos" or len(toks) >= self.request.max_new_tokens
-        reason = "eos" if sample.finish_reason == "eos" else ("length" if finished else "partial")
-        return PartialRollout(self.request, toks, self.token_logprobs + sample.token_logprobs, refs, ref_id,
-                              sample.policy_id, sample.model_id, reason, self.segments + 1, self.priority)
+            reference = tuple(self.reference_token_logprobs or ()) + tuple(sample.reference_token_logprobs)
+            reference_id = sample.reference_policy_id
+        if sample.finish_reason == "eos":
+            reason = "eos"
+        else:
+            reason = "length" if len(tokens) >= self.request.max_new_tokens else "partial"
+        return PartialRollout(self.request, tokens, tuple(self.token_logprobs) + tuple(sample.token_logprobs),
+                              reference, reference_id, sample.policy_id, sample.model_id, reason, self.segments + 1,
+                              self.priority)
 
     def to_sample(self) -> SequenceSample:
         if not self.complete:
-            raise ValueError("unfinished rollout cannot be materialized as a sample")
+            raise ValueError("an unfinished rollout is not a sample yet")
         return SequenceSample(self.request.prefix, self.token_ids, self.token_logprobs, self.policy_id, self.model_id,
                               self.request.request_id, self.finish_reason, self.reference_token_logprobs,
                               self.reference_policy_id)
@@ -132,74 +145,91 @@ class RolloutBrokerResult:
     snapshot: RolloutBrokerSnapshot
 
 
+def _urgency(r: PartialRollout) -> tuple:
+    """Heap key: higher priority, started rollouts, longer rollouts first; request id breaks ties."""
+    return (-r.priority, -int(bool(r.token_ids)), -len(r.token_ids), r.request.request_id)
+
+
 class AsyncRolloutBroker:
     def __init__(self, backend: AutoregressiveBackend, *, chunk_tokens: int = 16, max_batch_size: int | None = None):
-        if chunk_tokens <= 0:
-            raise ValueError("chunk_tokens must be positive")
-        if max_batch_size is not None and max_batch_size <= 0:
-            raise ValueError("max_batch_size must be positive")
-        self.backend, self.chunk_tokens, self.max_batch_size = backend, int(chunk_tokens), max_batch_size
+        if chunk_tokens < 1:
+            raise ValueError("chunk_tokens has to be positive")
+        if max_batch_size is not None and max_batch_size < 1:
+            raise ValueError("max_batch_size has to be positive")
+        self.backend = backend
+        self.chunk_tokens = int(chunk_tokens)
+        self.max_batch_size = max_batch_size
+
+    @staticmethod
+    def _target(count: int, completion_target: int | None) -> int:
+        if count == 0:
+            if completion_target not in (None, 0):
+                raise ValueError("no rollouts were submitted, so none can complete")
+            return 0
+        target = count if completion_target is None else int(completion_target)
+        if not 1 <= target <= count:
+            raise ValueError(f"completion_target {target} is outside 1..{count}")
+        return target
+
+    def _segment_batch(self, batch: list[PartialRollout]):
+        """Sample one segment of every rollout; returns (requests, samples, completion order)."""
+        requests = [r.next_request(self.chunk_tokens) for r in batch]
+        arrival: list[int] = []
+        guard = threading.Lock()
+
+        def on_done(index, _sample):
+            with guard:
+                if index not in arrival:
+                    arrival.append(index)
+
+        samples = sample_batch_with_callback(self.backend, requests, on_done)
+        if len(samples) != len(batch):
+            raise RuntimeError(f"{len(samples)} segments came back for {len(batch)} rollouts")
+        arrival.extend(i for i in range(len(batch)) if i not in arrival)
+        return requests, samples, arrival
 
     def run_until(self, rollouts: Sequence[PartialRollout | GenerationRequest], *,
                   completion_target: int | None = None,
                   on_complete: Callable[[SequenceSample], None] | None = None,
                   on_segment: Callable[[PartialRollout], None] | None = None) -> RolloutBrokerResult:
-        states = [x if isinstance(x, PartialRollout) else PartialRollout.from_request(x) for x in rollouts]
-        if not states:
-            if completion_target not in (None, 0):
-                raise ValueError("an empty broker run cannot complete requests")
-            target = 0
-        else:
-            target = len(states) if completion_target is None else int(completion_target)
-            if not 0 < target <= len(states):
-                raise ValueError("completion_target must lie within the submitted rollout count")
+        states = [r if isinstance(r, PartialRollout) else PartialRollout.from_request(r) for r in rollouts]
+        target = self._target(len(states), completion_target)
         ids = [s.request.request_id for s in states]
-        if len(ids) != len(set(ids)):
-            raise ValueError("rollout broker request ids must be unique")
+        if len(set(ids)) != len(ids):
+            raise ValueError("rollout request ids have to be distinct")
         if any(s.complete for s in states):
-            raise ValueError("completed samples should not be resubmitted to the broker")
-        init_partial = sum(len(s.token_ids) for s in states)
-        done: list[SequenceSample] = []
-        pending = list(states)
-        batches = segs = gen = resumed = 0
-        while pending and len(done) < target:
-            pending.sort(key=lambda s: (-s.priority, -int(bool(s.token_ids)), -len(s.token_ids), s.request.request_id))
-            n = self.max_batch_size or len(pending)
-            batch, pending = pending[:n], pending[n:]
-            reqs = [s.next_request(self.chunk_tokens) for s in batch]
-            order: list[int] = []
-            lock = threading.Lock()
-
-            def finished(i, _s, order=order, lock=lock):
-                with lock:
-                    order.append(i)
-
-            got = sample_batch_with_callback(self.backend, reqs, finished)
-            if len(got) != len(batch):
-                raise RuntimeError("rollout backend returned an invalid segment count")
-            order += [i for i in range(len(got)) if i not in order]
+            raise ValueError("finished rollouts cannot be submitted again")
+        initial_tokens = sum(len(s.token_ids) for s in states)
+        queue = [(_urgency(s), i, s) for i, s in enumerate(states)]
+        heapq.heapify(queue)
+        tiebreak = len(queue)
+        finished: list[SequenceSample] = []
+        batches = segments = generated = resumed = 0
+        while queue and len(finished) < target:
+            width = self.max_batch_size or len(queue)
+            batch = [heapq.heappop(queue)[2] for _ in range(min(width, len(queue)))]
+            requests, samples, arrival = self._segment_batch(batch)
             batches += 1
-            segs += len(got)
-            gen += sum(len(s.token_ids) for s in got)
-            resumed += sum(len(s.token_ids) for s in batch)
-            seen = set()
-            for i in order:
-                if i in seen:
-                    continue
-                seen.add(i)
-                st = batch[i].append(reqs[i], got[i])
+            segments += len(samples)
+            generated += sum(len(s.token_ids) for s in samples)
+            resumed += sum(len(r.token_ids) for r in batch)
+            for i in arrival:
+                advanced = batch[i].append(requests[i], samples[i])
                 if on_segment is not None:
-                    on_segment(st)
-                if st.complete:
-                    smp = st.to_sample()
-                    done.append(smp)
+                    on_segment(advanced)
+                if advanced.complete:
+                    sample = advanced.to_sample()
+                    finished.append(sample)
                     if on_complete is not None:
-                        on_complete(smp)
+                        on_complete(sample)
                 else:
-                    pending.append(st)
-        snap = RolloutBrokerSnapshot(target, len(done), len(pending), max(0, len(done) - target), batches, segs, gen,
-                                     init_partial, sum(len(s.token_ids) for s in pending), resumed)
-        return RolloutBrokerResult(tuple(done), tuple(pending), snap)
+                    heapq.heappush(queue, (_urgency(advanced), tiebreak, advanced))
+                    tiebreak += 1
+        left = [entry[2] for entry in sorted(queue)]
+        snapshot = RolloutBrokerSnapshot(target, len(finished), len(left), max(0, len(finished) - target), batches,
+                                         segments, generated, initial_tokens, sum(len(s.token_ids) for s in left),
+                                         resumed)
+        return RolloutBrokerResult(tuple(finished), tuple(left), snapshot)
 
 
 __all__ = ["AsyncRolloutBroker", "PartialRollout", "RolloutBrokerResult", "RolloutBrokerSnapshot"]
