@@ -1,19 +1,22 @@
-"""Whole-continuation independence MH for dLLM reward targets p(trace) exp(r / tau).
+"""Independence MH over whole dLLM continuations for reward targets p(trace) exp(r / tau).
 
-Reference behaviour: src/inference_scaling/dllm/algorithms/mh.py:99-168.  With
-proposals drawn from the base sampler the base trajectory density cancels, so
-the acceptance min(1, exp((r' - r) / tau)) needs rewards only.  All
-``updates + 1`` draws are independent of the chain state and are sampled in
-batches (``proposal_batch_size``) before the sequential accept / reject pass.
+Proposals come from the base sampler, so the base trajectory density cancels and
+the acceptance min(1, exp((r' - r) / tau)) needs rewards only.  Every one of the
+``updates + 1`` draws is independent of the chain, so all of them are generated
+first (in batches of ``proposal_batch_size``) and scored in one pass; the chain
+then only walks the precomputed rewards with precomputed uniforms.  Stream names
+(``("dllm-mh", d)`` draws, ``("dllm-mh", "accept", u)`` uniforms) and request ids
+follow src/inference_scaling/dllm/algorithms/mh.py.
 """
 
 from __future__ import annotations
 
 from collections.abc import Sequence
 from dataclasses import dataclass
-from math import isfinite
 
-from ...shared.mh import decide_metropolis_hastings
+import numpy as np
+
+from ...shared.mh import mh_accept_batch, mh_log_acceptance_batch
 from ...shared.rng import SeedStream
 from ...shared.types import TokenSequence
 from ..config import DiffusionMHConfig, DiffusionSamplingConfig
@@ -22,32 +25,34 @@ from ..types import DiffusionBackend, DiffusionGenerationRequest, DiffusionSampl
 
 def mh_requests(prompt: TokenSequence, config: DiffusionMHConfig, sampling: DiffusionSamplingConfig,
                 seeds: SeedStream) -> list[DiffusionGenerationRequest]:
-    return [DiffusionGenerationRequest(prompt, config.total_length, sampling, seeds.derive("dllm-mh", d),
-                                       f"dllm-mh:draw:{d}") for d in range(config.updates + 1)]
+    return [DiffusionGenerationRequest(prompt, config.total_length, sampling, seeds.derive("dllm-mh", draw),
+                                       f"dllm-mh:draw:{draw}") for draw in range(config.updates + 1)]
 
 
 def sample_in_batches(backend: DiffusionBackend, requests: Sequence[DiffusionGenerationRequest],
                       batch_size: int | None) -> list[DiffusionSample]:
-    if batch_size is not None and batch_size <= 0:
-        raise ValueError("proposal_batch_size must be positive when provided")
-    n = batch_size or len(requests)
-    out: list[DiffusionSample] = []
-    for i in range(0, len(requests), n):
-        out.extend(backend.sample_batch(requests[i:i + n]))
-    if len(out) != len(requests):
-        raise RuntimeError("backend returned an invalid number of MH proposals")
-    return out
+    if batch_size is not None and batch_size < 1:
+        raise ValueError("proposal_batch_size has to be positive")
+    width = batch_size or max(1, len(requests))
+    samples: list[DiffusionSample] = []
+    for start in range(0, len(requests), width):
+        samples.extend(backend.sample_batch(list(requests[start:start + width])))
+    if len(samples) != len(requests):
+        raise RuntimeError(f"{len(samples)} proposals came back for {len(requests)} requests")
+    return samples
 
 
 def mh_rewards(prompt, samples, reward, reward_batch) -> list[float]:
-    conts = [s.token_ids for s in samples]
-    vals = ([float(v) for v in reward_batch(prompt, conts)] if reward_batch is not None
-            else [float(reward(prompt, c)) for c in conts])
-    if len(vals) != len(samples):
-        raise RuntimeError("reward evaluator returned an invalid number of values")
-    if not all(isfinite(v) for v in vals):
-        raise ValueError("reward values must be finite")
-    return vals
+    continuations = [s.token_ids for s in samples]
+    if reward_batch is not None:
+        values = np.asarray(list(reward_batch(prompt, continuations)), dtype=np.float64)
+    else:
+        values = np.asarray([reward(prompt, c) for c in continuations], dtype=np.float64)
+    if values.shape != (len(samples),):
+        raise RuntimeError(f"{values.size} rewards for {len(samples)} proposals")
+    if not np.isfinite(values).all():
+        raise ValueError("rewards have to be finite")
+    return values.tolist()
 
 
 @dataclass(frozen=True, slots=True)
@@ -78,22 +83,23 @@ def run_diffusion_reward_mh(*, backend: DiffusionBackend, prompt: TokenSequence,
                             sampling: DiffusionSamplingConfig, reward=None, seed: int = 0, reward_batch=None,
                             proposal_batch_size: int | None = None) -> DiffusionMHResult:
     if (reward is None) == (reward_batch is None):
-        raise ValueError("provide exactly one of reward or reward_batch")
+        raise ValueError("give either reward or reward_batch")
     sampling.validate_generation_length(config.total_length, prefix_length=len(prompt))
     seeds = SeedStream(seed)
-    samples = sample_in_batches(backend, mh_requests(prompt, config, sampling, seeds), proposal_batch_size)
-    rewards = mh_rewards(prompt, samples, reward, reward_batch)
-    cur, cur_r = samples[0], rewards[0]
+    draws = sample_in_batches(backend, mh_requests(prompt, config, sampling, seeds), proposal_batch_size)
+    rewards = np.asarray(mh_rewards(prompt, draws, reward, reward_batch))
+    uniforms = np.asarray([seeds.generator("dllm-mh", "accept", u).random() for u in range(1, len(draws))])
+    tau = config.reward_temperature
+    state = 0
     steps = []
-    for u, (prop, pr) in enumerate(zip(samples[1:], rewards[1:]), start=1):
-        d = decide_metropolis_hastings(current_target_log_density=cur_r / config.reward_temperature,
-                                       proposed_target_log_density=pr / config.reward_temperature,
-                                       uniform=float(seeds.generator("dllm-mh", "accept", u).random()))
-        prev = cur_r
-        if d.accepted:
-            cur, cur_r = prop, pr
-        steps.append(DiffusionMHStep(u, prop, pr, prev, d.acceptance_probability, d.accepted))
-    return DiffusionMHResult(prompt, samples[0], rewards[0], tuple(steps), cur, cur_r)
+    for u in range(1, len(draws)):
+        log_a = mh_log_acceptance_batch(rewards[state] / tau, rewards[u] / tau)
+        accepted = bool(mh_accept_batch(log_a, uniforms[u - 1]))
+        steps.append(DiffusionMHStep(u, draws[u], float(rewards[u]), float(rewards[state]), float(np.exp(log_a)),
+                                     accepted))
+        if accepted:
+            state = u
+    return DiffusionMHResult(prompt, draws[0], float(rewards[0]), tuple(steps), draws[state], float(rewards[state]))
 
 
 __all__ = ["DiffusionMHResult", "DiffusionMHStep", "mh_requests", "mh_rewards", "run_diffusion_reward_mh",

@@ -1,11 +1,12 @@
 """Exact trajectory replay for block-diffusion rollout weights.
 
-Reference behaviour: src/inference_scaling/dllm/replay.py:108-385.  History
-rollouts are drawn once from a behaviour policy and scored under the target
-policy; a candidate's weight combines truncated-IS history terms
-min(c, p/q) exp(r / tau) with fresh target rollouts whose tail correction
-(1 - c q/p)+ keeps the estimator unbiased (shared.importance).  Exact
-trajectory densities make p/q the ratio of the same reverse trace.
+History rollouts are drawn once from a behaviour policy and scored under the target
+policy.  A candidate's weight combines truncated-IS history terms
+min(c, p / q) exp(r / tau) with fresh target rollouts, whose tail correction
+(1 - c q / p)+ keeps the estimate unbiased; with exact trajectory densities p / q is
+the ratio of the same reverse trace under the two policies.  Rollouts of all
+candidates are laid out as one (candidate x rollout) grid per call.  Stream names and
+request ids follow src/inference_scaling/dllm/replay.py (frozen histories replay).
 """
 
 from __future__ import annotations
@@ -28,15 +29,12 @@ from .types import DiffusionBackend, DiffusionGenerationRequest, DiffusionSample
 DiffusionReplayRewardBatch = Callable[[TokenSequence, Sequence[TokenSequence]], Sequence[float]]
 
 
-def _schedule(s: DiffusionSamplingConfig):
-    return s.block_length, s.steps_per_block, s.remasking, s.mask_token_id
-
-
 def validate_exact_pair(target: DiffusionSamplingConfig, behavior: DiffusionSamplingConfig) -> None:
     if not (target.has_exact_trajectory_density and behavior.has_exact_trajectory_density):
-        raise ValueError("replay correction requires exact target and behavior trajectories")
-    if _schedule(target) != _schedule(behavior):
-        raise ValueError("target and replay behavior trajectory schedules must match")
+        raise ValueError("replay weights need exact trajectory densities under both policies")
+    schedule = ("block_length", "steps_per_block", "remasking", "mask_token_id")
+    if any(getattr(target, f) != getattr(behavior, f) for f in schedule):
+        raise ValueError("target and behaviour trajectories must follow the same schedule")
 
 
 @dataclass(frozen=True, slots=True)
@@ -87,11 +85,16 @@ class DiffusionReplaySelection:
         return self.candidates[self.selected_index]
 
 
-def _rewards(reward_batch, prompt, conts, what: str) -> list[float]:
-    vals = [float(v) for v in reward_batch(prompt, conts)]
-    if len(vals) != len(conts):
-        raise RuntimeError(f"reward evaluator returned an invalid {what} count")
-    return vals
+def _rewards(reward_batch, prompt, texts, what: str) -> list[float]:
+    values = [float(v) for v in reward_batch(prompt, texts)]
+    if len(values) != len(texts):
+        raise RuntimeError(f"{len(values)} {what} rewards for {len(texts)} rollouts")
+    return values
+
+
+def _grid(counts: Sequence[int]) -> list[tuple[int, int]]:
+    """(candidate, index) cells of a ragged candidate x rollout grid, row by row."""
+    return [(c, i) for c, n in enumerate(counts) for i in range(n)]
 
 
 def build_diffusion_replay_history(*, target_backend: DiffusionBackend, behavior_backend: DiffusionBackend,
@@ -101,34 +104,40 @@ def build_diffusion_replay_history(*, target_backend: DiffusionBackend, behavior
                                    behavior_sampling: DiffusionSamplingConfig,
                                    reward_batch: DiffusionReplayRewardBatch, seed: int
                                    ) -> tuple[DiffusionReplayHistory, ...]:
-    """Draw immutable behaviour trajectories per candidate and precompute their target scores."""
+    """Draw immutable behaviour trajectories per candidate and score them under the target once."""
     validate_exact_pair(target_sampling, behavior_sampling)
-    if count_per_candidate <= 0:
-        raise ValueError("count_per_candidate must be positive")
-    prefixes = [prompt + generated_prefix + c.token_ids for c in candidates]
+    if count_per_candidate < 1:
+        raise ValueError("count_per_candidate has to be positive")
+    prefixes = [tuple(prompt) + tuple(generated_prefix) + tuple(c.token_ids) for c in candidates]
     if rollout_length <= 0:
         return tuple(DiffusionReplayHistory(p, ()) for p in prefixes)
     seeds = SeedStream(seed)
-    reqs, owners = [], []
-    for ci, p in enumerate(prefixes):
-        for hi in range(count_per_candidate):
-            reqs.append(DiffusionGenerationRequest(p, rollout_length, behavior_sampling,
-                                                   seeds.derive("dllm-replay", ci, hi), f"dllm-replay:{ci}:{hi}"))
-            owners.append(ci)
-    samples = behavior_backend.sample_batch(reqs)
-    if len(samples) != len(reqs):
-        raise RuntimeError("behavior backend returned an invalid replay sample count")
-    scores = target_backend.score_trajectories([DiffusionTrajectoryScoreRequest(s, target_sampling) for s in samples])
-    if len(scores) != len(samples):
-        raise RuntimeError("target backend returned an invalid replay score count")
-    rewards = _rewards(reward_batch, prompt, [generated_prefix + candidates[o].token_ids + s.token_ids
-                                              for o, s in zip(owners, samples)], "replay")
-    grouped: list[list[DiffusionReplayRecord]] = [[] for _ in candidates]
-    for o, s, t, r in zip(owners, samples, scores, rewards):
-        if s.trajectory_logprob is None:
-            raise RuntimeError("behavior backend omitted replay trajectory probability")
-        grouped[o].append(DiffusionReplayRecord(s.prefix, s, float(t), float(s.trajectory_logprob), r))
-    return tuple(DiffusionReplayHistory(p, tuple(g)) for p, g in zip(prefixes, grouped))
+    cells = _grid([count_per_candidate] * len(candidates))
+    requests = [DiffusionGenerationRequest(prefixes[c], rollout_length, behavior_sampling,
+                                           seeds.derive("dllm-replay", c, h), f"dllm-replay:{c}:{h}") for c, h in cells]
+    drawn = behavior_backend.sample_batch(requests)
+    if len(drawn) != len(requests):
+        raise RuntimeError(f"{len(drawn)} behaviour rollouts for {len(requests)} requests")
+    if any(s.trajectory_logprob is None for s in drawn):
+        raise RuntimeError("a behaviour rollout came without its trajectory probability")
+    target = target_backend.score_trajectories([DiffusionTrajectoryScoreRequest(s, target_sampling) for s in drawn])
+    if len(target) != len(drawn):
+        raise RuntimeError(f"{len(target)} target scores for {len(drawn)} rollouts")
+    texts = [tuple(generated_prefix) + tuple(candidates[c].token_ids) + tuple(s.token_ids)
+             for (c, _), s in zip(cells, drawn)]
+    rewards = _rewards(reward_batch, prompt, texts, "replay")
+    rows: list[list[DiffusionReplayRecord]] = [[] for _ in candidates]
+    for (c, _), s, t, r in zip(cells, drawn, target, rewards):
+        rows[c].append(DiffusionReplayRecord(s.prefix, s, float(t), float(s.trajectory_logprob), r))
+    return tuple(DiffusionReplayHistory(p, tuple(row)) for p, row in zip(prefixes, rows))
+
+
+def _terminal_selection(candidates, outer, rewards, tau, seed) -> DiffusionReplaySelection:
+    chosen = tuple(DiffusionReplayCandidate(c, ReplayWeightEstimate(r / tau, (), (r / tau,)), o)
+                   for c, r, o in zip(candidates, rewards, outer))
+    probabilities = normalize_log_weights([c.estimate.log_weight + c.outer_log_ratio for c in chosen])
+    pick = int(np.random.default_rng(seed).choice(len(chosen), p=probabilities))
+    return DiffusionReplaySelection(chosen, probabilities, pick, tuple(() for _ in candidates))
 
 
 def select_diffusion_candidates_with_replay(*, target_backend: DiffusionBackend,
@@ -142,75 +151,67 @@ def select_diffusion_candidates_with_replay(*, target_backend: DiffusionBackend,
                                             truncation: float, seed: int,
                                             candidate_log_ratios: Sequence[float] | None = None
                                             ) -> DiffusionReplaySelection:
-    """Weight every candidate from fresh rollouts, or corrected replay plus a fresh tail, then draw one."""
-    if not candidates:
-        raise ValueError("at least one candidate is required")
+    """Weight each candidate from fresh rollouts, or corrected replay plus a fresh tail, then draw one."""
     n = len(candidates)
-    fresh = (fresh_count,) * n if isinstance(fresh_count, int) else tuple(int(v) for v in fresh_count)
-    if len(fresh) != n or any(v <= 0 for v in fresh):
-        raise ValueError("fresh_count must be positive for every candidate")
-    if reward_temperature <= 0 or truncation <= 0:
-        raise ValueError("reward_temperature and truncation must be positive")
-    outer = tuple(candidate_log_ratios or (0.0,) * n)
+    if n == 0:
+        raise ValueError("selection needs at least one candidate")
+    fresh = [fresh_count] * n if isinstance(fresh_count, int) else [int(v) for v in fresh_count]
+    if len(fresh) != n or min(fresh) < 1:
+        raise ValueError("every candidate needs a positive fresh rollout count")
+    if not (reward_temperature > 0 and truncation > 0):
+        raise ValueError("reward_temperature and truncation have to be positive")
+    outer = tuple(candidate_log_ratios) if candidate_log_ratios is not None else (0.0,) * n
     if len(outer) != n or not all(isfinite(v) for v in outer):
-        raise ValueError("candidate log-ratios must be finite and match the candidates")
-    prefixes = [prompt + generated_prefix + c.token_ids for c in candidates]
-    histories = histories or tuple(DiffusionReplayHistory(p, ()) for p in prefixes)
-    if len(histories) != n:
-        raise ValueError("one replay history is required per candidate")
-    replay = any(h.records for h in histories)
-    if replay:
+        raise ValueError("candidate log-ratios must be finite, one per candidate")
+    prefixes = [tuple(prompt) + tuple(generated_prefix) + tuple(c.token_ids) for c in candidates]
+    histories = tuple(histories) if histories else tuple(DiffusionReplayHistory(p, ()) for p in prefixes)
+    if len(histories) != n or any(h.rollout_prefix != p for h, p in zip(histories, prefixes)):
+        raise ValueError("histories must match the candidates one to one")
+    replaying = any(h.records for h in histories)
+    if replaying:
         if behavior_backend is None or behavior_sampling is None:
-            raise ValueError("replay records require their behavior backend and policy")
+            raise ValueError("replayed records need their behaviour backend and policy")
         validate_exact_pair(target_sampling, behavior_sampling)
     tau = reward_temperature
     if rollout_length == 0:
-        rewards = _rewards(reward_batch, prompt, [generated_prefix + c.token_ids for c in candidates], "terminal")
-        cands = tuple(DiffusionReplayCandidate(c, ReplayWeightEstimate(r / tau, (), (r / tau,)), o)
-                      for c, r, o in zip(candidates, rewards, outer))
-        probs = normalize_log_weights([c.estimate.log_weight + c.outer_log_ratio for c in cands])
-        return DiffusionReplaySelection(cands, probs, int(np.random.default_rng(seed).choice(n, p=probs)),
-                                        tuple(() for _ in candidates))
+        rewards = _rewards(reward_batch, prompt,
+                           [tuple(generated_prefix) + tuple(c.token_ids) for c in candidates], "terminal")
+        return _terminal_selection(candidates, outer, rewards, tau, seed)
     seeds = SeedStream(seed)
-    reqs, owners = [], []
-    for ci, p in enumerate(prefixes):
-        if histories[ci].rollout_prefix != p:
-            raise ValueError("replay history does not belong to its candidate")
-        for fi in range(fresh[ci]):
-            reqs.append(DiffusionGenerationRequest(p, rollout_length, target_sampling,
-                                                   seeds.derive("dllm-replay-fresh", ci, fi),
-                                                   f"dllm-replay-fresh:{ci}:{fi}"))
-            owners.append(ci)
-    samples = target_backend.sample_batch(reqs)
-    if len(samples) != len(reqs):
-        raise RuntimeError("target backend returned an invalid fresh rollout count")
-    if replay:
-        beh = [float(v) for v in behavior_backend.score_trajectories(
-            [DiffusionTrajectoryScoreRequest(s, behavior_sampling) for s in samples])]
-        if len(beh) != len(samples):
-            raise RuntimeError("behavior backend returned an invalid fresh score count")
-    else:
-        beh = [None] * len(samples)
-    rewards = _rewards(reward_batch, prompt, [generated_prefix + candidates[o].token_ids + s.token_ids
-                                              for o, s in zip(owners, samples)], "fresh rollout")
-    grouped: list[list[DiffusionReplayRecord]] = [[] for _ in candidates]
-    for o, s, b, r in zip(owners, samples, beh, rewards):
-        if s.trajectory_logprob is None:
-            raise RuntimeError("target backend omitted fresh trajectory probability")
-        grouped[o].append(DiffusionReplayRecord(s.prefix, s, float(s.trajectory_logprob),
-                                                float(b) if b is not None else float(s.trajectory_logprob), r))
+    cells = _grid(fresh)
+    requests = [DiffusionGenerationRequest(prefixes[c], rollout_length, target_sampling,
+                                           seeds.derive("dllm-replay-fresh", c, f), f"dllm-replay-fresh:{c}:{f}")
+                for c, f in cells]
+    drawn = target_backend.sample_batch(requests)
+    if len(drawn) != len(requests):
+        raise RuntimeError(f"{len(drawn)} fresh rollouts for {len(requests)} requests")
+    if any(s.trajectory_logprob is None for s in drawn):
+        raise RuntimeError("a fresh rollout came without its trajectory probability")
+    own = np.asarray([float(s.trajectory_logprob) for s in drawn])
+    behaviour = own
+    if replaying:
+        behaviour = np.asarray([float(v) for v in behavior_backend.score_trajectories(
+            [DiffusionTrajectoryScoreRequest(s, behavior_sampling) for s in drawn])])
+        if behaviour.size != len(drawn):
+            raise RuntimeError(f"{behaviour.size} behaviour scores for {len(drawn)} fresh rollouts")
+    texts = [tuple(generated_prefix) + tuple(candidates[c].token_ids) + tuple(s.token_ids)
+             for (c, _), s in zip(cells, drawn)]
+    rewards = _rewards(reward_batch, prompt, texts, "fresh")
+    rows: list[list[DiffusionReplayRecord]] = [[] for _ in candidates]
+    for i, ((c, _), s, r) in enumerate(zip(cells, drawn, rewards)):
+        rows[c].append(DiffusionReplayRecord(s.prefix, s, float(own[i]), float(behaviour[i]), r))
     provider = TruncatedReplayRolloutWeightProvider(truncation=truncation, reward_temperature=tau)
-    cands = []
-    for c, h, f, o in zip(candidates, histories, grouped, outer):
-        if h.records:
-            est = provider.estimate([r.observation for r in h.records], [r.observation for r in f])
+    weighted = []
+    for cand, history, row, ratio in zip(candidates, histories, rows, outer):
+        if history.records:
+            estimate = provider.estimate([r.observation for r in history.records], [r.observation for r in row])
         else:
-            terms = tuple(r.reward / tau for r in f)
-            est = ReplayWeightEstimate(logmeanexp(terms), (), terms)
-        cands.append(DiffusionReplayCandidate(c, est, o))
-    probs = normalize_log_weights([c.estimate.log_weight + c.outer_log_ratio for c in cands])
-    sel = int(seeds.generator("dllm-replay-select").choice(n, p=probs))
-    return DiffusionReplaySelection(tuple(cands), probs, sel, tuple(tuple(g) for g in grouped))
+            terms = tuple(r.reward / tau for r in row)
+            estimate = ReplayWeightEstimate(logmeanexp(terms), (), terms)
+        weighted.append(DiffusionReplayCandidate(cand, estimate, ratio))
+    probabilities = normalize_log_weights([c.estimate.log_weight + c.outer_log_ratio for c in weighted])
+    pick = int(seeds.generator("dllm-replay-select").choice(n, p=probabilities))
+    return DiffusionReplaySelection(tuple(weighted), probabilities, pick, tuple(tuple(row) for row in rows))
 
 
 __all__ = ["DiffusionReplayCandidate", "DiffusionReplayHistory", "DiffusionReplayRecord",

@@ -1,15 +1,13 @@
-"""Finite-pool iterated SIR for conditional autoregressive generation.
+"""Iterated SIR over conditional-IS blocks with a finite pool.
 
-The extended state of one block is a base candidate together with every
-rollout used to estimate its conditional weight.  All 1 + U (N - 1) fresh
-states of a block are sampled and weighted in ONE batched backend call; then U
-i-SIR transitions run over them, each keeping the current state (with its
-original rollout estimate, not a re-estimate) in slot 0 of a pool of N.  The
-reward must be a fixed pointwise function of the completed sequence: a
-batch-normalised or history-dependent reward changes the target during the
-chain and breaks the invariance argument.
-
-Reference behaviour: src/inference_scaling/experimental/arllm/iterated_is.py:32-226.
+The extended state of a block is a base candidate together with every rollout its
+conditional weight was estimated from.  All 1 + U (N - 1) states a block can use
+are drawn and weighted up front in one batched backend call; the U i-SIR
+transitions then only reshuffle those evaluated states: each pool is the current
+state (with its original estimate, never re-estimated) plus the next N - 1 fresh
+ones.  The reward has to be a fixed pointwise function of the completed sequence;
+a batch-normalised or history-dependent reward would change the target during the
+chain.  Stream names follow src/inference_scaling/experimental/arllm/iterated_is.py.
 """
 
 from __future__ import annotations
@@ -70,6 +68,15 @@ class IteratedConditionalISResult:
         return sum(len(s.transitions) for s in self.steps)
 
 
+def _pools(evaluated, updates: int, fresh_per_pool: int):
+    """The fresh states of every transition, in draw order after the initial state."""
+    need = 1 + updates * fresh_per_pool
+    if len(evaluated) != need:
+        raise RuntimeError(f"{len(evaluated)} evaluated states for {updates} pools of {fresh_per_pool} fresh ones")
+    rest = evaluated[1:]
+    return [rest[u * fresh_per_pool:(u + 1) * fresh_per_pool] for u in range(updates)]
+
+
 def iterated_conditional_is_step(*, base_backend: AutoregressiveBackend, rollout_backend: AutoregressiveBackend,
                                  prompt: TokenSequence, generated_prefix: TokenSequence,
                                  config: IteratedConditionalISConfig, base_sampling: SamplingConfig,
@@ -78,30 +85,26 @@ def iterated_conditional_is_step(*, base_backend: AutoregressiveBackend, rollout
                                  ) -> IteratedConditionalISStep:
     _check_policies(base_sampling, rollout_sampling)
     prompt, generated_prefix = tuple(prompt), tuple(generated_prefix)
-    left = config.total_length - len(generated_prefix)
-    if left <= 0:
-        raise ValueError("generated prefix has already reached total_length")
-    block = min(config.block_size, left)
-    cands = sample_candidates(base_backend, prompt + generated_prefix, config.fresh_candidate_evaluations, block,
+    remaining = config.total_length - len(generated_prefix)
+    if remaining <= 0:
+        raise ValueError("the generated prefix already has total_length tokens")
+    block = min(config.block_size, remaining)
+    drawn = sample_candidates(base_backend, prompt + generated_prefix, config.fresh_candidate_evaluations, block,
                               base_sampling, seeds, step_index)
     evaluated = estimate_conditional_weights(
         base_backend=base_backend, rollout_backend=rollout_backend, prompt=prompt, generated_prefix=generated_prefix,
-        candidates=cands, rollout_length=max(0, left - block), rollout_count=config.rollout_count,
+        candidates=drawn, rollout_length=max(0, remaining - block), rollout_count=config.rollout_count,
         base_sampling=base_sampling, rollout_sampling=rollout_sampling, reward_temperature=config.reward_temperature,
         importance_log_ratio_clip=config.importance_log_ratio_clip,
         apply_importance_correction=config.apply_importance_correction, reward=reward, seeds=seeds,
         step_index=step_index, reward_batch=reward_batch)
-    current = StepwiseCandidate(evaluated[0], evaluated[0].log_weight)
-    fresh_per = config.pool_size - 1
+    state = StepwiseCandidate(evaluated[0], evaluated[0].log_weight)
     transitions = []
-    for u in range(config.updates):
-        group = evaluated[1 + u * fresh_per: 1 + (u + 1) * fresh_per]
-        if len(group) != fresh_per:
-            raise RuntimeError("candidate grouping does not match the i-SIR configuration")
-        t = iterated_sir_transition(current, [StepwiseCandidate(c, c.log_weight) for c in group],
-                                    rng=seeds.generator("iterated_conditional_is", step_index, u, "select"))
-        transitions.append(t)
-        current = t.selected
+    for u, fresh in enumerate(_pools(evaluated, config.updates, config.pool_size - 1)):
+        move = iterated_sir_transition(state, [StepwiseCandidate(c, c.log_weight) for c in fresh],
+                                       rng=seeds.generator("iterated_conditional_is", step_index, u, "select"))
+        transitions.append(move)
+        state = move.selected
     return IteratedConditionalISStep(len(generated_prefix), evaluated, tuple(transitions))
 
 
@@ -111,24 +114,29 @@ def run_iterated_conditional_is(base_backend: AutoregressiveBackend, prompt: Tok
                                 rollout_backend: AutoregressiveBackend | None = None,
                                 rollout_sampling: SamplingConfig | None = None,
                                 reward_batch: TokenBatchReward | None = None) -> IteratedConditionalISResult:
-    base_sampling = base_sampling or SamplingConfig()
-    rollout_sampling = rollout_sampling or base_sampling
-    rollout_backend = rollout_backend or base_backend
+    base_sampling = base_sampling if base_sampling is not None else SamplingConfig()
+    rollout_sampling = rollout_sampling if rollout_sampling is not None else base_sampling
+    rollout_backend = rollout_backend if rollout_backend is not None else base_backend
     _check_policies(base_sampling, rollout_sampling)
     prompt = tuple(prompt)
     eos = base_sampling.eos_token_id
-    gen: TokenSequence = ()
-    steps = []
-    while len(gen) < config.total_length and (eos is None or eos not in gen):
-        st = iterated_conditional_is_step(base_backend=base_backend, rollout_backend=rollout_backend, prompt=prompt,
-                                          generated_prefix=gen, config=config, base_sampling=base_sampling,
-                                          rollout_sampling=rollout_sampling, reward=reward, seeds=seeds,
-                                          step_index=len(steps), reward_batch=reward_batch)
-        gen += st.selected.token_ids
-        if eos is not None and eos in gen:
-            gen = gen[:gen.index(eos) + 1]
-        steps.append(st)
-    return IteratedConditionalISResult(prompt, gen, tuple(steps))
+    text: tuple = ()
+    steps: list[IteratedConditionalISStep] = []
+
+    def finished() -> bool:
+        return len(text) >= config.total_length or (eos is not None and eos in text)
+
+    while not finished():
+        step = iterated_conditional_is_step(base_backend=base_backend, rollout_backend=rollout_backend,
+                                            prompt=prompt, generated_prefix=text, config=config,
+                                            base_sampling=base_sampling, rollout_sampling=rollout_sampling,
+                                            reward=reward, seeds=seeds, step_index=len(steps),
+                                            reward_batch=reward_batch)
+        steps.append(step)
+        text += tuple(step.selected.token_ids)
+        if eos is not None and eos in text:
+            text = text[:text.index(eos) + 1]
+    return IteratedConditionalISResult(prompt, text, tuple(steps))
 
 
 __all__ = ["IteratedConditionalISResult", "IteratedConditionalISStep", "iterated_conditional_is_step",

@@ -1,23 +1,21 @@
-"""Iterated sampling-importance-resampling (i-SIR) transition.
+"""Iterated sampling-importance-resampling (i-SIR).
 
-One transition keeps the current weighted state in pool slot 0, adds fresh
-states drawn independently from the same extended proposal, and resamples one
-slot in proportion to the weights.  Retaining the full current state (with all
-auxiliary variables behind its weight) makes the kernel invariant for the
-target, for any pool size.
+One transition puts the current weighted state in slot 0 of a pool, fills the other
+slots with fresh states drawn independently from the same extended proposal, and
+keeps one slot chosen in proportion to the weights.  Because the current state is
+kept with everything its weight was computed from, the kernel leaves the target
+invariant for any pool size.
 
-``iterated_sir_tv_bound``: with L = sup w / E_q[w] and pool size N the kernel
-satisfies a minorisation with constant eps = (N - 1) / (2 L + N - 2), so the
-total variation after k updates is at most (1 - eps)^k.
-
-Reference behaviour: src/inference_scaling/experimental/shared/iterated_sir.py:17-103.
+Mixing: with L = sup w / E_q[w] and pool size N the kernel is minorised with
+constant eps = (N - 1) / (2 L + N - 2), so after k transitions the total variation
+to the target is at most (1 - eps)^k.  Public names follow
+src/inference_scaling/experimental/shared/iterated_sir.py.
 """
 
 from __future__ import annotations
 
 from collections.abc import Sequence
 from dataclasses import dataclass
-from math import isfinite
 from typing import Generic, TypeVar
 
 import numpy as np
@@ -35,14 +33,13 @@ class IteratedSIRTransition(Generic[StateT]):
     selected_index: int
 
     def __post_init__(self) -> None:
-        if len(self.pool) < 2:
-            raise ValueError("an i-SIR pool requires at least two states")
+        n = len(self.pool)
+        if n < 2:
+            raise ValueError("an i-SIR pool holds the current state and at least one fresh state")
         if self.pool[0] is not self.previous:
-            raise ValueError("pool slot zero must hold the previous state")
-        if len(self.probabilities) != len(self.pool):
-            raise ValueError("each pool state needs one probability")
-        if not 0 <= self.selected_index < len(self.pool):
-            raise ValueError("selected_index lies outside the pool")
+            raise ValueError("slot 0 of the pool is the current state")
+        if len(self.probabilities) != n or not 0 <= self.selected_index < n:
+            raise ValueError("probabilities and the selected index must match the pool")
 
     @property
     def selected(self) -> StepwiseCandidate[StateT]:
@@ -55,24 +52,24 @@ class IteratedSIRTransition(Generic[StateT]):
 
 def iterated_sir_transition(current: StepwiseCandidate[StateT], fresh: Sequence[StepwiseCandidate[StateT]], *,
                             rng: np.random.Generator) -> IteratedSIRTransition[StateT]:
-    fresh = tuple(fresh)
-    if not fresh:
-        raise ValueError("an i-SIR transition requires at least one fresh state")
-    pool = (current,) + fresh
-    probs = normalize_log_weights([c.log_weight for c in pool])
-    return IteratedSIRTransition(current, pool, probs, int(rng.choice(len(pool), p=probs)))
+    pool = (current, *fresh)
+    if len(pool) < 2:
+        raise ValueError("an i-SIR transition needs at least one fresh state")
+    probabilities = normalize_log_weights([state.log_weight for state in pool])
+    choice = int(rng.choice(len(pool), p=probabilities))
+    return IteratedSIRTransition(current, pool, probabilities, choice)
 
 
 def iterated_sir_tv_bound(*, pool_size: int, updates: int, normalized_weight_supremum: float) -> float:
-    if isinstance(pool_size, bool) or pool_size < 2:
-        raise ValueError("pool_size must be an integer of at least two")
-    if isinstance(updates, bool) or updates < 0:
-        raise ValueError("updates must be a non-negative integer")
-    L = float(normalized_weight_supremum)
-    if not isfinite(L) or L < 1:
-        raise ValueError("normalized_weight_supremum must be finite and at least one")
-    eps = (pool_size - 1) / (2.0 * L + pool_size - 2)
-    return float((1.0 - eps) ** updates)
+    if isinstance(pool_size, bool) or not isinstance(pool_size, (int, np.integer)) or pool_size < 2:
+        raise ValueError("pool_size is an integer of at least 2")
+    if isinstance(updates, bool) or not isinstance(updates, (int, np.integer)) or updates < 0:
+        raise ValueError("updates is a non-negative integer")
+    sup = float(normalized_weight_supremum)
+    if not np.isfinite(sup) or sup < 1.0:
+        raise ValueError("the normalised weight supremum is finite and at least 1")
+    eps = (pool_size - 1) / (2.0 * sup + pool_size - 2)
+    return float(np.power(1.0 - eps, updates))
 
 
 __all__ = ["IteratedSIRTransition", "iterated_sir_transition", "iterated_sir_tv_bound"]

@@ -1,22 +1,26 @@
-"""Estimators used by experiment reports (model independent).
+"""Estimators for experiment reports, vectorised over bootstrap replicates.
 
-Wilson score intervals, the unbiased pass@k estimator, linear-interpolation
-quantiles, percentile bootstrap of a mean, a clustered paired bootstrap of a
-binary difference (repeated draws per problem kept together), total variation
-and Jensen-Shannon divergence (bits) between answer distributions, and a
-bootstrap of the mean distance between two methods' answer distributions.
+* Wilson score interval of a binomial proportion;
+* the unbiased pass@k estimator 1 - C(n - c, k) / C(n, k);
+* quantiles with linear interpolation between order statistics;
+* percentile bootstrap of a mean (all replicates drawn as one index matrix);
+* clustered paired bootstrap of a difference in success rates, resampling whole
+  clusters (repeated draws of one problem stay together);
+* total variation and Jensen-Shannon divergence (bits) between answer laws, and a
+  bootstrap of their mean over problems.
 
-Reference behaviour: experiments/shared/statistics.py:14-206.
+Every bootstrap takes an explicit seed (numpy ``default_rng``), so reports are
+reproducible.  The estimators are those of the reference's experiment reports
+(experiments/shared/statistics.py); only their computation is different.
 """
 
 from __future__ import annotations
 
 import math
-import random
-from collections import Counter
 from collections.abc import Mapping, Sequence
-from statistics import fmean
 from typing import Any
+
+import numpy as np
 
 from ..shared.metrics import total_variation
 
@@ -24,117 +28,141 @@ Z95 = 1.959963984540054
 
 
 def wilson_interval(successes: int, trials: int, z: float = Z95) -> list[float]:
-    if trials <= 0 or not 0 <= successes <= trials:
-        raise ValueError("successes must lie between zero and positive trials")
-    p = successes / trials
-    zz = z * z
-    den = 1.0 + zz / trials
-    centre = (p + zz / (2 * trials)) / den
-    half = z * math.sqrt(p * (1 - p) / trials + zz / (4 * trials * trials)) / den
-    return [centre - half, centre + half]
+    if trials < 1 or not 0 <= successes <= trials:
+        raise ValueError(f"need 0 <= successes <= trials and trials >= 1, got {successes}/{trials}")
+    n = float(trials)
+    p = successes / n
+    shrink = 1.0 + z * z / n
+    centre = (p + z * z / (2 * n)) / shrink
+    spread = z * math.sqrt(p * (1 - p) / n + z * z / (4 * n * n)) / shrink
+    return [centre - spread, centre + spread]
 
 
 def estimated_pass_at_k(correct: int, draws: int, k: int) -> float:
-    """1 - C(n - c, k) / C(n, k): probability that k draws without replacement contain a correct one."""
+    """Probability that k of the n draws, taken without replacement, include a correct one."""
     if not 0 <= correct <= draws:
-        raise ValueError("correct must lie between zero and draws")
-    if draws <= 0 or not 1 <= k <= draws:
-        raise ValueError("k must lie between one and the number of draws")
-    if draws - correct < k:
+        raise ValueError("correct must lie in 0..draws")
+    if not 1 <= k <= draws:
+        raise ValueError("k must lie in 1..draws")
+    wrong = draws - correct
+    if wrong < k:
         return 1.0
-    return 1.0 - math.comb(draws - correct, k) / math.comb(draws, k)
+    # C(wrong, k) / C(draws, k) as a product of k ratios (no large integers)
+    steps = np.arange(k, dtype=np.float64)
+    ratio = np.prod((wrong - steps) / (draws - steps))
+    return float(1.0 - ratio)
 
 
 def quantile(values: Sequence[float], probability: float) -> float:
     if not len(values):
-        raise ValueError("quantile requires at least one value")
-    if not 0 <= probability <= 1:
+        raise ValueError("a quantile of no values is undefined")
+    if not 0.0 <= probability <= 1.0:
         raise ValueError("probability must lie in [0, 1]")
-    v = sorted(float(x) for x in values)
-    pos = (len(v) - 1) * probability
-    lo, hi = math.floor(pos), math.ceil(pos)
-    return v[lo] if lo == hi else v[lo] + (v[hi] - v[lo]) * (pos - lo)
+    return float(np.quantile(np.asarray(values, dtype=np.float64), probability))
 
 
-def _resample_means(values: Sequence[float], rng: random.Random, replicates: int) -> list[float]:
-    n = len(values)
-    return [fmean(values[rng.randrange(n)] for _ in range(n)) for _ in range(replicates)]
+def _bootstrap_means(values: np.ndarray, seed: int, replicates: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    picks = rng.integers(0, values.size, size=(replicates, values.size))
+    return values[picks].mean(axis=1)
+
+
+def _central_95(samples: np.ndarray) -> list[float]:
+    lo, hi = np.quantile(samples, [0.025, 0.975])
+    return [float(lo), float(hi)]
 
 
 def bootstrap_mean_interval(values: Sequence[float], *, seed: int, replicates: int = 10_000) -> list[float]:
-    if not len(values) or replicates <= 0:
-        raise ValueError("bootstrap values and replicate count must be positive")
-    means = _resample_means([float(x) for x in values], random.Random(seed), replicates)
-    return [quantile(means, 0.025), quantile(means, 0.975)]
+    if not len(values) or replicates < 1:
+        raise ValueError("the bootstrap needs values and a positive replicate count")
+    return _central_95(_bootstrap_means(np.asarray(values, dtype=np.float64), seed, replicates))
+
+
+def _rates_by_cluster(records: Sequence[Mapping[str, Any]], cluster_key: str, outcome_key: str
+                      ) -> dict[int, np.ndarray]:
+    grouped: dict[int, list[float]] = {}
+    for record in records:
+        grouped.setdefault(int(record[cluster_key]), []).append(float(bool(record[outcome_key])))
+    return {c: np.asarray(v) for c, v in grouped.items()}
 
 
 def clustered_paired_binary_difference(left_records: Sequence[Mapping[str, Any]],
                                        right_records: Sequence[Mapping[str, Any]], *, cluster_key: str,
                                        outcome_key: str, seed: int, replicates: int = 10_000) -> dict[str, Any]:
     """Mean over clusters of (left success rate - right success rate), with a cluster bootstrap interval."""
-    if not left_records or not right_records or replicates <= 0:
-        raise ValueError("paired records and replicate count must be positive")
-
-    def by_cluster(records):
-        out: dict[int, list[float]] = {}
-        for r in records:
-            out.setdefault(int(r[cluster_key]), []).append(float(bool(r[outcome_key])))
-        return out
-
-    left, right = by_cluster(left_records), by_cluster(right_records)
+    if not left_records or not right_records or replicates < 1:
+        raise ValueError("both methods need records, and the replicate count must be positive")
+    left = _rates_by_cluster(left_records, cluster_key, outcome_key)
+    right = _rates_by_cluster(right_records, cluster_key, outcome_key)
     if left.keys() != right.keys():
-        raise ValueError("paired methods must contain the same clusters")
-    diffs = []
-    for c in sorted(left):
-        if len(left[c]) != len(right[c]):
-            raise ValueError("paired methods must contain the same draws per cluster")
-        diffs.append(fmean(left[c]) - fmean(right[c]))
-    boot = _resample_means(diffs, random.Random(seed), replicates)
-    return {"difference": fmean(diffs), "clustered_bootstrap_95": [quantile(boot, 0.025), quantile(boot, 0.975)]}
+        raise ValueError("the two methods were not run on the same clusters")
+    clusters = sorted(left)
+    if any(left[c].size != right[c].size for c in clusters):
+        raise ValueError("the two methods have different draw counts in some cluster")
+    differences = np.asarray([left[c].mean() - right[c].mean() for c in clusters])
+    return {"difference": float(differences.mean()),
+            "clustered_bootstrap_95": _central_95(_bootstrap_means(differences, seed, replicates))}
 
 
 def probability_distribution(counts: Mapping[str, int]) -> dict[str, float]:
-    total = sum(counts.values())
-    if total <= 0:
-        raise ValueError("counts must have positive mass")
-    return {k: v / total for k, v in counts.items()}
+    keys = list(counts)
+    mass = np.asarray([counts[k] for k in keys], dtype=np.float64)
+    if mass.sum() <= 0:
+        raise ValueError("counts need positive total mass")
+    return dict(zip(keys, (mass / mass.sum()).tolist()))
 
 
 def total_variation_distance(left: Mapping[str, float], right: Mapping[str, float]) -> float:
     return total_variation(left, right)
 
 
+def _aligned(left: Mapping[str, float], right: Mapping[str, float]) -> tuple[np.ndarray, np.ndarray]:
+    keys = sorted(set(left) | set(right), key=str)
+    return (np.asarray([left.get(k, 0.0) for k in keys], dtype=np.float64),
+            np.asarray([right.get(k, 0.0) for k in keys], dtype=np.float64))
+
+
 def jensen_shannon_bits(left: Mapping[str, float], right: Mapping[str, float]) -> float:
-    keys = set(left) | set(right)
-    mid = {k: 0.5 * (left.get(k, 0.0) + right.get(k, 0.0)) for k in keys}
+    p, q = _aligned(left, right)
+    m = 0.5 * (p + q)
 
-    def kl(d):
-        return sum(p * math.log2(p / mid[k]) for k, p in d.items() if p > 0)
+    def kl_to_mid(a: np.ndarray) -> float:
+        support = a > 0
+        return float(np.sum(a[support] * np.log2(a[support] / m[support])))
 
-    return 0.5 * (kl(left) + kl(right))
+    return 0.5 * (kl_to_mid(p) + kl_to_mid(q))
 
 
 def bootstrap_answer_distance(left: Mapping[int, Sequence[str]], right: Mapping[int, Sequence[str]],
                               problem_indices: Sequence[int], *, seed: int = 0,
                               replicates: int = 2_000) -> dict[str, list[float]]:
-    if not problem_indices or replicates <= 0:
-        raise ValueError("problem indices and replicate count must be positive")
-    rng = random.Random(seed)
-    tv, js = [], []
-    for _ in range(replicates):
-        t_sum, j_sum = 0.0, 0.0
-        for i in problem_indices:
-            a, b = left[i], right[i]
-            if not a or not b:
-                raise ValueError("every problem requires observations from both methods")
-            pa = probability_distribution(Counter(a[rng.randrange(len(a))] for _ in a))
-            pb = probability_distribution(Counter(b[rng.randrange(len(b))] for _ in b))
-            t_sum += total_variation_distance(pa, pb)
-            j_sum += jensen_shannon_bits(pa, pb)
-        tv.append(t_sum / len(problem_indices))
-        js.append(j_sum / len(problem_indices))
-    return {"mean_total_variation_bootstrap_95": [quantile(tv, 0.025), quantile(tv, 0.975)],
-            "mean_jensen_shannon_bits_bootstrap_95": [quantile(js, 0.025), quantile(js, 0.975)]}
+    """Bootstrap of the mean (over problems) TV and JS distance between two methods' answers."""
+    if not problem_indices or replicates < 1:
+        raise ValueError("the bootstrap needs problems and a positive replicate count")
+    rng = np.random.default_rng(seed)
+    tv = np.zeros(replicates)
+    js = np.zeros(replicates)
+    for i in problem_indices:
+        a, b = list(left[i]), list(right[i])
+        if not a or not b:
+            raise ValueError(f"problem {i} lacks answers from one of the methods")
+        labels = sorted(set(a) | set(b), key=str)
+        code = {label: j for j, label in enumerate(labels)}
+        ca, cb = np.asarray([code[x] for x in a]), np.asarray([code[x] for x in b])
+        ra = ca[rng.integers(0, ca.size, size=(replicates, ca.size))]
+        rb = cb[rng.integers(0, cb.size, size=(replicates, cb.size))]
+        pa = np.stack([np.bincount(r, minlength=len(labels)) for r in ra]) / ca.size
+        pb = np.stack([np.bincount(r, minlength=len(labels)) for r in rb]) / cb.size
+        tv += 0.5 * np.abs(pa - pb).sum(axis=1)
+        m = 0.5 * (pa + pb)
+        with np.errstate(divide="ignore", invalid="ignore"):
+            kl_a = np.where(pa > 0, pa * np.log2(pa / m), 0.0).sum(axis=1)
+            kl_b = np.where(pb > 0, pb * np.log2(pb / m), 0.0).sum(axis=1)
+        js += 0.5 * (kl_a + kl_b)
+    tv /= len(problem_indices)
+    js /= len(problem_indices)
+    return {"mean_total_variation_bootstrap_95": _central_95(tv),
+            "mean_jensen_shannon_bits_bootstrap_95": _central_95(js)}
 
 
 __all__ = ["bootstrap_answer_distance", "bootstrap_mean_interval", "clustered_paired_binary_difference",
