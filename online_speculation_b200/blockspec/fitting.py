@@ -1,16 +1,18 @@
-"""File-backed draft-view fitting with deterministic data order and bit-exact resume.
+"""File-backed draft-view fitting with a deterministic data order and bit-exact resume.
 
-* ``TokenDataset``: indexed tokenized JSONL (``{"input_ids": [...]}`` per line);
-  random windows stay inside one record.
-* ``BatchStream``: seeded permutation + cursor, saved with its RNG state.
-* ``FitConfig``: schedule (linear warm-up then cosine to ``minimum_lr_ratio``),
-  AdamW hyper-parameters, precision.
-* ``Trainer``: ``run`` / ``evaluate`` / ``save`` / ``resume``; a checkpoint
-  is written only at optimizer-step boundaries and carries the data cursor,
-  every RNG state and a fingerprint of the frozen base, so an interrupted run
-  resumes to the same weights as an uninterrupted one.
-Reference: online-speculation/src/blockspec/parallel/fitting.py:18-263
-(training-state payload ``dual-fit-v1``).
+* ``TokenDataset``: tokenised JSONL (``{"input_ids": [...]}`` per line) indexed by byte
+  offset; a training window never crosses records.
+* ``BatchStream``: a seeded permutation walked by a cursor, reshuffled per epoch; its
+  state (generator state, permutation, cursor, epoch) is saved with the checkpoint.
+* ``FitConfig``: linear warm-up then cosine decay to ``minimum_lr_ratio``, AdamW
+  settings and precision.
+* ``Trainer``: ``run`` / ``evaluate`` / ``save`` / ``resume``.  Checkpoints are taken at
+  optimizer-step boundaries and carry the data cursor, every RNG state, the runtime
+  and a fingerprint of the frozen base, so an interrupted run resumes to the weights
+  an uninterrupted run reaches.
+
+The training-state payload (``format = "dual-fit-v1"`` and its keys) is the checkpoint
+contract of online-speculation/src/blockspec/parallel/fitting.py.
 """
 
 from __future__ import annotations
@@ -30,42 +32,42 @@ from .training import distillation_loss, distillation_update, sample_anchors
 from .weights import file_sha256, load_checkpoint, save_checkpoint
 
 
+def _token_ids(line: bytes, vocab_size: int) -> list[int]:
+    ids = json.loads(line).get("input_ids")
+    if not (isinstance(ids, list) and ids and all(type(t) is int and 0 <= t < vocab_size for t in ids)):
+        raise ValueError("every record needs a non-empty input_ids list of vocabulary ids")
+    return ids
+
+
 class TokenDataset:
     def __init__(self, path, vocab_size: int, sequence_length: int):
-        if min(vocab_size, sequence_length) < 1:
-            raise ValueError("positive vocabulary and window required")
+        if vocab_size < 1 or sequence_length < 1:
+            raise ValueError("vocab_size and sequence_length have to be positive")
         self.path = Path(path).resolve()
-        self.vocab_size, self.sequence_length = vocab_size, sequence_length
-        self.offsets, self.skipped = array("Q"), 0
-        with self.path.open("rb") as f:
-            while True:
-                off = f.tell()
-                line = f.readline()
-                if not line:
-                    break
-                if not line.strip():
-                    continue
-                if len(self._decode(line)) >= sequence_length:
-                    self.offsets.append(off)
-                else:
-                    self.skipped += 1
+        self.vocab_size = vocab_size
+        self.sequence_length = sequence_length
+        self.offsets = array("Q")
+        self.skipped = 0
+        offset = 0
+        with self.path.open("rb") as handle:
+            for line in handle:
+                if line.strip():
+                    if len(_token_ids(line, vocab_size)) >= sequence_length:
+                        self.offsets.append(offset)
+                    else:
+                        self.skipped += 1
+                offset += len(line)
         if not self.offsets:
-            raise ValueError("training data needs at least one complete window")
+            raise ValueError(f"{self.path} has no record of at least {sequence_length} tokens")
         self.fingerprint = file_sha256(self.path)
-
-    def _decode(self, line: bytes) -> list[int]:
-        ids = json.loads(line).get("input_ids")
-        if not isinstance(ids, list) or not ids or any(type(x) is not int or not 0 <= x < self.vocab_size for x in ids):
-            raise ValueError("each record needs valid input_ids")
-        return ids
 
     def __len__(self) -> int:
         return len(self.offsets)
 
     def __getitem__(self, i: int) -> torch.Tensor:
-        with self.path.open("rb") as f:
-            f.seek(self.offsets[i])
-            return torch.tensor(self._decode(f.readline()), dtype=torch.long)
+        with self.path.open("rb") as handle:
+            handle.seek(self.offsets[i])
+            return torch.tensor(_token_ids(handle.readline(), self.vocab_size), dtype=torch.long)
 
 
 class BatchStream:
@@ -73,31 +75,40 @@ class BatchStream:
         self.dataset = dataset
         self.rng = torch.Generator().manual_seed(seed)
         self.order = torch.randperm(len(dataset), generator=self.rng)
-        self.cursor = self.epoch = 0
+        self.cursor = 0
+        self.epoch = 0
+
+    def _next_record(self) -> torch.Tensor:
+        if self.cursor >= len(self.order):
+            self.order = torch.randperm(len(self.dataset), generator=self.rng)
+            self.cursor = 0
+            self.epoch += 1
+        record = self.dataset[int(self.order[self.cursor])]
+        self.cursor += 1
+        return record
 
     def batch(self, count: int) -> torch.Tensor:
-        rows, L = [], self.dataset.sequence_length
+        width = self.dataset.sequence_length
+        windows = []
         for _ in range(count):
-            if self.cursor == len(self.order):
-                self.order = torch.randperm(len(self.dataset), generator=self.rng)
-                self.cursor = 0
-                self.epoch += 1
-            seq = self.dataset[int(self.order[self.cursor])]
-            self.cursor += 1
-            start = int(torch.randint(len(seq) - L + 1, (), generator=self.rng))
-            rows.append(seq[start:start + L])
-        return torch.stack(rows)
+            record = self._next_record()
+            start = int(torch.randint(record.numel() - width + 1, (), generator=self.rng))
+            windows.append(record[start:start + width])
+        return torch.stack(windows)
 
     def state_dict(self) -> dict:
         return {"rng": self.rng.get_state(), "order": self.order.clone(), "cursor": self.cursor, "epoch": self.epoch}
 
     def load_state_dict(self, state: dict) -> None:
         order = state["order"].cpu()
-        if (order.shape != (len(self.dataset),) or not torch.equal(order.sort().values, torch.arange(len(self.dataset)))
-                or not 0 <= state["cursor"] <= len(order) or state["epoch"] < 0):
-            raise ValueError("invalid data permutation or cursor")
+        n = len(self.dataset)
+        is_permutation = order.shape == (n,) and torch.equal(torch.sort(order).values, torch.arange(n))
+        if not is_permutation or not 0 <= state["cursor"] <= n or state["epoch"] < 0:
+            raise ValueError("the saved data stream does not fit this dataset")
         self.rng.set_state(state["rng"].cpu())
-        self.order, self.cursor, self.epoch = order, state["cursor"], state["epoch"]
+        self.order = order
+        self.cursor = state["cursor"]
+        self.epoch = state["epoch"]
 
 
 @dataclass(frozen=True)
@@ -118,18 +129,21 @@ class FitConfig:
     optimizer_impl: str = "single"
 
     def __post_init__(self):
-        if min(self.steps, self.batch_size, self.sequence_length, self.anchors_per_sequence, self.accumulate,
-               self.chunk_rows) < 1:
-            raise ValueError("positive integer training dimensions required")
-        if not 0 <= self.warmup_steps < self.steps:
-            raise ValueError("warm-up must fit within the schedule")
-        if (not all(math.isfinite(v) for v in (self.learning_rate, self.minimum_lr_ratio, self.weight_decay,
-                                               self.clip_grad))
-                or self.learning_rate <= 0 or self.clip_grad <= 0 or self.weight_decay < 0
-                or not 0 <= self.minimum_lr_ratio <= 1):
-            raise ValueError("finite positive learning rate / clip and a valid decay required")
-        if self.precision not in ("fp32", "bf16") or self.optimizer_impl not in ("single", "fused"):
-            raise ValueError("precision fp32/bf16 and optimizer single/fused")
+        counts = (self.steps, self.batch_size, self.sequence_length, self.anchors_per_sequence, self.accumulate,
+                  self.chunk_rows)
+        scales = (self.learning_rate, self.minimum_lr_ratio, self.weight_decay, self.clip_grad)
+        checks = (
+            (min(counts) >= 1, "step, batch, window, anchor, accumulation and chunk counts must be positive"),
+            (0 <= self.warmup_steps < self.steps, "the warm-up must end before the last step"),
+            (all(math.isfinite(v) for v in scales), "optimizer scales must be finite"),
+            (self.learning_rate > 0 and self.clip_grad > 0, "learning_rate and clip_grad must be positive"),
+            (self.weight_decay >= 0 and 0 <= self.minimum_lr_ratio <= 1, "weight decay >= 0, min ratio in [0, 1]"),
+            (self.precision in ("fp32", "bf16"), "precision is fp32 or bf16"),
+            (self.optimizer_impl in ("single", "fused"), "optimizer_impl is single or fused"),
+        )
+        failed = [message for ok, message in checks if not ok]
+        if failed:
+            raise ValueError("invalid fit config: " + "; ".join(failed))
 
     def make_optimizer(self, params):
         return torch.optim.AdamW(params, lr=self.learning_rate, weight_decay=self.weight_decay, foreach=False,
@@ -138,33 +152,35 @@ class FitConfig:
     def rate(self, step: int) -> float:
         if step < self.warmup_steps:
             return self.learning_rate * (step + 1) / self.warmup_steps
-        frac = (step - self.warmup_steps) / max(1, self.steps - self.warmup_steps - 1)
-        return self.learning_rate * (self.minimum_lr_ratio
-                                     + (1 - self.minimum_lr_ratio) * (1 + math.cos(math.pi * frac)) / 2)
+        progress = (step - self.warmup_steps) / max(1, self.steps - self.warmup_steps - 1)
+        cosine = 0.5 * (1.0 + math.cos(math.pi * progress))
+        return self.learning_rate * (self.minimum_lr_ratio + (1.0 - self.minimum_lr_ratio) * cosine)
 
 
 def frozen_fingerprint(model) -> str:
-    h = hashlib.sha256()
-    for n, p in model.named_parameters():
-        if ".attention.draft." in n:
-            continue
-        h.update((n + str(tuple(p.shape)) + str(p.dtype)).encode())
-        h.update(p.detach().contiguous().cpu().float().numpy().tobytes())
-    return h.hexdigest()
+    """SHA-256 over the names, shapes, dtypes and values of every non-draft parameter."""
+    digest = hashlib.sha256()
+    for name, p in model.named_parameters():
+        if ".attention.draft." not in name:
+            digest.update(f"{name}{tuple(p.shape)}{p.dtype}".encode())
+            digest.update(p.detach().float().cpu().contiguous().numpy().tobytes())
+    return digest.hexdigest()
 
 
 class Trainer:
     def __init__(self, model, data: TokenDataset, config: FitConfig = FitConfig()):
-        if (data.sequence_length != config.sequence_length or data.vocab_size != model.config.vocab_size
-                or config.sequence_length < model.config.block_size):
-            raise ValueError("matching data windows and complete draft blocks required")
+        if data.sequence_length != config.sequence_length or data.vocab_size != model.config.vocab_size:
+            raise ValueError("the dataset's window and vocabulary must match the config and model")
+        if config.sequence_length < model.config.block_size:
+            raise ValueError("a training window must hold at least one draft block")
         if any(p.dtype != torch.float32 for p in model.parameters()):
-            raise ValueError("training keeps fp32 parameters (optional bf16 autocast)")
+            raise ValueError("parameters stay fp32 during fitting (bf16 runs through autocast)")
         self.model = model.train_draft_only()
-        self.config, self.data = config, data
+        self.config = config
+        self.data = data
         self.device = model.embedding.weight.device
         if config.precision == "bf16" and self.device.type != "cuda":
-            raise ValueError("bf16 autocast needs CUDA")
+            raise ValueError("bf16 autocast runs on CUDA only")
         self.parameters = [p for p in model.parameters() if p.requires_grad]
         self.optimizer = config.make_optimizer(self.parameters)
         self.stream = BatchStream(data, config.seed)
@@ -176,61 +192,57 @@ class Trainer:
         return torch.autocast("cuda", dtype=torch.bfloat16) if self.config.precision == "bf16" else nullcontext()
 
     def _runtime(self) -> dict:
+        on_cuda = self.device.type == "cuda"
         return {"torch": str(torch.__version__), "device_type": self.device.type,
-                "device_name": torch.cuda.get_device_name(self.device) if self.device.type == "cuda" else "cpu",
+                "device_name": torch.cuda.get_device_name(self.device) if on_cuda else "cpu",
                 "threads": torch.get_num_threads(), "matmul_precision": torch.get_float32_matmul_precision()}
 
-    def _batches(self, stream, rng):
-        out = []
-        for _ in range(self.config.accumulate):
-            tokens = stream.batch(self.config.batch_size)
-            anchors = sample_anchors(tokens, self.model.config.block_size, self.config.anchors_per_sequence,
-                                     generator=rng)
-            out.append((tokens.to(self.device), anchors.to(self.device)))
-        return out
+    def _micro_batch(self, stream: BatchStream, rng: torch.Generator):
+        tokens = stream.batch(self.config.batch_size)
+        anchors = sample_anchors(tokens, self.model.config.block_size, self.config.anchors_per_sequence,
+                                 generator=rng)
+        return tokens.to(self.device), anchors.to(self.device)
 
     def run(self, until: int | None = None, progress=None) -> list[dict]:
         end = self.config.steps if until is None else until
         if not self.step <= end <= self.config.steps:
-            raise ValueError("stop boundary must lie within the schedule")
-        records = []
+            raise ValueError(f"cannot run from step {self.step} to {end} of {self.config.steps}")
         self.model.train()
+        history = []
         while self.step < end:
-            t0 = time.perf_counter()
-            metrics = distillation_update(self.model, self._batches(self.stream, self.anchors_rng), self.optimizer,
-                                          learning_rate=self.config.rate(self.step), clip_grad=self.config.clip_grad,
-                                          chunk_rows=self.config.chunk_rows, autocast=self._autocast)
+            started = time.perf_counter()
+            batches = [self._micro_batch(self.stream, self.anchors_rng) for _ in range(self.config.accumulate)]
+            metrics = distillation_update(self.model, batches, self.optimizer, learning_rate=self.config.rate(self.step),
+                                          clip_grad=self.config.clip_grad, chunk_rows=self.config.chunk_rows,
+                                          autocast=self._autocast)
             self.step += 1
-            rec = {"step": self.step, **metrics, "seconds": time.perf_counter() - t0}
-            records.append(rec)
+            record = {"step": self.step, **metrics, "seconds": time.perf_counter() - started}
+            history.append(record)
             if progress is not None:
-                progress(rec)
-        return records
+                progress(record)
+        return history
 
     @torch.no_grad()
     def evaluate(self, data: TokenDataset, batches: int = 4) -> float:
         stream = BatchStream(data, self.config.seed + 2)
         rng = torch.Generator().manual_seed(self.config.seed + 3)
-        training = self.model.training
+        was_training = self.model.training
         self.model.eval()
+        total = 0.0
         try:
-            losses = []
             for _ in range(batches):
-                tokens = stream.batch(self.config.batch_size)
-                anchors = sample_anchors(tokens, self.model.config.block_size, self.config.anchors_per_sequence,
-                                         generator=rng)
+                tokens, anchors = self._micro_batch(stream, rng)
                 with self._autocast():
-                    losses.append(float(distillation_loss(self.model, tokens.to(self.device),
-                                                          anchors.to(self.device), chunk_rows=self.config.chunk_rows)))
+                    total += float(distillation_loss(self.model, tokens, anchors, chunk_rows=self.config.chunk_rows))
         finally:
-            self.model.train(training)
-        return sum(losses) / len(losses)
+            self.model.train(was_training)
+        return total / batches
 
     def save(self, path) -> None:
+        cuda_rng = torch.cuda.get_rng_state(self.device) if self.device.type == "cuda" else None
         state = {"format": "dual-fit-v1", "config": asdict(self.config), "data_sha256": self.data.fingerprint,
                  "data_stream": self.stream.state_dict(), "anchors_rng": self.anchors_rng.get_state(),
-                 "torch_rng": torch.get_rng_state(), "runtime": self._runtime(),
-                 "cuda_rng": torch.cuda.get_rng_state(self.device) if self.device.type == "cuda" else None,
+                 "torch_rng": torch.get_rng_state(), "runtime": self._runtime(), "cuda_rng": cuda_rng,
                  "base_fingerprint": self.base_fingerprint}
         save_checkpoint(path, self.model, optimizer=self.optimizer, step=self.step, training_state=state)
 
@@ -239,14 +251,16 @@ class Trainer:
         model, saved = load_checkpoint(path, device=device)
         state = saved["training_state"]
         if not isinstance(state, dict) or state.get("format") != "dual-fit-v1" or saved["optimizer"] is None:
-            raise ValueError("a complete training checkpoint is required")
+            raise ValueError(f"{path} is not a resumable dual-fit-v1 training checkpoint")
         if not isinstance(data, TokenDataset):
             data = TokenDataset(data, model.config.vocab_size, state["config"]["sequence_length"])
         if state["data_sha256"] != data.fingerprint:
-            raise ValueError("resume training data differs")
+            raise ValueError("the training data changed since the checkpoint was written")
         trainer = cls(model, data, FitConfig(**state["config"]))
-        if trainer.base_fingerprint != state["base_fingerprint"] or trainer._runtime() != state["runtime"]:
-            raise ValueError("resume requires the same runtime and frozen base")
+        if trainer.base_fingerprint != state["base_fingerprint"]:
+            raise ValueError("the frozen base weights changed since the checkpoint was written")
+        if trainer._runtime() != state["runtime"]:
+            raise ValueError("bit-exact resume needs the runtime the checkpoint was written with")
         trainer.optimizer.load_state_dict(saved["optimizer"])
         trainer.stream.load_state_dict(state["data_stream"])
         trainer.anchors_rng.set_state(state["anchors_rng"].cpu())

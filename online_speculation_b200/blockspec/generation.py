@@ -1,20 +1,22 @@
 """Batch-one block-speculative decoding with a pending committed anchor.
 
-Loop (online-speculation/src/blockspec/parallel/generation.py:74-212):
+A :class:`_Decoder` holds the state of one request (branch, sampler, KV history,
+anchor, result) and moves through three kinds of step:
 
-1. prefill the prompt and sample the first token exactly from the AR view;
-2. each round: the branch drafts ``[anchor, MASK x (K-1)]`` through the draft
-   view (read-only AR history, bidirectional block), the sampler proposes K-1
-   candidates, the AR view verifies ``[anchor, candidates]`` causally, the
-   exact correction commits the accepted prefix plus one corrected token, the
-   KV history is trimmed to the committed prefix, and feedback hooks may
-   observe the round (online learner);
-3. with one token left the AR view samples it directly.
+1. prefill: the prompt goes through the AR view and the first token is sampled
+   exactly from it;
+2. a speculative round: the branch drafts ``[anchor, MASK x (K - 1)]`` through the
+   draft view (read-only AR history, bidirectional block), the sampler proposes
+   K - 1 candidates, the AR view verifies ``[anchor, candidates]`` causally, the
+   exact correction commits the accepted prefix plus one corrected token, the KV
+   history is cut back to the committed prefix, and feedback hooks (the online
+   learner) may observe the round;
+3. a tail step: with one token of budget left the AR view samples it directly.
 
 Branches: :class:`MaskedAttentionBranch` (the PyTorch dual-view module) and
-``KernelBranch`` (the same weights on the sm_100a engine, in
-``kernel_branch.py``).  Samplers: :class:`ProposalSampler` (tensor maths of
-``sampling.py``).
+``KernelBranch`` (the same weights on the sm_100a engine, ``kernel_branch.py``).
+The counters of :class:`Generation` are the reference's report fields
+(online-speculation/src/blockspec/parallel/generation.py).
 """
 
 from __future__ import annotations
@@ -128,27 +130,100 @@ class MaskedAttentionBranch:
                           feedback is not None and capture is not None)
 
 
-def _length(branch, cache) -> int:
-    return branch.cache_length(cache) if hasattr(branch, "cache_length") else cache_length(cache)
-
-
-def _trim(branch, cache, n: int):
-    return branch.trim(cache, n) if hasattr(branch, "trim") else trim_cache(cache, n)
-
-
-def _append(result: Generation, tokens, budget: int, eos) -> bool:
-    for t in tokens:
-        if len(result.tokens) == budget:
-            return True
-        result.tokens.append(int(t))
-        if t == eos:
-            return True
-    return len(result.tokens) == budget
-
-
-def _sync(device):
+def _sync(device) -> None:
     if device.type == "cuda":
         torch.cuda.synchronize(device)
+
+
+def _check_prompt(prompt: Tensor) -> None:
+    if prompt.ndim != 2 or prompt.shape[0] != 1 or prompt.shape[1] == 0:
+        raise ValueError("decoding takes one non-empty prompt of shape [1, T]")
+
+
+class _Decoder:
+    """State of one batch-one decode."""
+
+    def __init__(self, branch, prompt: Tensor, budget: int, sampler: ProposalSampler, eos_id, generator, feedback):
+        self.branch = branch
+        self.prompt = prompt
+        self.budget = budget
+        self.sampler = sampler
+        self.eos = eos_id
+        self.generator = generator
+        self.feedback = feedback
+        self.result = Generation()
+        self.cache = None
+        self.stopped = False
+
+    # ---- cache helpers (branches may bring their own cache type)
+    def _cache_length(self, cache) -> int:
+        measure = getattr(self.branch, "cache_length", None)
+        return measure(cache) if measure is not None else cache_length(cache)
+
+    def _trim(self, cache, n: int):
+        cut = getattr(self.branch, "trim", None)
+        return cut(cache, n) if cut is not None else trim_cache(cache, n)
+
+    def emit(self, tokens) -> list[int]:
+        """Append tokens until the budget or EOS; returns the tokens actually kept."""
+        kept = []
+        for t in tokens:
+            if len(self.result.tokens) >= self.budget:
+                break
+            self.result.tokens.append(int(t))
+            kept.append(int(t))
+            if int(t) == self.eos:
+                self.stopped = True
+                break
+        if len(self.result.tokens) >= self.budget:
+            self.stopped = True
+        if self.feedback is not None and kept:
+            self.feedback.commit(kept)
+        return kept
+
+    @property
+    def anchor(self) -> Tensor:
+        return self.prompt.new_tensor([[self.result.tokens[-1]]])
+
+    def prefill(self) -> None:
+        logits, self.cache = self.branch.ar(self.prompt, logits_to_keep=1)
+        self.result.prefill_forwards = self.result.prefill_output_tokens = 1
+        self.emit([self.sampler.sample_ar(logits[0, -1], self.generator)])
+
+    def tail_step(self) -> None:
+        logits, self.cache = self.branch.ar(self.anchor, cache=self.cache, logits_to_keep=1)
+        self.result.tail_ar_forwards += 1
+        self.emit([self.sampler.sample_ar(logits[0, -1], self.generator)])
+
+    def speculative_round(self, block: int) -> None:
+        r = self.result
+        r.rounds += 1
+        expected = self.prompt.shape[1] + len(r.tokens) - 1
+        if self._cache_length(self.cache) != expected:
+            raise RuntimeError("the KV history must end right before the committed anchor")
+        remaining = self.budget - len(r.tokens)
+        if remaining == 1:
+            self.tail_step()
+            return
+        length = min(block, remaining + self.branch.input_budget_extra)
+        proposal = self.branch.draft(self.anchor, self.cache, length, self.sampler, self.generator, self.feedback)
+        r.draft_forwards += 1
+        logits, verified_cache = self.branch.ar(proposal.verifier_inputs, cache=proposal.cache)
+        r.verifier_forwards += 1
+        verdict, target = self.sampler.verify(proposal, logits[0], self.generator)
+        feedback, self.feedback = self.feedback, None          # commit the round's tokens only once, below
+        submitted = self.emit(list(proposal.guaranteed) + list(verdict.tokens))
+        self.feedback = feedback
+        n = proposal.candidates.numel()
+        kept = min(verdict.accepted, len(submitted))
+        r.accepted_per_round.append(kept)
+        r.proposed_per_round.append(n)
+        r.fully_covered_rounds += kept == n
+        self.cache = self._trim(verified_cache, self.prompt.shape[1] + len(r.tokens) - 1)
+        if feedback is not None:
+            feedback.commit(submitted)
+            feedback.observe(proposal, logits[0], target, used=min(verdict.supervised, len(submitted)),
+                             fully_covered=kept == n, done=self.stopped)
 
 
 @torch.no_grad()
@@ -156,110 +231,64 @@ def generate_ar(branch, prompt: Tensor, max_new_tokens: int, *, sampling=Samplin
                 generator=None, sampler=None, prefix_tokens: int | None = None) -> Generation:
     """Plain autoregressive decoding with the AR view (the speed-up denominator).
 
-    ``prefix_tokens``: also record when the first ``prefix_tokens`` outputs were
-    delivered (``prefix_seconds``; the answer's end when it is shorter) -- the
-    reference time of a live AR-prefix trial.  The device synchronisation that
-    measurement needs is reported as ``prefix_capture_seconds``.
+    ``prefix_tokens``: also record when the first ``prefix_tokens`` outputs were out
+    (``prefix_seconds``; the end of the answer when it is shorter), the reference time
+    of a live AR-prefix trial; the device synchronisation that measurement needs is
+    reported as ``prefix_capture_seconds``.
     """
     if prefix_tokens is not None and (type(prefix_tokens) is not int or prefix_tokens < 1):
-        raise ValueError("a positive prefix length is required")
-    if prompt.ndim != 2 or prompt.shape[0] != 1 or prompt.shape[1] < 1:
-        raise ValueError("nonempty batch-one prompt required")
-    result = Generation()
+        raise ValueError("prefix_tokens has to be a positive integer")
+    _check_prompt(prompt)
     if max_new_tokens == 0:
-        return result
-    sampler = sampler or ProposalSampler(sampling)
+        return Generation()
+    d = _Decoder(branch, prompt, max_new_tokens, sampler or ProposalSampler(sampling), eos_id, generator, None)
     _sync(prompt.device)
-    start = time.perf_counter()
-    logits, cache = branch.ar(prompt, logits_to_keep=1)
-    token = sampler.sample_ar(logits[0, -1], generator)
-    result.prefill_forwards = result.prefill_output_tokens = 1
-    stopped = _append(result, [token], max_new_tokens, eos_id)
+    started = time.perf_counter()
 
-    def capture():
-        if prefix_tokens is not None and not result.prefix_tokens and (
-                len(result.tokens) >= prefix_tokens or stopped):
-            c0 = time.perf_counter()
-            _sync(prompt.device)
-            c1 = time.perf_counter()
-            result.prefix_tokens = len(result.tokens)
-            result.prefix_seconds = c1 - start
-            result.prefix_capture_seconds = c1 - c0
+    def note_prefix() -> None:
+        r = d.result
+        if prefix_tokens is None or r.prefix_tokens or not (len(r.tokens) >= prefix_tokens or d.stopped):
+            return
+        before = time.perf_counter()
+        _sync(prompt.device)
+        after = time.perf_counter()
+        r.prefix_tokens = len(r.tokens)
+        r.prefix_seconds = after - started
+        r.prefix_capture_seconds = after - before
 
-    capture()
-    while not stopped:
-        logits, cache = branch.ar(prompt.new_tensor([[token]]), cache=cache, logits_to_keep=1)
-        token = sampler.sample_ar(logits[0, -1], generator)
-        result.tail_ar_forwards += 1
-        stopped = _append(result, [token], max_new_tokens, eos_id)
-        capture()
+    d.prefill()
+    note_prefix()
+    while not d.stopped:
+        d.tail_step()
+        note_prefix()
     _sync(prompt.device)
-    result.seconds = time.perf_counter() - start
-    result.rounds = len(result.tokens)
-    return result
+    d.result.seconds = time.perf_counter() - started
+    d.result.rounds = len(d.result.tokens)
+    return d.result
 
 
 @torch.no_grad()
 def generate(branch, prompt: Tensor, max_new_tokens: int, *, block_size=None, sampling=SamplingConfig(),
              eos_id=None, generator=None, sampler=None, feedback=None) -> Generation:
-    if prompt.ndim != 2 or prompt.shape[0] != 1 or prompt.shape[1] < 1:
-        raise ValueError("nonempty batch-one prompt required")
+    _check_prompt(prompt)
     block = branch.default_block_size if block_size is None else block_size
     if block < 2:
-        raise ValueError("parallel drafting requires block_size >= 2")
-    result = Generation()
+        raise ValueError("block drafting needs block_size >= 2")
     if feedback is not None:
         feedback.begin(prompt)
     if max_new_tokens == 0:
+        empty = Generation()
         if feedback is not None:
-            feedback.finish(result)
-        return result
-    sampler = sampler or ProposalSampler(sampling)
+            feedback.finish(empty)
+        return empty
+    d = _Decoder(branch, prompt, max_new_tokens, sampler or ProposalSampler(sampling), eos_id, generator, feedback)
     _sync(prompt.device)
-    start = time.perf_counter()
-    logits, cache = branch.ar(prompt, logits_to_keep=1)
-    token = sampler.sample_ar(logits[0, -1], generator)
-    result.prefill_forwards = result.prefill_output_tokens = 1
-    stopped = _append(result, [token], max_new_tokens, eos_id)
+    started = time.perf_counter()
+    d.prefill()
+    while not d.stopped:
+        d.speculative_round(block)
     if feedback is not None:
-        feedback.commit([token])
-    anchor = prompt.new_tensor([[token]])
-    while not stopped:
-        result.rounds += 1
-        if _length(branch, cache) != prompt.shape[1] + len(result.tokens) - 1:
-            raise RuntimeError("history must end right before the committed anchor")
-        remaining = max_new_tokens - len(result.tokens)
-        if remaining == 1:
-            logits, cache = branch.ar(anchor, cache=cache, logits_to_keep=1)
-            token = sampler.sample_ar(logits[0, -1], generator)
-            result.tail_ar_forwards += 1
-            stopped = _append(result, [token], max_new_tokens, eos_id)
-            if feedback is not None:
-                feedback.commit([token])
-            continue
-        length = min(block, remaining + branch.input_budget_extra)
-        proposal = branch.draft(anchor, cache, length, sampler, generator, feedback)
-        result.draft_forwards += 1
-        logits, verified_cache = branch.ar(proposal.verifier_inputs, cache=proposal.cache)
-        result.verifier_forwards += 1
-        verified, target = sampler.verify(proposal, logits[0], generator)
-        begin = len(result.tokens)
-        stopped = _append(result, proposal.guaranteed + verified.tokens, max_new_tokens, eos_id)
-        submitted = result.tokens[begin:]
-        kept = min(verified.accepted, len(submitted))
-        used = min(verified.supervised, len(submitted))
-        n = proposal.candidates.numel()
-        result.accepted_per_round.append(kept)
-        result.proposed_per_round.append(n)
-        full = kept == n
-        result.fully_covered_rounds += full
-        cache = _trim(branch, verified_cache, prompt.shape[1] + len(result.tokens) - 1)
-        anchor = prompt.new_tensor([[result.tokens[-1]]])
-        if feedback is not None:
-            feedback.commit(submitted)
-            feedback.observe(proposal, logits[0], target, used=used, fully_covered=full, done=stopped)
-    if feedback is not None:
-        feedback.finish(result)
+        feedback.finish(d.result)
     _sync(prompt.device)
-    result.seconds = time.perf_counter() - start
-    return result
+    d.result.seconds = time.perf_counter() - started
+    return d.result

@@ -1,44 +1,47 @@
-"""Dual-view decoder: one Qwen3-shaped backbone with two attention projection sets.
+"""Dual-view decoder: one Qwen3-shaped backbone carrying two attention projection sets.
 
-The ``ar`` view is the ordinary causal decoder and owns the persistent KV
-history.  The ``draft`` view re-reads that history read-only and attends
-bidirectionally inside a block ``[anchor, MASK, ..., MASK]``; everything but
-the attention projections (embeddings, norms, MLPs, head) is shared.
-Semantics follow online-speculation/src/blockspec/parallel/backbone.py:15-321.
+The ``ar`` view is the ordinary causal decoder and owns the KV history.  The
+``draft`` view re-reads that history read-only and attends bidirectionally inside a
+block ``[anchor, MASK, ..., MASK]``; embeddings, norms, MLPs and the head are shared.
+This module is the PyTorch training / oracle path (distillation, online suffix
+replay with :meth:`DualViewDecoder.forward_suffix`, audits); serving on B200 runs the
+same weights on the sm_100a kernels (:mod:`online_speculation_b200.blockspec.kernel_branch`).
 
-This PyTorch module is the training / oracle path (distillation, online
-suffix replay with ``forward_suffix``, audits).  Serving on B200 uses the same
-weights on the sm_100a kernels through :mod:`online_speculation_b200.blockspec.kernel_branch`.
-
-Parameter names match the reference's own state-dict keys
+Attention is computed in fp32 with ``scaled_dot_product_attention`` and grouped KV
+heads, under an explicit boolean visibility mask.  Module and parameter names
 (``layers.{i}.attention.{ar,draft}.{q,k,v,o,q_norm,k_norm}``, ``input_norm``,
-``post_norm``, ``gate``, ``up``, ``down``, ``embedding``, ``norm``, ``head``) so
-``blockspec-dual-view-v1`` checkpoints are interchangeable.
+``post_norm``, ``gate``, ``up``, ``down``, ``embedding``, ``norm``, ``head``) are the
+state-dict keys of ``blockspec-dual-view-v1`` checkpoints
+(online-speculation/src/blockspec/parallel/backbone.py), so checkpoints load unchanged.
 """
 
 from __future__ import annotations
 
 import math
-from dataclasses import asdict, dataclass
+from dataclasses import asdict, dataclass, fields
 
 import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
-Cache = tuple  # tuple[(k [B, Hkv, T, D], v [B, Hkv, T, D]), ...] per layer
+Cache = tuple  # per layer (k [B, Hkv, T, D], v [B, Hkv, T, D])
+
+VIEWS = ("ar", "draft")
 
 
 def cache_length(cache) -> int:
-    if cache is not None and not cache:
-        raise ValueError("empty cache tuple; use None for an empty prefix")
-    return 0 if cache is None else cache[0][0].shape[2]
+    if cache is None:
+        return 0
+    if not cache:
+        raise ValueError("an empty cache is written None, not ()")
+    return int(cache[0][0].shape[2])
 
 
 def trim_cache(cache, length: int):
-    """Keep the first ``length`` positions of every layer (detached)."""
-    if length < 0 or length > cache_length(cache):
-        raise ValueError("cannot extend a cache by trimming")
-    if cache is None or length == 0:
+    """The first ``length`` positions of every layer, detached (None when nothing is left)."""
+    if not 0 <= length <= cache_length(cache):
+        raise ValueError(f"cannot trim a cache of {cache_length(cache)} positions to {length}")
+    if length == 0:
         return None
     return tuple((k[:, :, :length].detach(), v[:, :, :length].detach()) for k, v in cache)
 
@@ -61,44 +64,48 @@ class DualViewConfig:
     eos_token_id: int | None = None
 
     def __post_init__(self):
-        dims = (self.vocab_size, self.hidden_size, self.intermediate_size, self.num_hidden_layers,
-                self.num_attention_heads, self.num_key_value_heads, self.head_dim)
-        if min(dims) < 1:
-            raise ValueError("positive model dimensions required")
-        if self.head_dim % 2 or self.num_attention_heads % self.num_key_value_heads:
-            raise ValueError("even head width and integral query/KV ratio required")
-        if self.block_size < 2 or not 0 <= self.mask_token_id < self.vocab_size:
-            raise ValueError("invalid mask token or block size")
-        if self.eos_token_id is not None and not 0 <= self.eos_token_id < self.vocab_size:
-            raise ValueError("invalid EOS token")
-        if not (math.isfinite(self.rms_norm_eps) and self.rms_norm_eps > 0):
-            raise ValueError("positive finite normalization epsilon required")
-        if not (math.isfinite(self.rope_theta) and self.rope_theta > 1):
-            raise ValueError("finite rotary base greater than one required")
+        sizes = (self.vocab_size, self.hidden_size, self.intermediate_size, self.num_hidden_layers,
+                 self.num_attention_heads, self.num_key_value_heads, self.head_dim)
+        checks = (
+            (min(sizes) >= 1, "model sizes must be positive"),
+            (self.head_dim % 2 == 0, "rotary embeddings need an even head_dim"),
+            (self.num_attention_heads % self.num_key_value_heads == 0, "query heads must group evenly over KV heads"),
+            (self.block_size >= 2, "a draft block holds the anchor and at least one mask"),
+            (0 <= self.mask_token_id < self.vocab_size, "mask_token_id must be a vocabulary id"),
+            (self.eos_token_id is None or 0 <= self.eos_token_id < self.vocab_size, "eos_token_id must be a vocabulary id"),
+            (math.isfinite(self.rms_norm_eps) and self.rms_norm_eps > 0, "rms_norm_eps must be positive"),
+            (math.isfinite(self.rope_theta) and self.rope_theta > 1, "rope_theta must exceed 1"),
+        )
+        failed = [message for ok, message in checks if not ok]
+        if failed:
+            raise ValueError("invalid dual-view config: " + "; ".join(failed))
 
     def to_dict(self) -> dict:
         return asdict(self)
 
     @classmethod
     def from_public(cls, data: dict) -> "DualViewConfig":
-        """From a HF ``config.json`` of a Qwen3 (or dual-view) checkpoint."""
-        if data.get("model_type") not in ("qwen3", "orthrus"):
-            raise ValueError("the dual-view importer requires a Qwen3 checkpoint")
-        if data.get("hidden_act", "silu") != "silu":
-            raise ValueError("SwiGLU activation required")
-        if data.get("use_sliding_window", False) or any(t != "full_attention" for t in data.get("layer_types", [])):
-            raise ValueError("this backbone implements full attention")
+        """From the ``config.json`` of a Qwen3 (or dual-view) checkpoint."""
         rope = data.get("rope_parameters") or data.get("rope_scaling") or {}
+        problems = []
+        if data.get("model_type") not in ("qwen3", "orthrus"):
+            problems.append("model_type must be qwen3")
+        if data.get("hidden_act", "silu") != "silu":
+            problems.append("the MLP must be SwiGLU (hidden_act silu)")
+        if data.get("use_sliding_window", False) or set(data.get("layer_types", [])) - {"full_attention"}:
+            problems.append("only full attention is implemented")
         if rope.get("rope_type", rope.get("type", "default")) != "default":
-            raise ValueError("ordinary RoPE required")
-        names = cls.__dataclass_fields__
+            problems.append("only plain RoPE is implemented")
+        if problems:
+            raise ValueError("cannot import this checkpoint: " + "; ".join(problems))
+        names = [f.name for f in fields(cls)]
         values = {k: data[k] for k in names if k in data}
         if "rope_theta" in rope:
             values["rope_theta"] = rope["rope_theta"]
-        required = set(names) - {"attention_bias", "tie_word_embeddings", "eos_token_id"}
-        missing = required - values.keys()
+        optional = {"attention_bias", "tie_word_embeddings", "eos_token_id"}
+        missing = sorted(set(names) - optional - set(values))
         if missing:
-            raise ValueError(f"missing architecture fields: {sorted(missing)}")
+            raise ValueError(f"config.json lacks architecture fields {missing}")
         return cls(**values)
 
 
@@ -109,29 +116,41 @@ class RMSNorm(nn.Module):
         self.epsilon = eps
 
     def forward(self, x: Tensor) -> Tensor:
-        work = x.float()
-        normed = work * torch.rsqrt(work.square().mean(-1, keepdim=True) + self.epsilon)
-        return normed.to(x.dtype) * self.weight
-
-
-class AttentionView(nn.Module):
-    """One projection set with per-head Q/K RMSNorm."""
-
-    def __init__(self, c: DualViewConfig):
-        super().__init__()
-        qw, kvw = c.num_attention_heads * c.head_dim, c.num_key_value_heads * c.head_dim
-        self.q = nn.Linear(c.hidden_size, qw, bias=c.attention_bias)
-        self.k = nn.Linear(c.hidden_size, kvw, bias=c.attention_bias)
-        self.v = nn.Linear(c.hidden_size, kvw, bias=c.attention_bias)
-        self.o = nn.Linear(qw, c.hidden_size, bias=c.attention_bias)
-        self.q_norm = RMSNorm(c.head_dim, c.rms_norm_eps)
-        self.k_norm = RMSNorm(c.head_dim, c.rms_norm_eps)
+        x32 = x.float()
+        scale = torch.rsqrt(x32.pow(2).mean(dim=-1, keepdim=True) + self.epsilon)
+        return (x32 * scale).to(x.dtype) * self.weight
 
 
 def rotate(x: Tensor, cos: Tensor, sin: Tensor) -> Tensor:
-    half = x.shape[-1] // 2
-    a, b = x[..., :half], x[..., half:]
-    return torch.cat((a * cos[..., :half] - b * sin[..., :half], b * cos[..., half:] + a * sin[..., half:]), -1)
+    """Rotate-half RoPE: pairs (i, i + D/2) turn by the position's angle."""
+    first, second = x.chunk(2, dim=-1)
+    turned = torch.cat((-second, first), dim=-1)
+    return x * cos + turned * sin
+
+
+class AttentionView(nn.Module):
+    """One projection set (q, k, v, o) with per-head Q / K RMSNorm."""
+
+    def __init__(self, c: DualViewConfig):
+        super().__init__()
+        q_width = c.num_attention_heads * c.head_dim
+        kv_width = c.num_key_value_heads * c.head_dim
+        self.q = nn.Linear(c.hidden_size, q_width, bias=c.attention_bias)
+        self.k = nn.Linear(c.hidden_size, kv_width, bias=c.attention_bias)
+        self.v = nn.Linear(c.hidden_size, kv_width, bias=c.attention_bias)
+        self.o = nn.Linear(q_width, c.hidden_size, bias=c.attention_bias)
+        self.q_norm = RMSNorm(c.head_dim, c.rms_norm_eps)
+        self.k_norm = RMSNorm(c.head_dim, c.rms_norm_eps)
+        self.head_dim = c.head_dim
+
+    def heads(self, x: Tensor, rotary) -> tuple[Tensor, Tensor, Tensor]:
+        """q [B, Hq, T, D], k and v [B, Hkv, T, D] with Q/K norm and RoPE applied."""
+        B, T, _ = x.shape
+        split = lambda t: t.view(B, T, -1, self.head_dim).transpose(1, 2)   # noqa: E731
+        cos, sin = rotary
+        q = rotate(split(self.q_norm(self.q(x).view(B, T, -1, self.head_dim)).flatten(2)), cos, sin)
+        k = rotate(split(self.k_norm(self.k(x).view(B, T, -1, self.head_dim)).flatten(2)), cos, sin)
+        return q, k, split(self.v(x))
 
 
 class DualAttention(nn.Module):
@@ -142,23 +161,15 @@ class DualAttention(nn.Module):
         self.draft = AttentionView(c)
 
     def forward(self, x, view, cache, rotary, allowed):
-        c = self.config
-        B, T, _ = x.shape
-        p = getattr(self, view)
-        q = p.q_norm(p.q(x).view(B, T, -1, c.head_dim)).transpose(1, 2)
-        k = p.k_norm(p.k(x).view(B, T, -1, c.head_dim)).transpose(1, 2)
-        v = p.v(x).view(B, T, -1, c.head_dim).transpose(1, 2)
-        cos, sin = rotary
-        q, k = rotate(q, cos, sin), rotate(k, cos, sin)
+        projections: AttentionView = getattr(self, view)
+        q, k, v = projections.heads(x, rotary)
         if cache is not None:
-            k, v = torch.cat((cache[0], k), 2), torch.cat((cache[1], v), 2)
-        g = c.num_attention_heads // c.num_key_value_heads
-        kk, vv = k.repeat_interleave(g, 1), v.repeat_interleave(g, 1)
-        scores = (q.float() @ kk.float().transpose(-1, -2)) * c.head_dim ** -0.5
-        if allowed is not None:
-            scores = scores.masked_fill(~allowed, float("-inf"))
-        out = (scores.softmax(-1).to(q.dtype) @ vv).transpose(1, 2).reshape(B, T, -1)
-        return p.o(out), (k, v)
+            k = torch.cat((cache[0], k), dim=2)
+            v = torch.cat((cache[1], v), dim=2)
+        mixed = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), attn_mask=allowed,
+                                               enable_gqa=q.shape[1] != k.shape[1])
+        B, _, T, _ = q.shape
+        return projections.o(mixed.to(q.dtype).transpose(1, 2).reshape(B, T, -1)), (k, v)
 
 
 class DualLayer(nn.Module):
@@ -171,11 +182,14 @@ class DualLayer(nn.Module):
         self.up = nn.Linear(c.hidden_size, c.intermediate_size, bias=False)
         self.down = nn.Linear(c.intermediate_size, c.hidden_size, bias=False)
 
-    def forward(self, x, view, cache, rotary, allowed):
-        a, kv = self.attention(self.input_norm(x), view, cache, rotary, allowed)
-        x = x + a
+    def _mlp(self, x: Tensor) -> Tensor:
         n = self.post_norm(x)
-        return x + self.down(F.silu(self.gate(n)) * self.up(n)), kv
+        return self.down(F.silu(self.gate(n)) * self.up(n))
+
+    def forward(self, x, view, cache, rotary, allowed):
+        mixed, kv = self.attention(self.input_norm(x), view, cache, rotary, allowed)
+        x = x + mixed
+        return x + self._mlp(x), kv
 
 
 @dataclass
@@ -189,8 +203,9 @@ class DraftBoundary:
     history_length: int
 
     def detached(self) -> "DraftBoundary":
-        return DraftBoundary(self.hidden.detach().clone(), tuple(t.detach().clone() for t in self.rotary),
-                             None if self.allowed is None else self.allowed.detach().clone(), self.start_layer,
+        copy = lambda t: t.detach().clone()   # noqa: E731
+        return DraftBoundary(copy(self.hidden), tuple(map(copy, self.rotary)),
+                             None if self.allowed is None else copy(self.allowed), self.start_layer,
                              self.history_length)
 
 
@@ -207,27 +222,30 @@ class DualViewDecoder(nn.Module):
         super().__init__()
         self.config = config
         self.embedding = nn.Embedding(config.vocab_size, config.hidden_size)
-        self.layers = nn.ModuleList(DualLayer(config) for _ in range(config.num_hidden_layers))
+        self.layers = nn.ModuleList([DualLayer(config) for _ in range(config.num_hidden_layers)])
         self.norm = RMSNorm(config.hidden_size, config.rms_norm_eps)
         self.head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
         self.register_buffer("frequencies", self._frequencies(self.embedding.weight.device), persistent=False)
-        for m in self.modules():
-            if isinstance(m, (nn.Linear, nn.Embedding)):
-                nn.init.normal_(m.weight, std=0.02)
-                if isinstance(m, nn.Linear) and m.bias is not None:
-                    nn.init.zeros_(m.bias)
+        self._init_weights()
         self.tie_weights()
         self.initialize_draft_from_ar()
         self.source: dict = {}
+
+    def _init_weights(self) -> None:
+        for module in self.modules():
+            if isinstance(module, (nn.Linear, nn.Embedding)):
+                nn.init.normal_(module.weight, std=0.02)
+            if isinstance(module, nn.Linear) and module.bias is not None:
+                nn.init.zeros_(module.bias)
 
     def tie_weights(self):
         if self.config.tie_word_embeddings:
             self.head.weight = self.embedding.weight
 
     def _frequencies(self, device):
-        # the fp32 table is formed on the host, then moved
-        idx = torch.arange(0, self.config.head_dim, 2, dtype=torch.float32)
-        return (1.0 / (self.config.rope_theta ** (idx / self.config.head_dim))).to(device)
+        # built in fp32 on the host, then moved
+        exponents = torch.arange(0, self.config.head_dim, 2, dtype=torch.float32) / self.config.head_dim
+        return torch.pow(self.config.rope_theta, -exponents).to(device)
 
     def _apply(self, fn, recurse=True):
         super()._apply(fn, recurse=recurse)
@@ -246,61 +264,69 @@ class DualViewDecoder(nn.Module):
         return self.train()
 
     def _rotary(self, positions: Tensor, dtype):
-        phase = positions.float()[..., None] * self.frequencies
-        phase = torch.cat((phase, phase), -1)[:, None]
-        return phase.cos().to(dtype), phase.sin().to(dtype)
+        angles = positions.float().unsqueeze(-1) * self.frequencies
+        angles = angles.repeat(*([1] * (angles.ndim - 1)), 2).unsqueeze(1)
+        return angles.cos().to(dtype), angles.sin().to(dtype)
+
+    @staticmethod
+    def _causal(past: int, T: int, device) -> Tensor:
+        queries = torch.arange(past, past + T, device=device)
+        keys = torch.arange(past + T, device=device)
+        return (keys.unsqueeze(0) <= queries.unsqueeze(1)).unsqueeze(0).unsqueeze(0)
 
     def forward(self, tokens: Tensor, *, view: str = "ar", cache=None, positions=None, allowed=None,
                 logits_to_keep: int = 0, compute_logits: bool = True, capture_layer: int | None = None
                 ) -> BackboneOutput:
-        if view not in ("ar", "draft"):
-            raise ValueError("view must be ar or draft")
-        if tokens.ndim != 2 or tokens.shape[1] < 1:
-            raise ValueError("nonempty tokens[batch, time] required")
-        if capture_layer is not None and (view != "draft" or not 0 <= capture_layer < len(self.layers)):
-            raise ValueError("draft capture requires a valid layer boundary")
-        B, T = tokens.shape
+        if view not in VIEWS:
+            raise ValueError(f"view {view!r} is not one of {VIEWS}")
+        if tokens.ndim != 2 or tokens.shape[1] == 0:
+            raise ValueError("tokens must be a non-empty [batch, time] tensor")
+        if capture_layer is not None and not (view == "draft" and 0 <= capture_layer < len(self.layers)):
+            raise ValueError("a boundary is captured only in the draft view, at an existing layer")
+        T = tokens.shape[1]
         past = cache_length(cache)
         if positions is None:
-            positions = torch.arange(past, past + T, device=tokens.device)[None]
+            positions = torch.arange(past, past + T, device=tokens.device).unsqueeze(0)
         if allowed is None and view == "ar":
-            q = torch.arange(past, past + T, device=tokens.device)
-            allowed = (torch.arange(past + T, device=tokens.device)[None] <= q[:, None])[None, None]
+            allowed = self._causal(past, T, tokens.device)
         h = self.embedding(tokens)
         rotary = self._rotary(positions, h.dtype)
-        new_cache, boundary = [], None
+        written, boundary = [], None
         for i, layer in enumerate(self.layers):
             if i == capture_layer:
                 boundary = DraftBoundary(h, rotary, allowed, i, past)
             h, kv = layer(h, view, None if cache is None else cache[i], rotary, allowed)
-            if view == "ar":
-                new_cache.append(kv)
+            written.append(kv)
         h = self.norm(h)
-        rows = h[:, -logits_to_keep:] if logits_to_keep else h
-        logits = self.head(rows) if compute_logits else None
-        return BackboneOutput(h, tuple(new_cache) if view == "ar" else cache, logits, boundary)
+        logits = None
+        if compute_logits:
+            logits = self.head(h[:, -logits_to_keep:] if logits_to_keep else h)
+        # the draft view reads the history but never extends it
+        return BackboneOutput(h, tuple(written) if view == "ar" else cache, logits, boundary)
 
     def forward_suffix(self, boundary: DraftBoundary, *, cache=None, logit_range=None, draft_weights=None
                        ) -> BackboneOutput:
-        """Replay the draft view from a frozen boundary; overrides carry master weights."""
+        """Replay the draft view from a frozen boundary; overrides supply master draft weights."""
         if cache_length(cache) != boundary.history_length:
-            raise ValueError("matching historical cache required")
-        overrides = draft_weights or {}
-        allowed_keys = {f"layers.{i}.attention.draft.{n}" for i in range(boundary.start_layer, len(self.layers))
-                        for n, _ in self.layers[i].attention.draft.named_parameters()}
-        if overrides.keys() - allowed_keys:
-            raise ValueError("suffix overrides are restricted to draft attention parameters")
+            raise ValueError("the replay needs the cache the boundary was captured with")
+        overrides = dict(draft_weights or {})
+        start = boundary.start_layer
+        replayed = list(enumerate(self.layers))[start:]
+        legal = {f"layers.{i}.attention.draft.{name}" for i, layer in replayed
+                 for name, _ in layer.attention.draft.named_parameters()}
+        if set(overrides) - legal:
+            raise ValueError("suffix overrides may only replace draft attention parameters of replayed layers")
         h = boundary.hidden
-        for off, layer in enumerate(self.layers[boundary.start_layer:]):
-            prefix = f"layers.{boundary.start_layer + off}."
-            w = {n[len(prefix):]: v for n, v in overrides.items() if n.startswith(prefix)}
-            args = (h, "draft", None if cache is None else cache[off], boundary.rotary, boundary.allowed)
-            h, _ = torch.func.functional_call(layer, w, args) if w else layer(*args)
+        for offset, (i, layer) in enumerate(replayed):
+            prefix = f"layers.{i}."
+            local = {name[len(prefix):]: value for name, value in overrides.items() if name.startswith(prefix)}
+            args = (h, "draft", None if cache is None else cache[offset], boundary.rotary, boundary.allowed)
+            h, _ = torch.func.functional_call(layer, local, args) if local else layer(*args)
         h = self.norm(h)
         rows = h if logit_range is None else h[:, logit_range[0]:logit_range[1]]
         return BackboneOutput(h, cache, self.head(rows))
 
 
 def draft_block_mask(history: int, block: int, device) -> Tensor:
-    """Draft view mask: the block sees the whole history and itself in both directions."""
+    """Draft view visibility: every block row sees the whole history and the whole block."""
     return torch.ones(1, 1, block, history + block, dtype=torch.bool, device=device)
