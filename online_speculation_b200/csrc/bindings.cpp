@@ -97,6 +97,76 @@ void gemm(Tensor w, Tensor x, Tensor out, c10::optional<Tensor> bias, c10::optio
   check(osb::gemm_launch(p, at::cuda::getCurrentCUDAStream()), "tcgen05 gemm");
 }
 
+// Vocabulary-head scoring without stored logits: the tcgen05 GEMM h[N, K] @ w[V, K]^T
+// runs with the row-statistics epilogue into `part` ([N, ceil(V / 128), 4] fp32), then
+// one warp per row folds the partials.  Outputs may be undefined tensors.
+void head_stats(Tensor w, Tensor x, c10::optional<Tensor> inv_temp, c10::optional<Tensor> targets, Tensor part,
+                Tensor target_logit, c10::optional<Tensor> lse1, c10::optional<Tensor> lseT,
+                c10::optional<Tensor> logp, c10::optional<Tensor> logq, Tensor status) {
+  CHECK_CUDA(w);
+  CHECK_CUDA(x);
+  CHECK_DT(w, torch::kBFloat16);
+  CHECK_DT(x, torch::kBFloat16);
+  CHECK_ROWS(w);
+  CHECK_ROWS(x);
+  TORCH_CHECK(w.size(1) == x.size(1), "reduction dimensions differ");
+  const int V = w.size(0), N = x.size(0), K = w.size(1);
+  const int tiles = (V + 127) / 128;
+  CHECK_DT(part, torch::kFloat32);
+  TORCH_CHECK(part.is_contiguous() && part.numel() >= static_cast<long long>(N) * tiles * 4,
+              "part must hold [N, ceil(V / 128), 4] floats");
+  CHECK_DT(target_logit, torch::kFloat32);
+  TORCH_CHECK(target_logit.numel() >= N, "target_logit needs one float per row");
+  for (const c10::optional<Tensor>* o : {&lse1, &lseT, &logp, &logq})
+    if (o->has_value() && (*o)->defined()) {
+      CHECK_DT((**o), torch::kFloat32);
+      TORCH_CHECK((*o)->numel() >= N && (*o)->is_contiguous(), "outputs need one float per row");
+    }
+  if (inv_temp.has_value() && inv_temp->defined()) {
+    CHECK_DT((*inv_temp), torch::kFloat32);
+    TORCH_CHECK(inv_temp->numel() >= N && inv_temp->is_contiguous(), "inv_temp needs one float per row");
+  }
+  if (targets.has_value() && targets->defined()) {
+    CHECK_DT((*targets), torch::kInt32);
+    TORCH_CHECK(targets->numel() >= N && targets->is_contiguous(), "targets need one int32 per row");
+  }
+  CHECK_DT(status, torch::kInt32);
+  c10::cuda::CUDAGuard guard(w.device());
+  osb::GemmProblem p{};
+  p.w = bf(w);
+  p.ldw = w.stride(0);
+  p.x = bf(x);
+  p.ldx = x.stride(0);
+  p.M = V;
+  p.N = N;
+  p.K = K;
+  p.out = part.data_ptr();     // not written in statistics mode
+  p.ldo = 0;
+  p.out_f32 = 1;
+  p.epilogue = 2;
+  p.allow_split = 0;
+  p.status = status.data_ptr<int>();
+  p.stat_inv_temp = ptr_or_null<const float>(inv_temp);
+  p.stat_targets = ptr_or_null<const int>(targets);
+  p.stat_part = part.data_ptr<float>();
+  p.stat_target_logit = target_logit.data_ptr<float>();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  check(osb::gemm_launch(p, stream), "tcgen05 head statistics gemm");
+  osb::HeadStatsArgs a{};
+  a.part = part.data_ptr<float>();
+  a.tiles = tiles;
+  a.rows = N;
+  a.V = V;
+  a.inv_temp = p.stat_inv_temp;
+  a.targets = p.stat_targets;
+  a.target_logit = target_logit.data_ptr<float>();
+  a.lse1 = ptr_or_null<float>(lse1);
+  a.lseT = ptr_or_null<float>(lseT);
+  a.logp = ptr_or_null<float>(logp);
+  a.logq = ptr_or_null<float>(logq);
+  check(osb::head_stats_merge_launch(a, stream), "head statistics merge");
+}
+
 void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_start, Tensor q_len, Tensor kv_len,
                Tensor mode, Tensor tile_seq, Tensor tile_row0, int64_t tile_rows, int64_t kv_splits, Tensor out,
                double scale, Tensor status) {
@@ -206,8 +276,26 @@ void page_copy(Tensor cache, Tensor pairs) {
         "page_copy");
 }
 
+// Per-row truncation arrays of the sampler / scorer (int32 top-k, float32 top-p; either optional).
+static void set_truncation(const c10::optional<Tensor>& top_k, const c10::optional<Tensor>& top_p, int64_t rows,
+                           const int*& k_out, const float*& p_out) {
+  if (top_k.has_value() && top_k->defined()) {
+    CHECK_CUDA((*top_k));
+    CHECK_DT((*top_k), torch::kInt32);
+    TORCH_CHECK(top_k->is_contiguous() && top_k->numel() >= rows, "top_k needs one int32 per row");
+    k_out = top_k->data_ptr<int>();
+  }
+  if (top_p.has_value() && top_p->defined()) {
+    CHECK_CUDA((*top_p));
+    CHECK_DT((*top_p), torch::kFloat32);
+    TORCH_CHECK(top_p->is_contiguous() && top_p->numel() >= rows, "top_p needs one float32 per row");
+    p_out = top_p->data_ptr<float>();
+  }
+}
+
 void sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor uniforms, Tensor tokens, c10::optional<Tensor> logq,
-            c10::optional<Tensor> logp, c10::optional<Tensor> arith, c10::optional<Tensor> next_uniforms) {
+            c10::optional<Tensor> logp, c10::optional<Tensor> arith, c10::optional<Tensor> next_uniforms,
+            c10::optional<Tensor> top_k, c10::optional<Tensor> top_p) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
   CHECK_DT(logits, torch::kFloat32);
@@ -231,12 +319,14 @@ void sample(Tensor logits, c10::optional<Tensor> inv_temp, Tensor uniforms, Tens
                 "next_uniforms must have the stride of uniforms");
     a.next_uniforms = next_uniforms->data_ptr<double>();
   }
+  set_truncation(top_k, top_p, logits.size(0), a.top_k, a.top_p);
   check(osb::sample_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "sample");
 }
 
 void row_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tensor> targets,
                c10::optional<Tensor> lse1, c10::optional<Tensor> lseT, c10::optional<Tensor> logp,
-               c10::optional<Tensor> logq, c10::optional<Tensor> split_part, c10::optional<Tensor> split_count) {
+               c10::optional<Tensor> logq, c10::optional<Tensor> split_part, c10::optional<Tensor> split_count,
+               c10::optional<Tensor> top_k, c10::optional<Tensor> top_p) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
   CHECK_DT(logits, torch::kFloat32);
@@ -260,6 +350,7 @@ void row_stats(Tensor logits, c10::optional<Tensor> inv_temp, c10::optional<Tens
     a.part = split_part->data_ptr<float>();
     a.count = split_count->data_ptr<int>();
   }
+  set_truncation(top_k, top_p, logits.size(0), a.top_k, a.top_p);
   check(osb::row_stats_launch(a, logits.size(0), at::cuda::getCurrentCUDAStream()), "row_stats");
 }
 
@@ -768,6 +859,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels and C++ runtime of online_speculation_b200";
   m.def("gemm", &gemm);
   m.def("gemm_push", &gemm_push);
+  m.def("head_stats", &head_stats);
   m.def("allreduce_pushed_add_rmsnorm", &allreduce_pushed_add_rmsnorm);
   m.def("attention", &attention);
   m.def("rmsnorm", &rmsnorm);

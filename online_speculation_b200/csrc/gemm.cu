@@ -22,7 +22,8 @@
 //    them and runs the epilogue.  No CTA ever waits on another one.
 //  * Epilogues: bias, residual add (in-place hidden += ...), SwiGLU of an
 //    interleaved gate/up weight ([64 gate rows | 64 up rows] per tile), fp32 or
-//    bf16 output.
+//    bf16 output; or row statistics (per-tile max / sum exp at T = 1 and at 1/T
+//    plus the target logit) for vocabulary-head scoring without storing logits.
 //  * TMA loads are plain tiled loads (no cluster multicast).
 #include "common.cuh"
 #include "gemm.h"
@@ -51,7 +52,11 @@ struct Args {
   const __nv_bfloat16* residual;
   long long ldr;
   const __nv_bfloat16* bias;
-  int epilogue;         // 0 linear, 1 swiglu
+  int epilogue;         // 0 linear, 1 swiglu, 2 row statistics (no output tile)
+  const float* stat_inv_temp;
+  const int* stat_targets;
+  float4* stat_part;
+  float* stat_target_logit;
   int out_f32;
   int vec_ok;           // output / residual rows are 16-byte aligned
   int cluster;          // >1: split-K over a thread-block cluster, reduced through DSMEM
@@ -242,6 +247,67 @@ __device__ __forceinline__ void finish_chunk(const Args& a, const float (&v)[32]
       else
         put_bf16(a, off, val);
     }
+  }
+  named_barrier(bar, 128);
+}
+
+
+// Row-statistics epilogue of one 32-token chunk (vocabulary head scoring): the
+// logits never leave the SM.  After the transpose, four threads share a token and
+// take 32 weight rows each; they reduce (max, sum exp, sum exp at 1/T) and merge
+// through two lane shuffles (lanes 4j..4j+3 hold token j), and the partial of the
+// tile goes out as one 16-byte store.  The thread whose rows hold the token's
+// target writes its logit.
+__device__ __forceinline__ void merge_stats(float& m, float& s1, float& sT, float m2, float s12, float sT2,
+                                            float invT) {
+  const float hi = fmaxf(m, m2);
+  if (hi == -INFINITY) return;
+  const float a = m == -INFINITY ? 0.0f : expf(m - hi), b = m2 == -INFINITY ? 0.0f : expf(m2 - hi);
+  const float aT = m == -INFINITY ? 0.0f : expf((m - hi) * invT), bT = m2 == -INFINITY ? 0.0f : expf((m2 - hi) * invT);
+  s1 = s1 * a + s12 * b;
+  sT = sT * aT + sT2 * bT;
+  m = hi;
+}
+
+template <int BN>
+__device__ __forceinline__ void stats_chunk(const Args& a, const float (&v)[32], int tm, int row0, int row_end,
+                                            int chunk, int r, float* stage, int ep_tid, int bar) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) stage[j * (kBM + 4) + r] = v[j];
+  named_barrier(bar, 128);
+  const int j = ep_tid >> 2, q = ep_tid & 3;
+  const int t = row0 + chunk * 32 + j;
+  const int f = tm * kBM + q * 32;                 // first weight row of this thread's quarter
+  const int nf = min(32, a.M - f);
+  const float* row = stage + j * (kBM + 4) + q * 32;
+  const bool live = t < row_end;
+  const float invT = (live && a.stat_inv_temp != nullptr) ? a.stat_inv_temp[t] : 1.0f;
+  float m = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < 32; ++e)
+    if (e < nf) m = fmaxf(m, row[e]);
+  float s1 = 0.0f, sT = 0.0f;
+  if (m != -INFINITY) {
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      if (e < nf) {
+        const float d = row[e] - m;
+        s1 += expf(d);
+        sT += expf(d * invT);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s12 = __shfl_xor_sync(0xffffffffu, s1, o);
+    const float sT2 = __shfl_xor_sync(0xffffffffu, sT, o);
+    merge_stats(m, s1, sT, m2, s12, sT2, invT);
+  }
+  if (live && q == 0) a.stat_part[static_cast<long long>(t) * a.tiles_m + tm] = make_float4(m, s1, sT, 0.0f);
+  if (live && a.stat_targets != nullptr && a.stat_target_logit != nullptr) {
+    const int tg = a.stat_targets[t] - f;
+    if (tg >= 0 && tg < nf) a.stat_target_logit[t] = row[tg];
   }
   named_barrier(bar, 128);
 }
@@ -525,7 +591,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
           tmem_ld32(t_acc + c * 32, v);
           if (ep_tid == 0 && c < 8) trace_stamp(a, 8 + 2 * c);
-          finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, gstage, ep_tid, gbar);
+          if (a.epilogue == 2)
+            stats_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, gstage, ep_tid, gbar);
+          else
+            finish_chunk<BN>(a, v, tm, tc.row0, tc.row_end, c, r, gstage, ep_tid, gbar);
           if (ep_tid == 0 && c < 8) trace_stamp(a, 9 + 2 * c);
         }
         tc_fence_before();
@@ -695,7 +764,8 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
   a.splits = 1;
   a.kb_per_split = a.k_blocks;
   a.cluster = 1;
-  if (p.allow_split && p.split_mode == 0 && tiles < sms) {
+  const bool may_split = p.allow_split && p.epilogue != 2;   // statistics need whole accumulators
+  if (may_split && p.split_mode == 0 && tiles < sms) {
     // Split-K across a thread-block cluster (2, 4 or 8 CTAs), reduced through DSMEM.
     // Only cluster sizes whose clusters all fit on the GPU at once are used, so
     // the launch is a single wave.
@@ -728,7 +798,7 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
       return cudaLaunchKernelEx(&cfg, gemm_tn_kernel<BN>, ma, mb, a);
     }
   }
-  if (p.allow_split && p.split_mode == 1 && tiles < sms && p.workspace != nullptr) {
+  if (may_split && p.split_mode == 1 && tiles < sms && p.workspace != nullptr) {
     const GemmPlan plan = gemm_workspace_plan(p.M, p.N, p.K, sms);
     if (plan.bn == BN && plan.splits > 1 && plan.workspace_floats <= p.workspace_floats &&
         tiles <= p.counter_slots) {
@@ -880,6 +950,9 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
       (reinterpret_cast<uintptr_t>(p.x) % 16))
     return cudaErrorInvalidValue;  // TMA needs 16-byte aligned rows
   if (p.epilogue == 1 && (p.M % kBM)) return cudaErrorInvalidValue;
+  if (p.epilogue == 2 && (p.stat_part == nullptr || p.group_tiles != nullptr || p.push_world > 0 ||
+                          (reinterpret_cast<uintptr_t>(p.stat_part) % 16)))
+    return cudaErrorInvalidValue;
   Args a{};
   a.M = p.M;
   a.N = p.N;
@@ -900,6 +973,10 @@ cudaError_t gemm_launch(const GemmProblem& p, cudaStream_t stream) {
   a.ldr = p.ldr;
   a.bias = p.bias;
   a.epilogue = p.epilogue;
+  a.stat_inv_temp = p.stat_inv_temp;
+  a.stat_targets = p.stat_targets;
+  a.stat_part = reinterpret_cast<float4*>(p.stat_part);
+  a.stat_target_logit = p.stat_target_logit;
   a.out_f32 = p.out_f32;
   a.workspace = p.workspace;
   a.counters = p.counters;

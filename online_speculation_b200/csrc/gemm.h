@@ -17,7 +17,16 @@ struct GemmProblem {
   const __nv_bfloat16* bias;      // [M] or null
   const __nv_bfloat16* residual;  // same layout as out (bf16) or null; may alias out
   long long ldr;
-  int epilogue;                   // 0 linear, 1 swiglu on [64 gate | 64 up] row tiles
+  int epilogue;                   // 0 linear, 1 swiglu on [64 gate | 64 up] row tiles, 2 row statistics
+  // Row statistics (epilogue 2, the vocabulary head without stored logits): for every
+  // token t and weight-row tile tm the kernel writes stat_part[t * tiles_m + tm] =
+  // {max, sum exp(l - max), sum exp((l - max) * inv_temp[t]), 0} over the tile's rows,
+  // and the tile that holds row targets[t] writes that logit to target_logit[t].
+  // `out` is not written.  head_stats_merge_launch (sampling.h) folds the partials.
+  const float* stat_inv_temp;     // [N] or null (T = 1)
+  const int* stat_targets;        // [N] or null
+  float* stat_part;               // [N, ceil(M / 128), 4]
+  float* stat_target_logit;       // [N] or null
   int allow_split;
   int split_mode;                 // 0: split-K over a cluster (DSMEM reduction); 1: global workspace
   float* workspace;               // split-K partials

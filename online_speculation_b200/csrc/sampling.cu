@@ -57,9 +57,13 @@ __device__ __forceinline__ float4 uniform4(unsigned long long seed, uint32_t str
 // monotone bit pattern of the float in the high word, complemented column in
 // the low word, top bit flipped so that a signed 64-bit maximum (NCCL MAX on
 // int64) picks the same winner as the unsharded argmax.
+__device__ __forceinline__ uint32_t order_key(float x) {
+  const uint32_t b = __float_as_uint(x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 __device__ __forceinline__ unsigned long long pack_argmax_key(float score, int column) {
-  const uint32_t b = __float_as_uint(score);
-  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  const uint32_t ord = order_key(score);
   const unsigned long long k =
       (static_cast<unsigned long long>(ord) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(column));
   return k ^ 0x8000000000000000ull;
@@ -187,6 +191,118 @@ __device__ double block_exclusive_scan(double v, double& total) {
   return res;
 }
 
+
+// ------------------------------------------------------ truncated policies ----
+// A truncated policy keeps the columns whose tempered logit z = l / T is at least
+// a per-row threshold key: the k-th largest z (top-k), then, inside that set, the
+// smallest z at which the descending cumulative mass first exceeds top_p of the
+// set's mass (top-p).  Columns tied with the threshold all stay.  The threshold is
+// found by a radix select from the most significant byte of the order-preserving
+// key of z: per byte one pass histograms the columns that share the bytes fixed so
+// far (counts for top-k, masses exp(z - zmax) for top-p) and one warp scans the 256
+// bins from the top for the bin where the running total reaches the target.
+// Histogram bins are fp32 (counts are exact below 2^24 columns).
+
+template <bool kMass>
+__device__ uint32_t radix_select_desc(const float* __restrict__ row, int V, float invT, float zmax, uint32_t keep_from,
+                                      float target) {
+  __shared__ float hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ float s_target;
+  uint32_t prefix = 0, fixed = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0.0f;
+    __syncthreads();
+    for (int v = threadIdx.x; v < V; v += blockDim.x) {
+      const float z = row[v] * invT;
+      const uint32_t key = order_key(z);
+      if (key < keep_from || (key & fixed) != prefix) continue;
+      atomicAdd(&hist[(key >> shift) & 0xFFu], kMass ? expf(z - zmax) : 1.0f);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      float mine[8];
+      float local = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        mine[j] = hist[255 - 8 * lane - j];   // lane 0 holds the top bins
+        local += mine[j];
+      }
+      float inc = local;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += n;
+      }
+      const bool reached = kMass ? inc > target : inc >= target;
+      const unsigned crossing = __ballot_sync(0xffffffffu, reached);
+      const unsigned nonempty = __ballot_sync(0xffffffffu, local > 0.0f);
+      // no bin reaches the target (rounding): keep every column of this prefix
+      const bool keep_all = crossing == 0u;
+      const int owner = keep_all ? (nonempty ? 31 - __clz(nonempty) : 31) : __ffs(crossing) - 1;
+      if (lane == owner) {
+        float before = inc - local;
+        int pick = 7;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const bool hit = keep_all ? false : (kMass ? before + mine[j] > target : before + mine[j] >= target);
+          if (hit) {
+            pick = j;
+            break;
+          }
+          if (keep_all && mine[j] > 0.0f) pick = j;
+          before += keep_all ? 0.0f : mine[j];
+        }
+        s_prefix = prefix | (static_cast<uint32_t>(255 - 8 * lane - pick) << shift);
+        s_target = target - before;
+      }
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    target = s_target;
+    fixed |= 0xFFu << shift;
+    __syncthreads();
+  }
+  return prefix;
+}
+
+// Block sum of exp(z - zmax) over columns with key >= keep_from (all threads get it).
+__device__ float kept_mass(const float* __restrict__ row, int V, float invT, float zmax, uint32_t keep_from) {
+  __shared__ float red[32];
+  float s = 0.0f;
+  for (int v = threadIdx.x; v < V; v += blockDim.x) {
+    const float z = row[v] * invT;
+    if (order_key(z) >= keep_from) s += expf(z - zmax);
+  }
+  s = warp_reduce_sum(s);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0f;
+    t = warp_reduce_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float total = red[0];
+  __syncthreads();
+  return total;
+}
+
+// Threshold key and log-normaliser of the kept set of a truncated policy.
+// zmax = max_v l_v * invT.  Returns keep_from 0 (everything kept) when neither filter binds.
+__device__ void truncation(const float* __restrict__ row, int V, float invT, float zmax, int top_k, float top_p,
+                           uint32_t& keep_from, float& lse_kept) {
+  keep_from = 0u;
+  if (top_k > 0 && top_k < V) keep_from = radix_select_desc<false>(row, V, invT, zmax, 0u, static_cast<float>(top_k));
+  float mass = kept_mass(row, V, invT, zmax, keep_from);
+  if (top_p < 1.0f) {
+    keep_from = radix_select_desc<true>(row, V, invT, zmax, keep_from, top_p * mass);
+    mass = kept_mass(row, V, invT, zmax, keep_from);
+  }
+  lse_kept = zmax + logf(mass);
+}
+
 __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -195,14 +311,22 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
   float mx, lse1, lseT;
   row_stats(row, a.V, invT, mx, lse1, lseT);
+  const int top_k = a.top_k ? a.top_k[r] : 0;
+  const float top_p = a.top_p ? a.top_p[r] : 1.0f;
+  uint32_t keep_from = 0u;
+  if ((top_k > 0 && top_k < a.V) || top_p < 1.0f) truncation(row, a.V, invT, mx * invT, top_k, top_p, keep_from, lseT);
+  // policy mass of column v: exp(z - lseT) on the kept columns, zero elsewhere
+  auto mass = [&](int v) -> double {
+    const float z = row[v] * invT;
+    return order_key(z) >= keep_from ? static_cast<double>(expf(z - lseT)) : 0.0;
+  };
   const double u = a.uniforms[r * a.uniform_stride];
   // contiguous segment per thread
   const int seg = (a.V + blockDim.x - 1) / blockDim.x;
   const int b0 = min(a.V, static_cast<int>(threadIdx.x) * seg);
   const int b1 = min(a.V, b0 + seg);
-  const float zoff = lseT;
   double s = 0.0;
-  for (int v = b0; v < b1; ++v) s += static_cast<double>(expf(row[v] * invT - zoff));
+  for (int v = b0; v < b1; ++v) s += mass(v);
   double total;
   const double excl = block_exclusive_scan(s, total);
   __shared__ int chosen;
@@ -213,7 +337,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     double c = excl;
     int tok = b1 - 1;
     for (int v = b0; v < b1; ++v) {
-      c += static_cast<double>(expf(row[v] * invT - zoff));
+      c += mass(v);
       if (c >= u) {
         tok = v;
         break;
@@ -228,9 +352,9 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     const int tok = chosen;
     if (b0 <= tok && tok < b1) {
       double c = excl;
-      for (int v = b0; v < tok; ++v) c += static_cast<double>(expf(row[v] * invT - zoff));
+      for (int v = b0; v < tok; ++v) c += mass(v);
       code_lo = c;
-      code_mass = static_cast<double>(expf(row[tok] * invT - zoff));
+      code_mass = mass(tok);
     }
     __syncthreads();
   }
@@ -238,7 +362,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     const int tok = chosen;
     a.tokens[r] = tok;
     const float l = row[tok];
-    if (a.logq) a.logq[r] = l * invT - lseT;
+    // a column outside the kept set is only reached when u exceeds the fp64 total (it has no mass)
+    if (a.logq) a.logq[r] = order_key(l * invT) >= keep_from ? l * invT - lseT : -INFINITY;
     if (a.logp) a.logp[r] = l - lse1;
     if (a.arith != nullptr && a.next_uniforms != nullptr && a.arith[r]) {
       double nu = code_mass > 0.0 ? (u - code_lo) / code_mass : 0.5;
@@ -255,6 +380,7 @@ __global__ void __launch_bounds__(kThreads) row_stats_kernel(RowStatsArgs a) {
   const float* row = a.logits + r * a.ld;
   const float invT = a.inv_temp ? a.inv_temp[r] : 1.0f;
   float lse1, lseT;
+  uint32_t keep_from = 0u;
   if (a.split > 1) {
     // This CTA's column chunk; the last CTA of the row to arrive merges the chunks
     // in chunk order (independent of arrival order) and finishes the row.
@@ -283,6 +409,9 @@ __global__ void __launch_bounds__(kThreads) row_stats_kernel(RowStatsArgs a) {
   } else {
     float mx;
     row_stats(row, a.V, invT, mx, lse1, lseT);
+    const int top_k = a.top_k ? a.top_k[r] : 0;
+    const float top_p = a.top_p ? a.top_p[r] : 1.0f;
+    if ((top_k > 0 && top_k < a.V) || top_p < 1.0f) truncation(row, a.V, invT, mx * invT, top_k, top_p, keep_from, lseT);
   }
   if (threadIdx.x == 0) {
     if (a.lse1) a.lse1[r] = lse1;
@@ -291,7 +420,7 @@ __global__ void __launch_bounds__(kThreads) row_stats_kernel(RowStatsArgs a) {
       const int t = a.targets[r];
       const float l = (t >= 0 && t < a.V) ? row[t] : -INFINITY;
       if (a.logp) a.logp[r] = l - lse1;
-      if (a.logq) a.logq[r] = l * invT - lseT;
+      if (a.logq) a.logq[r] = (t >= 0 && t < a.V && order_key(l * invT) >= keep_from) ? l * invT - lseT : -INFINITY;
     }
   }
 }
@@ -519,7 +648,50 @@ __global__ void __launch_bounds__(kThreads) spec_verify_kernel(SpecArgs a) {
   }
 }
 
+
+// One warp folds one row's head-GEMM partials: lanes stride over the tiles in a
+// fixed order, then a butterfly merges the lanes, so the result does not depend
+// on scheduling.
+__global__ void __launch_bounds__(256) head_stats_merge_kernel(HeadStatsArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  if (row >= a.rows) return;
+  const float invT = a.inv_temp ? a.inv_temp[row] : 1.0f;
+  const float4* p = reinterpret_cast<const float4*>(a.part) + static_cast<long long>(row) * a.tiles;
+  MaxSum2 acc{-INFINITY, 0.0f, 0.0f};
+  for (int i = lane; i < a.tiles; i += 32) {
+    const float4 v = p[i];
+    acc = ms_merge(acc, MaxSum2{v.x, v.y, v.z}, invT);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const MaxSum2 other{__shfl_xor_sync(0xffffffffu, acc.m, o), __shfl_xor_sync(0xffffffffu, acc.s1, o),
+                        __shfl_xor_sync(0xffffffffu, acc.sT, o)};
+    acc = ms_merge(acc, other, invT);
+  }
+  if (lane != 0) return;
+  const float lse1 = acc.m + logf(acc.s1);
+  const float lseT = acc.m * invT + logf(acc.sT);
+  if (a.lse1) a.lse1[row] = lse1;
+  if (a.lseT) a.lseT[row] = lseT;
+  if (a.targets != nullptr) {
+    const int t = a.targets[row];
+    const float l = (t >= 0 && t < a.V) ? a.target_logit[row] : -INFINITY;
+    if (a.logp) a.logp[row] = l - lse1;
+    if (a.logq) a.logq[row] = l * invT - lseT;
+  }
+}
 }  // namespace
+
+cudaError_t head_stats_merge_launch(const HeadStatsArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return cudaSuccess;
+  if (a.part == nullptr || a.tiles <= 0 || (a.targets != nullptr && a.target_logit == nullptr))
+    return cudaErrorInvalidValue;
+  const int blocks = (a.rows * 32 + 255) / 256;
+  return launch_pdl(head_stats_merge_kernel, dim3(blocks), dim3(256), 0, stream, a);
+}
 
 cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
@@ -531,7 +703,8 @@ cudaError_t row_stats_launch(const RowStatsArgs& a0, int rows, cudaStream_t stre
   RowStatsArgs a = a0;
   a.split = 1;
   a.chunk = a.V;
-  if (a.part != nullptr && a.count != nullptr && rows <= kRowStatsSplitRows) {
+  const bool truncated = a.top_k != nullptr || a.top_p != nullptr;
+  if (!truncated && a.part != nullptr && a.count != nullptr && rows <= kRowStatsSplitRows) {
     // Few rows: about two CTAs per SM in total, at least 8192 columns per CTA.
     static int sms = 0;
     if (sms == 0) {

@@ -19,6 +19,11 @@ struct SampleArgs {
   // the rescaled point (u - c) / q_t to next_uniforms[r * uniform_stride].
   const int* arith;           // [rows] or null
   double* next_uniforms;      // or null
+  // Truncated policies (either may be null): top_k[r] > 0 keeps the k largest
+  // tempered logits (ties at the k-th kept), top_p[r] < 1 then keeps the
+  // smallest descending prefix of that set whose mass exceeds top_p[r].
+  const int* top_k;
+  const float* top_p;
 };
 
 struct RowStatsArgs {
@@ -31,6 +36,10 @@ struct RowStatsArgs {
   float* lseT;
   float* logp;
   float* logq;
+  // Truncated policies as in SampleArgs: logq and lseT are taken over the kept
+  // columns (a target outside them gets -inf); rows are not split.
+  const int* top_k;
+  const float* top_p;
   // Split rows (set by the launcher): `split` CTAs per row over `chunk` columns each;
   // partial (max, sum exp, sum exp at 1/T) go to part[row][chunk][3] and the last CTA
   // of a row to arrive (count[row]) merges them and resets its counter (zero at rest).
@@ -104,6 +113,23 @@ struct SpecArgs {
   const float* cand_logits;
   unsigned long long* keys;
 };
+
+// Fold the per-tile partials of a row-statistics head GEMM (GemmProblem epilogue 2)
+// into lse at T = 1 and at T and the target log-probabilities (one warp per row).
+struct HeadStatsArgs {
+  const float* part;          // [rows, tiles, 4] {max, sum exp, sum exp at 1/T, -}
+  int tiles;
+  int rows;
+  int V;
+  const float* inv_temp;      // [rows] or null
+  const int* targets;         // [rows] or null
+  const float* target_logit;  // [rows] (written by the GEMM for in-range targets)
+  float* lse1;                // each output may be null
+  float* lseT;
+  float* logp;
+  float* logq;
+};
+cudaError_t head_stats_merge_launch(const HeadStatsArgs& a, cudaStream_t stream);
 
 cudaError_t sample_launch(const SampleArgs& a, int rows, cudaStream_t stream);
 cudaError_t row_stats_launch(const RowStatsArgs& a, int rows, cudaStream_t stream);

@@ -15,9 +15,12 @@ the same contract (:mod:`online_speculation_b200.arllm.types`):
   rescales the code point on the device after every token (cumulative mass in
   vocabulary order), so the whole sequence is a deterministic function of one
   uniform.
-* ``score_batch`` scores continuations with the fused row-statistics kernel
-  (log-sum-exp at T = 1 and at the requested temperature plus the target
-  gather), never materialising a log-softmax.
+* ``score_batch`` packs many continuations into shared prefill forwards and
+  scores their rows with the head GEMM's row-statistics epilogue (log-sum-exp at
+  T = 1 and at the requested temperature plus the target logit), so no logits
+  row is stored.  Top-k / top-p policies are sampled and scored with the
+  truncated-policy path of the sampler kernels (radix-selected per-row
+  threshold), as in the reference's policy log-softmax.
 
 Prefix reuse: full 32-token pages are keyed by a chained hash of their tokens
 and kept (reference-counted) in a prefix cache, so requests that share a
@@ -166,6 +169,11 @@ class _DecodeGraph:
         self.carry_host = torch.zeros(B, dtype=torch.float64).pin_memory()
         self.it_host = torch.ones(B, dtype=torch.float32).pin_memory()
         self.inv_temp = torch.ones(B, dtype=torch.float32, device=dev)
+        # truncated policies per row (0 / 1 = off); the sampler reads them every step
+        self.topk_host = torch.zeros(B, dtype=torch.int32).pin_memory()
+        self.topp_host = torch.ones(B, dtype=torch.float32).pin_memory()
+        self.top_k = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.top_p = torch.ones(B, dtype=torch.float32, device=dev)
         G = r.q_slots // r.kv_slots
         tr = K.attention_tile_rows(G, B * r.kv_slots, self.mp * K.PAGE_SIZE)
         tiles = -(-G // tr)
@@ -207,7 +215,8 @@ class _DecodeGraph:
         for s in range(self.S):
             logits = r.forward(StepMeta(self.ids[s], self.pos[s], self.slots[s], self.plans[s], None))
             K.sample(logits, self.inv_temp, self.uni[s], tokens=self.ids[s + 1], logq=self.logq[s],
-                     logp=self.logp[s], arith=self.arith, next_uniforms=self.uni[s + 1])
+                     logp=self.logp[s], arith=self.arith, next_uniforms=self.uni[s + 1], top_k=self.top_k,
+                     top_p=self.top_p)
         self.result[:, :, 0].copy_(self.ids[1:])
         self.result[:, :, 1].copy_(self.logq)
         self.result[:, :, 2].copy_(self.logp)
@@ -217,6 +226,8 @@ class _DecodeGraph:
         self.uni[:self.S].copy_(self.uni_host, non_blocking=True)
         self.arith.copy_(self.arith_host, non_blocking=True)
         self.inv_temp.copy_(self.it_host, non_blocking=True)
+        self.top_k.copy_(self.topk_host, non_blocking=True)
+        self.top_p.copy_(self.topp_host, non_blocking=True)
         if self.graph is not None:
             self.graph.replay()
             self.backend.stats["graph_kernel_launches"] += self.kernels_per_replay
@@ -233,7 +244,8 @@ class EngineBackend:
 
     def __init__(self, runner: ModelRunner, *, model_id: str | None = None, max_batch: int = 64,
                  bos_token_id: int | None = None, use_graphs: bool = True, prefix_cache_pages: int | None = None,
-                 max_seq_tokens: int = 4096, prefill_tokens: int = 4096, decode_chunk: int = 16):
+                 max_seq_tokens: int = 4096, prefill_tokens: int = 4096, decode_chunk: int = 16,
+                 score_pack: int = 256):
         self.runner = runner
         self.cache: KVCache = runner.cache
         self._model_id = model_id or f"b200:{runner.cfg.name}"
@@ -241,6 +253,7 @@ class EngineBackend:
         self.bos_token_id = bos_token_id
         self.use_graphs = use_graphs
         self.decode_chunk = decode_chunk
+        self.score_pack = score_pack          # continuations scored per packed pass (bounds the KV it holds)
         self.max_pages = -(-(max_seq_tokens + decode_chunk) // PAGE) + 1
         self.prefill_tokens = min(prefill_tokens, runner.max_tokens)
         budget = prefix_cache_pages if prefix_cache_pages is not None else self.cache.num_pages // 2
@@ -279,10 +292,11 @@ class EngineBackend:
         return (self.bos_token_id,)
 
     @staticmethod
-    def _check_policy(s: SamplingConfig) -> None:
-        if not s.full_support:
-            raise NotImplementedError("the fused GPU sampler implements temperature policies; top-k/top-p "
-                                      "truncation is available on the CPU tabular backend")
+    def _truncation(s: SamplingConfig | None) -> tuple[int, float]:
+        """(top_k, top_p) of a policy in the sampler's per-row encoding (0 / 1 = off)."""
+        if s is None:
+            return 0, 1.0
+        return (0 if s.top_k is None else int(s.top_k)), float(s.top_p)
 
     def _open(self, tokens: tuple, *, keep_last: bool) -> tuple[int, int]:
         """KV sequence holding ``tokens`` (minus the last one when ``keep_last``).
@@ -369,7 +383,6 @@ class EngineBackend:
         act: list[_Active] = []
         opened = []
         for i, req in group:
-            self._check_policy(req.sampling)
             tokens = self._model_prefix(req.prefix)
             seq, tail = self._open(tokens, keep_last=True)
             opened.append((seq, tokens, tail))
@@ -407,6 +420,7 @@ class EngineBackend:
                     g.uni_host[:, b] = torch.from_numpy(np.ascontiguousarray(a.uniforms[t:t + S], dtype=np.float64))
                     g.arith_host[b] = 0
                 g.it_host[b] = 1.0 / a.request.sampling.temperature
+                g.topk_host[b], g.topp_host[b] = self._truncation(a.request.sampling)
             self.cache.manager.fill_table_np([a.seq for a in act], g.h_table[:n])
             if n < B:
                 g.h_slots[:, n:] = -1
@@ -416,6 +430,8 @@ class EngineBackend:
                 g.h_table[n:] = 0
                 g.uni_host[:, n:] = 0.5
                 g.arith_host[n:] = 0
+                g.topk_host[n:] = 0
+                g.topp_host[n:] = 1.0
             res = g.run()
             self.stats["decode_steps"] += S
             still = []
@@ -460,13 +476,94 @@ class EngineBackend:
         with self._lock:
             flat = []
             for req in requests:
-                if req.sampling is not None:
-                    self._check_policy(req.sampling)
                 for cont in req.continuations:
                     flat.append((self._model_prefix(req.prefix), tuple(cont), req.sampling))
-            out = [self._score_one(p, c, s) for p, c, s in flat]
+            out: list = [None] * len(flat)
+            packed = [i for i, (_, c, s) in enumerate(flat)
+                      if c and self.runner.comm.world == 1 and self._truncation(s) == (0, 1.0)]
+            for lo in range(0, len(packed), self.score_pack):
+                chunk = packed[lo:lo + self.score_pack]
+                for i, values in zip(chunk, self._score_packed([flat[i] for i in chunk])):
+                    out[i] = values
+            for i, (p, c, s) in enumerate(flat):
+                if out[i] is None:
+                    out[i] = self._score_one(p, c, s)
             self.stats["score_calls"] += 1
             return out
+
+    def _score_packed(self, work: list[tuple]) -> list[tuple[float, ...]]:
+        """Score many (prefix, continuation, full-support policy) items in packed forwards.
+
+        Every item reuses the cached full pages of its prefix, its remaining tokens
+        are prefilled together with the other items' (at most ``prefill_tokens`` per
+        forward, a sequence at most once per forward), and the scored rows go
+        through the fused head-statistics GEMM, so no logits row is stored.
+        """
+        r = self.runner
+        G = r.q_slots // r.kv_slots
+        values = [np.empty(len(c), dtype=np.float64) for _, c, _ in work]
+        segments, opened = [], []
+        for i, (prefix, cont, pol) in enumerate(work):
+            full = prefix + cont
+            first_row = len(prefix) - 1                  # position whose logits score cont[0]
+            pages, _ = self.prefix.lookup(full, first_row)
+            reused = len(pages) * PAGE
+            seq = self.cache.manager.adopt(pages, reused) if pages else self.cache.create()
+            self.stats["reused_prefix_tokens"] += reused
+            opened.append((seq, full))
+            inv = 1.0 if pol is None else 1.0 / pol.temperature
+            pos = reused
+            while pos < len(full) - 1:
+                n = min(len(full) - 1 - pos, self.prefill_tokens)
+                segments.append((i, seq, full, pos, n, first_row, inv))
+                pos += n
+        self.cache.flush_copies()
+        groups, chunk, used, seen = [], [], 0, set()
+        for seg in segments:
+            if chunk and (used + seg[4] > self.prefill_tokens or seg[1] in seen):
+                groups.append(chunk)
+                chunk, used, seen = [], 0, set()
+            chunk.append(seg)
+            used += seg[4]
+            seen.add(seg[1])
+        if chunk:
+            groups.append(chunk)
+        for grp in groups:
+            ids, pos, slots, qlens, kvlens, seqs = [], [], [], [], [], []
+            rows, targets, inv_t, where = [], [], [], []
+            offset = 0
+            for i, seq, full, start, n, first_row, inv in grp:
+                slots += self.cache.append(seq, n)
+                ids += list(full[start:start + n])
+                pos += list(range(start, start + n))
+                qlens.append(n)
+                kvlens.append(start + n)
+                seqs.append(seq)
+                for p in range(max(first_row, start), start + n):
+                    rows.append(offset + p - start)
+                    targets.append(full[p + 1])
+                    inv_t.append(inv)
+                    where.append((i, p - first_row))
+                offset += n
+            table = torch.zeros(len(grp), self.max_pages, dtype=torch.int32)
+            self.cache.fill_table(seqs, table)
+            meta = build_meta(r.device, table, ids, pos, slots, qlens, kvlens, [0] * len(grp), G,
+                              logit_rows=rows if rows else None, kv_heads=r.kv_slots)
+            self.stats["prefill_tokens"] += len(ids)
+            if not rows:
+                r.forward(meta, compute_logits=False)
+                continue
+            it = torch.tensor(inv_t, dtype=torch.float32).to(r.device, non_blocking=True)
+            tg = torch.tensor(targets, dtype=torch.int32).to(r.device, non_blocking=True)
+            _, _, _, logq = r.forward_stats(meta, it, tg)
+            got = logq.cpu().numpy()
+            for (i, k), v in zip(where, got):
+                values[i][k] = v
+            self.stats["scored_tokens"] += len(rows)
+        for seq, full in opened:
+            self._cache_pages(seq, full)
+            self.cache.release(seq)
+        return [tuple(float(x) for x in v) for v in values]
 
     def score_statistics_batch(self, requests: Sequence[ScoreRequest], *, confidence_top_k: int | None = None
                                ) -> list[SequenceScoreStatistics]:
@@ -530,6 +627,8 @@ class EngineBackend:
         first_row = len(prefix) - 1        # position whose logits score cont[0]
         values: list[float] = []
         it = torch.full((1,), 1.0 if sampling is None else 1.0 / sampling.temperature, device=r.device)
+        k_row, p_row = self._truncation(sampling)
+        truncated = k_row > 0 or p_row < 1.0
         # positions [start, len(full) - 1) still need KV; logits are needed for [first_row, len(full) - 1)
         if start > first_row:
             # the cached prefix already covers scored positions: recompute from the first scored row
@@ -558,7 +657,11 @@ class EngineBackend:
                 if stats_topk is not None:
                     values += [tuple(v) for v in K.score_stats(logits, itr, targets, stats_topk).tolist()]
                 else:
-                    _, _, logp, logq = K.row_stats(logits, itr, targets)
+                    cut = {}
+                    if truncated:
+                        cut = {"top_k": torch.full((len(rows),), k_row, dtype=torch.int32, device=r.device),
+                               "top_p": torch.full((len(rows),), p_row, dtype=torch.float32, device=r.device)}
+                    _, _, logp, logq = K.row_stats(logits, itr, targets, **cut)
                     values += (logp if sampling is None else logq).tolist()
             else:
                 r.forward(meta, compute_logits=False)

@@ -248,6 +248,23 @@ class ModelRunner:
             return self.logits(sel, None, normed=True, gather=gather)
         return self.logits(h, meta.logit_rows)
 
+    def forward_stats(self, meta: StepMeta, inv_temp: torch.Tensor | None, targets: torch.Tensor | None):
+        """Decoder forward that scores ``meta.logit_rows`` without materialising logits.
+
+        Returns fp32 (lse at T = 1, lse at T, log p and log q of ``targets``) per
+        selected row from the fused head-statistics GEMM (one tensor-parallel rank only).
+        """
+        if self.comm.world > 1:
+            raise ValueError("head statistics run on an unsharded vocabulary head")
+        T = meta.ids.numel()
+        h = self._buf("h", (T, self.cfg.hidden_size))
+        self.embed(meta.ids, h)
+        self.layer_stack(h, meta, range(self.cfg.num_hidden_layers))
+        sel = h if meta.logit_rows is None else self._index_rows(h, meta.logit_rows)
+        x = K.rmsnorm(sel, self.w.final_norm, self.cfg.rms_norm_eps,
+                      out=self._buf("xl", (sel.shape[0], self.cfg.hidden_size)))
+        return K.head_stats(x, self.w.head, inv_temp, targets)
+
     @property
     def vocab_shard(self) -> "K.VocabShard | None":
         """This rank's vocabulary slice for vocabulary-parallel sampling (None without TP)."""

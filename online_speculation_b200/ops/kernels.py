@@ -318,14 +318,17 @@ def attention_reference(q, k_cache, v_cache, host, scale):
 
 
 # ---------------------------------------------------------------- sampling --
-def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None, arith=None, next_uniforms=None):
+def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None, arith=None, next_uniforms=None,
+           top_k=None, top_p=None):
     """Inverse-CDF sampling (float64 prefix sums) at per-row temperature.
 
     Returns (tokens int32, log q under the policy, log p at temperature one).
     With ``arith`` (int32 per row) and ``next_uniforms``, every flagged row is
     an arithmetic-coding draw: its uniform is a code point and the rescaled
     point for the next token, (u - cumulative mass before the token) / mass of
-    the token, is written to ``next_uniforms``.
+    the token, is written to ``next_uniforms``.  ``top_k`` (int32 per row, 0 =
+    off) and ``top_p`` (float32 per row, 1 = off) truncate the policy
+    (:func:`truncated_log_policy`); log p stays the full-support T = 1 law.
     """
     rows = logits.shape[0]
     dev = logits.device
@@ -333,9 +336,9 @@ def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None, ari
     logq = logq if logq is not None else torch.empty(rows, dtype=torch.float32, device=dev)
     logp = logp if logp is not None else torch.empty(rows, dtype=torch.float32, device=dev)
     if logits.is_cuda:
-        _ext.require().sample(logits, inv_temp, uniforms, tokens, logq, logp, arith, next_uniforms)
+        _ext.require().sample(logits, inv_temp, uniforms, tokens, logq, logp, arith, next_uniforms, top_k, top_p)
         return tokens, logq, logp
-    t, q, p, nxt = sample_reference(logits, inv_temp, uniforms, with_code=True)
+    t, q, p, nxt = sample_reference(logits, inv_temp, uniforms, with_code=True, top_k=top_k, top_p=top_p)
     tokens.copy_(t)
     logq.copy_(q)
     logp.copy_(p)
@@ -345,10 +348,39 @@ def sample(logits, inv_temp, uniforms, *, tokens=None, logq=None, logp=None, ari
     return tokens, logq, logp
 
 
-def sample_reference(logits, inv_temp, uniforms, *, with_code=False):
+def truncated_log_policy(z, top_k=None, top_p=None):
+    """log softmax of tempered logits ``z`` [rows, V] under per-row top-k / top-p truncation (fp32 oracle).
+
+    top-k keeps every column at least as large as the k-th largest; top-p then sorts
+    the kept columns in descending order and keeps each one whose preceding mass
+    (renormalised over the kept set) is at most top_p, the rule of
+    src/inference_scaling/arllm/backends/transformers_backend.py:323-348.
+    ``top_k`` / ``top_p`` are per-row tensors (0 / 1 disable a row's filter) or None.
+    """
+    z = z.float().clone()
+    rows, V = z.shape
+    if top_k is not None:
+        k = top_k.to(torch.long).cpu().tolist()
+        for r in range(rows):
+            if 0 < k[r] < V:
+                kth = torch.topk(z[r], k[r]).values[-1]
+                z[r] = z[r].masked_fill(z[r] < kth, float("-inf"))
+    if top_p is not None:
+        p = top_p.float().cpu().tolist()
+        for r in range(rows):
+            if p[r] < 1.0:
+                ordered, order = torch.sort(z[r], descending=True)
+                mass = torch.softmax(ordered, -1)
+                drop = mass.cumsum(-1) > p[r]
+                drop = torch.cat((drop.new_zeros(1), drop[:-1]))
+                z[r] = z[r].masked_fill(torch.zeros_like(drop).scatter(0, order, drop), float("-inf"))
+    return z.log_softmax(-1)
+
+
+def sample_reference(logits, inv_temp, uniforms, *, with_code=False, top_k=None, top_p=None):
     x = logits.float()
     it = inv_temp.float()[:, None] if inv_temp is not None else torch.ones(x.shape[0], 1, device=x.device)
-    log_q = (x * it).log_softmax(-1)
+    log_q = truncated_log_policy(x * it, top_k, top_p)
     log_p = x.log_softmax(-1)
     mass = log_q.exp().double()
     cumulative = mass.cumsum(-1)
@@ -364,8 +396,12 @@ def sample_reference(logits, inv_temp, uniforms, *, with_code=False):
     return out + (nxt,)
 
 
-def row_stats(logits, inv_temp=None, targets=None):
-    """Per-row lse at T=1 and at T, plus log p / log q of ``targets`` (scoring)."""
+def row_stats(logits, inv_temp=None, targets=None, *, top_k=None, top_p=None):
+    """Per-row lse at T=1 and at T, plus log p / log q of ``targets`` (scoring).
+
+    With ``top_k`` / ``top_p`` (per-row tensors) lse at T and log q are those of
+    the truncated policy; a target outside the kept columns gets log q = -inf.
+    """
     rows, dev = logits.shape[0], logits.device
     lse1 = torch.empty(rows, dtype=torch.float32, device=dev)
     lseT = torch.empty(rows, dtype=torch.float32, device=dev)
@@ -373,16 +409,66 @@ def row_stats(logits, inv_temp=None, targets=None):
     logq = torch.empty(rows, dtype=torch.float32, device=dev) if targets is not None else None
     if logits.is_cuda:
         _ext.require().row_stats(logits, inv_temp, targets, lse1, lseT, logp, logq,
-                                 *workspace.row_stats_split(dev))
+                                 *workspace.row_stats_split(dev), top_k, top_p)
         return lse1, lseT, logp, logq
     x = logits.float()
     it = inv_temp.float()[:, None] if inv_temp is not None else torch.ones(rows, 1)
+    z = x * it
     lse1.copy_(torch.logsumexp(x, -1))
-    lseT.copy_(torch.logsumexp(x * it, -1))
+    if top_k is None and top_p is None:
+        lseT.copy_(torch.logsumexp(z, -1))
+        log_q = z - lseT[:, None]
+    else:
+        log_q = truncated_log_policy(z, top_k, top_p)
+        kept = torch.isfinite(log_q)
+        lseT.copy_(torch.where(kept, z - log_q, torch.full_like(z, float("-inf"))).amax(-1))
     if targets is not None:
         idx = targets.long()[:, None]
         logp.copy_(x.gather(-1, idx).squeeze(-1) - lse1)
-        logq.copy_((x * it).gather(-1, idx).squeeze(-1) - lseT)
+        logq.copy_(log_q.gather(-1, idx).squeeze(-1))
+    return lse1, lseT, logp, logq
+
+
+HEAD_STATS_ROWS = 8192   # rows per head-statistics launch (bounds the partial buffer)
+
+
+def head_stats(x, weight, inv_temp=None, targets=None):
+    """Row statistics of ``x @ weight.T`` without storing the logits (vocabulary-head scoring).
+
+    ``x`` [R, H] bf16 (already normalised), ``weight`` [V, H] bf16.  Returns fp32
+    (lse at T = 1, lse at T, log p of ``targets`` at T = 1, log q at T); the last
+    two are None without targets.  On the GPU the tcgen05 GEMM reduces every
+    128-row vocabulary tile to (max, sum exp, sum exp at 1/T) in its epilogue and
+    one warp per row folds the tiles; rows go in chunks of ``HEAD_STATS_ROWS``.
+    """
+    R, V = x.shape[0], weight.shape[0]
+    dev = x.device
+    lse1 = torch.empty(R, dtype=torch.float32, device=dev)
+    lseT = torch.empty(R, dtype=torch.float32, device=dev)
+    logp = torch.empty(R, dtype=torch.float32, device=dev) if targets is not None else None
+    logq = torch.empty(R, dtype=torch.float32, device=dev) if targets is not None else None
+    if not x.is_cuda:
+        logits = x.float() @ weight.float().t()
+        a, b, c, d = row_stats(logits, inv_temp, targets)
+        lse1.copy_(a)
+        lseT.copy_(b)
+        if targets is not None:
+            logp.copy_(c)
+            logq.copy_(d)
+        return lse1, lseT, logp, logq
+    ext = _ext.require()
+    tiles = -(-V // 128)
+    chunk = min(R, HEAD_STATS_ROWS)
+    part = workspace.scratch(dev, "head_stats_part", chunk * tiles * 4, torch.float32)
+    tlogit = workspace.scratch(dev, "head_stats_target", chunk, torch.float32)
+    status = workspace.status(dev)
+    it = inv_temp.float().contiguous() if inv_temp is not None else None
+    tg = targets.to(torch.int32).contiguous() if targets is not None else None
+    for s in range(0, R, chunk):
+        e = min(R, s + chunk)
+        ext.head_stats(weight, x[s:e], None if it is None else it[s:e], None if tg is None else tg[s:e], part,
+                       tlogit, lse1[s:e], lseT[s:e], None if logp is None else logp[s:e],
+                       None if logq is None else logq[s:e], status)
     return lse1, lseT, logp, logq
 
 
@@ -508,8 +594,10 @@ def spec_verify(target, draft, candidates, inv_temp, seeds, *, streams=None, sal
                      "lse1_d": torch.empty(B * n, dtype=torch.float32, device=dev),
                      "lseT_d": torch.empty(B * n, dtype=torch.float32, device=dev)}
         split = workspace.row_stats_split(target.device)
-        ext.row_stats(target, stats["inv_target"], None, stats["lse1_t"], stats["lseT_t"], None, None, *split)
-        ext.row_stats(draft, stats["inv_draft"], None, stats["lse1_d"], stats["lseT_d"], None, None, *split)
+        ext.row_stats(target, stats["inv_target"], None, stats["lse1_t"], stats["lseT_t"], None, None, *split, None,
+                      None)
+        ext.row_stats(draft, stats["inv_draft"], None, stats["lse1_d"], stats["lseT_d"], None, None, *split, None,
+                      None)
         if shard is not None:
             return _spec_verify_shard(target, draft, candidates, inv_temp, seeds, streams, salt, res, stats, shard)
         ext.spec_verify(target, draft, candidates, n, inv_temp, seeds, streams, int(salt), res["count"],
@@ -767,7 +855,8 @@ class _TargetLogprob(torch.autograd.Function):
         lseT = torch.empty_like(lse1)
         logp = torch.empty_like(lse1)
         logq = torch.empty_like(lse1)
-        ext.row_stats(logits, None, targets, lse1, lseT, logp, logq, *workspace.row_stats_split(logits.device))
+        ext.row_stats(logits, None, targets, lse1, lseT, logp, logq, *workspace.row_stats_split(logits.device),
+                      None, None)
         ctx.save_for_backward(logits, lse1, targets)
         return logp
 
@@ -809,7 +898,7 @@ class _HeadLogprob(torch.autograd.Function):
             logits = linear(h[s:e], weight, out=buf[: (e - s) * V].view(e - s, V), out_dtype=torch.float32)
             if h.is_cuda:
                 _ext.require().row_stats(logits, None, targets[s:e], lse[s:e], None, logp[s:e], None,
-                                         *workspace.row_stats_split(logits.device))
+                                         *workspace.row_stats_split(logits.device), None, None)
             else:
                 lse[s:e] = logits.logsumexp(-1)
                 logp[s:e] = logits.gather(-1, targets[s:e].long()[:, None]).squeeze(-1) - lse[s:e]

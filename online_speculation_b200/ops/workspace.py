@@ -74,6 +74,22 @@ def row_stats_split(device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
     return part, count
 
 
+def scratch(device: torch.device, name: str, numel: int, dtype: torch.dtype) -> torch.Tensor:
+    """A named per-device scratch buffer of at least ``numel`` elements (grown on demand).
+
+    The buffer is reused across calls on the same stream, so a caller must be done
+    with one use before the next call of the same name.
+    """
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    key = (index, "scratch:" + name)
+    with _lock:
+        buffer = _buffers.get(key)
+        if buffer is None or buffer.numel() < numel or buffer.dtype != dtype:
+            buffer = torch.empty(numel, dtype=dtype, device=torch.device("cuda", index))
+            _buffers[key] = buffer
+    return buffer[:numel]
+
+
 def status(device: torch.device) -> torch.Tensor:
     return _get(device, "status", lambda d: torch.zeros(1, dtype=torch.int32, device=d))
 

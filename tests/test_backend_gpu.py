@@ -11,6 +11,7 @@ from online_speculation_b200.arllm.rewards import SequenceLogProbabilityReward
 from online_speculation_b200.arllm.types import GenerationRequest, ScoreRequest
 from online_speculation_b200.engine.backend import EngineBackend
 from online_speculation_b200.models.decoder import DecoderConfig, random_state_dict, reference_forward
+from online_speculation_b200.ops import kernels as ops
 from online_speculation_b200.ops import workspace
 from online_speculation_b200.shared.rng import SeedStream
 
@@ -51,6 +52,41 @@ def test_sample_logprobs_match_oracle(backend, oracle):
         got_p, got_q = torch.tensor(smp.reference_token_logprobs), torch.tensor(smp.token_logprobs)
         assert float((got_p - lp).norm() / lp.norm()) < 0.02 and float((got_p - lp).abs().max()) < 0.2
         assert float((got_q - lq).norm() / lq.norm()) < 0.03
+    workspace.check_status()
+
+
+def test_truncated_policies_sample_and_score_on_engine(backend, oracle):
+    reqs = [GenerationRequest(tuple(range(5, 5 + n)), 10, SamplingConfig(temperature=t, top_k=k, top_p=p), seed=40 + i,
+                              request_id=f"tr{i}")
+            for i, (n, t, k, p) in enumerate([(30, 1.0, 20, 1.0), (12, 0.8, None, 0.9), (25, 1.3, 50, 0.8)])]
+    out = backend.sample_batch(reqs)
+    for req, smp in zip(reqs, out):
+        logits = reference_forward(CFG, oracle, torch.tensor(list(req.prefix) + list(smp.token_ids)))
+        logits = logits[len(req.prefix) - 1:-1].float() / req.sampling.temperature
+        rows = logits.shape[0]
+        ks = torch.full((rows,), req.sampling.top_k or 0, dtype=torch.int32)
+        ps = torch.full((rows,), req.sampling.top_p, dtype=torch.float32)
+        want = ops.truncated_log_policy(logits, ks, ps).gather(-1, torch.tensor(smp.token_ids)[:, None]).squeeze(-1)
+        got = torch.tensor(smp.token_logprobs)
+        assert bool(torch.isfinite(got).all())
+        # bf16 activations vs the fp32 oracle; a token on the truncation boundary may fall outside the oracle's set
+        close = torch.isfinite(want)
+        assert close.float().mean() >= 0.8
+        assert float((got[close] - want[close]).abs().max()) < 0.25
+        scored = backend.score_batch([ScoreRequest(req.prefix, (smp.token_ids,), req.sampling)])[0]
+        assert torch.allclose(torch.tensor(scored), got, atol=0.02)
+    workspace.check_status()
+
+
+def test_packed_scoring_matches_one_at_a_time(backend):
+    prefix = tuple(range(300, 370))
+    conts = [tuple((7 * i + 3 * j) % 250 + 2 for j in range(n)) for i, n in enumerate((1, 5, 40, 33, 64))]
+    for pol in (None, SamplingConfig(temperature=0.7)):
+        packed = backend.score_batch([ScoreRequest(prefix, tuple(conts), pol)])
+        single = [backend._score_one(backend._model_prefix(prefix), c, pol) for c in conts]
+        for a, b in zip(packed, single):
+            assert len(a) == len(b)
+            assert torch.allclose(torch.tensor(a), torch.tensor(b), atol=0.03)
     workspace.check_status()
 
 

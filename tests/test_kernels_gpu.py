@@ -239,6 +239,75 @@ def test_sample_edge_uniforms(cuda):
     assert torch.equal(tok.cpu(), rt)
 
 
+def _truncation_rows(R, V, device):
+    ks = torch.tensor([0, 1, 5, 50, 1000, 0, 20, V], dtype=torch.int32).repeat(R // 8 + 1)[:R]
+    ps = torch.tensor([1.0, 0.9, 1.0, 0.5, 0.95, 0.1, 0.7, 0.3], dtype=torch.float32).roll(3).repeat(R // 8 + 1)[:R]
+    return ks.to(device), ps.to(device)
+
+
+def test_sample_truncated_policies_match_oracle(cuda):
+    torch.manual_seed(21)
+    R, V = 48, 152064
+    logits = torch.randn(R, V, device=cuda) * 3
+    inv_t = torch.full((R,), 1.0, device=cuda)
+    inv_t[1::3] = 1.25
+    ks, ps = _truncation_rows(R, V, cuda)
+    u = torch.rand(R, dtype=torch.float64, device=cuda)
+    tok, lq, lp = ops.sample(logits, inv_t, u, top_k=ks, top_p=ps)
+    log_q = ops.truncated_log_policy(logits.cpu() * inv_t.cpu()[:, None], ks.cpu(), ps.cpu())
+    t = tok.cpu().long()
+    assert bool(torch.isfinite(log_q.gather(-1, t[:, None])).all())          # every draw inside the kept set
+    cdf = log_q.exp().double().cumsum(-1)
+    upper = cdf.gather(-1, t[:, None]).squeeze(-1)
+    lower = torch.where(t > 0, cdf.gather(-1, (t - 1).clamp_min(0)[:, None]).squeeze(-1), torch.zeros_like(upper))
+    assert bool(((lower - 1e-5 < u.cpu()) & (u.cpu() <= upper + 1e-5)).all())
+    rt, rq, rp = ops.sample_reference(logits.cpu(), inv_t.cpu(), u.cpu(), top_k=ks.cpu(), top_p=ps.cpu())
+    assert (t == rt.long()).float().mean() > 0.9
+    assert torch.allclose(lq.cpu(), log_q.gather(-1, t[:, None]).squeeze(-1), atol=1e-3)
+    assert torch.allclose(lp.cpu(), logits.cpu().log_softmax(-1).gather(-1, t[:, None]).squeeze(-1), atol=1e-3)
+
+
+def test_row_stats_truncated_policies(cuda):
+    torch.manual_seed(22)
+    R, V = 32, 50000
+    x = torch.randn(R, V, device=cuda) * 2
+    it = torch.full((R,), 2.0, device=cuda)
+    ks, ps = _truncation_rows(R, V, cuda)
+    log_q = ops.truncated_log_policy(x.cpu() * it.cpu()[:, None], ks.cpu(), ps.cpu())
+    # half the targets inside the kept set (the argmax), half outside where the row truncates
+    tg = x.argmax(-1).to(torch.int32)
+    tg[1::2] = x[1::2].argmin(-1).to(torch.int32)
+    lse1, lseT, logp, logq = ops.row_stats(x, it, tg, top_k=ks, top_p=ps)
+    want = log_q.gather(-1, tg.cpu().long()[:, None]).squeeze(-1)
+    finite = torch.isfinite(want)
+    assert torch.equal(torch.isfinite(logq.cpu()), finite) and bool((~finite).any())
+    assert torch.allclose(logq.cpu()[finite], want[finite], atol=1e-3)
+    ref = ops.row_stats(x.cpu(), it.cpu(), tg.cpu(), top_k=ks.cpu(), top_p=ps.cpu())
+    assert torch.allclose(lseT.cpu(), ref[1], atol=1e-3) and torch.allclose(lse1.cpu(), ref[0], atol=1e-3)
+
+
+@pytest.mark.parametrize("rows,V", [(300, 151936), (37, 1000), (1, 129)])
+def test_head_stats_match_fp32_oracle(cuda, rows, V):
+    torch.manual_seed(rows + V)
+    H = 1536
+    x = (torch.randn(rows, H, device=cuda) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(V, H, device=cuda) * 0.05).to(torch.bfloat16)
+    inv = torch.rand(rows, device=cuda) * 1.5 + 0.5
+    tg = torch.randint(0, V, (rows,), dtype=torch.int32, device=cuda)
+    tg[::5] = -1                                            # an out-of-range target scores -inf
+    lse1, lseT, logp, logq = ops.head_stats(x, w, inv, tg)
+    logits = x.float() @ w.float().t()
+    want1 = torch.logsumexp(logits, -1)
+    wantT = torch.logsumexp(logits * inv[:, None], -1)
+    assert torch.allclose(lse1, want1, atol=2e-3, rtol=1e-4) and torch.allclose(lseT, wantT, atol=2e-3, rtol=1e-4)
+    ok = tg >= 0
+    idx = tg.clamp_min(0).long()[:, None]
+    assert torch.allclose(logp[ok], (logits.gather(-1, idx).squeeze(-1) - want1)[ok], atol=2e-3, rtol=1e-4)
+    assert torch.allclose(logq[ok], (logits.gather(-1, idx).squeeze(-1) * inv - wantT)[ok], atol=2e-3, rtol=1e-4)
+    assert bool(torch.isinf(logp[~ok]).all()) and bool(torch.isinf(logq[~ok]).all())
+    workspace.check_status()
+
+
 def test_row_stats(cuda):
     x = torch.randn(10, 50000, device=cuda) * 2
     it = torch.full((10,), 2.0, device=cuda)
