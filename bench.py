@@ -26,6 +26,7 @@ run_mh_chains_batched); under N ranks each rank runs 64/N chains on its own GPU.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -48,7 +49,7 @@ def parse():
     p.add_argument("--steps", type=int, default=4)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    p.add_argument("--workload", choices=("mh-spec", "grpo", "dllm"), default="mh-spec",
+    p.add_argument("--workload", choices=("mh-spec", "grpo", "dllm", "is"), default="mh-spec",
                    help="mh-spec: suffix-MH rollouts with speculative drafting (headline); "
                         "grpo: GRPO training on the Qwen2.5-1.5B shape, data parallel; "
                         "dllm: LLaDA-MoE-shaped block diffusion, expert parallel")
@@ -67,6 +68,15 @@ def parse():
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-gb", type=float, default=24.0)
+    # conditional importance sampling (Qwen2.5-1.5B shape): one decision block per prompt per step
+    p.add_argument("--is-prompts", type=int, default=64, help="prompts per step, whole job")
+    p.add_argument("--is-ref-prompts", type=int, default=8,
+                   help="prompts per step of the reference arm (it decodes prompt groups one batch at a time)")
+    p.add_argument("--is-prompt-len", type=int, default=256)
+    p.add_argument("--is-candidates", type=int, default=16)
+    p.add_argument("--is-block", type=int, default=32)
+    p.add_argument("--is-rollouts", type=int, default=8)
+    p.add_argument("--is-rollout-len", type=int, default=256)
     return p.parse_args()
 
 
@@ -520,6 +530,230 @@ def run_reference(args, rank, world, local, group) -> dict:
     }
 
 
+IS_METRIC = "conditional-IS generated tok/s (Qwen2.5-1.5B shape, whole job)"
+
+
+def _is_workload(args, rank, world, prompts_total):
+    """Per-rank prompts (distinct uniform-random ids) and the shared IS settings."""
+    import numpy as np
+
+    from online_speculation_b200.models.decoder import PRESETS
+
+    vocab = PRESETS["qwen2.5-1.5b"].vocab_size
+    per_rank = max(1, prompts_total // world)
+    rng = np.random.default_rng(args.seed + 101 + rank)
+    prompts = [tuple(int(x) for x in rng.integers(0, vocab - 2, size=args.is_prompt_len)) for _ in range(per_rank)]
+    tokens_per_prompt = (args.is_candidates * args.is_block
+                         + args.is_candidates * args.is_rollouts * args.is_rollout_len)
+    return prompts, tokens_per_prompt
+
+
+def _is_result(args, world, impl, ms, wall, tokens, prompts_per_step, clocks, extra):
+    out = {
+        "metric": IS_METRIC, "value": tokens / (ms / 1e3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform-random prompt ids, random-init weights)",
+        "config": {"model": "qwen2.5-1.5b (random init)", "global_batch": prompts_per_step,
+                   "seq_len": args.is_prompt_len + args.is_block + args.is_rollout_len,
+                   "parallelism": f"dp{world}", "candidates": args.is_candidates, "block": args.is_block,
+                   "rollouts_per_candidate": args.is_rollouts, "rollout_len": args.is_rollout_len,
+                   "reward": "sequence log-probability, c=0.5, tau=0.5", "temperature": 1.0,
+                   "step": "one conditional-IS decision block (first block) of every prompt",
+                   "l2": "weights (3 GB) and KV streamed every decode step exceed the 126 MB L2"},
+        "clocks": clocks,
+    }
+    if impl:
+        out["impl"] = impl
+    out.update(extra)
+    return out
+
+
+def run_is(args, rank, world, local, group) -> dict:
+    """Conditional IS on the engine backend: prompts run as threads whose sample/score
+    calls are merged by the continuous-batching wrapper into wide engine batches."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    import torch
+
+    from online_speculation_b200.api import build_runner
+    from online_speculation_b200.arllm.algorithms.conditional_is import conditional_is_step
+    from online_speculation_b200.arllm.backends.batching import ContinuousBatchingBackend
+    from online_speculation_b200.arllm.config import ConditionalISConfig, SamplingConfig
+    from online_speculation_b200.arllm.rewards import SequenceLogProbabilityReward
+    from online_speculation_b200.engine.backend import EngineBackend
+    from online_speculation_b200.ops import _ext
+    from online_speculation_b200.shared.rng import SeedStream
+
+    prompts, tokens_per_prompt = _is_workload(args, rank, world, args.is_prompts)
+    runner = build_runner("qwen2.5-1.5b", seed=args.seed, kv_bytes=int(args.kv_gb * 2**30), max_tokens=8192)
+    seq_max = args.is_prompt_len + args.is_block + args.is_rollout_len
+    engine = EngineBackend(runner, model_id="qwen2.5-1.5b-random", max_batch=256, max_seq_tokens=seq_max,
+                           prefill_tokens=8192, decode_chunk=16, score_pack=256)
+    backend = ContinuousBatchingBackend(engine, max_batch_size=256, max_batch_tokens=1 << 22,
+                                        batch_wait_seconds=0.002)
+    reward = SequenceLogProbabilityReward(backend, coefficient=0.5)
+    cfg = ConditionalISConfig(candidate_count=args.is_candidates, rollout_count=args.is_rollouts,
+                              block_size=args.is_block, total_length=args.is_block + args.is_rollout_len,
+                              reward_temperature=0.5)
+    policy = SamplingConfig(temperature=1.0)
+
+    def one(step, i):
+        st = conditional_is_step(base_backend=backend, rollout_backend=backend, prompt=prompts[i], generated_prefix=(),
+                                 config=cfg, base_sampling=policy, rollout_sampling=policy, reward=None,
+                                 seeds=SeedStream(args.seed * 1_000_003 + step * 10_007 + rank * 101 + i),
+                                 step_index=0, reward_batch=reward.batch)
+        return st.selected.token_ids
+
+    pool = ThreadPoolExecutor(max_workers=len(prompts))
+
+    def step(k):
+        return list(pool.map(lambda i: one(k, i), range(len(prompts))))
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    barrier(world)
+    launches0 = _ext.launches() + engine.stats["graph_kernel_launches"]
+    gen0 = engine.stats["generated_tokens"]
+    sampler = ClockSampler(local)
+    with sampler:
+        barrier(world)
+        wall0 = time.perf_counter()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        chosen = []
+        for k in range(args.steps):
+            chosen.append(step(args.warmup + k))
+        stop.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+        barrier(world)
+    pool.shutdown()
+    ms = max_over_ranks(start.elapsed_time(stop), world)
+    wall = max_over_ranks(wall, world)
+    generated = sum_over_ranks(engine.stats["generated_tokens"] - gen0, world)
+    expected = tokens_per_prompt * len(prompts) * args.steps * world
+    launches = _ext.launches() + engine.stats["graph_kernel_launches"] - launches0
+    out = _is_result(args, world, None, ms, wall, generated, len(prompts) * world, sampler.summary(), {
+        "generated_tokens": generated, "expected_tokens": expected,
+        "batching": dataclasses.asdict(backend.snapshot()),
+        "e2e": {"value": generated / wall, "unit": "tok/s",
+                "h2d_bytes_per_step": len(prompts) * world * args.is_prompt_len * 4,
+                "d2h_bytes_per_step": len(prompts) * world * args.is_block * 4},
+        "gpu_launches": int(launches),
+    })
+    backend.close()
+    engine.close()
+    return out
+
+
+def run_is_reference(args, rank, world, local, group) -> dict:
+    """The same IS decision blocks on the unmodified reference: its TransformersBackend behind its
+    own continuous-batching wrapper, prompts as threads, reward batches as in the repo arm."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "inference_scaling")):
+        return {"impl": "reference", "unavailable": "reference package not installed under baseline/_ref"}
+    sys.path.insert(0, ref)
+    from concurrent.futures import ThreadPoolExecutor
+
+    import torch
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+
+    from inference_scaling.arllm.algorithms.conditional_is import conditional_is_step
+    from inference_scaling.arllm.backends.batching import ContinuousBatchingBackend
+    from inference_scaling.arllm.backends.transformers_backend import TransformersBackend
+    from inference_scaling.arllm.config import ConditionalISConfig, SamplingConfig
+    from inference_scaling.arllm.rewards import SequenceLogProbabilityReward
+    from inference_scaling.shared.rng import SeedStream
+
+    from online_speculation_b200.models.decoder import PRESETS
+
+    c = PRESETS["qwen2.5-1.5b"]
+    hf = Qwen2Config(vocab_size=c.vocab_size, hidden_size=c.hidden_size, intermediate_size=c.intermediate_size,
+                     num_hidden_layers=c.num_hidden_layers, num_attention_heads=c.num_attention_heads,
+                     num_key_value_heads=c.num_key_value_heads, rope_theta=c.rope_theta, rms_norm_eps=c.rms_norm_eps,
+                     tie_word_embeddings=c.tie_word_embeddings, max_position_embeddings=4096,
+                     torch_dtype="bfloat16")
+    torch.manual_seed(args.seed)
+    with torch.device("cuda"):
+        model = Qwen2ForCausalLM(hf).to(torch.bfloat16)
+    model.eval()
+
+    class Tok:
+        pad_token_id = 0
+        eos_token_id = None
+        bos_token_id = 1
+
+    inner = TransformersBackend(model, Tok(), model_id="qwen2.5-1.5b-random", device="cuda")
+    backend = ContinuousBatchingBackend(inner, max_batch_size=256, max_batch_tokens=1 << 22, batch_wait_seconds=0.002)
+    prompts, tokens_per_prompt = _is_workload(args, rank, world, args.is_ref_prompts)
+    reward = SequenceLogProbabilityReward(backend, scale=0.5)
+    cfg = ConditionalISConfig(candidate_count=args.is_candidates, rollout_count=args.is_rollouts,
+                              block_size=args.is_block, total_length=args.is_block + args.is_rollout_len,
+                              reward_temperature=0.5)
+    policy = SamplingConfig(temperature=1.0)
+    counted = {"tokens": 0}
+    lock = threading.Lock()
+
+    class Counting:
+        def __init__(self, b):
+            self.b = b
+
+        @property
+        def model_id(self):
+            return self.b.model_id
+
+        def sample_batch(self, requests):
+            out = self.b.sample_batch(requests)
+            with lock:
+                counted["tokens"] += sum(len(s.token_ids) for s in out)
+            return out
+
+        def score_batch(self, requests):
+            return self.b.score_batch(requests)
+
+    counting = Counting(backend)
+
+    def one(step, i):
+        st = conditional_is_step(base_backend=counting, rollout_backend=counting, prompt=prompts[i],
+                                 generated_prefix=(), config=cfg, base_sampling=policy, rollout_sampling=policy,
+                                 reward=None, seeds=SeedStream(args.seed * 1_000_003 + step * 10_007 + rank * 101 + i),
+                                 step_index=0, reward_batch=reward.batch)
+        return st.selected.token_ids
+
+    pool = ThreadPoolExecutor(max_workers=len(prompts))
+
+    def step(k):
+        return list(pool.map(lambda i: one(k, i), range(len(prompts))))
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    barrier(world)
+    counted["tokens"] = 0
+    sampler = ClockSampler(local)
+    with sampler:
+        barrier(world)
+        wall0 = time.perf_counter()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for k in range(args.steps):
+            step(args.warmup + k)
+        stop.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+        barrier(world)
+    pool.shutdown()
+    ms = max_over_ranks(start.elapsed_time(stop), world)
+    wall = max_over_ranks(wall, world)
+    generated = sum_over_ranks(counted["tokens"], world)
+    return _is_result(args, world, "reference", ms, wall, generated, len(prompts) * world, sampler.summary(), {
+        "generated_tokens": generated,
+        "path": "inference_scaling TransformersBackend + ContinuousBatchingBackend + conditional_is_step (unmodified)",
+        "e2e": {"value": generated / wall, "unit": "tok/s", "h2d_bytes_per_step": None, "d2h_bytes_per_step": None},
+    })
+
+
 def main():
     args = parse()
     rank, world, local, group = dist_setup(args.gpus)
@@ -528,6 +762,9 @@ def main():
             out = (run_dllm(args, rank, world, local, group) if args.impl == "ours" else
                    {"impl": "reference", "unavailable": "the reference LLaDA-MoE path loads remote model code from "
                                                         "the Hugging Face hub, which this machine cannot reach"})
+        elif args.workload == "is":
+            out = (run_is(args, rank, world, local, group) if args.impl == "ours"
+                   else run_is_reference(args, rank, world, local, group))
         elif args.workload == "grpo":
             out = (run_grpo(args, rank, world, local, group) if args.impl == "ours" else
                    {"impl": "reference", "unavailable": "the reference GRPO path needs trl and peft, which are not "

@@ -580,6 +580,45 @@ class GRPOTrainer:
         self.stats = out
         return out
 
+    # ---- checkpointing ----
+    def state_dict(self) -> dict:
+        """This rank's resumable state: its fp32 master shard, AdamW moments, step and data RNG.
+
+        The bf16 parameters are not saved: they are the all-gathered bf16 image of the
+        master shards and are rebuilt on load.  The frozen reference copy is rebuilt
+        from the initial weights by the caller.
+        """
+        return {"format": "grpo-shard-v1", "rank": self.rank, "world": self.world, "step": self.step_count,
+                "shard_numel": self.params.shard_numel, "master": self.master.detach().cpu().clone(),
+                "exp_avg": self.exp_avg.detach().cpu().clone(), "exp_avg_sq": self.exp_avg_sq.detach().cpu().clone(),
+                "rng": self.rng.bit_generator.state}
+
+    def load_state_dict(self, state: dict) -> None:
+        """Restore :meth:`state_dict` of the same rank of a run with the same layout."""
+        if state.get("format") != "grpo-shard-v1":
+            raise ValueError("not a GRPO shard checkpoint")
+        if (state["rank"], state["world"], state["shard_numel"]) != (self.rank, self.world, self.params.shard_numel):
+            raise ValueError(f"checkpoint shard of rank {state['rank']} / {state['world']} "
+                             f"({state['shard_numel']} elements) does not fit rank {self.rank} / {self.world} "
+                             f"({self.params.shard_numel})")
+        for name in ("master", "exp_avg", "exp_avg_sq"):
+            saved = state[name]
+            if saved.shape != getattr(self, name).shape or not bool(torch.isfinite(saved).all()):
+                raise ValueError(f"checkpoint tensor {name} is malformed")
+            getattr(self, name).copy_(saved)
+        self.step_count = int(state["step"])
+        self.rng.bit_generator.state = state["rng"]
+        self.publish.copy_(self.master)
+        if self.world > 1:
+            import torch.distributed as dist
+
+            for (lo, hi, pos), (blo, bhi) in zip(self.params.shard_ranges(), self.params.bucket_ranges):
+                dist.all_gather_into_tensor(self.params.flat[blo:bhi], self.publish[pos:pos + hi - lo],
+                                            group=self.group)
+        else:
+            for lo, hi, pos in self.params.shard_ranges():
+                self.params.flat[lo:hi].copy_(self.publish[pos:pos + hi - lo])
+
     def check_finite(self) -> bool:
         return int(self.nonfinite.item()) == 0
 

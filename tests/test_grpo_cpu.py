@@ -142,3 +142,39 @@ def test_data_parallel_sharded_gradients_and_allgather():
         a, b = layout.view(name, dp), one.params.view(name, full)
         err = (a - b).norm() / b.norm().clamp(min=1e-12)
         assert err < 1e-2, (name, float(err))   # bf16 reductions over different row counts
+
+
+def _synthetic(step):
+    g = torch.Generator().manual_seed(100 + step)
+    ids = torch.randint(0, TINY.vocab_size, (4, 10), generator=g)
+    rewards = (torch.rand(4, generator=g) < 0.5).float()
+    return ids, torch.ones(4, 6, dtype=torch.bool), rewards
+
+
+def test_grpo_run_checkpoints_resume_bit_exact_and_refuse_changed_settings(tmp_path):
+    import json
+
+    from online_speculation_b200.training.grpo_run import GRPORun, latest_checkpoint
+
+    conf = GRPOConfig(group_size=2, prompts_per_rank=2, prompt_length=4, completion_length=6, learning_rate=1e-3)
+    straight = GRPORun(tmp_path / "a", TINY, conf, max_steps=4, save_steps=2, device="cpu", seed=3, data=_synthetic)
+    straight.train()
+    assert latest_checkpoint(tmp_path / "a").name == "checkpoint-4"
+    assert (tmp_path / "a" / "checkpoint-2" / "rank0.pt").is_file()
+    manifest = json.loads((tmp_path / "a" / "run_manifest.json").read_text())
+    assert manifest["status"] == "completed" and manifest["final_step"] == 4
+    # an interrupted run (2 steps) continued to 4 steps reaches the same parameters
+    first = GRPORun(tmp_path / "b", TINY, conf, max_steps=2, save_steps=2, device="cpu", seed=3, data=_synthetic)
+    first.train()
+    second = GRPORun(tmp_path / "b", TINY, conf, max_steps=4, save_steps=2, device="cpu", seed=3, data=_synthetic)
+    assert second.resumed_from.endswith("checkpoint-2") and second.trainer.step_count == 2
+    second.train()
+    assert torch.equal(second.trainer.params.flat, straight.trainer.params.flat)
+    assert torch.equal(second.trainer.master, straight.trainer.master)
+    # other hyper-parameters in the same directory are refused; more steps are not
+    other = GRPOConfig(group_size=2, prompts_per_rank=2, prompt_length=4, completion_length=6, learning_rate=2e-3)
+    with pytest.raises(ValueError, match="different"):
+        GRPORun(tmp_path / "b", TINY, other, max_steps=4, device="cpu", seed=3, data=_synthetic)
+    fresh = GRPORun(tmp_path / "b", TINY, conf, max_steps=6, save_steps=2, device="cpu", seed=3, data=_synthetic,
+                    resume="none")
+    assert fresh.trainer.step_count == 0
