@@ -65,6 +65,8 @@ def parse():
     p.add_argument("--block", type=int, default=4)
     p.add_argument("--stride", type=int, default=64)
     p.add_argument("--no-learner", action="store_true")
+    p.add_argument("--no-draft", action="store_true",
+                   help="plain one-token decoding without the draft head (shows what speculation adds)")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-gb", type=float, default=24.0)
@@ -201,7 +203,8 @@ def run_ours(args, rank, world, local, group) -> dict:
     engine = build_mh_engine(args.model, tp_group=group, seed=args.seed, alpha=args.alpha, length=args.gen_len,
                              block_size=args.block, learner_stride=None if args.no_learner else args.stride,
                              use_graphs=not args.no_graphs, kv_bytes=int(args.kv_gb * 2**30),
-                             max_seq_tokens=args.prompt_len + args.gen_len + 2 * args.block)
+                             max_seq_tokens=args.prompt_len + args.gen_len + 2 * args.block,
+                             draft=not args.no_draft)
     rng = np.random.default_rng(args.seed + 17)
     vocab = engine.runner.cfg.vocab_size
     # one uniform-random prompt shared by the chains (the reference API's shape)
@@ -266,8 +269,9 @@ def run_ours(args, rank, world, local, group) -> dict:
         "config": {"model": f"{args.model} (random init)", "global_batch": args.chains, "seq_len": args.prompt_len + args.gen_len,
                    "prompt": "one uniform-random prompt shared by all chains",
                    "prompt_len": args.prompt_len, "gen_len": args.gen_len, "parallelism": f"tp{world}",
-                   "mh_alpha": args.alpha, "draft": f"1-layer block-{args.block} draft head",
-                   "learner_stride_blocks": None if args.no_learner else args.stride,
+                   "mh_alpha": args.alpha,
+                   "draft": "none (plain decoding)" if args.no_draft else f"1-layer block-{args.block} draft head",
+                   "learner_stride_blocks": None if (args.no_learner or args.no_draft) else args.stride,
                    "l2": "weights (15 GB) streamed every round exceed the 126 MB L2",
                    "step": "64 completed MH updates; chains run asynchronously (no lock-step barrier)"},
         "spec_accept_len": accept_len,

@@ -44,11 +44,16 @@ def build_mh_engine(model: str | DecoderConfig = "qwen2.5-7b", *, tp_group=None,
                     length: int = 512, block_size: int = 4, learner_stride: int | None = 64,
                     learner_loss: str = "tv", learning_rate: float = 1e-5, use_graphs: bool = True,
                     kv_bytes: int = 24 << 30, max_seq_tokens: int = 1040, max_batch: int = 64,
-                    fused_collectives: bool = True) -> MHEngine:
+                    fused_collectives: bool = True, draft: bool = True) -> MHEngine:
+    """Suffix-MH engine; ``draft=False`` decodes one token per round without a draft head (the
+    baseline that shows what block speculation adds)."""
     runner = build_runner(model, tp_group=tp_group, seed=seed, kv_bytes=kv_bytes,
                           max_logit_rows=max(512, max_batch * block_size), fused_collectives=fused_collectives)
-    draft = init_draft(runner.w, seed=seed + 1)
-    head = DraftHead(runner, draft, block_size=block_size)
+    if not draft:
+        return MHEngine(runner, None, alpha=alpha, length=length, root_seed=seed, learner=None,
+                        use_graphs=use_graphs, max_pages_per_seq=-(-max_seq_tokens // 32) + 1)
+    draft_weights = init_draft(runner.w, seed=seed + 1)
+    head = DraftHead(runner, draft_weights, block_size=block_size)
     learner = None
     if learner_stride:
         learner = SuffixLearner(head, SuffixConfig(stride=learner_stride, loss=learner_loss,

@@ -125,7 +125,8 @@ class _RoundGraph:
         splits = K.attention_kv_splits(ctas * tiles_per, mp * K.PAGE_SIZE) if tr == K.TC_TILE_ROWS else 1
         self.plan_draft = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(1), tile_seq, tile_row0, tr, {}, splits)
         self.plan_verify = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(0), tile_seq, tile_row0, tr, {}, splits)
-        self.ids_draft = torch.full((B, Kb), engine.head.mask_token_id, dtype=torch.int32, device=dev)
+        mask_id = engine.head.mask_token_id if engine.head is not None else 0
+        self.ids_draft = torch.full((B, Kb), mask_id, dtype=torch.int32, device=dev)
         self.ids_verify = torch.zeros(B, Kb, dtype=torch.int32, device=dev)
         rows = torch.arange(B * Kb, device=dev).view(B, Kb)[:, : Kb - 1].reshape(-1)
         self.draft_rows = rows.to(torch.int64)
@@ -155,6 +156,9 @@ class _RoundGraph:
     def _body(self):
         e, B, Kb = self.e, self.B, self.e.block
         v = self.views
+        if e.head is None:
+            self._body_plain()
+            return
         self.ids_draft[:, 0].copy_(v["anchors"])
         self.active.copy_(v["active"])
         self.row_streams.copy_(v["streams"].repeat_interleave(Kb - 1))
@@ -181,6 +185,23 @@ class _RoundGraph:
         self.result[:, 2:2 + Kb].copy_(o["emitted"])
         self.result[:, 2 + Kb:2 + 2 * Kb].copy_(o["logq"])
         self.result[:, 2 + 2 * Kb:].copy_(o["logp"])
+
+    def _body_plain(self):
+        """Plain decoding (no draft): one token per job from the target at temperature 1 / alpha."""
+        e, B = self.e, self.B
+        v = self.views
+        self.ids_verify[:, 0].copy_(v["anchors"])
+        meta = StepMeta(self.ids_verify.view(-1), v["positions"], v["slots"], self.plan_verify, None)
+        logits = e.runner.forward(meta)
+        tok = self.out["emitted"][:, 0]
+        K.gumbel_sample(logits, self.inv_temp, self.seeds, streams=v["streams"], salt=0x777, tokens=tok)
+        _, _, logp, logq = K.row_stats(logits, self.inv_temp, tok)
+        o = self.out
+        self.result[:, 0].zero_()
+        self.result[:, 1].fill_(1.0)
+        self.result[:, 2].copy_(tok)
+        self.result[:, 3].copy_(logq)
+        self.result[:, 4].copy_(logp)
 
     def _capture(self):
         from ..ops import _ext
@@ -217,13 +238,13 @@ class _RoundGraph:
 class MHEngine:
     """Suffix-MH chains with speculative block drafting on one TP group."""
 
-    def __init__(self, runner: ModelRunner, head: DraftHead, *, alpha: float = 4.0, length: int = 512,
+    def __init__(self, runner: ModelRunner, head: DraftHead | None, *, alpha: float = 4.0, length: int = 512,
                  root_seed: int = 0, learner: SuffixLearner | None = None, use_graphs: bool = True,
                  max_pages_per_seq: int | None = None):
         self.runner = runner
         self.head = head
         self.cache: KVCache = runner.cache
-        self.block = head.block_size
+        self.block = head.block_size if head is not None else 1     # no draft head: plain decoding
         self.alpha = float(alpha)
         self.inv_temp = self.alpha  # proposal temperature 1 / alpha
         self.length = int(length)

@@ -115,6 +115,67 @@ def test_mh_engine_logprobs_are_exact(graphs):
     workspace.check_status()
 
 
+def test_mh_engine_without_draft_is_exact():
+    """Plain decoding (no draft head) emits one token per round with exact log p / log q."""
+    cfg = SMALL
+    eng = build_mh_engine(cfg, seed=3, alpha=2.0, length=16, use_graphs=True, kv_bytes=64 << 20, max_seq_tokens=64,
+                          max_batch=8, draft=False)
+    prompt = list(range(5, 21))
+    eng.add_chains([prompt] * 4)
+    eng.run_until_idle()
+    eng.set_quota(2)
+    eng.run_until_idle()
+    assert eng.stats["mh_updates"] == 8 and eng.mean_accept_length == 1.0
+    sd = {k: v.cpu() for k, v in random_state_dict(cfg, seed=3, std=0.02, device="cuda").items()}
+    for ch in eng.chains:
+        full = torch.tensor(ch.prompt + ch.tokens)
+        logits = reference_forward(cfg, sd, full)[len(prompt) - 1:-1]
+        lp = logits.log_softmax(-1).gather(-1, torch.tensor(ch.tokens)[:, None]).squeeze(-1)
+        lq = (logits * 2.0).log_softmax(-1).gather(-1, torch.tensor(ch.tokens)[:, None]).squeeze(-1)
+        assert torch.allclose(torch.tensor(ch.logp), lp, atol=0.05)
+        assert torch.allclose(torch.tensor(ch.logq), lq, atol=0.1)
+    eng.close()
+    workspace.check_status()
+
+
+def test_online_learner_raises_acceptance():
+    """A draft copied from the target's last attention and then corrupted with noise recovers
+    acceptance through the online learner."""
+    from online_speculation_b200.api import build_runner
+    from online_speculation_b200.engine.draft import DraftHead, SuffixConfig, SuffixLearner, init_draft
+    from online_speculation_b200.engine.mh_engine import MHEngine
+
+    cfg = SMALL
+    runner = build_runner(cfg, seed=4, kv_bytes=128 << 20, max_tokens=2048)
+    draft = init_draft(runner.w, seed=5, copy_from_target=True)
+    g = torch.Generator(device="cuda").manual_seed(6)
+    for name in ("w_qkv", "w_o"):
+        t = getattr(draft, name)
+        noise = torch.randn(t.shape, generator=g, device="cuda") * float(t.float().std())
+        t.copy_((t.float() + noise * (t != 0).float()).to(t.dtype))
+    head = DraftHead(runner, draft, block_size=4)
+    learner = SuffixLearner(head, SuffixConfig(stride=4, learning_rate=2e-3), use_graphs=True)
+    eng = MHEngine(runner, head, alpha=4.0, length=64, root_seed=7, learner=learner, use_graphs=True,
+                   max_pages_per_seq=8)
+    eng.add_chains([list(range(5, 37))] * 8)
+    eng.set_quota(10_000)
+
+    def window(rounds):
+        b0, e0 = eng.stats["blocks"], eng.stats["emitted"]
+        for _ in range(rounds):
+            eng.round()
+        return (eng.stats["emitted"] - e0) / max(1, eng.stats["blocks"] - b0)
+
+    before = window(50)
+    window(500)
+    after = window(50)
+    print(f"accept length before {before:.3f} after {after:.3f}, learner updates {learner.updates}")
+    assert learner.updates >= 100
+    assert after > before + 0.05
+    eng.close()
+    workspace.check_status()
+
+
 def test_kernel_branch_matches_module_branch():
     from online_speculation_b200.blockspec.generation import MaskedAttentionBranch, ProposalSampler, generate
     from online_speculation_b200.blockspec.kernel_branch import KernelBranch
