@@ -8,6 +8,10 @@ Workload (random-init bf16 weights, synthetic uniform-random prompt ids):
   1/4); every MH update regenerates the suffix after a uniformly drawn cut while
   reusing the prefix KV.  Drafting uses a
   1-layer block-4 draft head; the online learner updates every 64 verified blocks.
+  The engine drafts in the rounds where the measured acceptance makes speculation
+  faster than plain decoding, and at least every 8th round so the learner keeps
+  training (``--spec-policy always`` drafts every round; ``--no-draft`` runs plain
+  decoding only).  Every emitted token follows the proposal policy exactly either way.
   Tensor parallel over N GPUs of one node (one process per GPU, NCCL).
 
 A "step" is one MH update of every chain (64 proposals).  W warm-up steps run
@@ -67,6 +71,10 @@ def parse():
     p.add_argument("--no-learner", action="store_true")
     p.add_argument("--no-draft", action="store_true",
                    help="plain one-token decoding without the draft head (shows what speculation adds)")
+    p.add_argument("--spec-policy", choices=("adaptive", "always", "never"), default="adaptive",
+                   help="draft every round (always) or where the measured acceptance makes it pay (adaptive)")
+    p.add_argument("--probe-every", type=int, default=8,
+                   help="adaptive policy: at least one speculative round per this many rounds")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-gb", type=float, default=24.0)
@@ -204,7 +212,7 @@ def run_ours(args, rank, world, local, group) -> dict:
                              block_size=args.block, learner_stride=None if args.no_learner else args.stride,
                              use_graphs=not args.no_graphs, kv_bytes=int(args.kv_gb * 2**30),
                              max_seq_tokens=args.prompt_len + args.gen_len + 2 * args.block,
-                             draft=not args.no_draft)
+                             draft=not args.no_draft, spec_policy=args.spec_policy, probe_every=args.probe_every)
     rng = np.random.default_rng(args.seed + 17)
     vocab = engine.runner.cfg.vocab_size
     # one uniform-random prompt shared by the chains (the reference API's shape)
@@ -272,12 +280,16 @@ def run_ours(args, rank, world, local, group) -> dict:
                    "mh_alpha": args.alpha,
                    "draft": "none (plain decoding)" if args.no_draft else f"1-layer block-{args.block} draft head",
                    "learner_stride_blocks": None if (args.no_learner or args.no_draft) else args.stride,
+                   "spec_policy": "none" if args.no_draft else args.spec_policy,
+                   "probe_every": args.probe_every if args.spec_policy == "adaptive" else None,
                    "l2": "weights (15 GB) streamed every round exceed the 126 MB L2",
                    "step": "64 completed MH updates; chains run asynchronously (no lock-step barrier)"},
         "spec_accept_len": accept_len,
         "generated_tokens": generated,
         "mh_acceptance_rate": (st["mh_accepted"] - stats0["mh_accepted"]) / max(1, st["mh_updates"] - stats0["mh_updates"]),
         "learner_updates": (engine.learner.updates - learner0) if engine.learner else 0,
+        "spec_rounds": st["spec_rounds"] - stats0["spec_rounds"],
+        "plain_rounds": st["plain_rounds"] - stats0["plain_rounds"],
         "clocks": sampler.summary(),
         "e2e": {"value": generated / wall, "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},

@@ -44,9 +44,16 @@ def build_mh_engine(model: str | DecoderConfig = "qwen2.5-7b", *, tp_group=None,
                     length: int = 512, block_size: int = 4, learner_stride: int | None = 64,
                     learner_loss: str = "tv", learning_rate: float = 1e-5, use_graphs: bool = True,
                     kv_bytes: int = 24 << 30, max_seq_tokens: int = 1040, max_batch: int = 64,
-                    fused_collectives: bool = True, draft: bool = True) -> MHEngine:
-    """Suffix-MH engine; ``draft=False`` decodes one token per round without a draft head (the
-    baseline that shows what block speculation adds)."""
+                    fused_collectives: bool = True, draft: bool = True, spec_policy: str = "adaptive",
+                    probe_every: int = 8) -> MHEngine:
+    """Suffix-MH engine.
+
+    ``draft=False`` decodes one token per round without a draft head (the baseline
+    that shows what block speculation adds).  ``spec_policy``: ``adaptive`` drafts
+    in the rounds where the measured acceptance makes speculation faster than plain
+    decoding, with a speculative round at least every ``probe_every`` rounds so the
+    online learner keeps training; ``always`` drafts every round; ``never`` never.
+    """
     runner = build_runner(model, tp_group=tp_group, seed=seed, kv_bytes=kv_bytes,
                           max_logit_rows=max(512, max_batch * block_size), fused_collectives=fused_collectives)
     if not draft:
@@ -60,4 +67,5 @@ def build_mh_engine(model: str | DecoderConfig = "qwen2.5-7b", *, tp_group=None,
                                                    learning_rate=learning_rate), use_graphs=use_graphs)
     max_pages = -(-max_seq_tokens // 32) + 1
     return MHEngine(runner, head, alpha=alpha, length=length, root_seed=seed, learner=learner,
-                    use_graphs=use_graphs, max_pages_per_seq=max_pages)
+                    use_graphs=use_graphs, max_pages_per_seq=max_pages, spec_policy=spec_policy,
+                    probe_every=probe_every)

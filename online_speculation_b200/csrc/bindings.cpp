@@ -14,6 +14,7 @@
 #include "attention.h"
 #include "ep.h"
 #include "comm.h"
+#include "diffusion.h"
 #include "elementwise.h"
 #include "gemm.h"
 #include "moe.h"
@@ -165,6 +166,54 @@ void head_stats(Tensor w, Tensor x, c10::optional<Tensor> inv_temp, c10::optiona
   a.logp = ptr_or_null<float>(logp);
   a.logq = ptr_or_null<float>(logq);
   check(osb::head_stats_merge_launch(a, stream), "head statistics merge");
+}
+
+// One block-diffusion remasking step (see diffusion.h).
+void remask_select(Tensor tokens, int64_t a0, int64_t bl, int64_t mask_id, Tensor drawn, c10::optional<Tensor> prio,
+                   c10::optional<Tensor> logq, int64_t tc, bool subset, c10::optional<Tensor> traj,
+                   c10::optional<Tensor> step_lp, Tensor out_pos, Tensor out_tok, int64_t pos_offset) {
+  CHECK_CUDA(tokens);
+  CHECK_DT(tokens, torch::kInt64);
+  CHECK_ROWS(tokens);
+  CHECK_DT(drawn, torch::kInt32);
+  CHECK_DT(out_pos, torch::kInt64);
+  CHECK_DT(out_tok, torch::kInt64);
+  const int rows = tokens.size(0);
+  TORCH_CHECK(a0 >= 0 && bl > 0 && a0 + bl <= tokens.size(1), "block outside the sequences");
+  TORCH_CHECK(drawn.is_contiguous() && drawn.numel() >= rows * bl, "drawn must hold rows * bl tokens");
+  TORCH_CHECK(out_pos.dim() == 2 && out_pos.size(0) == rows && out_pos.size(1) >= tc && out_pos.stride(1) == 1 &&
+                  out_tok.sizes() == out_pos.sizes() && out_tok.strides() == out_pos.strides(),
+              "out_pos / out_tok must be [rows, >= tc] with unit column stride");
+  for (const c10::optional<Tensor>* o : {&prio, &logq})
+    if (o->has_value() && (*o)->defined()) {
+      CHECK_DT((**o), torch::kFloat32);
+      TORCH_CHECK((*o)->is_contiguous() && (*o)->numel() >= rows * bl, "per-position inputs need rows * bl floats");
+    }
+  for (const c10::optional<Tensor>* o : {&traj, &step_lp})
+    if (o->has_value() && (*o)->defined()) {
+      CHECK_DT((**o), torch::kFloat64);
+      TORCH_CHECK((*o)->is_contiguous() && (*o)->numel() >= rows, "per-row outputs need rows doubles");
+    }
+  c10::cuda::CUDAGuard guard(tokens.device());
+  osb::RemaskArgs a{};
+  a.tokens = reinterpret_cast<long long*>(tokens.data_ptr<int64_t>());
+  a.ld_tokens = tokens.stride(0);
+  a.a0 = static_cast<int>(a0);
+  a.bl = static_cast<int>(bl);
+  a.mask_id = mask_id;
+  a.drawn = drawn.data_ptr<int>();
+  a.prio = ptr_or_null<const float>(prio);
+  a.logq = ptr_or_null<const float>(logq);
+  a.tc = static_cast<int>(tc);
+  a.rows = rows;
+  a.subset = subset ? 1 : 0;
+  a.traj = ptr_or_null<double>(traj);
+  a.step_lp = ptr_or_null<double>(step_lp);
+  a.out_pos = reinterpret_cast<long long*>(out_pos.data_ptr<int64_t>());
+  a.out_tok = reinterpret_cast<long long*>(out_tok.data_ptr<int64_t>());
+  a.out_ld = out_pos.stride(0);
+  a.pos_offset = pos_offset;
+  check(osb::remask_select_launch(a, at::cuda::getCurrentCUDAStream()), "remask_select");
 }
 
 void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_start, Tensor q_len, Tensor kv_len,
@@ -860,6 +909,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("gemm_push", &gemm_push);
   m.def("head_stats", &head_stats);
+  m.def("remask_select", &remask_select);
   m.def("allreduce_pushed_add_rmsnorm", &allreduce_pushed_add_rmsnorm);
   m.def("attention", &attention);
   m.def("rmsnorm", &rmsnorm);

@@ -247,26 +247,19 @@ class DiffusionEngineBackend:
                     drawn = K.gumbel_sample(logits, inv_t, seeds, seed_index=seed_index, streams=streams,
                                             row_in_seq=row_in, salt=_GUMBEL_SALT)
                 _, _, logp1, logq = K.row_stats(logits, inv_t, drawn)
-                masked = tokens[:, a0:a0 + bl] == mask                       # [B, bl]
                 if sp.remasking in ("low_confidence", "low_confidence_static"):
-                    prio = logp1.view(B, bl).clone()
+                    prio = logp1                                             # most confident first
                 elif sp.remasking == "random":
                     prio = torch.from_numpy(np.stack([h.random(bl) for h in hosts])).to(dev, torch.float32)
                 else:
-                    prio = (-arange_bl.float()).expand(B, bl).clone()
-                prio = prio.masked_fill(~masked, float("-inf"))
-                sel = torch.topk(prio, tc, dim=1).indices.sort(dim=1).values   # [B, tc] relative to block
-                drawn2 = drawn.view(B, bl).long()
-                chosen = drawn2.gather(1, sel)
-                tokens.scatter_(1, a0 + sel, chosen)
+                    prio = None                                              # earliest position first
+                # one fused step: choose, commit, compact and score the transferred positions
+                pos, chosen, lp = K.remask_select(tokens, a0, bl, mask, drawn, tc, prio=prio,
+                                                  logq=logq if exact else None, subset=sp.remasking == "random",
+                                                  traj=traj if exact else None, pos_offset=blk * bl)
                 if exact:
-                    avail = masked.sum(1)
-                    lp = logq.view(B, bl).double().gather(1, sel).sum(1)
-                    if sp.remasking == "random":
-                        lp = lp + _subset_tensor(avail, tc)
-                    traj += lp
                     rec_lp.append(lp)
-                rec_pos.append(sel + blk * bl)
+                rec_pos.append(pos)
                 rec_tok.append(chosen)
                 step_global += 1
         # one device -> host copy of the whole trace

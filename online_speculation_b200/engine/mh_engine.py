@@ -33,6 +33,7 @@ from dataclasses import dataclass, field
 
 import numpy as np
 import torch
+import torch.distributed as dist
 
 from ..ops import kernels as K
 from ..shared.mh import decide_metropolis_hastings
@@ -76,10 +77,10 @@ class Chain:
 class _RoundGraph:
     """Static buffers (and optionally a captured CUDA graph) for one round of B blocks."""
 
-    def __init__(self, engine: "MHEngine", B: int, use_graph: bool):
+    def __init__(self, engine: "MHEngine", B: int, use_graph: bool, Kb: int):
         self.e = engine
         self.B = B
-        Kb = engine.block
+        self.Kb = Kb                      # 1: plain decoding round (no draft)
         dev = engine.device
         mp = engine.max_pages
         self.mp = mp
@@ -148,15 +149,16 @@ class _RoundGraph:
         self.result = torch.zeros(B, 2 + 3 * Kb, dtype=torch.float32, device=dev)
         self.result_host = torch.zeros(B, 2 + 3 * Kb, dtype=torch.float32).pin_memory()
         self.graph = None
+        self.runs = 0                     # rounds run on these buffers (the first one includes capture)
         self.teacher = None
         self.launches_per_round = 0
         if use_graph:
             self._capture()
 
     def _body(self):
-        e, B, Kb = self.e, self.B, self.e.block
+        e, B, Kb = self.e, self.B, self.Kb
         v = self.views
-        if e.head is None:
+        if Kb == 1:
             self._body_plain()
             return
         self.ids_draft[:, 0].copy_(v["anchors"])
@@ -221,6 +223,7 @@ class _RoundGraph:
         self.graph = g
 
     def run(self):
+        self.runs += 1
         self.e.stats["h2d_bytes"] += self.host.numel() * 4 + self.seeds_host.numel() * 8
         self.e.stats["d2h_bytes"] += self.result_host.numel() * 4
         self.dev.copy_(self.host, non_blocking=True)
@@ -240,7 +243,7 @@ class MHEngine:
 
     def __init__(self, runner: ModelRunner, head: DraftHead | None, *, alpha: float = 4.0, length: int = 512,
                  root_seed: int = 0, learner: SuffixLearner | None = None, use_graphs: bool = True,
-                 max_pages_per_seq: int | None = None):
+                 max_pages_per_seq: int | None = None, spec_policy: str = "adaptive", probe_every: int = 8):
         self.runner = runner
         self.head = head
         self.cache: KVCache = runner.cache
@@ -255,9 +258,19 @@ class MHEngine:
         self.max_pages = max_pages_per_seq or 64
         self.chains: list[Chain] = []
         self.jobs: dict[int, Job] = {}
-        self._graphs: dict[int, _RoundGraph] = {}
+        self._graphs: dict[tuple[int, int], _RoundGraph] = {}
+        if spec_policy not in ("adaptive", "always", "never"):
+            raise ValueError("spec_policy is adaptive, always or never")
+        self.spec_policy = spec_policy if head is not None else "never"
+        self.probe_every = probe_every
+        # per-round wall time (EMA) of speculative and plain rounds and the mean emitted tokens per
+        # speculative block; the adaptive policy compares expected tokens per second of the two
+        self._t_spec = self._t_plain = None
+        self._accept_ema = None
+        self._since_spec = 0
         self.stats = {"rounds": 0, "blocks": 0, "emitted": 0, "generated": 0, "mh_updates": 0, "mh_accepted": 0,
-                      "learner_updates": 0, "graph_kernel_launches": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+                      "learner_updates": 0, "graph_kernel_launches": 0, "h2d_bytes": 0, "d2h_bytes": 0,
+                      "spec_rounds": 0, "plain_rounds": 0}
 
     # ---- setup ----
     def add_chains(self, prompts: list[list[int]]) -> None:
@@ -360,22 +373,46 @@ class MHEngine:
                 self._next_job(c)
 
     # ---- rounds ----
-    def _graph(self, B: int) -> _RoundGraph:
+    def _graph(self, B: int, Kb: int) -> _RoundGraph:
         bucket = next(b for b in BUCKETS if b >= B) if B <= BUCKETS[-1] else B
-        g = self._graphs.get(bucket)
+        g = self._graphs.get((bucket, Kb))
         if g is None:
-            g = _RoundGraph(self, bucket, self.use_graphs)
-            self._graphs[bucket] = g
+            g = _RoundGraph(self, bucket, self.use_graphs, Kb)
+            self._graphs[(bucket, Kb)] = g
         return g
 
+    def _speculate_next(self) -> bool:
+        """Speculation policy for the next round.
+
+        ``always`` / ``never`` are fixed.  ``adaptive`` drafts when the expected
+        tokens per second of a speculative round, (mean emitted per block) / (its
+        time), beat those of a plain one, 1 / (its time); both times and the
+        acceptance are running means of measured rounds.  While a learner is
+        attached, or before both kinds have been measured, a speculative round runs
+        at least every ``probe_every`` rounds, so the draft keeps learning from
+        verified blocks and the acceptance estimate stays current.  The emitted
+        tokens follow the proposal policy exactly in both kinds of round.
+        """
+        if self.spec_policy != "adaptive":
+            return self.spec_policy == "always"
+        if self._t_spec is None:
+            return True
+        if self._t_plain is None:
+            return False
+        if self._since_spec + 1 >= self.probe_every:
+            return True
+        return self._accept_ema * self._t_plain > self._t_spec
+
     def round(self) -> int:
-        """Advance every active job by one speculative round; returns tokens generated."""
+        """Advance every active job by one round (speculative or plain); returns tokens generated."""
         jobs = sorted(self.jobs.values(), key=lambda j: j.chain)
         if not jobs:
             return 0
-        Kb = self.block
+        speculate = self._speculate_next()
+        Kb = self.block if speculate else 1
+        started = time.perf_counter()
         self.cache.flush_copies()
-        g = self._graph(len(jobs))
+        g = self._graph(len(jobs), Kb)
         B, nj = g.B, len(jobs)
         hv = g.host_views
         seqs = [j.seq for j in jobs]
@@ -404,7 +441,7 @@ class MHEngine:
         counts = res[:, 0].astype(np.int64)
         if (res[:nj, 1] == 0).any():
             raise RuntimeError("speculative correction reported invalid probabilities")
-        if self.learner is not None:
+        if self.learner is not None and speculate:
             fb = FeedbackRound(g.ids_draft, g.views["positions"].view(B, Kb), g.views["table"].view(B, g.mp),
                                g.teacher, g.out["count"], g.active, nj)
             if self.learner.observe(fb):
@@ -428,13 +465,36 @@ class MHEngine:
             j.n = int(new_len[b])
             if len(j.tokens) >= j.need:
                 finished.append(j)
-        self.stats["emitted"] += int((counts[:nj] + 1).sum())
         self.stats["rounds"] += 1
-        self.stats["blocks"] += nj
         self.stats["generated"] += generated
+        if speculate:
+            self.stats["emitted"] += int((counts[:nj] + 1).sum())
+            self.stats["blocks"] += nj
+            self.stats["spec_rounds"] += 1
+        else:
+            self.stats["plain_rounds"] += 1
         for j in finished:
             self._finish(j)
+        self._note_round(speculate, time.perf_counter() - started, float((counts[:nj] + 1).mean()), g.runs == 1)
         return generated
+
+    def _note_round(self, speculate: bool, seconds: float, emitted_per_job: float, first_run: bool) -> None:
+        if self.spec_policy != "adaptive" or first_run:
+            return                               # a round that built (and captured) its buffers is not representative
+        comm = self.runner.comm
+        if comm.world > 1:
+            # every rank must take the same decision: use the slowest rank's round time
+            t = torch.tensor([seconds], dtype=torch.float32, device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=comm.group)
+            seconds = float(t.item())
+        ema = lambda old, new: new if old is None else 0.8 * old + 0.2 * new
+        if speculate:
+            self._t_spec = ema(self._t_spec, seconds)
+            self._accept_ema = ema(self._accept_ema, emitted_per_job)
+            self._since_spec = 0
+        else:
+            self._t_plain = ema(self._t_plain, seconds)
+            self._since_spec += 1
 
     def run_until_idle(self, max_rounds: int | None = None) -> int:
         total = 0

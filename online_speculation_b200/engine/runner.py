@@ -120,7 +120,7 @@ class ModelRunner:
         H, D, T, R = self.cfg.hidden_size, 128, max_tokens, max_logit_rows
         V = self.vocab_local * self.comm.world
         self._reserve = {
-            "h": T * H, "x": T * H, "part": T * H, "sel": T * H, "dh": T * H, "dx": T * H, "xl": R * H,
+            "h": T * H, "x": T * H, "part": T * H, "sel": T * H, "dh": T * H, "dx": T * H, "xl": R * H, "xs": T * H,
             "qkv": T * (self.q_slots + 2 * self.kv_slots) * D, "q": T * self.q_slots * D,
             "att": T * self.q_slots * D, "act": T * weights.ffn_local,
             "logits_local": R * self.vocab_local, "logits_full": R * V, "logits_scratch": R * V,
@@ -262,7 +262,7 @@ class ModelRunner:
         self.layer_stack(h, meta, range(self.cfg.num_hidden_layers))
         sel = h if meta.logit_rows is None else self._index_rows(h, meta.logit_rows)
         x = K.rmsnorm(sel, self.w.final_norm, self.cfg.rms_norm_eps,
-                      out=self._buf("xl", (sel.shape[0], self.cfg.hidden_size)))
+                      out=self._buf("xs", (sel.shape[0], self.cfg.hidden_size)))
         return K.head_stats(x, self.w.head, inv_temp, targets)
 
     @property

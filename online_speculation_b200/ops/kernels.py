@@ -472,6 +472,50 @@ def head_stats(x, weight, inv_temp=None, targets=None):
     return lse1, lseT, logp, logq
 
 
+def remask_select(tokens, a0, bl, mask_id, drawn, tc, *, prio=None, logq=None, subset=False, traj=None,
+                  pos_offset=0):
+    """One block-diffusion remasking step, in place on ``tokens`` [B, S] (int64).
+
+    Among the masked positions of block [a0, a0 + bl) every row commits the ``tc``
+    with the highest ``prio`` [B * bl] (ties: lower position; None: earliest first)
+    to its ``drawn`` [B * bl] token.  Returns (chosen positions + ``pos_offset`` in
+    increasing order [B, tc], chosen tokens [B, tc], the step's log density [B] in
+    float64 or None without ``logq``); ``traj`` [B] float64 accumulates the density,
+    plus log 1 / C(masked, tc) with ``subset``.
+    """
+    B = tokens.shape[0]
+    dev = tokens.device
+    out_pos = torch.empty(B, tc, dtype=torch.int64, device=dev)
+    out_tok = torch.empty(B, tc, dtype=torch.int64, device=dev)
+    step_lp = torch.empty(B, dtype=torch.float64, device=dev) if logq is not None else None
+    if tokens.is_cuda:
+        _ext.require().remask_select(tokens, int(a0), int(bl), int(mask_id), drawn.to(torch.int32).contiguous(),
+                                     None if prio is None else prio.float().contiguous(),
+                                     None if logq is None else logq.float().contiguous(), int(tc), bool(subset),
+                                     traj, step_lp, out_pos, out_tok, int(pos_offset))
+        return out_pos, out_tok, step_lp
+    masked = tokens[:, a0:a0 + bl] == mask_id
+    positions = torch.arange(bl, device=dev)
+    p = (-positions.float()).expand(B, bl) if prio is None else prio.view(B, bl).float()
+    p = p.masked_fill(~masked, float("-inf"))
+    # rank by (priority descending, position ascending)
+    order = torch.argsort(-p, dim=1, stable=True)
+    sel = order[:, :tc].sort(dim=1).values
+    chosen = drawn.view(B, bl).long().gather(1, sel)
+    tokens[:, a0:a0 + bl].scatter_(1, sel, chosen)
+    out_pos.copy_(sel + pos_offset)
+    out_tok.copy_(chosen)
+    if logq is not None:
+        lp = logq.view(B, bl).double().gather(1, sel).sum(1)
+        if subset:
+            n = masked.sum(1).double()
+            lp = lp - (torch.lgamma(n + 1) - math.lgamma(tc + 1) - torch.lgamma(n - tc + 1))
+        step_lp.copy_(lp)
+        if traj is not None:
+            traj += lp
+    return out_pos, out_tok, step_lp
+
+
 @dataclass
 class VocabShard:
     """This rank's slice [v_lo, v_lo + width) of a vocabulary of v_total columns (tensor parallel).

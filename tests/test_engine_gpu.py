@@ -85,12 +85,12 @@ def test_forked_sequences_share_prefix_pages():
     assert cache.free_pages == cache.num_pages
 
 
-@pytest.mark.parametrize("graphs", [False, True])
-def test_mh_engine_logprobs_are_exact(graphs):
+@pytest.mark.parametrize("graphs,policy", [(False, "always"), (True, "always"), (True, "adaptive")])
+def test_mh_engine_logprobs_are_exact(graphs, policy):
     """Every emitted token's log p / log q must equal the oracle's log-softmax of the chain prefix."""
     cfg = SMALL
     eng = build_mh_engine(cfg, seed=3, alpha=2.0, length=24, block_size=4, learner_stride=8, use_graphs=graphs,
-                          kv_bytes=64 << 20, max_seq_tokens=64, max_batch=8)
+                          kv_bytes=64 << 20, max_seq_tokens=64, max_batch=8, spec_policy=policy, probe_every=3)
     prompt = list(range(5, 21))
     eng.add_chains([prompt] * 6)
     eng.run_until_idle()
@@ -112,6 +112,8 @@ def test_mh_engine_logprobs_are_exact(graphs):
     held = sum(1 for p in range(eng.cache.num_pages) if eng.cache.manager.refcount(p) > 0)
     assert held <= 6 * 2 + 2
     assert eng.mean_accept_length >= 1.0
+    if policy == "adaptive":
+        assert eng.stats["spec_rounds"] > 0 and eng.stats["plain_rounds"] > 0
     workspace.check_status()
 
 
@@ -156,7 +158,7 @@ def test_online_learner_raises_acceptance():
     head = DraftHead(runner, draft, block_size=4)
     learner = SuffixLearner(head, SuffixConfig(stride=4, learning_rate=2e-3), use_graphs=True)
     eng = MHEngine(runner, head, alpha=4.0, length=64, root_seed=7, learner=learner, use_graphs=True,
-                   max_pages_per_seq=8)
+                   max_pages_per_seq=8, spec_policy="always")
     eng.add_chains([list(range(5, 37))] * 8)
     eng.set_quota(10_000)
 

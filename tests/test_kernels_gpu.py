@@ -308,6 +308,33 @@ def test_head_stats_match_fp32_oracle(cuda, rows, V):
     workspace.check_status()
 
 
+@pytest.mark.parametrize("bl,tc,mode", [(32, 4, "prio"), (32, 32, "prio"), (256, 17, "prio"), (64, 8, "position"),
+                                         (96, 5, "subset")])
+def test_remask_select_matches_torch_path(cuda, bl, tc, mode):
+    torch.manual_seed(bl + tc)
+    B, P, mask = 6, 40, 999
+    S = P + 2 * bl
+    tokens = torch.randint(0, 500, (B, S), dtype=torch.int64)
+    a0 = P + bl
+    region = torch.rand(B, bl) < 0.6
+    region[:, :tc] = True                                 # at least tc masked positions per row
+    tokens[:, a0:a0 + bl] = torch.where(region, torch.full_like(region, mask, dtype=torch.int64),
+                                        tokens[:, a0:a0 + bl])
+    drawn = torch.randint(0, 500, (B * bl,), dtype=torch.int32)
+    prio = None if mode == "position" else torch.randn(B * bl)
+    logq = -torch.rand(B * bl) * 5
+    traj_cpu = torch.zeros(B, dtype=torch.float64)
+    traj_gpu = traj_cpu.to(cuda)
+    t_cpu, t_gpu = tokens.clone(), tokens.to(cuda)
+    want = ops.remask_select(t_cpu, a0, bl, mask, drawn, tc, prio=prio, logq=logq, subset=mode == "subset",
+                             traj=traj_cpu, pos_offset=bl)
+    got = ops.remask_select(t_gpu, a0, bl, mask, drawn.to(cuda), tc, prio=None if prio is None else prio.to(cuda),
+                            logq=logq.to(cuda), subset=mode == "subset", traj=traj_gpu, pos_offset=bl)
+    assert torch.equal(t_gpu.cpu(), t_cpu)
+    assert torch.equal(got[0].cpu(), want[0]) and torch.equal(got[1].cpu(), want[1])
+    assert torch.allclose(got[2].cpu(), want[2], atol=1e-9) and torch.allclose(traj_gpu.cpu(), traj_cpu, atol=1e-9)
+
+
 def test_row_stats(cuda):
     x = torch.randn(10, 50000, device=cuda) * 2
     it = torch.full((10,), 2.0, device=cuda)
@@ -368,7 +395,7 @@ def test_row_stats_split_rows_match_one_cta_per_row(cuda):
         for _ in range(2):
             got = ops.row_stats(logits, inv, tg)
             want = [torch.empty(R, device=cuda) for _ in range(4)]
-            _ext.require().row_stats(logits, inv, tg, *want, None, None)
+            _ext.require().row_stats(logits, inv, tg, *want, None, None, None, None)
             for g, w in zip(got, want):
                 assert torch.allclose(g, w, atol=1e-4, rtol=1e-5)
         ref = torch.logsumexp(logits.double(), -1)
