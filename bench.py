@@ -260,7 +260,7 @@ def run_ours(args, rank, world, local, group) -> dict:
     h2d = (st["h2d_bytes"] - stats0["h2d_bytes"]) / args.steps + args.chains * args.gen_len * 4 * 0
     d2h = (st["d2h_bytes"] - stats0["d2h_bytes"]) / args.steps + args.chains * args.gen_len * 4
     value = generated / (ms / 1e3)
-    accept_len = emitted / max(1, blocks)
+    accept_len = emitted / blocks if blocks else None       # over the speculative rounds
     out = {
         "metric": METRIC,
         "value": value,

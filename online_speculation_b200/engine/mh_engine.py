@@ -80,7 +80,7 @@ class _RoundGraph:
     def __init__(self, engine: "MHEngine", B: int, use_graph: bool, Kb: int):
         self.e = engine
         self.B = B
-        self.Kb = Kb                      # 1: plain decoding round (no draft)
+        self.Kb = Kb
         dev = engine.device
         mp = engine.max_pages
         self.mp = mp
@@ -158,9 +158,6 @@ class _RoundGraph:
     def _body(self):
         e, B, Kb = self.e, self.B, self.Kb
         v = self.views
-        if Kb == 1:
-            self._body_plain()
-            return
         self.ids_draft[:, 0].copy_(v["anchors"])
         self.active.copy_(v["active"])
         self.row_streams.copy_(v["streams"].repeat_interleave(Kb - 1))
@@ -187,23 +184,6 @@ class _RoundGraph:
         self.result[:, 2:2 + Kb].copy_(o["emitted"])
         self.result[:, 2 + Kb:2 + 2 * Kb].copy_(o["logq"])
         self.result[:, 2 + 2 * Kb:].copy_(o["logp"])
-
-    def _body_plain(self):
-        """Plain decoding (no draft): one token per job from the target at temperature 1 / alpha."""
-        e, B = self.e, self.B
-        v = self.views
-        self.ids_verify[:, 0].copy_(v["anchors"])
-        meta = StepMeta(self.ids_verify.view(-1), v["positions"], v["slots"], self.plan_verify, None)
-        logits = e.runner.forward(meta)
-        tok = self.out["emitted"][:, 0]
-        K.gumbel_sample(logits, self.inv_temp, self.seeds, streams=v["streams"], salt=0x777, tokens=tok)
-        _, _, logp, logq = K.row_stats(logits, self.inv_temp, tok)
-        o = self.out
-        self.result[:, 0].zero_()
-        self.result[:, 1].fill_(1.0)
-        self.result[:, 2].copy_(tok)
-        self.result[:, 3].copy_(logq)
-        self.result[:, 4].copy_(logp)
 
     def _capture(self):
         from ..ops import _ext
@@ -238,12 +218,124 @@ class _RoundGraph:
         return self.result_host
 
 
+class _PlainGraph:
+    """Static buffers (and optionally a captured CUDA graph) of S chained plain decode steps for B jobs.
+
+    Step s decodes one token per job from the target at the proposal temperature:
+    its input ids are row s of ``ids`` and the drawn tokens land in row s + 1, so a
+    replay decodes S tokens per job with one host round trip.  Positions, KV slots,
+    KV lengths and the random streams of all S steps are uploaded before the replay.
+    """
+
+    def __init__(self, engine: "MHEngine", B: int, S: int, use_graph: bool):
+        self.e = engine
+        self.B, self.S = B, S
+        dev = engine.device
+        r = engine.runner
+        mp = engine.max_pages
+        self.mp = mp
+        self.layout = [("positions", S * B), ("slots", S * B), ("kv_len", S * B), ("streams", S * B),
+                       ("table", B * mp), ("anchors", B)]
+        total = sum(n for _, n in self.layout)
+        self.host = torch.zeros(total, dtype=torch.int32).pin_memory()
+        self.dev = torch.zeros(total, dtype=torch.int32, device=dev)
+        self.views, self.host_views, off = {}, {}, 0
+        host_np = self.host.numpy()
+        for name, n in self.layout:
+            self.views[name] = self.dev[off:off + n]
+            self.host_views[name] = host_np[off:off + n]
+            off += n
+        for name in ("positions", "slots", "kv_len", "streams"):
+            self.views[name] = self.views[name].view(S, B)
+            self.host_views[name] = self.host_views[name].reshape(S, B)
+        self.seeds_host = torch.zeros(B, dtype=torch.int64).pin_memory()
+        self.seeds_np = self.seeds_host.numpy()
+        self.seeds = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.inv_temp = torch.full((B,), engine.inv_temp, dtype=torch.float32, device=dev)
+        self.ids = torch.zeros(S + 1, B, dtype=torch.int32, device=dev)
+        self.logq = torch.zeros(S, B, dtype=torch.float32, device=dev)
+        self.logp = torch.zeros(S, B, dtype=torch.float32, device=dev)
+        table = self.views["table"].view(B, mp)
+        G = r.q_slots // r.kv_slots
+        tr = K.attention_tile_rows(G, B * r.kv_slots, mp * K.PAGE_SIZE)
+        tiles = -(-G // tr)
+        q_start = torch.arange(B, dtype=torch.int32, device=dev)
+        q_len = torch.ones(B, dtype=torch.int32, device=dev)
+        mode = torch.zeros(B, dtype=torch.int32, device=dev)
+        tile_seq = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(tiles)
+        tile_row = (torch.arange(tiles, dtype=torch.int32, device=dev) * tr).repeat(B)
+        splits = K.attention_kv_splits(B * tiles * r.kv_slots, mp * K.PAGE_SIZE) if tr == K.TC_TILE_ROWS else 1
+        self.plans = [K.AttentionPlan(table, q_start, q_len, self.views["kv_len"][s], mode, tile_seq, tile_row, tr,
+                                      {}, splits) for s in range(S)]
+        # packed result [B, 2 + 3 S] for one D2H copy: (S - 1, valid, tokens, log q, log p)
+        self.result = torch.zeros(B, 2 + 3 * S, dtype=torch.float32, device=dev)
+        self.result[:, 0] = S - 1
+        self.result[:, 1] = 1
+        self.result_host = torch.zeros(B, 2 + 3 * S, dtype=torch.float32).pin_memory()
+        self.graph = None
+        self.runs = 0
+        self.launches_per_round = 0
+        if use_graph:
+            self._capture()
+
+    def _body(self):
+        e, S = self.e, self.S
+        v = self.views
+        self.ids[0].copy_(v["anchors"])
+        shard = e.runner.vocab_shard
+        for s in range(S):
+            meta = StepMeta(self.ids[s], v["positions"][s], v["slots"][s], self.plans[s], None)
+            if shard is None:
+                logits = e.runner.forward(meta)
+                K.gumbel_sample(logits, self.inv_temp, self.seeds, streams=v["streams"][s], salt=0x777,
+                                tokens=self.ids[s + 1])
+                _, _, lp, lq = K.row_stats(logits, self.inv_temp, self.ids[s + 1])
+                self.logq[s].copy_(lq)
+                self.logp[s].copy_(lp)
+                continue
+            # vocabulary-parallel: local-shard draw (global noise keys), exchanged row scalars only
+            local = e.runner.forward(meta, gather=False)
+            tok = self.ids[s + 1]
+            K.gumbel_sample(local, self.inv_temp, self.seeds, streams=v["streams"][s], salt=0x777, tokens=tok,
+                            shard=shard)
+            lse1, lseT, _, _ = K.row_stats(local, self.inv_temp)
+            lse = shard.logsumexp(torch.stack((lse1, lseT)))
+            col = tok.long() - shard.v_lo
+            own = (col >= 0) & (col < shard.width)
+            logit = shard.buf("plain_token_logit", (self.B,), torch.float32, local.device)
+            logit.copy_(torch.where(own, local.gather(1, col.clamp(0, shard.width - 1)[:, None]).squeeze(1), 0.0))
+            shard.all_reduce(logit)
+            self.logq[s].copy_(logit * self.inv_temp - lse[1])
+            self.logp[s].copy_(logit - lse[0])
+        self.result[:, 2:2 + S].copy_(self.ids[1:].t())
+        self.result[:, 2 + S:2 + 2 * S].copy_(self.logq.t())
+        self.result[:, 2 + 2 * S:].copy_(self.logp.t())
+
+    _capture = _RoundGraph._capture
+
+    def run(self):
+        self.runs += 1
+        self.e.stats["h2d_bytes"] += self.host.numel() * 4 + self.seeds_host.numel() * 8
+        self.e.stats["d2h_bytes"] += self.result_host.numel() * 4
+        self.dev.copy_(self.host, non_blocking=True)
+        self.seeds.copy_(self.seeds_host, non_blocking=True)
+        if self.graph is not None:
+            self.graph.replay()
+            self.e.stats["graph_kernel_launches"] += self.launches_per_round
+        else:
+            self._body()
+        self.result_host.copy_(self.result, non_blocking=True)
+        torch.cuda.current_stream(self.e.device).synchronize()
+        return self.result_host
+
+
 class MHEngine:
     """Suffix-MH chains with speculative block drafting on one TP group."""
 
     def __init__(self, runner: ModelRunner, head: DraftHead | None, *, alpha: float = 4.0, length: int = 512,
                  root_seed: int = 0, learner: SuffixLearner | None = None, use_graphs: bool = True,
-                 max_pages_per_seq: int | None = None, spec_policy: str = "adaptive", probe_every: int = 8):
+                 max_pages_per_seq: int | None = None, spec_policy: str = "adaptive", probe_every: int = 8,
+                 plain_steps: int = 4):
         self.runner = runner
         self.head = head
         self.cache: KVCache = runner.cache
@@ -263,6 +355,9 @@ class MHEngine:
             raise ValueError("spec_policy is adaptive, always or never")
         self.spec_policy = spec_policy if head is not None else "never"
         self.probe_every = probe_every
+        if plain_steps < 1:
+            raise ValueError("plain_steps must be positive")
+        self.plain_steps = plain_steps    # chained decode steps per plain round
         # per-round wall time (EMA) of speculative and plain rounds and the mean emitted tokens per
         # speculative block; the adaptive policy compares expected tokens per second of the two
         self._t_spec = self._t_plain = None
@@ -386,7 +481,7 @@ class MHEngine:
 
         ``always`` / ``never`` are fixed.  ``adaptive`` drafts when the expected
         tokens per second of a speculative round, (mean emitted per block) / (its
-        time), beat those of a plain one, 1 / (its time); both times and the
+        time), beat those of a plain one, ``plain_steps`` / (its time); both times and the
         acceptance are running means of measured rounds.  While a learner is
         attached, or before both kinds have been measured, a speculative round runs
         at least every ``probe_every`` rounds, so the draft keeps learning from
@@ -401,22 +496,23 @@ class MHEngine:
             return False
         if self._since_spec + 1 >= self.probe_every:
             return True
-        return self._accept_ema * self._t_plain > self._t_spec
+        return self._accept_ema * self._t_plain > self._t_spec * self.plain_steps
 
-    def round(self) -> int:
-        """Advance every active job by one round (speculative or plain); returns tokens generated."""
-        jobs = sorted(self.jobs.values(), key=lambda j: j.chain)
-        if not jobs:
-            return 0
-        speculate = self._speculate_next()
-        Kb = self.block if speculate else 1
-        started = time.perf_counter()
-        self.cache.flush_copies()
+    def _plain_graph(self, B: int) -> _PlainGraph:
+        bucket = next(b for b in BUCKETS if b >= B) if B <= BUCKETS[-1] else B
+        key = (bucket, -self.plain_steps)
+        g = self._graphs.get(key)
+        if g is None:
+            g = _PlainGraph(self, bucket, self.plain_steps, self.use_graphs)
+            self._graphs[key] = g
+        return g
+
+    def _run_spec(self, jobs, seqs, n):
+        """One speculative round: returns (packed result, block width)."""
+        Kb = self.block
         g = self._graph(len(jobs), Kb)
         B, nj = g.B, len(jobs)
         hv = g.host_views
-        seqs = [j.seq for j in jobs]
-        n = np.fromiter((j.n for j in jobs), dtype=np.int64, count=nj)
         slots = np.asarray(self.cache.manager.append_many(seqs, Kb), dtype=np.int32).reshape(nj, Kb)
         pos = hv["positions"].reshape(B, Kb)
         sl = hv["slots"].reshape(B, Kb)
@@ -438,21 +534,65 @@ class MHEngine:
             hv["active"][nj:] = 0
             table[nj:] = 0
         res = g.run().numpy()
-        counts = res[:, 0].astype(np.int64)
         if (res[:nj, 1] == 0).any():
             raise RuntimeError("speculative correction reported invalid probabilities")
-        if self.learner is not None and speculate:
+        if self.learner is not None:
             fb = FeedbackRound(g.ids_draft, g.views["positions"].view(B, Kb), g.views["table"].view(B, g.mp),
                                g.teacher, g.out["count"], g.active, nj)
             if self.learner.observe(fb):
                 self.stats["learner_updates"] += 1
+        for j in jobs:
+            j.rounds += 1
+        return res, Kb, g.runs
+
+    def _run_plain(self, jobs, seqs, n):
+        """``plain_steps`` chained decode steps: returns (packed result, steps)."""
+        S = self.plain_steps
+        g = self._plain_graph(len(jobs))
+        B, nj = g.B, len(jobs)
+        hv = g.host_views
+        slots = np.asarray(self.cache.manager.append_many(seqs, S), dtype=np.int32).reshape(nj, S)
+        steps = np.arange(S)[:, None]
+        hv["positions"][:, :nj] = n[None, :] + steps
+        hv["slots"][:, :nj] = slots.T
+        hv["kv_len"][:, :nj] = n[None, :] + 1 + steps
+        hv["streams"][:, :nj] = np.asarray([j.rounds for j in jobs])[None, :] + steps
+        hv["anchors"][:nj] = [j.anchor for j in jobs]
+        g.seeds_np[:nj] = [j.seed & ((1 << 63) - 1) for j in jobs]
+        table = hv["table"].reshape(B, g.mp)
+        self.cache.manager.fill_table_np(seqs, table[:nj])
+        if nj < B:  # padding rows: no cache writes
+            hv["positions"][:, nj:] = steps
+            hv["slots"][:, nj:] = -1
+            hv["kv_len"][:, nj:] = 1 + steps
+            hv["streams"][:, nj:] = 0
+            hv["anchors"][nj:] = 0
+            table[nj:] = 0
+        res = g.run().numpy()
+        for j in jobs:
+            j.rounds += S
+        return res, S, g.runs
+
+    def round(self) -> int:
+        """Advance every active job by one round (speculative or plain); returns tokens generated."""
+        jobs = sorted(self.jobs.values(), key=lambda j: j.chain)
+        if not jobs:
+            return 0
+        speculate = self._speculate_next()
+        started = time.perf_counter()
+        self.cache.flush_copies()
+        seqs = [j.seq for j in jobs]
+        nj = len(jobs)
+        n = np.fromiter((j.n for j in jobs), dtype=np.int64, count=nj)
+        res, W, runs = self._run_spec(jobs, seqs, n) if speculate else self._run_plain(jobs, seqs, n)
+        counts = res[:nj, 0].astype(np.int64)
+        emitted = res[:nj, 2:2 + W].astype(np.int64)
+        logq = res[:nj, 2 + W:2 + 2 * W]
+        logp = res[:nj, 2 + 2 * W:2 + 3 * W]
+        new_len = n + 1 + counts
+        self.cache.manager.truncate_many(seqs, new_len.tolist())
         generated = 0
         finished = []
-        emitted = res[:, 2:2 + Kb].astype(np.int64)
-        logq = res[:, 2 + Kb:2 + 2 * Kb]
-        logp = res[:, 2 + 2 * Kb:2 + 3 * Kb]
-        new_len = n + 1 + counts[:nj]
-        self.cache.manager.truncate_many(seqs, new_len.tolist())
         for b, j in enumerate(jobs):
             c = int(counts[b])
             take = min(c + 1, j.need - len(j.tokens))
@@ -460,7 +600,6 @@ class MHEngine:
             j.logq.extend(logq[b, :take].tolist())
             j.logp.extend(logp[b, :take].tolist())
             generated += take
-            j.rounds += 1
             j.anchor = int(emitted[b, c])
             j.n = int(new_len[b])
             if len(j.tokens) >= j.need:
@@ -468,14 +607,14 @@ class MHEngine:
         self.stats["rounds"] += 1
         self.stats["generated"] += generated
         if speculate:
-            self.stats["emitted"] += int((counts[:nj] + 1).sum())
+            self.stats["emitted"] += int((counts + 1).sum())
             self.stats["blocks"] += nj
             self.stats["spec_rounds"] += 1
         else:
             self.stats["plain_rounds"] += 1
         for j in finished:
             self._finish(j)
-        self._note_round(speculate, time.perf_counter() - started, float((counts[:nj] + 1).mean()), g.runs == 1)
+        self._note_round(speculate, time.perf_counter() - started, float((counts + 1).mean()), runs == 1)
         return generated
 
     def _note_round(self, speculate: bool, seconds: float, emitted_per_job: float, first_run: bool) -> None:

@@ -127,7 +127,7 @@ def test_mh_engine_without_draft_is_exact():
     eng.run_until_idle()
     eng.set_quota(2)
     eng.run_until_idle()
-    assert eng.stats["mh_updates"] == 8 and eng.mean_accept_length == 1.0
+    assert eng.stats["mh_updates"] == 8 and eng.stats["spec_rounds"] == 0 and eng.stats["plain_rounds"] > 0
     sd = {k: v.cpu() for k, v in random_state_dict(cfg, seed=3, std=0.02, device="cuda").items()}
     for ch in eng.chains:
         full = torch.tensor(ch.prompt + ch.tokens)

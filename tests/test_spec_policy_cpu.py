@@ -6,7 +6,8 @@ from online_speculation_b200.engine.mh_engine import MHEngine
 
 
 def _state(**kw):
-    base = dict(spec_policy="adaptive", probe_every=8, _t_spec=None, _t_plain=None, _accept_ema=None, _since_spec=0)
+    base = dict(spec_policy="adaptive", probe_every=8, plain_steps=1, _t_spec=None, _t_plain=None, _accept_ema=None,
+                _since_spec=0)
     base.update(kw)
     return SimpleNamespace(**base)
 
@@ -25,3 +26,6 @@ def test_adaptive_measures_both_then_compares_tokens_per_second():
     assert MHEngine._speculate_next(_state(_t_spec=9.3, _t_plain=4.3, _accept_ema=3.0, _since_spec=2))
     # a probe round is due after probe_every - 1 plain rounds
     assert MHEngine._speculate_next(_state(_t_spec=9.3, _t_plain=4.3, _accept_ema=1.01, _since_spec=7))
+    # a plain round of 4 chained steps yields 4 tokens per job: 3 tokens per 9.3 ms lose to 4 per 12 ms
+    assert not MHEngine._speculate_next(_state(_t_spec=9.3, _t_plain=12.0, _accept_ema=3.0, _since_spec=2,
+                                               plain_steps=4))
