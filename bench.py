@@ -75,6 +75,7 @@ def parse():
                    help="draft every round (always) or where the measured acceptance makes it pay (adaptive)")
     p.add_argument("--probe-every", type=int, default=8,
                    help="adaptive policy: at least one speculative round per this many rounds")
+    p.add_argument("--plain-steps", type=int, default=4, help="decode steps chained in one plain round")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-gb", type=float, default=24.0)
@@ -212,7 +213,8 @@ def run_ours(args, rank, world, local, group) -> dict:
                              block_size=args.block, learner_stride=None if args.no_learner else args.stride,
                              use_graphs=not args.no_graphs, kv_bytes=int(args.kv_gb * 2**30),
                              max_seq_tokens=args.prompt_len + args.gen_len + 2 * args.block,
-                             draft=not args.no_draft, spec_policy=args.spec_policy, probe_every=args.probe_every)
+                             draft=not args.no_draft, spec_policy=args.spec_policy, probe_every=args.probe_every,
+                             plain_steps=args.plain_steps)
     rng = np.random.default_rng(args.seed + 17)
     vocab = engine.runner.cfg.vocab_size
     # one uniform-random prompt shared by the chains (the reference API's shape)
@@ -282,6 +284,7 @@ def run_ours(args, rank, world, local, group) -> dict:
                    "learner_stride_blocks": None if (args.no_learner or args.no_draft) else args.stride,
                    "spec_policy": "none" if args.no_draft else args.spec_policy,
                    "probe_every": args.probe_every if args.spec_policy == "adaptive" else None,
+                   "plain_steps": args.plain_steps,
                    "l2": "weights (15 GB) streamed every round exceed the 126 MB L2",
                    "step": "64 completed MH updates; chains run asynchronously (no lock-step barrier)"},
         "spec_accept_len": accept_len,
