@@ -101,12 +101,10 @@ class SymmetricCollectives(NcclCollectives):
         self._parts_ptrs = [list(h.buffer_ptrs) for h in self._handles]
         self._rows_ptrs = list(self._rows_h.buffer_ptrs)
         self._pads = list(self._rows_h.signal_pad_ptrs)
-        if push is None:
-            # Off by default: measured on two B200s (7B verify round, bench.py --gpus 2) the
-            # push variant ran 8147 tok/s against 8626 for the pull all-reduce -- the GEMM
-            # epilogue's extra peer stores and its closing system fence cost more than the
-            # overlap gains.  OSB_TP_PUSH=1 enables it.
-            push = os.environ.get("OSB_TP_PUSH", "0") == "1"
+        # Off unless asked for: measured on two B200s (7B verify round, bench.py --gpus 2) the
+        # push variant ran 8147 tok/s against 8626 for the pull all-reduce -- the GEMM
+        # epilogue's extra peer stores and its closing system fence cost more than the
+        # overlap gains.
         self.push = bool(push) and self.world <= 4
         if self.push:
             # receive buffers [world, max_tokens, hidden] per flip; slot q holds rank q's partial
