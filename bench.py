@@ -76,6 +76,8 @@ def parse():
     p.add_argument("--probe-every", type=int, default=8,
                    help="adaptive policy: at least one speculative round per this many rounds")
     p.add_argument("--plain-steps", type=int, default=4, help="decode steps chained in one plain round")
+    p.add_argument("--distinct-prompts", action="store_true",
+                   help="a different uniform-random prompt per chain (no shared prefix pages)")
     p.add_argument("--no-graphs", action="store_true")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--kv-gb", type=float, default=24.0)
@@ -218,9 +220,12 @@ def run_ours(args, rank, world, local, group) -> dict:
     rng = np.random.default_rng(args.seed + 17)
     vocab = engine.runner.cfg.vocab_size
     # one uniform-random prompt shared by the chains (the reference API's shape)
-    prompt_host = torch.from_numpy(rng.integers(0, vocab - 2, size=(1, args.prompt_len)).astype(np.int32)).pin_memory()
+    rows = args.chains if args.distinct_prompts else 1
+    prompt_host = torch.from_numpy(rng.integers(0, vocab - 2, size=(rows, args.prompt_len)).astype(np.int32))
+    prompt_host = prompt_host.pin_memory()
     prompt_dev = prompt_host.to("cuda", non_blocking=True)
-    engine.add_chains(prompt_dev.cpu().tolist() * args.chains)
+    prompts = prompt_dev.cpu().tolist()
+    engine.add_chains(prompts if args.distinct_prompts else prompts * args.chains)
     engine.run_until_idle()                       # initial extension of every chain to 512 tokens
     # Chains run asynchronously: a chain starts its next update as soon as its
     # proposal is decided.  A step is `chains` completed updates (in any order).
@@ -277,7 +282,8 @@ def run_ours(args, rank, world, local, group) -> dict:
         "dtype": "bf16",
         "data": "synthetic (uniform-random prompt ids, random-init weights)",
         "config": {"model": f"{args.model} (random init)", "global_batch": args.chains, "seq_len": args.prompt_len + args.gen_len,
-                   "prompt": "one uniform-random prompt shared by all chains",
+                   "prompt": ("a distinct uniform-random prompt per chain" if args.distinct_prompts
+                              else "one uniform-random prompt shared by all chains"),
                    "prompt_len": args.prompt_len, "gen_len": args.gen_len, "parallelism": f"tp{world}",
                    "mh_alpha": args.alpha,
                    "draft": "none (plain decoding)" if args.no_draft else f"1-layer block-{args.block} draft head",
@@ -457,6 +463,9 @@ def run_grpo(args, rank, world, local, group) -> dict:
 
 
 def run_reference(args, rank, world, local, group) -> dict:
+    if args.distinct_prompts:
+        return {"impl": "reference", "unavailable": "the reference's batched MH API (run_mh_chains_batched) "
+                                                    "takes one prompt for all chains"}
     ref = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "inference_scaling")):
         return {"impl": "reference", "unavailable": "reference package not installed under baseline/_ref"}
