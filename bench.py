@@ -76,6 +76,7 @@ def parse():
     p.add_argument("--probe-every", type=int, default=8,
                    help="adaptive policy: at least one speculative round per this many rounds")
     p.add_argument("--plain-steps", type=int, default=4, help="decode steps chained in one plain round")
+    p.add_argument("--json-out", help="also write the result line to this file (rank 0)")
     p.add_argument("--distinct-prompts", action="store_true",
                    help="a different uniform-random prompt per chain (no shared prefix pages)")
     p.add_argument("--no-graphs", action="store_true")
@@ -804,6 +805,10 @@ def main():
         pass
     if rank == 0:
         print(json.dumps(out), flush=True)
+        if args.json_out:
+            os.makedirs(os.path.dirname(os.path.abspath(args.json_out)), exist_ok=True)
+            with open(args.json_out, "w", encoding="utf-8") as handle:
+                handle.write(json.dumps(out) + "\n")
     if world > 1:
         import gc
 
