@@ -37,6 +37,9 @@ def main(argv=None) -> int:
     p.add_argument("--policy", choices=("always", "never", "adaptive"), default="always",
                    help="speculation policy of the engine (never: plain decode rounds only)")
     p.add_argument("--plain-steps", type=int, default=4)
+    p.add_argument("--no-pdl", action="store_true",
+                   help="launch without programmatic dependent launch, so each kernel's traced duration is its "
+                        "own (with it, a kernel's span includes its wait for the predecessor)")
     p.add_argument("--kernel-table", help="write a per-kernel device-time table of the bracketed rounds "
                                           "(CUDA activity trace through torch.profiler) to this JSON file; "
                                           "{rank} in the name is replaced by the rank")
@@ -60,6 +63,10 @@ def main(argv=None) -> int:
         group, rank = dist.group.WORLD, dist.get_rank()
     else:
         torch.cuda.set_device(0)
+    if a.no_pdl:
+        from ..ops import _ext
+
+        _ext.require().set_pdl(False)
     eng = build_mh_engine(a.model, tp_group=group, seed=a.seed, alpha=4.0, length=a.gen_len, block_size=a.block,
                           learner_stride=a.stride, use_graphs=True, kv_bytes=24 << 30,
                           max_seq_tokens=a.prompt_len + a.gen_len + 2 * a.block, spec_policy=a.policy,
