@@ -127,6 +127,59 @@ class _Rotate:
         return v
 
 
+def _allreduce_probe(a) -> int:
+    """CUDA-event time per call of the fused reduction, max over ranks; bytes = partial rows read per rank."""
+    import datetime
+    import json as _json
+    import os
+
+    import torch.distributed as dist
+
+    from ..parallel.symm import NcclCollectives, SymmetricCollectives
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    world, rank = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", local)
+    group = dist.group.WORLD
+    if a.algorithm == "nccl":
+        comm = NcclCollectives(group, a.hidden, a.T, dev)
+    else:
+        comm = SymmetricCollectives(group, a.hidden, a.T, dev, algorithm=a.algorithm)
+    h = torch.randn(a.T, a.hidden, device=dev).bfloat16()
+    w = torch.ones(a.hidden, device=dev).bfloat16()
+    x = torch.empty_like(h)
+    scratch = torch.empty_like(h)
+
+    def call():
+        part = comm.partial_buffer(a.T) if hasattr(comm, "partial_buffer") else scratch
+        comm.reduce_add_norm(part, h, w, x, 1e-6)
+
+    for _ in range(a.warmup):
+        call()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(a.iters):
+        call()
+    t1.record()
+    torch.cuda.synchronize()
+    us = torch.tensor([t0.elapsed_time(t1) * 1e3 / a.iters], device=dev)
+    dist.all_reduce(us, op=dist.ReduceOp.MAX)
+    K.workspace.check_status(dev)
+    if rank == 0:
+        peer_bytes = (world - 1) * a.T * a.hidden * 2
+        print(_json.dumps({"kind": "allreduce", "world": world, "T": a.T, "hidden": a.hidden, "algorithm": a.algorithm,
+                           "us_per_call_max_over_ranks": float(us), "peer_bytes_read_per_rank": peer_bytes,
+                           "peer_gbs": peer_bytes / float(us) / 1e3}))
+    dist.barrier()
+    del comm
+    dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(prog="python -m online_speculation_b200.utils.kernel_probe")
     sub = p.add_subparsers(dest="kind", required=True)
@@ -163,12 +216,19 @@ def main(argv=None) -> int:
     sa.add_argument("--gumbel", choices=("split", "one-cta"), default=None,
                     help="time the Gumbel-max draft sampler (split rows, or one CTA per row) instead of the "
                          "inverse-CDF sampler")
-    for q in (g, gr, mo, at, sa):
+    ar = sub.add_parser("allreduce", help="tensor-parallel all-reduce + residual + RMSNorm (run under "
+                                          "torch.distributed.run; one process per GPU)")
+    ar.add_argument("T", type=int, help="token rows")
+    ar.add_argument("--hidden", type=int, default=3584)
+    ar.add_argument("--algorithm", choices=("auto", "oneshot", "twoshot", "nccl"), default="auto")
+    for q in (g, gr, mo, at, sa, ar):
         q.add_argument("--iters", type=int, default=20)
         q.add_argument("--warmup", type=int, default=3)
         q.add_argument("--copies", type=int, default=0, help="weight buffers to rotate through (0 = auto)")
         q.add_argument("--no-graph", action="store_true")
     a = p.parse_args(argv)
+    if a.kind == "allreduce":
+        return _allreduce_probe(a)
     dev = torch.device("cuda", torch.cuda.current_device())
     torch.manual_seed(0)
     peaks = _peaks()
