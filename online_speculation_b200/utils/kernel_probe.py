@@ -189,6 +189,8 @@ def main(argv=None) -> int:
     g.add_argument("K", type=int)
     g.add_argument("--swiglu", action="store_true")
     g.add_argument("--residual", action="store_true")
+    g.add_argument("--split-mode", type=int, choices=(0, 1), default=0,
+                   help="split-K across a cluster reduced through DSMEM (0) or through the global workspace (1)")
     g.add_argument("--trace", action="store_true",
                    help="also print the per-CTA timeline of one launch (globaltimer stamps, microseconds)")
     gr = sub.add_parser("grouped")
@@ -246,11 +248,12 @@ def main(argv=None) -> int:
         o = torch.randn(a.N, cols, device=dev).bfloat16()
 
         def body():
-            K.linear(x, ws.next(), swiglu=a.swiglu, residual=o if a.residual else None, out=o)
+            K.linear(x, ws.next(), swiglu=a.swiglu, residual=o if a.residual else None, out=o, split_mode=a.split_mode)
         us = _time(body, a.iters, a.warmup, graph)
         flops = 2 * a.M * a.N * a.K
         bytes_ = wb + a.N * a.K * 2 + a.N * cols * 2 * (2 if a.residual else 1)
-        out.update(M=a.M, N=a.N, K=a.K, us=us, tflops=flops / us / 1e6, gbs=bytes_ / us / 1e3)
+        out.update(M=a.M, N=a.N, K=a.K, split_mode=a.split_mode, us=us, tflops=flops / us / 1e6,
+                   gbs=bytes_ / us / 1e3)
         if a.trace:
             out["timeline"] = _gemm_timeline(body)
     elif a.kind == "grouped":
