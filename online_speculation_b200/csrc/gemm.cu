@@ -42,6 +42,7 @@ constexpr int kUmmaK = 16; // K per tcgen05.mma for 16-bit inputs
 constexpr int kEpiGroups = 2;                      // epilogue warpgroups, alternating 32-token chunks
 constexpr int kThreads = 64 + 128 * kEpiGroups;
 constexpr int kPushMaxRanks = 8;
+constexpr int kMaxClusterSplit = 8;                // portable thread-block cluster size
 
 struct Args {
   int M, N, K;          // M = weight rows (features), N = tokens
@@ -321,13 +322,14 @@ template <int BN>
 __device__ __forceinline__ void cluster_reduce_store(const Args& a, const float* stage, int tm, int tn) {
   const int S = a.cluster;
   const uint32_t rank = cluster_ctarank();
-  const int cs = BN / S;
+  const int cs = (BN + S - 1) / S;          // tokens reduced by each cluster rank (the last may get fewer)
   const bool swiglu = a.epilogue == 1;
   const int width = swiglu ? 64 : kBM;
   const int f0 = swiglu ? tm * 64 : tm * kBM;
   const int out_cols = swiglu ? a.M / 2 : a.M;
   const int vpr = width / 8;
-  const int items = cs * vpr;
+  const int c_end = min(BN, static_cast<int>(rank + 1) * cs);
+  const int items = max(0, c_end - static_cast<int>(rank) * cs) * vpr;
   const uint32_t base = smem_u32(stage);
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
     const int cl = it / vpr;
@@ -339,15 +341,33 @@ __device__ __forceinline__ void cluster_reduce_store(const Args& a, const float*
 #pragma unroll
     for (int e = 0; e < 8; ++e) g[e] = u[e] = 0.0f;
     const uint32_t row = base + static_cast<uint32_t>(c * (kBM + 4) + fl) * 4;
-    for (int q = 0; q < S; ++q) {
-      const uint32_t ra = map_shared_rank(row, q);
-      const float4 x0 = ld_dsmem_f4(ra), x1 = ld_dsmem_f4(ra + 16);
-      g[0] += x0.x; g[1] += x0.y; g[2] += x0.z; g[3] += x0.w;
-      g[4] += x1.x; g[5] += x1.y; g[6] += x1.z; g[7] += x1.w;
-      if (swiglu) {
-        const float4 y0 = ld_dsmem_f4(ra + 64 * 4), y1 = ld_dsmem_f4(ra + 64 * 4 + 16);
-        u[0] += y0.x; u[1] += y0.y; u[2] += y0.z; u[3] += y0.w;
-        u[4] += y1.x; u[5] += y1.y; u[6] += y1.z; u[7] += y1.w;
+    // Issue the loads of four ranks before their adds: DSMEM loads are independent, and
+    // summing in rank order afterwards keeps the result identical to a sequential reduction.
+    constexpr int kBatch = 4;
+    for (int q0 = 0; q0 < S; q0 += kBatch) {
+      float4 xs[kBatch][2], ys[kBatch][2];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (q0 + i < S) {
+          const uint32_t ra = map_shared_rank(row, q0 + i);
+          xs[i][0] = ld_dsmem_f4(ra);
+          xs[i][1] = ld_dsmem_f4(ra + 16);
+          if (swiglu) {
+            ys[i][0] = ld_dsmem_f4(ra + 64 * 4);
+            ys[i][1] = ld_dsmem_f4(ra + 64 * 4 + 16);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (q0 + i < S) {
+          g[0] += xs[i][0].x; g[1] += xs[i][0].y; g[2] += xs[i][0].z; g[3] += xs[i][0].w;
+          g[4] += xs[i][1].x; g[5] += xs[i][1].y; g[6] += xs[i][1].z; g[7] += xs[i][1].w;
+          if (swiglu) {
+            u[0] += ys[i][0].x; u[1] += ys[i][0].y; u[2] += ys[i][0].z; u[3] += ys[i][0].w;
+            u[4] += ys[i][1].x; u[5] += ys[i][1].y; u[6] += ys[i][1].z; u[7] += ys[i][1].w;
+          }
+        }
       }
     }
     const int f = f0 + fl;
@@ -709,9 +729,9 @@ int sm_count(int device) {
 // Largest number of co-resident clusters of `cluster` CTAs for this kernel (cached per device).
 template <int BN>
 int max_active_clusters(int dev, int cluster) {
-  static int cache[64][4] = {};
-  const int slot = cluster == 2 ? 0 : cluster == 4 ? 1 : 2;
-  if (dev < 0 || dev >= 64) return 0;
+  static int cache[64][kMaxClusterSplit + 1] = {};
+  if (dev < 0 || dev >= 64 || cluster < 2 || cluster > kMaxClusterSplit) return 0;
+  const int slot = cluster;
   if (cache[dev][slot] == 0) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cluster * 64);
@@ -766,11 +786,13 @@ cudaError_t launch_bn(const GemmProblem& p, const Args& a0, cudaStream_t stream)
   a.cluster = 1;
   const bool may_split = p.allow_split && p.epilogue != 2;   // statistics need whole accumulators
   if (may_split && p.split_mode == 0 && tiles < sms) {
-    // Split-K across a thread-block cluster (2, 4 or 8 CTAs), reduced through DSMEM.
+    // Split-K across a thread-block cluster of 2..8 CTAs, reduced through DSMEM.
     // Only cluster sizes whose clusters all fit on the GPU at once are used, so
-    // the launch is a single wave.
+    // the launch is a single wave; the largest such size streams the weights with
+    // the most SMs (36 weight tiles: 3-CTA clusters, 108 SMs, where 4-CTA clusters
+    // do not all fit and 2-CTA clusters leave half the GPU idle).
     const int want = sms / tiles;
-    for (int c = 8; c >= 2; c /= 2) {
+    for (int c = kMaxClusterSplit; c >= 2; --c) {
       const int per = (a.k_blocks + c - 1) / c;
       if (c <= want && a.k_blocks >= 2 * c && (c - 1) * per < a.k_blocks &&
           tiles <= max_active_clusters<BN>(dev, c)) {

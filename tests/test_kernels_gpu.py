@@ -18,7 +18,9 @@ def _rel(a, b):
 @pytest.mark.parametrize(
     "M,N,K",
     [(128, 16, 64), (256, 64, 512), (4608, 64, 3584), (3584, 256, 3584), (1000, 37, 200), (512, 300, 1024),
-     (2048, 1024, 1536), (152064 // 8, 64, 3584), (1004, 40, 512), (4736, 256, 512)],
+     (2048, 1024, 1536), (152064 // 8, 64, 3584), (1004, 40, 512), (4736, 256, 512),
+     # split-K over 3-, 5-, 6- and 7-CTA clusters (ragged token slices per cluster rank)
+     (2304, 64, 3584), (3840, 64, 2048), (2944, 48, 4096), (2688, 40, 3584)],
 )
 def test_gemm_matches_fp32(cuda, M, N, K):
     torch.manual_seed(0)
