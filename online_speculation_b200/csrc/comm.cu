@@ -116,6 +116,10 @@ constexpr int kOneShotRegVecs = 4;   // rows up to 256 * 4 * 8 = 8192 wide stay 
 // slot kPushSlot; the kernel waits for those flags and reads only local memory.
 template <bool kPushed>
 __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArArgs a) {
+  // The partials (and the previous call's epoch) belong to the predecessor; every block is
+  // resident once it gets here, so the successor may launch (its own wait covers this grid).
+  pdl_wait();
+  pdl_trigger();
   const uint32_t epoch = *a.epoch + 1;
   const bool ok = kPushed ? wait_flags(a, kPushSlot, epoch) : rank_barrier(a, 2, epoch);
   const int nvec = a.H / 8;
@@ -223,6 +227,7 @@ __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArA
 // block waits for all peers (the grid is sized to be co-resident); phase B
 // copies the other ranks' reduced rows and applies RMSNorm to every row.
 __global__ void __launch_bounds__(kOneShotThreads) twoshot_norm_kernel(const ArArgs a) {
+  pdl_wait();
   const uint32_t epoch = *a.epoch + 1;
   bool ok = rank_barrier(a, 2, epoch);
   const int r0 = slice_begin(a.T, a.world, a.rank), r1 = slice_begin(a.T, a.world, a.rank + 1);
@@ -284,6 +289,7 @@ __global__ void __launch_bounds__(kOneShotThreads) twoshot_norm_kernel(const ArA
     }
   }
   __syncthreads();
+  pdl_trigger();     // every block has passed the phase barrier: the grid no longer needs co-residency
   __shared__ float red[33];
   if (ok && ok2) {
     for (int row = blockIdx.x; row < a.T; row += gridDim.x) {
@@ -341,8 +347,7 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream
     // one row per block (the blocks of a row wait on remote loads; more rows in flight hide that latency)
     const int cap = 4 * blocks;
     const int grid = a.T < cap ? a.T : cap;
-    oneshot_norm_kernel<false><<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(oneshot_norm_kernel<false>, dim3(grid > 0 ? grid : 1), dim3(kOneShotThreads), 0, stream, a);
   }
   // every block of the two-shot kernel waits for the others between its phases: keep the grid co-resident
   static int resident = 0;
@@ -357,16 +362,14 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream
   }
   int grid = blocks < a.T ? blocks : a.T;
   if (grid > resident) grid = resident;
-  twoshot_norm_kernel<<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(twoshot_norm_kernel, dim3(grid > 0 ? grid : 1), dim3(kOneShotThreads), 0, stream, a);
 }
 
 cudaError_t allreduce_pushed_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
   if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
   const int cap = 4 * blocks;
   const int grid = a.T < cap ? a.T : cap;
-  oneshot_norm_kernel<true><<<grid > 0 ? grid : 1, kOneShotThreads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(oneshot_norm_kernel<true>, dim3(grid > 0 ? grid : 1), dim3(kOneShotThreads), 0, stream, a);
 }
 
 }  // namespace osb
