@@ -406,22 +406,26 @@ class EngineBackend:
             S = 1 << (min(self.decode_chunk, rem).bit_length() - 1)     # power of two <= the shortest remainder
             g = self._graph(n, S)
             B = g.B
-            steps = np.arange(S, dtype=np.int32)
+            steps = np.arange(S, dtype=np.int64)[:, None]
+            seqs = [a.seq for a in act]
+            g.h_slots[:, :n] = np.asarray(self.cache.manager.append_many(seqs, S), dtype=np.int64).reshape(n, S).T
+            starts = np.fromiter((a.pos for a in act), dtype=np.int64, count=n)
+            g.h_ids[:n] = [a.last for a in act]
+            g.h_pos[:, :n] = starts[None, :] + steps
+            g.h_kv[:, :n] = starts[None, :] + 1 + steps
+            uni = g.uni_host.numpy()
             for b, a in enumerate(act):
-                g.h_slots[:, b] = self.cache.append(a.seq, S)
-                g.h_ids[b] = a.last
-                g.h_pos[:, b] = a.pos + steps
-                g.h_kv[:, b] = a.pos + 1 + steps
-                t = len(a.tokens)
                 if a.carry is not None:
-                    g.uni_host[:, b] = a.carry
-                    g.arith_host[b] = 1
+                    uni[:, b] = a.carry
                 else:
-                    g.uni_host[:, b] = torch.from_numpy(np.ascontiguousarray(a.uniforms[t:t + S], dtype=np.float64))
-                    g.arith_host[b] = 0
-                g.it_host[b] = 1.0 / a.request.sampling.temperature
-                g.topk_host[b], g.topp_host[b] = self._truncation(a.request.sampling)
-            self.cache.manager.fill_table_np([a.seq for a in act], g.h_table[:n])
+                    t = len(a.tokens)
+                    uni[:, b] = a.uniforms[t:t + S]
+            g.arith_host.numpy()[:n] = [a.carry is not None for a in act]
+            g.it_host.numpy()[:n] = [1.0 / a.request.sampling.temperature for a in act]
+            cuts = [self._truncation(a.request.sampling) for a in act]
+            g.topk_host.numpy()[:n] = [c[0] for c in cuts]
+            g.topp_host.numpy()[:n] = [c[1] for c in cuts]
+            self.cache.manager.fill_table_np(seqs, g.h_table[:n])
             if n < B:
                 g.h_slots[:, n:] = -1
                 g.h_ids[n:] = 0
@@ -434,24 +438,29 @@ class EngineBackend:
                 g.topp_host[n:] = 1.0
             res = g.run()
             self.stats["decode_steps"] += S
+            # per sequence: how many of the S tokens it keeps (up to and including EOS, within budget)
+            toks = res[:, :n, 0].astype(np.int64).T                       # [n, S]
+            eos_ids = np.array([-1 if a.request.sampling.eos_token_id is None else a.request.sampling.eos_token_id
+                                for a in act], dtype=np.int64)
+            hit = toks == eos_ids[:, None]
+            first_eos = np.where(hit.any(1), hit.argmax(1) + 1, S)
+            room = np.array([a.request.max_new_tokens - len(a.tokens) for a in act], dtype=np.int64)
+            keep = np.minimum(first_eos, np.minimum(room, S))
+            logq_cols = res[:, :n, 1].T.tolist()
+            logp_cols = res[:, :n, 2].T.tolist()
+            tok_cols = toks.tolist()
             still = []
             for b, a in enumerate(act):
-                eos = a.request.sampling.eos_token_id
-                start = a.pos
+                k = int(keep[b])
                 if a.carry is not None:
                     a.carry = float(g.carry_host[b])
-                for s in range(S):
-                    tok = int(res[s, b, 0])
-                    a.tokens.append(tok)
-                    a.logq.append(float(res[s, b, 1]))
-                    a.logp.append(float(res[s, b, 2]))
-                    a.last, a.pos = tok, a.pos + 1
-                    if eos is not None and tok == eos:
-                        a.finish = "eos"
-                        break
-                    if len(a.tokens) >= a.request.max_new_tokens:
-                        break
-                if a.pos - start < S:
+                a.tokens.extend(tok_cols[b][:k])
+                a.logq.extend(logq_cols[b][:k])
+                a.logp.extend(logp_cols[b][:k])
+                a.last, a.pos = tok_cols[b][k - 1], a.pos + k
+                if first_eos[b] <= k:
+                    a.finish = "eos"
+                if k < S:
                     self.cache.truncate(a.seq, a.pos)      # drop KV of steps past the sequence's end
                 if a.finish == "eos" or len(a.tokens) >= a.request.max_new_tokens:
                     done.append(a)
@@ -529,41 +538,47 @@ class EngineBackend:
         if chunk:
             groups.append(chunk)
         for grp in groups:
-            ids, pos, slots, qlens, kvlens, seqs = [], [], [], [], [], []
-            rows, targets, inv_t, where = [], [], [], []
+            ids, pos, slots, rows, targets, inv_t = [], [], [], [], [], []
+            qlens, kvlens, seqs, spans = [], [], [], []
             offset = 0
             for i, seq, full, start, n, first_row, inv in grp:
-                slots += self.cache.append(seq, n)
-                ids += list(full[start:start + n])
-                pos += list(range(start, start + n))
+                arr = np.asarray(full, dtype=np.int64)
+                slots.append(np.asarray(self.cache.append(seq, n), dtype=np.int64))
+                ids.append(arr[start:start + n])
+                pos.append(np.arange(start, start + n))
                 qlens.append(n)
                 kvlens.append(start + n)
                 seqs.append(seq)
-                for p in range(max(first_row, start), start + n):
-                    rows.append(offset + p - start)
-                    targets.append(full[p + 1])
-                    inv_t.append(inv)
-                    where.append((i, p - first_row))
+                lo = max(first_row, start)
+                if lo < start + n:
+                    # positions lo .. start+n-1 predict tokens lo+1 .. start+n of the continuation
+                    rows.append(np.arange(lo - start, n) + offset)
+                    targets.append(arr[lo + 1:start + n + 1])
+                    inv_t.append(np.full(start + n - lo, inv, dtype=np.float32))
+                    spans.append((i, lo - first_row, start + n - lo))
                 offset += n
             table = torch.zeros(len(grp), self.max_pages, dtype=torch.int32)
             self.cache.fill_table(seqs, table)
-            meta = build_meta(r.device, table, ids, pos, slots, qlens, kvlens, [0] * len(grp), G,
-                              logit_rows=rows if rows else None, kv_heads=r.kv_slots)
-            self.stats["prefill_tokens"] += len(ids)
+            cat = np.concatenate
+            meta = build_meta(r.device, table, cat(ids), cat(pos), cat(slots), qlens, kvlens, [0] * len(grp), G,
+                              logit_rows=cat(rows) if rows else None, kv_heads=r.kv_slots)
+            self.stats["prefill_tokens"] += offset
             if not rows:
                 r.forward(meta, compute_logits=False)
                 continue
-            it = torch.tensor(inv_t, dtype=torch.float32).to(r.device, non_blocking=True)
-            tg = torch.tensor(targets, dtype=torch.int32).to(r.device, non_blocking=True)
+            it = torch.from_numpy(cat(inv_t)).to(r.device, non_blocking=True)
+            tg = torch.from_numpy(cat(targets).astype(np.int32)).to(r.device, non_blocking=True)
             _, _, _, logq = r.forward_stats(meta, it, tg)
             got = logq.cpu().numpy()
-            for (i, k), v in zip(where, got):
-                values[i][k] = v
-            self.stats["scored_tokens"] += len(rows)
+            at = 0
+            for i, k0, count in spans:
+                values[i][k0:k0 + count] = got[at:at + count]
+                at += count
+            self.stats["scored_tokens"] += at
         for seq, full in opened:
             self._cache_pages(seq, full)
             self.cache.release(seq)
-        return [tuple(float(x) for x in v) for v in values]
+        return [tuple(v.tolist()) for v in values]
 
     def score_statistics_batch(self, requests: Sequence[ScoreRequest], *, confidence_top_k: int | None = None
                                ) -> list[SequenceScoreStatistics]:
