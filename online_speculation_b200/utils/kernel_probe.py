@@ -212,6 +212,10 @@ def main(argv=None) -> int:
     at.add_argument("--kv-splits", type=int, default=None, help="tcgen05 kernel: key splits per tile (default: auto)")
     at.add_argument("--trace", action="store_true",
                     help="tcgen05 kernel: print the per-chunk timeline of the first CTAs (one extra launch)")
+    at.add_argument("--shared-prefix", type=int, default=0,
+                    help="the first this many keys (whole 32-key pages) are the same pages for every sequence")
+    at.add_argument("--flush-l2", action="store_true",
+                    help="write 256 MB between launches (outside the timed spans), as weight streaming would")
     sa = sub.add_parser("sample")
     sa.add_argument("rows", type=int)
     sa.add_argument("V", type=int)
@@ -296,9 +300,13 @@ def main(argv=None) -> int:
     elif a.kind == "attention":
         B, ctx, hq, hkv = a.B, a.ctx, a.heads, a.kv_heads
         pps = -(-ctx // 32)
-        kc = torch.randn(B * pps, hkv, 32, 128, device=dev).bfloat16()
+        shared = min(a.shared_prefix // 32, pps)
+        own = pps - shared
+        kc = torch.randn(shared + B * own, hkv, 32, 128, device=dev).bfloat16()
         vc = torch.randn_like(kc)
-        table = (torch.arange(B, dtype=torch.int32)[:, None] * pps + torch.arange(pps, dtype=torch.int32)[None])
+        table = torch.cat((torch.arange(shared, dtype=torch.int32)[None].expand(B, shared),
+                           shared + torch.arange(B, dtype=torch.int32)[:, None] * own
+                           + torch.arange(own, dtype=torch.int32)[None]), 1).contiguous()
         plan = K.plan_attention(table, [a.qlen] * B, [ctx] * B, [int(a.bidirectional)] * B, hq // hkv, dev,
                                 tile_rows=a.tile_rows, kv_splits=a.kv_splits, kv_heads=hkv)
         q = torch.randn(B * a.qlen, hq, 128, device=dev).bfloat16()
@@ -306,7 +314,22 @@ def main(argv=None) -> int:
 
         def body():
             K.attention(q, kc, vc, plan, out=o)
-        us = _time(body, a.iters, a.warmup, graph)
+        if a.flush_l2:
+            scrub = torch.empty(128 << 20, dtype=torch.float16, device=dev)
+            spans = []
+            for i in range(a.warmup + a.iters):
+                scrub.fill_(float(i % 7))
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                body()
+                e1.record()
+                spans.append((e0, e1))
+            torch.cuda.synchronize()
+            us = sum(x.elapsed_time(y) for x, y in spans[a.warmup:]) * 1e3 / a.iters
+            out["l2"] = "flushed before every launch"
+        else:
+            us = _time(body, a.iters, a.warmup, graph)
+        out["shared_prefix_keys"] = shared * 32
         if a.trace and plan.tile_rows == K.TC_TILE_ROWS:
             buf = torch.zeros(1024, dtype=torch.int64, device=dev)
             ext = K._ext.require()
@@ -315,7 +338,7 @@ def main(argv=None) -> int:
             torch.cuda.synchronize()
             ext.attention_set_trace(None)
             out["trace"] = _attention_timeline(buf.cpu().view(8, 128))
-        bytes_ = 2 * B * ctx * hkv * 128 * 2
+        bytes_ = 2 * (shared * 32 + B * (ctx - shared * 32)) * hkv * 128 * 2    # distinct K/V bytes
         # causal blocks see on average about half of a prompt-sized query range
         seen = ctx if a.bidirectional or a.qlen == 1 else ctx - (a.qlen - 1) / 2
         flops = 4 * B * a.qlen * hq * seen * 128
