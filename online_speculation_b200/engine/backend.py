@@ -443,7 +443,7 @@ class EngineBackend:
             eos_ids = np.array([-1 if a.request.sampling.eos_token_id is None else a.request.sampling.eos_token_id
                                 for a in act], dtype=np.int64)
             hit = toks == eos_ids[:, None]
-            first_eos = np.where(hit.any(1), hit.argmax(1) + 1, S)
+            first_eos = np.where(hit.any(1), hit.argmax(1) + 1, S + 1)   # S + 1: no EOS among the S tokens
             room = np.array([a.request.max_new_tokens - len(a.tokens) for a in act], dtype=np.int64)
             keep = np.minimum(first_eos, np.minimum(room, S))
             logq_cols = res[:, :n, 1].T.tolist()
