@@ -143,8 +143,6 @@ struct Smem {
   static constexpr int kXchgBytes = kEpiGroups * 32 * (kBM + 4) * 4;   // one transpose buffer per group
   static constexpr int kBarBytes = 256;
   static constexpr int kTotal = 1024 + kStages * kStageBytes + kBarBytes + kXchgBytes;
-  // cluster split-K receive rows (at most BN + S - 1 of kBM + 4 floats) reuse the idle pipeline
-  static_assert((BN + kMaxClusterSplit - 1) * (kBM + 4) * 4 <= kStages * kStageBytes, "receive rows do not fit");
 };
 
 // Epilogue of one 32-token chunk.  Every epilogue thread owns one accumulator
@@ -315,10 +313,10 @@ __device__ __forceinline__ void stats_chunk(const Args& a, const float (&v)[32],
   named_barrier(bar, 128);
 }
 
-// Cluster split-K reduction.  CTA `rank` owns tokens [rank * cs, (rank + 1) * cs) of
-// the tile (cs = ceil(BN / S)); every split has pushed its fp32 rows of those tokens
-// into this CTA's receive rows, stage[q * cs + token - rank * cs][feature] (row stride
-// kBM + 4) for split q.  The rows are summed in split order and written with the fused
+// Cluster split-K reduction.  Every CTA of the cluster holds one split's fp32
+// tile in its own shared memory, token-major: stage[c][r] (row stride kBM + 4).
+// CTA `rank` reduces tokens [rank * BN / S, (rank + 1) * BN / S) across all S
+// CTAs through distributed shared memory and writes them with the fused
 // epilogue (bias, SwiGLU, residual) as 16-byte vectors.
 template <int BN>
 __device__ __forceinline__ void cluster_reduce_store(const Args& a, const float* stage, int tm, int tn) {
@@ -332,6 +330,7 @@ __device__ __forceinline__ void cluster_reduce_store(const Args& a, const float*
   const int vpr = width / 8;
   const int c_end = min(BN, static_cast<int>(rank + 1) * cs);
   const int items = max(0, c_end - static_cast<int>(rank) * cs) * vpr;
+  const uint32_t base = smem_u32(stage);
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
     const int cl = it / vpr;
     const int fl = (it % vpr) * 8;
@@ -341,16 +340,34 @@ __device__ __forceinline__ void cluster_reduce_store(const Args& a, const float*
     float g[8], u[8];
 #pragma unroll
     for (int e = 0; e < 8; ++e) g[e] = u[e] = 0.0f;
-    // Received slices of this token from every split, summed in split order.
-    for (int q = 0; q < S; ++q) {
-      const float* src = stage + (q * cs + cl) * (kBM + 4) + fl;
-      const float4 x0 = *reinterpret_cast<const float4*>(src), x1 = *reinterpret_cast<const float4*>(src + 4);
-      g[0] += x0.x; g[1] += x0.y; g[2] += x0.z; g[3] += x0.w;
-      g[4] += x1.x; g[5] += x1.y; g[6] += x1.z; g[7] += x1.w;
-      if (swiglu) {
-        const float4 y0 = *reinterpret_cast<const float4*>(src + 64), y1 = *reinterpret_cast<const float4*>(src + 68);
-        u[0] += y0.x; u[1] += y0.y; u[2] += y0.z; u[3] += y0.w;
-        u[4] += y1.x; u[5] += y1.y; u[6] += y1.z; u[7] += y1.w;
+    const uint32_t row = base + static_cast<uint32_t>(c * (kBM + 4) + fl) * 4;
+    // Issue the loads of four ranks before their adds: DSMEM loads are independent, and
+    // summing in rank order afterwards keeps the result identical to a sequential reduction.
+    constexpr int kBatch = 4;
+    for (int q0 = 0; q0 < S; q0 += kBatch) {
+      float4 xs[kBatch][2], ys[kBatch][2];
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (q0 + i < S) {
+          const uint32_t ra = map_shared_rank(row, q0 + i);
+          xs[i][0] = ld_dsmem_f4(ra);
+          xs[i][1] = ld_dsmem_f4(ra + 16);
+          if (swiglu) {
+            ys[i][0] = ld_dsmem_f4(ra + 64 * 4);
+            ys[i][1] = ld_dsmem_f4(ra + 64 * 4 + 16);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        if (q0 + i < S) {
+          g[0] += xs[i][0].x; g[1] += xs[i][0].y; g[2] += xs[i][0].z; g[3] += xs[i][0].w;
+          g[4] += xs[i][1].x; g[5] += xs[i][1].y; g[6] += xs[i][1].z; g[7] += xs[i][1].w;
+          if (swiglu) {
+            u[0] += ys[i][0].x; u[1] += ys[i][0].y; u[2] += ys[i][0].z; u[3] += ys[i][0].w;
+            u[4] += ys[i][1].x; u[5] += ys[i][1].y; u[6] += ys[i][1].z; u[7] += ys[i][1].w;
+          }
+        }
       }
     }
     const int f = f0 + fl;
@@ -579,8 +596,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t t_acc = tmem_base + lane_base + acc * BN;
       if (a.cluster > 1) {
-        // One split of one tile per CTA: the accumulator stays in TMEM until every CTA of
-        // the cluster has finished its main loop (the pushes below the role branches).
+        // Stage this split's tile token-major into the (now idle) pipeline smem.
+        float* st = reinterpret_cast<float*>(smem);
+        for (int c = grp; c < BN / 32; c += kEpiGroups) {
+          float v[32];
+          tmem_ld32(t_acc + c * 32, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) st[(c * 32 + j) * (kBM + 4) + r] = v[j];
+        }
+        if (ep_lead) trace_stamp(a, 24);
         tc_fence_before();
       } else if (a.splits == 1) {
         for (int c = grp; c < BN / 32; c += kEpiGroups) {
@@ -643,42 +667,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (a.cluster > 1) {
-    // Every CTA holds exactly one split of one tile (grid = tiles x cluster).  Token t of the
-    // tile is reduced by cluster rank t / cs: after the first barrier (every CTA's MMAs are
-    // complete, so every pipeline buffer is idle) each epilogue thread stores its accumulator
-    // row straight into the owning rank's receive rows (remote shared-memory stores do not
-    // wait for a reply), and after the second barrier each rank sums its received slices
-    // from local shared memory.
+    // Every CTA holds exactly one split of one tile (grid = tiles x cluster).
     const int tile = blockIdx.x / a.cluster;
-    const int S = a.cluster;
-    const int cs = (BN + S - 1) / S;
-    cluster_sync();                       // every split's accumulator is final
-    if (threadIdx.x >= 64 && !*abort_flag) {
-      tc_fence_after();
-      const int q4 = warp % 4, grp = (warp - 2) / 4;
-      const int r = q4 * 32 + lane;
-      const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(q4 * 32) << 16);
-      const uint32_t me = cluster_ctarank();
-      const uint32_t recv = smem_u32(smem);
-      for (int c = grp; c < BN / 32; c += kEpiGroups) {
-        float v[32];
-        tmem_ld32(t_acc + c * 32, v);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int t = c * 32 + j;
-          const int owner = t / cs, slot = t - owner * cs;
-          const uint32_t off = recv + static_cast<uint32_t>(((me * cs + slot) * (kBM + 4) + r) * 4);
-          st_dsmem_f32(map_shared_rank(off, owner), v[j]);
-        }
-      }
-      tc_fence_before();
-    }
-    if (threadIdx.x == 64) trace_stamp(a, 24);
-    cluster_sync();                       // every pushed row has landed
+    cluster_sync();                       // all splits staged
     if (threadIdx.x == 0) trace_stamp(a, 25);
     if (!*abort_flag) cluster_reduce_store<BN>(a, reinterpret_cast<const float*>(smem), tile % a.tiles_m,
                                                tile / a.tiles_m);
     if (threadIdx.x == 0) trace_stamp(a, 26);
+    cluster_sync();                       // peers finished reading this CTA's tile
   }
   if (warp == 1) {
     tc_fence_after();
