@@ -53,6 +53,12 @@ struct AttnArgs {
   float scale_log2;  // softmax scale * log2(e)
   int* status;
   unsigned long long* trace;  // tcgen05 kernel timeline (tuning): kTraceSlots globaltimer stamps per CTA, or null
+  // Two-pass (shared-prefix) attention, TMA kernel only; every field may be null:
+  const int* k_lo;            // [B] first key of each sequence's range (a multiple of the page size)
+  float* o_f32;               // [T, Hq, D] fp32 normalised output instead of `out`
+  float* lse_out;             // [T, Hq] log2-domain log-sum-exp of the scaled scores of the range
+  const float* prior_o;       // [T, Hq, D] normalised output of an earlier key range, merged in
+  const float* prior_lse;     // [T, Hq] its log2-domain log-sum-exp
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
@@ -412,7 +418,8 @@ __global__ void __launch_bounds__(128 * MT, 2)
   load_q(a, st, q0, rows, row0 + mt * 16, g, qlen, kvlen, lane, bidir);
   const int last_row = min(rows - 1, row0 + 16 * MT - 1);
   const int max_key = bidir ? kvlen : min(kvlen, kvlen - qlen + last_row / a.G + 1);
-  const int nchunks = (max(max_key, 0) + kCh - 1) / kCh;
+  const int klo = a.k_lo != nullptr ? a.k_lo[b] : 0;      // keys [klo, max_key)
+  const int nchunks = (max(max_key - klo, 0) + kCh - 1) / kCh;
   const int mine = nchunks > kg ? (nchunks - kg + kKG - 1) / kKG : 0;
   const int* tbl = a.table + static_cast<long long>(b) * a.table_stride;
   uint8_t* gbase = base + kg * kGroupBytes;
@@ -420,7 +427,7 @@ __global__ void __launch_bounds__(128 * MT, 2)
   uint64_t* gempty = empty + kg * kTStages;
   const bool producer = mt == 0 && lane == 0;
   auto issue = [&](int i) {
-    const int key0 = (kg + kKG * i) * kCh;
+    const int key0 = klo + (kg + kKG * i) * kCh;
     const int y = (tbl[key0 / kPage] * a.Hkv + g) * kPage + key0 % kPage;
     const int s = i % kTStages;
     uint8_t* dst = gbase + s * kChunkBytes;
@@ -443,7 +450,7 @@ __global__ void __launch_bounds__(128 * MT, 2)
       break;
     }
     consumed = i + 1;
-    const int key0 = (kg + kKG * i) * kCh;
+    const int key0 = klo + (kg + kKG * i) * kCh;
     const uint32_t kb = smem_u32(gbase + s * kChunkBytes);
     const uint32_t vb = kb + 2 * kBoxBytes;
     if (kvlen - key0 < kCh) {
@@ -506,7 +513,11 @@ __global__ void __launch_bounds__(128 * MT, 2)
   const int tm = r / 16, rr = r % 16;
   const int row = row0 + r;
   if (row < rows) {
-    float M = -INFINITY;
+    const int tok = row / a.G, head = g * a.G + row % a.G;
+    const long long slot = static_cast<long long>(q0 + tok) * a.Hq + head;    // (token, head)
+    // an earlier key range enters as one more partial: (max = its lse, sum = 1, normalised output)
+    const float prior_m = a.prior_lse != nullptr ? a.prior_lse[slot] : -INFINITY;
+    float M = prior_m;
 #pragma unroll
     for (int k = 0; k < kKG; ++k) M = fmaxf(M, sm[(tm * kKG + k) * 16 + rr]);
     float wgt[kKG], L = 0.0f;
@@ -516,9 +527,11 @@ __global__ void __launch_bounds__(128 * MT, 2)
       wgt[k] = (M == -INFINITY || mk == -INFINITY) ? 0.0f : exp2f(mk - M);
       L += wgt[k] * sl[(tm * kKG + k) * 16 + rr];
     }
+    const float wprior = (M == -INFINITY || prior_m == -INFINITY) ? 0.0f : exp2f(prior_m - M);
+    L += wprior;
     const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    const int tok = row / a.G, head = g * a.G + row % a.G;
-    __nv_bfloat16* p = a.out + (static_cast<long long>(q0 + tok) * a.Hq + head) * kD;
+    if (a.lse_out != nullptr && (threadIdx.x % 8) == 0) a.lse_out[slot] = L > 0.0f ? M + log2f(L) : -INFINITY;
+    __nv_bfloat16* p = a.out + slot * kD;
 #pragma unroll
     for (int j = 0; j < kD / 32; ++j) {
       float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
@@ -530,10 +543,22 @@ __global__ void __launch_bounds__(128 * MT, 2)
         v.z += wgt[k] * x.z;
         v.w += wgt[k] * x.w;
       }
-      uint2 packed;
-      packed.x = pack_bf16(v.x * inv, v.y * inv);
-      packed.y = pack_bf16(v.z * inv, v.w * inv);
-      *reinterpret_cast<uint2*>(p + c4 + 32 * j) = packed;
+      if (wprior != 0.0f) {
+        const float4 x = *reinterpret_cast<const float4*>(a.prior_o + slot * kD + c4 + 32 * j);
+        v.x += wprior * x.x;
+        v.y += wprior * x.y;
+        v.z += wprior * x.z;
+        v.w += wprior * x.w;
+      }
+      if (a.o_f32 != nullptr) {
+        *reinterpret_cast<float4*>(a.o_f32 + slot * kD + c4 + 32 * j) =
+            make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+      } else {
+        uint2 packed;
+        packed.x = pack_bf16(v.x * inv, v.y * inv);
+        packed.y = pack_bf16(v.z * inv, v.w * inv);
+        *reinterpret_cast<uint2*>(p + c4 + 32 * j) = packed;
+      }
     }
   }
 }
@@ -1129,6 +1154,14 @@ cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream) {
   a.scale_log2 = p.scale * 1.4426950408889634f;
   a.status = p.status;
   a.trace = attention_trace_buffer();
+  a.k_lo = p.k_lo;
+  a.o_f32 = p.o_f32;
+  a.lse_out = p.lse_out;
+  a.prior_o = p.prior_o;
+  a.prior_lse = p.prior_lse;
+  const bool two_pass = p.k_lo || p.o_f32 || p.lse_out || p.prior_o || p.prior_lse;
+  if (two_pass && ((p.tile_rows != 16 && p.tile_rows != 32) || (p.prior_o == nullptr) != (p.prior_lse == nullptr)))
+    return cudaErrorInvalidValue;    // the key-range options are implemented by the TMA kernel
   if (p.num_tiles <= 0) return cudaSuccess;
   dim3 grid(p.num_tiles, p.Hkv);
   if (p.tile_rows == 128) {

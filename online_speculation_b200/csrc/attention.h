@@ -25,6 +25,14 @@ struct AttentionProblem {
   int cache_pages;               // pages in k_cache / v_cache
   float scale;
   int* status;
+  // Two-pass attention over a shared key prefix (tile_rows 16 / 32 only; each may be null):
+  // keys [k_lo[b], kv_len[b]) only; fp32 output and/or the log2-domain log-sum-exp of the
+  // range; and an earlier range's normalised output and log-sum-exp merged into the result.
+  const int* k_lo;
+  float* o_f32;
+  float* lse_out;
+  const float* prior_o;
+  const float* prior_lse;
 };
 
 cudaError_t attention_launch(const AttentionProblem& p, cudaStream_t stream);

@@ -218,7 +218,8 @@ void remask_select(Tensor tokens, int64_t a0, int64_t bl, int64_t mask_id, Tenso
 
 void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_start, Tensor q_len, Tensor kv_len,
                Tensor mode, Tensor tile_seq, Tensor tile_row0, int64_t tile_rows, int64_t kv_splits, Tensor out,
-               double scale, Tensor status) {
+               double scale, Tensor status, c10::optional<Tensor> k_lo, c10::optional<Tensor> o_f32,
+               c10::optional<Tensor> lse_out, c10::optional<Tensor> prior_o, c10::optional<Tensor> prior_lse) {
   CHECK_CUDA(q);
   CHECK_DT(q, torch::kBFloat16);
   CHECK_DT(k_cache, torch::kBFloat16);
@@ -255,6 +256,27 @@ void attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor table, Tensor q_
   p.cache_pages = k_cache.size(0);
   p.scale = static_cast<float>(scale);
   p.status = status.data_ptr<int>();
+  const long long rows = q.size(0) * q.size(1);
+  if (k_lo.has_value() && k_lo->defined()) {
+    CHECK_DT((*k_lo), torch::kInt32);
+    TORCH_CHECK(k_lo->is_cuda() && k_lo->is_contiguous() && k_lo->numel() >= q_start.numel(), "k_lo: one per sequence");
+    p.k_lo = k_lo->data_ptr<int>();
+  }
+  for (const c10::optional<Tensor>* o : {&o_f32, &prior_o})
+    if (o->has_value() && (*o)->defined()) {
+      CHECK_DT((**o), torch::kFloat32);
+      TORCH_CHECK((*o)->is_cuda() && (*o)->is_contiguous() && (*o)->numel() >= rows * q.size(2),
+                  "fp32 outputs / priors must hold [T, Hq, D]");
+    }
+  for (const c10::optional<Tensor>* o : {&lse_out, &prior_lse})
+    if (o->has_value() && (*o)->defined()) {
+      CHECK_DT((**o), torch::kFloat32);
+      TORCH_CHECK((*o)->is_cuda() && (*o)->is_contiguous() && (*o)->numel() >= rows, "log-sum-exp rows: [T, Hq]");
+    }
+  p.o_f32 = ptr_or_null<float>(o_f32);
+  p.lse_out = ptr_or_null<float>(lse_out);
+  p.prior_o = ptr_or_null<const float>(prior_o);
+  p.prior_lse = ptr_or_null<const float>(prior_lse);
   check(osb::attention_launch(p, at::cuda::getCurrentCUDAStream()), "paged attention");
 }
 

@@ -126,6 +126,11 @@ class _RoundGraph:
         splits = K.attention_kv_splits(ctas * tiles_per, mp * K.PAGE_SIZE) if tr == K.TC_TILE_ROWS else 1
         self.plan_draft = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(1), tile_seq, tile_row0, tr, {}, splits)
         self.plan_verify = K.AttentionPlan(table, starts, mk(Kb), kv_len, mk(0), tile_seq, tile_row0, tr, {}, splits)
+        keys = engine.shared_prefix_keys
+        if keys and tr in (16, 32):
+            # the prompt pages are the same pages for every job: one pass over them for all jobs
+            for plan in (self.plan_draft, self.plan_verify):
+                plan.shared = K.shared_prefix(table, B * Kb, keys, B, G, engine.runner.q_slots, dev)
         mask_id = engine.head.mask_token_id if engine.head is not None else 0
         self.ids_draft = torch.full((B, Kb), mask_id, dtype=torch.int32, device=dev)
         self.ids_verify = torch.zeros(B, Kb, dtype=torch.int32, device=dev)
@@ -267,6 +272,11 @@ class _PlainGraph:
         splits = K.attention_kv_splits(B * tiles * r.kv_slots, mp * K.PAGE_SIZE) if tr == K.TC_TILE_ROWS else 1
         self.plans = [K.AttentionPlan(table, q_start, q_len, self.views["kv_len"][s], mode, tile_seq, tile_row, tr,
                                       {}, splits) for s in range(S)]
+        keys = engine.shared_prefix_keys
+        if keys and tr in (16, 32):
+            shared = K.shared_prefix(table, B, keys, B, G, r.q_slots, dev)
+            for plan in self.plans:
+                plan.shared = shared
         # packed result [B, 2 + 3 S] for one D2H copy: (S - 1, valid, tokens, log q, log p)
         self.result = torch.zeros(B, 2 + 3 * S, dtype=torch.float32, device=dev)
         self.result[:, 0] = S - 1
@@ -335,7 +345,7 @@ class MHEngine:
     def __init__(self, runner: ModelRunner, head: DraftHead | None, *, alpha: float = 4.0, length: int = 512,
                  root_seed: int = 0, learner: SuffixLearner | None = None, use_graphs: bool = True,
                  max_pages_per_seq: int | None = None, spec_policy: str = "adaptive", probe_every: int = 8,
-                 plain_steps: int = 4):
+                 plain_steps: int = 4, share_prefix: bool = True):
         self.runner = runner
         self.head = head
         self.cache: KVCache = runner.cache
@@ -357,6 +367,8 @@ class MHEngine:
         self.probe_every = probe_every
         if plain_steps < 1:
             raise ValueError("plain_steps must be positive")
+        self.share_prefix = share_prefix          # two-pass attention over the common prompt pages
+        self.shared_prefix_keys = 0
         self.plain_steps = plain_steps    # chained decode steps per plain round
         # per-round wall time (EMA) of speculative and plain rounds and the mean emitted tokens per
         # speculative block; the adaptive policy compares expected tokens per second of the two
@@ -372,6 +384,15 @@ class MHEngine:
         P = len(prompts[0])
         if any(len(p) != P for p in prompts):
             raise ValueError("prompts of one engine share a length")
+        if self._graphs:
+            raise RuntimeError("add every chain before the first round")
+        # Chains with one prompt fork one prefilled sequence, so the full pages of prompt[:-1]
+        # are the same cache pages for every job: attention reads them in one shared pass.
+        # Shorter shared runs are not worth the extra pass.
+        first = tuple(prompts[0]) if not self.chains else tuple(self.chains[0].prompt)
+        same = all(tuple(p) == first for p in prompts)
+        keys = (P - 1) // K.PAGE_SIZE * K.PAGE_SIZE
+        self.shared_prefix_keys = keys if same and keys >= 4 * K.PAGE_SIZE and self.share_prefix else 0
         start = len(self.chains)
         for p in prompts:
             self.chains.append(Chain(list(p)))

@@ -209,6 +209,45 @@ class AttentionPlan:
     # host copies for the CPU oracle
     host: dict
     kv_splits: int = 1
+    # two-pass attention over a key prefix that every sequence shares (None: one pass)
+    shared: "SharedPrefix | None" = None
+
+
+@dataclass
+class SharedPrefix:
+    """The shared-prefix pass of two-pass attention and the buffers it hands to the second pass.
+
+    Every sequence of the batch sees the same first ``keys`` keys (the same cache pages).  The
+    first pass treats the query rows of all sequences as one bidirectional block against those
+    keys, so each prefix page is read once per KV head instead of once per sequence, and writes
+    the normalised fp32 output and the log2-domain log-sum-exp per (token, head); the second pass
+    runs each sequence over keys [keys, kv_len) and merges the first pass into its result.
+    """
+
+    plan: AttentionPlan       # one bidirectional sequence: all query tokens x the shared keys
+    k_lo: torch.Tensor        # [B] int32, the first key of the per-sequence pass (= keys)
+    o: torch.Tensor           # [T, Hq, D] fp32
+    lse: torch.Tensor         # [T, Hq] fp32
+    keys: int
+
+
+def shared_prefix(table: torch.Tensor, tokens: int, keys: int, sequences: int, group: int, q_heads: int,
+                  device, tile_rows: int = 32) -> SharedPrefix:
+    """Plan the shared-prefix pass for ``tokens`` query tokens (row 0 of ``table`` holds the shared pages).
+
+    ``keys`` must be a multiple of the page size; ``group`` is query heads per KV head.
+    """
+    if keys % PAGE_SIZE:
+        raise ValueError("the shared prefix must be whole pages")
+    rows = tokens * group
+    tiles = -(-rows // tile_rows)
+    one = lambda v: torch.tensor([v], dtype=torch.int32, device=device)
+    plan = AttentionPlan(table[:1], one(0), one(tokens), one(keys), one(1),
+                         torch.zeros(tiles, dtype=torch.int32, device=device),
+                         torch.arange(0, tiles * tile_rows, tile_rows, dtype=torch.int32, device=device), tile_rows, {})
+    return SharedPrefix(plan, torch.full((sequences,), keys, dtype=torch.int32, device=device),
+                        torch.empty(tokens, q_heads, 128, dtype=torch.float32, device=device),
+                        torch.empty(tokens, q_heads, dtype=torch.float32, device=device), keys)
 
 
 TC_TILE_ROWS = 128          # query rows per CTA of the tcgen05 attention kernel
@@ -284,9 +323,20 @@ def attention(q, k_cache, v_cache, plan: AttentionPlan, *, out=None, scale=None)
         out = torch.empty_like(q)
     scale = scale if scale is not None else q.shape[-1] ** -0.5
     if q.is_cuda:
-        _ext.require().attention(q, k_cache, v_cache, plan.table, plan.q_start, plan.q_len, plan.kv_len, plan.mode,
-                                 plan.tile_seq, plan.tile_row0, plan.tile_rows, plan.kv_splits, out, float(scale),
-                                 workspace.status(q.device))
+        ext = _ext.require()
+        st = workspace.status(q.device)
+        pre = plan.shared
+        if pre is None:
+            ext.attention(q, k_cache, v_cache, plan.table, plan.q_start, plan.q_len, plan.kv_len, plan.mode,
+                          plan.tile_seq, plan.tile_row0, plan.tile_rows, plan.kv_splits, out, float(scale), st,
+                          None, None, None, None, None)
+            return out
+        p = pre.plan
+        ext.attention(q, k_cache, v_cache, p.table, p.q_start, p.q_len, p.kv_len, p.mode, p.tile_seq, p.tile_row0,
+                      p.tile_rows, 1, out, float(scale), st, None, pre.o, pre.lse, None, None)
+        ext.attention(q, k_cache, v_cache, plan.table, plan.q_start, plan.q_len, plan.kv_len, plan.mode,
+                      plan.tile_seq, plan.tile_row0, plan.tile_rows, plan.kv_splits, out, float(scale), st,
+                      pre.k_lo, None, None, pre.o, pre.lse)
         return out
     out.copy_(attention_reference(q, k_cache, v_cache, plan.host, scale))
     return out

@@ -117,6 +117,29 @@ def test_mh_engine_logprobs_are_exact(graphs, policy):
     workspace.check_status()
 
 
+@pytest.mark.parametrize("policy", ["always", "never"])
+def test_mh_engine_shared_prompt_two_pass_attention_is_exact(policy):
+    """A 160-token prompt shared by every chain: attention reads its 128 full-page keys in one shared
+    pass; the emitted tokens' log p / log q still equal the oracle's."""
+    cfg = SMALL
+    eng = build_mh_engine(cfg, seed=3, alpha=2.0, length=20, block_size=4, learner_stride=None, use_graphs=True,
+                          kv_bytes=64 << 20, max_seq_tokens=200, max_batch=8, spec_policy=policy)
+    prompt = [(7 * i) % 900 + 5 for i in range(160)]
+    eng.add_chains([prompt] * 5)
+    assert eng.shared_prefix_keys == 128
+    eng.run_until_idle()
+    eng.set_quota(2)
+    eng.run_until_idle()
+    sd = {k: v.cpu() for k, v in random_state_dict(cfg, seed=3, std=0.02, device="cuda").items()}
+    for ch in eng.chains:
+        full = torch.tensor(ch.prompt + ch.tokens)
+        logits = reference_forward(cfg, sd, full)[len(prompt) - 1:-1]
+        lp = logits.log_softmax(-1).gather(-1, torch.tensor(ch.tokens)[:, None]).squeeze(-1)
+        assert torch.allclose(torch.tensor(ch.logp), lp, atol=0.05)
+    eng.close()
+    workspace.check_status()
+
+
 def test_mh_engine_without_draft_is_exact():
     """Plain decoding (no draft head) emits one token per round with exact log p / log q."""
     cfg = SMALL

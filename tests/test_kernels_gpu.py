@@ -163,6 +163,36 @@ def test_attention_ignores_non_finite_rows_past_the_end(cuda, tile_rows, kv_spli
     assert _rel(out.cpu(), ref) < 2e-2
 
 
+@pytest.mark.parametrize("q_len,mode,tile_rows", [(1, 0, 16), (4, 0, 16), (4, 1, 16), (4, 0, 32), (1, 0, 32)])
+def test_two_pass_shared_prefix_attention_matches_one_pass(cuda, q_len, mode, tile_rows):
+    """Sequences whose first pages are the same cache pages: the shared-prefix pass plus the
+    per-sequence pass equal one pass over all keys (and the fp32 oracle)."""
+    torch.manual_seed(q_len + mode + tile_rows)
+    B, Hq, Hkv, shared_keys = 9, 28, 4, 192
+    kv_lens = [shared_keys + q_len + 7 * b for b in range(B)]        # every sequence has own keys too
+    own_pages = [(kv - shared_keys + 31) // 32 for kv in kv_lens]
+    sp = shared_keys // 32
+    kc = torch.randn(sp + sum(own_pages), Hkv, 32, 128, device=cuda).bfloat16()
+    vc = torch.randn_like(kc)
+    width = sp + max(own_pages)
+    table = torch.zeros(B, width, dtype=torch.int32)
+    nxt = sp
+    for b in range(B):
+        table[b, :sp] = torch.arange(sp)
+        table[b, sp:sp + own_pages[b]] = torch.arange(nxt, nxt + own_pages[b])
+        nxt += own_pages[b]
+    q = torch.randn(B * q_len, Hq, 128, device=cuda).bfloat16()
+    plan = ops.plan_attention(table, [q_len] * B, kv_lens, [mode] * B, Hq // Hkv, cuda, tile_rows=tile_rows)
+    one = ops.attention(q, kc, vc, plan)
+    plan.shared = ops.shared_prefix(plan.table, B * q_len, shared_keys, B, Hq // Hkv, Hq, cuda)
+    two = ops.attention(q, kc, vc, plan)
+    ref = ops.attention_reference(q.cpu(), kc.cpu(), vc.cpu(), plan.host, 128 ** -0.5)
+    torch.cuda.synchronize()
+    workspace.check_status(cuda)
+    assert torch.isfinite(two).all()
+    assert _rel(two.cpu(), ref) < 2e-2 and _rel(two, one) < 1e-2
+
+
 def test_rmsnorm_and_fused_add(cuda):
     x = torch.randn(37, 3584, device=cuda).bfloat16()
     w = (1 + 0.1 * torch.randn(3584, device=cuda)).bfloat16()
