@@ -45,7 +45,7 @@ def build_mh_engine(model: str | DecoderConfig = "qwen2.5-7b", *, tp_group=None,
                     learner_loss: str = "tv", learning_rate: float = 1e-5, use_graphs: bool = True,
                     kv_bytes: int = 24 << 30, max_seq_tokens: int = 1040, max_batch: int = 64,
                     fused_collectives: bool = True, draft: bool = True, spec_policy: str = "adaptive",
-                    probe_every: int = 8, plain_steps: int = 4) -> MHEngine:
+                    probe_every: int = 8, plain_steps: int = 4, share_prefix: bool = False) -> MHEngine:
     """Suffix-MH engine.
 
     ``draft=False`` decodes one token per round without a draft head (the baseline
@@ -53,14 +53,16 @@ def build_mh_engine(model: str | DecoderConfig = "qwen2.5-7b", *, tp_group=None,
     in the rounds where the measured acceptance makes speculation faster than plain
     decoding, with a speculative round at least every ``probe_every`` rounds so the
     online learner keeps training; ``always`` drafts every round; ``never`` never.
-    A plain round chains ``plain_steps`` decode steps in one graph replay.
+    A plain round chains ``plain_steps`` decode steps in one graph replay.  ``share_prefix``:
+    two-pass attention over the prompt pages every chain shares (measured slower on the 7B
+    headline workload, so off by default).
     """
     runner = build_runner(model, tp_group=tp_group, seed=seed, kv_bytes=kv_bytes,
                           max_logit_rows=max(512, max_batch * block_size), fused_collectives=fused_collectives)
     if not draft:
         return MHEngine(runner, None, alpha=alpha, length=length, root_seed=seed, learner=None,
                         use_graphs=use_graphs, max_pages_per_seq=-(-(max_seq_tokens + plain_steps) // 32) + 1,
-                        plain_steps=plain_steps)
+                        plain_steps=plain_steps, share_prefix=share_prefix)
     draft_weights = init_draft(runner.w, seed=seed + 1)
     head = DraftHead(runner, draft_weights, block_size=block_size)
     learner = None
@@ -70,4 +72,4 @@ def build_mh_engine(model: str | DecoderConfig = "qwen2.5-7b", *, tp_group=None,
     max_pages = -(-(max_seq_tokens + plain_steps) // 32) + 1
     return MHEngine(runner, head, alpha=alpha, length=length, root_seed=seed, learner=learner,
                     use_graphs=use_graphs, max_pages_per_seq=max_pages, spec_policy=spec_policy,
-                    probe_every=probe_every, plain_steps=plain_steps)
+                    probe_every=probe_every, plain_steps=plain_steps, share_prefix=share_prefix)

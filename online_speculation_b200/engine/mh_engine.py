@@ -345,7 +345,7 @@ class MHEngine:
     def __init__(self, runner: ModelRunner, head: DraftHead | None, *, alpha: float = 4.0, length: int = 512,
                  root_seed: int = 0, learner: SuffixLearner | None = None, use_graphs: bool = True,
                  max_pages_per_seq: int | None = None, spec_policy: str = "adaptive", probe_every: int = 8,
-                 plain_steps: int = 4, share_prefix: bool = True):
+                 plain_steps: int = 4, share_prefix: bool = False):
         self.runner = runner
         self.head = head
         self.cache: KVCache = runner.cache
