@@ -3,7 +3,7 @@
 //
 //   h <- h + sum_r P_r ;  x <- rmsnorm(h) * w
 //
-// Up to four ranks: one-shot.  After a cross-rank barrier every rank loads the
+// Up to four ranks (and above that for small batches): one-shot.  After a cross-rank barrier every rank loads the
 // rows of every rank's partial (peer loads), sums them in rank order (so the
 // residual stream stays bitwise identical on all ranks), adds the residual,
 // and applies RMSNorm in the same pass: one kernel, one barrier, and each rank
@@ -109,6 +109,7 @@ __device__ __forceinline__ void finish_call(const ArArgs& a, uint32_t epoch) {
 }
 
 constexpr int kOneShotThreads = 256;
+constexpr long long kOneShotPeerBytes = 4ll << 20;   // "auto" above four ranks: one-shot up to this peer read
 constexpr int kOneShotRegVecs = 4;   // rows up to 256 * 4 * 8 = 8192 wide stay in registers
 
 // kPushed: the partials were stored into this rank's memory by the ranks' GEMMs
@@ -342,7 +343,12 @@ __global__ void __launch_bounds__(kOneShotThreads) twoshot_norm_kernel(const ArA
 cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
   if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
   if (a.algorithm < 0 || a.algorithm > 2) return cudaErrorInvalidValue;
-  const bool oneshot = a.algorithm == 1 || (a.algorithm == 0 && a.world <= 4);
+  // "auto": one-shot up to four ranks, and above that while each rank's peer reads stay small.
+  // Measured on two B200s with graph-replayed calls (T = 64 / 256 rows of 3584): one-shot 12.0 /
+  // 13.6 us, two-shot 24.6 / 26.4 us -- a call is bound by its barriers, not its bytes, so the
+  // second barrier of two-shot costs more than reading 7 partials of a decode batch would.
+  const long long peer_bytes = static_cast<long long>(a.world - 1) * a.T * a.H * 2;
+  const bool oneshot = a.algorithm == 1 || (a.algorithm == 0 && (a.world <= 4 || peer_bytes <= kOneShotPeerBytes));
   if (oneshot) {
     // one row per block (the blocks of a row wait on remote loads; more rows in flight hide that latency)
     const int cap = 4 * blocks;
