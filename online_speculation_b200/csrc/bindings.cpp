@@ -979,6 +979,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       osb::gemm_trace_buffer() = nullptr;
     }
   });
+  m.def("allreduce_set_trace", [](c10::optional<Tensor> buf) {
+    if (buf.has_value() && buf->defined()) {
+      CHECK_CUDA(*buf);
+      TORCH_CHECK(buf->scalar_type() == torch::kInt64 && buf->is_contiguous() && buf->numel() >= 8,
+                  "trace buffer must be a contiguous int64 tensor of at least 8 values");
+      osb::allreduce_trace_buffer() = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    } else {
+      osb::allreduce_trace_buffer() = nullptr;
+    }
+  });
   m.def("pdl_enabled", []() -> bool { return osb::pdl_enabled(); });
 
   pybind11::class_<osb::KVManager>(m, "KVManager")

@@ -48,6 +48,7 @@ __device__ __forceinline__ bool rank_barrier(const ArArgs& a, int slot, uint32_t
   if (blockIdx.x == 0 && threadIdx.x < a.world) {
     __threadfence_system();
     st_release_sys(a.pads[threadIdx.x] + slot * kMaxRanks + a.rank, epoch);
+    if (threadIdx.x == 0 && a.trace != nullptr) a.trace[2] = global_ns();
   }
   __shared__ int ok;
   if (threadIdx.x == 0) {
@@ -115,14 +116,21 @@ constexpr int kOneShotRegVecs = 4;   // rows up to 256 * 4 * 8 = 8192 wide stay 
 // kPushed: the partials were stored into this rank's memory by the ranks' GEMMs
 // (parts[q] are local slots) and each GEMM released the call's epoch into flag
 // slot kPushSlot; the kernel waits for those flags and reads only local memory.
+__device__ __forceinline__ void ar_stamp(const ArArgs& a, int slot) {
+  if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.trace[slot] = global_ns();
+}
+
 template <bool kPushed>
 __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArArgs a) {
+  ar_stamp(a, 0);
   // The partials (and the previous call's epoch) belong to the predecessor; every block is
   // resident once it gets here, so the successor may launch (its own wait covers this grid).
   pdl_wait();
   pdl_trigger();
+  ar_stamp(a, 1);
   const uint32_t epoch = *a.epoch + 1;
   const bool ok = kPushed ? wait_flags(a, kPushSlot, epoch) : rank_barrier(a, 2, epoch);
+  ar_stamp(a, 3);
   const int nvec = a.H / 8;
   __shared__ float red[33];
   if (ok) {
@@ -188,6 +196,7 @@ __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArA
 #pragma unroll
         for (int e = 0; e < 8; ++e) ss += bf2f(oe[e]) * bf2f(oe[e]);
       }
+      if (row == static_cast<int>(blockIdx.x)) ar_stamp(a, 4);
       ss = warp_sum(ss);
       const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
       if (lane == 0) red[warp] = ss;
@@ -198,6 +207,7 @@ __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArA
         if (lane == 0) red[32] = rsqrtf(t / a.H + a.eps);
       }
       __syncthreads();
+      if (row == static_cast<int>(blockIdx.x)) ar_stamp(a, 5);
       const float rs = red[32];
       auto emit = [&](int v, const uint4& hv) {
         const uint4 wv = *reinterpret_cast<const uint4*>(a.w + v * 8);
@@ -217,9 +227,11 @@ __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArA
       for (int v = threadIdx.x + kOneShotRegVecs * kOneShotThreads; v < nvec; v += kOneShotThreads)
         emit(v, *reinterpret_cast<const uint4*>(hr + v * 8));
       __syncthreads();
+      if (row == static_cast<int>(blockIdx.x)) ar_stamp(a, 6);
     }
   }
   finish_call(a, epoch);
+  ar_stamp(a, 7);
 }
 
 // Two-shot in one kernel (more than four ranks): phase A reduces this rank's row
@@ -340,7 +352,14 @@ __global__ void __launch_bounds__(kOneShotThreads) twoshot_norm_kernel(const ArA
 
 }  // namespace
 
-cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
+unsigned long long*& allreduce_trace_buffer() {
+  static unsigned long long* buf = nullptr;
+  return buf;
+}
+
+cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a0, int blocks, cudaStream_t stream) {
+  ArArgs a = a0;
+  a.trace = allreduce_trace_buffer();
   if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
   if (a.algorithm < 0 || a.algorithm > 2) return cudaErrorInvalidValue;
   // "auto": one-shot up to four ranks, and above that while each rank's peer reads stay small.
@@ -371,7 +390,9 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream
   return launch_pdl(twoshot_norm_kernel, dim3(grid > 0 ? grid : 1), dim3(kOneShotThreads), 0, stream, a);
 }
 
-cudaError_t allreduce_pushed_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream) {
+cudaError_t allreduce_pushed_add_rmsnorm_launch(const ArArgs& a0, int blocks, cudaStream_t stream) {
+  ArArgs a = a0;
+  a.trace = allreduce_trace_buffer();
   if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
   const int cap = 4 * blocks;
   const int grid = a.T < cap ? a.T : cap;

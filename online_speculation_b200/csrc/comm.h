@@ -26,7 +26,14 @@ struct ArArgs {
   int* status;
   int algorithm;                          // 0: one-shot up to four ranks, two-shot above; 1: one-shot; 2: two-shot
   unsigned long long wait_ns;             // limit of every cross-rank wait (0: two seconds)
+  unsigned long long* trace;              // one-shot timeline of block 0 (tuning) or null
 };
+
+// Timeline capture for tuning the one-shot reduction: when non-null, block 0 of every
+// later one-shot call writes 8 globaltimer stamps (entry, predecessor done, barrier
+// published, barrier passed, partial rows loaded, norm reduced, output stored, call
+// retired) over the previous call's, into this device buffer of at least 8 values.
+unsigned long long*& allreduce_trace_buffer();
 
 cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a, int blocks, cudaStream_t stream);
 

@@ -156,6 +156,10 @@ def _allreduce_probe(a) -> int:
         part = comm.partial_buffer(a.T) if hasattr(comm, "partial_buffer") else scratch
         comm.reduce_add_norm(part, h, w, x, 1e-6)
 
+    trace = None
+    if a.trace:
+        trace = torch.zeros(8, dtype=torch.int64, device=dev)
+        K._ext.require().allreduce_set_trace(trace)
     for _ in range(a.warmup):
         call()
     torch.cuda.synchronize()
@@ -186,11 +190,21 @@ def _allreduce_probe(a) -> int:
     us = torch.tensor([t0.elapsed_time(t1) * 1e3 / iters], device=dev)
     dist.all_reduce(us, op=dist.ReduceOp.MAX)
     K.workspace.check_status(dev)
+    stamps = None
+    if trace is not None:
+        K._ext.require().allreduce_set_trace(None)
+        rel = (trace - trace[0]).float() / 1e3
+        gathered = [torch.empty_like(rel) for _ in range(world)]
+        dist.all_gather(gathered, rel)
+        names = ("entry", "predecessor_done", "barrier_published", "barrier_passed", "rows_loaded", "norm_reduced",
+                 "output_stored", "retired")
+        stamps = [{n: round(float(v), 2) for n, v in zip(names, g.tolist())} for g in gathered]
     if rank == 0:
         peer_bytes = (world - 1) * a.T * a.hidden * 2
         print(_json.dumps({"kind": "allreduce", "world": world, "T": a.T, "hidden": a.hidden, "algorithm": a.algorithm,
                            "graph": run is not None,
                            "us_per_call_max_over_ranks": float(us), "peer_bytes_read_per_rank": peer_bytes,
+                           "block0_timeline_us": stamps,
                            "peer_gbs": peer_bytes / float(us) / 1e3}))
     dist.barrier()
     del comm
@@ -245,6 +259,8 @@ def main(argv=None) -> int:
     ar.add_argument("T", type=int, help="token rows")
     ar.add_argument("--hidden", type=int, default=3584)
     ar.add_argument("--algorithm", choices=("auto", "oneshot", "twoshot", "nccl"), default="auto")
+    ar.add_argument("--trace", action="store_true",
+                    help="one-shot: print block 0's stamps of the last call on every rank (microseconds from entry)")
     for q in (g, gr, mo, at, sa, ar):
         q.add_argument("--iters", type=int, default=20)
         q.add_argument("--warmup", type=int, default=3)
