@@ -44,9 +44,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Cross-rank barrier at the start of a kernel (slot distinguishes kernels).
+// The data a peer reads after this barrier was written by the predecessor kernel, which
+// has completed (and its writes are visible) once griddepcontrol.wait returns, so the
+// signal needs no fence of its own beyond its release.
 __device__ __forceinline__ bool rank_barrier(const ArArgs& a, int slot, uint32_t epoch) {
   if (blockIdx.x == 0 && threadIdx.x < a.world) {
-    __threadfence_system();
     st_release_sys(a.pads[threadIdx.x] + slot * kMaxRanks + a.rank, epoch);
     if (threadIdx.x == 0 && a.trace != nullptr) a.trace[2] = global_ns();
   }
@@ -109,9 +111,9 @@ __device__ __forceinline__ void finish_call(const ArArgs& a, uint32_t epoch) {
   }
 }
 
-constexpr int kOneShotThreads = 256;
+constexpr int kOneShotThreads = 512;    // one 16-byte vector of a 3584-wide row per thread: one round of peer loads
 constexpr long long kOneShotPeerBytes = 4ll << 20;   // "auto" above four ranks: one-shot up to this peer read
-constexpr int kOneShotRegVecs = 4;   // rows up to 256 * 4 * 8 = 8192 wide stay in registers
+constexpr int kOneShotRegVecs = 4;   // rows up to 512 * 4 * 8 = 16384 wide stay in registers
 
 // kPushed: the partials were stored into this rank's memory by the ranks' GEMMs
 // (parts[q] are local slots) and each GEMM released the call's epoch into flag
