@@ -111,9 +111,9 @@ __device__ __forceinline__ void finish_call(const ArArgs& a, uint32_t epoch) {
   }
 }
 
-constexpr int kOneShotThreads = 512;    // one 16-byte vector of a 3584-wide row per thread: one round of peer loads
+constexpr int kOneShotThreads = 256;
 constexpr long long kOneShotPeerBytes = 4ll << 20;   // "auto" above four ranks: one-shot up to this peer read
-constexpr int kOneShotRegVecs = 4;   // rows up to 512 * 4 * 8 = 16384 wide stay in registers
+constexpr int kOneShotRegVecs = 4;   // rows up to 256 * 4 * 8 = 8192 wide stay in registers (even count)
 
 // kPushed: the partials were stored into this rank's memory by the ranks' GEMMs
 // (parts[q] are local slots) and each GEMM released the call's epoch into flag
@@ -122,7 +122,7 @@ __device__ __forceinline__ void ar_stamp(const ArArgs& a, int slot) {
   if (a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) a.trace[slot] = global_ns();
 }
 
-template <bool kPushed>
+template <bool kPushed, int kRanks>
 __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArArgs a) {
   ar_stamp(a, 0);
   // The partials (and the previous call's epoch) belong to the predecessor; every block is
@@ -140,24 +140,36 @@ __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArA
       __nv_bfloat16* hr = a.h + static_cast<long long>(row) * a.ldh;
       uint4 keep[kOneShotRegVecs];
       float ss = 0.0f;
+      // Two vectors at a time: both vectors' peer loads are issued before either is summed
+      // (the stores to h could alias them for the compiler), so a row costs one round trip
+      // to the peers per pair instead of one per vector.
 #pragma unroll
-      for (int i = 0; i < kOneShotRegVecs; ++i) {
-        const int v = threadIdx.x + i * kOneShotThreads;
-        if (v < nvec) {
-          uint4 parts[kMaxRanks];
+      for (int i0 = 0; i0 < kOneShotRegVecs; i0 += 2) {
+        uint4 parts[2][kRanks], hv[2];
 #pragma unroll
-          for (int q = 0; q < kMaxRanks; ++q)
-            if (q < a.world)
-              parts[q] = __ldcg(reinterpret_cast<const uint4*>(a.parts[q] + static_cast<long long>(row) * a.H + v * 8));
-          const uint4 hv = *reinterpret_cast<const uint4*>(hr + v * 8);
-          const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv);
+        for (int j = 0; j < 2; ++j) {
+          const int v = threadIdx.x + (i0 + j) * kOneShotThreads;
+          if (v < nvec) {
+#pragma unroll
+            for (int q = 0; q < kRanks; ++q)
+              if (q < a.world)
+                parts[j][q] =
+                    __ldcg(reinterpret_cast<const uint4*>(a.parts[q] + static_cast<long long>(row) * a.H + v * 8));
+            hv[j] = *reinterpret_cast<const uint4*>(hr + v * 8);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int v = threadIdx.x + (i0 + j) * kOneShotThreads;
+          if (v >= nvec) continue;
+          const __nv_bfloat16* he = reinterpret_cast<const __nv_bfloat16*>(&hv[j]);
           float acc[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) acc[e] = bf2f(he[e]);
 #pragma unroll
-          for (int q = 0; q < kMaxRanks; ++q) {
+          for (int q = 0; q < kRanks; ++q) {
             if (q < a.world) {
-              const __nv_bfloat16* pe = reinterpret_cast<const __nv_bfloat16*>(&parts[q]);
+              const __nv_bfloat16* pe = reinterpret_cast<const __nv_bfloat16*>(&parts[j][q]);
 #pragma unroll
               for (int e = 0; e < 8; ++e) acc[e] += bf2f(pe[e]);
             }
@@ -167,7 +179,7 @@ __global__ void __launch_bounds__(kOneShotThreads) oneshot_norm_kernel(const ArA
 #pragma unroll
           for (int e = 0; e < 4; ++e) ob[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
           *reinterpret_cast<uint4*>(hr + v * 8) = out;
-          keep[i] = out;
+          keep[i0 + j] = out;
           const __nv_bfloat16* oe = reinterpret_cast<const __nv_bfloat16*>(&out);
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -374,7 +386,10 @@ cudaError_t allreduce_add_rmsnorm_launch(const ArArgs& a0, int blocks, cudaStrea
     // one row per block (the blocks of a row wait on remote loads; more rows in flight hide that latency)
     const int cap = 4 * blocks;
     const int grid = a.T < cap ? a.T : cap;
-    return launch_pdl(oneshot_norm_kernel<false>, dim3(grid > 0 ? grid : 1), dim3(kOneShotThreads), 0, stream, a);
+    const dim3 g(grid > 0 ? grid : 1), blk(kOneShotThreads);
+    if (a.world <= 2) return launch_pdl(oneshot_norm_kernel<false, 2>, g, blk, 0, stream, a);
+    if (a.world <= 4) return launch_pdl(oneshot_norm_kernel<false, 4>, g, blk, 0, stream, a);
+    return launch_pdl(oneshot_norm_kernel<false, kMaxRanks>, g, blk, 0, stream, a);
   }
   // every block of the two-shot kernel waits for the others between its phases: keep the grid co-resident
   static int resident = 0;
@@ -398,7 +413,10 @@ cudaError_t allreduce_pushed_add_rmsnorm_launch(const ArArgs& a0, int blocks, cu
   if (a.world < 1 || a.world > kMaxRanks || a.H % 8 || a.T <= 0) return cudaErrorInvalidValue;
   const int cap = 4 * blocks;
   const int grid = a.T < cap ? a.T : cap;
-  return launch_pdl(oneshot_norm_kernel<true>, dim3(grid > 0 ? grid : 1), dim3(kOneShotThreads), 0, stream, a);
+  const dim3 g(grid > 0 ? grid : 1), blk(kOneShotThreads);
+  if (a.world <= 2) return launch_pdl(oneshot_norm_kernel<true, 2>, g, blk, 0, stream, a);
+  if (a.world <= 4) return launch_pdl(oneshot_norm_kernel<true, 4>, g, blk, 0, stream, a);
+  return launch_pdl(oneshot_norm_kernel<true, kMaxRanks>, g, blk, 0, stream, a);
 }
 
 }  // namespace osb
