@@ -91,6 +91,9 @@ def parse():
     p.add_argument("--is-block", type=int, default=32)
     p.add_argument("--is-rollouts", type=int, default=8)
     p.add_argument("--is-rollout-len", type=int, default=256)
+    p.add_argument("--is-workers", type=int, default=16,
+                   help="prompt threads of the repo arm (more threads than needed to fill 256-wide "
+                        "batches only add interpreter contention)")
     return p.parse_args()
 
 
@@ -588,6 +591,8 @@ def _is_result(args, world, impl, ms, wall, tokens, prompts_per_step, clocks, ex
                    "rollouts_per_candidate": args.is_rollouts, "rollout_len": args.is_rollout_len,
                    "reward": "sequence log-probability, c=0.5, tau=0.5", "temperature": 1.0,
                    "step": "one conditional-IS decision block (first block) of every prompt",
+                   "prompt_threads_per_rank": (min(args.is_workers, prompts_per_step // world) if impl is None
+                                               else prompts_per_step // world),
                    "l2": "weights (3 GB) and KV streamed every decode step exceed the 126 MB L2"},
         "clocks": clocks,
     }
@@ -633,7 +638,7 @@ def run_is(args, rank, world, local, group) -> dict:
                                  step_index=0, reward_batch=reward.batch)
         return st.selected.token_ids
 
-    pool = ThreadPoolExecutor(max_workers=len(prompts))
+    pool = ThreadPoolExecutor(max_workers=max(1, min(args.is_workers, len(prompts))))
 
     def step(k):
         return list(pool.map(lambda i: one(k, i), range(len(prompts))))
