@@ -17,6 +17,11 @@ with the engine of this package behind every role)::
 
     [model_loading]                          # shared.model_loading options (per-role tables allowed)
 
+    [acceleration.speculation]               # optional rollout-reuse speculation in the engine backend
+    enabled = true
+    tiers = [[4, 8], [16, 4], [512, 0]]      # [maximum active batch, draft tokens]
+    stochastic_tree = false                  # plus min_context_tokens, min_token_probability, tree_max_*
+
 Checkpoints are read from safetensors in the HF Qwen2 / Qwen3 layout
 (``config.json`` + ``model*.safetensors``); the tokenizer is loaded with
 ``transformers.AutoTokenizer`` when present (for ``encode`` / ``decode``).
@@ -43,6 +48,36 @@ def _table(value: Any, name: str) -> dict[str, Any]:
     if not isinstance(value, Mapping):
         raise TypeError(f"{name} must be a table")
     return dict(value)
+
+
+_SPECULATION_KEYS = ("min_context_tokens", "min_token_probability", "tree_max_context_tokens", "tree_max_contexts",
+                     "vllm_max_cached_requests", "stochastic_tree")
+
+
+def speculation_from_config(config: Mapping[str, Any]):
+    """``[acceleration.speculation]`` as an ``ActiveBatchSpeculationConfig`` (None when absent or disabled).
+
+    Keys of src/inference_scaling/arllm/backends/loader.py:81-116; ``dynamic_vllm`` is accepted
+    and has no effect here (the engine has no separate vLLM speculation mode).
+    """
+    from ..acceleration import ActiveBatchSpeculationConfig, SpeculationTier
+
+    table = _table(_table(config.get("acceleration"), "acceleration").get("speculation"), "acceleration.speculation")
+    if not table or not bool(table.pop("enabled", False)):
+        return None
+    table.pop("dynamic_vllm", None)
+    tiers = table.pop("tiers", None)
+    unknown = sorted(set(table) - set(_SPECULATION_KEYS))
+    if unknown:
+        raise ValueError("unknown speculation settings: " + ", ".join(unknown))
+    if tiers is not None:
+        if not isinstance(tiers, (list, tuple)):
+            raise TypeError("acceleration.speculation.tiers must be an array")
+        try:
+            table["tiers"] = tuple(SpeculationTier(int(t[0]), int(t[1])) for t in tiers)
+        except (TypeError, ValueError, IndexError) as err:
+            raise ValueError("each speculation tier is [maximum_active_batch, draft_tokens]") from err
+    return ActiveBatchSpeculationConfig(**table)
 
 
 def load_state_dict(path: Path, device="cpu") -> dict[str, torch.Tensor]:
@@ -95,7 +130,8 @@ class LoadedModel:
                               max_tokens=int(rt.get("max_prefill_tokens", 8192)))
         self.backend = EngineBackend(runner, model_id=self.model_id, max_batch=int(rt.get("max_batch_size", 64)),
                                      max_seq_tokens=int(rt.get("max_sequence_tokens", 8192)),
-                                     bos_token_id=getattr(self.tokenizer, "bos_token_id", None))
+                                     bos_token_id=getattr(self.tokenizer, "bos_token_id", None),
+                                     speculation=speculation_from_config(config))
         self.backend.tokenizer = self.tokenizer
 
 

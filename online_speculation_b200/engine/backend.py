@@ -27,6 +27,18 @@ and kept (reference-counted) in a prefix cache, so requests that share a
 prompt -- and suffix-MH proposals that regenerate after a cut -- reuse the KV of
 every cached full page instead of recomputing it.  Only the uncached remainder
 is prefilled, in one packed batch.
+
+Rollout-reuse speculation (``speculation=ActiveBatchSpeculationConfig``): a
+:class:`~online_speculation_b200.arllm.acceleration.RolloutTokenTree` observes every
+finished sample; when the call's batch is small enough for its tier, each request
+gets a draft continuation from the tree, and all drafts of the call are verified in
+ONE packed forward (last prompt token + draft, logits of every draft row) followed by
+one sampler launch over those rows.  A deterministic draft token is kept only when it
+equals the token the request's own uniform draws at that position, so the output law
+is the target policy's; a stochastic draft is accepted with min(1, p / q) and a
+rejection is redrawn from the normalised residual (p - q)+.  The KV of rejected draft
+positions is truncated and decoding continues from the first unverified position
+(reference: transformers_backend.py:468-642 and :1091-1224).
 """
 
 from __future__ import annotations
@@ -41,9 +53,11 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from ..arllm.acceleration import ActiveBatchSpeculationConfig, DraftProposal, RolloutTokenTree
 from ..arllm.config import SamplingConfig
 from ..arllm.types import GenerationRequest, ScoreRequest, SequenceSample
 from ..ops import kernels as K
+from ..shared.rng import SeedStream
 from .kv_cache import PAGE, KVCache
 from .runner import ModelRunner, StepMeta, build_meta
 
@@ -61,6 +75,31 @@ class SequenceScoreStatistics:
     token_topk_confidences: tuple[float, ...] = ()
     confidence_top_k: int | None = None
 BUCKETS = (1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 192, 256)
+
+
+def draft_acceptance(draft: Sequence[int], sampled: Sequence[int], room: int, eos: int | None
+                     ) -> tuple[int, int, bool]:
+    """(tokens kept, draft tokens accepted, ended by EOS) of one verified draft.
+
+    ``sampled[j]`` is the target's draw at draft position j (one entry more than
+    ``draft``: the position after the whole draft).  Draws are kept while they equal
+    the draft; the first differing draw is kept as well, and when the whole draft
+    matches, the draw after it follows.  EOS and the request's remaining budget
+    ``room`` end the run early.
+    """
+    limit = min(len(draft), room)
+    accepted = 0
+    for j in range(limit):
+        tok = int(sampled[j])
+        match = tok == int(draft[j])
+        accepted += match
+        if eos is not None and tok == eos:
+            return j + 1, accepted, True
+        if not match:
+            return j + 1, accepted, False
+    if limit < room:
+        return limit + 1, accepted, eos is not None and int(sampled[limit]) == eos
+    return limit, accepted, False
 
 
 class PrefixCache:
@@ -245,7 +284,10 @@ class EngineBackend:
     def __init__(self, runner: ModelRunner, *, model_id: str | None = None, max_batch: int = 64,
                  bos_token_id: int | None = None, use_graphs: bool = True, prefix_cache_pages: int | None = None,
                  max_seq_tokens: int = 4096, prefill_tokens: int = 4096, decode_chunk: int = 16,
-                 score_pack: int = 256):
+                 score_pack: int = 256, speculation: ActiveBatchSpeculationConfig | None = None,
+                 draft_tree: RolloutTokenTree | None = None):
+        if draft_tree is not None and speculation is None:
+            raise ValueError("a draft tree needs an active-batch speculation config")
         self.runner = runner
         self.cache: KVCache = runner.cache
         self._model_id = model_id or f"b200:{runner.cfg.name}"
@@ -260,9 +302,13 @@ class EngineBackend:
         self.prefix = PrefixCache(self.cache, budget)
         self._graphs: dict[int, _DecodeGraph] = {}
         self._lock = threading.RLock()
+        self.speculation = speculation
+        self.draft_tree = draft_tree if draft_tree is not None else (
+            RolloutTokenTree.from_config(speculation) if speculation is not None else None)
         self.stats = {"sample_calls": 0, "score_calls": 0, "sampled_sequences": 0, "generated_tokens": 0,
                       "prefill_tokens": 0, "reused_prefix_tokens": 0, "decode_steps": 0, "scored_tokens": 0,
-                      "graph_kernel_launches": 0}
+                      "graph_kernel_launches": 0, "speculative_requests": 0, "speculative_hits": 0,
+                      "draft_tokens_proposed": 0, "draft_tokens_accepted": 0, "verification_token_slots": 0}
 
     @property
     def model_id(self) -> str:
@@ -274,6 +320,19 @@ class EngineBackend:
 
     def snapshot(self) -> dict:
         return dict(self.stats, prefix_cache_pages=len(self.prefix._pages))
+
+    def observe_draft_samples(self, samples) -> None:
+        """Feed finished samples (from this or another backend) to the draft tree."""
+        if self.draft_tree is not None:
+            self.draft_tree.observe_samples(samples)
+
+    def observe_draft_sequences(self, sequences) -> None:
+        if self.draft_tree is not None:
+            for seq in sequences:
+                self.draft_tree.observe(seq)
+
+    def draft_cache_snapshot(self):
+        return None if self.draft_tree is None else self.draft_tree.snapshot()
 
     def close(self) -> None:
         with self._lock:
@@ -375,6 +434,8 @@ class EngineBackend:
                 group, pending = pending[: self.max_batch], pending[self.max_batch:]
                 for i, smp in self._sample_group(group):
                     out[i] = smp
+            if self.draft_tree is not None:
+                self.draft_tree.observe_samples(out)
             self.stats["sample_calls"] += 1
             self.stats["sampled_sequences"] += len(requests)
             return out  # type: ignore[return-value]
@@ -400,6 +461,13 @@ class EngineBackend:
         for a, (seq, tokens, _) in zip(act, opened):
             self._cache_pages(seq, tokens)
         done: list[_Active] = []
+        proposals = self._propose(act)
+        if proposals:
+            self._verify_drafts(act, proposals)
+            still = []
+            for a in act:
+                (done if a.finish == "eos" or len(a.tokens) >= a.request.max_new_tokens else still).append(a)
+            act = still
         while act:
             n = len(act)
             rem = min(a.request.max_new_tokens - len(a.tokens) for a in act)
@@ -478,6 +546,135 @@ class EngineBackend:
                 req.request_id, a.finish, tuple(a.logp), BASE_POLICY)))
             self.stats["generated_tokens"] += len(a.tokens)
         return results
+
+    # ---------------------------------------------------------- speculation --
+    def _propose(self, act: list[_Active]) -> dict[int, DraftProposal]:
+        """Draft continuations from the rollout tree for the rows of one call (tiered by its size)."""
+        spec, tree = self.speculation, self.draft_tree
+        if spec is None or tree is None or not act:
+            return {}
+        self.stats["speculative_requests"] += len(act)
+        n = spec.draft_tokens(len(act))
+        if n <= 0:
+            return {}
+        out = {}
+        for j, a in enumerate(act):
+            req = a.request
+            if a.carry is not None:            # arithmetic coding: one code point, no per-token uniforms
+                continue
+            seed = SeedStream(req.seed).derive("stochastic-draft", req.request_id) if spec.stochastic_tree else None
+            prop = tree.draft(self._model_prefix(req.prefix), min(n, req.max_new_tokens),
+                              stochastic=spec.stochastic_tree, seed=seed)
+            if prop.token_ids:
+                out[j] = prop
+        return out
+
+    def _verify_drafts(self, act: list[_Active], proposals: dict[int, DraftProposal]) -> None:
+        """Verify every proposal in packed forwards of (last fed token + draft) rows."""
+        cap = min(self.prefill_tokens, self.runner.max_logit_rows)
+        chunk, used = [], 0
+        for j in sorted(proposals):
+            need = len(proposals[j].token_ids) + 1
+            if chunk and used + need > cap:
+                self._verify_chunk(chunk)
+                chunk, used = [], 0
+            chunk.append((act[j], proposals[j]))
+            used += need
+        if chunk:
+            self._verify_chunk(chunk)
+
+    def _verify_chunk(self, chunk: list[tuple[_Active, DraftProposal]]) -> None:
+        r = self.runner
+        G = r.q_slots // r.kv_slots
+        ids, pos, slots, qlens, kvlens, seqs = [], [], [], [], [], []
+        inv_t, uni, top_k, top_p = [], [], [], []
+        for a, p in chunk:
+            n = len(p.token_ids) + 1
+            slots += self.cache.append(a.seq, n)
+            ids += [a.last] + [int(t) for t in p.token_ids]
+            pos += list(range(a.pos, a.pos + n))
+            qlens.append(n)
+            kvlens.append(a.pos + n)
+            seqs.append(a.seq)
+            t0 = len(a.tokens)
+            u = np.full(n, 0.5)
+            have = a.uniforms[t0:t0 + n]
+            u[:have.size] = have
+            uni.append(u)
+            cut = self._truncation(a.request.sampling)
+            inv_t += [1.0 / a.request.sampling.temperature] * n
+            top_k += [cut[0]] * n
+            top_p += [cut[1]] * n
+        table = torch.zeros(len(chunk), self.max_pages, dtype=torch.int32)
+        self.cache.fill_table(seqs, table)
+        meta = build_meta(r.device, table, ids, pos, slots, qlens, kvlens, [0] * len(chunk), G, kv_heads=r.kv_slots)
+        logits = r.forward(meta)
+        dev = logits.device
+        it_d = torch.tensor(inv_t, dtype=torch.float32, device=dev)
+        tk_d = torch.tensor(top_k, dtype=torch.int32, device=dev)
+        tp_d = torch.tensor(top_p, dtype=torch.float32, device=dev)
+        tok, lq, lp = K.sample(logits, it_d, torch.from_numpy(np.concatenate(uni)).to(dev), top_k=tk_d, top_p=tp_d)
+        tok, lq, lp = tok.cpu().numpy(), lq.cpu().numpy(), lp.cpu().numpy()
+        self.stats["verification_token_slots"] += len(ids)
+        row = 0
+        for a, p in chunk:
+            D = len(p.token_ids)
+            rows = slice(row, row + D + 1)
+            drawn, logq, logp = tok[rows].tolist(), lq[rows].tolist(), lp[rows].tolist()
+            if p.stochastic:
+                self._stochastic_draws(a, p, logits[rows], it_d[rows], tk_d[rows], tp_d[rows], drawn, logq, logp)
+            row += D + 1
+            room = a.request.max_new_tokens - len(a.tokens)
+            keep, accepted, eos = draft_acceptance(p.token_ids, drawn, room, a.request.sampling.eos_token_id)
+            a.tokens.extend(drawn[:keep])
+            a.logq.extend(logq[:keep])
+            a.logp.extend(logp[:keep])
+            a.last, a.pos = drawn[keep - 1], a.pos + keep
+            self.cache.truncate(a.seq, a.pos)        # KV of the fed token and the accepted draft prefix
+            if eos:
+                a.finish = "eos"
+            self.draft_tree.record_verification(proposed=min(D, room), accepted=accepted)
+            self.stats["speculative_hits"] += 1
+            self.stats["draft_tokens_proposed"] += min(D, room)
+            self.stats["draft_tokens_accepted"] += accepted
+
+    @staticmethod
+    def _stochastic_draws(a: _Active, p: DraftProposal, logits, inv_t, top_k, top_p, drawn, logq, logp) -> None:
+        """Replace the inverse-CDF draws of a stochastic draft's positions by speculative sampling.
+
+        Position j keeps draft token d with probability min(1, p(d) / q(d)) (acceptance uniforms
+        from the request's ``stochastic-draft-verification`` stream); a rejection draws from
+        (p - q)+ / |(p - q)+| with the position's own uniform.  Positions after the first
+        rejection are never used.  The entry after the draft keeps the sampler's ordinary draw.
+        """
+        D = len(p.token_ids)
+        acc_u = np.random.default_rng(SeedStream(a.request.seed).derive(
+            "stochastic-draft-verification", a.request.request_id)).random(D)
+        policy = K.truncated_log_policy(logits[:D].float() * inv_t[:D, None], top_k[:D], top_p[:D])
+        full = torch.log_softmax(logits[:D].float(), dim=-1)
+        t0 = len(a.tokens)
+        for j, d in enumerate(int(t) for t in p.token_ids):
+            law = dict(p.token_distributions[j])
+            q = law.get(d, 0.0)
+            if q <= 0:
+                raise RuntimeError("a drafted token has zero proposal probability")
+            target = float(policy[j, d].exp())
+            if acc_u[j] < min(1.0, target / q):
+                tok = d
+            else:
+                resid = policy[j].double().exp()
+                idx = torch.tensor(list(law), dtype=torch.long, device=resid.device)
+                resid.index_add_(0, idx, -torch.tensor(list(law.values()), dtype=torch.float64, device=resid.device))
+                resid.clamp_min_(0.0)
+                total = float(resid.sum())
+                if not math.isfinite(total) or total <= 0:
+                    raise RuntimeError("a rejected stochastic draft has no residual mass")
+                u = float(a.uniforms[t0 + j]) if t0 + j < a.uniforms.size else 0.5
+                cdf = torch.cumsum(resid / total, 0)
+                tok = min(int((cdf < u).sum()), resid.numel() - 1)
+            drawn[j], logq[j], logp[j] = tok, float(policy[j, tok]), float(full[j, tok])
+            if tok != d:
+                return
 
     # --------------------------------------------------------------- score --
     def score_batch(self, requests: Sequence[ScoreRequest]) -> list[tuple[float, ...]]:

@@ -181,3 +181,37 @@ def test_arithmetic_coding_requests(backend, oracle):
         lp, lq = _oracle_logprobs(oracle, prefix, s.token_ids, 1.3)
         assert float((torch.tensor(s.token_logprobs) - lq).abs().max()) < 0.2
     workspace.check_status()
+
+
+@pytest.mark.parametrize("stochastic", [False, True])
+def test_rollout_reuse_speculation_verifies_drafts(oracle, stochastic):
+    from online_speculation_b200.arllm.acceleration import ActiveBatchSpeculationConfig, SpeculationTier
+
+    spec = ActiveBatchSpeculationConfig(tiers=(SpeculationTier(8, 6), SpeculationTier(512, 0)),
+                                        stochastic_tree=stochastic)
+    b = EngineBackend(build_runner(CFG, seed=11, kv_bytes=128 << 20, max_tokens=2048), max_batch=8,
+                      max_seq_tokens=512, speculation=spec)
+    try:
+        reqs = [GenerationRequest(tuple(range(60 + 100 * i, 100 + 100 * i)), 24, SamplingConfig(temperature=t),
+                                  seed=i, request_id=f"v{i}") for i, t in enumerate((0.3, 1.0))]
+        first = b.sample_batch(reqs)              # empty tree: no drafts; the outputs fill it
+        assert b.stats["speculative_hits"] == 0
+        again = b.sample_batch(reqs)              # same uniforms: each draft is the first output
+        assert b.stats["speculative_hits"] == 2 and b.stats["draft_tokens_proposed"] == 12
+        assert b.draft_cache_snapshot().accepted_tokens == b.stats["draft_tokens_accepted"]
+        if not stochastic:
+            # a kept draft token equals the target's own draw; a boundary draw moved by bf16 logits of
+            # another forward shape can end the run early, so the first request alone must agree
+            assert b.stats["draft_tokens_accepted"] >= 6
+            assert again[0].token_ids[:6] == first[0].token_ids[:6]
+        for req, smp in zip(reqs, again):
+            assert len(smp.token_ids) == 24
+            lp, lq = _oracle_logprobs(oracle, req.prefix, smp.token_ids, req.sampling.temperature)
+            assert float((torch.tensor(smp.token_logprobs) - lq).abs().max()) < 0.3
+            assert float((torch.tensor(smp.reference_token_logprobs) - lp).abs().max()) < 0.2
+            # the KV of rejected draft rows was dropped: scoring the output reproduces its log-probabilities
+            scored = b.score_batch([ScoreRequest(req.prefix, (smp.token_ids,), req.sampling)])[0]
+            assert torch.allclose(torch.tensor(scored), torch.tensor(smp.token_logprobs), atol=0.03)
+    finally:
+        b.close()
+    workspace.check_status()
