@@ -215,3 +215,21 @@ def test_rollout_reuse_speculation_verifies_drafts(oracle, stochastic):
     finally:
         b.close()
     workspace.check_status()
+
+
+def test_rollout_infra_benchmark_decode_section_on_engine():
+    from online_speculation_b200.experiments.rollout_infra import run_benchmark
+
+    def make(spec):
+        return EngineBackend(build_runner(CFG, seed=11, kv_bytes=64 << 20, max_tokens=2048), max_batch=8,
+                             max_seq_tokens=512, speculation=spec)
+
+    rep = run_benchmark(make, prompts=[tuple(range(10, 50)), tuple(range(300, 340))], section="decode",
+                        max_new_tokens=32, batch_sizes=(2, 1), history_rollouts=2, draft_tokens=6,
+                        release=lambda b: b.close())
+    plain, tree = rep["decode"]
+    assert plain["online"]["output_tokens"] == tree["online"]["output_tokens"] == 6 * 32
+    assert tree["online"]["draft_cache"]["queries"] > 0
+    # exact verification with the same uniforms reproduces the plain draws (up to bf16 boundary draws)
+    assert tree["online"]["agreement_with_plain"]["mean_matching_prefix"] > 0.8
+    workspace.check_status()
