@@ -12,6 +12,13 @@ algorithm budgets, so only the accelerator differs:
   draws except where bf16 logits of another forward shape move a boundary draw.
 * ``algorithm``: conditional IS with and without speculation, and the SMC rollout forest
   with and without reservoir reuse; each reports output tokens/s and its rollout counts.
+* ``reuse``: reward MH against a verifier with a controlled delay (``--verifier-delay``
+  seconds per exact reward): the standard chain, the prefetched chain (the next proposals
+  are generated while the reward of the current one is computed; same decisions, so the
+  same chain), and the delayed-acceptance chain (a cheap surrogate screens proposals and
+  only survivors pay for the exact reward).  Each reports wall seconds, exact reward
+  evaluations and whether its chain equals the standard one (the purpose of
+  experiments/arllm/benchmark_is_mh_reuse.py).
 
 Device work is bracketed by ``torch.cuda.synchronize`` and timed with CUDA events (wall
 time is recorded beside them).  Model weights are random (``random:<preset>``) or a local
@@ -20,7 +27,7 @@ scaled log-probability under the base model (no tokenizer or dataset is needed).
 
     python -m online_speculation_b200.experiments.rollout_infra --output infra.json \\
         [--model random:qwen2.5-0.5b] [--section decode|algorithm|all] [--prompts 2] \\
-        [--max-new-tokens 64] [--batch-sizes 4,2,1] [--draft-tokens 8]
+        [--max-new-tokens 64] [--batch-sizes 4,2,1] [--draft-tokens 8] [--verifier-delay 0.05]
 
 Purpose and arm layout of experiments/arllm/benchmark_rollout_infra.py; the record keys
 (``cache_build``, ``online``, ``draft_cache``) follow it so summaries read both.
@@ -185,11 +192,55 @@ def algorithm_arm(backend, *, name: str, prompts: Sequence[tuple], length: int, 
                                      "diagnostics": diagnostics}}
 
 
+def reuse_arms(backend, *, prompt: tuple, length: int, block: int, updates: int, seed: int, reward: Callable,
+               verifier_delay: float) -> list[dict]:
+    """Standard, prefetched and delayed-acceptance reward MH on one backend and prompt."""
+    import hashlib
+
+    from ..arllm.algorithms.mh import run_reward_mh_chain
+    from ..arllm.algorithms.mh_acceleration import run_reward_mh_chain_delayed, run_reward_mh_chain_prefetched
+    from ..arllm.config import RewardMHConfig
+
+    calls = {"exact": 0}
+
+    def slow(p, y):
+        calls["exact"] += 1
+        time.sleep(verifier_delay)
+        return reward(p, y)
+
+    cfg = RewardMHConfig(total_length=length, block_size=block, reward_temperature=0.5, iterations=updates)
+    sampling = SamplingConfig()
+    out, standard = [], None
+    for name in ("mh_standard", "mh_prefetched", "mh_delayed"):
+        calls["exact"] = 0
+        seeds = SeedStream(SeedStream(seed).derive("infra", "reuse"))
+        if name == "mh_standard":
+            res, t = measure(lambda: run_reward_mh_chain(backend, prompt, cfg, sampling, slow, seeds))
+            chain = res
+        elif name == "mh_prefetched":
+            res, t = measure(lambda: run_reward_mh_chain_prefetched(backend, prompt, cfg, sampling, slow, seeds))
+            chain = res.chain
+        else:
+            res, t = measure(lambda: run_reward_mh_chain_delayed(backend, prompt, cfg, sampling, slow, reward, seeds))
+            chain = res
+        tokens = tuple(chain.token_ids)
+        if standard is None:
+            standard = tokens
+        accepted = sum(bool(getattr(st, "accepted", False)) for st in chain.trace)
+        out.append({"name": name, "online": {"telemetry": t, "exact_reward_evaluations": calls["exact"],
+                                             "updates": len(chain.trace), "accepted_updates": accepted,
+                                             "token_sha256": hashlib.sha256(np.asarray(tokens, np.int64).tobytes())
+                                             .hexdigest()[:16],
+                                             "identical_to_standard": tokens == standard}})
+    return out
+
+
 def run_benchmark(make_backend: Callable[[ActiveBatchSpeculationConfig | None], Any], *, prompts: Sequence[tuple],
                   section: str = "all", max_new_tokens: int = 64, batch_sizes: Sequence[int] = (4, 2, 1),
                   history_rollouts: int = 2, draft_tokens: int = 8, block_size: int = 16, candidates: int = 3,
                   rollouts: int = 2, seed: int = 20260812, reward_factory: Callable[[Any], Callable] | None = None,
-                  release: Callable[[Any], None] = lambda b: None) -> dict:
+                  release: Callable[[Any], None] = lambda b: None, mh_updates: int = 8,
+                  verifier_delay: float = 0.05) -> dict:
     """All arms of the selected sections; ``make_backend(speculation)`` builds a fresh backend per arm."""
     spec = ActiveBatchSpeculationConfig(tiers=(SpeculationTier(max(batch_sizes), draft_tokens),
                                                SpeculationTier(1 << 20, 0)))
@@ -227,6 +278,15 @@ def run_benchmark(make_backend: Callable[[ActiveBatchSpeculationConfig | None], 
             finally:
                 release(b)
         report["algorithm"] = arms
+    if section in ("reuse", "all"):
+        b = make_backend(None)
+        try:
+            reward = reward_factory(b) if reward_factory is not None else (lambda _p, y: 0.0)
+            report["reuse"] = reuse_arms(b, prompt=tuple(prompts[0]), length=max_new_tokens, block=block_size,
+                                         updates=mh_updates, seed=seed, reward=reward, verifier_delay=verifier_delay)
+        finally:
+            release(b)
+        report["workload"].update(mh_updates=mh_updates, verifier_delay_seconds=verifier_delay)
     return report
 
 
@@ -242,7 +302,9 @@ def main(argv=None) -> int:
     p = argparse.ArgumentParser(prog="python -m online_speculation_b200.experiments.rollout_infra")
     p.add_argument("--output", type=Path, required=True)
     p.add_argument("--model", default="random:qwen2.5-0.5b", help="random:<preset> or a local checkpoint directory")
-    p.add_argument("--section", choices=("decode", "algorithm", "all"), default="all")
+    p.add_argument("--section", choices=("decode", "algorithm", "reuse", "all"), default="all")
+    p.add_argument("--mh-updates", type=int, default=8)
+    p.add_argument("--verifier-delay", type=float, default=0.05, help="seconds added to every exact reward")
     p.add_argument("--prompts", type=int, default=2)
     p.add_argument("--prompt-tokens", type=int, default=128)
     p.add_argument("--max-new-tokens", type=int, default=64)
@@ -285,7 +347,7 @@ def main(argv=None) -> int:
                            batch_sizes=[int(x) for x in a.batch_sizes.split(",")],
                            history_rollouts=a.history_rollouts, draft_tokens=a.draft_tokens,
                            block_size=a.block_size, candidates=a.candidate_count, rollouts=a.rollout_count,
-                           seed=a.seed, release=release,
+                           seed=a.seed, release=release, mh_updates=a.mh_updates, verifier_delay=a.verifier_delay,
                            reward_factory=lambda b: SequenceLogProbabilityReward(b, coefficient=0.5))
     report.update(model=a.model, machine=_machine(), data="synthetic uniform-random prompts, random-init weights"
                   if a.model.startswith("random:") else "synthetic uniform-random prompts")
@@ -293,6 +355,7 @@ def main(argv=None) -> int:
     a.output.write_text(json.dumps(report, indent=2))
     summary = {arm["name"]: round(arm["online"]["output_tokens_per_second"], 1)
                for sec in ("decode", "algorithm") for arm in report.get(sec, [])}
+    summary.update({arm["name"]: round(arm["online"]["telemetry"]["wall_seconds"], 2) for arm in report.get("reuse", [])})
     print(json.dumps({"output": str(a.output), "tokens_per_second": summary}))
     return 0
 

@@ -15,7 +15,8 @@ def test_harness_runs_every_arm_on_the_tabular_backend():
         return TabularBackend.per_position_logits(16, 12, seed=2, prompt_length=3)
 
     rep = run_benchmark(make, prompts=[(1, 2, 3), (4, 5, 6)], max_new_tokens=8, batch_sizes=(2, 1),
-                        history_rollouts=1, draft_tokens=4, block_size=4, candidates=2, rollouts=2)
+                        history_rollouts=1, draft_tokens=4, block_size=4, candidates=2, rollouts=2, mh_updates=6,
+                        verifier_delay=0.0)
     assert [a["name"] for a in rep["decode"]] == ["plain", "rollout_tree"]
     assert [a["name"] for a in rep["algorithm"]] == ["conditional_plain", "conditional_rollout_tree",
                                                      "smc_no_reuse", "smc_reuse"]
@@ -28,6 +29,11 @@ def test_harness_runs_every_arm_on_the_tabular_backend():
     smc = rep["algorithm"][3]["online"]["diagnostics"]
     assert len(smc) == 2 and all("reused_rollouts" in d for d in smc)
     assert all(np.isfinite(a["online"]["output_tokens_per_second"]) for a in rep["algorithm"])
+    reuse = {a["name"]: a["online"] for a in rep["reuse"]}
+    assert set(reuse) == {"mh_standard", "mh_prefetched", "mh_delayed"}
+    # prefetching changes when proposals are generated, not which: the same chain
+    assert reuse["mh_prefetched"]["identical_to_standard"]
+    assert reuse["mh_delayed"]["exact_reward_evaluations"] <= reuse["mh_standard"]["exact_reward_evaluations"]
 
 
 def test_agreement_metric():
