@@ -17,6 +17,7 @@
 #include "diffusion.h"
 #include "elementwise.h"
 #include "gemm.h"
+#include "grpo.h"
 #include "moe.h"
 #include "kv_manager.h"
 #include "sampling.h"
@@ -752,6 +753,33 @@ void grad_sq_norm(Tensor g, Tensor out) {
         "grad_sq_norm");
 }
 
+void grpo_loss(Tensor logp, Tensor old_logp, Tensor ref_logp, Tensor adv, Tensor mask, double beta, double eps,
+               Tensor grad, Tensor row_stats, Tensor out, Tensor counter) {
+  for (const Tensor* t : {&logp, &old_logp, &ref_logp, &grad}) {
+    CHECK_CUDA(*t);
+    CHECK_DT(*t, torch::kFloat32);
+    TORCH_CHECK(t->is_contiguous() && t->sizes() == logp.sizes() && t->dim() == 2,
+                "GRPO loss rows must be contiguous fp32 [B, C] tensors of one shape");
+  }
+  CHECK_DT(adv, torch::kFloat32);
+  CHECK_DT(row_stats, torch::kFloat32);
+  CHECK_DT(out, torch::kFloat32);
+  CHECK_DT(counter, torch::kInt32);
+  TORCH_CHECK(mask.scalar_type() == torch::kBool || mask.scalar_type() == torch::kUInt8, "mask must be bool or uint8");
+  TORCH_CHECK(mask.is_contiguous() && mask.sizes() == logp.sizes(), "mask must match logp");
+  const int B = static_cast<int>(logp.size(0)), C = static_cast<int>(logp.size(1));
+  TORCH_CHECK(adv.is_contiguous() && adv.numel() == B, "one advantage per sequence");
+  TORCH_CHECK(row_stats.is_contiguous() && row_stats.numel() >= 4LL * B, "row_stats holds 4 values per sequence");
+  TORCH_CHECK(out.numel() >= 3 && counter.numel() >= 1, "out holds 3 values, counter 1");
+  const c10::cuda::CUDAGuard guard(logp.device());
+  osb::GrpoLossArgs a{logp.data_ptr<float>(), old_logp.data_ptr<float>(), ref_logp.data_ptr<float>(),
+                      adv.data_ptr<float>(), reinterpret_cast<const unsigned char*>(mask.data_ptr()), B, C,
+                      static_cast<float>(beta), static_cast<float>(eps), grad.data_ptr<float>(),
+                      row_stats.data_ptr<float>(), out.data_ptr<float>(),
+                      reinterpret_cast<unsigned int*>(counter.data_ptr<int>())};
+  check(osb::grpo_loss_launch(a, at::cuda::getCurrentCUDAStream()), "grpo_loss");
+}
+
 void adamw(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> publish, c10::optional<Tensor> sq_norm,
            double clip, double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
            c10::optional<Tensor> nonfinite, c10::optional<Tensor> step_tensor) {
@@ -949,6 +977,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("divergence_grad", &divergence_grad);
   m.def("logprob_grad", &logprob_grad);
   m.def("adamw", &adamw);
+  m.def("grpo_loss", &grpo_loss);
   m.def("gemm_pick_bn", &osb::gemm_pick_bn);
   m.def("score_stats", &score_stats);
   m.def("grouped_tiles", &grouped_tiles);

@@ -778,6 +778,52 @@ def _spec_verify_shard(target, draft, candidates, inv_temp, seeds, streams, salt
     return res
 
 
+# ------------------------------------------------------------------- grpo --
+def grpo_loss_reference(logp, old_logp, ref_logp, advantages, mask, *, beta, epsilon):
+    """fp32 oracle of the GRPO loss: (loss, per-token dLoss/dlogp, [loss, token-mean KL, clip fraction]).
+
+    Per token min(r A, clip(r, 1 - eps, 1 + eps) A) - beta (exp(ref - lp) - (ref - lp) - 1) with
+    r = exp(lp - old), token mean per sequence, mean over sequences, negated; the gradient
+    comes from autograd of exactly that expression.
+    """
+    lp = logp.detach().float().clone().requires_grad_(True)
+    ratio = torch.exp(lp - old_logp.float())
+    a = advantages.float()[:, None]
+    obj = torch.minimum(ratio * a, ratio.clamp(1 - epsilon, 1 + epsilon) * a)
+    delta = ref_logp.float() - lp
+    kl = torch.exp(delta) - delta - 1
+    m = mask.float()
+    per_seq = ((obj - beta * kl) * m).sum(1) / m.sum(1).clamp(min=1)
+    loss = -per_seq.mean()
+    (grad,) = torch.autograd.grad(loss, lp)
+    with torch.no_grad():
+        tokens = m.sum().clamp(min=1)
+        clipped = ((ratio - 1).abs() > epsilon).float()
+        stats = torch.stack((loss.detach(), (kl * m).sum() / tokens, (clipped * m).sum() / tokens))
+    return loss.detach(), grad, stats
+
+
+def grpo_loss(logp, old_logp, ref_logp, advantages, mask, *, beta, epsilon):
+    """Fused GRPO loss on the GPU (one launch): returns (loss [], dLoss/dlogp [B, C], stats [3]).
+
+    ``stats`` = (loss, token-mean KL, clipped-token fraction), left on the device.  CPU
+    tensors take :func:`grpo_loss_reference`.
+    """
+    if not logp.is_cuda:
+        return grpo_loss_reference(logp, old_logp, ref_logp, advantages, mask, beta=beta, epsilon=epsilon)
+    B, C = logp.shape
+    dev = logp.device
+    lp, old, ref = (t.detach().float().contiguous() for t in (logp, old_logp, ref_logp))
+    grad = torch.empty_like(lp)
+    rows = torch.empty(B, 4, dtype=torch.float32, device=dev)
+    out = torch.empty(3, dtype=torch.float32, device=dev)
+    # zero when created; the kernel's last block resets it after every launch
+    counter = workspace.zeros(dev, "grpo_counter", 1, torch.int32)
+    _ext.require().grpo_loss(lp, old, ref, advantages.detach().float().contiguous(), mask.contiguous(),
+                             float(beta), float(epsilon), grad, rows, out, counter)
+    return out[0], grad, out
+
+
 # ------------------------------------------------------------------ adamw --
 def adamw_step(params, grads, exp_avg, exp_avg_sq, *, step, lr, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
                clip=None, publish=None, norm_out=None, nonfinite=None, step_tensor=None):

@@ -90,6 +90,11 @@ def scratch(device: torch.device, name: str, numel: int, dtype: torch.dtype) -> 
     return buffer[:numel]
 
 
+def zeros(device: torch.device, name: str, numel: int, dtype: torch.dtype) -> torch.Tensor:
+    """A named per-device buffer created zeroed once (for counters that kernels reset themselves)."""
+    return _get(device, "zeros:" + name, lambda d: torch.zeros(numel, dtype=dtype, device=d))
+
+
 def status(device: torch.device) -> torch.Tensor:
     return _get(device, "status", lambda d: torch.zeros(1, dtype=torch.int32, device=d))
 

@@ -68,7 +68,7 @@ class SymmetricCollectives(NcclCollectives):
     def __init__(self, group, hidden: int, max_tokens: int, device, *, blocks: int = 132, push: bool | None = None,
                  algorithm: str = "auto", wait_limit_ns: int = 0):
         """``algorithm``: "auto" (one-shot up to four ranks, and above while each rank reads at most
-        4 MiB of peer partials; two-shot otherwise), "oneshot" or "twoshot".
+        16 MiB of peer partials; two-shot otherwise), "oneshot" or "twoshot".
         ``wait_limit_ns``: limit of every cross-rank wait inside the kernels (0: two seconds); a wait
         that runs out records an error in the status word instead of hanging."""
         import os

@@ -97,9 +97,33 @@ def group_advantages(rewards: torch.Tensor, group: int, scale: str = "none") -> 
     return adv.reshape(-1)
 
 
+class _PrecomputedGradLoss(torch.autograd.Function):
+    """A scalar loss whose gradient with respect to ``logp`` was computed along with it."""
+
+    @staticmethod
+    def forward(ctx, logp, loss, grad):
+        ctx.save_for_backward(grad)
+        return loss.clone()
+
+    @staticmethod
+    def backward(ctx, g):
+        (grad,) = ctx.saved_tensors
+        return grad * g, None, None
+
+
 def grpo_loss(logp: torch.Tensor, old_logp: torch.Tensor, ref_logp: torch.Tensor, advantages: torch.Tensor,
               mask: torch.Tensor, *, beta: float, epsilon: float) -> tuple[torch.Tensor, dict]:
-    """Clipped-ratio policy loss with a k3 KL penalty, token-mean per sequence then sequence mean."""
+    """Clipped-ratio policy loss with a k3 KL penalty, token-mean per sequence then sequence mean.
+
+    On the GPU one fused kernel computes the loss, its gradient and the metrics
+    (``csrc/grpo.cu``); on the CPU the same expression runs in torch.  The metrics come
+    back as floats: one device-to-host read of three values.
+    """
+    if logp.is_cuda:
+        value, grad, stats = K.grpo_loss(logp, old_logp, ref_logp, advantages, mask, beta=beta, epsilon=epsilon)
+        loss = _PrecomputedGradLoss.apply(logp, value, grad)
+        kl, clip = stats[1:].tolist()
+        return loss, {"kl": kl, "clip_fraction": clip}
     ratio = torch.exp(logp - old_logp)
     a = advantages[:, None]
     obj = torch.minimum(ratio * a, ratio.clamp(1 - epsilon, 1 + epsilon) * a)

@@ -178,3 +178,21 @@ def test_grpo_run_checkpoints_resume_bit_exact_and_refuse_changed_settings(tmp_p
     fresh = GRPORun(tmp_path / "b", TINY, conf, max_steps=6, save_steps=2, device="cpu", seed=3, data=_synthetic,
                     resume="none")
     assert fresh.trainer.step_count == 0
+
+
+def test_grpo_loss_cpu_matches_the_kernel_oracle():
+    from online_speculation_b200.ops import kernels as K
+    from online_speculation_b200.training.grpo import grpo_loss
+
+    g = torch.Generator().manual_seed(3)
+    old = -torch.rand(5, 19, generator=g) * 3
+    lp = (old + torch.randn(5, 19, generator=g) * 0.3).requires_grad_(True)
+    ref = old + torch.randn(5, 19, generator=g) * 0.2
+    adv = torch.randn(5, generator=g)
+    mask = torch.rand(5, 19, generator=g) < 0.7
+    loss, info = grpo_loss(lp, old, ref, adv, mask, beta=0.04, epsilon=0.2)
+    loss.backward()
+    want, grad, stats = K.grpo_loss_reference(lp, old, ref, adv, mask, beta=0.04, epsilon=0.2)
+    assert torch.allclose(loss.detach(), want) and torch.allclose(lp.grad, grad)
+    assert info["kl"] == pytest.approx(float(stats[1]), rel=1e-6)
+    assert info["clip_fraction"] == pytest.approx(float(stats[2]), rel=1e-6)

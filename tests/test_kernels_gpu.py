@@ -557,3 +557,23 @@ def test_sample_arithmetic_code_point_rescaling(cuda):
     assert (nxt.cpu()[~flagged] == -1.0).all()
     assert ((nxt.cpu()[flagged] >= 0) & (nxt.cpu()[flagged] < 1)).all()
 
+
+
+@pytest.mark.parametrize("B,C", [(4, 37), (64, 256), (3, 1000)])
+def test_grpo_loss_kernel_matches_fp32_oracle(B, C):
+    g = torch.Generator(device="cuda").manual_seed(B * 1000 + C)
+    old = -torch.rand(B, C, device="cuda", generator=g) * 4
+    lp = old + torch.randn(B, C, device="cuda", generator=g) * 0.3       # ratios on both sides of the clip range
+    ref = old + torch.randn(B, C, device="cuda", generator=g) * 0.2
+    adv = torch.randn(B, device="cuda", generator=g)
+    mask = torch.rand(B, C, device="cuda", generator=g) < 0.8
+    mask[0] = False                                                       # a sequence without completion tokens
+    loss, grad, stats = ops.grpo_loss(lp, old, ref, adv, mask, beta=0.04, epsilon=0.2)
+    want_loss, want_grad, want_stats = ops.grpo_loss_reference(lp.cpu(), old.cpu(), ref.cpu(), adv.cpu(),
+                                                               mask.cpu(), beta=0.04, epsilon=0.2)
+    assert torch.allclose(loss.cpu(), want_loss, rtol=1e-4, atol=1e-6)
+    assert torch.allclose(grad.cpu(), want_grad, rtol=1e-4, atol=1e-8)
+    assert torch.allclose(stats.cpu(), want_stats, rtol=1e-4, atol=1e-6)
+    # the arrival counter resets itself: a second launch gives the same result
+    loss2, _, _ = ops.grpo_loss(lp, old, ref, adv, mask, beta=0.04, epsilon=0.2)
+    assert float(loss2) == float(loss)
