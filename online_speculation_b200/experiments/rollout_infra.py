@@ -7,9 +7,11 @@ algorithm budgets, so only the accelerator differs:
   tree, tiered by batch size).  A history phase fills the tree (timed and counted on its
   own, so the offline cost stays visible), then evaluation batches of shrinking size run
   -- the long tail where drafting pays.  Besides tokens/s and the draft counters, every arm
-  reports the fraction of evaluation requests whose tokens equal the plain arm's: the
-  verification keeps the sampled law, and with the same uniforms it reproduces the plain
-  draws except where bf16 logits of another forward shape move a boundary draw.
+  reports the fraction of evaluation requests whose tokens equal the plain arm's.  The
+  verification keeps the sampled law; with the same uniforms it reproduces the plain draws
+  as far as the two forward shapes give the same logits, which holds for the peaked laws of
+  a trained model but not for the near-flat laws of random-init weights, where bf16
+  differences move inverse-CDF draws by a few token ids.
 * ``algorithm``: conditional IS with and without speculation, and the SMC rollout forest
   with and without reservoir reuse; each reports output tokens/s and its rollout counts.
 * ``reuse``: reward MH against a verifier with a controlled delay (``--verifier-delay``
