@@ -210,8 +210,10 @@ def test_rollout_reuse_speculation_verifies_drafts(oracle, stochastic):
         for req, smp in zip(reqs, again):
             assert len(smp.token_ids) == 24
             lp, lq = _oracle_logprobs(oracle, req.prefix, smp.token_ids, req.sampling.temperature)
-            assert float((torch.tensor(smp.token_logprobs) - lq).abs().max()) < 0.3
-            assert float((torch.tensor(smp.reference_token_logprobs) - lp).abs().max()) < 0.2
+            # bf16 activations vs the fp32 oracle (errors grow as 1 / T), as in the plain-sampling test
+            got_p, got_q = torch.tensor(smp.reference_token_logprobs), torch.tensor(smp.token_logprobs)
+            assert float((got_p - lp).norm() / lp.norm()) < 0.02 and float((got_p - lp).abs().max()) < 0.2
+            assert float((got_q - lq).norm() / lq.norm()) < 0.03 / min(1.0, req.sampling.temperature) ** 0.5
             # the KV of rejected draft rows was dropped: scoring the output reproduces its log-probabilities
             scored = b.score_batch([ScoreRequest(req.prefix, (smp.token_ids,), req.sampling)])[0]
             assert torch.allclose(torch.tensor(scored), torch.tensor(smp.token_logprobs), atol=0.03)
