@@ -853,12 +853,10 @@ EncodeTiledFn tensor_map_encoder() {
 // used two warpgroups (an earlier build, with a single-warpgroup epilogue, ran
 // decode steps about 6% slower with it).  Every kernel launched this way waits
 // (griddepcontrol.wait) before it reads its predecessor's output; only static
-// weights are prefetched ahead of that wait.  OSB_PDL=0 (or set_pdl) disables it.
+// weights are prefetched ahead of that wait.  The extension's set_pdl(False) disables it
+// (for A/B timing).
 bool& pdl_enabled() {
-  static bool on = [] {
-    const char* v = getenv("OSB_PDL");
-    return v == nullptr || v[0] != '0';
-  }();
+  static bool on = true;
   return on;
 }
 
