@@ -15,6 +15,7 @@
 #include "ep.h"
 #include "comm.h"
 #include "diffusion.h"
+#include "dp.h"
 #include "elementwise.h"
 #include "gemm.h"
 #include "grpo.h"
@@ -616,6 +617,64 @@ void allreduce_pushed_add_rmsnorm(std::vector<int64_t> parts, std::vector<int64_
   allreduce_norm_impl(parts, {}, pads, epoch, h, w, x, T, rank, eps, blocks, status, true, 0, wait_ns);
 }
 
+osb::DpArgs dp_args(const std::vector<int64_t>& grads, const std::vector<int64_t>& params,
+                    const std::vector<int64_t>& pads, Tensor counters, int64_t rank, Tensor status, int64_t wait_ns) {
+  const int world = static_cast<int>(pads.size());
+  TORCH_CHECK(world >= 2 && world <= osb::kMaxRanks, "data-parallel collectives need 2..8 ranks");
+  TORCH_CHECK(grads.empty() || static_cast<int>(grads.size()) == world, "one gradient pointer per rank");
+  TORCH_CHECK(params.empty() || static_cast<int>(params.size()) == world, "one parameter pointer per rank");
+  TORCH_CHECK(rank >= 0 && rank < world, "rank out of range");
+  CHECK_CUDA(counters);
+  CHECK_DT(counters, torch::kInt32);
+  TORCH_CHECK(counters.numel() >= 4, "counters holds 4 words");
+  CHECK_DT(status, torch::kInt32);
+  osb::DpArgs a{};
+  for (int q = 0; q < world; ++q) {
+    a.grads[q] = grads.empty() ? nullptr : reinterpret_cast<const float*>(grads[q]);
+    a.params[q] = params.empty() ? nullptr : reinterpret_cast<__nv_bfloat16*>(params[q]);
+    a.pads[q] = reinterpret_cast<uint32_t*>(pads[q]);
+  }
+  a.counters = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
+  a.rank = static_cast<int>(rank);
+  a.world = world;
+  a.status = status.data_ptr<int>();
+  a.wait_ns = static_cast<unsigned long long>(wait_ns);
+  return a;
+}
+
+// shard = scale * (sum over ranks of grads[q][lo + rank * n, + n)), rank order, peer loads.
+void dp_reduce_scatter(std::vector<int64_t> grads, std::vector<int64_t> pads, Tensor counters, int64_t rank,
+                       int64_t lo, int64_t n, Tensor shard, double scale, Tensor status, int64_t wait_ns) {
+  CHECK_CUDA(shard);
+  CHECK_DT(shard, torch::kFloat32);
+  TORCH_CHECK(shard.is_contiguous() && shard.numel() >= n, "shard must hold n contiguous floats");
+  const c10::cuda::CUDAGuard guard(shard.device());
+  const osb::DpArgs a = dp_args(grads, {}, pads, counters, rank, status, wait_ns);
+  check(osb::dp_reduce_scatter_launch(a, lo, n, shard.data_ptr<float>(), static_cast<float>(scale),
+                                      at::cuda::getCurrentCUDAStream()),
+        "data-parallel reduce-scatter");
+}
+
+// params[q][lo + rank * n, + n) = src for every rank q (peer stores), between two barriers.
+void dp_all_gather(std::vector<int64_t> params, std::vector<int64_t> pads, Tensor counters, int64_t rank, Tensor src,
+                   int64_t lo, int64_t n, Tensor status, int64_t wait_ns) {
+  CHECK_CUDA(src);
+  CHECK_DT(src, torch::kBFloat16);
+  TORCH_CHECK(src.is_contiguous() && src.numel() >= n, "src must hold n contiguous bf16 values");
+  const c10::cuda::CUDAGuard guard(src.device());
+  const osb::DpArgs a = dp_args({}, params, pads, counters, rank, status, wait_ns);
+  check(osb::dp_all_gather_launch(a, reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()), lo, n,
+                                  at::cuda::getCurrentCUDAStream()),
+        "data-parallel all-gather");
+}
+
+// Zeroes `bytes` at a raw device address on the current stream (signal-pad reset).
+void zero_device_bytes(int64_t ptr, int64_t bytes) {
+  TORCH_CHECK(ptr != 0 && bytes > 0, "zero_device_bytes needs an address and a positive size");
+  check(cudaMemsetAsync(reinterpret_cast<void*>(ptr), 0, static_cast<size_t>(bytes), at::cuda::getCurrentCUDAStream()),
+        "zero_device_bytes");
+}
+
 // Row-parallel GEMM whose bf16 output tile is stored into every rank's receive slot for
 // this rank (dsts[q], row stride = M) and whose last CTA releases *epoch + 1 into
 // flags[q]; `out` is this rank's own slot (shape / stride checks only).
@@ -978,6 +1037,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("logprob_grad", &logprob_grad);
   m.def("adamw", &adamw);
   m.def("grpo_loss", &grpo_loss);
+  m.def("dp_reduce_scatter", &dp_reduce_scatter);
+  m.def("dp_all_gather", &dp_all_gather);
+  m.def("zero_device_bytes", &zero_device_bytes);
   m.def("gemm_pick_bn", &osb::gemm_pick_bn);
   m.def("score_stats", &score_stats);
   m.def("grouped_tiles", &grouped_tiles);

@@ -75,6 +75,7 @@ class GRPOConfig:
     head_chunk_rows: int = 2048
     eos_token_id: int | None = None
     seed: int = 0
+    dp_collectives: str = "symmetric"   # "symmetric" (peer-memory kernels, CUDA) | "nccl"
 
     def __post_init__(self):
         if min(self.group_size, self.prompts_per_rank, self.prompt_length, self.completion_length,
@@ -86,6 +87,8 @@ class GRPOConfig:
             raise ValueError("scale_rewards must be none or group")
         if not (self.learning_rate > 0 and self.epsilon > 0 and self.beta >= 0 and self.max_grad_norm > 0):
             raise ValueError("positive learning rate / epsilon / clip and non-negative beta required")
+        if self.dp_collectives not in ("symmetric", "nccl"):
+            raise ValueError("dp_collectives must be symmetric or nccl")
 
 
 def group_advantages(rewards: torch.Tensor, group: int, scale: str = "none") -> torch.Tensor:
@@ -151,7 +154,7 @@ class FlatParameters:
     """bf16 parameters as views of one flat buffer, bucketed and sharded over data-parallel ranks."""
 
     def __init__(self, named: list[tuple[str, torch.Tensor, int, int]], world: int, rank: int, device,
-                 align: int = 64):
+                 align: int = 64, allocate: Callable[[int, torch.dtype], torch.Tensor] | None = None):
         # named: (name, tensor, bucket key, uses per forward)
         self.world, self.rank = world, rank
         buckets: dict[int, list] = {}
@@ -169,7 +172,8 @@ class FlatParameters:
             off = lo + -(-(off - lo) // quantum) * quantum
             self.bucket_ranges.append((lo, off))
         self.numel = off
-        self.flat = torch.zeros(self.numel, dtype=torch.bfloat16, device=device)
+        self.flat = (allocate(self.numel, torch.bfloat16) if allocate is not None
+                     else torch.zeros(self.numel, dtype=torch.bfloat16, device=device))
         for name, t, _, _ in named:
             self.view(name).copy_(t)
         self.trainable = sum(t.numel() for _, t, _, _ in named)
@@ -194,13 +198,20 @@ class FlatParameters:
 
 
 class GradientSink:
-    """fp32 gradient buffer whose buckets are reduce-scattered as soon as they are complete."""
+    """fp32 gradient buffer whose buckets are reduce-scattered as soon as they are complete.
 
-    def __init__(self, params: FlatParameters, group, device):
+    ``dp`` (:mod:`online_speculation_b200.parallel.dp`) owns the gradient buffer and the
+    reduce-scatter: the peer-memory kernel or NCCL; every bucket's shard is the data-parallel
+    mean of the ranks' gradients.
+    """
+
+    def __init__(self, params: FlatParameters, group, device, dp=None):
         self.p = params
         self.group = group
         self.world = params.world
-        self.grad = torch.zeros(params.numel, dtype=torch.float32, device=device)
+        self.dp = dp
+        self.grad = (dp.allocate(params.numel, torch.float32) if dp is not None
+                     else torch.zeros(params.numel, dtype=torch.float32, device=device))
         # one rank: the whole buffer is the shard
         self.shard = self.grad if self.world == 1 else torch.zeros(params.shard_numel, dtype=torch.float32,
                                                                    device=device)
@@ -258,14 +269,12 @@ class GradientSink:
         self.launched.append(b)
         if self.world == 1:
             return
-        import torch.distributed as dist
-
         if self.stream is None:
-            dist.reduce_scatter_tensor(self.shard[pos:pos + n], self.grad[lo:hi], group=self.group)
+            self.dp.reduce_scatter(self.grad, lo, hi, self.shard[pos:pos + n], 1.0 / self.world)
             return
         self.stream.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(self.stream):
-            dist.reduce_scatter_tensor(self.shard[pos:pos + n], self.grad[lo:hi], group=self.group)
+            self.dp.reduce_scatter(self.grad, lo, hi, self.shard[pos:pos + n], 1.0 / self.world)
 
     def finish(self) -> torch.Tensor:
         """Reduce any bucket not launched yet, wait for the reductions, return the averaged shard."""
@@ -275,8 +284,6 @@ class GradientSink:
                 self._reduce(b)
         if self.stream is not None:
             torch.cuda.current_stream().wait_stream(self.stream)
-        if self.world > 1:
-            self.shard.div_(self.world)
         return self.shard
 
 
@@ -441,10 +448,18 @@ class GRPOTrainer:
         policy = build_weights(model, sd, device=self.device)
         ref = build_weights(model, sd, device=self.device)
         del sd
+        # data-parallel collectives: peer-memory kernels over symmetric buffers on GPUs, else the process group
+        self.dp = None
+        if self.world > 1:
+            from ..parallel.dp import make_data_parallel
+
+            kind = config.dp_collectives if self.device.type == "cuda" else "nccl"
+            self.dp = make_data_parallel(group, self.device, kind)
         # flat bf16 parameters; the runner's weights become views of it
-        self.params = FlatParameters(_named_tensors(policy), self.world, self.rank, self.device)
+        self.params = FlatParameters(_named_tensors(policy), self.world, self.rank, self.device,
+                                     allocate=None if self.dp is None else self.dp.allocate)
         self.policy_weights = self._rebind(policy)
-        self.sink = GradientSink(self.params, group, self.device)
+        self.sink = GradientSink(self.params, group, self.device, dp=self.dp)
         leaves = {}
         for name in self.params.slots:
             v = self.params.view(name)
@@ -581,13 +596,14 @@ class GRPOTrainer:
                          lr=c.learning_rate, betas=c.adam_betas, eps=c.adam_eps, weight_decay=c.weight_decay,
                          publish=self.publish)
         if self.world > 1:
-            import torch.distributed as dist
-
-            for (lo, hi, pos), (blo, bhi) in zip(self.params.shard_ranges(), self.params.bucket_ranges):
-                dist.all_gather_into_tensor(self.params.flat[blo:bhi], self.publish[pos:pos + hi - lo],
-                                            group=self.group)
+            self._gather_parameters()
         else:
             self.params.flat.copy_(self.publish)
+
+    def _gather_parameters(self) -> None:
+        """Every rank's bf16 shard into every rank's flat parameters (one collective per bucket)."""
+        for (lo, hi, pos), (blo, bhi) in zip(self.params.shard_ranges(), self.params.bucket_ranges):
+            self.dp.all_gather(self.params.flat, blo, bhi, self.publish[pos:pos + hi - lo])
 
     def step(self) -> dict:
         t0 = time.perf_counter()
@@ -598,6 +614,9 @@ class GRPOTrainer:
         out = self.train_on(ids, mask, rewards)
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
+            from ..ops import workspace
+
+            workspace.check_status(self.device)     # a cross-rank wait that ran out raises here
         t2 = time.perf_counter()
         out.update(tokens=int(ids.numel()), completion_tokens=int(mask.sum()), rollout_s=t1 - t0, train_s=t2 - t1,
                    grad_norm=float(self.sq_norm.sqrt()), step=self.step_count)
@@ -634,11 +653,7 @@ class GRPOTrainer:
         self.rng.bit_generator.state = state["rng"]
         self.publish.copy_(self.master)
         if self.world > 1:
-            import torch.distributed as dist
-
-            for (lo, hi, pos), (blo, bhi) in zip(self.params.shard_ranges(), self.params.bucket_ranges):
-                dist.all_gather_into_tensor(self.params.flat[blo:bhi], self.publish[pos:pos + hi - lo],
-                                            group=self.group)
+            self._gather_parameters()
         else:
             for lo, hi, pos in self.params.shard_ranges():
                 self.params.flat[lo:hi].copy_(self.publish[pos:pos + hi - lo])
