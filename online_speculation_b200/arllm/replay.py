@@ -261,18 +261,41 @@ def mixture_logprobabilities(registry: BehaviorRegistry, key: ReplayKey, behavio
     return tuple(np.logaddexp.reduce(table + weights, axis=0).tolist())
 
 
+def declared_logprob_tolerance(backend) -> tuple[float, float] | None:
+    """(absolute, per-token) difference a backend declares between the log-probabilities it
+    returns when sampling and when re-scoring the same tokens (its ``logprob_tolerance``),
+    looked up through wrapper backends; None when no backend in the chain declares one."""
+    for _ in range(8):
+        if backend is None:
+            return None
+        tol = getattr(backend, "logprob_tolerance", None)
+        if tol is not None:
+            return float(tol[0]), float(tol[1])
+        backend = getattr(backend, "_backend", None) or getattr(backend, "backend", None)
+    return None
+
+
 def validate_record_probabilities(records: Sequence[ReplayRecord], registry: BehaviorRegistry, *,
                                   absolute_tolerance: float = 1e-5, per_token_tolerance: float = 2e-4) -> None:
-    """Re-score stored completions; a stored behaviour probability that is not reproduced is an error."""
+    """Re-score stored completions; a stored behaviour probability that is not reproduced is an error.
+
+    A backend whose sampling and scoring passes differ numerically (bf16 activations through
+    kernels of different shapes) declares that difference; the larger tolerance applies.
+    """
     if min(absolute_tolerance, per_token_tolerance) < 0:
         raise ValueError("tolerances cannot be negative")
     groups: dict[tuple, list[ReplayRecord]] = {}
     for record in records:
         groups.setdefault((record.key, record.behavior_id), []).append(record)
     for (key, behavior), group in groups.items():
-        fresh = np.asarray(score_continuations(registry.get(behavior), key, [r.completion for r in group]))
+        policy = registry.get(behavior)
+        fresh = np.asarray(score_continuations(policy, key, [r.completion for r in group]))
         stored = np.asarray([r.behavior_logprob for r in group])
-        allowed = absolute_tolerance + per_token_tolerance * np.asarray([len(r.completion) for r in group])
+        a_tol, t_tol = absolute_tolerance, per_token_tolerance
+        declared = declared_logprob_tolerance(policy.backend)
+        if declared is not None:
+            a_tol, t_tol = max(a_tol, declared[0]), max(t_tol, declared[1])
+        allowed = a_tol + t_tol * np.asarray([len(r.completion) for r in group])
         bad = np.flatnonzero(np.abs(stored - fresh) > allowed)
         if bad.size:
             r = group[int(bad[0])]
@@ -351,4 +374,4 @@ def sample_replay_records_brokered(policy: BehaviorPolicy, work: Sequence[Replay
 __all__ = ["BehaviorPolicy", "BehaviorRegistry", "BrokeredReplayResult", "BrokeredReplayState", "FrozenReplayClaim",
            "InMemoryReplayStore", "ReplayKey", "ReplayRecord", "ReplaySampleRequest", "mixture_logprobabilities",
            "sample_replay_record", "sample_replay_records", "sample_replay_records_brokered", "score_continuations",
-           "validate_record_probabilities"]
+           "declared_logprob_tolerance", "validate_record_probabilities"]

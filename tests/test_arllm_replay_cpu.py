@@ -109,3 +109,18 @@ def test_streaming_rewards_match_direct_evaluation():
     with StreamingRewardEvaluator(workers=2) as ev:
         samples, rewards, snap = ev.sample_and_score(b, reqs, [((1,), ())] * 4, reward)
     assert rewards == tuple(reward((1,), s.token_ids) for s in samples) and snap.submitted_rewards == 4
+
+
+def test_declared_logprob_tolerance_is_found_through_wrappers():
+    from online_speculation_b200.arllm.backends.batching import ContinuousBatchingBackend
+    from online_speculation_b200.arllm.backends.cache import ScoreCachingBackend
+    from online_speculation_b200.arllm.replay import declared_logprob_tolerance
+
+    inner = _tab(1)
+    assert declared_logprob_tolerance(inner) is None
+    inner.logprob_tolerance = (1e-3, 2e-2)
+    wrapped = ScoreCachingBackend(ContinuousBatchingBackend(inner))
+    try:
+        assert declared_logprob_tolerance(wrapped) == (1e-3, 2e-2)
+    finally:
+        wrapped._backend.close()
