@@ -9,9 +9,9 @@ Two sections over the same prompts, seeds, lengths and candidate counts:
   candidate reuses up to ``max_history`` of them next to its fresh rollouts);
 * ``dynamic_is`` -- defensive-mixture candidates with a variance-cost rollout budget:
   ``base_candidate_fixed`` (base candidates only, constant design statistics),
-  ``replay_aware_fixed`` (an auxiliary proposal mixed into the candidates, reserve history,
-  constant statistics) and ``replay_aware_optimal`` (the same with the empirical
-  variance-cost design statistics).
+  ``replay_aware_fixed`` (an auxiliary proposal mixed into the candidates and a store
+  prepared with history rollouts of the decision's candidates, constant statistics) and
+  ``replay_aware_optimal`` (the same with the empirical variance-cost design statistics).
 
 Every arm reports device and wall seconds, generated tokens per second, the rollouts it
 drew fresh against those it reused from the store, the candidates' mean effective sample
@@ -132,30 +132,70 @@ class _Result:
 
 
 def dynamic_is_arms(backend, *, prompts: Sequence[tuple], length: int, block: int, candidates: int, seed: int,
-                    reward: Callable, history: int = 4, budget: float = 16.0,
-                    auxiliary_temperature: float = 1.5) -> list[dict]:
-    from ..experimental.arllm.dynamic_is import (CandidateProposal, constant_design_statistics,
-                                                 empirical_design_statistics, run_dynamic_is)
+                    reward: Callable, history: int = 4, budget: float = 16.0, auxiliary_temperature: float = 1.5,
+                    history_temperature: float = 1.3) -> list[dict]:
+    """Dynamic IS arms.  The replay-aware arms prepare the store before every decision: the
+    decision's candidate draws (the step's own seed stream, so the step redraws the same
+    blocks) get ``history`` rollouts each from the history policy -- the cache build, timed
+    apart -- which the variance-cost allocation may spend instead of fresh rollouts."""
+    from ..arllm.replay import ReplayKey, ReplaySampleRequest, sample_replay_records
+    from ..experimental.arllm.dynamic_is import (CandidateProposal, _draw_candidates, constant_design_statistics,
+                                                 dynamic_is_step, empirical_design_statistics)
 
     out = []
+    sampling = SamplingConfig()
     hot = CandidateProposal.for_backend(backend, SamplingConfig(temperature=auxiliary_temperature), label="hot")
+    hist_policy = BehaviorPolicy.for_backend(backend, SamplingConfig(temperature=history_temperature),
+                                             label="history")
     for name in ("base_candidate_fixed", "replay_aware_fixed", "replay_aware_optimal"):
         aware = name != "base_candidate_fixed"
         cfg = DynamicISConfig(candidate_count=candidates, block_size=block, total_length=length, reward_temperature=0.5,
-                              max_history_per_candidate=history if aware else 0, reserve_rollouts=history if aware else 0,
-                              rollout_budget=budget, auxiliary_mixture=0.25 if aware else 0.0)
+                              max_history_per_candidate=history if aware else 0, rollout_budget=budget,
+                              auxiliary_mixture=0.25 if aware else 0.0)
         stats = empirical_design_statistics if name == "replay_aware_optimal" else constant_design_statistics
         snap = getattr(backend, "snapshot", lambda: None)
+        build = {"wall_seconds": 0.0, "device_seconds": 0.0, "records": 0}
+
+        def one(i, prompt):
+            seeds = SeedStream(SeedStream(seed).derive("dynamic", i))
+            registry, store = BehaviorRegistry([hist_policy]), InMemoryReplayStore()
+            generated: tuple = ()
+            steps = []
+            while len(generated) < length:
+                k = len(steps)
+                b = min(block, length - len(generated))
+                rollout = length - len(generated) - b
+                if aware and rollout > 0:
+                    def prepare():
+                        draws = _draw_candidates(base_backend=backend, base_sampling=sampling,
+                                                 prefix=tuple(prompt) + generated, count=candidates, block=b,
+                                                 mixture=cfg.auxiliary_mixture, source=hot, seeds=seeds, step=k)
+                        keys = dict.fromkeys(ReplayKey(tuple(prompt), generated, d.token_ids, "reward")
+                                             for d in draws)
+                        reqs = [ReplaySampleRequest(key, rollout, seeds.derive("history", k, j, h),
+                                                    f"history:{i}:{k}:{j}:{h}")
+                                for j, key in enumerate(keys) for h in range(history)]
+                        return sample_replay_records(hist_policy, reqs, reward)
+
+                    recs, t = measure(prepare)
+                    for r in recs:
+                        store.add_evaluation(r)
+                    build["wall_seconds"] += t["wall_seconds"]
+                    build["device_seconds"] += t["device_seconds"]
+                    build["records"] += len(recs)
+                st = dynamic_is_step(base_backend=backend, registry=registry, store=store, prompt=tuple(prompt),
+                                     generated_prefix=generated, config=cfg, base_sampling=sampling, reward=reward,
+                                     reward_version="reward", seeds=seeds, step_index=k,
+                                     auxiliary_proposal=hot if aware else None, statistics_provider=stats)
+                steps.append(st)
+                generated += tuple(st.selected.token_ids)
+            return _Result(generated, tuple(steps), 0)
+
         before = snap()
-
-        def run():
-            return [run_dynamic_is(backend, BehaviorRegistry(), InMemoryReplayStore(), p, cfg, reward, "reward",
-                                   SeedStream(SeedStream(seed).derive("dynamic", i)),
-                                   auxiliary_proposal=hot if aware else None, statistics_provider=stats)
-                    for i, p in enumerate(prompts)]
-
-        results, t = measure(run)
+        results, t = measure(lambda: [one(i, p) for i, p in enumerate(prompts)])
+        t = {k: t[k] - build[k] for k in t}
         rec = _summary(name, results, t, reward, prompts, before, snap())
+        rec["cache_build"] = build
         draws = [c.draw for r in results for st in r.steps for c in st.candidates]
         rec["online"]["auxiliary_candidates"] = sum(d.source == "auxiliary" for d in draws)
         out.append(rec)

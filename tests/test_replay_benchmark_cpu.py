@@ -25,4 +25,7 @@ def test_replay_and_dynamic_is_arms():
     assert arms["base_candidate_fixed"]["auxiliary_candidates"] == 0
     assert arms["base_candidate_fixed"]["history_rollouts_reused"] == 0
     assert all(a["output_tokens"] == 16 and a["mean_candidate_ess"] > 0 for a in arms.values())
+    # the prepared store is spent: the allocation reuses history in the replay-aware arms
+    assert arms["replay_aware_fixed"]["history_rollouts_reused"] > 0
+    assert rep["dynamic_is"][1]["cache_build"]["records"] > 0
     assert 0.0 <= arms["replay_aware_optimal"]["mean_output_reward"] <= 1.0
