@@ -618,7 +618,8 @@ class GRPOTrainer:
 
             workspace.check_status(self.device)     # a cross-rank wait that ran out raises here
         t2 = time.perf_counter()
-        out.update(tokens=int(ids.numel()), completion_tokens=int(mask.sum()), rollout_s=t1 - t0, train_s=t2 - t1,
+        out.update(tokens=int(ids.numel()), completions=int(ids.shape[0]), completion_tokens=int(mask.sum()),
+                   rollout_s=t1 - t0, train_s=t2 - t1,
                    grad_norm=float(self.sq_norm.sqrt()), step=self.step_count)
         self.stats = out
         return out

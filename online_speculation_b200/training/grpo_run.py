@@ -195,7 +195,16 @@ class GRPORun:
             raise
         if latest_checkpoint(self.output) != self.output / f"checkpoint-{tr.step_count}":
             self.save()
-        self._set_status("completed", train_seconds=time.perf_counter() - started, final_step=tr.step_count)
+        extra = {}
+        if self.log and all("tokens" in r and "completions" in r for r in self.log):
+            from ..shared.compute import estimate_grpo_compute_from_steps
+
+            n = tr.params.trainable
+            extra["compute"] = estimate_grpo_compute_from_steps(
+                self.log, total_parameters=n, trainable_parameters=n, reference_scoring=tr.config.beta > 0,
+                world=tr.world).as_dict()
+        self._set_status("completed", train_seconds=time.perf_counter() - started, final_step=tr.step_count,
+                         **extra)
         return self.log
 
     def close(self) -> None:

@@ -251,3 +251,28 @@ def test_distribution_audit_power_target_small():
     out = audit_power_mh(400, 1)
     assert out["passed"], out
     assert 0.0 <= out["tv"] < 0.2
+
+
+def test_grpo_compute_estimate():
+    from online_speculation_b200.shared.compute import (ADAMW_FLOPS_PER_PARAMETER, estimate_grpo_compute,
+                                                        estimate_grpo_compute_from_steps)
+
+    e = estimate_grpo_compute(model_sequence_tokens=1000, generated_completions=10, total_parameters=100,
+                              trainable_parameters=100, optimizer_steps=2, reference_scoring=True)
+    assert e.rollout_generation_forward_token_slots == 990
+    assert e.reference_scoring_forward_token_slots == 1000
+    assert e.policy_forward_backward_equivalent_token_slots == 3000      # forward + two gradient passes
+    assert e.total_forward_equivalent_token_slots == 4990
+    assert e.estimated_dense_model_flops == 2 * 100 * 4990
+    assert e.estimated_optimizer_flops == ADAMW_FLOPS_PER_PARAMETER * 100 * 2
+    lora = estimate_grpo_compute(model_sequence_tokens=1000, generated_completions=10, total_parameters=100,
+                                 trainable_parameters=1, optimizer_steps=1, reference_scoring=False, recompute=True)
+    assert lora.policy_forward_backward_equivalent_token_slots == 3000 + 10 and lora.reference_scoring_forward_token_slots == 0
+    steps = [{"tokens": 500, "completions": 5}, {"tokens": 500, "completions": 5}]
+    two = estimate_grpo_compute_from_steps(steps, total_parameters=100, trainable_parameters=100,
+                                           reference_scoring=True, world=2)
+    assert two.trainer_observed_prompt_plus_completion_tokens == 2000 and two.optimizer_steps == 2
+    assert set(two.as_dict()) >= {"estimated_total_petaflops", "definition", "exclusions"}
+    with pytest.raises(ValueError):
+        estimate_grpo_compute(model_sequence_tokens=5, generated_completions=6, total_parameters=1,
+                              trainable_parameters=1, optimizer_steps=1, reference_scoring=True)
