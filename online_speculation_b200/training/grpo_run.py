@@ -78,13 +78,14 @@ class GRPORun:
 
     def __init__(self, output, model: DecoderConfig, config: GRPOConfig, *, max_steps: int, save_steps: int = 25,
                  logging_steps: int = 1, resume: str = "auto", group=None, device=None, seed: int = 0,
-                 trainer_kwargs: dict | None = None, data=None):
+                 trainer_kwargs: dict | None = None, data=None, power_monitor: bool = False):
         if max_steps < 1 or save_steps < 1 or logging_steps < 1:
             raise ValueError("max_steps, save_steps and logging_steps are positive")
         self.output = Path(output)
         self.max_steps, self.save_steps, self.logging_steps = max_steps, save_steps, logging_steps
         self.group = group
         self.data = data
+        self.power_monitor = power_monitor       # nvidia-smi power / utilisation summary in the manifest
         initial = random_state_dict(model, seed=seed, device="cpu")
         self.effective = {
             "model": dataclasses.asdict(model),
@@ -176,6 +177,11 @@ class GRPORun:
         tr = self.trainer
         self._set_status("training", resume_from_checkpoint=self.resumed_from)
         started = time.perf_counter()
+        monitor = None
+        if self.power_monitor and tr.device.type == "cuda":
+            from ..utils.power import PowerMonitor
+
+            monitor = PowerMonitor(tr.device.index if tr.device.index is not None else 0).start()
         try:
             while tr.step_count < self.max_steps:
                 if self.data is None:
@@ -191,11 +197,13 @@ class GRPORun:
                 if tr.step_count % self.save_steps == 0:
                     self.save()
         except BaseException:
-            self._set_status("interrupted", elapsed_before_interruption_seconds=time.perf_counter() - started)
+            extra = {"power": monitor.stop()} if monitor is not None else {}
+            self._set_status("interrupted", elapsed_before_interruption_seconds=time.perf_counter() - started,
+                             **extra)
             raise
         if latest_checkpoint(self.output) != self.output / f"checkpoint-{tr.step_count}":
             self.save()
-        extra = {}
+        extra = {"power": monitor.stop()} if monitor is not None else {}
         if self.log and all("tokens" in r and "completions" in r for r in self.log):
             from ..shared.compute import estimate_grpo_compute_from_steps
 
@@ -227,6 +235,7 @@ def main(argv=None) -> None:
     p.add_argument("--completion-length", type=int, default=512)
     p.add_argument("--learning-rate", type=float, default=1e-6)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--power-monitor", action="store_true", help="record nvidia-smi power / utilisation samples")
     args = p.parse_args(argv)
     group = None
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
@@ -241,7 +250,7 @@ def main(argv=None) -> None:
                         prompt_length=args.prompt_length, completion_length=args.completion_length,
                         learning_rate=args.learning_rate, seed=args.seed)
     run = GRPORun(args.output, PRESETS[args.model], config, max_steps=args.max_steps, save_steps=args.save_steps,
-                  resume=args.resume, group=group, seed=args.seed)
+                  resume=args.resume, group=group, seed=args.seed, power_monitor=args.power_monitor)
     try:
         run.train()
     finally:
