@@ -58,6 +58,7 @@ from ..arllm.config import SamplingConfig
 from ..arllm.types import GenerationRequest, ScoreRequest, SequenceSample
 from ..ops import kernels as K
 from ..shared.rng import SeedStream
+from ..utils.tracing import trace_range
 from .kv_cache import PAGE, KVCache
 from .runner import ModelRunner, StepMeta, build_meta
 
@@ -433,7 +434,7 @@ class EngineBackend:
 
     # -------------------------------------------------------------- sample --
     def sample_batch(self, requests: Sequence[GenerationRequest]) -> list[SequenceSample]:
-        with self._lock:
+        with self._lock, trace_range("engine.sample_batch"):
             out: list[SequenceSample | None] = [None] * len(requests)
             pending = list(enumerate(requests))
             while pending:
@@ -685,7 +686,7 @@ class EngineBackend:
     # --------------------------------------------------------------- score --
     def score_batch(self, requests: Sequence[ScoreRequest]) -> list[tuple[float, ...]]:
         """Per-token log-probabilities of every continuation (policy ``sampling`` or T = 1)."""
-        with self._lock:
+        with self._lock, trace_range("engine.score_batch"):
             flat = []
             for req in requests:
                 for cont in req.continuations:

@@ -41,6 +41,7 @@ from ..shared.rng import SeedStream
 from .draft import DraftHead, FeedbackRound, SuffixLearner
 from .kv_cache import KVCache
 from .runner import ModelRunner, StepMeta
+from ..utils.tracing import trace_range
 
 BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
 
@@ -605,7 +606,8 @@ class MHEngine:
         seqs = [j.seq for j in jobs]
         nj = len(jobs)
         n = np.fromiter((j.n for j in jobs), dtype=np.int64, count=nj)
-        res, W, runs = self._run_spec(jobs, seqs, n) if speculate else self._run_plain(jobs, seqs, n)
+        with trace_range("mh.spec_round" if speculate else "mh.plain_round"):
+            res, W, runs = self._run_spec(jobs, seqs, n) if speculate else self._run_plain(jobs, seqs, n)
         counts = res[:nj, 0].astype(np.int64)
         emitted = res[:nj, 2:2 + W].astype(np.int64)
         logq = res[:nj, 2 + W:2 + 2 * W]

@@ -606,12 +606,16 @@ class GRPOTrainer:
             self.dp.all_gather(self.params.flat, blo, bhi, self.publish[pos:pos + hi - lo])
 
     def step(self) -> dict:
+        from ..utils.tracing import trace_range
+
         t0 = time.perf_counter()
-        ids, mask, rewards, _ = self.rollout()
+        with trace_range("grpo.rollout"):
+            ids, mask, rewards, _ = self.rollout()
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
         t1 = time.perf_counter()
-        out = self.train_on(ids, mask, rewards)
+        with trace_range("grpo.train"):
+            out = self.train_on(ids, mask, rewards)
         if self.device.type == "cuda":
             torch.cuda.synchronize(self.device)
             from ..ops import workspace

@@ -32,3 +32,23 @@ def test_missing_tool_does_not_raise():
     assert out["samples"] == 0 and out["mean_power_watts"] is None and out["monitor_error"]
     with pytest.raises(ValueError):
         PowerMonitor(interval_seconds=0)
+
+
+def test_trace_ranges_nest_and_switch_off():
+    import torch
+
+    from online_speculation_b200.utils.tracing import set_tracing, trace_range, tracing_enabled
+
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CPU]) as prof:
+        with trace_range("outer.phase"):
+            with trace_range("inner.phase"):
+                torch.ones(4).sum()
+    names = {e.name for e in prof.events()}
+    assert {"outer.phase", "inner.phase"} <= names
+    set_tracing(False)
+    try:
+        assert not tracing_enabled()
+        with trace_range("ignored"):
+            pass
+    finally:
+        set_tracing(True)
