@@ -38,10 +38,10 @@ import torch.distributed as dist
 from ..ops import kernels as K
 from ..shared.mh import decide_metropolis_hastings
 from ..shared.rng import SeedStream
+from ..utils.tracing import trace_range
 from .draft import DraftHead, FeedbackRound, SuffixLearner
 from .kv_cache import KVCache
 from .runner import ModelRunner, StepMeta
-from ..utils.tracing import trace_range
 
 BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
 
