@@ -2,13 +2,16 @@
 
 Problem (per candidate i with outer probability ratio r_i): estimate a mean
 from n^h_i replayed history rollouts (std s^h_i, cost c^h_i each) and n^f_i
-fresh rollouts (std s^f_i, cost c^f_i), minimising sum_i r_i^2 (s^2 / n) over
-all sources subject to sum c n <= budget, n^h_i <= cap_i, per-group history
-caps and a minimum number of fresh rollouts per candidate.  The Lagrangian
-solution is n proportional to r s / sqrt(c); caps are handled by water
-filling (a source whose share would exceed its cap is fixed at the cap and
-the rest of the budget is re-split among the others), then counts are
-rounded down and the leftover budget is given out by largest fractional
+fresh rollouts (std s^f_i, cost c^f_i), minimising sum over all sources of
+a / n with a = (r s)^2, subject to sum c n <= budget, n^h_i <= cap_i, per-group
+history caps and a minimum number of fresh rollouts per candidate.  The problem
+is convex and separable, so its optimum is the KKT point
+n = min(cap, sqrt(a / (lambda c + mu_g))): lambda prices the budget, mu_g >= 0
+the history group g (zero unless the group is full), fresh sources have no cap.
+Both multipliers are found by bisection -- each group's mu for a given lambda,
+lambda for the budget -- so the continuous solution is exact to rounding.
+Without any cap binding this is n proportional to r s / sqrt(c).  Counts are
+then rounded down and the leftover budget is given out by largest fractional
 remainder while every hard constraint still holds.
 
 Reference behaviour: src/inference_scaling/shared/budget.py:46-353.
@@ -63,21 +66,46 @@ def allocate_fresh_rollout_budget(*, outer_ratios: Sequence[float], standard_dev
         rollout_budget=rollout_budget, minimum_fresh=minimum_fresh)
 
 
-def _fill_capped(total: float, weights: np.ndarray, caps: np.ndarray) -> np.ndarray:
-    """Split ``total`` proportionally to ``weights`` without exceeding ``caps`` (water filling)."""
-    out = np.zeros_like(weights)
-    free = weights > 0
-    left = min(float(total), float(caps[free].sum()) if free.any() else 0.0)
-    while left > 1e-12 and free.any():
-        share = left * np.where(free, weights, 0.0) / weights[free].sum()
-        over = free & (share >= caps - out - 1e-12)
-        if not over.any():
-            out += share
+def _bisect(fn, target: float, lo: float, hi: float, iterations: int = 200) -> float:
+    """The smallest argument (to rounding) where a non-increasing ``fn`` is at most ``target``
+    (geometric bisection; ``hi`` grows until it brackets the crossing)."""
+    if fn(lo) <= target:
+        return lo
+    for _ in range(400):
+        if fn(hi) <= target:
             break
-        add = np.where(over, np.maximum(caps - out, 0.0), 0.0)
-        out += add
-        left -= float(add.sum())
-        free &= ~over
+        hi *= 4.0
+    for _ in range(iterations):
+        mid = sqrt(lo * hi)
+        if fn(mid) > target:
+            lo = mid
+        else:
+            hi = mid
+        if hi <= lo * (1 + 1e-15):
+            break
+    return hi
+
+
+def _history_at(lam: float, a: np.ndarray, c: np.ndarray, cap: np.ndarray, groups: list, room: Mapping) -> np.ndarray:
+    """History counts at budget price ``lam``: per group the smallest mu >= 0 that keeps it within its room."""
+    out = np.zeros_like(a)
+    for g in dict.fromkeys(groups):
+        idx = np.asarray([i for i, gi in enumerate(groups) if gi == g and a[i] > 0 and cap[i] > 0], dtype=np.int64)
+        if idx.size == 0:
+            continue
+
+        def counts(mu, idx=idx):
+            return np.minimum(cap[idx], np.sqrt(a[idx] / (lam * c[idx] + mu)))
+
+        total = float(room[g])
+        if counts(0.0).sum() <= total:
+            out[idx] = counts(0.0)
+        elif total <= 0:
+            out[idx] = 0.0
+        else:
+            hi = max(1.0, float((a[idx] / np.maximum(total / idx.size, 1e-300) ** 2).max()))
+            mu = _bisect(lambda m: float(counts(m).sum()), total, 1e-300, hi * 4)
+            out[idx] = counts(mu)
     return out
 
 
@@ -111,56 +139,46 @@ def allocate_variance_cost_budget(*, outer_ratios: Sequence[float], statistics: 
         raise ValueError("history group capacities must be non-negative")
     ch = np.array([s.history_cost for s in statistics])
     cf = np.array([s.fresh_cost for s in statistics])
-    wh = np.array([ri * s.history_std / sqrt(s.history_cost) for ri, s in zip(r, statistics)])
-    wf = np.array([ri * s.fresh_std / sqrt(s.fresh_cost) for ri, s in zip(r, statistics)])
-    wh[hcap == 0] = 0.0
     budget = rollout_budget - float(minimum @ cf)
     if budget < -1e-9:
         raise ValueError("rollout budget cannot cover the required fresh sample for every candidate")
+    groups = list(history_groups)
+    ah = np.where(hcap > 0, (r * np.array([s.history_std for s in statistics])) ** 2, 0.0)
+    af = (r * np.array([s.fresh_std for s in statistics])) ** 2
+    room = {g: float(c) for g, c in group_capacities.items()}
     hist = np.zeros(n)
     fresh = np.zeros(n)
-    h_open = wh > 0
-    groups = list(history_groups)
-    g_left = {g: float(c) for g, c in group_capacities.items()}
-    while budget > 1e-12:
-        f_w = wf.copy()
-        f_open = f_w > 0
-        denom = float((wh * ch)[h_open].sum() + (f_w * cf)[f_open].sum())
-        if denom <= 0:
+    if budget > 1e-12:
+        if (af > 0).any():
+            def spend(lam):
+                h = _history_at(lam, ah, ch, hcap, groups, room)
+                f = np.sqrt(af / (lam * cf))
+                return float(h @ ch + f @ cf)
+
+            # a price high enough that almost nothing is bought, and one low enough to overspend
+            hi_p = max(1.0, float(((ah + af) / np.minimum(ch, cf) / (budget / n) ** 2).max()) * 4)
+            lam = _bisect(spend, budget, 1e-300, hi_p)
+            hist = _history_at(lam, ah, ch, hcap, groups, room)
+            fresh = np.sqrt(af / (lam * cf))
+            scale = budget / max(float(hist @ ch + fresh @ cf), 1e-300)
+            if scale < 1:           # the bisection lands on the feasible side; absorb its last bit
+                hist *= scale
+                fresh *= scale
+        elif (ah > 0).any():
+            # no fresh variance: history only, capped (the rest of the budget stays unspent)
+            def spend_h(lam):
+                return float(_history_at(lam, ah, ch, hcap, groups, room) @ ch)
+
+            if spend_h(1e-300) <= budget:
+                hist = _history_at(1e-300, ah, ch, hcap, groups, room)
+            else:
+                hi_p = max(1.0, float((ah / ch / (budget / n) ** 2).max()) * 4)
+                hist = _history_at(_bisect(spend_h, budget, 1e-300, hi_p), ah, ch, hcap, groups, room)
+        else:
             # no variance information: spread the remainder evenly over candidates that need fresh draws
-            f_open = minimum > 0
-            if not f_open.any():
-                break
-            f_w = 1.0 / cf
-            denom = float((f_w * cf)[f_open].sum())
-        ph = np.where(h_open, budget * wh / denom, 0.0)
-        pf = np.where(f_open, budget * f_w / denom, 0.0)
-        # a history group over its capacity: fix its members by capped proportional fill
-        bad = next((g for g in dict.fromkeys(groups)
-                    if sum(ph[i] for i in range(n) if h_open[i] and groups[i] == g) > g_left[g] + 1e-12), None)
-        if bad is not None:
-            members = [i for i in range(n) if h_open[i] and groups[i] == bad]
-            fill = _fill_capped(g_left[bad], wh[members], hcap[members] - hist[members])
-            cost = float(fill @ ch[members])
-            if cost > budget + 1e-12:
-                fill *= budget / cost
-            for i, v in zip(members, fill):
-                hist[i] += v
-                budget -= v * ch[i]
-                h_open[i] = False
-            g_left[bad] = 0.0
-            continue
-        over = next((i for i in range(n) if h_open[i] and ph[i] > hcap[i] - hist[i] + 1e-12), None)
-        if over is not None:
-            add = hcap[over] - hist[over]
-            hist[over] += add
-            budget -= add * ch[over]
-            g_left[groups[over]] = max(0.0, g_left[groups[over]] - add)
-            h_open[over] = False
-            continue
-        hist += ph
-        fresh += pf
-        budget = 0.0
+            need = minimum > 0
+            if need.any():
+                fresh = np.where(need, budget / float(cf[need].sum()), 0.0)
     cont_f = minimum + fresh
     hi = np.floor(hist + 1e-12).astype(np.int64)
     fi = minimum + np.floor(fresh + 1e-12).astype(np.int64)
