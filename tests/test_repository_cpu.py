@@ -1,5 +1,6 @@
-"""Repository hygiene: the files the documents cite exist, every profile summary carries the
-command that made it, and the driver-facing entry points keep their contracts."""
+"""Repository hygiene: the files the user documentation and the profile summaries cite exist,
+every profile summary carries the command that made it, and the driver-facing entry points keep
+their contracts."""
 
 import ast
 import glob
@@ -31,10 +32,12 @@ def _expand(path: str):
     return [q for alt in m.group(1).split(",") for q in _expand(path[:m.start()] + alt + path[m.end():])]
 
 
-@pytest.mark.parametrize("markdown", ["README.md", "DESIGN.md"])
+@pytest.mark.parametrize("markdown", ["README.md"] + sorted(os.path.relpath(p, ROOT) for p in
+                                                          glob.glob(os.path.join(ROOT, "profiles", "*.md"))))
 def test_cited_files_exist(markdown):
+    here = os.path.dirname(os.path.join(ROOT, markdown))
     missing = [q for p in _cited_files(markdown) for q in _expand(p)
-               if not any(glob.glob(os.path.join(base, q)) for base in (ROOT, PKG))]
+               if not any(glob.glob(os.path.join(base, q)) for base in (ROOT, PKG, here))]
     assert not missing, f"{markdown} cites files that do not exist: {missing}"
 
 
