@@ -200,7 +200,9 @@ def _make_draw(sample_tokens, base_scores, aux, aux_scores, used_aux: bool, mixt
                                 "auxiliary" if used_aux else "base", aux_id)
 
 
-def _draw_candidates(*, base_backend, base_sampling, prefix, count, block, mixture, source, seeds, step):
+def draw_candidates(*, base_backend, base_sampling, prefix, count, block, mixture, source, seeds, step):
+    """The candidate draws of one dynamic-IS step (the step's own seed stream): a caller that draws them
+    first -- to prepare replay history for exactly these blocks -- gets the blocks the step will draw."""
     def component(k):
         return bool(mixture > 0 and seeds.generator("dynamic_is", step, k, "component").random() < mixture)
 
@@ -273,7 +275,7 @@ def dynamic_is_step(*, base_backend: AutoregressiveBackend, registry: BehaviorRe
     if left <= 0:
         raise ValueError("generated prefix has already reached total_length")
     block = min(config.block_size, left)
-    draws = _draw_candidates(base_backend=base_backend, base_sampling=base_sampling, prefix=prompt + generated_prefix,
+    draws = draw_candidates(base_backend=base_backend, base_sampling=base_sampling, prefix=prompt + generated_prefix,
                              count=config.candidate_count, block=block, mixture=config.auxiliary_mixture,
                              source=auxiliary_proposal, seeds=seeds, step=step_index)
     base_policy = BehaviorPolicy.for_backend(base_backend, base_sampling, label="base")
@@ -389,4 +391,5 @@ def run_dynamic_is(base_backend: AutoregressiveBackend, registry: BehaviorRegist
 __all__ = ["CandidateProposal", "CandidateProposalFactory", "CandidateProposalSource", "DesignPreparation",
            "DesignStatisticsContext", "DesignStatisticsProvider", "DynamicCandidate", "DynamicCandidateDraw",
            "DynamicISResult", "DynamicISStep", "RolloutBudgetContext", "RolloutBudgetProvider",
-           "constant_design_statistics", "dynamic_is_step", "empirical_design_statistics", "run_dynamic_is"]
+           "constant_design_statistics", "draw_candidates", "dynamic_is_step", "empirical_design_statistics",
+           "run_dynamic_is"]

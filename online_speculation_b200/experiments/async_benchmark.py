@@ -38,7 +38,7 @@ import numpy as np
 from ..arllm.backends.batching import ContinuousBatchingBackend
 from ..arllm.backends.cache import ScoreCachingBackend
 from .methods import MethodSettings, run_ar_method
-from .rollout_infra import _delta, agreement, measure
+from .rollout_infra import agreement, counter_delta, measure
 
 DEFAULT_METHODS = ("best_of_n", "reward_mh", "conditional_is")
 
@@ -89,8 +89,8 @@ def run_benchmark(backend, *, prompts: Sequence[tuple], methods: Sequence[str] =
         sync_ids = {str(i): tuple(o.token_ids) for i, o in enumerate(sync_out)}
         async_ids = {str(i): tuple(o.token_ids) for i, o in enumerate(async_out)}
         report["methods"][method] = {
-            "synchronous": {"telemetry": ts, "main_model": _delta(before, mid), "output_tokens": tokens_s},
-            "asynchronous": {"telemetry": ta, "main_model": _delta(mid, after), "output_tokens": tokens_a,
+            "synchronous": {"telemetry": ts, "main_model": counter_delta(before, mid), "output_tokens": tokens_s},
+            "asynchronous": {"telemetry": ta, "main_model": counter_delta(mid, after), "output_tokens": tokens_a,
                              "batching": batching, "agreement_with_synchronous": agreement(async_ids, sync_ids)},
             "speedup": ts["device_seconds"] / ta["device_seconds"] if ta["device_seconds"] else None,
         }

@@ -41,7 +41,7 @@ from ..dllm.config import DiffusionISConfig, DiffusionMHConfig, DiffusionSamplin
 from ..dllm.types import DiffusionGenerationRequest
 from ..shared.config import SMCForestConfig
 from ..shared.rng import SeedStream
-from .rollout_infra import _delta, measure
+from .rollout_infra import counter_delta, measure
 
 FAMILIES = ("block_continuous_batching", "resume_committed_blocks", "streaming_reward", "delayed_acceptance_mh",
             "progressive_is", "block_smc_rollout_forest")
@@ -51,7 +51,7 @@ def _arm(backend, call: Callable[[], tuple[Sequence[int], dict]]) -> dict:
     snap = getattr(backend, "snapshot", lambda: None)
     before = snap()
     (tokens, info), t = measure(call)
-    return {"telemetry": t, "tokens": len(tokens), "backend": _delta(before, snap()), **info}
+    return {"telemetry": t, "tokens": len(tokens), "backend": counter_delta(before, snap()), **info}
 
 
 def run_families(backend, *, prompt: tuple, sampling: DiffusionSamplingConfig, block: int, generation: int,

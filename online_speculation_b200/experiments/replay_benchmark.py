@@ -42,7 +42,7 @@ import numpy as np
 from ..arllm.config import BaseReplayConfig, DynamicISConfig, SamplingConfig
 from ..arllm.replay import BehaviorPolicy, BehaviorRegistry, InMemoryReplayStore
 from ..shared.rng import SeedStream
-from .rollout_infra import _delta, measure
+from .rollout_infra import counter_delta, measure
 
 
 def _estimates(steps) -> list:
@@ -54,7 +54,7 @@ def _summary(name: str, results, t: dict, reward: Callable, prompts, before, aft
     tokens = sum(len(r.token_ids) for r in results)
     ess = [float(e.history_ess) + float(e.fresh_ess) for e in est]
     return {"name": name, "online": {
-        "telemetry": t, "main_model": _delta(before, after), "output_tokens": tokens,
+        "telemetry": t, "main_model": counter_delta(before, after), "output_tokens": tokens,
         "output_tokens_per_second": tokens / t["device_seconds"] if t["device_seconds"] else 0.0,
         "decisions": sum(len(r.steps) for r in results),
         "history_rollouts_reused": int(sum(e.history_count for e in est)),
@@ -139,7 +139,7 @@ def dynamic_is_arms(backend, *, prompts: Sequence[tuple], length: int, block: in
     blocks) get ``history`` rollouts each from the history policy -- the cache build, timed
     apart -- which the variance-cost allocation may spend instead of fresh rollouts."""
     from ..arllm.replay import ReplayKey, ReplaySampleRequest, sample_replay_records
-    from ..experimental.arllm.dynamic_is import (CandidateProposal, _draw_candidates, constant_design_statistics,
+    from ..experimental.arllm.dynamic_is import (CandidateProposal, constant_design_statistics, draw_candidates,
                                                  dynamic_is_step, empirical_design_statistics)
 
     out = []
@@ -167,7 +167,7 @@ def dynamic_is_arms(backend, *, prompts: Sequence[tuple], length: int, block: in
                 rollout = length - len(generated) - b
                 if aware and rollout > 0:
                     def prepare():
-                        draws = _draw_candidates(base_backend=backend, base_sampling=sampling,
+                        draws = draw_candidates(base_backend=backend, base_sampling=sampling,
                                                  prefix=tuple(prompt) + generated, count=candidates, block=b,
                                                  mixture=cfg.auxiliary_mixture, source=hot, seeds=seeds, step=k)
                         keys = dict.fromkeys(ReplayKey(tuple(prompt), generated, d.token_ids, "reward")

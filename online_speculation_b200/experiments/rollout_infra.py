@@ -62,7 +62,8 @@ def _numbers(snapshot: Any) -> dict[str, float]:
     return {k: v for k, v in dict(snapshot).items() if isinstance(v, (int, float)) and not isinstance(v, bool)}
 
 
-def _delta(before: Any, after: Any) -> dict[str, float]:
+def counter_delta(before: Any, after: Any) -> dict[str, float]:
+    """Numeric counters of ``after`` minus those of ``before`` (snapshots as dataclasses or dicts)."""
     a, b = _numbers(before), _numbers(after)
     return {k: b[k] - a.get(k, 0) for k in b}
 
@@ -129,10 +130,10 @@ def decode_arm(backend, *, name: str, speculative: bool, history: Sequence[Seque
     tokens = sum(len(s.token_ids) for s in samples)
     record = {
         "name": name,
-        "cache_build": {"telemetry": hist_t, "main_model": _delta(before, mid), "sequences": len(hist),
+        "cache_build": {"telemetry": hist_t, "main_model": counter_delta(before, mid), "sequences": len(hist),
                         "tokens": sum(len(s.token_ids) for s in hist)},
-        "online": {"telemetry": t, "main_model": _delta(mid, after),
-                   "draft_cache": _delta(tree0, _tree_snapshot(backend)), "sequences": len(samples),
+        "online": {"telemetry": t, "main_model": counter_delta(mid, after),
+                   "draft_cache": counter_delta(tree0, _tree_snapshot(backend)), "sequences": len(samples),
                    "output_tokens": tokens, "output_tokens_per_second": tokens / t["device_seconds"]},
     }
     return record, {s.request_id: tuple(s.token_ids) for s in samples}
@@ -187,8 +188,8 @@ def algorithm_arm(backend, *, name: str, prompts: Sequence[tuple], length: int, 
     tokens = sum(len(o) for o in outs)
     return {"name": name, "cache_build": {"telemetry": hist_t, "sequences": len(hist),
                                           "tokens": sum(len(s.token_ids) for s in hist)},
-            "online": {"telemetry": t, "main_model": _delta(before, getattr(backend, "snapshot", lambda: None)()),
-                                     "draft_cache": _delta(tree0, _tree_snapshot(backend)),
+            "online": {"telemetry": t, "main_model": counter_delta(before, getattr(backend, "snapshot", lambda: None)()),
+                                     "draft_cache": counter_delta(tree0, _tree_snapshot(backend)),
                                      "problems": len(prompts), "output_tokens": tokens,
                                      "output_tokens_per_second": tokens / t["device_seconds"],
                                      "diagnostics": diagnostics}}
