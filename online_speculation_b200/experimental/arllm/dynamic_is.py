@@ -20,7 +20,7 @@ Reference behaviour: src/inference_scaling/experimental/arllm/dynamic_is.py:55-7
 from __future__ import annotations
 
 from collections.abc import Callable, Mapping, Sequence
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 from math import exp, isfinite, log
 
 import numpy as np
@@ -388,8 +388,69 @@ def run_dynamic_is(base_backend: AutoregressiveBackend, registry: BehaviorRegist
     return DynamicISResult(prompt, tuple(gen), tuple(steps), written)
 
 
+DYNAMIC_ARMS = ("base_candidate_fixed", "replay_aware_fixed", "replay_aware_optimal")
+
+
+def run_dynamic_is_arm(backend: AutoregressiveBackend, prompt: TokenSequence, *, arm: str, candidate_count: int,
+                       block_size: int, total_length: int, reward: TokenReward, seeds: SeedStream,
+                       reward_temperature: float = 0.5, history: int = 4, rollout_budget: float = 16.0,
+                       auxiliary_mixture: float = 0.25, auxiliary_temperature: float = 1.5,
+                       history_temperature: float = 1.3, base_sampling: SamplingConfig | None = None,
+                       prepare: Callable[[Callable[[], tuple]], tuple] | None = None) -> DynamicISResult:
+    """One prompt under one of the dynamic-IS benchmark arms.
+
+    ``base_candidate_fixed``: base candidates only, constant design statistics.
+    ``replay_aware_fixed``: a hotter auxiliary policy of the same backend mixed into the
+    candidates, and before every decision ``history`` rollouts per candidate block from a
+    history policy written into the store (the decision's own draws, so the step redraws
+    the same blocks), constant statistics.  ``replay_aware_optimal``: the same with the
+    empirical variance-cost statistics.  ``prepare`` receives each history preparation as
+    a zero-argument callable and returns its records (a caller times it this way).
+    """
+    if arm not in DYNAMIC_ARMS:
+        raise ValueError(f"unknown dynamic-IS arm {arm!r}; choose from {DYNAMIC_ARMS}")
+    sampling = base_sampling or SamplingConfig()
+    aware = arm != "base_candidate_fixed"
+    cfg = DynamicISConfig(candidate_count=candidate_count, block_size=block_size, total_length=total_length,
+                          reward_temperature=reward_temperature, max_history_per_candidate=history if aware else 0,
+                          rollout_budget=rollout_budget, auxiliary_mixture=auxiliary_mixture if aware else 0.0)
+    stats = empirical_design_statistics if arm == "replay_aware_optimal" else constant_design_statistics
+    hot = CandidateProposal.for_backend(backend, replace(sampling, temperature=auxiliary_temperature), label="hot")
+    hist_policy = BehaviorPolicy.for_backend(backend, replace(sampling, temperature=history_temperature),
+                                             label="history")
+    registry, store = BehaviorRegistry([hist_policy]), InMemoryReplayStore()
+    prompt = tuple(prompt)
+    generated: tuple = ()
+    steps: list[DynamicISStep] = []
+    while len(generated) < total_length:
+        k = len(steps)
+        b = min(block_size, total_length - len(generated))
+        rollout = total_length - len(generated) - b
+        if aware and rollout > 0:
+            def make(k=k, b=b, rollout=rollout, generated=generated):
+                draws = draw_candidates(base_backend=backend, base_sampling=sampling, prefix=prompt + generated,
+                                        count=candidate_count, block=b, mixture=cfg.auxiliary_mixture, source=hot,
+                                        seeds=seeds, step=k)
+                keys = dict.fromkeys(ReplayKey(prompt, generated, d.token_ids, "reward") for d in draws)
+                reqs = [ReplaySampleRequest(key, rollout, seeds.derive("history", k, j, h), f"history:{k}:{j}:{h}")
+                        for j, key in enumerate(keys) for h in range(history)]
+                return sample_replay_records(hist_policy, reqs, reward)
+
+            for r in (prepare(make) if prepare is not None else make()):
+                store.add_evaluation(r)
+        st = dynamic_is_step(base_backend=backend, registry=registry, store=store, prompt=prompt,
+                             generated_prefix=generated, config=cfg, base_sampling=sampling, reward=reward,
+                             reward_version="reward", seeds=seeds, step_index=k,
+                             auxiliary_proposal=hot if aware else None, statistics_provider=stats)
+        steps.append(st)
+        generated += tuple(st.selected.token_ids)
+        if sampling.eos_token_id is not None and sampling.eos_token_id in st.selected.token_ids:
+            break
+    return DynamicISResult(prompt, generated, tuple(steps), 0)
+
+
 __all__ = ["CandidateProposal", "CandidateProposalFactory", "CandidateProposalSource", "DesignPreparation",
            "DesignStatisticsContext", "DesignStatisticsProvider", "DynamicCandidate", "DynamicCandidateDraw",
            "DynamicISResult", "DynamicISStep", "RolloutBudgetContext", "RolloutBudgetProvider",
-           "constant_design_statistics", "draw_candidates", "dynamic_is_step", "empirical_design_statistics",
-           "run_dynamic_is"]
+           "DYNAMIC_ARMS", "constant_design_statistics", "draw_candidates", "dynamic_is_step",
+           "empirical_design_statistics", "run_dynamic_is", "run_dynamic_is_arm"]

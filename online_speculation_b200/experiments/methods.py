@@ -16,7 +16,6 @@ from __future__ import annotations
 
 from collections.abc import Callable, Sequence
 from dataclasses import dataclass, field
-from typing import Any
 
 from ..arllm.algorithms.conditional_is import run_conditional_is
 from ..arllm.algorithms.mh import run_mh_chains_batched, run_reward_mh_chain
@@ -218,12 +217,26 @@ def run_ar_method(name: str, backend: AutoregressiveBackend, prompt: Sequence[in
         res = run_smc_rollout_forest(backend, prompt, cfg, reward, seeds, base_sampling=_base_sampling(s))
         return MethodOutcome(name, res.token_ids, {"reused_rollouts": res.reused_rollouts,
                                                    "fresh_rollouts": res.fresh_rollouts})
+    if name in ("base_candidate_fixed", "replay_aware_fixed", "replay_aware_optimal"):
+        from ..experimental.arllm.dynamic_is import run_dynamic_is_arm
+
+        res = run_dynamic_is_arm(backend, prompt, arm=name, candidate_count=s.candidates,
+                                 block_size=min(s.block_size, s.max_new_tokens), total_length=s.max_new_tokens,
+                                 reward=reward, seeds=seeds, reward_temperature=s.reward_temperature,
+                                 history=int(s.extra.get("history", 4)),
+                                 rollout_budget=float(s.extra.get("rollout_budget", s.candidates * s.rollouts)),
+                                 base_sampling=_base_sampling(s))
+        est = [c.estimate for st in res.steps for c in st.candidates]
+        return MethodOutcome(name, res.token_ids, {"steps": len(res.steps),
+                                                   "history_rollouts_reused": sum(e.history_count for e in est),
+                                                   "fresh_rollouts": sum(e.fresh_count for e in est)})
     raise NotImplementedError(f"method {name!r} needs resources this runner does not build (a proposal model, "
                               "an adapter or a replay store); call its sampler directly")
 
 
 RUNNABLE_AR_METHODS = ("base", "best_of_n", "mh", "reward_mh", "verifier_mh", "conditional_is",
-                       "verifier_conditional_is", "iterated_conditional_is", "progressive_is", "smc_forest")
+                       "verifier_conditional_is", "iterated_conditional_is", "progressive_is", "smc_forest",
+                       "base_candidate_fixed", "replay_aware_fixed", "replay_aware_optimal")
 
 
 __all__ = ["AR_ASYNC_METHODS", "AR_DEFAULT_METHODS", "AR_DISTRIBUTION_METHODS", "AR_DYNAMIC_METHODS",

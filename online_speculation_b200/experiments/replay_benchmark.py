@@ -39,7 +39,7 @@ from typing import Any
 
 import numpy as np
 
-from ..arllm.config import BaseReplayConfig, DynamicISConfig, SamplingConfig
+from ..arllm.config import BaseReplayConfig, SamplingConfig
 from ..arllm.replay import BehaviorPolicy, BehaviorRegistry, InMemoryReplayStore
 from ..shared.rng import SeedStream
 from .rollout_infra import counter_delta, measure
@@ -132,67 +132,32 @@ class _Result:
 
 
 def dynamic_is_arms(backend, *, prompts: Sequence[tuple], length: int, block: int, candidates: int, seed: int,
-                    reward: Callable, history: int = 4, budget: float = 16.0, auxiliary_temperature: float = 1.5,
-                    history_temperature: float = 1.3) -> list[dict]:
-    """Dynamic IS arms.  The replay-aware arms prepare the store before every decision: the
-    decision's candidate draws (the step's own seed stream, so the step redraws the same
-    blocks) get ``history`` rollouts each from the history policy -- the cache build, timed
-    apart -- which the variance-cost allocation may spend instead of fresh rollouts."""
-    from ..arllm.replay import ReplayKey, ReplaySampleRequest, sample_replay_records
-    from ..experimental.arllm.dynamic_is import (CandidateProposal, constant_design_statistics, draw_candidates,
-                                                 dynamic_is_step, empirical_design_statistics)
+                    reward: Callable, history: int = 4, budget: float = 16.0) -> list[dict]:
+    """Dynamic IS arms (:func:`~online_speculation_b200.experimental.arllm.dynamic_is.run_dynamic_is_arm`);
+    the replay-aware arms' history preparation is the cache build, timed apart."""
+    from ..experimental.arllm.dynamic_is import DYNAMIC_ARMS, run_dynamic_is_arm
 
     out = []
-    sampling = SamplingConfig()
-    hot = CandidateProposal.for_backend(backend, SamplingConfig(temperature=auxiliary_temperature), label="hot")
-    hist_policy = BehaviorPolicy.for_backend(backend, SamplingConfig(temperature=history_temperature),
-                                             label="history")
-    for name in ("base_candidate_fixed", "replay_aware_fixed", "replay_aware_optimal"):
-        aware = name != "base_candidate_fixed"
-        cfg = DynamicISConfig(candidate_count=candidates, block_size=block, total_length=length, reward_temperature=0.5,
-                              max_history_per_candidate=history if aware else 0, rollout_budget=budget,
-                              auxiliary_mixture=0.25 if aware else 0.0)
-        stats = empirical_design_statistics if name == "replay_aware_optimal" else constant_design_statistics
+    for name in DYNAMIC_ARMS:
         snap = getattr(backend, "snapshot", lambda: None)
         build = {"wall_seconds": 0.0, "device_seconds": 0.0, "records": 0}
 
-        def one(i, prompt):
-            seeds = SeedStream(SeedStream(seed).derive("dynamic", i))
-            registry, store = BehaviorRegistry([hist_policy]), InMemoryReplayStore()
-            generated: tuple = ()
-            steps = []
-            while len(generated) < length:
-                k = len(steps)
-                b = min(block, length - len(generated))
-                rollout = length - len(generated) - b
-                if aware and rollout > 0:
-                    def prepare():
-                        draws = draw_candidates(base_backend=backend, base_sampling=sampling,
-                                                 prefix=tuple(prompt) + generated, count=candidates, block=b,
-                                                 mixture=cfg.auxiliary_mixture, source=hot, seeds=seeds, step=k)
-                        keys = dict.fromkeys(ReplayKey(tuple(prompt), generated, d.token_ids, "reward")
-                                             for d in draws)
-                        reqs = [ReplaySampleRequest(key, rollout, seeds.derive("history", k, j, h),
-                                                    f"history:{i}:{k}:{j}:{h}")
-                                for j, key in enumerate(keys) for h in range(history)]
-                        return sample_replay_records(hist_policy, reqs, reward)
+        def timed(make):
+            recs, t = measure(make)
+            build["wall_seconds"] += t["wall_seconds"]
+            build["device_seconds"] += t["device_seconds"]
+            build["records"] += len(recs)
+            return recs
 
-                    recs, t = measure(prepare)
-                    for r in recs:
-                        store.add_evaluation(r)
-                    build["wall_seconds"] += t["wall_seconds"]
-                    build["device_seconds"] += t["device_seconds"]
-                    build["records"] += len(recs)
-                st = dynamic_is_step(base_backend=backend, registry=registry, store=store, prompt=tuple(prompt),
-                                     generated_prefix=generated, config=cfg, base_sampling=sampling, reward=reward,
-                                     reward_version="reward", seeds=seeds, step_index=k,
-                                     auxiliary_proposal=hot if aware else None, statistics_provider=stats)
-                steps.append(st)
-                generated += tuple(st.selected.token_ids)
-            return _Result(generated, tuple(steps), 0)
+        def run():
+            return [run_dynamic_is_arm(backend, p, arm=name, candidate_count=candidates, block_size=block,
+                                       total_length=length, reward=reward,
+                                       seeds=SeedStream(SeedStream(seed).derive("dynamic", i)), history=history,
+                                       rollout_budget=budget, prepare=timed)
+                    for i, p in enumerate(prompts)]
 
         before = snap()
-        results, t = measure(lambda: [one(i, p) for i, p in enumerate(prompts)])
+        results, t = measure(run)
         t = {k: t[k] - build[k] for k in t}
         rec = _summary(name, results, t, reward, prompts, before, snap())
         rec["cache_build"] = build

@@ -29,3 +29,15 @@ def test_replay_and_dynamic_is_arms():
     assert arms["replay_aware_fixed"]["history_rollouts_reused"] > 0
     assert rep["dynamic_is"][1]["cache_build"]["records"] > 0
     assert 0.0 <= arms["replay_aware_optimal"]["mean_output_reward"] <= 1.0
+
+
+def test_dynamic_is_arms_run_through_the_method_runner():
+    from online_speculation_b200.experiments.methods import MethodSettings, RUNNABLE_AR_METHODS, run_ar_method
+
+    backend = TabularBackend.per_position_logits(16, 12, seed=2, prompt_length=3)
+    s = MethodSettings(max_new_tokens=8, block_size=4, candidates=3, rollouts=2)
+    for arm in ("base_candidate_fixed", "replay_aware_fixed", "replay_aware_optimal"):
+        assert arm in RUNNABLE_AR_METHODS
+        out = run_ar_method(arm, backend, (1, 2, 3), s, 7, reward=lambda p, y: sum(t == 0 for t in y) / len(y))
+        assert len(out.token_ids) == 8 and out.diagnostics["steps"] == 2
+        assert (out.diagnostics["history_rollouts_reused"] > 0) == (arm != "base_candidate_fixed")
