@@ -788,21 +788,34 @@ def run_is_reference(args, rank, world, local, group) -> dict:
     })
 
 
+# reference arms that cannot run in this image, whatever the hardware (reported before any device setup)
+REFERENCE_UNAVAILABLE = {
+    "dllm": "the reference LLaDA-MoE path loads remote model code from the Hugging Face hub, which this machine "
+            "cannot reach",
+    "grpo": "the reference GRPO path needs trl and peft, which are not installed in this image",
+}
+
+
 def main():
     args = parse()
+    if args.impl == "reference" and args.workload in REFERENCE_UNAVAILABLE:
+        if int(os.environ.get("RANK", "0")) == 0:
+            out = {"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE[args.workload]}
+            print(json.dumps(out), flush=True)
+            if args.json_out:
+                os.makedirs(os.path.dirname(os.path.abspath(args.json_out)), exist_ok=True)
+                with open(args.json_out, "w", encoding="utf-8") as handle:
+                    handle.write(json.dumps(out) + "\n")
+        return
     rank, world, local, group = dist_setup(args.gpus)
     try:
         if args.workload == "dllm":
-            out = (run_dllm(args, rank, world, local, group) if args.impl == "ours" else
-                   {"impl": "reference", "unavailable": "the reference LLaDA-MoE path loads remote model code from "
-                                                        "the Hugging Face hub, which this machine cannot reach"})
+            out = run_dllm(args, rank, world, local, group)
         elif args.workload == "is":
             out = (run_is(args, rank, world, local, group) if args.impl == "ours"
                    else run_is_reference(args, rank, world, local, group))
         elif args.workload == "grpo":
-            out = (run_grpo(args, rank, world, local, group) if args.impl == "ours" else
-                   {"impl": "reference", "unavailable": "the reference GRPO path needs trl and peft, which are not "
-                                                        "installed in this image"})
+            out = run_grpo(args, rank, world, local, group)
         else:
             out = (run_ours(args, rank, world, local, group) if args.impl == "ours"
                    else run_reference(args, rank, world, local, group))

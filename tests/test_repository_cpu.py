@@ -75,3 +75,16 @@ def test_every_module_imports_without_a_gpu():
         except Exception as err:                # noqa: BLE001 - collected for the report
             failed.append(f"{mod.name}: {type(err).__name__}: {err}")
     assert not failed, failed
+
+
+@pytest.mark.parametrize("workload", ["grpo", "dllm"])
+def test_unavailable_reference_arms_report_without_a_gpu(workload):
+    import json
+    import subprocess
+    import sys
+
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--workload",
+                          workload], capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["unavailable"]
